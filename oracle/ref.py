@@ -1,0 +1,215 @@
+"""ctypes access to the reference's own CPU kernels, compiled from its sources
+into oracle/_ref/ by `make -C oracle ref` -- TEST INFRASTRUCTURE ONLY.
+
+Two uses: tests/test_oracle_vs_reference.py checks the C restatement against
+these (bit for bit where the reference's operation order allows), and
+bench.py's cpu_baseline / `--impl reference` legs time them on the host cores.
+The call signatures are the reference's C ABI, as bound by
+src/pcketlm/native/__init__.py.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import torch
+
+from .kernels import _I64, _INT, _P, _Tables, _check, _f32, _ptr, _rows, _u8
+
+REF_DIR = Path(__file__).resolve().parent / "_ref"
+REFERENCE_SOURCES = Path("/root/reference/src/pcketlm/native")
+_LIBS: dict[str, ctypes.CDLL] = {}
+
+
+def build() -> bool:
+    """Compile the reference libraries when the reference tree is present.
+
+    Returns True when oracle/_ref/ holds a usable build afterwards.  On a
+    machine without the reference tree (the GPU box) the prebuilt files that
+    travelled with the repository are used as they are.
+    """
+    if REFERENCE_SOURCES.is_dir():
+        subprocess.run(["make", "-s", "-C", str(REF_DIR.parent), "ref"], check=True)
+    return available()
+
+
+def available() -> bool:
+    return (REF_DIR / "fp8_linear.so").exists()
+
+
+def lib(name: str) -> ctypes.CDLL:
+    if name not in _LIBS:
+        path = REF_DIR / f"{name}.so"
+        if not path.exists():
+            raise FileNotFoundError(f"reference build missing: {path} (run `make -C oracle ref`)")
+        handle = ctypes.CDLL(str(path))
+        _LIBS[name] = handle
+    return _LIBS[name]
+
+
+def threads() -> int:
+    return len(os.sched_getaffinity(0))
+
+
+def fp8_linear(w, s, x):
+    w, s, x = _u8(w), _f32(s), _rows(x)
+    out = torch.empty((x.shape[0], w.shape[0]), dtype=torch.float32)
+    f = lib("fp8_linear").fp8_e4m3_block_linear_f32
+    f.restype = _INT
+    _check(f(_ptr(w), _ptr(s), _ptr(x), _ptr(out), _I64(x.shape[0]), _I64(w.shape[0]),
+             _I64(w.shape[1]), _I64(s.shape[1])), "ref fp8_linear")
+    return out
+
+
+def fp8_mlp(gate, gate_s, up, up_s, down, down_s, x, *, avx512: bool = False):
+    gate, up, down = _u8(gate), _u8(up), _u8(down)
+    gate_s, up_s, down_s, x = _f32(gate_s), _f32(up_s), _f32(down_s), _rows(x)
+    inter, hidden = int(gate.shape[0]), int(gate.shape[1])
+    out = torch.empty((x.shape[0], hidden), dtype=torch.float32)
+    if avx512:
+        f = lib("fp8_linear_avx512").fp8_e4m3_block_mlp_avx512_f32
+    else:
+        f = lib("fp8_linear").fp8_e4m3_block_mlp_f32
+    f.restype = _INT
+    _check(f(_ptr(gate), _ptr(gate_s), _ptr(up), _ptr(up_s), _ptr(down), _ptr(down_s), _ptr(x),
+             _ptr(out), _I64(x.shape[0]), _I64(inter), _I64(hidden), _I64(gate_s.shape[1]),
+             _I64(down_s.shape[1])), "ref fp8_mlp")
+    return out
+
+
+def fp8_mlp_many(items, x):
+    t, x = _Tables(items), _rows(x)
+    out = torch.zeros((len(items), x.shape[0], t.hidden), dtype=torch.float32)
+    f = lib("fp8_linear").fp8_e4m3_block_mlp_many_f32
+    f.restype = _INT
+    _check(f(*t.args(), _ptr(x), _ptr(out), _I64(len(items)), _I64(x.shape[0]), _I64(t.inter),
+             _I64(t.hidden), _I64(t.gsc), _I64(t.dsc)), "ref fp8_mlp_many")
+    return out
+
+
+def fp8_mlp_many_weighted(items, x, route, *, avx512: bool = False):
+    t, x, route = _Tables(items), _rows(x), _f32(route.reshape(-1))
+    out = torch.empty((x.shape[0], t.hidden), dtype=torch.float32)
+    if avx512:
+        f = lib("fp8_linear_avx512").fp8_e4m3_block_mlp_many_weighted_avx512_f32
+    else:
+        f = lib("fp8_linear").fp8_e4m3_block_mlp_many_weighted_f32
+    f.restype = _INT
+    _check(f(*t.args(), _ptr(x), _ptr(route), _ptr(out), _I64(len(items)), _I64(x.shape[0]),
+             _I64(t.inter), _I64(t.hidden), _I64(t.gsc), _I64(t.dsc)), "ref fp8_mlp_many_weighted")
+    return out
+
+
+def fp8_mlp_many_row_weighted(items, x, route):
+    t, x, route = _Tables(items), _rows(x), _f32(route)
+    out = torch.empty((x.shape[0], t.hidden), dtype=torch.float32)
+    f = lib("fp8_linear").fp8_e4m3_block_mlp_many_row_weighted_f32
+    f.restype = _INT
+    _check(f(*t.args(), _ptr(x), _ptr(route), _ptr(out), _I64(len(items)), _I64(x.shape[0]),
+             _I64(t.inter), _I64(t.hidden), _I64(t.gsc), _I64(t.dsc)), "ref fp8_mlp_many_row_weighted")
+    return out
+
+
+def fp8_mlp_many_pair_weighted(items, x, pair_items, pair_rows, pair_weights):
+    t, x = _Tables(items), _rows(x)
+    pi = pair_items.detach().cpu().contiguous().reshape(-1).to(torch.int64)
+    pr = pair_rows.detach().cpu().contiguous().reshape(-1).to(torch.int64)
+    pw = _f32(pair_weights.reshape(-1))
+    out = torch.empty((x.shape[0], t.hidden), dtype=torch.float32)
+    f = lib("fp8_linear").fp8_e4m3_block_mlp_many_pair_weighted_f32
+    f.restype = _INT
+    _check(f(*t.args(), _ptr(x), _ptr(pi), _ptr(pr), _ptr(pw), _ptr(out), _I64(len(items)),
+             _I64(pi.numel()), _I64(x.shape[0]), _I64(t.inter), _I64(t.hidden), _I64(t.gsc),
+             _I64(t.dsc)), "ref fp8_mlp_many_pair_weighted")
+    return out
+
+
+def fp8_dequant(w, s, dtype):
+    w, s = _u8(w), _f32(s)
+    rows, cols = int(w.shape[0]), int(w.shape[1])
+    out = torch.empty((rows, cols), dtype=torch.int16)
+    name = "fp8_e4m3_dequant_to_bf16" if dtype == torch.bfloat16 else "fp8_e4m3_dequant_to_fp16"
+    f = getattr(lib("fp8_dequant"), name)
+    f.restype = _INT
+    _check(f(_ptr(w), _ptr(s), _ptr(out), _I64(rows), _I64(cols), _I64(s.shape[1])), "ref dequant")
+    return out.view(dtype)
+
+
+def q4_dequant_to_fp16(packed, scales, channels: int, channel_size: int):
+    packed = packed.detach().cpu().contiguous().to(torch.uint8)
+    scales = scales.detach().cpu().contiguous().to(torch.float16)
+    out = torch.empty((channels * channel_size,), dtype=torch.float16)
+    f = lib("q4_dequant").q4_dequant_to_fp16
+    f.restype = None
+    f(_ptr(packed), _ptr(scales), _ptr(out), _I64(channels), _I64(channel_size))
+    return out
+
+
+def q4_moe_selected_forward(hidden, experts, route, hidden_size: int, intermediate_size: int):
+    x = hidden.detach().cpu().contiguous().reshape(-1).to(torch.float16)
+    r = _f32(route.reshape(-1))
+    keep = []
+    arrays = [(ctypes.c_void_p * len(experts))() for _ in range(6)]
+    for i, item in enumerate(experts):
+        conv = [t.detach().cpu().contiguous().to(torch.uint8 if j % 2 == 0 else torch.float16)
+                for j, t in enumerate(item)]
+        keep.append(conv)
+        for j, t in enumerate(conv):
+            arrays[j][i] = ctypes.c_void_p(int(t.data_ptr()))
+    out = torch.empty((hidden_size,), dtype=torch.float16)
+    f = lib("q4_dequant").q4_moe_selected_forward_u16
+    f.restype = _INT
+    _check(f(_ptr(x), *arrays, _ptr(r), _ptr(out), _I64(hidden_size), _I64(intermediate_size),
+             _I64(len(experts))), "ref q4_moe_selected_forward")
+    return out
+
+
+def pack_rows8(weight):
+    w = weight.detach().cpu().contiguous()
+    rows, cols = int(w.shape[0]), int(w.shape[1])
+    out = torch.empty((((rows + 7) // 8) * cols * 8,), dtype=torch.int16)
+    f = lib("fp16_packed_gemv").native_pack_u16_rows8
+    f.restype = _INT
+    _check(f(_ptr(w), _ptr(out), _I64(rows), _I64(cols)), "ref pack_rows8")
+    return out
+
+
+def packed_gemv_rows8(hidden, packed, rows: int, cols: int):
+    x = hidden.detach().cpu().contiguous().reshape(-1)
+    p = packed.detach().cpu().contiguous()
+    out = torch.empty((rows,), dtype=torch.float32)
+    f = lib("fp16_packed_gemv").native_packed_gemv_rows8
+    f.restype = _INT
+    _check(f(_ptr(x), _ptr(p), _ptr(out), _I64(rows), _I64(cols),
+             _INT(1 if x.dtype == torch.bfloat16 else 0)), "ref packed_gemv_rows8")
+    return out
+
+
+def moe_selected_forward_u16(hidden, gate, up, down, route):
+    x = hidden.detach().cpu().contiguous()
+    g, u, d = (t.detach().cpu().contiguous() for t in (gate, up, down))
+    r = _f32(route)
+    out = torch.empty(tuple(x.shape), dtype=hidden.dtype)
+    f = lib("fp16_moe").native_moe_selected_forward_u16
+    f.restype = _INT
+    _check(f(_ptr(x), _ptr(g), _ptr(u), _ptr(d), _ptr(r), _ptr(out), _I64(x.shape[0]),
+             _I64(x.shape[1]), _I64(g.shape[0]), _I64(g.shape[1]),
+             _INT(1 if x.dtype == torch.bfloat16 else 0)), "ref moe_selected_forward_u16")
+    return out
+
+
+def router_softmax_topk_u16(hidden, router_weights, k: int):
+    x = hidden.detach().cpu().contiguous().reshape(-1)
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        x = x.to(torch.float16)
+    w = router_weights.detach().cpu().contiguous().to(x.dtype)
+    ids = torch.empty((k,), dtype=torch.int64)
+    weights = torch.empty((k,), dtype=torch.float32)
+    f = lib("ds_forward").ds_router_topk_u16
+    f.restype = _INT
+    _check(f(_ptr(x), _ptr(w), _I64(w.shape[1]), _I64(w.shape[0]), _I64(k),
+             _I64(1 if x.dtype == torch.bfloat16 else 0), _ptr(ids), _ptr(weights)), "ref router")
+    return ids, weights
