@@ -1,0 +1,371 @@
+"""Benchmark: DeepSeek-V3 MoE layer tokens/s on B200 (decode).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
+
+A step is one MoE layer forward (router -> dispatch -> FP8 SwiGLU experts ->
+weighted combine + shared expert) over a batch of T tokens (default 64, the
+largest decode batch of config 2) with all 256 routed experts + the shared
+expert resident in HBM (11.3 GB of e4m3 weights + fp32 block scales,
+synthetic, seeded).  The weights streamed per step exceed the 126 MB L2, and
+L2 is additionally flushed (256 MiB write) between timed steps; each step is
+timed with CUDA events on the launching stream.  The same measurement is
+repeated for T = 1, 4, 16 ("sweep").
+
+Printed (rank 0, one JSON line): tokens/s with inputs resident in HBM
+(`value`), the same through the public API from pinned host buffers with the
+copies inside the timed region (`e2e`), the HBM roofline of the dominant
+kernel (the grouped GEMV gate/up stage), the reference's own CPU path timed
+on this host (`cpu_baseline`, oracle/_ref), clocks sampled during the run.
+
+--impl reference times the reference's CPU path alone (oracle/_ref kernels
+driven through run_fp8_moe's default flow) on a bounded token sample.
+With --gpus N > 1 (torchrun), each rank runs its own replica of the layer on
+its own tokens (weak scaling); value is the sum over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+os.environ.setdefault("OMP_NUM_THREADS", str(len(os.sched_getaffinity(0))))
+os.environ.setdefault("PCKETLM_NATIVE_THREADS", os.environ["OMP_NUM_THREADS"])
+
+import torch  # noqa: E402
+
+METRIC = "DS-V3 MoE layer tokens/s @1/2/4/8 B200; % of HBM or FP8 TC roofline"
+L2_FLUSH_BYTES = 256 << 20
+KERNELS_PER_LAYER = 7  # router logits, router select, dispatch, chunk list, gate/up, down, combine
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return {**json.loads(path.read_text()), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"moe_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, _, flags in rows for i, f in enumerate(flags) if f == "Active"})
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own kernels (oracle/_ref) in run_fp8_moe's flow
+# ---------------------------------------------------------------------------
+
+def cpu_reference_sample(tokens: int, seed: int, reps: int = 1) -> dict:
+    """Time run_fp8_moe's default flow (fp8_source.py:1569-1884) on the host
+    cores with the reference's compiled fp8_e4m3_block_mlp_f32 on a bounded
+    sample of `tokens` tokens of the config-2 workload (weights generated on
+    the CPU for exactly the experts those tokens select)."""
+    import oracle
+    from oracle import ref
+    from pocketlm_b200 import synth
+
+    if not ref.available():
+        raise RuntimeError("reference build oracle/_ref missing")
+    cfg = synth.C2_DSV3
+    x = synth.make_hidden(tokens, cfg.hidden, seed=seed)
+    probe = synth.make_fp8_layer(cfg, seed=seed, experts=[])
+    route = oracle.route_deepseek(x, probe.router_weight, probe.bias, top_k=cfg.top_k, n_groups=cfg.n_group,
+                                  topk_groups=cfg.topk_group, route_scale=cfg.route_scale)
+    experts = sorted({int(v) for v in route.ids.reshape(-1).tolist()})
+    layer = synth.make_fp8_layer(cfg, seed=seed, experts=experts + [cfg.n_routed])
+    times = []
+    for _ in range(max(1, reps)):
+        t0 = time.perf_counter()
+        oracle.ds_moe_layer(x, layer, route=None, mlp_fn=ref.fp8_mlp)
+        times.append(time.perf_counter() - t0)
+    per_step = statistics.median(times)
+    return {"value": tokens / per_step, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)),
+            "kind": "reference", "seconds_per_sample": per_step,
+            "sample": (f"{tokens} tokens of the config-2 decode batch through run_fp8_moe's default flow "
+                       f"(torch CPU router, per-expert fp8_e4m3_block_mlp_f32 from oracle/_ref, bf16 combine, "
+                       f"shared expert); {len(experts)} routed experts; OMP threads {os.environ['OMP_NUM_THREADS']}")}
+
+
+# ---------------------------------------------------------------------------
+# GPU measurement
+# ---------------------------------------------------------------------------
+
+def flush_l2(buf: torch.Tensor) -> None:
+    buf.add_(1)
+
+
+def time_steps(fn, steps: int, warmup: int, flush: torch.Tensor) -> list[float]:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush_l2(flush)
+        starts[i].record(stream)
+        fn()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+def layer_bytes(cfg, ids: torch.Tensor, tokens: int) -> dict:
+    n_exp = len({int(v) for v in ids.reshape(-1).tolist()}) + 1  # + shared
+    gs, ds = cfg.gate_scale_shape, cfg.down_scale_shape
+    gateup = n_exp * (2 * cfg.inter * cfg.hidden + 2 * 4 * gs[0] * gs[1])
+    down = n_exp * (cfg.hidden * cfg.inter + 4 * ds[0] * ds[1])
+    router = cfg.n_routed * cfg.hidden * 2
+    acts = tokens * cfg.hidden * 2 * 2
+    return {"experts": n_exp, "gateup": gateup, "down": down, "router": router,
+            "total": gateup + down + router + acts}
+
+
+def stage_times(gpu_layer, x, steps: int, flush: torch.Tensor) -> list[float]:
+    from pocketlm_b200 import native
+    import ctypes
+
+    lib = native.load_library()
+    lib.moe_b200_stage_timing(1)
+    acc = None
+    buf = (ctypes.c_float * 8)()
+    for _ in range(steps):
+        flush_l2(flush)
+        gpu_layer.forward(x)
+        n = lib.moe_b200_stage_times(buf, 8)
+        vals = [buf[i] for i in range(n)]
+        acc = vals if acc is None else [a + v for a, v in zip(acc, vals)]
+    lib.moe_b200_stage_timing(0)
+    return [a / steps for a in acc]
+
+
+def read_traffic(name: str):
+    path = ROOT / "profiles" / name
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def run_ours(args, rank: int, world: int) -> dict | None:
+    from pocketlm_b200 import native, synth
+    from pocketlm_b200.runtime import DsMoELayerGPU
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    native.load_library()
+    cfg = synth.C2_DSV3
+    layer = synth.make_fp8_layer(cfg, seed=args.seed, device=dev)
+    gpu_layer = DsMoELayerGPU(layer)
+    flush = torch.zeros((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
+    peaks = measured_peaks()
+    results = {}
+    token_list = [args.tokens] + [t for t in (1, 4, 16, 64) if t != args.tokens]
+    with ClockSampler(dev.index) as clocks:
+        for T in token_list:
+            x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 100 * rank + T, device=dev)
+            out = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=dev)
+            ids = torch.empty((T, cfg.top_k), dtype=torch.int64, device=dev)
+            gpu_layer.forward(x, out=out, ids=ids)
+            torch.cuda.synchronize()
+            fn = lambda: gpu_layer.forward(x, out=out)  # noqa: E731
+            if world > 1:
+                torch.distributed.barrier()
+            torch.cuda.synchronize()
+            times = time_steps(fn, args.steps, args.warmup, flush)
+            if world > 1:
+                torch.distributed.barrier()
+            torch.cuda.synchronize()
+            ms = statistics.mean(times)
+            if world > 1:
+                t = torch.tensor([ms], device=dev)
+                torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+                ms = float(t.item())
+            stages = stage_times(gpu_layer, x, max(5, min(args.steps, 50)), flush)
+            b = layer_bytes(cfg, ids, T)
+            # stage marks: [route+dispatch, chunk list, gate/up, down, combine]
+            gateup_ms = stages[2] if len(stages) >= 3 else None
+            down_ms = stages[3] if len(stages) >= 4 else None
+            # end to end through the public API: pinned host in, pinned host out
+            x_host = x.cpu().pin_memory()
+            out_host = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
+            x_dev = torch.empty_like(x)
+
+            def e2e_step():
+                x_dev.copy_(x_host, non_blocking=True)
+                gpu_layer.forward(x_dev, out=out)
+                out_host.copy_(out, non_blocking=True)
+
+            e2e_ms = statistics.mean(time_steps(e2e_step, args.steps, args.warmup, flush))
+            if world > 1:
+                t = torch.tensor([e2e_ms], device=dev)
+                torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+                e2e_ms = float(t.item())
+            results[T] = {
+                "tokens": T, "ms_per_step": ms, "tokens_per_s": T * world / (ms / 1e3),
+                "e2e_tokens_per_s": T * world / (e2e_ms / 1e3), "e2e_ms": e2e_ms,
+                "experts_streamed": b["experts"], "layer_bytes": b["total"],
+                "layer_hbm_frac": (b["total"] / (ms / 1e3)) / (peaks["hbm_gbs"] * 1e9),
+                "gateup_ms": gateup_ms, "down_ms": down_ms, "stage_ms": stages,
+                "gateup_bytes": b["gateup"],
+                "gateup_gbs": (b["gateup"] / (gateup_ms / 1e3) / 1e9) if gateup_ms else None,
+                "down_gbs": (b["down"] / (down_ms / 1e3) / 1e9) if down_ms else None,
+            }
+    clock_info = clocks.summary()
+    if rank != 0:
+        return None
+    head = results[args.tokens]
+    peak = peaks["hbm_gbs"]
+    achieved = head["gateup_gbs"]
+    cpu = None
+    if not args.no_cpu_baseline:
+        try:
+            cpu = cpu_reference_sample(args.cpu_sample_tokens, seed=args.seed, reps=2)
+        except Exception as exc:  # the baseline is reported, not required
+            cpu = {"value": None, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)), "kind": "reference",
+                   "sample": f"unavailable: {exc}"}
+    return {
+        "metric": METRIC, "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (e4m3 weights decoded exactly, bf16 activations, fp32 accumulate)",
+        "data": "synthetic (seeded random DS-V3-shape weights and activations; no checkpoint)",
+        "config": {"workload": f"c2-dsv3-decode-T{args.tokens}", "tokens_per_gpu": args.tokens,
+                   "hidden": cfg.hidden, "moe_intermediate": cfg.inter, "experts": f"{cfg.n_routed}+1",
+                   "top_k": cfg.top_k, "n_group": cfg.n_group, "topk_group": cfg.topk_group,
+                   "parallelism": "single GPU" if world == 1 else f"replicas x{world}",
+                   "l2": "weights streamed per step exceed L2; 256 MiB L2 flush between timed steps"},
+        "roofline": {"bound": "hbm", "kernel": "grouped_gemv gate/up+SwiGLU (fp8_gemv.cu)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": (achieved / peak) if achieved else None,
+                     "peak_source": f"{peaks['source']} hbm_gbs",
+                     "algorithmic_bytes_per_launch": head["gateup_bytes"],
+                     "traffic": read_traffic(f"grouped_gemv_gateup_c2_decode_T{args.tokens}.md"),
+                     "layer_frac": head["layer_hbm_frac"]},
+        "e2e": {"value": head["e2e_tokens_per_s"], "unit": "tokens/s",
+                "h2d_bytes_per_step": args.tokens * cfg.hidden * 2, "d2h_bytes_per_step": args.tokens * cfg.hidden * 2},
+        "gpu_launches": KERNELS_PER_LAYER * args.steps,
+        "cpu_baseline": cpu,
+        "clocks": clock_info,
+        "sweep": {str(T): {k: v for k, v in r.items() if k != "stage_ms"} | {"stage_ms": r["stage_ms"]}
+                  for T, r in sorted(results.items())},
+    }
+
+
+def run_reference(args, rank: int, world: int) -> dict | None:
+    if rank != 0:
+        return None
+    from oracle import ref
+
+    if not ref.available():
+        return {"impl": "reference", "unavailable": "reference CPU build (oracle/_ref) missing"}
+    samples = []
+    for i in range(args.warmup + args.steps):
+        s = cpu_reference_sample(args.cpu_sample_tokens, seed=args.seed, reps=1)
+        if i >= args.warmup:
+            samples.append(s["seconds_per_sample"])
+    per = statistics.mean(samples)
+    value = args.cpu_sample_tokens / per
+    return {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (reference CPU: e4m3 LUT decode, fp32 accumulate)",
+        "data": "synthetic (seeded random DS-V3-shape weights and activations; no checkpoint)",
+        "config": {"workload": f"c2-dsv3-decode-T{args.tokens}", "tokens_per_gpu": args.tokens,
+                   "parallelism": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)),
+                         "kind": "reference", "sample": s["sample"]},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--tokens", type=int, default=64)
+    parser.add_argument("--seed", type=int, default=20)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--cpu-sample-tokens", type=int, default=4)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    try:
+        result = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world)
+        if result is not None:
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1 and args.impl == "ours":
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

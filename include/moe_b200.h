@@ -1,0 +1,226 @@
+/*
+ * moe_b200.h -- C ABI of libmoe_b200.so, the sm_100a (B200) MoE expert path.
+ *
+ * Drop-in boundary for PocketLM's native bridge (src/pcketlm/native/__init__.py
+ * of the reference): every entry point keeps the argument order, meaning and
+ * return-code convention of the reference C function named beside it, with
+ * these differences:
+ *
+ *   - all tensor pointers are DEVICE pointers (CUDA global memory on the
+ *     current device), and every call takes a trailing `void* stream`
+ *     (a cudaStream_t; NULL = the legacy default stream).  Calls only enqueue
+ *     work and return; results are ready when the stream reaches them.
+ *   - expert "pointer tables" (uint64_t per expert, as in the reference:
+ *     fp8_linear.cpp:365-370) are DEVICE arrays of device addresses.
+ *   - entry points that need scratch memory take `void* workspace,
+ *     int64_t workspace_bytes`; pass NULL/0 to let the call allocate it
+ *     stream-ordered (cudaMallocAsync / cudaFreeAsync).  The *_workspace_bytes
+ *     functions return the size a caller-provided workspace must have.
+ *
+ * Return codes: 0 = ok; -1 null pointer; -2 bad dimensions; -3 out of memory
+ * or workspace too small; -4 index out of range; -5 unsupported shape;
+ * <= -100: CUDA error (-100 - cudaError_t).  moe_b200_last_error() returns a
+ * message for the last failing call on the calling thread.
+ *
+ * Element types: e4m3 weights are raw bytes (uint8_t), block scales are fp32
+ * [ceil(rows/128), ceil(cols/128)] ("weight_scale_inv"), 16-bit tensors are
+ * passed as uint16_t storage with a dtype code (0 = fp16, 1 = bf16, the
+ * reference's _u16_storage_dtype_code, native/__init__.py:141-146).
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_B200_ABI_VERSION 1
+
+int moe_b200_abi_version(void);
+const char* moe_b200_last_error(void);
+
+/* ---------------------------------------------------------------------------
+ * FP8 e4m3 block-scaled linears and expert MLPs.  fp32 activations in and
+ * out; e4m3 codes 0x7F/0xFF decode as +0 (fp8_linear.cpp:31-33).
+ * ------------------------------------------------------------------------- */
+
+/* replaces fp8_e4m3_block_linear_f32, src/pcketlm/native/fp8_linear.cpp:50 */
+int moe_fp8_e4m3_block_linear_f32(const uint8_t* fp8_weight, const float* scale_inv,
+                                  const float* hidden, float* out, int64_t batch,
+                                  int64_t out_rows, int64_t in_cols, int64_t scale_cols,
+                                  void* stream);
+
+/* replaces fp8_e4m3_block_dual_linear_f32, fp8_linear.cpp:119 */
+int moe_fp8_e4m3_block_dual_linear_f32(const uint8_t* fp8_weight_a, const float* scale_inv_a,
+                                       const uint8_t* fp8_weight_b, const float* scale_inv_b,
+                                       const float* hidden, float* out_a, float* out_b,
+                                       int64_t batch, int64_t out_rows, int64_t in_cols,
+                                       int64_t scale_cols, void* stream);
+
+/* replaces fp8_e4m3_block_mlp_f32, fp8_linear.cpp:212 (and the AVX-512 twin
+ * fp8_e4m3_block_mlp_avx512_f32, fp8_linear_avx512.cpp:157) */
+int moe_fp8_e4m3_block_mlp_f32(const uint8_t* gate_weight, const float* gate_scale_inv,
+                               const uint8_t* up_weight, const float* up_scale_inv,
+                               const uint8_t* down_weight, const float* down_scale_inv,
+                               const float* hidden, float* out, int64_t batch,
+                               int64_t intermediate_rows, int64_t hidden_cols,
+                               int64_t gate_scale_cols, int64_t down_scale_cols,
+                               void* workspace, int64_t workspace_bytes, void* stream);
+
+/* replaces fp8_e4m3_block_mlp_many_f32, fp8_linear.cpp:364 -- out [E, B, H] */
+int moe_fp8_e4m3_block_mlp_many_f32(const uint64_t* gate_weight_ptrs, const uint64_t* gate_scale_ptrs,
+                                    const uint64_t* up_weight_ptrs, const uint64_t* up_scale_ptrs,
+                                    const uint64_t* down_weight_ptrs, const uint64_t* down_scale_ptrs,
+                                    const float* hidden, float* out, int64_t expert_count,
+                                    int64_t batch, int64_t intermediate_rows, int64_t hidden_cols,
+                                    int64_t gate_scale_cols, int64_t down_scale_cols,
+                                    void* workspace, int64_t workspace_bytes, void* stream);
+
+/* replaces fp8_e4m3_block_mlp_many_weighted_f32, fp8_linear.cpp:475 (and
+ * fp8_e4m3_block_mlp_many_weighted_avx512_f32, fp8_linear_avx512.cpp:252):
+ * out [B, H] = sum_e route_weights[e] * expert_e(hidden) */
+int moe_fp8_e4m3_block_mlp_many_weighted_f32(const uint64_t* gate_weight_ptrs, const uint64_t* gate_scale_ptrs,
+                                             const uint64_t* up_weight_ptrs, const uint64_t* up_scale_ptrs,
+                                             const uint64_t* down_weight_ptrs, const uint64_t* down_scale_ptrs,
+                                             const float* hidden, const float* route_weights, float* out,
+                                             int64_t expert_count, int64_t batch, int64_t intermediate_rows,
+                                             int64_t hidden_cols, int64_t gate_scale_cols,
+                                             int64_t down_scale_cols, void* workspace,
+                                             int64_t workspace_bytes, void* stream);
+
+/* replaces fp8_e4m3_block_mlp_many_row_weighted_f32, fp8_linear.cpp:591:
+ * route_weights [E, B]; zero weights skip that (expert, row) entirely */
+int moe_fp8_e4m3_block_mlp_many_row_weighted_f32(const uint64_t* gate_weight_ptrs, const uint64_t* gate_scale_ptrs,
+                                                 const uint64_t* up_weight_ptrs, const uint64_t* up_scale_ptrs,
+                                                 const uint64_t* down_weight_ptrs, const uint64_t* down_scale_ptrs,
+                                                 const float* hidden, const float* route_weights, float* out,
+                                                 int64_t expert_count, int64_t batch,
+                                                 int64_t intermediate_rows, int64_t hidden_cols,
+                                                 int64_t gate_scale_cols, int64_t down_scale_cols,
+                                                 void* workspace, int64_t workspace_bytes, void* stream);
+
+/* replaces fp8_e4m3_block_mlp_many_pair_weighted_f32, fp8_linear.cpp:833:
+ * (item, row, weight) triples; out [B, H] */
+int moe_fp8_e4m3_block_mlp_many_pair_weighted_f32(const uint64_t* gate_weight_ptrs, const uint64_t* gate_scale_ptrs,
+                                                  const uint64_t* up_weight_ptrs, const uint64_t* up_scale_ptrs,
+                                                  const uint64_t* down_weight_ptrs, const uint64_t* down_scale_ptrs,
+                                                  const float* hidden, const int64_t* pair_item_indices,
+                                                  const int64_t* pair_row_indices, const float* pair_weights,
+                                                  float* out, int64_t expert_count, int64_t pair_count,
+                                                  int64_t batch, int64_t intermediate_rows,
+                                                  int64_t hidden_cols, int64_t gate_scale_cols,
+                                                  int64_t down_scale_cols, void* workspace,
+                                                  int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes for the MLP entry points above, given the number of
+ * (expert, row) pairs they evaluate (mlp: batch; many/weighted: E*B;
+ * row/pair weighted: the nonzero count or pair_count; pass the upper bound). */
+int64_t moe_fp8_mlp_workspace_bytes(int64_t pairs, int64_t segments, int64_t batch,
+                                    int64_t intermediate_rows, int64_t hidden_cols);
+
+/* ---------------------------------------------------------------------------
+ * FP8 block dequantisation (NaN codes decode to the reference's NaN bits).
+ * ------------------------------------------------------------------------- */
+
+/* replaces fp8_e4m3_dequant_to_fp16, src/pcketlm/native/fp8_dequant.cpp:119 */
+int moe_fp8_e4m3_dequant_to_fp16(const uint8_t* fp8_weight, const float* scale_inv, uint16_t* out_fp16,
+                                 int64_t rows, int64_t cols, int64_t scale_cols, void* stream);
+
+/* replaces fp8_e4m3_dequant_to_bf16, fp8_dequant.cpp:166 */
+int moe_fp8_e4m3_dequant_to_bf16(const uint8_t* fp8_weight, const float* scale_inv, uint16_t* out_bf16,
+                                 int64_t rows, int64_t cols, int64_t scale_cols, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Routers.
+ * ------------------------------------------------------------------------- */
+
+/* replaces ds_router_topk_u16, src/pcketlm/native/ds_forward.cpp:879: one
+ * token, softmax with fp64 denominators, top-k (ties to the lower id), fp64
+ * renormalisation. */
+int moe_ds_router_topk_u16(const uint16_t* hidden_u16, const uint16_t* router_weights_u16,
+                           int64_t hidden_dim, int64_t num_experts, int64_t k, int64_t dtype_code,
+                           int64_t* output_expert_ids, float* output_weights, void* stream);
+
+/* Batched router; replaces the routing math of run_fp8_router
+ * (src/pcketlm/core/runtime/fp8_source.py:1522-1547, group mask :5125-5140),
+ * which the reference runs in torch.  scoring: 0 sigmoid, 1 softmax.  With
+ * sigmoid scoring the picked scores are renormalised; `renorm` forces it for
+ * softmax too (Mixtral norm_topk_prob, core/runtime/layer_bridge.py:2682-2689).
+ * hidden_dtype / router_dtype: 0 fp32, 1 bf16, 2 fp16.  bias may be NULL.
+ * round_bf16 rounds the final weights through bf16 (the reference casts them
+ * to the hidden dtype).  Any of the three outputs may be NULL. */
+int moe_route_topk(const void* hidden, int hidden_dtype, const void* router_weight, int router_dtype,
+                   const float* bias, int64_t tokens, int64_t hidden_dim, int64_t num_experts,
+                   int64_t n_group, int64_t topk_group, int64_t top_k, int scoring, int renorm,
+                   float route_scale, int round_bf16, int64_t* out_ids, float* out_weights_f32,
+                   uint16_t* out_weights_bf16, void* workspace, int64_t workspace_bytes, void* stream);
+
+int64_t moe_route_topk_workspace_bytes(int64_t tokens, int64_t num_experts);
+
+/* ---------------------------------------------------------------------------
+ * Whole DeepSeek-V3 MoE layer: route -> dispatch -> FP8 SwiGLU experts ->
+ * weighted combine + shared expert.  Replaces run_fp8_moe
+ * (fp8_source.py:1569-1884).  hidden: [tokens, hidden_dim] bf16 (dtype 1) or
+ * fp32 (dtype 0).  tables: device uint64 array [6][n_routed + has_shared]
+ * (gate w, gate scale, up w, up scale, down w, down scale; the shared expert
+ * is the last entry).  out_bf16: [tokens, hidden_dim] bf16.  out_ids (int64)
+ * and out_weights_bf16 ([tokens, top_k]) may be NULL.
+ * ------------------------------------------------------------------------- */
+int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t tokens, int64_t hidden_dim,
+                         int64_t intermediate, const void* router_weight, int router_dtype,
+                         const float* router_bias, int64_t n_routed, int64_t n_group, int64_t topk_group,
+                         int64_t top_k, int scoring, float route_scale, const uint64_t* tables,
+                         int has_shared, uint16_t* out_bf16, int64_t* out_ids, uint16_t* out_weights_bf16,
+                         void* workspace, int64_t workspace_bytes, void* stream);
+
+int64_t moe_ds_moe_layer_workspace_bytes(int64_t tokens, int64_t hidden_dim, int64_t intermediate,
+                                         int64_t n_routed, int64_t top_k, int has_shared);
+
+/* ---------------------------------------------------------------------------
+ * DeepSeek session: opaque handle with the reference's observable counters.
+ * ------------------------------------------------------------------------- */
+
+/* replaces ds_session_create / ds_session_destroy, ds_forward.cpp:192-219 */
+void* moe_ds_session_create(int64_t num_layers, int64_t hidden_dim, int64_t num_experts, int64_t top_k);
+void moe_ds_session_destroy(void* handle);
+
+/* replace ds_monolithic_call_counter, ds_expert_invocation_count and
+ * ds_layers_executed_count, ds_forward.cpp:265-335 (-1 for a null handle) */
+int64_t moe_ds_monolithic_call_counter(void* handle);
+int64_t moe_ds_expert_invocation_count(void* handle);
+int64_t moe_ds_layers_executed_count(void* handle);
+
+/* replaces ds_moe_layer_forward_f32, ds_forward.cpp:337:
+ * hidden_out[b, h] = sum_e route_weights[e] * expert_outputs[e, b, h] */
+int moe_ds_moe_layer_forward_f32(void* handle, const float* expert_outputs, const float* route_weights,
+                                 int64_t selected_count, int64_t batch, int64_t hidden_dim,
+                                 float* hidden_out, void* stream);
+
+/* replaces ds_moe_layer_forward_fp8_f32, ds_forward.cpp:784 */
+int moe_ds_moe_layer_forward_fp8_f32(void* handle, const uint64_t* gate_weight_ptrs,
+                                     const uint64_t* gate_scale_ptrs, const uint64_t* up_weight_ptrs,
+                                     const uint64_t* up_scale_ptrs, const uint64_t* down_weight_ptrs,
+                                     const uint64_t* down_scale_ptrs, const float* hidden,
+                                     const float* route_weights, int64_t selected_count, int64_t batch,
+                                     int64_t intermediate_rows, int64_t hidden_dim,
+                                     int64_t gate_scale_cols, int64_t down_scale_cols, float* hidden_out,
+                                     void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Profiling (no reference counterpart): when enabled, moe_ds_moe_layer_fp8
+ * records CUDA events on its stream at the boundaries of its stages --
+ * [start, route+dispatch done, chunk list done, gate/up done, down done,
+ * combine done].  moe_b200_stage_times waits for the last event and writes the
+ * elapsed milliseconds between consecutive marks (returns how many).
+ * Single-threaded use only.
+ * ------------------------------------------------------------------------- */
+int moe_b200_stage_timing(int enable);
+int moe_b200_stage_times(float* ms, int max_n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H_ */

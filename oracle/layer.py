@@ -26,12 +26,16 @@ from . import kernels
 from .router import RouteResult, route_deepseek, route_softmax_topk
 
 
-def ds_moe_layer(hidden: torch.Tensor, layer, route: RouteResult | None = None):
+def ds_moe_layer(hidden: torch.Tensor, layer, route: RouteResult | None = None, mlp_fn=None):
     """Return (out_bf16 [T, H], RouteResult).
 
     `layer` is a pocketlm_b200.synth.Fp8MoELayer (any device); the expert
     tensors of the selected experts are copied to the CPU as needed.
+    `mlp_fn` replaces the expert kernel (default: the C restatement,
+    oracle.kernels.fp8_mlp); bench.py passes the reference's own compiled
+    fp8_e4m3_block_mlp_f32 (oracle.ref.fp8_mlp) to time the reference path.
     """
+    mlp = mlp_fn or kernels.fp8_mlp
     cfg = layer.cfg
     flat = hidden.detach().cpu().reshape(-1, int(hidden.shape[-1]))
     if route is None:
@@ -45,11 +49,11 @@ def ds_moe_layer(hidden: torch.Tensor, layer, route: RouteResult | None = None):
     for expert in sorted({int(v) for v in ids.reshape(-1).tolist()}):
         rows, slots = torch.where(ids == expert)
         tensors = [t.cpu() for t in layer.expert(expert)]
-        y = kernels.fp8_mlp(*tensors, flat[rows].to(torch.bfloat16).float()).to(torch.bfloat16)
+        y = mlp(*tensors, flat[rows].to(torch.bfloat16).float()).to(torch.bfloat16)
         w = weights[rows, slots].view(-1, 1).to(torch.bfloat16)
         out[rows] += y * w
     shared = [t.cpu() for t in layer.shared_expert()]
-    shared_out = kernels.fp8_mlp(*shared, flat.to(torch.bfloat16).float()).to(torch.bfloat16)
+    shared_out = mlp(*shared, flat.to(torch.bfloat16).float()).to(torch.bfloat16)
     out = out + shared_out
     return out, route
 

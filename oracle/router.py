@@ -24,6 +24,7 @@ class RouteResult:
     weights: torch.Tensor      # [T, k] in the hidden dtype (bf16 on the layer path)
     choice: torch.Tensor       # fp32 [T, E] selection scores after bias + group mask
     weights_f32: torch.Tensor  # fp32 [T, k] before the final dtype cast
+    group_gap: torch.Tensor | None = None  # fp32 [T]: kept-group boundary margin (None: no groups)
 
 
 def group_mask(choice: torch.Tensor, n_groups: int, topk_groups: int, use_bias: bool) -> torch.Tensor:
@@ -64,7 +65,9 @@ def route_deepseek(
         probs = logits.sigmoid()
     bias_f = None if bias is None else bias.detach().cpu().float()
     choice = probs + bias_f if bias_f is not None else probs
+    group_gap = None
     if n_groups > 1:
+        group_gap = _group_boundary_gap(choice, n_groups, topk_groups, bias_f is not None)
         choice = group_mask(choice, n_groups, topk_groups, bias_f is not None)
     k = max(1, min(int(top_k), int(choice.shape[-1])))
     ids = torch.topk(choice, k, dim=-1)[1]
@@ -72,7 +75,19 @@ def route_deepseek(
     if scoring_func == "sigmoid":
         picked = picked / picked.sum(dim=-1, keepdim=True).clamp_min(1e-12)
     scaled = picked * float(route_scale)
-    return RouteResult(ids=ids, weights=scaled.to(dtype=hidden.dtype), choice=choice, weights_f32=scaled)
+    return RouteResult(ids=ids, weights=scaled.to(dtype=hidden.dtype), choice=choice, weights_f32=scaled,
+                       group_gap=group_gap)
+
+
+def _group_boundary_gap(choice: torch.Tensor, n_groups: int, topk_groups: int, use_bias: bool) -> torch.Tensor:
+    """Margin between the last kept group's score and the best dropped one."""
+    grouped = choice.view(int(choice.shape[0]), int(n_groups), -1)
+    score = grouped.topk(2, dim=-1)[0].sum(dim=-1) if use_bias else grouped.amax(dim=-1)
+    kg = max(1, min(int(topk_groups), int(n_groups)))
+    if kg >= n_groups:
+        return torch.full((int(choice.shape[0]),), float("inf"))
+    top = score.topk(kg + 1, dim=-1)[0]
+    return top[:, kg - 1] - top[:, kg]
 
 
 def route_softmax_topk(hidden: torch.Tensor, router_weight: torch.Tensor, *, top_k: int,

@@ -1,0 +1,763 @@
+// extern "C" entry points of libmoe_b200.so (declared in include/moe_b200.h).
+//
+// Each function validates its arguments the way the reference C function it
+// replaces does (same return codes for null pointers and bad dimensions),
+// plans its scratch memory, and enqueues the kernels on the caller's stream.
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "../../include/moe_b200.h"
+#include "common.cuh"
+#include "dequant.cuh"
+#include "dispatch.cuh"
+#include "fp8_gemv.cuh"
+#include "router.cuh"
+
+using namespace moe;
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* what) {
+  std::snprintf(g_last_error, sizeof g_last_error, "%s", what);
+  return code;
+}
+
+int cuda_fail(cudaError_t err, const char* where) {
+  std::snprintf(g_last_error, sizeof g_last_error, "%s: %s", where, cudaGetErrorString(err));
+  return kCudaError - static_cast<int>(err);
+}
+
+#define MOE_CUDA(expr, where)                 \
+  do {                                        \
+    cudaError_t _e = (expr);                  \
+    if (_e != cudaSuccess) return cuda_fail(_e, where); \
+  } while (0)
+
+// Bump allocator over one workspace block; sizes round up to 256 bytes.
+class Plan {
+ public:
+  explicit Plan(char* base = nullptr) : base_(base) {}
+  template <typename T>
+  T* take(int64_t count) {
+    const size_t bytes = (static_cast<size_t>(count > 0 ? count : 1) * sizeof(T) + 255) & ~size_t(255);
+    T* p = base_ ? reinterpret_cast<T*>(base_ + used_) : nullptr;
+    used_ += bytes;
+    return p;
+  }
+  size_t used() const { return used_; }
+
+ private:
+  char* base_;
+  size_t used_ = 0;
+};
+
+// Either the caller's workspace or a stream-ordered allocation freed at scope end.
+class Scratch {
+ public:
+  Scratch(void* workspace, int64_t bytes, size_t need, cudaStream_t stream) : stream_(stream) {
+    if (workspace) {
+      ok_ = bytes >= static_cast<int64_t>(need);
+      base_ = static_cast<char*>(workspace);
+    } else {
+      ok_ = cudaMallocAsync(reinterpret_cast<void**>(&base_), need > 0 ? need : 256, stream) == cudaSuccess;
+      owned_ = ok_;
+    }
+  }
+  ~Scratch() {
+    if (owned_) cudaFreeAsync(base_, stream_);
+  }
+  bool ok() const { return ok_; }
+  char* base() const { return base_; }
+
+ private:
+  cudaStream_t stream_;
+  char* base_ = nullptr;
+  bool ok_ = false;
+  bool owned_ = false;
+};
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Optional stage timing of the fused layer (moe_b200_stage_timing): CUDA events
+// recorded on the launching stream between the layer's kernels.
+constexpr int kMaxStageEvents = 8;
+bool g_timing = false;
+cudaEvent_t g_events[kMaxStageEvents] = {};
+int g_marks = 0;
+
+void stage_mark(cudaStream_t stream) {
+  if (!g_timing || g_marks >= kMaxStageEvents) return;
+  cudaEventRecord(g_events[g_marks++], stream);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Scratch of the grouped FP8 MLP: pairs, chunk list, activations and outputs.
+struct MlpScratch {
+  int32_t* seg_offset;
+  int32_t* pair_row;
+  float* pair_weight;
+  int32_t* pair_entry;
+  int32_t* entry_pair;
+  int32_t* chunk_seg;
+  int32_t* chunk_start;
+  int32_t* chunk_len;
+  int32_t* n_chunks;
+  int32_t* keys;
+  int32_t* entry_row;
+  float* entry_weight;
+  float* act;
+  float* y;
+};
+
+MlpScratch plan_mlp(Plan& plan, int64_t pairs, int64_t segments, int64_t entries, int64_t inter,
+                    int64_t hidden, int nt, bool need_y) {
+  MlpScratch s{};
+  s.seg_offset = plan.take<int32_t>(segments + 2);
+  s.pair_row = plan.take<int32_t>(pairs);
+  s.pair_weight = plan.take<float>(pairs);
+  s.pair_entry = plan.take<int32_t>(pairs);
+  s.entry_pair = plan.take<int32_t>(entries);
+  const int64_t cap = chunk_capacity(pairs, segments + 1, nt);
+  s.chunk_seg = plan.take<int32_t>(cap);
+  s.chunk_start = plan.take<int32_t>(cap);
+  s.chunk_len = plan.take<int32_t>(cap);
+  s.n_chunks = plan.take<int32_t>(1);
+  s.keys = plan.take<int32_t>(entries);
+  s.entry_row = plan.take<int32_t>(entries);
+  s.entry_weight = plan.take<float>(entries);
+  s.act = plan.take<float>(pairs * inter);
+  s.y = need_y ? plan.take<float>(pairs * hidden) : nullptr;
+  return s;
+}
+
+struct Tables {
+  const uint64_t *gw, *gs, *uw, *us, *dw, *ds;
+};
+
+// gate/up + SwiGLU then down for every pair: act -> y (fp32 [P, H]).
+int run_expert_stages(const Tables& t, const void* x, int x_dtype, const MlpScratch& s, float* y,
+                      int64_t n_segments, int64_t inter, int64_t hidden, int64_t gsc, int64_t dsc, int nt,
+                      bool vec, cudaStream_t stream) {
+  ChunkArgs ca{s.seg_offset, static_cast<int>(n_segments), nt, s.chunk_seg, s.chunk_start, s.chunk_len, s.n_chunks};
+  MOE_CUDA(launch_chunks(ca, stream), "chunk list");
+  GemvArgs g1{};
+  g1.w0 = t.gw; g1.s0 = t.gs; g1.w1 = t.uw; g1.s1 = t.us;
+  g1.x = x; g1.pair_row = s.pair_row;
+  g1.chunk_seg = s.chunk_seg; g1.chunk_start = s.chunk_start; g1.chunk_len = s.chunk_len; g1.n_chunks = s.n_chunks;
+  g1.out0 = s.act; g1.N = static_cast<int>(inter); g1.K = static_cast<int>(hidden); g1.scale_cols = static_cast<int>(gsc);
+  stage_mark(stream);
+  MOE_CUDA(launch_grouped_gemv(g1, x_dtype, 2, kEpiSwiglu, nt, vec, stream), "gate/up stage");
+  stage_mark(stream);
+  const int nt2 = std::min(nt, gemv_chunk_tokens(static_cast<int>(inter), kXF32));
+  if (nt2 != nt) {
+    // the down stage walks the same chunks; it needs the same chunk size
+    return fail(kUnsupported, "intermediate size too large for the staged down projection");
+  }
+  GemvArgs g2 = g1;
+  g2.w0 = t.dw; g2.s0 = t.ds; g2.w1 = nullptr; g2.s1 = nullptr;
+  g2.x = s.act; g2.pair_row = nullptr; g2.out0 = y;
+  g2.N = static_cast<int>(hidden); g2.K = static_cast<int>(inter); g2.scale_cols = static_cast<int>(dsc);
+  const bool vec2 = vec && (inter % 16 == 0);
+  MOE_CUDA(launch_grouped_gemv(g2, kXF32, 1, kEpiStore, nt, vec2, stream), "down stage");
+  stage_mark(stream);
+  return kOk;
+}
+
+int pick_nt(int64_t max_rows_per_segment, int64_t K1, int64_t K2, int x_dtype) {
+  int cap = std::min(gemv_chunk_tokens(static_cast<int>(K1), x_dtype), gemv_chunk_tokens(static_cast<int>(K2), kXF32));
+  if (cap <= 0) return 0;
+  int nt = max_rows_per_segment <= 1 ? 1 : (max_rows_per_segment <= 4 ? 4 : 8);
+  while (nt > cap) nt = nt == 8 ? 4 : 1;
+  return nt;
+}
+
+// Entries of the many / weighted / row-weighted calls: entry i = (item i / B,
+// row i % B).  mode 0: weight 1; mode 1: route[item]; mode 2: route[i], and a
+// zero weight drops the entry (the reference skips that work, fp8_linear.cpp:753-755).
+__global__ void fill_entries_kernel(int32_t* keys, int32_t* rows, float* weights, int64_t n, int64_t B, int mode,
+                                    const float* route) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t item = i / B;
+    float w = 1.0f;
+    if (mode == 1) w = route[item];
+    if (mode == 2) w = route[i];
+    keys[i] = (mode == 2 && w == 0.0f) ? -1 : static_cast<int32_t>(item);
+    rows[i] = static_cast<int32_t>(i % B);
+    weights[i] = w;
+  }
+}
+
+// entry_pair [E, B] (item-major) -> row_pairs [B, E]
+__global__ void transpose_entries_kernel(const int32_t* entry_pair, int32_t* row_pairs, int64_t E, int64_t B) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < E * B;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = i / B, b = i % B;
+    row_pairs[b * E + e] = entry_pair[i];
+  }
+}
+
+// pair index of each listed entry (in place allowed)
+__global__ void map_entries_kernel(const int32_t* entries, const int32_t* entry_pair, int32_t* out, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t e = entries[i];
+    out[i] = e >= 0 ? entry_pair[e] : -1;
+  }
+}
+
+__global__ void i64_to_i32_kernel(const int64_t* in, int32_t* out, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = static_cast<int32_t>(in[i]);
+}
+
+__global__ void validate_pairs_kernel(const int64_t* item, const int64_t* row, int64_t n, int64_t items,
+                                      int64_t rows, int32_t* bad) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    if (item[i] < 0 || item[i] >= items || row[i] < 0 || row[i] >= rows) atomicExch(bad, 1);
+}
+
+unsigned grid_for(int64_t n, int threads = 256) {
+  return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, threads), 4096)));
+}
+
+// Shared body of the many / weighted / row-weighted MLP entry points.
+// Entry i = (item i / batch, row i % batch) in item-major order; every row's
+// combine then walks its entries in item order, as the reference sums them.
+int mlp_items(const Tables& t, const float* hidden, const float* route, int route_mode, float* out,
+              bool per_expert_out, int64_t E, int64_t B, int64_t I, int64_t H, int64_t gsc, int64_t dsc,
+              void* workspace, int64_t ws_bytes, cudaStream_t stream) {
+  const int64_t entries = E * B;
+  const int nt = pick_nt(B, H, I, kXF32);
+  if (nt == 0) return fail(kUnsupported, "hidden/intermediate size too large for the staged GEMV");
+  Plan sizing;
+  plan_mlp(sizing, entries, E, entries, I, H, nt, !per_expert_out);
+  Scratch scratch(workspace, ws_bytes, sizing.used(), stream);
+  if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
+  Plan plan(scratch.base());
+  MlpScratch s = plan_mlp(plan, entries, E, entries, I, H, nt, !per_expert_out);
+  fill_entries_kernel<<<grid_for(entries), 256, 0, stream>>>(s.keys, s.entry_row, s.entry_weight, entries, B,
+                                                               route ? (route_mode == 1 ? 2 : 1) : 0, route);
+  MOE_CUDA(cudaGetLastError(), "entries");
+  BucketArgs ba{};
+  ba.keys = s.keys; ba.rows = s.entry_row; ba.weights = s.entry_weight;
+  ba.n = static_cast<int>(entries); ba.k = 1; ba.key_lo = 0; ba.n_buckets = static_cast<int>(E);
+  ba.bucket_offset = s.seg_offset; ba.pair_row = s.pair_row; ba.pair_weight = s.pair_weight;
+  ba.pair_entry = s.pair_entry; ba.entry_pair = s.entry_pair;
+  MOE_CUDA(launch_bucket(ba, stream), "bucket");
+  const bool vec = H % 16 == 0 && I % 16 == 0 && aligned16(hidden);
+  float* y = per_expert_out ? out : s.y;
+  int code = run_expert_stages(t, hidden, kXF32, s, y, E, I, H, gsc, dsc, nt, vec, stream);
+  if (code != kOk) return code;
+  if (!per_expert_out) {
+    // row b's entries are e * B + b for e in item order: stride-1 lists via row_ptr = null,
+    // built as a transposed view of entry_pair
+    CombineArgs c{};
+    c.y = s.y;
+    c.row_ptr = nullptr;
+    c.stride = static_cast<int>(E);
+    int32_t* row_pairs = s.keys;  // reuse: [B, E]
+    transpose_entries_kernel<<<grid_for(entries), 256, 0, stream>>>(s.entry_pair, row_pairs, E, B);
+    MOE_CUDA(cudaGetLastError(), "row lists");
+    c.row_pairs = row_pairs;
+    c.pair_weight = s.pair_weight;
+    c.extra_base = -1;
+    c.T = static_cast<int>(B);
+    c.H = static_cast<int>(H);
+    c.out_f32 = out;
+    MOE_CUDA(launch_combine(c, stream), "combine");
+  }
+  return kOk;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_b200_abi_version(void) { return MOE_B200_ABI_VERSION; }
+
+const char* moe_b200_last_error(void) { return g_last_error; }
+
+// ---------------------------------------------------------------------------
+// FP8 linears
+// ---------------------------------------------------------------------------
+
+static int linear_common(const uint8_t* wa, const float* sa, const uint8_t* wb, const float* sb, const float* x,
+                         float* oa, float* ob, int64_t batch, int64_t rows, int64_t cols, int64_t scols,
+                         cudaStream_t stream) {
+  if (batch <= 0 || rows <= 0 || cols <= 0 || scols <= 0) return fail(kBadDims, "bad dimensions");
+  if (scols != ceil_div(cols, kBlock)) return fail(kBadDims, "scale_cols != ceil(in_cols / 128)");
+  const bool dual = wb != nullptr;
+  const int nt = pick_nt(batch, cols, 16, kXF32);
+  if (nt == 0) return fail(kUnsupported, "in_cols too large for the staged GEMV");
+  // one segment holding every row of `hidden`
+  Plan sizing;
+  const int64_t cap = chunk_capacity(batch, 1, nt);
+  sizing.take<uint64_t>(4);
+  sizing.take<int32_t>(3);
+  sizing.take<int32_t>(cap * 3 + 1);
+  Scratch scratch(nullptr, 0, sizing.used(), stream);
+  if (!scratch.ok()) return fail(kNoMemory, "allocation failed");
+  Plan plan(scratch.base());
+  uint64_t* tab = plan.take<uint64_t>(4);
+  int32_t* seg = plan.take<int32_t>(3);
+  int32_t* chunks = plan.take<int32_t>(cap * 3 + 1);
+  const uint64_t host_tab[4] = {reinterpret_cast<uint64_t>(wa), reinterpret_cast<uint64_t>(sa),
+                                reinterpret_cast<uint64_t>(wb), reinterpret_cast<uint64_t>(sb)};
+  const int32_t host_seg[3] = {0, static_cast<int32_t>(batch), 0};
+  MOE_CUDA(cudaMemcpyAsync(tab, host_tab, sizeof host_tab, cudaMemcpyHostToDevice, stream), "tables");
+  MOE_CUDA(cudaMemcpyAsync(seg, host_seg, sizeof host_seg, cudaMemcpyHostToDevice, stream), "segments");
+  ChunkArgs ca{seg, 1, nt, chunks, chunks + cap, chunks + 2 * cap, chunks + 3 * cap};
+  MOE_CUDA(launch_chunks(ca, stream), "chunk list");
+  GemvArgs g{};
+  g.w0 = tab; g.s0 = tab + 1; g.w1 = tab + 2; g.s1 = tab + 3;
+  g.x = x; g.pair_row = nullptr;
+  g.chunk_seg = ca.chunk_seg; g.chunk_start = ca.chunk_start; g.chunk_len = ca.chunk_len; g.n_chunks = ca.n_chunks;
+  g.out0 = oa; g.out1 = ob; g.N = static_cast<int>(rows); g.K = static_cast<int>(cols); g.scale_cols = static_cast<int>(scols);
+  const bool vec = cols % 16 == 0 && aligned16(x) && aligned16(wa) && (!dual || aligned16(wb));
+  MOE_CUDA(launch_grouped_gemv(g, kXF32, dual ? 2 : 1, dual ? kEpiStoreBoth : kEpiStore, nt, vec, stream),
+           "linear");
+  return kOk;
+}
+
+int moe_fp8_e4m3_block_linear_f32(const uint8_t* fp8_weight, const float* scale_inv, const float* hidden,
+                                  float* out, int64_t batch, int64_t out_rows, int64_t in_cols,
+                                  int64_t scale_cols, void* stream) {
+  if (!fp8_weight || !scale_inv || !hidden || !out) return fail(kNullPointer, "null pointer");
+  return linear_common(fp8_weight, scale_inv, nullptr, nullptr, hidden, out, nullptr, batch, out_rows, in_cols,
+                       scale_cols, as_stream(stream));
+}
+
+int moe_fp8_e4m3_block_dual_linear_f32(const uint8_t* wa, const float* sa, const uint8_t* wb, const float* sb,
+                                       const float* hidden, float* out_a, float* out_b, int64_t batch,
+                                       int64_t out_rows, int64_t in_cols, int64_t scale_cols, void* stream) {
+  if (!wa || !sa || !wb || !sb || !hidden || !out_a || !out_b) return fail(kNullPointer, "null pointer");
+  return linear_common(wa, sa, wb, sb, hidden, out_a, out_b, batch, out_rows, in_cols, scale_cols,
+                       as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------
+// FP8 expert MLPs
+// ---------------------------------------------------------------------------
+
+static int check_mlp_dims(int64_t E, int64_t B, int64_t I, int64_t H, int64_t gsc, int64_t dsc) {
+  if (E <= 0 || B <= 0 || I <= 0 || H <= 0 || gsc <= 0 || dsc <= 0) return fail(kBadDims, "bad dimensions");
+  if (gsc != ceil_div(H, kBlock) || dsc != ceil_div(I, kBlock))
+    return fail(kBadDims, "scale columns do not match the 128x128 block layout");
+  if (E > kMaxBuckets) return fail(kUnsupported, "too many experts in one call");
+  if (E * B > (int64_t(1) << 30)) return fail(kUnsupported, "too many (expert, row) pairs");
+  return kOk;
+}
+
+int64_t moe_fp8_mlp_workspace_bytes(int64_t pairs, int64_t segments, int64_t batch, int64_t I, int64_t H) {
+  Plan p;
+  plan_mlp(p, pairs, segments, std::max(pairs, segments * batch), I, H, 1, true);
+  p.take<uint64_t>(6 * segments);
+  return static_cast<int64_t>(p.used());
+}
+
+int moe_fp8_e4m3_block_mlp_f32(const uint8_t* gate_weight, const float* gate_scale_inv, const uint8_t* up_weight,
+                               const float* up_scale_inv, const uint8_t* down_weight, const float* down_scale_inv,
+                               const float* hidden, float* out, int64_t batch, int64_t I, int64_t H,
+                               int64_t gsc, int64_t dsc, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!gate_weight || !gate_scale_inv || !up_weight || !up_scale_inv || !down_weight || !down_scale_inv ||
+      !hidden || !out)
+    return fail(kNullPointer, "null pointer");
+  int code = check_mlp_dims(1, batch, I, H, gsc, dsc);
+  if (code != kOk) return code;
+  cudaStream_t s = as_stream(stream);
+  // a one-entry device table of the six pointers, then the many_f32 path (E = 1: out is [1, B, H])
+  uint64_t* tab = nullptr;
+  MOE_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&tab), 6 * sizeof(uint64_t), s), "table alloc");
+  const uint64_t host[6] = {reinterpret_cast<uint64_t>(gate_weight), reinterpret_cast<uint64_t>(gate_scale_inv),
+                            reinterpret_cast<uint64_t>(up_weight),   reinterpret_cast<uint64_t>(up_scale_inv),
+                            reinterpret_cast<uint64_t>(down_weight), reinterpret_cast<uint64_t>(down_scale_inv)};
+  cudaError_t err = cudaMemcpyAsync(tab, host, sizeof host, cudaMemcpyHostToDevice, s);
+  if (err != cudaSuccess) {
+    cudaFreeAsync(tab, s);
+    return cuda_fail(err, "table copy");
+  }
+  Tables t{tab, tab + 1, tab + 2, tab + 3, tab + 4, tab + 5};
+  code = mlp_items(t, hidden, nullptr, 0, out, true, 1, batch, I, H, gsc, dsc, workspace, workspace_bytes, s);
+  cudaFreeAsync(tab, s);
+  return code;
+}
+
+#define MOE_TABLES_OK(g, gs, u, us, d, ds) ((g) && (gs) && (u) && (us) && (d) && (ds))
+
+int moe_fp8_e4m3_block_mlp_many_f32(const uint64_t* gw, const uint64_t* gs, const uint64_t* uw, const uint64_t* us,
+                                    const uint64_t* dw, const uint64_t* ds, const float* hidden, float* out,
+                                    int64_t E, int64_t B, int64_t I, int64_t H, int64_t gsc, int64_t dsc,
+                                    void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!MOE_TABLES_OK(gw, gs, uw, us, dw, ds) || !hidden || !out) return fail(kNullPointer, "null pointer");
+  int code = check_mlp_dims(E, B, I, H, gsc, dsc);
+  if (code != kOk) return code;
+  Tables t{gw, gs, uw, us, dw, ds};
+  return mlp_items(t, hidden, nullptr, 0, out, true, E, B, I, H, gsc, dsc, workspace, workspace_bytes,
+                   as_stream(stream));
+}
+
+int moe_fp8_e4m3_block_mlp_many_weighted_f32(const uint64_t* gw, const uint64_t* gs, const uint64_t* uw,
+                                             const uint64_t* us, const uint64_t* dw, const uint64_t* ds,
+                                             const float* hidden, const float* route, float* out, int64_t E,
+                                             int64_t B, int64_t I, int64_t H, int64_t gsc, int64_t dsc,
+                                             void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!MOE_TABLES_OK(gw, gs, uw, us, dw, ds) || !hidden || !route || !out) return fail(kNullPointer, "null pointer");
+  int code = check_mlp_dims(E, B, I, H, gsc, dsc);
+  if (code != kOk) return code;
+  Tables t{gw, gs, uw, us, dw, ds};
+  return mlp_items(t, hidden, route, 0, out, false, E, B, I, H, gsc, dsc, workspace, workspace_bytes,
+                   as_stream(stream));
+}
+
+int moe_fp8_e4m3_block_mlp_many_row_weighted_f32(const uint64_t* gw, const uint64_t* gs, const uint64_t* uw,
+                                                 const uint64_t* us, const uint64_t* dw, const uint64_t* ds,
+                                                 const float* hidden, const float* route, float* out, int64_t E,
+                                                 int64_t B, int64_t I, int64_t H, int64_t gsc, int64_t dsc,
+                                                 void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!MOE_TABLES_OK(gw, gs, uw, us, dw, ds) || !hidden || !route || !out) return fail(kNullPointer, "null pointer");
+  int code = check_mlp_dims(E, B, I, H, gsc, dsc);
+  if (code != kOk) return code;
+  Tables t{gw, gs, uw, us, dw, ds};
+  return mlp_items(t, hidden, route, 1, out, false, E, B, I, H, gsc, dsc, workspace, workspace_bytes,
+                   as_stream(stream));
+}
+
+int moe_fp8_e4m3_block_mlp_many_pair_weighted_f32(const uint64_t* gw, const uint64_t* gs, const uint64_t* uw,
+                                                  const uint64_t* us, const uint64_t* dw, const uint64_t* ds,
+                                                  const float* hidden, const int64_t* pair_item,
+                                                  const int64_t* pair_row, const float* pair_w, float* out,
+                                                  int64_t E, int64_t P, int64_t B, int64_t I, int64_t H,
+                                                  int64_t gsc, int64_t dsc, void* workspace,
+                                                  int64_t workspace_bytes, void* stream) {
+  if (!MOE_TABLES_OK(gw, gs, uw, us, dw, ds) || !hidden || !pair_item || !pair_row || !pair_w || !out)
+    return fail(kNullPointer, "null pointer");
+  if (P < 0) return fail(kBadDims, "bad dimensions");
+  int code = check_mlp_dims(E, B, I, H, gsc, dsc);
+  if (code != kOk) return code;
+  if (B > kMaxBuckets) return fail(kUnsupported, "batch too large for the pair combine");
+  cudaStream_t s = as_stream(stream);
+  MOE_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(B * H) * sizeof(float), s), "clear out");
+  if (P == 0) return kOk;
+  const int nt = pick_nt(P, H, I, kXF32);
+  if (nt == 0) return fail(kUnsupported, "hidden/intermediate size too large for the staged GEMV");
+  Plan sizing;
+  plan_mlp(sizing, P, E, P, I, H, nt, true);
+  sizing.take<int32_t>(P);           // rows32
+  sizing.take<int32_t>(B + 2);       // row_ptr
+  sizing.take<int32_t>(P);           // row_pairs (pair entry order per row)
+  sizing.take<int32_t>(P);           // row pair rows (unused)
+  sizing.take<int32_t>(1);           // bad flag
+  Scratch scratch(workspace, workspace_bytes, sizing.used(), s);
+  if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
+  Plan plan(scratch.base());
+  MlpScratch m = plan_mlp(plan, P, E, P, I, H, nt, true);
+  int32_t* rows32 = plan.take<int32_t>(P);
+  int32_t* row_ptr = plan.take<int32_t>(B + 2);
+  int32_t* row_entries = plan.take<int32_t>(P);
+  int32_t* row_rows = plan.take<int32_t>(P);
+  int32_t* bad = plan.take<int32_t>(1);
+  // reject out-of-range indices (fp8_linear.cpp:873-880 returns -4)
+  MOE_CUDA(cudaMemsetAsync(bad, 0, sizeof(int32_t), s), "clear flag");
+  validate_pairs_kernel<<<grid_for(P), 256, 0, s>>>(pair_item, pair_row, P, E, B, bad);
+  int32_t host_bad = 0;
+  MOE_CUDA(cudaMemcpyAsync(&host_bad, bad, sizeof host_bad, cudaMemcpyDeviceToHost, s), "flag copy");
+  MOE_CUDA(cudaStreamSynchronize(s), "flag sync");
+  if (host_bad) return fail(kBadIndex, "pair index out of range");
+  i64_to_i32_kernel<<<grid_for(P), 256, 0, s>>>(pair_item, m.keys, P);
+  i64_to_i32_kernel<<<grid_for(P), 256, 0, s>>>(pair_row, rows32, P);
+  MOE_CUDA(cudaGetLastError(), "index copy");
+  BucketArgs ba{};
+  ba.keys = m.keys; ba.rows = rows32; ba.weights = pair_w; ba.n = static_cast<int>(P); ba.k = 1;
+  ba.key_lo = 0; ba.n_buckets = static_cast<int>(E);
+  ba.bucket_offset = m.seg_offset; ba.pair_row = m.pair_row; ba.pair_weight = m.pair_weight;
+  ba.pair_entry = m.pair_entry; ba.entry_pair = m.entry_pair;
+  MOE_CUDA(launch_bucket(ba, s), "bucket by item");
+  Tables t{gw, gs, uw, us, dw, ds};
+  const bool vec = H % 16 == 0 && I % 16 == 0 && aligned16(hidden);
+  code = run_expert_stages(t, hidden, kXF32, m, m.y, E, I, H, gsc, dsc, nt, vec, s);
+  if (code != kOk) return code;
+  // per-row lists in pair order: bucket the entries by row, then map entry -> pair
+  BucketArgs br{};
+  br.keys = rows32; br.rows = nullptr; br.weights = nullptr; br.n = static_cast<int>(P); br.k = 1;
+  br.key_lo = 0; br.n_buckets = static_cast<int>(B);
+  br.bucket_offset = row_ptr; br.pair_row = row_rows; br.pair_entry = row_entries;
+  MOE_CUDA(launch_bucket(br, s), "bucket by row");
+  map_entries_kernel<<<grid_for(P), 256, 0, s>>>(row_entries, m.entry_pair, row_entries, P);
+  MOE_CUDA(cudaGetLastError(), "row lists");
+  CombineArgs c{};
+  c.y = m.y; c.row_ptr = row_ptr; c.stride = 0; c.row_pairs = row_entries; c.pair_weight = m.pair_weight;
+  c.extra_base = -1; c.T = static_cast<int>(B); c.H = static_cast<int>(H); c.out_f32 = out;
+  MOE_CUDA(launch_combine(c, s), "combine");
+  return kOk;
+}
+
+// ---------------------------------------------------------------------------
+// Dequant
+// ---------------------------------------------------------------------------
+
+static int dequant_common(const uint8_t* w, const float* s, uint16_t* out, int64_t rows, int64_t cols,
+                          int64_t scols, bool bf16, void* stream) {
+  if (!w || !s || !out) return fail(kNullPointer, "null pointer");
+  if (rows <= 0 || cols <= 0 || scols <= 0) return fail(kBadDims, "bad dimensions");
+  if (scols != ceil_div(cols, kBlock)) return fail(-3, "scale_cols != ceil(cols / 128)");  // fp8_dequant.cpp:133-136
+  MOE_CUDA(launch_fp8_dequant(w, s, out, rows, cols, scols, bf16, as_stream(stream)), "dequant");
+  return kOk;
+}
+
+int moe_fp8_e4m3_dequant_to_fp16(const uint8_t* w, const float* s, uint16_t* out, int64_t rows, int64_t cols,
+                                 int64_t scols, void* stream) {
+  return dequant_common(w, s, out, rows, cols, scols, false, stream);
+}
+
+int moe_fp8_e4m3_dequant_to_bf16(const uint8_t* w, const float* s, uint16_t* out, int64_t rows, int64_t cols,
+                                 int64_t scols, void* stream) {
+  return dequant_common(w, s, out, rows, cols, scols, true, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Routers
+// ---------------------------------------------------------------------------
+
+int64_t moe_route_topk_workspace_bytes(int64_t tokens, int64_t experts) {
+  Plan p;
+  p.take<float>(tokens * experts);
+  return static_cast<int64_t>(p.used());
+}
+
+static int route_impl(const void* hidden, int hd, const void* w, int wd, const float* bias, int64_t T, int64_t H,
+                      int64_t E, int64_t n_group, int64_t topk_group, int64_t k, int scoring, int renorm,
+                      int fp64, float scale, int round_bf16, int64_t* ids64, int32_t* ids32, float* wf32,
+                      uint16_t* wbf16, float* logits, cudaStream_t stream) {
+  MOE_CUDA(launch_router_logits(hidden, hd, w, wd, logits, static_cast<int>(T), static_cast<int>(H),
+                                static_cast<int>(E), stream),
+           "router logits");
+  RouterSelectParams p{};
+  p.tokens = static_cast<int>(T);
+  p.experts = static_cast<int>(E);
+  p.top_k = static_cast<int>(k);
+  p.n_group = static_cast<int>(n_group);
+  p.topk_group = static_cast<int>(topk_group);
+  p.scoring = scoring;
+  p.renorm = renorm || scoring == kScoreSigmoid;
+  p.softmax_fp64 = fp64;
+  p.round_bf16 = round_bf16;
+  p.route_scale = scale;
+  MOE_CUDA(launch_router_select(logits, bias, p, ids64, ids32, wf32, reinterpret_cast<__nv_bfloat16*>(wbf16),
+                                stream),
+           "router select");
+  return kOk;
+}
+
+static int check_route(int64_t T, int64_t H, int64_t E, int64_t n_group, int64_t topk_group, int64_t k) {
+  if (T <= 0 || H <= 0 || E <= 0 || k <= 0 || k > E) return fail(kBadDims, "bad dimensions");
+  if (k > 32) return fail(kUnsupported, "top_k > 32");
+  if (E > 2048) return fail(kUnsupported, "more than 2048 experts");
+  if (n_group < 1 || n_group > 32 || E % n_group != 0) return fail(kBadDims, "n_group must divide num_experts (<= 32)");
+  if (topk_group < 1) return fail(kBadDims, "topk_group < 1");
+  return kOk;
+}
+
+int moe_route_topk(const void* hidden, int hidden_dtype, const void* router_weight, int router_dtype,
+                   const float* bias, int64_t T, int64_t H, int64_t E, int64_t n_group, int64_t topk_group,
+                   int64_t k, int scoring, int renorm, float route_scale, int round_bf16, int64_t* out_ids,
+                   float* out_weights_f32, uint16_t* out_weights_bf16, void* workspace, int64_t workspace_bytes,
+                   void* stream) {
+  if (!hidden || !router_weight) return fail(kNullPointer, "null pointer");
+  int code = check_route(T, H, E, n_group, topk_group, k);
+  if (code != kOk) return code;
+  cudaStream_t s = as_stream(stream);
+  Scratch scratch(workspace, workspace_bytes, moe_route_topk_workspace_bytes(T, E), s);
+  if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
+  return route_impl(hidden, hidden_dtype, router_weight, router_dtype, bias, T, H, E, n_group, topk_group, k,
+                    scoring, renorm, 0, route_scale, round_bf16, out_ids, nullptr, out_weights_f32,
+                    out_weights_bf16, reinterpret_cast<float*>(scratch.base()), s);
+}
+
+int moe_ds_router_topk_u16(const uint16_t* hidden_u16, const uint16_t* router_u16, int64_t H, int64_t E,
+                           int64_t k, int64_t dtype_code, int64_t* out_ids, float* out_weights, void* stream) {
+  if (!hidden_u16 || !router_u16 || !out_ids || !out_weights) return 1;       // ds_forward.cpp:889-894
+  if (H <= 0 || E <= 0 || k <= 0 || k > E) return 2;                          // :895-897
+  if (k > 32 || E > 2048) return fail(kUnsupported, "k > 32 or more than 2048 experts");
+  cudaStream_t s = as_stream(stream);
+  Scratch scratch(nullptr, 0, moe_route_topk_workspace_bytes(1, E), s);
+  if (!scratch.ok()) return fail(kNoMemory, "allocation failed");
+  const int dt = dtype_code == 1 ? kDtypeBF16 : kDtypeF16;
+  return route_impl(hidden_u16, dt, router_u16, dt, nullptr, 1, H, E, 1, 1, k, kScoreSoftmax, 1, 1, 1.0f, 0,
+                    out_ids, nullptr, out_weights, nullptr, reinterpret_cast<float*>(scratch.base()), s);
+}
+
+// ---------------------------------------------------------------------------
+// Whole DeepSeek-V3 layer
+// ---------------------------------------------------------------------------
+
+struct LayerPlan {
+  float* logits;
+  int32_t* ids32;
+  float* wts;
+  MlpScratch m;
+};
+
+static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, int shared, int nt) {
+  LayerPlan l{};
+  l.logits = p.take<float>(T * E);
+  l.ids32 = p.take<int32_t>(T * k);
+  l.wts = p.take<float>(T * k);
+  const int64_t pairs = T * k + (shared ? T : 0);
+  l.m = plan_mlp(p, pairs, E + 1, T * k, I, H, nt, true);
+  return l;
+}
+
+int64_t moe_ds_moe_layer_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, int shared) {
+  Plan p;
+  plan_layer(p, T, H, I, E, k, shared, 1);
+  return static_cast<int64_t>(p.used());
+}
+
+int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_t H, int64_t I,
+                         const void* router_weight, int router_dtype, const float* router_bias, int64_t E,
+                         int64_t n_group, int64_t topk_group, int64_t k, int scoring, float route_scale,
+                         const uint64_t* tables, int has_shared, uint16_t* out_bf16, int64_t* out_ids,
+                         uint16_t* out_weights_bf16, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!hidden || !router_weight || !tables || !out_bf16) return fail(kNullPointer, "null pointer");
+  int code = check_route(T, H, E, n_group, topk_group, k);
+  if (code != kOk) return code;
+  if (I <= 0) return fail(kBadDims, "bad dimensions");
+  if (hidden_dtype != kDtypeBF16 && hidden_dtype != kDtypeF32) return fail(kUnsupported, "hidden must be bf16 or fp32");
+  if (E + 1 > kMaxBuckets) return fail(kUnsupported, "too many experts");
+  const int xd = hidden_dtype == kDtypeBF16 ? kXBF16 : kXF32;
+  const int nt = pick_nt(T, H, I, xd);
+  if (nt == 0) return fail(kUnsupported, "hidden/intermediate size too large for the staged GEMV");
+  cudaStream_t s = as_stream(stream);
+  Plan sizing;
+  plan_layer(sizing, T, H, I, E, k, has_shared, nt);
+  Scratch scratch(workspace, workspace_bytes, sizing.used(), s);
+  if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
+  Plan plan(scratch.base());
+  LayerPlan l = plan_layer(plan, T, H, I, E, k, has_shared, nt);
+  g_marks = 0;
+  stage_mark(s);
+  // 1. route (weights rounded through bf16 like fp8_source.py:1547 when hidden is bf16)
+  code = route_impl(hidden, hidden_dtype, router_weight, router_dtype, router_bias, T, H, E, n_group, topk_group, k,
+                    scoring, 0, 0, route_scale, hidden_dtype == kDtypeBF16, out_ids, l.ids32, l.wts,
+                    out_weights_bf16, l.logits, s);
+  if (code != kOk) return code;
+  // 2. dispatch: expert-contiguous pairs, ascending token order inside an expert, shared expert last
+  BucketArgs ba{};
+  ba.keys = l.ids32; ba.rows = nullptr; ba.weights = l.wts; ba.n = static_cast<int>(T * k);
+  ba.k = static_cast<int>(k); ba.key_lo = 0; ba.n_buckets = static_cast<int>(E);
+  ba.bucket_offset = l.m.seg_offset; ba.pair_row = l.m.pair_row; ba.pair_weight = l.m.pair_weight;
+  ba.pair_entry = l.m.pair_entry; ba.entry_pair = l.m.entry_pair; ba.tail = has_shared ? static_cast<int>(T) : 0;
+  MOE_CUDA(launch_bucket(ba, s), "dispatch");
+  // 3. experts
+  const int64_t S = E + (has_shared ? 1 : 0);
+  Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
+  const bool vec = H % 16 == 0 && I % 16 == 0 && aligned16(hidden);
+  code = run_expert_stages(t, hidden, xd, l.m, l.m.y, S, I, H, ceil_div(H, kBlock), ceil_div(I, kBlock), nt, vec, s);
+  if (code != kOk) return code;
+  // 4. combine: routed slots in top-k order, then the shared expert; one bf16 rounding
+  CombineArgs c{};
+  c.y = l.m.y; c.row_ptr = nullptr; c.stride = static_cast<int>(k); c.row_pairs = l.m.entry_pair;
+  c.pair_weight = l.m.pair_weight; c.extra_base = has_shared ? static_cast<int>(T * k) : -1;
+  c.T = static_cast<int>(T); c.H = static_cast<int>(H);
+  c.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
+  MOE_CUDA(launch_combine(c, s), "combine");
+  stage_mark(s);
+  return kOk;
+}
+
+// ---------------------------------------------------------------------------
+// Stage timing
+// ---------------------------------------------------------------------------
+
+int moe_b200_stage_timing(int enable) {
+  if (enable && !g_events[0]) {
+    for (auto& e : g_events) MOE_CUDA(cudaEventCreate(&e), "event create");
+  }
+  g_timing = enable != 0;
+  g_marks = 0;
+  return kOk;
+}
+
+int moe_b200_stage_times(float* ms, int max_n) {
+  if (!ms) return fail(kNullPointer, "null pointer");
+  if (g_marks < 2) return 0;
+  MOE_CUDA(cudaEventSynchronize(g_events[g_marks - 1]), "event sync");
+  const int n = std::min(max_n, g_marks - 1);
+  for (int i = 0; i < n; ++i) MOE_CUDA(cudaEventElapsedTime(&ms[i], g_events[i], g_events[i + 1]), "elapsed");
+  return n;
+}
+
+// ---------------------------------------------------------------------------
+// Sessions
+// ---------------------------------------------------------------------------
+
+struct DsSession {
+  int64_t num_layers, hidden_dim, num_experts, top_k;
+  int64_t monolithic_calls = 0;
+  int64_t expert_invocations = 0;
+  int64_t layers_executed = 0;
+};
+
+void* moe_ds_session_create(int64_t num_layers, int64_t hidden_dim, int64_t num_experts, int64_t top_k) {
+  if (num_layers <= 0 || hidden_dim <= 0 || num_experts < 0 || top_k < 0) return nullptr;  // ds_forward.cpp:200-202
+  DsSession* s = new (std::nothrow) DsSession();
+  if (!s) return nullptr;
+  s->num_layers = num_layers;
+  s->hidden_dim = hidden_dim;
+  s->num_experts = num_experts;
+  s->top_k = top_k;
+  return s;
+}
+
+void moe_ds_session_destroy(void* handle) { delete static_cast<DsSession*>(handle); }
+
+int64_t moe_ds_monolithic_call_counter(void* h) { return h ? static_cast<DsSession*>(h)->monolithic_calls : -1; }
+int64_t moe_ds_expert_invocation_count(void* h) { return h ? static_cast<DsSession*>(h)->expert_invocations : -1; }
+int64_t moe_ds_layers_executed_count(void* h) { return h ? static_cast<DsSession*>(h)->layers_executed : -1; }
+
+__global__ void combine_dense_kernel(const float* outputs, const float* route, int64_t E, int64_t width, float* out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < width;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float acc = 0.0f;
+    for (int64_t e = 0; e < E; ++e) acc = fmaf(route[e], outputs[e * width + i], acc);
+    out[i] = acc;
+  }
+}
+
+int moe_ds_moe_layer_forward_f32(void* handle, const float* expert_outputs, const float* route, int64_t E,
+                                 int64_t B, int64_t H, float* out, void* stream) {
+  DsSession* session = static_cast<DsSession*>(handle);
+  if (!session || !expert_outputs || !route || !out) return 1;  // ds_forward.cpp:347-352
+  if (E <= 0 || B <= 0 || H <= 0) return 2;                     // :353-355
+  combine_dense_kernel<<<grid_for(B * H), 256, 0, as_stream(stream)>>>(expert_outputs, route, E, B * H, out);
+  MOE_CUDA(cudaGetLastError(), "combine");
+  session->monolithic_calls += 1;
+  session->expert_invocations += E;
+  return 0;
+}
+
+int moe_ds_moe_layer_forward_fp8_f32(void* handle, const uint64_t* gw, const uint64_t* gs, const uint64_t* uw,
+                                     const uint64_t* us, const uint64_t* dw, const uint64_t* ds,
+                                     const float* hidden, const float* route, int64_t E, int64_t B, int64_t I,
+                                     int64_t H, int64_t gsc, int64_t dsc, float* out, void* workspace,
+                                     int64_t workspace_bytes, void* stream) {
+  DsSession* session = static_cast<DsSession*>(handle);
+  if (!session || !MOE_TABLES_OK(gw, gs, uw, us, dw, ds) || !hidden || !route || !out) return 1;  // :803-809
+  if (E <= 0 || B <= 0 || I <= 0 || H <= 0 || gsc <= 0 || dsc <= 0) return 2;                   // :810-815
+  const int code = moe_fp8_e4m3_block_mlp_many_weighted_f32(gw, gs, uw, us, dw, ds, hidden, route, out, E, B, I, H,
+                                                            gsc, dsc, workspace, workspace_bytes, stream);
+  if (code != 0) return 100 + code;  // :858-860
+  session->monolithic_calls += 1;
+  session->expert_invocations += E;
+  return 0;
+}
+
+}  // extern "C"
+

@@ -1,0 +1,47 @@
+// Dispatch launchers (dispatch.cu).
+#pragma once
+#include "common.cuh"
+
+namespace moe {
+
+constexpr int kMaxBuckets = 1536;  // bitmask window in shared memory: 128 B per bucket
+
+struct BucketArgs {
+  const int32_t* keys;     // [n]
+  const int32_t* rows;     // [n] or null: row = i / k
+  const float* weights;    // [n] or null: weight 1
+  int n;
+  int k;
+  int key_lo;
+  int n_buckets;
+  int32_t* bucket_offset;  // [n_buckets + 1]
+  int32_t* pair_row;       // [total]
+  float* pair_weight;      // [total] or null
+  int32_t* pair_entry;     // [total] or null: source entry of each pair
+  int32_t* entry_pair;     // [n] or null: pair of each entry, -1 when dropped
+  int32_t* counts;         // [n_buckets] or null
+  int32_t* total;          // [1] or null
+  int tail;                // > 0: append one more bucket holding rows 0..tail-1, weight 1
+                           // (the shared expert); bucket_offset then has n_buckets + 2 entries
+};
+
+struct ChunkArgs {
+  const int32_t* seg_offset;  // [n_segments + 1]
+  int n_segments;
+  int chunk;                  // max pairs per chunk
+  int32_t* chunk_seg;         // [capacity]
+  int32_t* chunk_start;
+  int32_t* chunk_len;
+  int32_t* n_chunks;          // [1]
+};
+
+// Upper bound on the chunk count for `pairs` pairs in `segments` segments.
+inline int64_t chunk_capacity(int64_t pairs, int64_t segments, int chunk) {
+  return pairs / chunk + segments + 1;
+}
+
+size_t bucket_smem_bytes(int n_buckets);
+cudaError_t launch_bucket(const BucketArgs& a, cudaStream_t stream);
+cudaError_t launch_chunks(const ChunkArgs& a, cudaStream_t stream);
+
+}  // namespace moe

@@ -1,0 +1,52 @@
+// Grouped FP8 GEMV launchers (fp8_gemv.cu).
+#pragma once
+#include "common.cuh"
+
+namespace moe {
+
+enum GemvEpilogue : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiStoreBoth = 2 };
+enum GemvX : int { kXF32 = 0, kXBF16 = 1 };
+
+struct GemvArgs {
+  // per-segment device tables of device addresses (uint64): weights and
+  // fp32 [ceil(N/128), scale_cols] block scales; w1/s1 only for two streams
+  const uint64_t* w0;
+  const uint64_t* s0;
+  const uint64_t* w1;
+  const uint64_t* s1;
+  const void* x;             // activations [rows, K] (float or bf16)
+  const int32_t* pair_row;   // [P] row of x for each pair, or null: row = pair
+  const int32_t* chunk_seg;  // chunk list (dispatch.cuh)
+  const int32_t* chunk_start;
+  const int32_t* chunk_len;
+  const int32_t* n_chunks;   // device scalar
+  float* out0;               // [P, N]
+  float* out1;               // [P, N] (kEpiStoreBoth)
+  int N;                     // output rows per expert
+  int K;                     // reduction length
+  int scale_cols;            // ceil(K / 128)
+};
+
+struct CombineArgs {
+  const float* y;            // [P, H]
+  const int32_t* row_ptr;    // [T + 1] or null: row t owns [t*stride, (t+1)*stride)
+  int stride;
+  const int32_t* row_pairs;  // pair index per list entry (-1 = skip), or null: entry = pair
+  const float* pair_weight;  // [P] or null: weight 1
+  int extra_base;            // >= 0: also add y[extra_base + t] with weight 1 (shared expert)
+  int T;
+  int H;
+  float* out_f32;            // [T, H] or null
+  __nv_bfloat16* out_bf16;   // [T, H] or null
+};
+
+// Largest supported chunk size (1, 4 or 8 rows) whose staged rows fit in
+// shared memory; 0 when even one row does not fit.
+int gemv_chunk_tokens(int K, int x_dtype);
+int gemv_grid_ctas();
+
+cudaError_t launch_grouped_gemv(const GemvArgs& a, int x_dtype, int ns, int epi, int nt, bool vec,
+                                cudaStream_t stream);
+cudaError_t launch_combine(const CombineArgs& a, cudaStream_t stream);
+
+}  // namespace moe

@@ -1,0 +1,365 @@
+// Router kernels: fp32 router logits and top-k expert selection.
+//
+// Replaces the router math of run_fp8_router
+// (src/pcketlm/core/runtime/fp8_source.py:1522-1547) with its group mask
+// _mask_deepseek_route_groups (fp8_source.py:5125-5140), the native softmax
+// router ds_router_topk_u16 (src/pcketlm/native/ds_forward.cpp:879-955) and
+// the Mixtral softmax top-k (core/runtime/layer_bridge.py:2682-2689).
+//
+// Logits are dot products in fp32 of the hidden state with each router row
+// (the reference computes F.linear(x.float(), W.float())); only the
+// summation order differs, so selections agree except at score ties.
+#include "common.cuh"
+#include "router.cuh"
+
+namespace moe {
+
+MOE_D float to_float_any(float v) { return v; }
+MOE_D float to_float_any(__nv_bfloat16 v) { return __bfloat162float(v); }
+MOE_D float to_float_any(__half v) { return __half2float(v); }
+
+template <typename T>
+MOE_D void load8(const T* p, float* out);
+
+template <>
+MOE_D void load8<float>(const float* p, float* out) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+  out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+}
+
+template <>
+MOE_D void load8<__nv_bfloat16>(const __nv_bfloat16* p, float* out) {
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(w[i] << 16);
+    out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+template <>
+MOE_D void load8<__half>(const __half* p, float* out) {
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// Logits, small token counts: one CTA per pair of experts, 4 warps per expert
+// each summing a quarter of the hidden dimension.  The router weight streams
+// from HBM once; the activations are re-read from L1/L2.
+// ---------------------------------------------------------------------------
+constexpr int kGemvExpertsPerCta = 2;
+constexpr int kGemvSplit = 4;
+constexpr int kGemvTokens = 8;
+
+template <typename XT, typename WT>
+__global__ void __launch_bounds__(256) router_logits_gemv_kernel(
+    const XT* __restrict__ x, const WT* __restrict__ w, float* __restrict__ logits,
+    int tokens, int hidden, int experts, int vec_ok) {
+  __shared__ float partial[kGemvExpertsPerCta][kGemvSplit][kGemvTokens];
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int local_e = warp / kGemvSplit, part = warp % kGemvSplit;
+  const int e = blockIdx.x * kGemvExpertsPerCta + local_e;
+  const int per_part = static_cast<int>(ceil_div(ceil_div(hidden, 8), kGemvSplit)) * 8;
+  const int k_lo = part * per_part;
+  const int k_hi = min(hidden, k_lo + per_part);
+  for (int t0 = 0; t0 < tokens; t0 += kGemvTokens) {
+    const int nt = min(kGemvTokens, tokens - t0);
+    float acc[kGemvTokens];
+#pragma unroll
+    for (int t = 0; t < kGemvTokens; ++t) acc[t] = 0.0f;
+    if (e < experts) {
+      const WT* wrow = w + static_cast<int64_t>(e) * hidden;
+      if (vec_ok) {
+        for (int k = k_lo + lane * 8; k < k_hi; k += kWarp * 8) {
+          float wv[8];
+          load8<WT>(wrow + k, wv);
+#pragma unroll
+          for (int t = 0; t < kGemvTokens; ++t) {
+            if (t < nt) {
+              float xv[8];
+              load8<XT>(x + static_cast<int64_t>(t0 + t) * hidden + k, xv);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) acc[t] = fmaf(xv[i], wv[i], acc[t]);
+            }
+          }
+        }
+      } else {
+        for (int k = k_lo + lane; k < k_hi; k += kWarp) {
+          const float wv = to_float_any(wrow[k]);
+          for (int t = 0; t < nt; ++t) {
+            acc[t] = fmaf(to_float_any(x[static_cast<int64_t>(t0 + t) * hidden + k]), wv, acc[t]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kGemvTokens; ++t) {
+      const float s = warp_sum(acc[t]);
+      if (lane == 0) partial[local_e][part][t] = s;
+    }
+    __syncthreads();
+    if (threadIdx.x < kGemvExpertsPerCta * kGemvTokens) {
+      const int le = threadIdx.x / kGemvTokens, t = threadIdx.x % kGemvTokens;
+      const int ee = blockIdx.x * kGemvExpertsPerCta + le;
+      if (ee < experts && t < nt) {
+        float s = 0.0f;
+#pragma unroll
+        for (int p = 0; p < kGemvSplit; ++p) s += partial[le][p][t];
+        logits[static_cast<int64_t>(t0 + t) * experts + ee] = s;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Logits, large token counts: 64x64 output tiles, 4x4 per thread, k-tiles of
+// 32 staged through shared memory (row-major copies of x and w tiles).
+// ---------------------------------------------------------------------------
+constexpr int kTileM = 64, kTileN = 64, kTileK = 32;
+
+template <typename XT, typename WT>
+__global__ void __launch_bounds__(256) router_logits_tiled_kernel(
+    const XT* __restrict__ x, const WT* __restrict__ w, float* __restrict__ logits,
+    int tokens, int hidden, int experts) {
+  __shared__ float xs[kTileK][kTileM + 4];
+  __shared__ float ws[kTileK][kTileN + 4];
+  const int tm = blockIdx.y * kTileM, tn = blockIdx.x * kTileN;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < hidden; k0 += kTileK) {
+    for (int i = threadIdx.x; i < kTileM * kTileK; i += 256) {
+      const int r = i / kTileK, c = i % kTileK;
+      const int gr = tm + r, gc = k0 + c;
+      xs[c][r] = (gr < tokens && gc < hidden) ? to_float_any(x[static_cast<int64_t>(gr) * hidden + gc]) : 0.0f;
+      const int er = tn + r;
+      ws[c][r] = (er < experts && gc < hidden) ? to_float_any(w[static_cast<int64_t>(er) * hidden + gc]) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < kTileK; ++k) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = xs[k][ty * 4 + i];
+        b[i] = ws[k][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = tm + ty * 4 + i;
+    if (r >= tokens) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = tn + tx * 4 + j;
+      if (c < experts) logits[static_cast<int64_t>(r) * experts + c] = acc[i][j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Selection: one warp per token.
+// ---------------------------------------------------------------------------
+constexpr int kSelectWarps = 4;
+
+__global__ void __launch_bounds__(kSelectWarps * kWarp) router_select_kernel(
+    const float* __restrict__ logits, const float* __restrict__ bias, RouterSelectParams p,
+    int64_t* __restrict__ ids64, int32_t* __restrict__ ids32, float* __restrict__ weights_f32,
+    __nv_bfloat16* __restrict__ weights_bf16) {
+  extern __shared__ float smem[];
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int t = blockIdx.x * kSelectWarps + warp;
+  if (t >= p.tokens) return;
+  const int E = p.experts;
+  float* probs = smem + warp * 2 * E;
+  float* choice = probs + E;
+  const float* row = logits + static_cast<int64_t>(t) * E;
+
+  // scores: sigmoid, or softmax (max-subtracted)
+  if (p.scoring == kScoreSigmoid) {
+    for (int e = lane; e < E; e += kWarp) probs[e] = 1.0f / (1.0f + expf(-row[e]));
+  } else {
+    float m = -INFINITY;
+    for (int e = lane; e < E; e += kWarp) m = fmaxf(m, row[e]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    for (int e = lane; e < E; e += kWarp) probs[e] = expf(row[e] - m);
+    __syncwarp();
+    if (p.softmax_fp64) {
+      // ds_router_topk_u16: fp64 denominator, summed in expert order
+      // (ds_forward.cpp:913-924)
+      double denom = 0.0;
+      if (lane == 0)
+        for (int e = 0; e < E; ++e) denom += static_cast<double>(probs[e]);
+      denom = __shfl_sync(0xFFFFFFFFu, denom, 0);
+      for (int e = lane; e < E; e += kWarp) probs[e] = static_cast<float>(static_cast<double>(probs[e]) / denom);
+    } else {
+      float s = 0.0f;
+      for (int e = lane; e < E; e += kWarp) s += probs[e];
+      s = warp_sum(s);
+      for (int e = lane; e < E; e += kWarp) probs[e] = probs[e] / s;
+    }
+  }
+  __syncwarp();
+  for (int e = lane; e < E; e += kWarp) choice[e] = bias ? probs[e] + bias[e] : probs[e];
+  __syncwarp();
+
+  // group-limited selection (fp8_source.py:5125-5140)
+  if (p.n_group > 1) {
+    const int G = E / p.n_group;
+    float gscore = -INFINITY;
+    if (lane < p.n_group) {
+      float best = -INFINITY, second = -INFINITY;
+      for (int i = 0; i < G; ++i) {
+        const float v = choice[lane * G + i];
+        if (v > best) {
+          second = best;
+          best = v;
+        } else if (v > second) {
+          second = v;
+        }
+      }
+      gscore = bias ? best + second : best;
+    }
+    uint32_t keep = 0;
+    const int kg = max(1, min(p.topk_group, p.n_group));
+    for (int j = 0; j < kg; ++j) {
+      float v = (keep >> lane) & 1u ? -INFINITY : gscore;
+      int idx = lane < p.n_group ? lane : 0x7FFFFFFF;
+      if ((keep >> lane) & 1u) idx = 0x7FFFFFFF;
+      warp_argmax(v, idx);
+      if (idx < kWarp) keep |= 1u << idx;
+    }
+    for (int e = lane; e < E; e += kWarp)
+      if (!((keep >> (e / G)) & 1u)) choice[e] = -INFINITY;
+    __syncwarp();
+  }
+
+  // top-k, ties to the lower expert id
+  const int k = p.top_k;
+  int my_id = -1;      // lane j < k holds the j-th pick
+  float my_prob = 0.0f;
+  for (int j = 0; j < k; ++j) {
+    float v = -INFINITY;
+    int idx = 0x7FFFFFFF;
+    for (int e = lane; e < E; e += kWarp) {
+      const float c = choice[e];
+      if (c > v || (c == v && e < idx)) {
+        v = c;
+        idx = e;
+      }
+    }
+    warp_argmax(v, idx);
+    if (idx == 0x7FFFFFFF) idx = 0;  // every remaining score is -inf / NaN
+    if (lane == j) {
+      my_id = idx;
+      my_prob = probs[idx];
+    }
+    __syncwarp();
+    // a picked expert becomes NaN: every comparison with it is false, so it
+    // is never picked again even when the remaining scores are all -inf
+    if (lane == 0) choice[idx] = __int_as_float(0x7FC00000);
+    __syncwarp();
+  }
+
+  float w = my_prob;
+  if (p.renorm) {
+    if (p.softmax_fp64) {
+      double s = 0.0;
+      for (int j = 0; j < k; ++j) s += static_cast<double>(__shfl_sync(0xFFFFFFFFu, my_prob, j));
+      w = static_cast<float>(static_cast<double>(my_prob) / s);
+    } else {
+      float s = 0.0f;
+      for (int j = 0; j < k; ++j) s += __shfl_sync(0xFFFFFFFFu, my_prob, j);
+      w = my_prob / fmaxf(s, 1e-12f);
+    }
+  }
+  w = w * p.route_scale;
+  if (lane < k) {
+    const int64_t o = static_cast<int64_t>(t) * k + lane;
+    if (p.round_bf16) w = __bfloat162float(__float2bfloat16_rn(w));
+    if (ids64) ids64[o] = my_id;
+    if (ids32) ids32[o] = my_id;
+    if (weights_f32) weights_f32[o] = w;
+    if (weights_bf16) weights_bf16[o] = __float2bfloat16_rn(w);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+template <typename XT, typename WT>
+static cudaError_t launch_logits_t(const void* x, const void* w, float* logits, int tokens, int hidden,
+                                   int experts, cudaStream_t stream) {
+  const XT* xp = static_cast<const XT*>(x);
+  const WT* wp = static_cast<const WT*>(w);
+  if (tokens <= 32) {
+    const bool vec_ok = hidden % 8 == 0 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                        (reinterpret_cast<uintptr_t>(w) % 16 == 0) &&
+                        (sizeof(XT) == 4 ? (hidden % 4 == 0) : true);
+    dim3 grid(static_cast<unsigned>(ceil_div(experts, kGemvExpertsPerCta)));
+    router_logits_gemv_kernel<XT, WT><<<grid, 256, 0, stream>>>(xp, wp, logits, tokens, hidden, experts,
+                                                                  vec_ok ? 1 : 0);
+  } else {
+    dim3 grid(static_cast<unsigned>(ceil_div(experts, kTileN)), static_cast<unsigned>(ceil_div(tokens, kTileM)));
+    router_logits_tiled_kernel<XT, WT><<<grid, 256, 0, stream>>>(xp, wp, logits, tokens, hidden, experts);
+  }
+  return cudaGetLastError();
+}
+
+template <typename XT>
+static cudaError_t launch_logits_w(const void* x, int w_dtype, const void* w, float* logits, int tokens,
+                                   int hidden, int experts, cudaStream_t stream) {
+  switch (w_dtype) {
+    case kDtypeF32: return launch_logits_t<XT, float>(x, w, logits, tokens, hidden, experts, stream);
+    case kDtypeBF16: return launch_logits_t<XT, __nv_bfloat16>(x, w, logits, tokens, hidden, experts, stream);
+    case kDtypeF16: return launch_logits_t<XT, __half>(x, w, logits, tokens, hidden, experts, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_router_logits(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
+                                 int tokens, int hidden, int experts, cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  switch (x_dtype) {
+    case kDtypeF32: return launch_logits_w<float>(x, w_dtype, w, logits, tokens, hidden, experts, stream);
+    case kDtypeBF16: return launch_logits_w<__nv_bfloat16>(x, w_dtype, w, logits, tokens, hidden, experts, stream);
+    case kDtypeF16: return launch_logits_w<__half>(x, w_dtype, w, logits, tokens, hidden, experts, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_router_select(const float* logits, const float* bias, const RouterSelectParams& p,
+                                 int64_t* ids64, int32_t* ids32, float* weights_f32,
+                                 __nv_bfloat16* weights_bf16, cudaStream_t stream) {
+  if (p.tokens <= 0) return cudaSuccess;
+  const size_t smem = static_cast<size_t>(kSelectWarps) * 2 * p.experts * sizeof(float);
+  const unsigned grid = static_cast<unsigned>(ceil_div(p.tokens, kSelectWarps));
+  if (smem > 48 * 1024) {
+    cudaError_t err = cudaFuncSetAttribute(router_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+  }
+  router_select_kernel<<<grid, kSelectWarps * kWarp, smem, stream>>>(logits, bias, p, ids64, ids32,
+                                                                      weights_f32, weights_bf16);
+  return cudaGetLastError();
+}
+
+}  // namespace moe

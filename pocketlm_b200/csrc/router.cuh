@@ -1,0 +1,31 @@
+// Router launchers (router.cu).
+#pragma once
+#include "common.cuh"
+
+namespace moe {
+
+// Element types of activations / router weights.
+enum Dtype : int { kDtypeF32 = 0, kDtypeBF16 = 1, kDtypeF16 = 2 };
+enum Scoring : int { kScoreSigmoid = 0, kScoreSoftmax = 1 };
+
+struct RouterSelectParams {
+  int tokens;
+  int experts;       // <= 2048, divisible by n_group
+  int top_k;         // <= 32
+  int n_group;       // <= 32; 1 disables the group mask
+  int topk_group;
+  int scoring;       // Scoring
+  int renorm;        // divide the picked probabilities by their sum
+  int softmax_fp64;  // ds_router_topk_u16 semantics: fp64 denominators
+  int round_bf16;    // round the final weights through bf16 (fp8_source.py:1547)
+  float route_scale;
+};
+
+cudaError_t launch_router_logits(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
+                                 int tokens, int hidden, int experts, cudaStream_t stream);
+
+cudaError_t launch_router_select(const float* logits, const float* bias, const RouterSelectParams& p,
+                                 int64_t* ids64, int32_t* ids32, float* weights_f32,
+                                 __nv_bfloat16* weights_bf16, cudaStream_t stream);
+
+}  // namespace moe

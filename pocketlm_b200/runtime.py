@@ -1,0 +1,160 @@
+"""Layer-level entry points: the GPU counterparts of run_fp8_router and
+run_fp8_moe (src/pcketlm/core/runtime/fp8_source.py:1500-1884).
+
+The reference resolves a layer's tensors through its model catalog
+(model_id, layer_index); here the caller hands in an HBM-resident layer
+(pocketlm_b200.synth.Fp8MoELayer or any object with the same tensors), since
+the catalog / pack loaders are outside this path.  Results carry the fields
+of the reference's FP8RouterResult / FP8MoEResult that describe the
+computation (selected experts, shapes, weight bytes, timings, blockers).
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from . import native
+from .synth import Fp8MoELayer
+
+
+@dataclass
+class FP8RouterResult:
+    layer_index: int
+    hidden_shape: list[int]
+    weights_shape: list[int]
+    indices_shape: list[int]
+    selected_experts: list[int]
+    scoring_func: str
+    route_scale: float
+    n_groups: int
+    topk_groups: int
+    bias_loaded: bool
+    weights_tensor: torch.Tensor | None
+    indices_tensor: torch.Tensor | None
+    blockers: list[str] = field(default_factory=list)
+    ready: bool = False
+
+
+@dataclass
+class FP8MoEResult:
+    layer_index: int
+    hidden_shape: list[int]
+    output_shape: list[int]
+    selected_experts: list[int]
+    routed_weight_bytes: int
+    shared_weight_bytes: int
+    router: FP8RouterResult | None
+    output_tensor: torch.Tensor | None
+    total_elapsed_seconds: float = 0.0
+    blockers: list[str] = field(default_factory=list)
+    ready: bool = False
+
+
+class DsMoELayerGPU:
+    """An FP8 DeepSeek-V3 MoE layer resident in HBM, ready for the fused path.
+
+    Holds the [6, E+1] device table of expert addresses (gate, gate scale,
+    up, up scale, down, down scale; the shared expert last) that
+    moe_ds_moe_layer_fp8 walks, and a reusable workspace."""
+
+    def __init__(self, layer: Fp8MoELayer, layer_index: int = 0):
+        if not layer.is_full:
+            raise ValueError("the fused layer path needs every expert resident (a full layer)")
+        if layer.device.type != "cuda":
+            layer = layer.to(native._device())
+        self.layer = layer
+        self.cfg = layer.cfg
+        self.layer_index = int(layer_index)
+        n = self.cfg.n_routed + 1
+        cols = [[0] * n for _ in range(6)]
+        for e in range(n):
+            for j, t in enumerate(layer.expert(e)):
+                cols[j][e] = int(t.data_ptr())
+        self.tables = torch.tensor(cols, dtype=torch.int64, device=layer.device)
+        self._workspace = torch.empty((0,), dtype=torch.uint8, device=layer.device)
+
+    def workspace_for(self, tokens: int) -> torch.Tensor:
+        lib = native.load_library()
+        need = int(lib.moe_ds_moe_layer_workspace_bytes(tokens, self.cfg.hidden, self.cfg.inter,
+                                                        self.cfg.n_routed, self.cfg.top_k, 1))
+        if self._workspace.numel() < need:
+            self._workspace = torch.empty((need,), dtype=torch.uint8, device=self.layer.device)
+        return self._workspace
+
+    def forward(self, hidden: torch.Tensor, *, out: torch.Tensor | None = None,
+                ids: torch.Tensor | None = None, weights: torch.Tensor | None = None) -> torch.Tensor:
+        """hidden [T, H] bf16 on the layer's device -> out [T, H] bf16.
+
+        `ids` (int64 [T, k]) and `weights` (bf16 [T, k]) receive the routing
+        when given.  Everything is enqueued on the current stream."""
+        cfg = self.cfg
+        x = hidden.reshape(-1, cfg.hidden)
+        if x.device != self.layer.device:
+            raise ValueError("hidden must be on the layer's device")
+        if x.dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("hidden must be bf16 or fp32")
+        x = x.contiguous()
+        T = int(x.shape[0])
+        if out is None:
+            out = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=x.device)
+        ws = self.workspace_for(T)
+        rw = self.layer.router_weight
+        rdt = {torch.float32: native.DTYPE_F32, torch.bfloat16: native.DTYPE_BF16, torch.float16: native.DTYPE_F16}
+        code = native.load_library().moe_ds_moe_layer_fp8(
+            native._ptr(x), native.DTYPE_BF16 if x.dtype == torch.bfloat16 else native.DTYPE_F32, T, cfg.hidden,
+            cfg.inter, native._ptr(rw), rdt[rw.dtype], native._ptr(self.layer.bias), cfg.n_routed, cfg.n_group,
+            cfg.topk_group, cfg.top_k, 1 if cfg.scoring_func == "softmax" else 0, float(cfg.route_scale),
+            native._ptr(self.tables), 1, native._ptr(out), native._ptr(ids), native._ptr(weights),
+            native._ptr(ws), ws.numel(), native._stream())
+        native._check(code, "moe_ds_moe_layer_fp8")
+        return out
+
+
+def run_fp8_router(layer: Fp8MoELayer | DsMoELayerGPU, hidden: torch.Tensor, layer_index: int = 0) -> FP8RouterResult:
+    """The router of fp8_source.py:1500-1566 on the GPU."""
+    base = layer.layer if isinstance(layer, DsMoELayerGPU) else layer
+    cfg = base.cfg
+    ids, weights = native.route_topk(hidden, base.router_weight, base.bias, top_k=cfg.top_k, n_group=cfg.n_group,
+                                     topk_group=cfg.topk_group, scoring_func=cfg.scoring_func,
+                                     route_scale=cfg.route_scale, round_to_hidden_dtype=True)
+    selected = sorted({int(v) for v in ids.reshape(-1).tolist()})
+    return FP8RouterResult(
+        layer_index=int(layer_index), hidden_shape=[int(v) for v in hidden.shape],
+        weights_shape=[int(v) for v in weights.shape], indices_shape=[int(v) for v in ids.shape],
+        selected_experts=selected, scoring_func=cfg.scoring_func, route_scale=float(cfg.route_scale),
+        n_groups=cfg.n_group, topk_groups=cfg.topk_group, bias_loaded=base.bias is not None,
+        weights_tensor=weights, indices_tensor=ids, blockers=[], ready=True)
+
+
+def run_fp8_moe(layer: DsMoELayerGPU, hidden: torch.Tensor, *, dtype: torch.dtype = torch.bfloat16,
+                layer_index: int | None = None) -> FP8MoEResult:
+    """One MoE layer (routed experts + shared expert) on the GPU, the
+    counterpart of fp8_source.py:1569-1884.  Output in bf16 (the reference's
+    default dtype); fp32 inputs are accepted and rounded once at the end."""
+    if dtype != torch.bfloat16:
+        raise ValueError("the fused GPU layer produces bf16 output")
+    start = time.perf_counter()
+    cfg = layer.cfg
+    dev = layer.layer.device
+    flat = hidden.reshape(-1, cfg.hidden)
+    x = flat.to(dev).to(torch.bfloat16) if flat.dtype != torch.float32 else flat.to(dev)
+    T = int(x.shape[0])
+    ids = torch.empty((T, cfg.top_k), dtype=torch.int64, device=dev)
+    weights = torch.empty((T, cfg.top_k), dtype=torch.bfloat16, device=dev)
+    out = layer.forward(x, ids=ids, weights=weights)
+    selected = sorted({int(v) for v in ids.reshape(-1).tolist()})
+    router = FP8RouterResult(
+        layer_index=int(layer.layer_index if layer_index is None else layer_index),
+        hidden_shape=[int(v) for v in hidden.shape], weights_shape=[T, cfg.top_k], indices_shape=[T, cfg.top_k],
+        selected_experts=selected, scoring_func=cfg.scoring_func, route_scale=float(cfg.route_scale),
+        n_groups=cfg.n_group, topk_groups=cfg.topk_group, bias_loaded=layer.layer.bias is not None,
+        weights_tensor=weights.to(hidden.device), indices_tensor=ids.to(hidden.device), ready=True)
+    output = out.reshape(hidden.shape).to(hidden.device)
+    return FP8MoEResult(
+        layer_index=router.layer_index, hidden_shape=[int(v) for v in hidden.shape],
+        output_shape=[int(v) for v in output.shape], selected_experts=selected,
+        routed_weight_bytes=len(selected) * cfg.expert_bytes, shared_weight_bytes=cfg.expert_bytes,
+        router=router, output_tensor=output, total_elapsed_seconds=time.perf_counter() - start, ready=True)

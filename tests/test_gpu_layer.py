@@ -1,0 +1,112 @@
+"""GPU parity of the router and of the whole DeepSeek-V3 MoE layer against the
+CPU oracle (which reproduces the reference's run_fp8_router / run_fp8_moe
+bit for bit, tests/test_golden.py).
+
+Gates: expert ids bit-exact barring score ties within
+1e-6; layer output relative L2 <= 2e-2 and cosine distance <= 1e-3.  The GPU
+path rounds once to bf16 where the reference accumulates in bf16, so the
+measured errors sit far inside the gate (about 3e-3 relative L2).
+"""
+
+import pytest
+import torch
+
+import oracle
+from oracle import kernels as orc
+from pocketlm_b200 import native, synth
+from pocketlm_b200.runtime import DsMoELayerGPU, run_fp8_moe, run_fp8_router
+from tests.parity import COS_GATE, REL_L2_GATE, cos_dist, id_mismatches, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def test_softmax_router_matches_reference_vectors(cuda_device, golden_dir):
+    g = torch.load(golden_dir / "softmax_router_20260519.pt", weights_only=False)
+    for row, ids, weights in zip(g["hidden"], g["ids"], g["weights"]):
+        i, w = native.ds_router_topk(row.cuda(), g["router"].cuda(), k=4)
+        assert torch.equal(i.cpu(), ids)
+        assert torch.allclose(w.cpu(), weights, atol=1e-6, rtol=1e-6)
+
+
+def test_sigmoid_bias_router_known_answer(cuda_device):
+    router = torch.tensor([[4.0, 4.0, 4.0, 4.0], [0.0, 0.0, 0.0, 0.0]])
+    bias = torch.tensor([-20.0, 0.0])
+    ids, w = native.route_topk(torch.ones((1, 4), dtype=torch.bfloat16).cuda(), router.cuda(), bias.cuda(),
+                               top_k=1, n_group=1, topk_group=1, scoring_func="sigmoid", route_scale=2.5)
+    assert ids.cpu().tolist() == [[1]]
+    assert torch.allclose(w.float().cpu(), torch.tensor([[2.5]]))
+
+
+@pytest.mark.parametrize("cfg,tokens,seed,bias", [
+    (synth.C1_TINY, 64, 0, "uniform"),
+    (synth.C2_DSV3, 64, 3, "uniform"),
+    (synth.C2_DSV3, 512, 4, "zipf"),
+])
+def test_grouped_router_matches_oracle(cuda_device, cfg, tokens, seed, bias):
+    layer = synth.make_fp8_layer(cfg, seed=seed, device="cuda", bias_kind=bias, experts=[])
+    x = synth.make_hidden(tokens, cfg.hidden, seed=seed, device="cuda")
+    ids, w = native.route_topk(x, layer.router_weight, layer.bias, top_k=cfg.top_k, n_group=cfg.n_group,
+                               topk_group=cfg.topk_group, route_scale=cfg.route_scale)
+    r = oracle.route_deepseek(x.cpu(), layer.router_weight.cpu(), layer.bias.cpu(), top_k=cfg.top_k,
+                              n_groups=cfg.n_group, topk_groups=cfg.topk_group, route_scale=cfg.route_scale)
+    bad, excused = id_mismatches(ids, r)
+    assert bad == excused, f"{bad} tokens route differently, {excused} of them at score ties"
+    same = (torch.sort(ids.cpu(), 1).values == torch.sort(r.ids, 1).values).all(dim=1)
+    # weights per expert id, for tokens whose set matches
+    got = torch.zeros((tokens, cfg.n_routed)).scatter_(1, ids.cpu(), w.float().cpu())
+    want = torch.zeros((tokens, cfg.n_routed)).scatter_(1, r.ids, r.weights.float())
+    assert torch.allclose(got[same], want[same], atol=1e-2 * cfg.route_scale / cfg.top_k, rtol=8e-3)
+
+
+def _layer_case(cfg, tokens, seed, full):
+    x = synth.make_hidden(tokens, cfg.hidden, seed=seed, device="cuda")
+    layer = synth.make_fp8_layer(cfg, seed=seed, device="cuda")
+    gpu = DsMoELayerGPU(layer)
+    ids = torch.empty((tokens, cfg.top_k), dtype=torch.int64, device="cuda")
+    w = torch.empty((tokens, cfg.top_k), dtype=torch.bfloat16, device="cuda")
+    out = gpu.forward(x, ids=ids, weights=w)
+    torch.cuda.synchronize()
+    # oracle on the same tensors (copies the selected experts to the host)
+    expected, route = oracle.ds_moe_layer(x.cpu(), layer)
+    return out, ids, w, expected, route
+
+
+@pytest.mark.parametrize("tokens", [1, 3, 17, 64])
+def test_tiny_layer_matches_oracle(cuda_device, tokens):
+    out, ids, _w, expected, route = _layer_case(synth.C1_TINY, tokens, seed=0, full=True)
+    bad, excused = id_mismatches(ids, route)
+    assert bad == excused
+    assert rel_l2(out, expected) <= REL_L2_GATE
+    assert cos_dist(out, expected) <= COS_GATE
+
+
+def test_tiny_layer_matches_reference_golden(cuda_device, golden_dir):
+    g = torch.load(golden_dir / "c1_tiny_T64.pt", weights_only=False)
+    cfg = synth.C1_TINY
+    layer = synth.make_fp8_layer(cfg, seed=g["seed"]).to("cuda")
+    x = synth.make_hidden(g["tokens"], cfg.hidden, seed=g["seed"]).to("cuda")
+    res = run_fp8_moe(DsMoELayerGPU(layer), x)
+    assert res.ready
+    assert torch.equal(torch.sort(res.router.indices_tensor.cpu(), 1).values, torch.sort(g["ids"], 1).values)
+    assert rel_l2(res.output_tensor, g["out"]) <= REL_L2_GATE
+    assert cos_dist(res.output_tensor, g["out"]) <= COS_GATE
+
+
+@pytest.mark.parametrize("tokens", [1, 4, 16, 64])
+def test_dsv3_decode_layer_matches_oracle(cuda_device, tokens):
+    out, ids, _w, expected, route = _layer_case(synth.C2_DSV3, tokens, seed=10 + tokens, full=True)
+    bad, excused = id_mismatches(ids, route)
+    assert bad == excused
+    err, cd = rel_l2(out, expected), cos_dist(out, expected)
+    assert err <= REL_L2_GATE and cd <= COS_GATE, (err, cd)
+
+
+def test_dsv3_router_result_api(cuda_device):
+    cfg = synth.C2_DSV3
+    layer = synth.make_fp8_layer(cfg, seed=5, device="cuda", experts=[])
+    x = synth.make_hidden(4, cfg.hidden, seed=5, device="cuda")
+    res = run_fp8_router(layer, x)
+    assert res.ready and res.indices_tensor.shape == (4, 8) and res.weights_tensor.dtype == torch.bfloat16
+    assert res.scoring_func == "sigmoid" and res.n_groups == 8 and res.topk_groups == 4
+    sums = res.weights_tensor.float().sum(dim=1)
+    assert torch.allclose(sums.cpu(), torch.full((4,), 2.5), atol=3e-2)
