@@ -8,8 +8,10 @@ largest decode batch of config 2) with all 256 routed experts + the shared
 expert resident in HBM (11.3 GB of e4m3 weights + fp32 block scales,
 synthetic, seeded).  The weights streamed per step exceed the 126 MB L2, and
 L2 is additionally flushed (256 MiB write) between timed steps; each step is
-timed with CUDA events on the launching stream.  The same measurement is
-repeated for T = 1, 4, 16 ("sweep").
+timed with CUDA events on the launching stream.  The layer runs as one CUDA
+graph replay (GraphedDsMoELayer: 7 kernels); the plain per-call path is
+timed too (eager_ms_per_step).  The same measurement is repeated for
+T = 1, 4, 16 ("sweep").
 
 Printed (rank 0, one JSON line): tokens/s with inputs resident in HBM
 (`value`), the same through the public API from pinned host buffers with the
@@ -227,11 +229,14 @@ def run_ours(args, rank: int, world: int) -> dict | None:
             ids = torch.empty((T, cfg.top_k), dtype=torch.int64, device=dev)
             gpu_layer.forward(x, out=out, ids=ids)
             torch.cuda.synchronize()
-            fn = lambda: gpu_layer.forward(x, out=out)  # noqa: E731
+            graphed = gpu_layer.capture(T)
+            graphed.input.copy_(x)
+            eager_ms = statistics.mean(time_steps(lambda: gpu_layer.forward(x, out=out), args.steps, args.warmup,
+                                                  flush))
             if world > 1:
                 torch.distributed.barrier()
             torch.cuda.synchronize()
-            times = time_steps(fn, args.steps, args.warmup, flush)
+            times = time_steps(graphed.replay, args.steps, args.warmup, flush)
             if world > 1:
                 torch.distributed.barrier()
             torch.cuda.synchronize()
@@ -242,18 +247,17 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                 ms = float(t.item())
             stages = stage_times(gpu_layer, x, max(5, min(args.steps, 50)), flush)
             b = layer_bytes(cfg, ids, T)
-            # stage marks: [route+dispatch, chunk list, gate/up, down, combine]
-            gateup_ms = stages[2] if len(stages) >= 3 else None
-            down_ms = stages[3] if len(stages) >= 4 else None
+            # stage intervals: [route + dispatch + chunk list, gate/up, down, combine]
+            gateup_ms = stages[1] if len(stages) >= 2 else None
+            down_ms = stages[2] if len(stages) >= 3 else None
             # end to end through the public API: pinned host in, pinned host out
             x_host = x.cpu().pin_memory()
             out_host = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
-            x_dev = torch.empty_like(x)
 
             def e2e_step():
-                x_dev.copy_(x_host, non_blocking=True)
-                gpu_layer.forward(x_dev, out=out)
-                out_host.copy_(out, non_blocking=True)
+                graphed.input.copy_(x_host, non_blocking=True)
+                graphed.replay()
+                out_host.copy_(graphed.output, non_blocking=True)
 
             e2e_ms = statistics.mean(time_steps(e2e_step, args.steps, args.warmup, flush))
             if world > 1:
@@ -262,6 +266,7 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                 e2e_ms = float(t.item())
             results[T] = {
                 "tokens": T, "ms_per_step": ms, "tokens_per_s": T * world / (ms / 1e3),
+                "eager_ms_per_step": eager_ms,
                 "e2e_tokens_per_s": T * world / (e2e_ms / 1e3), "e2e_ms": e2e_ms,
                 "experts_streamed": b["experts"], "layer_bytes": b["total"],
                 "layer_hbm_frac": (b["total"] / (ms / 1e3)) / (peaks["hbm_gbs"] * 1e9),

@@ -310,7 +310,7 @@ static cudaError_t launch_logits_t(const void* x, const void* w, float* logits, 
                                    int experts, cudaStream_t stream) {
   const XT* xp = static_cast<const XT*>(x);
   const WT* wp = static_cast<const WT*>(w);
-  if (tokens <= 32) {
+  if (tokens <= 256) {
     const bool vec_ok = hidden % 8 == 0 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                         (reinterpret_cast<uintptr_t>(w) % 16 == 0) &&
                         (sizeof(XT) == 4 ? (hidden % 4 == 0) : true);

@@ -113,6 +113,50 @@ class DsMoELayerGPU:
         return out
 
 
+    def capture(self, tokens: int, *, input_dtype: torch.dtype = torch.bfloat16) -> "GraphedDsMoELayer":
+        """Record the whole layer (7 kernels) for a fixed token count into a
+        CUDA graph; replaying it removes the per-kernel host launch cost,
+        which at decode sizes is comparable to the kernels themselves."""
+        return GraphedDsMoELayer(self, tokens, input_dtype)
+
+
+class GraphedDsMoELayer:
+    """A DsMoELayerGPU forward for one token count, captured as a CUDA graph.
+
+    Write the activations into `.input` (or pass them to __call__), replay,
+    read `.output`; `.ids` / `.weights` hold the routing of the last replay."""
+
+    def __init__(self, layer: DsMoELayerGPU, tokens: int, input_dtype: torch.dtype):
+        cfg = layer.cfg
+        dev = layer.layer.device
+        self.layer = layer
+        self.tokens = int(tokens)
+        self.input = torch.zeros((tokens, cfg.hidden), dtype=input_dtype, device=dev)
+        self.output = torch.empty((tokens, cfg.hidden), dtype=torch.bfloat16, device=dev)
+        self.ids = torch.empty((tokens, cfg.top_k), dtype=torch.int64, device=dev)
+        self.weights = torch.empty((tokens, cfg.top_k), dtype=torch.bfloat16, device=dev)
+        layer.workspace_for(tokens)
+        # warm up outside the capture (kernel attributes, lazy module loading)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            layer.forward(self.input, out=self.output, ids=self.ids, weights=self.weights)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            layer.forward(self.input, out=self.output, ids=self.ids, weights=self.weights)
+        torch.cuda.synchronize(dev)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.output
+
+    def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
+        self.input.copy_(hidden.reshape(self.input.shape), non_blocking=True)
+        return self.replay()
+
+
 def run_fp8_router(layer: Fp8MoELayer | DsMoELayerGPU, hidden: torch.Tensor, layer_index: int = 0) -> FP8RouterResult:
     """The router of fp8_source.py:1500-1566 on the GPU."""
     base = layer.layer if isinstance(layer, DsMoELayerGPU) else layer

@@ -110,3 +110,17 @@ def test_dsv3_router_result_api(cuda_device):
     assert res.scoring_func == "sigmoid" and res.n_groups == 8 and res.topk_groups == 4
     sums = res.weights_tensor.float().sum(dim=1)
     assert torch.allclose(sums.cpu(), torch.full((4,), 2.5), atol=3e-2)
+
+
+def test_graphed_layer_equals_eager(cuda_device):
+    cfg = synth.C1_TINY
+    layer = DsMoELayerGPU(synth.make_fp8_layer(cfg, seed=3, device="cuda"))
+    x = synth.make_hidden(5, cfg.hidden, seed=3, device="cuda")
+    eager = layer.forward(x).clone()
+    graphed = layer.capture(5)
+    for _ in range(2):
+        out = graphed(x)
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+    x2 = synth.make_hidden(5, cfg.hidden, seed=4, device="cuda")
+    assert torch.equal(graphed(x2), layer.forward(x2))
