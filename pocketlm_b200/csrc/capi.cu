@@ -88,6 +88,15 @@ bool g_timing = false;
 cudaEvent_t g_events[kMaxStageEvents] = {};
 int g_marks = 0;
 
+// 0: bulk-copy streaming GEMV where supported, else the direct-load one; 1: direct-load only
+int g_gemv_impl = 0;
+
+cudaError_t gemv(const GemvArgs& a, int x_dtype, int ns, int epi, int nt, bool vec, cudaStream_t stream) {
+  if (g_gemv_impl == 0 && vec && stream_gemv_supported(a.K, x_dtype, nt))
+    return launch_stream_gemv(a, x_dtype, ns, epi, nt, stream);
+  return launch_grouped_gemv(a, x_dtype, ns, epi, nt, vec, stream);
+}
+
 void stage_mark(cudaStream_t stream) {
   if (!g_timing || g_marks >= kMaxStageEvents) return;
   cudaEventRecord(g_events[g_marks++], stream);
@@ -150,7 +159,7 @@ int run_expert_stages(const Tables& t, const void* x, int x_dtype, const MlpScra
   g1.chunk_seg = s.chunk_seg; g1.chunk_start = s.chunk_start; g1.chunk_len = s.chunk_len; g1.n_chunks = s.n_chunks;
   g1.out0 = s.act; g1.N = static_cast<int>(inter); g1.K = static_cast<int>(hidden); g1.scale_cols = static_cast<int>(gsc);
   stage_mark(stream);
-  MOE_CUDA(launch_grouped_gemv(g1, x_dtype, 2, kEpiSwiglu, nt, vec, stream), "gate/up stage");
+  MOE_CUDA(gemv(g1, x_dtype, 2, kEpiSwiglu, nt, vec, stream), "gate/up stage");
   stage_mark(stream);
   const int nt2 = std::min(nt, gemv_chunk_tokens(static_cast<int>(inter), kXF32));
   if (nt2 != nt) {
@@ -162,7 +171,7 @@ int run_expert_stages(const Tables& t, const void* x, int x_dtype, const MlpScra
   g2.x = s.act; g2.pair_row = nullptr; g2.out0 = y;
   g2.N = static_cast<int>(hidden); g2.K = static_cast<int>(inter); g2.scale_cols = static_cast<int>(dsc);
   const bool vec2 = vec && (inter % 16 == 0);
-  MOE_CUDA(launch_grouped_gemv(g2, kXF32, 1, kEpiStore, nt, vec2, stream), "down stage");
+  MOE_CUDA(gemv(g2, kXF32, 1, kEpiStore, nt, vec2, stream), "down stage");
   stage_mark(stream);
   return kOk;
 }
@@ -321,8 +330,7 @@ static int linear_common(const uint8_t* wa, const float* sa, const uint8_t* wb, 
   g.chunk_seg = ca.chunk_seg; g.chunk_start = ca.chunk_start; g.chunk_len = ca.chunk_len; g.n_chunks = ca.n_chunks;
   g.out0 = oa; g.out1 = ob; g.N = static_cast<int>(rows); g.K = static_cast<int>(cols); g.scale_cols = static_cast<int>(scols);
   const bool vec = cols % 16 == 0 && aligned16(x) && aligned16(wa) && (!dual || aligned16(wb));
-  MOE_CUDA(launch_grouped_gemv(g, kXF32, dual ? 2 : 1, dual ? kEpiStoreBoth : kEpiStore, nt, vec, stream),
-           "linear");
+  MOE_CUDA(gemv(g, kXF32, dual ? 2 : 1, dual ? kEpiStoreBoth : kEpiStore, nt, vec, stream), "linear");
   return kOk;
 }
 
@@ -684,6 +692,14 @@ int moe_b200_stage_timing(int enable) {
   g_marks = 0;
   return kOk;
 }
+
+int moe_b200_select_gemv(int impl) {
+  if (impl != 0 && impl != 1) return fail(kBadDims, "impl must be 0 or 1");
+  g_gemv_impl = impl;
+  return kOk;
+}
+
+int moe_b200_device_error(void* stream) { return read_and_clear_device_error(as_stream(stream)); }
 
 int moe_b200_stage_times(float* ms, int max_n) {
   if (!ms) return fail(kNullPointer, "null pointer");

@@ -49,4 +49,11 @@ cudaError_t launch_grouped_gemv(const GemvArgs& a, int x_dtype, int ns, int epi,
                                 cudaStream_t stream);
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t stream);
 
+// Warp-specialised variant (fp8_stream.cu): bulk-copy weight ring.  Needs
+// K % 16 == 0 and 16-byte aligned weight rows.
+bool stream_gemv_supported(int K, int x_dtype, int nt);
+cudaError_t launch_stream_gemv(const GemvArgs& a, int x_dtype, int ns, int epi, int nt, cudaStream_t stream);
+// Device error word of the bounded waits; returns it (or -1) and clears it.
+int read_and_clear_device_error(cudaStream_t stream);
+
 }  // namespace moe

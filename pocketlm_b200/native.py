@@ -104,6 +104,8 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_ds_moe_layer_forward_fp8_f32": ([_P] * 9 + [_I64] * 6 + [_P, _P, _I64, _P], _INT),
     "moe_b200_stage_timing": ([_INT], _INT),
     "moe_b200_stage_times": ([_P, _INT], _INT),
+    "moe_b200_select_gemv": ([_INT], _INT),
+    "moe_b200_device_error": ([_P], _INT),
 }
 
 

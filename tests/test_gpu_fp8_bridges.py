@@ -18,6 +18,20 @@ from pocketlm_b200 import native
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True, params=["stream", "direct"])
+def gemv_impl(request):
+    """Run every case on both expert-GEMV kernels: the bulk-copy streaming one
+    (fp8_stream.cu) and the direct-load one (fp8_gemv.cu)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    lib = native.load_library()
+    assert lib.moe_b200_select_gemv(0 if request.param == "stream" else 1) == 0
+    yield request.param
+    torch.cuda.synchronize()
+    assert lib.moe_b200_device_error(None) == 0, "a bounded wait inside a kernel gave up"
+    lib.moe_b200_select_gemv(0)
+
+
 def _fp8(values: torch.Tensor) -> torch.Tensor:
     return values.to(torch.float8_e4m3fn).view(torch.uint8).contiguous()
 

@@ -20,6 +20,20 @@ from tests.parity import COS_GATE, REL_L2_GATE, cos_dist, id_mismatches, rel_l2
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True, params=["stream", "direct"])
+def gemv_impl(request):
+    """Run every case on both expert-GEMV kernels: the bulk-copy streaming one
+    (fp8_stream.cu) and the direct-load one (fp8_gemv.cu)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    lib = native.load_library()
+    assert lib.moe_b200_select_gemv(0 if request.param == "stream" else 1) == 0
+    yield request.param
+    torch.cuda.synchronize()
+    assert lib.moe_b200_device_error(None) == 0, "a bounded wait inside a kernel gave up"
+    lib.moe_b200_select_gemv(0)
+
+
 def test_softmax_router_matches_reference_vectors(cuda_device, golden_dir):
     g = torch.load(golden_dir / "softmax_router_20260519.pt", weights_only=False)
     for row, ids, weights in zip(g["hidden"], g["ids"], g["weights"]):
