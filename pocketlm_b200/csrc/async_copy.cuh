@@ -9,7 +9,9 @@ namespace moe {
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 // Device error word: nonzero after a bounded wait gave up (moe_b200_device_error).
-extern __device__ int g_device_error;
+// Defined per translation unit (no relocatable device code); only
+// fp8_stream.cu includes this header and reads the word back.
+static __device__ int g_device_error = 0;
 
 MOE_D uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 

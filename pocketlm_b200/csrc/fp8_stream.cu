@@ -25,8 +25,6 @@
 
 namespace moe {
 
-__device__ int g_device_error = 0;
-
 constexpr int kConsumerWarps = 8;
 constexpr int kStreamThreads = (kConsumerWarps + 1) * kWarp;
 constexpr int kSlice = 1024;  // bytes of one weight row per ring stage
