@@ -219,9 +219,9 @@ int moe_ds_moe_layer_forward_fp8_f32(void* handle, const uint64_t* gate_weight_p
 int moe_b200_stage_timing(int enable);
 int moe_b200_stage_times(float* ms, int max_n);
 
-/* Expert-GEMV implementation (no reference counterpart): 0 = warp-specialised
- * bulk-copy streaming kernel wherever the shape allows (default), 1 = the
- * direct-load kernel everywhere.  For A/B parity tests and measurements. */
+/* Expert-GEMV implementation (no reference counterpart): 0 = the direct-load
+ * kernel (default), 1 = the warp-specialised bulk-copy streaming kernel
+ * wherever the shape allows.  For A/B parity tests and measurements. */
 int moe_b200_select_gemv(int impl);
 
 /* Device error word (no reference counterpart): nonzero when a bounded wait

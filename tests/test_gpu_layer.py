@@ -27,7 +27,7 @@ def gemv_impl(request):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     lib = native.load_library()
-    assert lib.moe_b200_select_gemv(0 if request.param == "stream" else 1) == 0
+    assert lib.moe_b200_select_gemv(1 if request.param == "stream" else 0) == 0
     yield request.param
     torch.cuda.synchronize()
     assert lib.moe_b200_device_error(None) == 0, "a bounded wait inside a kernel gave up"
