@@ -13,28 +13,11 @@
 #include "dispatch.cuh"
 #include "fp8_gemv.cuh"
 #include "router.cuh"
+#include "status.cuh"
 
 using namespace moe;
 
 namespace {
-
-thread_local char g_last_error[512] = "";
-
-int fail(int code, const char* what) {
-  std::snprintf(g_last_error, sizeof g_last_error, "%s", what);
-  return code;
-}
-
-int cuda_fail(cudaError_t err, const char* where) {
-  std::snprintf(g_last_error, sizeof g_last_error, "%s: %s", where, cudaGetErrorString(err));
-  return kCudaError - static_cast<int>(err);
-}
-
-#define MOE_CUDA(expr, where)                 \
-  do {                                        \
-    cudaError_t _e = (expr);                  \
-    if (_e != cudaSuccess) return cuda_fail(_e, where); \
-  } while (0)
 
 // Bump allocator over one workspace block; sizes round up to 256 bytes.
 class Plan {

@@ -90,6 +90,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) grouped_gemv_kernel(GemvArgs 
     // an absent expert (null table entry) contributes zeros, as the reference
     // skips it (fp8_linear.cpp:410-415, :449-451)
     const bool present = w0 && s0 && (NS == 1 || (w1 && s1));
+    // 16-byte vector loads need 16-byte aligned weight rows; otherwise take the byte path
+    const bool wal = ((reinterpret_cast<uintptr_t>(w0) | reinterpret_cast<uintptr_t>(w1) |
+                       static_cast<uintptr_t>(K)) & 15u) == 0;
 
     for (int step = 0; step < kRowsPerWarp / RS; ++step) {
       const int r0 = rt * kTileRows + warp * kRowsPerWarp + step * RS;
@@ -116,7 +119,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) grouped_gemv_kernel(GemvArgs 
 
       if (!present) {
         // acc stays zero
-      } else if (VEC) {
+      } else if (VEC && wal) {
         const int nk = K / 16;
 #pragma unroll 2
         for (int kc = lane; kc < nk; kc += kWarp) {

@@ -76,7 +76,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1) stream_gemv_kernel(GemvArgs
       const int seg = a.chunk_seg[c];
       const uint8_t* wb0 = reinterpret_cast<const uint8_t*>(a.w0[seg]);
       const uint8_t* wb1 = NS == 2 ? reinterpret_cast<const uint8_t*>(a.w1[seg]) : nullptr;
-      const bool present = wb0 && a.s0[seg] && (NS == 1 || (wb1 && a.s1[seg]));
+      bool present = wb0 && a.s0[seg] && (NS == 1 || (wb1 && a.s1[seg]));
+      if (present && ((reinterpret_cast<uintptr_t>(wb0) | reinterpret_cast<uintptr_t>(wb1)) & 15u) != 0) {
+        // bulk copies need 16-byte aligned sources: refuse loudly, compute nothing
+        if (lane == 0) atomicOr(&g_device_error, 8);
+        present = false;
+      }
       const int rows_valid = min(R, N - r0);
       for (int s = 0; s < nslice; ++s, ++it) {
         const uint32_t stage = it % stages, use = it / stages;
@@ -136,7 +141,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) stream_gemv_kernel(GemvArgs
       named_barrier_sync(1, kConsumerThreads);
       staged = c;
     }
-    const bool present = a.w0[seg] && a.s0[seg] && (NS == 1 || (a.w1[seg] && a.s1[seg]));
+    const bool present = a.w0[seg] && a.s0[seg] && (NS == 1 || (a.w1[seg] && a.s1[seg])) &&
+                         ((a.w0[seg] | (NS == 2 ? a.w1[seg] : 0ull)) & 15ull) == 0;
     const float* sb0 = reinterpret_cast<const float*>(a.s0[seg]);
     const float* sb1 = NS == 2 ? reinterpret_cast<const float*>(a.s1[seg]) : nullptr;
     const int rbase = rt * R + cw * RW;

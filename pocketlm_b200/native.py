@@ -165,7 +165,10 @@ def _gpu(t: torch.Tensor, dtype: torch.dtype | None = None) -> torch.Tensor:
     dev = _device()
     if t.device != dev:
         t = t.to(dev, non_blocking=False)
-    return t.contiguous()
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()  # the kernels' vector and bulk loads want 16-byte aligned rows
+    return t
 
 
 def _ptr(t: torch.Tensor | None) -> _P:
