@@ -114,6 +114,28 @@ int moe_fp8_e4m3_block_mlp_many_pair_weighted_f32(const uint64_t* gate_weight_pt
                                                   int64_t down_scale_cols, void* workspace,
                                                   int64_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference.  The expert MLP of
+ * moe_fp8_e4m3_block_mlp_f32 for callers that cannot allocate device memory:
+ * a process whose GPU memory is all reserved up front by its own arena, a
+ * hot path that must not take the CUDA allocator's locks or its implicit
+ * synchronisation, or a binding that only owns the pointers it passes.  It
+ * allocates nothing: its scratch (pointer table, chunk list, fp32 SwiGLU
+ * activations) is a static device array of MOE_B200_NOALLOC_SCRATCH_BYTES
+ * (4 MiB) that every GPU loading the library holds until exit.  Calls needing
+ * more (roughly batch * intermediate_rows * 4 bytes plus a few KiB) return -3
+ * with a message.  All calls share the array, so calls that overlap on the GPU
+ * (different streams or devices' threads racing on one device) race; serialise
+ * them.  The first call on a device looks the array's address up and should
+ * come before any stream capture.  Same arguments and results as
+ * moe_fp8_e4m3_block_mlp_f32, minus the workspace. */
+#define MOE_B200_NOALLOC_SCRATCH_BYTES (4u << 20)
+int moe_fp8_e4m3_block_mlp_f32_noalloc(const uint8_t* gate_weight, const float* gate_scale_inv,
+                                       const uint8_t* up_weight, const float* up_scale_inv,
+                                       const uint8_t* down_weight, const float* down_scale_inv,
+                                       const float* hidden, float* out, int64_t batch,
+                                       int64_t intermediate_rows, int64_t hidden_cols,
+                                       int64_t gate_scale_cols, int64_t down_scale_cols, void* stream);
+
 /* Workspace bytes for the MLP entry points above, given the number of
  * (expert, row) pairs they evaluate (mlp: batch; many/weighted: E*B;
  * row/pair weighted: the nonzero count or pair_count; pass the upper bound). */

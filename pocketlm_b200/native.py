@@ -86,6 +86,7 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_fp8_e4m3_block_mlp_many_row_weighted_f32": ([_P] * 9 + [_I64] * 6 + [_P, _I64, _P], _INT),
     "moe_fp8_e4m3_block_mlp_many_pair_weighted_f32": ([_P] * 11 + [_I64] * 7 + [_P, _I64, _P], _INT),
     "moe_fp8_mlp_workspace_bytes": ([_I64] * 5, _I64),
+    "moe_fp8_e4m3_block_mlp_f32_noalloc": ([_P] * 8 + [_I64] * 5 + [_P], _INT),
     "moe_fp8_e4m3_dequant_to_fp16": ([_P, _P, _P, _I64, _I64, _I64, _P], _INT),
     "moe_fp8_e4m3_dequant_to_bf16": ([_P, _P, _P, _I64, _I64, _I64, _P], _INT),
     "moe_ds_router_topk_u16": ([_P, _P, _I64, _I64, _I64, _I64, _P, _P, _P], _INT),
