@@ -45,7 +45,7 @@ import torch  # noqa: E402
 
 METRIC = "DS-V3 MoE layer tokens/s @1/2/4/8 B200; % of HBM or FP8 TC roofline"
 L2_FLUSH_BYTES = 256 << 20
-KERNELS_PER_LAYER = 7  # router logits, router select, dispatch, chunk list, gate/up, down, combine
+KERNELS_PER_LAYER = 9  # router logits, router select, dispatch, chunk list, x->f16, gate/up, act->f16, down, combine
 
 
 def measured_peaks() -> dict:
@@ -247,9 +247,10 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                 ms = float(t.item())
             stages = stage_times(gpu_layer, x, max(5, min(args.steps, 50)), flush)
             b = layer_bytes(cfg, ids, T)
-            # stage intervals: [route + dispatch + chunk list, gate/up, down, combine]
+            # stage intervals: [route + dispatch + chunk list (+ x to f16), gate/up,
+            # (activations to f16 on the MMA path,) down, combine]
             gateup_ms = stages[1] if len(stages) >= 2 else None
-            down_ms = stages[2] if len(stages) >= 3 else None
+            down_ms = (stages[3] if len(stages) >= 5 else stages[2]) if len(stages) >= 3 else None
             # end to end through the public API: pinned host in, pinned host out
             x_host = x.cpu().pin_memory()
             out_host = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
@@ -299,7 +300,7 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                    "top_k": cfg.top_k, "n_group": cfg.n_group, "topk_group": cfg.topk_group,
                    "parallelism": "single GPU" if world == 1 else f"replicas x{world}",
                    "l2": "weights streamed per step exceed L2; 256 MiB L2 flush between timed steps"},
-        "roofline": {"bound": "hbm", "kernel": "grouped_gemv gate/up+SwiGLU (fp8_gemv.cu)",
+        "roofline": {"bound": "hbm", "kernel": "mma_gemv_kernel<2, swiglu> gate/up+SwiGLU (fp8_mma.cu)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None,
                      "peak_source": f"{peaks['source']} hbm_gbs",

@@ -232,18 +232,22 @@ int moe_ds_moe_layer_forward_fp8_f32(void* handle, const uint64_t* gate_weight_p
 
 /* ---------------------------------------------------------------------------
  * Profiling (no reference counterpart): when enabled, moe_ds_moe_layer_fp8
- * records CUDA events on its stream at the boundaries of its stages --
- * [start, route+dispatch done, chunk list done, gate/up done, down done,
- * combine done].  moe_b200_stage_times waits for the last event and writes the
+ * records CUDA events on its stream at the boundaries of its stages:
+ * start | route, dispatch, chunk list (+ f16 staging of x on the MMA path) |
+ * gate/up | (f16 staging of the activations on the MMA path |) down |
+ * combine.  moe_b200_stage_times waits for the last event and writes the
  * elapsed milliseconds between consecutive marks (returns how many).
  * Single-threaded use only.
  * ------------------------------------------------------------------------- */
 int moe_b200_stage_timing(int enable);
 int moe_b200_stage_times(float* ms, int max_n);
 
-/* Expert-GEMV implementation (no reference counterpart): 0 = the direct-load
- * kernel (default), 1 = the warp-specialised bulk-copy streaming kernel
- * wherever the shape allows.  For A/B parity tests and measurements. */
+/* Expert-GEMV implementation (no reference counterpart): 0 = auto (default:
+ * the warp-MMA kernel on the whole-layer path when hidden and intermediate
+ * sizes are multiples of 128, the direct-load kernel elsewhere), 1 = the
+ * warp-specialised bulk-copy streaming kernel wherever the shape allows,
+ * 2 = the direct-load kernel everywhere.  For A/B parity tests and
+ * measurements. */
 int moe_b200_select_gemv(int impl);
 
 /* Device error word (no reference counterpart): nonzero when a bounded wait

@@ -71,7 +71,9 @@ bool g_timing = false;
 cudaEvent_t g_events[kMaxStageEvents] = {};
 int g_marks = 0;
 
-// 0: direct-load GEMV (default, fastest measured); 1: bulk-copy streaming GEMV where supported
+// Expert GEMV selection: 0 = auto (warp-MMA kernel on the layer path where the
+// shapes allow, direct-load elsewhere), 1 = bulk-copy streaming kernel where
+// supported, 2 = direct-load kernel everywhere.
 int g_gemv_impl = 0;
 
 cudaError_t gemv(const GemvArgs& a, int x_dtype, int ns, int epi, int nt, bool vec, cudaStream_t stream) {
@@ -593,6 +595,10 @@ struct LayerPlan {
   int32_t* ids32;
   float* wts;
   MlpScratch m;
+  __half* x16;
+  float* xscale;
+  __half* act16;
+  float* ascale;
 };
 
 static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, int shared, int nt) {
@@ -602,7 +608,43 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
   l.wts = p.take<float>(T * k);
   const int64_t pairs = T * k + (shared ? T : 0);
   l.m = plan_mlp(p, pairs, E + 1, T * k, I, H, nt, true);
+  l.x16 = p.take<__half>(T * H);
+  l.xscale = p.take<float>(T);
+  l.act16 = p.take<__half>(pairs * I);
+  l.ascale = p.take<float>(pairs);
   return l;
+}
+
+// The expert stages on the warp-MMA kernel: x and the SwiGLU activations are
+// staged as f16 rows with power-of-two scales.
+static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, const LayerPlan& l, int64_t T,
+                                 int64_t pairs, int64_t n_segments, int64_t I, int64_t H, cudaStream_t s) {
+  const MlpScratch& m = l.m;
+  ChunkArgs ca{m.seg_offset, static_cast<int>(n_segments), 8, m.chunk_seg, m.chunk_start, m.chunk_len, m.n_chunks};
+  MOE_CUDA(launch_chunks(ca, s), "chunk list");
+  MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.x16, l.xscale, s),
+           "stage x");
+  stage_mark(s);
+  MmaArgs g1{};
+  g1.w0 = t.gw; g1.s0 = t.gs; g1.w1 = t.uw; g1.s1 = t.us;
+  g1.x16 = l.x16; g1.xscale = l.xscale; g1.pair_row = m.pair_row;
+  g1.chunk_seg = m.chunk_seg; g1.chunk_start = m.chunk_start; g1.chunk_len = m.chunk_len; g1.n_chunks = m.n_chunks;
+  g1.out0 = m.act; g1.N = static_cast<int>(I); g1.K = static_cast<int>(H);
+  g1.scale_cols = static_cast<int>(ceil_div(H, kBlock)); g1.nanfix = 1;
+  MOE_CUDA(launch_mma_gemv(g1, 2, kEpiSwiglu, s), "gate/up stage");
+  stage_mark(s);
+  MOE_CUDA(launch_rows_to_f16(m.act, false, static_cast<int>(pairs), static_cast<int>(I), nullptr, l.act16,
+                              l.ascale, s),
+           "stage activations");
+  stage_mark(s);
+  MmaArgs g2 = g1;
+  g2.w0 = t.dw; g2.s0 = t.ds; g2.w1 = nullptr; g2.s1 = nullptr;
+  g2.x16 = l.act16; g2.xscale = l.ascale; g2.pair_row = nullptr;
+  g2.out0 = m.y; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
+  g2.scale_cols = static_cast<int>(ceil_div(I, kBlock));
+  MOE_CUDA(launch_mma_gemv(g2, 1, kEpiStore, s), "down stage");
+  stage_mark(s);
+  return kOk;
 }
 
 int64_t moe_ds_moe_layer_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, int shared) {
@@ -650,7 +692,12 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   const int64_t S = E + (has_shared ? 1 : 0);
   Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
   const bool vec = H % 16 == 0 && I % 16 == 0 && aligned16(hidden);
-  code = run_expert_stages(t, hidden, xd, l.m, l.m.y, S, I, H, ceil_div(H, kBlock), ceil_div(I, kBlock), nt, vec, s);
+  if (g_gemv_impl == 0 && mma_gemv_supported(static_cast<int>(H), static_cast<int>(I)) &&
+      mma_gemv_supported(static_cast<int>(I), static_cast<int>(H))) {
+    code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I, H, s);
+  } else {
+    code = run_expert_stages(t, hidden, xd, l.m, l.m.y, S, I, H, ceil_div(H, kBlock), ceil_div(I, kBlock), nt, vec, s);
+  }
   if (code != kOk) return code;
   // 4. combine: routed slots in top-k order, then the shared expert; one bf16 rounding
   CombineArgs c{};
@@ -677,7 +724,7 @@ int moe_b200_stage_timing(int enable) {
 }
 
 int moe_b200_select_gemv(int impl) {
-  if (impl != 0 && impl != 1) return fail(kBadDims, "impl must be 0 or 1");
+  if (impl < 0 || impl > 2) return fail(kBadDims, "impl must be 0, 1 or 2");
   g_gemv_impl = impl;
   return kOk;
 }

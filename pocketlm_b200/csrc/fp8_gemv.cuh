@@ -1,5 +1,7 @@
 // Grouped FP8 GEMV launchers (fp8_gemv.cu).
 #pragma once
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace moe {
@@ -53,6 +55,31 @@ cudaError_t launch_combine(const CombineArgs& a, cudaStream_t stream);
 // K % 16 == 0 and 16-byte aligned weight rows.
 bool stream_gemv_supported(int K, int x_dtype, int nt);
 cudaError_t launch_stream_gemv(const GemvArgs& a, int x_dtype, int ns, int epi, int nt, cudaStream_t stream);
+// Warp-MMA GEMV (fp8_mma.cu), layer path: activations staged as f16 rows with
+// per-row power-of-two scales.  Needs K % 128 == 0.
+struct MmaArgs {
+  const uint64_t* w0;
+  const uint64_t* s0;
+  const uint64_t* w1;
+  const uint64_t* s1;
+  const __half* x16;         // [rows, K] activations / scale
+  const float* xscale;       // [rows]
+  const int32_t* pair_row;   // [P] row of x16 per pair, or null: row = pair
+  const int32_t* chunk_seg;  // chunk list (chunks of <= 8 pairs)
+  const int32_t* chunk_start;
+  const int32_t* chunk_len;
+  const int32_t* n_chunks;
+  float* out0;               // [P, N]
+  int N;
+  int K;
+  int scale_cols;
+  int nanfix;                // decode e4m3 0x7F/0xFF as +0 (the reference's linear semantics)
+};
+bool mma_gemv_supported(int K, int N);
+cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream);
+cudaError_t launch_rows_to_f16(const void* src, bool src_bf16, int rows, int K, const int32_t* n_rows_dev,
+                               __half* dst, float* scale, cudaStream_t stream);
+
 // Device error word of the bounded waits; returns it (or -1) and clears it.
 int read_and_clear_device_error(cudaStream_t stream);
 

@@ -1,0 +1,257 @@
+// Grouped FP8 GEMV on the warp MMA pipe (decode batches, layer path).
+//
+// The decode GEMV is bound by HBM, but decoding e4m3 and multiplying on the
+// FMA pipe costs about three instructions per weight byte, which is as much
+// issue bandwidth as an SM has at 6.5 TB/s.  Here every warp streams 16 (or
+// 32) weight rows with 16-byte loads, turns each e4m3 pair into an f16 pair
+// with one exact conversion, and lets mma.m16n8k16 (fp32 accumulate) do the
+// products against up to 8 token rows: about one instruction per weight byte,
+// whatever the number of tokens up to 8.  The tensor pipe is idle otherwise;
+// its throughput is not what this kernel needs.
+//
+// Fragment trick: a dot product is invariant under any permutation of k
+// applied to both operands.  Lane (g = lane/4, c = lane%4) loads bytes
+// [16c, 16c+16) of a 64-byte k-span of rows g and g+8; in k-step s it feeds
+// word s of that load as its A fragment (low byte pair -> logical k 2c, 2c+1,
+// high pair -> 2c+8, 2c+9) and the matching activations x[16c+4s .. +3] of
+// token g as its B fragment, so the four k-steps of a span cover its 64
+// physical columns exactly once.
+//
+// Scales: the two spans of a 128-column k-block accumulate into a fresh
+// fp32 fragment, which is then multiplied by that block's weight scale and
+// added to the running sums -- the reference's "sum the block, then scale"
+// (fp8_linear.cpp:103-112).  Activations are staged as f16 divided by a
+// per-row power of two (rows_to_f16_kernel), undone in the epilogue, so any
+// fp32/bf16 magnitude survives and bf16 inputs stay exact.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "fp8_gemv.cuh"
+
+namespace moe {
+
+constexpr int kMmaCtaWarps = 4;
+
+MOE_D uint32_t e4m3x2_to_f16x2_bits(uint32_t pair) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair & 0xFFFFu), __NV_E4M3);
+  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+}
+
+MOE_D void mma_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+MOE_D uint4 ldg_stream(const void* p) { return __ldcs(reinterpret_cast<const uint4*>(p)); }
+
+MOE_D uint32_t word_of(const uint4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+// One 128-column k-block of operands for one lane.
+struct KBlock {
+  uint4 a[2][2][2];  // [span][stream][row g, row g+8]
+  uint4 b[2][2];     // [span][lo 8 halfs, hi 8 halfs] of the lane's token row
+};
+
+// Activation rows -> f16 with a per-row power-of-two scale:
+// dst[r, k] = src[r, k] / scale[r], scale = 2^(floor(log2(amax)) - 13) so the
+// largest magnitude lands in [2^13, 2^14) (1 for an all-zero row).
+template <typename T>
+__global__ void __launch_bounds__(256) rows_to_f16_kernel(const T* __restrict__ src, int rows, int K,
+                                                          const int32_t* __restrict__ n_rows_dev,
+                                                          __half* __restrict__ dst, float* __restrict__ scale) {
+  __shared__ float red[8];
+  const int n_rows = n_rows_dev ? min(rows, *n_rows_dev) : rows;
+  for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
+    const T* s = src + static_cast<int64_t>(r) * K;
+    float amax = 0.0f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) amax = fmaxf(amax, fabsf(to_float<T>(s[k])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+    if (threadIdx.x % kWarp == 0) red[threadIdx.x / kWarp] = amax;
+    __syncthreads();
+    if (threadIdx.x < kWarp) {
+      float v = threadIdx.x < blockDim.x / kWarp ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+      if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    amax = red[0];
+    const float sc = (amax > 0.0f && isfinite(amax)) ? ldexpf(1.0f, ilogbf(amax) - 13) : 1.0f;
+    const float inv = 1.0f / sc;  // exact: power of two
+    __half* d = dst + static_cast<int64_t>(r) * K;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) d[k] = __float2half_rn(to_float<T>(s[k]) * inv);
+    if (threadIdx.x == 0) scale[r] = sc;
+    __syncthreads();
+  }
+}
+
+// NS == 2: each warp task is 16 rows of two matrices (gate + up, SwiGLU
+// epilogue).  NS == 1: 32 rows of one matrix as two 16-row tiles.
+template <int NS, int EPI>
+__global__ void __launch_bounds__(kMmaCtaWarps * kWarp) mma_gemv_kernel(MmaArgs a) {
+  const int lane = threadIdx.x % kWarp;
+  const int g = lane / 4, c = lane % 4;
+  const int K = a.K, N = a.N;
+  constexpr int kTaskRows = NS == 2 ? 16 : 32;
+  const int row_tiles = static_cast<int>(ceil_div(N, kTaskRows));
+  const int64_t tasks = static_cast<int64_t>(*a.n_chunks) * row_tiles;
+  const int64_t warp_global = static_cast<int64_t>(blockIdx.x) * kMmaCtaWarps + threadIdx.x / kWarp;
+  const int64_t warp_count = static_cast<int64_t>(gridDim.x) * kMmaCtaWarps;
+  const int nkb = K / kBlock;
+
+  for (int64_t task = warp_global; task < tasks; task += warp_count) {
+    const int ch = static_cast<int>(task / row_tiles);
+    const int r0 = static_cast<int>(task % row_tiles) * kTaskRows;
+    const int seg = a.chunk_seg[ch], p0 = a.chunk_start[ch], len = a.chunk_len[ch];
+    const uint8_t* w0 = reinterpret_cast<const uint8_t*>(a.w0[seg]);
+    const float* s0 = reinterpret_cast<const float*>(a.s0[seg]);
+    const uint8_t* w1 = NS == 2 ? reinterpret_cast<const uint8_t*>(a.w1[seg]) : w0;
+    const float* s1 = NS == 2 ? reinterpret_cast<const float*>(a.s1[seg]) : s0;
+    const bool present = w0 && s0 && w1 && s1 &&
+                         ((reinterpret_cast<uintptr_t>(w0) | reinterpret_cast<uintptr_t>(w1)) & 15u) == 0;
+
+    // A rows of this lane: stream st, row half rr
+    const uint8_t* arow[2][2];
+    const float* srow[2];
+#pragma unroll
+    for (int st = 0; st < 2; ++st) {
+      const int base = NS == 2 ? r0 : r0 + 16 * st;
+      const uint8_t* w = st == 0 ? w0 : w1;
+      const float* sc = st == 0 ? s0 : s1;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int row = min(base + g + 8 * rr, N - 1);
+        arow[st][rr] = present ? w + static_cast<int64_t>(row) * K + 16 * c : nullptr;
+      }
+      srow[st] = present ? sc + static_cast<int64_t>(min(base, N - 1) / kBlock) * a.scale_cols : nullptr;
+    }
+    // B row: token g of the chunk
+    const bool bvalid = g < len;
+    const int64_t brow = bvalid ? (a.pair_row ? a.pair_row[p0 + g] : static_cast<int64_t>(p0 + g)) : 0;
+    const __half* xb = a.x16 + brow * K + 16 * c;
+
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if (present) {
+      auto load = [&](KBlock& kb, int kbi) {
+#pragma unroll
+        for (int sp = 0; sp < 2; ++sp) {
+          const int off = kbi * kBlock + sp * 64;
+#pragma unroll
+          for (int st = 0; st < 2; ++st)
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) kb.a[sp][st][rr] = ldg_stream(arow[st][rr] + off);
+          if (bvalid) {
+            kb.b[sp][0] = __ldg(reinterpret_cast<const uint4*>(xb + off));
+            kb.b[sp][1] = __ldg(reinterpret_cast<const uint4*>(xb + off + 8));
+          } else {
+            kb.b[sp][0] = make_uint4(0, 0, 0, 0);
+            kb.b[sp][1] = make_uint4(0, 0, 0, 0);
+          }
+        }
+      };
+      auto compute = [&](const KBlock& kb, int kbi) {
+        float t[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int sp = 0; sp < 2; ++sp) {
+          const uint32_t bw[8] = {kb.b[sp][0].x, kb.b[sp][0].y, kb.b[sp][0].z, kb.b[sp][0].w,
+                                  kb.b[sp][1].x, kb.b[sp][1].y, kb.b[sp][1].z, kb.b[sp][1].w};
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+#pragma unroll
+            for (int st = 0; st < 2; ++st) {
+              uint32_t wg = word_of(kb.a[sp][st][0], s);
+              uint32_t wh = word_of(kb.a[sp][st][1], s);
+              if (a.nanfix) {
+                wg = e4m3x4_nan_to_zero(wg);
+                wh = e4m3x4_nan_to_zero(wh);
+              }
+              mma_16816(t[st], e4m3x2_to_f16x2_bits(wg), e4m3x2_to_f16x2_bits(wh),
+                        e4m3x2_to_f16x2_bits(wg >> 16), e4m3x2_to_f16x2_bits(wh >> 16), bw[2 * s], bw[2 * s + 1]);
+            }
+          }
+        }
+#pragma unroll
+        for (int st = 0; st < 2; ++st) {
+          const float sc = __ldg(srow[st] + kbi);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[st][i] = fmaf(t[st][i], sc, acc[st][i]);
+        }
+      };
+      // ping-pong register buffers, one k-block of loads in flight ahead of the math
+      KBlock buf0, buf1;
+      load(buf0, 0);
+      for (int kbi = 0; kbi < nkb; kbi += 2) {
+        if (kbi + 1 < nkb) load(buf1, kbi + 1);
+        compute(buf0, kbi);
+        if (kbi + 1 < nkb) {
+          if (kbi + 2 < nkb) load(buf0, kbi + 2);
+          compute(buf1, kbi + 1);
+        }
+      }
+    }
+
+    // epilogue: lane holds rows (g, g+8) x tokens (2c, 2c+1) per stream
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int tok = 2 * c + j;
+      if (tok >= len) continue;
+      const int64_t tr = a.pair_row ? a.pair_row[p0 + tok] : static_cast<int64_t>(p0 + tok);
+      const float xs = a.xscale[tr];
+      const int64_t p = p0 + tok;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int i = rr * 2 + j;
+        if (NS == 2) {
+          const int row = r0 + g + 8 * rr;
+          if (row < N) {
+            const float gv = acc[0][i] * xs, uv = acc[1][i] * xs;
+            const float silu = gv / (1.0f + expf(-gv));
+            a.out0[p * N + row] = EPI == kEpiSwiglu ? silu * uv : gv;
+          }
+        } else {
+#pragma unroll
+          for (int st = 0; st < 2; ++st) {
+            const int row = r0 + 16 * st + g + 8 * rr;
+            if (row < N) a.out0[p * N + row] = acc[st][i] * xs;
+          }
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+bool mma_gemv_supported(int K, int N) { return K % kBlock == 0 && K > 0 && N > 0; }
+
+cudaError_t launch_rows_to_f16(const void* src, bool src_bf16, int rows, int K, const int32_t* n_rows_dev,
+                               __half* dst, float* scale, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  const unsigned grid = static_cast<unsigned>(std::min(rows, gemv_grid_ctas() * 8));
+  if (src_bf16)
+    rows_to_f16_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(src), rows, K,
+                                                                 n_rows_dev, dst, scale);
+  else
+    rows_to_f16_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(src), rows, K, n_rows_dev, dst,
+                                                         scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream) {
+  const int blocks_per_sm = 16;  // 64 warps per SM at most
+  const unsigned grid = static_cast<unsigned>(gemv_grid_ctas() * blocks_per_sm);
+  if (ns == 2 && epi == kEpiSwiglu) mma_gemv_kernel<2, kEpiSwiglu><<<grid, kMmaCtaWarps * kWarp, 0, stream>>>(a);
+  else if (ns == 1 && epi == kEpiStore) mma_gemv_kernel<1, kEpiStore><<<grid, kMmaCtaWarps * kWarp, 0, stream>>>(a);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+}  // namespace moe
