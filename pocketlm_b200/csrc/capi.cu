@@ -603,7 +603,7 @@ struct LayerPlan {
 
 static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, int shared, int nt) {
   LayerPlan l{};
-  l.logits = p.take<float>(T * E);
+  l.logits = p.take<float>(static_cast<int64_t>(std::max(1, router_split_parts(static_cast<int>(H)))) * T * E);
   l.ids32 = p.take<int32_t>(T * k);
   l.wts = p.take<float>(T * k);
   const int64_t pairs = T * k + (shared ? T : 0);
@@ -618,10 +618,13 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
 // The expert stages on the warp-MMA kernel: x and the SwiGLU activations are
 // staged as f16 rows with power-of-two scales.
 static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, const LayerPlan& l, int64_t T,
-                                 int64_t pairs, int64_t n_segments, int64_t I, int64_t H, cudaStream_t s) {
+                                 int64_t pairs, int64_t n_segments, int64_t I, int64_t H, bool chunks_ready,
+                                 cudaStream_t s) {
   const MlpScratch& m = l.m;
-  ChunkArgs ca{m.seg_offset, static_cast<int>(n_segments), 8, m.chunk_seg, m.chunk_start, m.chunk_len, m.n_chunks};
-  MOE_CUDA(launch_chunks(ca, s), "chunk list");
+  if (!chunks_ready) {
+    ChunkArgs ca{m.seg_offset, static_cast<int>(n_segments), 8, m.chunk_seg, m.chunk_start, m.chunk_len, m.n_chunks};
+    MOE_CUDA(launch_chunks(ca, s), "chunk list");
+  }
   MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.x16, l.xscale, s),
            "stage x");
   stage_mark(s);
@@ -676,25 +679,61 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   LayerPlan l = plan_layer(plan, T, H, I, E, k, has_shared, nt);
   g_marks = 0;
   stage_mark(s);
-  // 1. route (weights rounded through bf16 like fp8_source.py:1547 when hidden is bf16)
-  code = route_impl(hidden, hidden_dtype, router_weight, router_dtype, router_bias, T, H, E, n_group, topk_group, k,
-                    scoring, 0, 0, route_scale, hidden_dtype == kDtypeBF16, out_ids, l.ids32, l.wts,
-                    out_weights_bf16, l.logits, s);
-  if (code != kOk) return code;
-  // 2. dispatch: expert-contiguous pairs, ascending token order inside an expert, shared expert last
+  const int64_t S = E + (has_shared ? 1 : 0);
+  const bool use_mma = g_gemv_impl == 0 && mma_gemv_supported(static_cast<int>(H), static_cast<int>(I)) &&
+                       mma_gemv_supported(static_cast<int>(I), static_cast<int>(H));
+  const int chunk = use_mma ? 8 : nt;
   BucketArgs ba{};
   ba.keys = l.ids32; ba.rows = nullptr; ba.weights = l.wts; ba.n = static_cast<int>(T * k);
   ba.k = static_cast<int>(k); ba.key_lo = 0; ba.n_buckets = static_cast<int>(E);
   ba.bucket_offset = l.m.seg_offset; ba.pair_row = l.m.pair_row; ba.pair_weight = l.m.pair_weight;
   ba.pair_entry = l.m.pair_entry; ba.entry_pair = l.m.entry_pair; ba.tail = has_shared ? static_cast<int>(T) : 0;
-  MOE_CUDA(launch_bucket(ba, s), "dispatch");
+  ChunkArgs ca{l.m.seg_offset, static_cast<int>(S), chunk, l.m.chunk_seg, l.m.chunk_start, l.m.chunk_len,
+               l.m.n_chunks};
+  bool chunks_ready = false;
+  if (T <= 256 && E <= 768) {
+    // decode batches: split-K logits, then selection + dispatch + chunk list in one CTA
+    MOE_CUDA(launch_router_logits_split(hidden, hidden_dtype, router_weight, router_dtype, l.logits,
+                                        static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s),
+             "router logits");
+    RouteDispatchArgs rd{};
+    rd.partial = l.logits;
+    rd.nparts = router_split_parts(static_cast<int>(H));
+    rd.part_stride = T * E;
+    rd.bias = router_bias;
+    rd.select.tokens = static_cast<int>(T);
+    rd.select.experts = static_cast<int>(E);
+    rd.select.top_k = static_cast<int>(k);
+    rd.select.n_group = static_cast<int>(n_group);
+    rd.select.topk_group = static_cast<int>(topk_group);
+    rd.select.scoring = scoring;
+    rd.select.renorm = scoring == kScoreSigmoid;
+    rd.select.softmax_fp64 = 0;
+    rd.select.round_bf16 = hidden_dtype == kDtypeBF16;
+    rd.select.route_scale = route_scale;
+    rd.ids64 = out_ids;
+    rd.weights_bf16 = reinterpret_cast<__nv_bfloat16*>(out_weights_bf16);
+    rd.bucket.keys_out = l.ids32;
+    rd.bucket.weights_out = l.wts;
+    rd.bucket.args = ba;
+    rd.chunks = ca;
+    MOE_CUDA(launch_route_dispatch(rd, s), "route + dispatch");
+    chunks_ready = true;
+  } else {
+    // 1. route (weights rounded through bf16 like fp8_source.py:1547 when hidden is bf16)
+    code = route_impl(hidden, hidden_dtype, router_weight, router_dtype, router_bias, T, H, E, n_group, topk_group,
+                      k, scoring, 0, 0, route_scale, hidden_dtype == kDtypeBF16, out_ids, l.ids32, l.wts,
+                      out_weights_bf16, l.logits, s);
+    if (code != kOk) return code;
+    // 2. dispatch: expert-contiguous pairs, ascending token order inside an expert, shared expert last
+    MOE_CUDA(launch_bucket(ba, s), "dispatch");
+  }
   // 3. experts
-  const int64_t S = E + (has_shared ? 1 : 0);
   Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
   const bool vec = H % 16 == 0 && I % 16 == 0 && aligned16(hidden);
-  if (g_gemv_impl == 0 && mma_gemv_supported(static_cast<int>(H), static_cast<int>(I)) &&
-      mma_gemv_supported(static_cast<int>(I), static_cast<int>(H))) {
-    code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I, H, s);
+  if (use_mma) {
+    code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I, H,
+                                 chunks_ready, s);
   } else {
     code = run_expert_stages(t, hidden, xd, l.m, l.m.y, S, I, H, ceil_div(H, kBlock), ceil_div(I, kBlock), nt, vec, s);
   }

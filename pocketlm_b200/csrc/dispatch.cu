@@ -11,120 +11,57 @@
 // returns.  The scatter is deterministic: the rank of an entry inside its
 // bucket comes from a per-bucket bitmask of the current 1024-entry window, not
 // from atomics.
+#include <algorithm>
+
 #include "common.cuh"
 #include "dispatch.cuh"
+#include "dispatch_device.cuh"
+#include "router_device.cuh"
 
 namespace moe {
 
-constexpr int kBucketThreads = 1024;
-constexpr int kWindowWords = kBucketThreads / 32;
 
-// One CTA.  Entry i has key keys[i] (entries whose key falls outside
-// [key_lo, key_lo + n_buckets) are dropped), row rows ? rows[i] : i / k and
-// weight weights ? weights[i] : 1.
 __global__ void __launch_bounds__(kBucketThreads) bucket_kernel(BucketArgs a) {
   extern __shared__ uint32_t sm[];
-  uint32_t* mask = sm;                                  // [n_buckets][32]
-  int32_t* count = reinterpret_cast<int32_t*>(mask + a.n_buckets * kWindowWords);  // [n_buckets]
-  int32_t* base = count + a.n_buckets;                 // [n_buckets + 1]
-  const int tid = threadIdx.x;
-
-  for (int b = tid; b < a.n_buckets; b += kBucketThreads) count[b] = 0;
-  __syncthreads();
-  for (int i = tid; i < a.n; i += kBucketThreads) {
-    const int key = a.keys[i] - a.key_lo;
-    if (key >= 0 && key < a.n_buckets) atomicAdd(&count[key], 1);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int running = 0;
-    for (int b = 0; b < a.n_buckets; ++b) {
-      base[b] = running;
-      a.bucket_offset[b] = running;
-      running += count[b];
-    }
-    base[a.n_buckets] = running;
-    a.bucket_offset[a.n_buckets] = running;
-    if (a.tail > 0) a.bucket_offset[a.n_buckets + 1] = running + a.tail;
-    if (a.total) *a.total = running + (a.tail > 0 ? a.tail : 0);
-  }
-  if (a.counts)
-    for (int b = tid; b < a.n_buckets; b += kBucketThreads) a.counts[b] = count[b];
-  __syncthreads();
-  // base[b] now advances window by window: offset of the next free slot.
-  for (int w0 = 0; w0 < a.n; w0 += kBucketThreads) {
-    for (int j = tid; j < a.n_buckets * kWindowWords; j += kBucketThreads) mask[j] = 0;
-    __syncthreads();
-    const int i = w0 + tid;
-    int key = -1;
-    if (i < a.n) {
-      key = a.keys[i] - a.key_lo;
-      if (key >= 0 && key < a.n_buckets) {
-        atomicOr(&mask[key * kWindowWords + tid / 32], 1u << (tid % 32));
-      } else {
-        key = -1;
-      }
-    }
-    __syncthreads();
-    if (key >= 0) {
-      const uint32_t* m = mask + key * kWindowWords;
-      int rank = __popc(m[tid / 32] & ((1u << (tid % 32)) - 1u));
-      for (int wd = 0; wd < tid / 32; ++wd) rank += __popc(m[wd]);
-      const int p = base[key] + rank;
-      a.pair_row[p] = a.rows ? a.rows[i] : i / a.k;
-      if (a.pair_weight) a.pair_weight[p] = a.weights ? a.weights[i] : 1.0f;
-      if (a.pair_entry) a.pair_entry[p] = i;
-      if (a.entry_pair) a.entry_pair[i] = p;
-    } else if (i < a.n && a.entry_pair) {
-      a.entry_pair[i] = -1;
-    }
-    __syncthreads();
-    for (int b = tid; b < a.n_buckets; b += kBucketThreads) {
-      int c = 0;
-      for (int wd = 0; wd < kWindowWords; ++wd) c += __popc(mask[b * kWindowWords + wd]);
-      base[b] += c;
-    }
-    __syncthreads();
-  }
-  if (a.tail > 0) {
-    const int first = base[a.n_buckets];  // == number of kept entries
-    for (int r = tid; r < a.tail; r += kBucketThreads) {
-      a.pair_row[first + r] = r;
-      if (a.pair_weight) a.pair_weight[first + r] = 1.0f;
-      if (a.pair_entry) a.pair_entry[first + r] = -1;
-    }
-  }
+  bucket_body(a, sm);
 }
 
-// One CTA: segments -> chunks of at most `chunk` consecutive pairs.
 __global__ void __launch_bounds__(kBucketThreads) chunk_kernel(ChunkArgs a) {
   __shared__ int32_t scan[kBucketThreads];
-  const int tid = threadIdx.x;
-  const int per = static_cast<int>(ceil_div(a.n_segments, kBucketThreads));
-  const int s_lo = tid * per, s_hi = min(a.n_segments, s_lo + per);
-  int mine = 0;
-  for (int s = s_lo; s < s_hi; ++s) {
-    const int n = a.seg_offset[s + 1] - a.seg_offset[s];
-    mine += (n + a.chunk - 1) / a.chunk;
-  }
-  scan[tid] = mine;
+  chunk_body(a, scan);
+}
+
+// Decode batches in one launch: select every token's experts (one warp per
+// token, logits given as split-K partials), then bucket the (token, slot)
+// entries by expert and build the chunk list -- the work of
+// router_select_kernel + bucket_kernel + chunk_kernel without two launch gaps.
+__global__ void __launch_bounds__(kBucketThreads) route_dispatch_kernel(RouteDispatchArgs a) {
+  extern __shared__ uint32_t sm[];
+  __shared__ int32_t scan[kBucketThreads];
+  const int warp = threadIdx.x / kWarp;
+  float* scratch = reinterpret_cast<float*>(sm) + static_cast<size_t>(warp) * 2 * a.select.experts;
+  for (int t = warp; t < a.select.tokens; t += kBucketThreads / kWarp)
+    select_token(a.partial, a.nparts, a.part_stride, a.bias, a.select, t, scratch, scratch + a.select.experts,
+                 a.ids64, a.bucket.keys_out, a.bucket.weights_out, a.weights_bf16);
   __syncthreads();
-  for (int o = 1; o < kBucketThreads; o <<= 1) {
-    const int v = tid >= o ? scan[tid - o] : 0;
-    __syncthreads();
-    scan[tid] += v;
-    __syncthreads();
-  }
-  int c = scan[tid] - mine;
-  if (tid == kBucketThreads - 1) *a.n_chunks = scan[tid];
-  for (int s = s_lo; s < s_hi; ++s) {
-    const int lo = a.seg_offset[s], hi = a.seg_offset[s + 1];
-    for (int p = lo; p < hi; p += a.chunk, ++c) {
-      a.chunk_seg[c] = s;
-      a.chunk_start[c] = p;
-      a.chunk_len[c] = min(a.chunk, hi - p);
-    }
-  }
+  bucket_body(a.bucket.args, sm);
+  __syncthreads();
+  chunk_body(a.chunks, scan);
+}
+
+size_t route_dispatch_smem_bytes(int experts) {
+  const size_t select = static_cast<size_t>(kBucketThreads / kWarp) * 2 * experts * sizeof(float);
+  return std::max(select, bucket_smem_bytes(experts));
+}
+
+cudaError_t launch_route_dispatch(const RouteDispatchArgs& a, cudaStream_t stream) {
+  const size_t smem = route_dispatch_smem_bytes(a.select.experts);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  cudaError_t err = cudaFuncSetAttribute(route_dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+  if (err != cudaSuccess) return err;
+  route_dispatch_kernel<<<1, kBucketThreads, smem, stream>>>(a);
+  return cudaGetLastError();
 }
 
 size_t bucket_smem_bytes(int n_buckets) {

@@ -1,6 +1,7 @@
 // Dispatch launchers (dispatch.cu).
 #pragma once
 #include "common.cuh"
+#include "router.cuh"
 
 namespace moe {
 
@@ -39,6 +40,25 @@ struct ChunkArgs {
 inline int64_t chunk_capacity(int64_t pairs, int64_t segments, int chunk) {
   return pairs / chunk + segments + 1;
 }
+
+// Fused selection + bucket + chunk list (one CTA) for decode batches.
+struct RouteDispatchArgs {
+  const float* partial;       // split-K router logits partials
+  int nparts;
+  int64_t part_stride;        // floats between consecutive parts (tokens * experts)
+  const float* bias;          // [experts] or null
+  RouterSelectParams select;
+  int64_t* ids64;             // optional user outputs
+  __nv_bfloat16* weights_bf16;
+  struct {
+    int32_t* keys_out;        // == args.keys (ids32)
+    float* weights_out;       // == args.weights (fp32 route weights)
+    BucketArgs args;
+  } bucket;
+  ChunkArgs chunks;
+};
+size_t route_dispatch_smem_bytes(int experts);
+cudaError_t launch_route_dispatch(const RouteDispatchArgs& a, cudaStream_t stream);
 
 size_t bucket_smem_bytes(int n_buckets);
 cudaError_t launch_bucket(const BucketArgs& a, cudaStream_t stream);

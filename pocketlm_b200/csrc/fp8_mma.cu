@@ -91,21 +91,24 @@ __global__ void __launch_bounds__(256) rows_to_f16_kernel(const T* __restrict__ 
   }
 }
 
-// NS == 2: each warp task is 16 rows of two matrices (gate + up, SwiGLU
-// epilogue).  NS == 1: 32 rows of one matrix as two 16-row tiles.
+// A task is (chunk of <= 8 pairs, row tile): 16 rows of two matrices (gate +
+// up, SwiGLU epilogue) when NS == 2, 32 rows of one matrix as two 16-row tiles
+// when NS == 1.  The 4 warps of a CTA split the task's k-blocks round-robin
+// (warp w takes blocks w, w+4, ...), so even a one-token batch keeps four
+// warps per row tile streaming; their fp32 partial fragments meet in shared
+// memory, warp 0 adds them in a fixed order and writes the outputs.
 template <int NS, int EPI>
 __global__ void __launch_bounds__(kMmaCtaWarps * kWarp) mma_gemv_kernel(MmaArgs a) {
-  const int lane = threadIdx.x % kWarp;
+  __shared__ float red[kMmaCtaWarps - 1][kWarp][8];
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   const int g = lane / 4, c = lane % 4;
   const int K = a.K, N = a.N;
   constexpr int kTaskRows = NS == 2 ? 16 : 32;
   const int row_tiles = static_cast<int>(ceil_div(N, kTaskRows));
   const int64_t tasks = static_cast<int64_t>(*a.n_chunks) * row_tiles;
-  const int64_t warp_global = static_cast<int64_t>(blockIdx.x) * kMmaCtaWarps + threadIdx.x / kWarp;
-  const int64_t warp_count = static_cast<int64_t>(gridDim.x) * kMmaCtaWarps;
   const int nkb = K / kBlock;
 
-  for (int64_t task = warp_global; task < tasks; task += warp_count) {
+  for (int64_t task = blockIdx.x; task < tasks; task += gridDim.x) {
     const int ch = static_cast<int>(task / row_tiles);
     const int r0 = static_cast<int>(task % row_tiles) * kTaskRows;
     const int seg = a.chunk_seg[ch], p0 = a.chunk_start[ch], len = a.chunk_len[ch];
@@ -183,46 +186,65 @@ __global__ void __launch_bounds__(kMmaCtaWarps * kWarp) mma_gemv_kernel(MmaArgs 
           for (int i = 0; i < 4; ++i) acc[st][i] = fmaf(t[st][i], sc, acc[st][i]);
         }
       };
-      // ping-pong register buffers, one k-block of loads in flight ahead of the math
+      // this warp's k-blocks: warp, warp + 4, ...; ping-pong register buffers
+      // keep one k-block of loads in flight ahead of the math
       KBlock buf0, buf1;
-      load(buf0, 0);
-      for (int kbi = 0; kbi < nkb; kbi += 2) {
-        if (kbi + 1 < nkb) load(buf1, kbi + 1);
+      constexpr int kStep = kMmaCtaWarps;
+      if (warp < nkb) load(buf0, warp);
+      for (int kbi = warp; kbi < nkb; kbi += 2 * kStep) {
+        if (kbi + kStep < nkb) load(buf1, kbi + kStep);
         compute(buf0, kbi);
-        if (kbi + 1 < nkb) {
-          if (kbi + 2 < nkb) load(buf0, kbi + 2);
-          compute(buf1, kbi + 1);
+        if (kbi + kStep < nkb) {
+          if (kbi + 2 * kStep < nkb) load(buf0, kbi + 2 * kStep);
+          compute(buf1, kbi + kStep);
         }
       }
     }
 
-    // epilogue: lane holds rows (g, g+8) x tokens (2c, 2c+1) per stream
+    // combine the 4 warps' partial fragments (fixed order), warp 0 finishes
+    if (warp > 0) {
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int tok = 2 * c + j;
-      if (tok >= len) continue;
-      const int64_t tr = a.pair_row ? a.pair_row[p0 + tok] : static_cast<int64_t>(p0 + tok);
-      const float xs = a.xscale[tr];
-      const int64_t p = p0 + tok;
+      for (int st = 0; st < 2; ++st)
 #pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int i = rr * 2 + j;
-        if (NS == 2) {
-          const int row = r0 + g + 8 * rr;
-          if (row < N) {
-            const float gv = acc[0][i] * xs, uv = acc[1][i] * xs;
-            const float silu = gv / (1.0f + expf(-gv));
-            a.out0[p * N + row] = EPI == kEpiSwiglu ? silu * uv : gv;
-          }
-        } else {
+        for (int i = 0; i < 4; ++i) red[warp - 1][lane][st * 4 + i] = acc[st][i];
+    }
+    __syncthreads();
+    if (warp == 0) {
 #pragma unroll
-          for (int st = 0; st < 2; ++st) {
-            const int row = r0 + 16 * st + g + 8 * rr;
-            if (row < N) a.out0[p * N + row] = acc[st][i] * xs;
+      for (int w = 0; w < kMmaCtaWarps - 1; ++w)
+#pragma unroll
+        for (int st = 0; st < 2; ++st)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[st][i] += red[w][lane][st * 4 + i];
+      // epilogue: lane holds rows (g, g+8) x tokens (2c, 2c+1) per stream
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int tok = 2 * c + j;
+        if (tok >= len) continue;
+        const int64_t tr = a.pair_row ? a.pair_row[p0 + tok] : static_cast<int64_t>(p0 + tok);
+        const float xs = a.xscale[tr];
+        const int64_t p = p0 + tok;
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int i = rr * 2 + j;
+          if (NS == 2) {
+            const int row = r0 + g + 8 * rr;
+            if (row < N) {
+              const float gv = acc[0][i] * xs, uv = acc[1][i] * xs;
+              const float silu = gv / (1.0f + expf(-gv));
+              a.out0[p * N + row] = EPI == kEpiSwiglu ? silu * uv : gv;
+            }
+          } else {
+#pragma unroll
+            for (int st = 0; st < 2; ++st) {
+              const int row = r0 + 16 * st + g + 8 * rr;
+              if (row < N) a.out0[p * N + row] = acc[st][i] * xs;
+            }
           }
         }
       }
     }
+    __syncthreads();  // red[] is reused by the next task
   }
 }
 
@@ -246,7 +268,7 @@ cudaError_t launch_rows_to_f16(const void* src, bool src_bf16, int rows, int K, 
 }
 
 cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream) {
-  const int blocks_per_sm = 16;  // 64 warps per SM at most
+  const int blocks_per_sm = 4;  // register-limited: about 3 resident CTAs of 4 warps
   const unsigned grid = static_cast<unsigned>(gemv_grid_ctas() * blocks_per_sm);
   if (ns == 2 && epi == kEpiSwiglu) mma_gemv_kernel<2, kEpiSwiglu><<<grid, kMmaCtaWarps * kWarp, 0, stream>>>(a);
   else if (ns == 1 && epi == kEpiStore) mma_gemv_kernel<1, kEpiStore><<<grid, kMmaCtaWarps * kWarp, 0, stream>>>(a);

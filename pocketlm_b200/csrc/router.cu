@@ -11,12 +11,10 @@
 // summation order differs, so selections agree except at score ties.
 #include "common.cuh"
 #include "router.cuh"
+#include "router_device.cuh"
 
 namespace moe {
 
-MOE_D float to_float_any(float v) { return v; }
-MOE_D float to_float_any(__nv_bfloat16 v) { return __bfloat162float(v); }
-MOE_D float to_float_any(__half v) { return __half2float(v); }
 
 template <typename T>
 MOE_D void load8(const T* p, float* out);
@@ -124,6 +122,60 @@ __global__ void __launch_bounds__(256) router_logits_gemv_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Logits, decode batches: split-K partial dot products.  CTA (expert octet,
+// 1024-column part): each warp holds its expert's 1024 weights in registers
+// (32 per lane) and walks the tokens; partial[q][t][e] is summed over the
+// parts q in a fixed order by the selection (select_token), so the result is
+// deterministic.  Parallelism = experts/8 x ceil(H/1024) CTAs of 8 warps.
+// ---------------------------------------------------------------------------
+constexpr int kSplitCols = 1024;
+
+template <typename XT, typename WT>
+__global__ void __launch_bounds__(256) router_logits_split_kernel(
+    const XT* __restrict__ x, const WT* __restrict__ w, float* __restrict__ partial, int tokens, int hidden,
+    int experts, int vec_ok) {
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int e = blockIdx.x * 8 + warp;
+  const int q = blockIdx.y;
+  if (e >= experts) return;
+  const int lo = q * kSplitCols, hi = min(hidden, lo + kSplitCols);
+  const WT* wrow = w + static_cast<int64_t>(e) * hidden;
+  float wv[4][8];
+  bool on[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int k = lo + j * 256 + lane * 8;
+    on[j] = k < hi;
+    if (vec_ok) {
+      if (on[j]) load8<WT>(wrow + k, wv[j]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wv[j][i] = (on[j] && k + i < hi) ? to_float_any(wrow[k + i]) : 0.0f;
+    }
+  }
+  for (int t = 0; t < tokens; ++t) {
+    const XT* xr = x + static_cast<int64_t>(t) * hidden;
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (!on[j]) continue;
+      const int k = lo + j * 256 + lane * 8;
+      float xv[8];
+      if (vec_ok) {
+        load8<XT>(xr + k, xv);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xv[i] = k + i < hi ? to_float_any(xr[k + i]) : 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[j][i], acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) partial[(static_cast<int64_t>(q) * tokens + t) * experts + e] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Logits, large token counts: 64x64 output tiles, 4x4 per thread, k-tiles of
 // 32 staged through shared memory (row-major copies of x and w tiles).
 // ---------------------------------------------------------------------------
@@ -177,129 +229,17 @@ __global__ void __launch_bounds__(256) router_logits_tiled_kernel(
 // ---------------------------------------------------------------------------
 // Selection: one warp per token.
 // ---------------------------------------------------------------------------
-constexpr int kSelectWarps = 4;
-
 __global__ void __launch_bounds__(kSelectWarps * kWarp) router_select_kernel(
-    const float* __restrict__ logits, const float* __restrict__ bias, RouterSelectParams p,
-    int64_t* __restrict__ ids64, int32_t* __restrict__ ids32, float* __restrict__ weights_f32,
-    __nv_bfloat16* __restrict__ weights_bf16) {
+    const float* __restrict__ logits, int nparts, int64_t part_stride, const float* __restrict__ bias,
+    RouterSelectParams p, int64_t* __restrict__ ids64, int32_t* __restrict__ ids32,
+    float* __restrict__ weights_f32, __nv_bfloat16* __restrict__ weights_bf16) {
   extern __shared__ float smem[];
-  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int warp = threadIdx.x / kWarp;
   const int t = blockIdx.x * kSelectWarps + warp;
   if (t >= p.tokens) return;
-  const int E = p.experts;
-  float* probs = smem + warp * 2 * E;
-  float* choice = probs + E;
-  const float* row = logits + static_cast<int64_t>(t) * E;
-
-  // scores: sigmoid, or softmax (max-subtracted)
-  if (p.scoring == kScoreSigmoid) {
-    for (int e = lane; e < E; e += kWarp) probs[e] = 1.0f / (1.0f + expf(-row[e]));
-  } else {
-    float m = -INFINITY;
-    for (int e = lane; e < E; e += kWarp) m = fmaxf(m, row[e]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-    for (int e = lane; e < E; e += kWarp) probs[e] = expf(row[e] - m);
-    __syncwarp();
-    if (p.softmax_fp64) {
-      // ds_router_topk_u16: fp64 denominator, summed in expert order
-      // (ds_forward.cpp:913-924)
-      double denom = 0.0;
-      if (lane == 0)
-        for (int e = 0; e < E; ++e) denom += static_cast<double>(probs[e]);
-      denom = __shfl_sync(0xFFFFFFFFu, denom, 0);
-      for (int e = lane; e < E; e += kWarp) probs[e] = static_cast<float>(static_cast<double>(probs[e]) / denom);
-    } else {
-      float s = 0.0f;
-      for (int e = lane; e < E; e += kWarp) s += probs[e];
-      s = warp_sum(s);
-      for (int e = lane; e < E; e += kWarp) probs[e] = probs[e] / s;
-    }
-  }
-  __syncwarp();
-  for (int e = lane; e < E; e += kWarp) choice[e] = bias ? probs[e] + bias[e] : probs[e];
-  __syncwarp();
-
-  // group-limited selection (fp8_source.py:5125-5140)
-  if (p.n_group > 1) {
-    const int G = E / p.n_group;
-    float gscore = -INFINITY;
-    if (lane < p.n_group) {
-      float best = -INFINITY, second = -INFINITY;
-      for (int i = 0; i < G; ++i) {
-        const float v = choice[lane * G + i];
-        if (v > best) {
-          second = best;
-          best = v;
-        } else if (v > second) {
-          second = v;
-        }
-      }
-      gscore = bias ? best + second : best;
-    }
-    uint32_t keep = 0;
-    const int kg = max(1, min(p.topk_group, p.n_group));
-    for (int j = 0; j < kg; ++j) {
-      float v = (keep >> lane) & 1u ? -INFINITY : gscore;
-      int idx = lane < p.n_group ? lane : 0x7FFFFFFF;
-      if ((keep >> lane) & 1u) idx = 0x7FFFFFFF;
-      warp_argmax(v, idx);
-      if (idx < kWarp) keep |= 1u << idx;
-    }
-    for (int e = lane; e < E; e += kWarp)
-      if (!((keep >> (e / G)) & 1u)) choice[e] = -INFINITY;
-    __syncwarp();
-  }
-
-  // top-k, ties to the lower expert id
-  const int k = p.top_k;
-  int my_id = -1;      // lane j < k holds the j-th pick
-  float my_prob = 0.0f;
-  for (int j = 0; j < k; ++j) {
-    float v = -INFINITY;
-    int idx = 0x7FFFFFFF;
-    for (int e = lane; e < E; e += kWarp) {
-      const float c = choice[e];
-      if (c > v || (c == v && e < idx)) {
-        v = c;
-        idx = e;
-      }
-    }
-    warp_argmax(v, idx);
-    if (idx == 0x7FFFFFFF) idx = 0;  // every remaining score is -inf / NaN
-    if (lane == j) {
-      my_id = idx;
-      my_prob = probs[idx];
-    }
-    __syncwarp();
-    // a picked expert becomes NaN: every comparison with it is false, so it
-    // is never picked again even when the remaining scores are all -inf
-    if (lane == 0) choice[idx] = __int_as_float(0x7FC00000);
-    __syncwarp();
-  }
-
-  float w = my_prob;
-  if (p.renorm) {
-    if (p.softmax_fp64) {
-      double s = 0.0;
-      for (int j = 0; j < k; ++j) s += static_cast<double>(__shfl_sync(0xFFFFFFFFu, my_prob, j));
-      w = static_cast<float>(static_cast<double>(my_prob) / s);
-    } else {
-      float s = 0.0f;
-      for (int j = 0; j < k; ++j) s += __shfl_sync(0xFFFFFFFFu, my_prob, j);
-      w = my_prob / fmaxf(s, 1e-12f);
-    }
-  }
-  w = w * p.route_scale;
-  if (lane < k) {
-    const int64_t o = static_cast<int64_t>(t) * k + lane;
-    if (p.round_bf16) w = __bfloat162float(__float2bfloat16_rn(w));
-    if (ids64) ids64[o] = my_id;
-    if (ids32) ids32[o] = my_id;
-    if (weights_f32) weights_f32[o] = w;
-    if (weights_bf16) weights_bf16[o] = __float2bfloat16_rn(w);
-  }
+  float* probs = smem + warp * 2 * p.experts;
+  select_token(logits, nparts, part_stride, bias, p, t, probs, probs + p.experts, ids64, ids32, weights_f32,
+               weights_bf16);
 }
 
 // ---------------------------------------------------------------------------
@@ -335,6 +275,41 @@ static cudaError_t launch_logits_w(const void* x, int w_dtype, const void* w, fl
   }
 }
 
+template <typename XT, typename WT>
+static cudaError_t launch_split_t(const void* x, const void* w, float* partial, int tokens, int hidden, int experts,
+                                  cudaStream_t stream) {
+  const bool vec_ok = hidden % 8 == 0 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                      (reinterpret_cast<uintptr_t>(w) % 16 == 0);
+  dim3 grid(static_cast<unsigned>(ceil_div(experts, 8)), static_cast<unsigned>(ceil_div(hidden, kSplitCols)));
+  router_logits_split_kernel<XT, WT><<<grid, 256, 0, stream>>>(static_cast<const XT*>(x), static_cast<const WT*>(w),
+                                                                partial, tokens, hidden, experts, vec_ok ? 1 : 0);
+  return cudaGetLastError();
+}
+
+template <typename XT>
+static cudaError_t launch_split_w(const void* x, int w_dtype, const void* w, float* partial, int tokens, int hidden,
+                                  int experts, cudaStream_t stream) {
+  switch (w_dtype) {
+    case kDtypeF32: return launch_split_t<XT, float>(x, w, partial, tokens, hidden, experts, stream);
+    case kDtypeBF16: return launch_split_t<XT, __nv_bfloat16>(x, w, partial, tokens, hidden, experts, stream);
+    case kDtypeF16: return launch_split_t<XT, __half>(x, w, partial, tokens, hidden, experts, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+int router_split_parts(int hidden) { return static_cast<int>(ceil_div(hidden, kSplitCols)); }
+
+cudaError_t launch_router_logits_split(const void* x, int x_dtype, const void* w, int w_dtype, float* partial,
+                                       int tokens, int hidden, int experts, cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  switch (x_dtype) {
+    case kDtypeF32: return launch_split_w<float>(x, w_dtype, w, partial, tokens, hidden, experts, stream);
+    case kDtypeBF16: return launch_split_w<__nv_bfloat16>(x, w_dtype, w, partial, tokens, hidden, experts, stream);
+    case kDtypeF16: return launch_split_w<__half>(x, w_dtype, w, partial, tokens, hidden, experts, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 cudaError_t launch_router_logits(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
                                  int tokens, int hidden, int experts, cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
@@ -357,7 +332,7 @@ cudaError_t launch_router_select(const float* logits, const float* bias, const R
                                            static_cast<int>(smem));
     if (err != cudaSuccess) return err;
   }
-  router_select_kernel<<<grid, kSelectWarps * kWarp, smem, stream>>>(logits, bias, p, ids64, ids32,
+  router_select_kernel<<<grid, kSelectWarps * kWarp, smem, stream>>>(logits, 1, 0, bias, p, ids64, ids32,
                                                                       weights_f32, weights_bf16);
   return cudaGetLastError();
 }

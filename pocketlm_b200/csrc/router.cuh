@@ -24,6 +24,11 @@ struct RouterSelectParams {
 cudaError_t launch_router_logits(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
                                  int tokens, int hidden, int experts, cudaStream_t stream);
 
+// Split-K logits for decode batches: partial[q][t][e], q < router_split_parts(hidden).
+int router_split_parts(int hidden);
+cudaError_t launch_router_logits_split(const void* x, int x_dtype, const void* w, int w_dtype, float* partial,
+                                       int tokens, int hidden, int experts, cudaStream_t stream);
+
 cudaError_t launch_router_select(const float* logits, const float* bias, const RouterSelectParams& p,
                                  int64_t* ids64, int32_t* ids32, float* weights_f32,
                                  __nv_bfloat16* weights_bf16, cudaStream_t stream);
