@@ -246,12 +246,14 @@ int moe_b200_stage_times(float* ms, int max_n);
  * the warp-MMA kernel on the whole-layer path when hidden and intermediate
  * sizes are multiples of 128, the direct-load kernel elsewhere), 1 = the
  * warp-specialised bulk-copy streaming kernel wherever the shape allows,
- * 2 = the direct-load kernel everywhere.  For A/B parity tests and
- * measurements. */
+ * 2 = the direct-load kernel everywhere, 3 = like 0 but the warp-MMA kernel
+ * loads its weights into registers instead of through its TMA bulk-copy
+ * ring.  For A/B parity tests and measurements. */
 int moe_b200_select_gemv(int impl);
 
 /* Device error word (no reference counterpart): nonzero when a bounded wait
- * inside a kernel gave up (1: producer, 2: consumer, 4: drain).  Synchronises
+ * inside a kernel gave up (1: producer, 2: consumer, 4: drain, 8: misaligned
+ * weights refused by the streaming kernel, 16: warp-MMA ring).  Synchronises
  * `stream`, returns the word (-1 if it cannot be read) and clears it. */
 int moe_b200_device_error(void* stream);
 

@@ -13,6 +13,24 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 // fp8_stream.cu includes this header and reads the word back.
 static __device__ int g_device_error = 0;
 
+// Host: read this translation unit's error word, clear it, return it (-1 if unreadable).
+static inline int read_and_clear_local_error(cudaStream_t stream) {
+  int host = 0;
+  if (cudaMemcpyFromSymbolAsync(&host, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return -1;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return -1;
+  if (host) {
+    const int zero = 0;
+    cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
+    cudaStreamSynchronize(stream);
+  }
+  return host;
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (bulk copy) writes to the same shared memory.
+MOE_D void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 MOE_D uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
 MOE_D uint64_t global_timer_ns() {

@@ -75,6 +75,8 @@ int g_marks = 0;
 // shapes allow, direct-load elsewhere), 1 = bulk-copy streaming kernel where
 // supported, 2 = direct-load kernel everywhere.
 int g_gemv_impl = 0;
+// Operand feed of the warp-MMA kernel: 1 = TMA bulk-copy ring per warp (default), 0 = register loads.
+int g_mma_feed = 1;
 
 cudaError_t gemv(const GemvArgs& a, int x_dtype, int ns, int epi, int nt, bool vec, cudaStream_t stream) {
   if (g_gemv_impl == 1 && vec && stream_gemv_supported(a.K, x_dtype, nt))
@@ -634,7 +636,8 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
   g1.chunk_seg = m.chunk_seg; g1.chunk_start = m.chunk_start; g1.chunk_len = m.chunk_len; g1.n_chunks = m.n_chunks;
   g1.out0 = m.act; g1.N = static_cast<int>(I); g1.K = static_cast<int>(H);
   g1.scale_cols = static_cast<int>(ceil_div(H, kBlock)); g1.nanfix = 1;
-  MOE_CUDA(launch_mma_gemv(g1, 2, kEpiSwiglu, s), "gate/up stage");
+  MOE_CUDA(g_mma_feed == 1 ? launch_tma_mma_gemv(g1, 2, kEpiSwiglu, s) : launch_mma_gemv(g1, 2, kEpiSwiglu, s),
+           "gate/up stage");
   stage_mark(s);
   MOE_CUDA(launch_rows_to_f16(m.act, false, static_cast<int>(pairs), static_cast<int>(I), nullptr, l.act16,
                               l.ascale, s),
@@ -645,7 +648,8 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
   g2.x16 = l.act16; g2.xscale = l.ascale; g2.pair_row = nullptr;
   g2.out0 = m.y; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
   g2.scale_cols = static_cast<int>(ceil_div(I, kBlock));
-  MOE_CUDA(launch_mma_gemv(g2, 1, kEpiStore, s), "down stage");
+  MOE_CUDA(g_mma_feed == 1 ? launch_tma_mma_gemv(g2, 1, kEpiStore, s) : launch_mma_gemv(g2, 1, kEpiStore, s),
+           "down stage");
   stage_mark(s);
   return kOk;
 }
@@ -691,7 +695,7 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   ChunkArgs ca{l.m.seg_offset, static_cast<int>(S), chunk, l.m.chunk_seg, l.m.chunk_start, l.m.chunk_len,
                l.m.n_chunks};
   bool chunks_ready = false;
-  if (T <= 256 && E <= 768) {
+  if (T <= 256 && route_dispatch_smem_bytes(static_cast<int>(T), static_cast<int>(E)) <= 200 * 1024) {
     // decode batches: split-K logits, then selection + dispatch + chunk list in one CTA
     MOE_CUDA(launch_router_logits_split(hidden, hidden_dtype, router_weight, router_dtype, l.logits,
                                         static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s),
@@ -763,12 +767,17 @@ int moe_b200_stage_timing(int enable) {
 }
 
 int moe_b200_select_gemv(int impl) {
-  if (impl < 0 || impl > 2) return fail(kBadDims, "impl must be 0, 1 or 2");
-  g_gemv_impl = impl;
+  if (impl < 0 || impl > 3) return fail(kBadDims, "impl must be 0, 1, 2 or 3");
+  g_gemv_impl = impl == 3 ? 0 : impl;
+  g_mma_feed = impl == 3 ? 0 : 1;
   return kOk;
 }
 
-int moe_b200_device_error(void* stream) { return read_and_clear_device_error(as_stream(stream)); }
+int moe_b200_device_error(void* stream) {
+  const int a = read_and_clear_device_error(as_stream(stream));
+  const int b = read_and_clear_mma_device_error(as_stream(stream));
+  return (a < 0 || b < 0) ? -1 : (a | b);
+}
 
 int moe_b200_stage_times(float* ms, int max_n) {
   if (!ms) return fail(kNullPointer, "null pointer");

@@ -39,24 +39,38 @@ __global__ void __launch_bounds__(kBucketThreads) route_dispatch_kernel(RouteDis
   extern __shared__ uint32_t sm[];
   __shared__ int32_t scan[kBucketThreads];
   const int warp = threadIdx.x / kWarp;
-  float* scratch = reinterpret_cast<float*>(sm) + static_cast<size_t>(warp) * 2 * a.select.experts;
-  for (int t = warp; t < a.select.tokens; t += kBucketThreads / kWarp)
-    select_token(a.partial, a.nparts, a.part_stride, a.bias, a.select, t, scratch, scratch + a.select.experts,
-                 a.ids64, a.bucket.keys_out, a.bucket.weights_out, a.weights_bf16);
+  const int E = a.select.experts, T = a.select.tokens;
+  // logits = sum of the split-K partials, in part order, summed by the whole CTA
+  float* logits = reinterpret_cast<float*>(sm);
+  for (int i = threadIdx.x; i < T * E; i += kBucketThreads) {
+    float parts[kMaxRouterParts];
+#pragma unroll
+    for (int q = 0; q < kMaxRouterParts; ++q) parts[q] = q < a.nparts ? a.partial[q * a.part_stride + i] : 0.0f;
+    float v = parts[0];
+#pragma unroll
+    for (int q = 1; q < kMaxRouterParts; ++q) v += q < a.nparts ? parts[q] : 0.0f;
+    logits[i] = v;
+  }
+  __syncthreads();
+  float* scratch = logits + static_cast<size_t>(T) * E + static_cast<size_t>(warp) * 2 * E;
+  for (int t = warp; t < T; t += kBucketThreads / kWarp)
+    select_token(logits, 1, 0, a.bias, a.select, t, scratch, scratch + E, a.ids64, a.bucket.keys_out,
+                 a.bucket.weights_out, a.weights_bf16);
   __syncthreads();
   bucket_body(a.bucket.args, sm);
   __syncthreads();
   chunk_body(a.chunks, scan);
 }
 
-size_t route_dispatch_smem_bytes(int experts) {
-  const size_t select = static_cast<size_t>(kBucketThreads / kWarp) * 2 * experts * sizeof(float);
+size_t route_dispatch_smem_bytes(int tokens, int experts) {
+  const size_t select = (static_cast<size_t>(tokens) * experts +
+                         static_cast<size_t>(kBucketThreads / kWarp) * 2 * experts) * sizeof(float);
   return std::max(select, bucket_smem_bytes(experts));
 }
 
 cudaError_t launch_route_dispatch(const RouteDispatchArgs& a, cudaStream_t stream) {
-  const size_t smem = route_dispatch_smem_bytes(a.select.experts);
-  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  const size_t smem = route_dispatch_smem_bytes(a.select.tokens, a.select.experts);
+  if (smem > 200 * 1024 || a.nparts > kMaxRouterParts) return cudaErrorInvalidValue;
   cudaError_t err = cudaFuncSetAttribute(route_dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return err;

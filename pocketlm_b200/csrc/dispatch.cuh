@@ -57,7 +57,7 @@ struct RouteDispatchArgs {
   } bucket;
   ChunkArgs chunks;
 };
-size_t route_dispatch_smem_bytes(int experts);
+size_t route_dispatch_smem_bytes(int tokens, int experts);
 cudaError_t launch_route_dispatch(const RouteDispatchArgs& a, cudaStream_t stream);
 
 size_t bucket_smem_bytes(int n_buckets);

@@ -223,6 +223,7 @@ __global__ void combine_kernel(CombineArgs a) {
   if (h >= a.H) return;
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   const int width = vec ? 4 : 1;
+#pragma unroll 8
   for (int j = lo; j < hi; ++j) {
     const int p = a.row_pairs ? a.row_pairs[j] : j;
     if (p < 0) continue;
@@ -310,7 +311,7 @@ cudaError_t launch_grouped_gemv(const GemvArgs& a, int x_dtype, int ns, int epi,
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t stream) {
   if (a.T <= 0) return cudaSuccess;
   const int per_thread = (a.H % 4) == 0 ? 4 : 1;
-  const int threads = 256;
+  const int threads = 64;
   dim3 grid(static_cast<unsigned>(ceil_div(ceil_div(a.H, per_thread), threads)), static_cast<unsigned>(a.T));
   combine_kernel<<<grid, threads, 0, stream>>>(a);
   return cudaGetLastError();

@@ -77,6 +77,9 @@ struct MmaArgs {
 };
 bool mma_gemv_supported(int K, int N);
 cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream);
+// Same computation, weights fed to each warp by TMA bulk copies (fp8_mma.cu).
+cudaError_t launch_tma_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream);
+int read_and_clear_mma_device_error(cudaStream_t stream);
 cudaError_t launch_rows_to_f16(const void* src, bool src_bf16, int rows, int K, const int32_t* n_rows_dev,
                                __half* dst, float* scale, cudaStream_t stream);
 

@@ -27,6 +27,7 @@
 
 #include <algorithm>
 
+#include "async_copy.cuh"
 #include "common.cuh"
 #include "fp8_gemv.cuh"
 
@@ -61,15 +62,48 @@ struct KBlock {
 // dst[r, k] = src[r, k] / scale[r], scale = 2^(floor(log2(amax)) - 13) so the
 // largest magnitude lands in [2^13, 2^14) (1 for an all-zero row).
 template <typename T>
+MOE_D void unpack16(const uint4& v, float* out);
+
+template <>
+MOE_D void unpack16<float>(const uint4& v, float* out) {
+  out[0] = __uint_as_float(v.x);
+  out[1] = __uint_as_float(v.y);
+  out[2] = __uint_as_float(v.z);
+  out[3] = __uint_as_float(v.w);
+}
+
+template <>
+MOE_D void unpack16<__nv_bfloat16>(const uint4& v, float* out) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(w[i] << 16);
+    out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// Activation rows -> f16 with a per-row power-of-two scale:
+// dst[r, k] = src[r, k] / scale[r], scale = 2^(floor(log2(amax)) - 13) so the
+// largest magnitude lands in [2^13, 2^14) (1 for an all-zero row).  One CTA
+// per row, 16-byte loads (K * sizeof(T) must be a multiple of 16).
+template <typename T>
 __global__ void __launch_bounds__(256) rows_to_f16_kernel(const T* __restrict__ src, int rows, int K,
                                                           const int32_t* __restrict__ n_rows_dev,
                                                           __half* __restrict__ dst, float* __restrict__ scale) {
+  constexpr int V = 16 / sizeof(T);
   __shared__ float red[8];
   const int n_rows = n_rows_dev ? min(rows, *n_rows_dev) : rows;
+  const int n16 = K / V;
   for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
-    const T* s = src + static_cast<int64_t>(r) * K;
+    const uint4* s = reinterpret_cast<const uint4*>(src + static_cast<int64_t>(r) * K);
     float amax = 0.0f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) amax = fmaxf(amax, fabsf(to_float<T>(s[k])));
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+      float v[V];
+      unpack16<T>(__ldg(s + i), v);
+#pragma unroll
+      for (int j = 0; j < V; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
     if (threadIdx.x % kWarp == 0) red[threadIdx.x / kWarp] = amax;
@@ -85,7 +119,19 @@ __global__ void __launch_bounds__(256) rows_to_f16_kernel(const T* __restrict__ 
     const float sc = (amax > 0.0f && isfinite(amax)) ? ldexpf(1.0f, ilogbf(amax) - 13) : 1.0f;
     const float inv = 1.0f / sc;  // exact: power of two
     __half* d = dst + static_cast<int64_t>(r) * K;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) d[k] = __float2half_rn(to_float<T>(s[k]) * inv);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+      float v[V];
+      unpack16<T>(__ldg(s + i), v);
+      __align__(16) __half h[V];
+#pragma unroll
+      for (int j = 0; j < V; ++j) h[j] = __float2half_rn(v[j] * inv);
+      if (V == 8) {
+        *reinterpret_cast<uint4*>(d + i * V) = *reinterpret_cast<const uint4*>(h);
+      } else {
+        *reinterpret_cast<uint2*>(d + i * V) = *reinterpret_cast<const uint2*>(h);
+      }
+    }
     if (threadIdx.x == 0) scale[r] = sc;
     __syncthreads();
   }
@@ -249,6 +295,181 @@ __global__ void __launch_bounds__(kMmaCtaWarps * kWarp) mma_gemv_kernel(MmaArgs 
 }
 
 // ---------------------------------------------------------------------------
+// The same tasks fed by TMA: every warp owns a ring of kTmaStages shared-memory
+// stages; lane l bulk-copies (cp.async.bulk) the 128-byte k-block slice of its
+// row-stream l (stream l / 16, row l % 16 of the task) into slot l of a stage,
+// completing on the stage's mbarrier.  Slots are 192 bytes apart so that the
+// eight lanes of each shared-memory phase (rows g, g+1, all four c) hit 32
+// distinct banks.  With four stages a warp keeps 16 KiB of weight reads in
+// flight without holding them in registers.
+// ---------------------------------------------------------------------------
+constexpr int kTmaWarps = 4;
+constexpr int kTmaStages = 4;
+constexpr int kSlotBytes = 192;
+constexpr int kStageBytes = 32 * kSlotBytes;
+constexpr size_t kTmaSmem = static_cast<size_t>(kTmaWarps) * kTmaStages * kStageBytes +
+                            static_cast<size_t>(kTmaWarps) * kTmaStages * sizeof(uint64_t);
+
+template <int NS, int EPI>
+__global__ void __launch_bounds__(kTmaWarps * kWarp) tma_mma_gemv_kernel(MmaArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int g = lane / 4, c = lane % 4;
+  const int K = a.K, N = a.N;
+  unsigned char* ring = smem + static_cast<size_t>(warp) * kTmaStages * kStageBytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(kTmaWarps) * kTmaStages * kStageBytes) +
+                  warp * kTmaStages;
+  if (lane == 0) {
+    for (int s = 0; s < kTmaStages; ++s) mbar_init(&bar[s], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+
+  constexpr int kTaskRows = NS == 2 ? 16 : 32;
+  const int row_tiles = static_cast<int>(ceil_div(N, kTaskRows));
+  const int64_t tasks = static_cast<int64_t>(*a.n_chunks) * row_tiles;
+  const int64_t warp_global = static_cast<int64_t>(blockIdx.x) * kTmaWarps + warp;
+  const int64_t warp_count = static_cast<int64_t>(gridDim.x) * kTmaWarps;
+  const int nkb = K / kBlock;
+  uint32_t issued = 0, consumed = 0;
+
+  for (int64_t task = warp_global; task < tasks; task += warp_count) {
+    const int ch = static_cast<int>(task / row_tiles);
+    const int r0 = static_cast<int>(task % row_tiles) * kTaskRows;
+    const int seg = a.chunk_seg[ch], p0 = a.chunk_start[ch], len = a.chunk_len[ch];
+    const uint8_t* w0 = reinterpret_cast<const uint8_t*>(a.w0[seg]);
+    const float* s0 = reinterpret_cast<const float*>(a.s0[seg]);
+    const uint8_t* w1 = NS == 2 ? reinterpret_cast<const uint8_t*>(a.w1[seg]) : w0;
+    const float* s1 = NS == 2 ? reinterpret_cast<const float*>(a.s1[seg]) : s0;
+    const bool present = w0 && s0 && w1 && s1 &&
+                         ((reinterpret_cast<uintptr_t>(w0) | reinterpret_cast<uintptr_t>(w1)) & 15u) == 0;
+    // row-stream of this lane's copies: stream lane / 16, row lane % 16 of that stream's 16-row tile
+    const int my_st = lane / 16;
+    const int my_row = min((NS == 2 ? r0 : r0 + 16 * my_st) + lane % 16, N - 1);
+    const uint8_t* my_src = present ? (my_st == 0 ? w0 : w1) + static_cast<int64_t>(my_row) * K : nullptr;
+    const float* srow[2];
+#pragma unroll
+    for (int st = 0; st < 2; ++st) {
+      const int base = NS == 2 ? r0 : r0 + 16 * st;
+      srow[st] = present ? (st == 0 ? s0 : s1) + static_cast<int64_t>(min(base, N - 1) / kBlock) * a.scale_cols
+                         : nullptr;
+    }
+    const bool bvalid = g < len;
+    const int64_t brow = bvalid ? (a.pair_row ? a.pair_row[p0 + g] : static_cast<int64_t>(p0 + g)) : 0;
+    const __half* xb = a.x16 + brow * K + 16 * c;
+
+    auto issue = [&](int kbi) {
+      const uint32_t stage = issued % kTmaStages;
+      if (lane == 0) mbar_arrive_expect_tx(&bar[stage], 32u * kBlock);
+      __syncwarp();
+      bulk_copy_g2s(ring + stage * kStageBytes + lane * kSlotBytes, my_src + static_cast<int64_t>(kbi) * kBlock,
+                    kBlock, &bar[stage]);
+      ++issued;
+    };
+    auto load_b = [&](uint4 (&b)[2][2], int kbi) {
+#pragma unroll
+      for (int sp = 0; sp < 2; ++sp) {
+        const int off = kbi * kBlock + sp * 64;
+        if (bvalid) {
+          b[sp][0] = __ldg(reinterpret_cast<const uint4*>(xb + off));
+          b[sp][1] = __ldg(reinterpret_cast<const uint4*>(xb + off + 8));
+        } else {
+          b[sp][0] = make_uint4(0, 0, 0, 0);
+          b[sp][1] = make_uint4(0, 0, 0, 0);
+        }
+      }
+    };
+
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if (present) {
+      for (int j = 0; j < min(kTmaStages, nkb); ++j) issue(j);
+      uint4 bcur[2][2], bnxt[2][2];
+      load_b(bcur, 0);
+      for (int kbi = 0; kbi < nkb; ++kbi) {
+        const uint32_t stage = consumed % kTmaStages;
+        if (!mbar_wait(&bar[stage], (consumed / kTmaStages) & 1u, 16)) return;  // error word set
+        ++consumed;
+        const unsigned char* st_base = ring + stage * kStageBytes;
+        uint4 af[2][2][2];  // [span][stream][row g, row g + 8]
+#pragma unroll
+        for (int sp = 0; sp < 2; ++sp)
+#pragma unroll
+          for (int st = 0; st < 2; ++st)
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr)
+              af[sp][st][rr] = *reinterpret_cast<const uint4*>(st_base + (st * 16 + g + 8 * rr) * kSlotBytes +
+                                                               sp * 64 + 16 * c);
+        if (kbi + 1 < nkb) load_b(bnxt, kbi + 1);
+        // the slices are in registers: hand the stage back to the async proxy
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (kbi + kTmaStages < nkb) issue(kbi + kTmaStages);
+        float t[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int sp = 0; sp < 2; ++sp) {
+          const uint32_t bw[8] = {bcur[sp][0].x, bcur[sp][0].y, bcur[sp][0].z, bcur[sp][0].w,
+                                  bcur[sp][1].x, bcur[sp][1].y, bcur[sp][1].z, bcur[sp][1].w};
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+#pragma unroll
+            for (int st = 0; st < 2; ++st) {
+              uint32_t wg = word_of(af[sp][st][0], s);
+              uint32_t wh = word_of(af[sp][st][1], s);
+              if (a.nanfix) {
+                wg = e4m3x4_nan_to_zero(wg);
+                wh = e4m3x4_nan_to_zero(wh);
+              }
+              mma_16816(t[st], e4m3x2_to_f16x2_bits(wg), e4m3x2_to_f16x2_bits(wh),
+                        e4m3x2_to_f16x2_bits(wg >> 16), e4m3x2_to_f16x2_bits(wh >> 16), bw[2 * s], bw[2 * s + 1]);
+            }
+          }
+        }
+#pragma unroll
+        for (int st = 0; st < 2; ++st) {
+          const float sc = __ldg(srow[st] + kbi);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[st][i] = fmaf(t[st][i], sc, acc[st][i]);
+        }
+        if (kbi + 1 < nkb) {
+#pragma unroll
+          for (int sp = 0; sp < 2; ++sp) {
+            bcur[sp][0] = bnxt[sp][0];
+            bcur[sp][1] = bnxt[sp][1];
+          }
+        }
+      }
+    }
+
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int tok = 2 * c + j;
+      if (tok >= len) continue;
+      const int64_t tr = a.pair_row ? a.pair_row[p0 + tok] : static_cast<int64_t>(p0 + tok);
+      const float xs = a.xscale[tr];
+      const int64_t p = p0 + tok;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int i = rr * 2 + j;
+        if (NS == 2) {
+          const int row = r0 + g + 8 * rr;
+          if (row < N) {
+            const float gv = acc[0][i] * xs, uv = acc[1][i] * xs;
+            const float silu = gv / (1.0f + expf(-gv));
+            a.out0[p * N + row] = EPI == kEpiSwiglu ? silu * uv : gv;
+          }
+        } else {
+#pragma unroll
+          for (int st = 0; st < 2; ++st) {
+            const int row = r0 + 16 * st + g + 8 * rr;
+            if (row < N) a.out0[p * N + row] = acc[st][i] * xs;
+          }
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -266,6 +487,26 @@ cudaError_t launch_rows_to_f16(const void* src, bool src_bf16, int rows, int K, 
                                                          scale);
   return cudaGetLastError();
 }
+
+cudaError_t launch_tma_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream) {
+  const unsigned grid = static_cast<unsigned>(gemv_grid_ctas() * 2);  // 2 CTAs (8 warps) per SM
+  auto k2 = tma_mma_gemv_kernel<2, kEpiSwiglu>;
+  auto k1 = tma_mma_gemv_kernel<1, kEpiStore>;
+  if (ns == 2 && epi == kEpiSwiglu) {
+    cudaError_t err = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTmaSmem));
+    if (err != cudaSuccess) return err;
+    k2<<<grid, kTmaWarps * kWarp, kTmaSmem, stream>>>(a);
+  } else if (ns == 1 && epi == kEpiStore) {
+    cudaError_t err = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTmaSmem));
+    if (err != cudaSuccess) return err;
+    k1<<<grid, kTmaWarps * kWarp, kTmaSmem, stream>>>(a);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+int read_and_clear_mma_device_error(cudaStream_t stream) { return read_and_clear_local_error(stream); }
 
 cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream) {
   const int blocks_per_sm = 4;  // register-limited: about 3 resident CTAs of 4 warps

@@ -303,18 +303,6 @@ cudaError_t launch_stream_gemv(const GemvArgs& a, int x_dtype, int ns, int epi, 
   return cudaErrorInvalidValue;
 }
 
-int read_and_clear_device_error(cudaStream_t stream) {
-  int host = 0;
-  if (cudaMemcpyFromSymbolAsync(&host, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, stream) !=
-      cudaSuccess)
-    return -1;
-  if (cudaStreamSynchronize(stream) != cudaSuccess) return -1;
-  if (host) {
-    const int zero = 0;
-    cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
-    cudaStreamSynchronize(stream);
-  }
-  return host;
-}
+int read_and_clear_device_error(cudaStream_t stream) { return read_and_clear_local_error(stream); }
 
 }  // namespace moe

@@ -13,6 +13,8 @@
 #include "router.cuh"
 #include "router_device.cuh"
 
+#include <algorithm>
+
 namespace moe {
 
 
@@ -122,81 +124,31 @@ __global__ void __launch_bounds__(256) router_logits_gemv_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Logits, decode batches: split-K partial dot products.  CTA (expert octet,
-// 1024-column part): each warp holds its expert's 1024 weights in registers
-// (32 per lane) and walks the tokens; partial[q][t][e] is summed over the
-// parts q in a fixed order by the selection (select_token), so the result is
-// deterministic.  Parallelism = experts/8 x ceil(H/1024) CTAs of 8 warps.
-// ---------------------------------------------------------------------------
-constexpr int kSplitCols = 1024;
-
-template <typename XT, typename WT>
-__global__ void __launch_bounds__(256) router_logits_split_kernel(
-    const XT* __restrict__ x, const WT* __restrict__ w, float* __restrict__ partial, int tokens, int hidden,
-    int experts, int vec_ok) {
-  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-  const int e = blockIdx.x * 8 + warp;
-  const int q = blockIdx.y;
-  if (e >= experts) return;
-  const int lo = q * kSplitCols, hi = min(hidden, lo + kSplitCols);
-  const WT* wrow = w + static_cast<int64_t>(e) * hidden;
-  float wv[4][8];
-  bool on[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int k = lo + j * 256 + lane * 8;
-    on[j] = k < hi;
-    if (vec_ok) {
-      if (on[j]) load8<WT>(wrow + k, wv[j]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) wv[j][i] = (on[j] && k + i < hi) ? to_float_any(wrow[k + i]) : 0.0f;
-    }
-  }
-  for (int t = 0; t < tokens; ++t) {
-    const XT* xr = x + static_cast<int64_t>(t) * hidden;
-    float acc = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (!on[j]) continue;
-      const int k = lo + j * 256 + lane * 8;
-      float xv[8];
-      if (vec_ok) {
-        load8<XT>(xr + k, xv);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) xv[i] = k + i < hi ? to_float_any(xr[k + i]) : 0.0f;
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[j][i], acc);
-    }
-    acc = warp_sum(acc);
-    if (lane == 0) partial[(static_cast<int64_t>(q) * tokens + t) * experts + e] = acc;
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Logits, large token counts: 64x64 output tiles, 4x4 per thread, k-tiles of
 // 32 staged through shared memory (row-major copies of x and w tiles).
 // ---------------------------------------------------------------------------
 constexpr int kTileM = 64, kTileN = 64, kTileK = 32;
 
+// blockIdx.z selects a K part of `kpart` columns; its sums go to
+// logits + z * tokens * experts (partials summed later in part order).
 template <typename XT, typename WT>
 __global__ void __launch_bounds__(256) router_logits_tiled_kernel(
     const XT* __restrict__ x, const WT* __restrict__ w, float* __restrict__ logits,
-    int tokens, int hidden, int experts) {
+    int tokens, int hidden, int experts, int kpart) {
   __shared__ float xs[kTileK][kTileM + 4];
   __shared__ float ws[kTileK][kTileN + 4];
   const int tm = blockIdx.y * kTileM, tn = blockIdx.x * kTileN;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int k_lo = blockIdx.z * kpart, k_hi = min(hidden, k_lo + kpart);
+  logits += static_cast<int64_t>(blockIdx.z) * tokens * experts;
   float acc[4][4] = {};
-  for (int k0 = 0; k0 < hidden; k0 += kTileK) {
+  for (int k0 = k_lo; k0 < k_hi; k0 += kTileK) {
     for (int i = threadIdx.x; i < kTileM * kTileK; i += 256) {
       const int r = i / kTileK, c = i % kTileK;
       const int gr = tm + r, gc = k0 + c;
-      xs[c][r] = (gr < tokens && gc < hidden) ? to_float_any(x[static_cast<int64_t>(gr) * hidden + gc]) : 0.0f;
+      xs[c][r] = (gr < tokens && gc < k_hi) ? to_float_any(x[static_cast<int64_t>(gr) * hidden + gc]) : 0.0f;
       const int er = tn + r;
-      ws[c][r] = (er < experts && gc < hidden) ? to_float_any(w[static_cast<int64_t>(er) * hidden + gc]) : 0.0f;
+      ws[c][r] = (er < experts && gc < k_hi) ? to_float_any(w[static_cast<int64_t>(er) * hidden + gc]) : 0.0f;
     }
     __syncthreads();
 #pragma unroll 8
@@ -259,7 +211,7 @@ static cudaError_t launch_logits_t(const void* x, const void* w, float* logits, 
                                                                   vec_ok ? 1 : 0);
   } else {
     dim3 grid(static_cast<unsigned>(ceil_div(experts, kTileN)), static_cast<unsigned>(ceil_div(tokens, kTileM)));
-    router_logits_tiled_kernel<XT, WT><<<grid, 256, 0, stream>>>(xp, wp, logits, tokens, hidden, experts);
+    router_logits_tiled_kernel<XT, WT><<<grid, 256, 0, stream>>>(xp, wp, logits, tokens, hidden, experts, hidden);
   }
   return cudaGetLastError();
 }
@@ -278,11 +230,12 @@ static cudaError_t launch_logits_w(const void* x, int w_dtype, const void* w, fl
 template <typename XT, typename WT>
 static cudaError_t launch_split_t(const void* x, const void* w, float* partial, int tokens, int hidden, int experts,
                                   cudaStream_t stream) {
-  const bool vec_ok = hidden % 8 == 0 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
-                      (reinterpret_cast<uintptr_t>(w) % 16 == 0);
-  dim3 grid(static_cast<unsigned>(ceil_div(experts, 8)), static_cast<unsigned>(ceil_div(hidden, kSplitCols)));
-  router_logits_split_kernel<XT, WT><<<grid, 256, 0, stream>>>(static_cast<const XT*>(x), static_cast<const WT*>(w),
-                                                                partial, tokens, hidden, experts, vec_ok ? 1 : 0);
+  const int parts = router_split_parts(hidden);
+  const int kpart = static_cast<int>(ceil_div(ceil_div(hidden, parts), kTileK)) * kTileK;
+  dim3 grid(static_cast<unsigned>(ceil_div(experts, kTileN)), static_cast<unsigned>(ceil_div(tokens, kTileM)),
+            static_cast<unsigned>(parts));
+  router_logits_tiled_kernel<XT, WT><<<grid, 256, 0, stream>>>(static_cast<const XT*>(x), static_cast<const WT*>(w),
+                                                                partial, tokens, hidden, experts, kpart);
   return cudaGetLastError();
 }
 
@@ -297,7 +250,9 @@ static cudaError_t launch_split_w(const void* x, int w_dtype, const void* w, flo
   }
 }
 
-int router_split_parts(int hidden) { return static_cast<int>(ceil_div(hidden, kSplitCols)); }
+int router_split_parts(int hidden) {
+  return static_cast<int>(std::min<int64_t>(kMaxRouterParts, ceil_div(hidden, 448)));
+}
 
 cudaError_t launch_router_logits_split(const void* x, int x_dtype, const void* w, int w_dtype, float* partial,
                                        int tokens, int hidden, int experts, cudaStream_t stream) {

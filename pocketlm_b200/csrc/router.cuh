@@ -24,7 +24,9 @@ struct RouterSelectParams {
 cudaError_t launch_router_logits(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
                                  int tokens, int hidden, int experts, cudaStream_t stream);
 
-// Split-K logits for decode batches: partial[q][t][e], q < router_split_parts(hidden).
+// Split-K logits for decode batches: partial[q][t][e], q < router_split_parts(hidden)
+// (at most kMaxRouterParts); the parts are summed in order by the selection.
+constexpr int kMaxRouterParts = 16;
 int router_split_parts(int hidden);
 cudaError_t launch_router_logits_split(const void* x, int x_dtype, const void* w, int w_dtype, float* partial,
                                        int tokens, int hidden, int experts, cudaStream_t stream);

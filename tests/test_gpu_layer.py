@@ -20,15 +20,16 @@ from tests.parity import COS_GATE, REL_L2_GATE, cos_dist, id_mismatches, rel_l2
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["auto", "stream", "direct"])
+@pytest.fixture(autouse=True, params=["auto", "mma_regs", "stream", "direct"])
 def gemv_impl(request):
-    """Run every case on each expert-GEMV kernel: auto (warp-MMA on the layer
-    path, fp8_mma.cu), the bulk-copy streaming one (fp8_stream.cu) and the
-    direct-load one (fp8_gemv.cu)."""
+    """Run every case on each expert-GEMV kernel: auto (TMA-fed warp-MMA on
+    the layer path), the register-fed warp-MMA one (both fp8_mma.cu), the
+    bulk-copy streaming one (fp8_stream.cu) and the direct-load one
+    (fp8_gemv.cu)."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     lib = native.load_library()
-    assert lib.moe_b200_select_gemv({"auto": 0, "stream": 1, "direct": 2}[request.param]) == 0
+    assert lib.moe_b200_select_gemv({"auto": 0, "stream": 1, "direct": 2, "mma_regs": 3}[request.param]) == 0
     yield request.param
     torch.cuda.synchronize()
     assert lib.moe_b200_device_error(None) == 0, "a bounded wait inside a kernel gave up"
