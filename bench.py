@@ -45,7 +45,16 @@ import torch  # noqa: E402
 
 METRIC = "DS-V3 MoE layer tokens/s @1/2/4/8 B200; % of HBM or FP8 TC roofline"
 L2_FLUSH_BYTES = 256 << 20
-KERNELS_PER_LAYER = 9  # router logits, router select, dispatch, chunk list, x->f16, gate/up, act->f16, down, combine
+# kernels per layer forward: router logits, route + dispatch + chunk list, then on the warp-MMA path
+# x -> f16, gate/up, activations -> f16, down (else chunk list, gate/up, down), combine
+KERNELS_PER_LAYER = {"auto": 7, "mma_tma": 7, "stream": 6, "direct": 6}
+GEMV_IMPLS = {"auto": 0, "stream": 1, "direct": 2, "mma_tma": 4}
+ROOFLINE_KERNEL = {
+    "auto": "mma_gemv_kernel<2, swiglu> gate/up+SwiGLU (fp8_mma.cu)",
+    "mma_tma": "tma_mma_gemv_kernel<2, swiglu> gate/up+SwiGLU (fp8_mma.cu)",
+    "stream": "stream_gemv_kernel gate/up+SwiGLU (fp8_stream.cu)",
+    "direct": "grouped_gemv_kernel gate/up+SwiGLU (fp8_gemv.cu)",
+}
 
 
 def measured_peaks() -> dict:
@@ -221,7 +230,8 @@ def run_ours(args, rank: int, world: int) -> dict | None:
     flush = torch.zeros((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
     peaks = measured_peaks()
     results = {}
-    token_list = [args.tokens] + [t for t in (1, 4, 16, 64) if t != args.tokens]
+    sweep = [] if args.sweep == "none" else [int(v) for v in args.sweep.split(",") if v]
+    token_list = [args.tokens] + [t for t in sweep if t != args.tokens]
     with ClockSampler(dev.index) as clocks:
         for T in token_list:
             x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 100 * rank + T, device=dev)
@@ -300,7 +310,7 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                    "top_k": cfg.top_k, "n_group": cfg.n_group, "topk_group": cfg.topk_group,
                    "parallelism": "single GPU" if world == 1 else f"replicas x{world}",
                    "l2": "weights streamed per step exceed L2; 256 MiB L2 flush between timed steps"},
-        "roofline": {"bound": "hbm", "kernel": "mma_gemv_kernel<2, swiglu> gate/up+SwiGLU (fp8_mma.cu)",
+        "roofline": {"bound": "hbm", "kernel": ROOFLINE_KERNEL[args.gemv],
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None,
                      "peak_source": f"{peaks['source']} hbm_gbs",
@@ -309,12 +319,40 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                      "layer_frac": head["layer_hbm_frac"]},
         "e2e": {"value": head["e2e_tokens_per_s"], "unit": "tokens/s",
                 "h2d_bytes_per_step": args.tokens * cfg.hidden * 2, "d2h_bytes_per_step": args.tokens * cfg.hidden * 2},
-        "gpu_launches": KERNELS_PER_LAYER * args.steps,
+        "gpu_launches": KERNELS_PER_LAYER[args.gemv] * args.steps,
         "cpu_baseline": cpu,
         "clocks": clock_info,
         "sweep": {str(T): {k: v for k, v in r.items() if k != "stage_ms"} | {"stage_ms": r["stage_ms"]}
                   for T, r in sorted(results.items())},
     }
+
+
+def run_profile_case(args) -> dict:
+    """A small case for ncu: the config-2 layer with only the experts that
+    `--tokens` tokens select materialised (the others are absent and skipped
+    by the kernels), run eagerly warmup + steps times.  Holds about
+    (experts selected + 1) x 44 MB of weights instead of 11.3 GB."""
+    from pocketlm_b200 import native, synth
+    import oracle
+    from pocketlm_b200.runtime import DsMoELayerGPU
+
+    dev = torch.device("cuda", 0)
+    native.load_library()
+    cfg = synth.C2_DSV3
+    x = synth.make_hidden(args.tokens, cfg.hidden, seed=args.seed)
+    probe = synth.make_fp8_layer(cfg, seed=args.seed, experts=[])
+    route = oracle.route_deepseek(x, probe.router_weight, probe.bias, top_k=cfg.top_k, n_groups=cfg.n_group,
+                                  topk_groups=cfg.topk_group, route_scale=cfg.route_scale)
+    experts = sorted({int(v) for v in route.ids.reshape(-1).tolist()}) + [cfg.n_routed]
+    if args.profile_no_experts:
+        experts = []  # routing kernels only: every expert absent, the GEMVs skip them
+    layer = DsMoELayerGPU(synth.make_fp8_layer(cfg, seed=args.seed, device=dev, experts=experts), allow_partial=True)
+    xd = x.to(dev)
+    for _ in range(args.warmup + args.steps):
+        layer.forward(xd)
+    torch.cuda.synchronize()
+    return {"profile_case": f"c2-dsv3-decode-T{args.tokens}", "experts_materialised": len(experts),
+            "launches": args.warmup + args.steps}
 
 
 def run_reference(args, rank: int, world: int) -> dict | None:
@@ -354,6 +392,14 @@ def main() -> None:
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--cpu-sample-tokens", type=int, default=4)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--sweep", default="1,4,16,64",
+                        help="comma-separated extra batch sizes measured after --tokens, or 'none'")
+    parser.add_argument("--gemv", choices=list(GEMV_IMPLS), default="auto",
+                        help="expert GEMV kernel (moe_b200_select_gemv); auto is the product default")
+    parser.add_argument("--profile", action="store_true",
+                        help="run the small ncu case (selected experts only) instead of the benchmark")
+    parser.add_argument("--profile-no-experts", action="store_true",
+                        help="with --profile: materialise no expert (for captures of the routing kernels)")
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -364,8 +410,15 @@ def main() -> None:
 
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    if args.impl == "ours":
+        from pocketlm_b200 import native
+
+        native.load_library().moe_b200_select_gemv(GEMV_IMPLS[args.gemv])
     try:
-        result = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world)
+        if args.profile:
+            result = run_profile_case(args)
+        else:
+            result = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world)
         if result is not None:
             print(json.dumps(result), flush=True)
     finally:

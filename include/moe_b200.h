@@ -243,12 +243,12 @@ int moe_b200_stage_timing(int enable);
 int moe_b200_stage_times(float* ms, int max_n);
 
 /* Expert-GEMV implementation (no reference counterpart): 0 = auto (default:
- * the warp-MMA kernel on the whole-layer path when hidden and intermediate
- * sizes are multiples of 128, the direct-load kernel elsewhere), 1 = the
- * warp-specialised bulk-copy streaming kernel wherever the shape allows,
- * 2 = the direct-load kernel everywhere, 3 = like 0 but the warp-MMA kernel
- * loads its weights into registers instead of through its TMA bulk-copy
- * ring.  For A/B parity tests and measurements. */
+ * the register-fed warp-MMA kernel on the whole-layer path when hidden and
+ * intermediate sizes are multiples of 128, the direct-load kernel
+ * elsewhere), 1 = the warp-specialised bulk-copy streaming kernel wherever
+ * the shape allows, 2 = the direct-load kernel everywhere, 3 = same as 0,
+ * 4 = like 0 but the warp-MMA kernel is fed through per-warp TMA bulk-copy
+ * rings.  For A/B parity tests and measurements. */
 int moe_b200_select_gemv(int impl);
 
 /* Device error word (no reference counterpart): nonzero when a bounded wait

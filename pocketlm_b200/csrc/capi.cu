@@ -75,8 +75,8 @@ int g_marks = 0;
 // shapes allow, direct-load elsewhere), 1 = bulk-copy streaming kernel where
 // supported, 2 = direct-load kernel everywhere.
 int g_gemv_impl = 0;
-// Operand feed of the warp-MMA kernel: 1 = TMA bulk-copy ring per warp (default), 0 = register loads.
-int g_mma_feed = 1;
+// Operand feed of the warp-MMA kernel: 0 = register loads (default), 1 = TMA bulk-copy ring per warp.
+int g_mma_feed = 0;
 
 cudaError_t gemv(const GemvArgs& a, int x_dtype, int ns, int epi, int nt, bool vec, cudaStream_t stream) {
   if (g_gemv_impl == 1 && vec && stream_gemv_supported(a.K, x_dtype, nt))
@@ -601,6 +601,12 @@ struct LayerPlan {
   float* xscale;
   __half* act16;
   float* ascale;
+  // register-fed MMA kernel k-split: partial fragments + per-task counters
+  int ksplit1, ksplit2;    // gate/up, down
+  int64_t tasks1, tasks2;  // upper bounds on tasks (chunks x row tiles)
+  float* partial;
+  int32_t* counters;       // [tasks1] gate/up then [tasks2] down (only the split stages)
+  int64_t n_counters;
 };
 
 static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, int shared, int nt) {
@@ -614,6 +620,16 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
   l.xscale = p.take<float>(T);
   l.act16 = p.take<__half>(pairs * I);
   l.ascale = p.take<float>(pairs);
+  const int64_t chunks = std::min(pairs, chunk_capacity(pairs, E + (shared ? 1 : 0), 8));
+  l.tasks1 = chunks * ceil_div(I, mma_task_rows(2));
+  l.tasks2 = chunks * ceil_div(H, mma_task_rows(1));
+  l.ksplit1 = mma_gemv_ksplit(l.tasks1, static_cast<int>(H));
+  l.ksplit2 = mma_gemv_ksplit(l.tasks2, static_cast<int>(I));
+  const int64_t frag = 32 * 8;
+  const int64_t part = std::max(l.ksplit1 > 1 ? l.tasks1 * l.ksplit1 : 0, l.ksplit2 > 1 ? l.tasks2 * l.ksplit2 : 0);
+  l.partial = part > 0 ? p.take<float>(part * frag) : nullptr;
+  l.n_counters = (l.ksplit1 > 1 ? l.tasks1 : 0) + (l.ksplit2 > 1 ? l.tasks2 : 0);
+  l.counters = l.n_counters > 0 ? p.take<int32_t>(l.n_counters) : nullptr;
   return l;
 }
 
@@ -627,7 +643,8 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
     ChunkArgs ca{m.seg_offset, static_cast<int>(n_segments), 8, m.chunk_seg, m.chunk_start, m.chunk_len, m.n_chunks};
     MOE_CUDA(launch_chunks(ca, s), "chunk list");
   }
-  MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.x16, l.xscale, s),
+  MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.x16, l.xscale,
+                              l.counters, l.n_counters, s),
            "stage x");
   stage_mark(s);
   MmaArgs g1{};
@@ -636,11 +653,13 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
   g1.chunk_seg = m.chunk_seg; g1.chunk_start = m.chunk_start; g1.chunk_len = m.chunk_len; g1.n_chunks = m.n_chunks;
   g1.out0 = m.act; g1.N = static_cast<int>(I); g1.K = static_cast<int>(H);
   g1.scale_cols = static_cast<int>(ceil_div(H, kBlock)); g1.nanfix = 1;
-  MOE_CUDA(g_mma_feed == 1 ? launch_tma_mma_gemv(g1, 2, kEpiSwiglu, s) : launch_mma_gemv(g1, 2, kEpiSwiglu, s),
+  g1.ksplit = l.ksplit1; g1.partial = l.partial; g1.counters = l.counters;
+  MOE_CUDA(g_mma_feed == 1 ? launch_tma_mma_gemv(g1, 2, kEpiSwiglu, s)
+                           : launch_mma_gemv(g1, 2, kEpiSwiglu, l.tasks1, s),
            "gate/up stage");
   stage_mark(s);
   MOE_CUDA(launch_rows_to_f16(m.act, false, static_cast<int>(pairs), static_cast<int>(I), nullptr, l.act16,
-                              l.ascale, s),
+                              l.ascale, nullptr, 0, s),
            "stage activations");
   stage_mark(s);
   MmaArgs g2 = g1;
@@ -648,7 +667,10 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
   g2.x16 = l.act16; g2.xscale = l.ascale; g2.pair_row = nullptr;
   g2.out0 = m.y; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
   g2.scale_cols = static_cast<int>(ceil_div(I, kBlock));
-  MOE_CUDA(g_mma_feed == 1 ? launch_tma_mma_gemv(g2, 1, kEpiStore, s) : launch_mma_gemv(g2, 1, kEpiStore, s),
+  g2.ksplit = l.ksplit2;
+  g2.counters = l.counters ? l.counters + (l.ksplit1 > 1 ? l.tasks1 : 0) : nullptr;
+  MOE_CUDA(g_mma_feed == 1 ? launch_tma_mma_gemv(g2, 1, kEpiStore, s)
+                           : launch_mma_gemv(g2, 1, kEpiStore, l.tasks2, s),
            "down stage");
   stage_mark(s);
   return kOk;
@@ -767,9 +789,9 @@ int moe_b200_stage_timing(int enable) {
 }
 
 int moe_b200_select_gemv(int impl) {
-  if (impl < 0 || impl > 3) return fail(kBadDims, "impl must be 0, 1, 2 or 3");
-  g_gemv_impl = impl == 3 ? 0 : impl;
-  g_mma_feed = impl == 3 ? 0 : 1;
+  if (impl < 0 || impl > 4) return fail(kBadDims, "impl must be 0, 1, 2, 3 or 4");
+  g_gemv_impl = impl >= 3 ? 0 : impl;
+  g_mma_feed = impl == 4 ? 1 : 0;
   return kOk;
 }
 

@@ -27,8 +27,7 @@ __global__ void __launch_bounds__(kBucketThreads) bucket_kernel(BucketArgs a) {
 }
 
 __global__ void __launch_bounds__(kBucketThreads) chunk_kernel(ChunkArgs a) {
-  __shared__ int32_t scan[kBucketThreads];
-  chunk_body(a, scan);
+  chunk_body(a);
 }
 
 // Decode batches in one launch: select every token's experts (one warp per
@@ -37,7 +36,6 @@ __global__ void __launch_bounds__(kBucketThreads) chunk_kernel(ChunkArgs a) {
 // router_select_kernel + bucket_kernel + chunk_kernel without two launch gaps.
 __global__ void __launch_bounds__(kBucketThreads) route_dispatch_kernel(RouteDispatchArgs a) {
   extern __shared__ uint32_t sm[];
-  __shared__ int32_t scan[kBucketThreads];
   const int warp = threadIdx.x / kWarp;
   const int E = a.select.experts, T = a.select.tokens;
   // logits = sum of the split-K partials, in part order, summed by the whole CTA
@@ -59,7 +57,7 @@ __global__ void __launch_bounds__(kBucketThreads) route_dispatch_kernel(RouteDis
   __syncthreads();
   bucket_body(a.bucket.args, sm);
   __syncthreads();
-  chunk_body(a.chunks, scan);
+  chunk_body(a.chunks);
 }
 
 size_t route_dispatch_smem_bytes(int tokens, int experts) {

@@ -10,6 +10,38 @@ namespace moe {
 constexpr int kBucketThreads = 1024;
 constexpr int kWindowWords = kBucketThreads / 32;
 
+// Exclusive prefix sum of one value per thread over the CTA (blockDim.x ==
+// kBucketThreads, called by every thread); *total gets the CTA sum.  Ends
+// with the CTA synchronised.
+static __device__ int block_exclusive_scan(int v, int* total) {
+  __shared__ int warp_part[kBucketThreads / 32];
+  __shared__ int sum_all;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  __syncthreads();  // warp_part may still be read by a previous call
+  if (lane == 31) warp_part[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int mine = warp_part[lane];
+    int wi = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    warp_part[lane] = wi - mine;
+    if (lane == 31) sum_all = wi;
+  }
+  __syncthreads();
+  if (total) *total = sum_all;
+  return warp_part[warp] + incl - v;
+}
+
 // One CTA.  Entry i has key keys[i] (entries whose key falls outside
 // [key_lo, key_lo + n_buckets) are dropped), row rows ? rows[i] : i / k and
 // weight weights ? weights[i] : 1.
@@ -26,17 +58,25 @@ static __device__ void bucket_body(const BucketArgs& a, uint32_t* sm) {
     if (key >= 0 && key < a.n_buckets) atomicAdd(&count[key], 1);
   }
   __syncthreads();
-  if (tid == 0) {
+  {
+    // bucket offsets: thread tid owns buckets [tid * per, tid * per + per)
+    const int per = static_cast<int>(ceil_div(a.n_buckets, kBucketThreads));
+    const int b_lo = min(a.n_buckets, tid * per), b_hi = min(a.n_buckets, b_lo + per);
+    int mine = 0;
+    for (int b = b_lo; b < b_hi; ++b) mine += count[b];
     int running = 0;
-    for (int b = 0; b < a.n_buckets; ++b) {
-      base[b] = running;
-      a.bucket_offset[b] = running;
-      running += count[b];
+    int off = block_exclusive_scan(mine, &running);
+    for (int b = b_lo; b < b_hi; ++b) {
+      base[b] = off;
+      a.bucket_offset[b] = off;
+      off += count[b];
     }
-    base[a.n_buckets] = running;
-    a.bucket_offset[a.n_buckets] = running;
-    if (a.tail > 0) a.bucket_offset[a.n_buckets + 1] = running + a.tail;
-    if (a.total) *a.total = running + (a.tail > 0 ? a.tail : 0);
+    if (tid == 0) {
+      base[a.n_buckets] = running;
+      a.bucket_offset[a.n_buckets] = running;
+      if (a.tail > 0) a.bucket_offset[a.n_buckets + 1] = running + a.tail;
+      if (a.total) *a.total = running + (a.tail > 0 ? a.tail : 0);
+    }
   }
   if (a.counts)
     for (int b = tid; b < a.n_buckets; b += kBucketThreads) a.counts[b] = count[b];
@@ -87,7 +127,7 @@ static __device__ void bucket_body(const BucketArgs& a, uint32_t* sm) {
 }
 
 // One CTA: segments -> chunks of at most `chunk` consecutive pairs.
-static __device__ void chunk_body(const ChunkArgs& a, int32_t* scan) {
+static __device__ void chunk_body(const ChunkArgs& a) {
   const int tid = threadIdx.x;
   const int per = static_cast<int>(ceil_div(a.n_segments, kBucketThreads));
   const int s_lo = tid * per, s_hi = min(a.n_segments, s_lo + per);
@@ -96,16 +136,9 @@ static __device__ void chunk_body(const ChunkArgs& a, int32_t* scan) {
     const int n = a.seg_offset[s + 1] - a.seg_offset[s];
     mine += (n + a.chunk - 1) / a.chunk;
   }
-  scan[tid] = mine;
-  __syncthreads();
-  for (int o = 1; o < kBucketThreads; o <<= 1) {
-    const int v = tid >= o ? scan[tid - o] : 0;
-    __syncthreads();
-    scan[tid] += v;
-    __syncthreads();
-  }
-  int c = scan[tid] - mine;
-  if (tid == kBucketThreads - 1) *a.n_chunks = scan[tid];
+  int total = 0;
+  int c = block_exclusive_scan(mine, &total);
+  if (tid == 0) *a.n_chunks = total;
   for (int s = s_lo; s < s_hi; ++s) {
     const int lo = a.seg_offset[s], hi = a.seg_offset[s + 1];
     for (int p = lo; p < hi; p += a.chunk, ++c) {

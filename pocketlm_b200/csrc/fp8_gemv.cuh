@@ -74,14 +74,24 @@ struct MmaArgs {
   int K;
   int scale_cols;
   int nanfix;                // decode e4m3 0x7F/0xFF as +0 (the reference's linear semantics)
+  int ksplit;                // register-fed kernel: k-block ranges per task (1: none)
+  float* partial;            // [tasks * ksplit, 32, 8] fp32 fragments when ksplit > 1
+  int32_t* counters;         // [tasks] arrival counters: zero on entry, left zero on exit
 };
+constexpr int kMaxMmaKSplit = 8;
+// Rows of one warp task of the MMA kernels: 16 (gate + up) or 32 (one matrix).
+constexpr int mma_task_rows(int ns) { return ns == 2 ? 16 : 32; }
 bool mma_gemv_supported(int K, int N);
-cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream);
+// k-split for an upper bound on the launch's tasks (chunks x row tiles): 1
+// when the tasks already occupy every resident warp.
+int mma_gemv_ksplit(int64_t tasks_bound, int K);
+cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream);
 // Same computation, weights fed to each warp by TMA bulk copies (fp8_mma.cu).
 cudaError_t launch_tma_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream);
 int read_and_clear_mma_device_error(cudaStream_t stream);
+// Also zeroes zero[0, zero_n) (the k-split counters of the stages that follow).
 cudaError_t launch_rows_to_f16(const void* src, bool src_bf16, int rows, int K, const int32_t* n_rows_dev,
-                               __half* dst, float* scale, cudaStream_t stream);
+                               __half* dst, float* scale, int32_t* zero, int64_t zero_n, cudaStream_t stream);
 
 // Device error word of the bounded waits; returns it (or -1) and clears it.
 int read_and_clear_device_error(cudaStream_t stream);

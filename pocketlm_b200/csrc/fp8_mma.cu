@@ -89,9 +89,13 @@ MOE_D void unpack16<__nv_bfloat16>(const uint4& v, float* out) {
 template <typename T>
 __global__ void __launch_bounds__(256) rows_to_f16_kernel(const T* __restrict__ src, int rows, int K,
                                                           const int32_t* __restrict__ n_rows_dev,
-                                                          __half* __restrict__ dst, float* __restrict__ scale) {
+                                                          __half* __restrict__ dst, float* __restrict__ scale,
+                                                          int32_t* __restrict__ zero, int64_t zero_n) {
   constexpr int V = 16 / sizeof(T);
   __shared__ float red[8];
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < zero_n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    zero[i] = 0;
   const int n_rows = n_rows_dev ? min(rows, *n_rows_dev) : rows;
   const int n16 = K / V;
   for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
@@ -139,22 +143,33 @@ __global__ void __launch_bounds__(256) rows_to_f16_kernel(const T* __restrict__ 
 
 // A task is (chunk of <= 8 pairs, row tile): 16 rows of two matrices (gate +
 // up, SwiGLU epilogue) when NS == 2, 32 rows of one matrix as two 16-row tiles
-// when NS == 1.  The 4 warps of a CTA split the task's k-blocks round-robin
-// (warp w takes blocks w, w+4, ...), so even a one-token batch keeps four
-// warps per row tile streaming; their fp32 partial fragments meet in shared
-// memory, warp 0 adds them in a fixed order and writes the outputs.
+// when NS == 1.  Each warp streams the k-blocks [kb0, kb1) of one task with
+// ping-pong register buffers.  With a.ksplit == 1 that range is all of K and
+// the warp writes the outputs itself.  With a.ksplit > 1 (too few tasks to
+// occupy every warp, e.g. one-token batches) a task's k-blocks are cut into
+// ksplit ranges taken by different warps: each writes its fp32 fragment to
+// a.partial, and the warp arriving last at the task's counter adds the
+// partials in range order -- the same order whoever arrives last -- runs the
+// epilogue and resets the counter to zero for the next launch.
 template <int NS, int EPI>
 __global__ void __launch_bounds__(kMmaCtaWarps * kWarp) mma_gemv_kernel(MmaArgs a) {
-  __shared__ float red[kMmaCtaWarps - 1][kWarp][8];
-  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int lane = threadIdx.x % kWarp;
   const int g = lane / 4, c = lane % 4;
   const int K = a.K, N = a.N;
   constexpr int kTaskRows = NS == 2 ? 16 : 32;
   const int row_tiles = static_cast<int>(ceil_div(N, kTaskRows));
+  const int ksplit = a.ksplit;
   const int64_t tasks = static_cast<int64_t>(*a.n_chunks) * row_tiles;
+  const int64_t units = tasks * ksplit;
+  const int64_t warp_global = static_cast<int64_t>(blockIdx.x) * kMmaCtaWarps + threadIdx.x / kWarp;
+  const int64_t warp_count = static_cast<int64_t>(gridDim.x) * kMmaCtaWarps;
   const int nkb = K / kBlock;
 
-  for (int64_t task = blockIdx.x; task < tasks; task += gridDim.x) {
+  for (int64_t unit = warp_global; unit < units; unit += warp_count) {
+    const int64_t task = unit / ksplit;
+    const int ks = static_cast<int>(unit % ksplit);
+    const int kb0 = static_cast<int>(static_cast<int64_t>(ks) * nkb / ksplit);
+    const int kb1 = static_cast<int>(static_cast<int64_t>(ks + 1) * nkb / ksplit);
     const int ch = static_cast<int>(task / row_tiles);
     const int r0 = static_cast<int>(task % row_tiles) * kTaskRows;
     const int seg = a.chunk_seg[ch], p0 = a.chunk_start[ch], len = a.chunk_len[ch];
@@ -186,7 +201,7 @@ __global__ void __launch_bounds__(kMmaCtaWarps * kWarp) mma_gemv_kernel(MmaArgs 
     const __half* xb = a.x16 + brow * K + 16 * c;
 
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    if (present) {
+    if (present && kb0 < kb1) {
       auto load = [&](KBlock& kb, int kbi) {
 #pragma unroll
         for (int sp = 0; sp < 2; ++sp) {
@@ -232,80 +247,89 @@ __global__ void __launch_bounds__(kMmaCtaWarps * kWarp) mma_gemv_kernel(MmaArgs 
           for (int i = 0; i < 4; ++i) acc[st][i] = fmaf(t[st][i], sc, acc[st][i]);
         }
       };
-      // this warp's k-blocks: warp, warp + 4, ...; ping-pong register buffers
-      // keep one k-block of loads in flight ahead of the math
+      // ping-pong register buffers, one k-block of loads in flight ahead of the math
       KBlock buf0, buf1;
-      constexpr int kStep = kMmaCtaWarps;
-      if (warp < nkb) load(buf0, warp);
-      for (int kbi = warp; kbi < nkb; kbi += 2 * kStep) {
-        if (kbi + kStep < nkb) load(buf1, kbi + kStep);
+      load(buf0, kb0);
+      for (int kbi = kb0; kbi < kb1; kbi += 2) {
+        if (kbi + 1 < kb1) load(buf1, kbi + 1);
         compute(buf0, kbi);
-        if (kbi + kStep < nkb) {
-          if (kbi + 2 * kStep < nkb) load(buf0, kbi + 2 * kStep);
-          compute(buf1, kbi + kStep);
+        if (kbi + 1 < kb1) {
+          if (kbi + 2 < kb1) load(buf0, kbi + 2);
+          compute(buf1, kbi + 1);
         }
       }
     }
 
-    // combine the 4 warps' partial fragments (fixed order), warp 0 finishes
-    if (warp > 0) {
+    if (ksplit > 1) {
+      float4* part = reinterpret_cast<float4*>(a.partial + (task * ksplit + ks) * (kWarp * 8) + lane * 8);
+      __stcg(part, make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]));
+      __stcg(part + 1, make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]));
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(a.counters + task, 1) == ksplit - 1;
+      last = __shfl_sync(0xFFFFFFFFu, last, 0);
+      if (!last) continue;
+      __threadfence();
 #pragma unroll
       for (int st = 0; st < 2; ++st)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) red[warp - 1][lane][st * 4 + i] = acc[st][i];
+        for (int i = 0; i < 4; ++i) acc[st][i] = 0.0f;
+      const float4* parts = reinterpret_cast<const float4*>(a.partial + task * ksplit * (kWarp * 8) + lane * 8);
+      for (int r = 0; r < ksplit; ++r) {
+        const float4 v0 = __ldcg(parts + r * (kWarp * 2));
+        const float4 v1 = __ldcg(parts + r * (kWarp * 2) + 1);
+        acc[0][0] += v0.x; acc[0][1] += v0.y; acc[0][2] += v0.z; acc[0][3] += v0.w;
+        acc[1][0] += v1.x; acc[1][1] += v1.y; acc[1][2] += v1.z; acc[1][3] += v1.w;
+      }
+      if (lane == 0) a.counters[task] = 0;
     }
-    __syncthreads();
-    if (warp == 0) {
+
+    // epilogue: lane holds rows (g, g+8) x tokens (2c, 2c+1) per stream
 #pragma unroll
-      for (int w = 0; w < kMmaCtaWarps - 1; ++w)
+    for (int j = 0; j < 2; ++j) {
+      const int tok = 2 * c + j;
+      if (tok >= len) continue;
+      const int64_t tr = a.pair_row ? a.pair_row[p0 + tok] : static_cast<int64_t>(p0 + tok);
+      const float xs = a.xscale[tr];
+      const int64_t p = p0 + tok;
 #pragma unroll
-        for (int st = 0; st < 2; ++st)
+      for (int rr = 0; rr < 2; ++rr) {
+        const int i = rr * 2 + j;
+        if (NS == 2) {
+          const int row = r0 + g + 8 * rr;
+          if (row < N) {
+            const float gv = acc[0][i] * xs, uv = acc[1][i] * xs;
+            const float silu = gv / (1.0f + expf(-gv));
+            a.out0[p * N + row] = EPI == kEpiSwiglu ? silu * uv : gv;
+          }
+        } else {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) acc[st][i] += red[w][lane][st * 4 + i];
-      // epilogue: lane holds rows (g, g+8) x tokens (2c, 2c+1) per stream
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int tok = 2 * c + j;
-        if (tok >= len) continue;
-        const int64_t tr = a.pair_row ? a.pair_row[p0 + tok] : static_cast<int64_t>(p0 + tok);
-        const float xs = a.xscale[tr];
-        const int64_t p = p0 + tok;
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const int i = rr * 2 + j;
-          if (NS == 2) {
-            const int row = r0 + g + 8 * rr;
-            if (row < N) {
-              const float gv = acc[0][i] * xs, uv = acc[1][i] * xs;
-              const float silu = gv / (1.0f + expf(-gv));
-              a.out0[p * N + row] = EPI == kEpiSwiglu ? silu * uv : gv;
-            }
-          } else {
-#pragma unroll
-            for (int st = 0; st < 2; ++st) {
-              const int row = r0 + 16 * st + g + 8 * rr;
-              if (row < N) a.out0[p * N + row] = acc[st][i] * xs;
-            }
+          for (int st = 0; st < 2; ++st) {
+            const int row = r0 + 16 * st + g + 8 * rr;
+            if (row < N) a.out0[p * N + row] = acc[st][i] * xs;
           }
         }
       }
     }
-    __syncthreads();  // red[] is reused by the next task
   }
 }
 
 // ---------------------------------------------------------------------------
 // The same tasks fed by TMA: every warp owns a ring of kTmaStages shared-memory
-// stages; lane l bulk-copies (cp.async.bulk) the 128-byte k-block slice of its
-// row-stream l (stream l / 16, row l % 16 of the task) into slot l of a stage,
-// completing on the stage's mbarrier.  Slots are 192 bytes apart so that the
-// eight lanes of each shared-memory phase (rows g, g+1, all four c) hit 32
-// distinct banks.  With four stages a warp keeps 16 KiB of weight reads in
-// flight without holding them in registers.
+// stages; lane l bulk-copies (cp.async.bulk) a 512-byte slice (4 k-blocks) of
+// its row-stream l (stream l / 16, row l % 16 of the task) into slot l of a
+// stage, completing on the stage's mbarrier.  Slots are 576 bytes apart (an
+// odd multiple of 64) so that the eight lanes of each shared-memory phase
+// (rows g, g+1, all four c) hit 32 distinct banks.  With three stages a warp
+// keeps up to 32 KiB of weight reads in flight without holding them in
+// registers, and each row is read in 512-byte runs.
 // ---------------------------------------------------------------------------
 constexpr int kTmaWarps = 4;
-constexpr int kTmaStages = 4;
-constexpr int kSlotBytes = 192;
+constexpr int kTmaStages = 3;
+constexpr int kSliceBlocks = 4;                    // k-blocks per stage: 512 contiguous bytes per row
+constexpr int kSliceBytes = kSliceBlocks * kBlock;
+constexpr int kSlotBytes = kSliceBytes + 64;       // odd 64-byte offset keeps the fragment reads conflict-free
 constexpr int kStageBytes = 32 * kSlotBytes;
 constexpr size_t kTmaSmem = static_cast<size_t>(kTmaWarps) * kTmaStages * kStageBytes +
                             static_cast<size_t>(kTmaWarps) * kTmaStages * sizeof(uint64_t);
@@ -358,12 +382,14 @@ __global__ void __launch_bounds__(kTmaWarps * kWarp) tma_mma_gemv_kernel(MmaArgs
     const int64_t brow = bvalid ? (a.pair_row ? a.pair_row[p0 + g] : static_cast<int64_t>(p0 + g)) : 0;
     const __half* xb = a.x16 + brow * K + 16 * c;
 
-    auto issue = [&](int kbi) {
+    const int nslices = static_cast<int>(ceil_div(nkb, kSliceBlocks));
+    auto issue = [&](int sl) {
       const uint32_t stage = issued % kTmaStages;
-      if (lane == 0) mbar_arrive_expect_tx(&bar[stage], 32u * kBlock);
+      const int blocks = min(kSliceBlocks, nkb - sl * kSliceBlocks);
+      if (lane == 0) mbar_arrive_expect_tx(&bar[stage], 32u * blocks * kBlock);
       __syncwarp();
-      bulk_copy_g2s(ring + stage * kStageBytes + lane * kSlotBytes, my_src + static_cast<int64_t>(kbi) * kBlock,
-                    kBlock, &bar[stage]);
+      bulk_copy_g2s(ring + stage * kStageBytes + lane * kSlotBytes,
+                    my_src + static_cast<int64_t>(sl) * kSliceBytes, blocks * kBlock, &bar[stage]);
       ++issued;
     };
     auto load_b = [&](uint4 (&b)[2][2], int kbi) {
@@ -382,59 +408,69 @@ __global__ void __launch_bounds__(kTmaWarps * kWarp) tma_mma_gemv_kernel(MmaArgs
 
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     if (present) {
-      for (int j = 0; j < min(kTmaStages, nkb); ++j) issue(j);
+      for (int j = 0; j < min(kTmaStages, nslices); ++j) issue(j);
       uint4 bcur[2][2], bnxt[2][2];
       load_b(bcur, 0);
-      for (int kbi = 0; kbi < nkb; ++kbi) {
+      for (int sl = 0; sl < nslices; ++sl) {
         const uint32_t stage = consumed % kTmaStages;
-        if (!mbar_wait(&bar[stage], (consumed / kTmaStages) & 1u, 16)) return;  // error word set
+        if (!mbar_wait(&bar[stage], (consumed / kTmaStages) & 1u, 16)) {
+          // error word set; let the copies still in flight land (bounded) before the CTA exits
+          for (uint32_t q = consumed + 1; q < issued; ++q) mbar_wait(&bar[q % kTmaStages], (q / kTmaStages) & 1u, 16);
+          return;
+        }
         ++consumed;
         const unsigned char* st_base = ring + stage * kStageBytes;
-        uint4 af[2][2][2];  // [span][stream][row g, row g + 8]
+        const int blocks = min(kSliceBlocks, nkb - sl * kSliceBlocks);
+        for (int bi = 0; bi < blocks; ++bi) {
+          const int kbi = sl * kSliceBlocks + bi;
+          uint4 af[2][2][2];  // [span][stream][row g, row g + 8]
 #pragma unroll
-        for (int sp = 0; sp < 2; ++sp)
+          for (int sp = 0; sp < 2; ++sp)
 #pragma unroll
-          for (int st = 0; st < 2; ++st)
+            for (int st = 0; st < 2; ++st)
 #pragma unroll
-            for (int rr = 0; rr < 2; ++rr)
-              af[sp][st][rr] = *reinterpret_cast<const uint4*>(st_base + (st * 16 + g + 8 * rr) * kSlotBytes +
-                                                               sp * 64 + 16 * c);
-        if (kbi + 1 < nkb) load_b(bnxt, kbi + 1);
-        // the slices are in registers: hand the stage back to the async proxy
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (kbi + kTmaStages < nkb) issue(kbi + kTmaStages);
-        float t[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-        for (int sp = 0; sp < 2; ++sp) {
-          const uint32_t bw[8] = {bcur[sp][0].x, bcur[sp][0].y, bcur[sp][0].z, bcur[sp][0].w,
-                                  bcur[sp][1].x, bcur[sp][1].y, bcur[sp][1].z, bcur[sp][1].w};
-#pragma unroll
-          for (int s = 0; s < 4; ++s) {
-#pragma unroll
-            for (int st = 0; st < 2; ++st) {
-              uint32_t wg = word_of(af[sp][st][0], s);
-              uint32_t wh = word_of(af[sp][st][1], s);
-              if (a.nanfix) {
-                wg = e4m3x4_nan_to_zero(wg);
-                wh = e4m3x4_nan_to_zero(wh);
-              }
-              mma_16816(t[st], e4m3x2_to_f16x2_bits(wg), e4m3x2_to_f16x2_bits(wh),
-                        e4m3x2_to_f16x2_bits(wg >> 16), e4m3x2_to_f16x2_bits(wh >> 16), bw[2 * s], bw[2 * s + 1]);
-            }
+              for (int rr = 0; rr < 2; ++rr)
+                af[sp][st][rr] = *reinterpret_cast<const uint4*>(st_base + (st * 16 + g + 8 * rr) * kSlotBytes +
+                                                                 bi * kBlock + sp * 64 + 16 * c);
+          if (kbi + 1 < nkb) load_b(bnxt, kbi + 1);
+          if (bi == blocks - 1) {
+            // the whole slice is in registers now: hand the stage back to the async proxy
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (sl + kTmaStages < nslices) issue(sl + kTmaStages);
           }
-        }
-#pragma unroll
-        for (int st = 0; st < 2; ++st) {
-          const float sc = __ldg(srow[st] + kbi);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) acc[st][i] = fmaf(t[st][i], sc, acc[st][i]);
-        }
-        if (kbi + 1 < nkb) {
+          float t[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
           for (int sp = 0; sp < 2; ++sp) {
-            bcur[sp][0] = bnxt[sp][0];
-            bcur[sp][1] = bnxt[sp][1];
+            const uint32_t bw[8] = {bcur[sp][0].x, bcur[sp][0].y, bcur[sp][0].z, bcur[sp][0].w,
+                                    bcur[sp][1].x, bcur[sp][1].y, bcur[sp][1].z, bcur[sp][1].w};
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+#pragma unroll
+              for (int st = 0; st < 2; ++st) {
+                uint32_t wg = word_of(af[sp][st][0], s);
+                uint32_t wh = word_of(af[sp][st][1], s);
+                if (a.nanfix) {
+                  wg = e4m3x4_nan_to_zero(wg);
+                  wh = e4m3x4_nan_to_zero(wh);
+                }
+                mma_16816(t[st], e4m3x2_to_f16x2_bits(wg), e4m3x2_to_f16x2_bits(wh),
+                          e4m3x2_to_f16x2_bits(wg >> 16), e4m3x2_to_f16x2_bits(wh >> 16), bw[2 * s], bw[2 * s + 1]);
+              }
+            }
+          }
+#pragma unroll
+          for (int st = 0; st < 2; ++st) {
+            const float sc = __ldg(srow[st] + kbi);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[st][i] = fmaf(t[st][i], sc, acc[st][i]);
+          }
+          if (kbi + 1 < nkb) {
+#pragma unroll
+            for (int sp = 0; sp < 2; ++sp) {
+              bcur[sp][0] = bnxt[sp][0];
+              bcur[sp][1] = bnxt[sp][1];
+            }
           }
         }
       }
@@ -476,20 +512,21 @@ __global__ void __launch_bounds__(kTmaWarps * kWarp) tma_mma_gemv_kernel(MmaArgs
 bool mma_gemv_supported(int K, int N) { return K % kBlock == 0 && K > 0 && N > 0; }
 
 cudaError_t launch_rows_to_f16(const void* src, bool src_bf16, int rows, int K, const int32_t* n_rows_dev,
-                               __half* dst, float* scale, cudaStream_t stream) {
+                               __half* dst, float* scale, int32_t* zero, int64_t zero_n, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
+  if (zero_n > 0 && !zero) return cudaErrorInvalidValue;
   const unsigned grid = static_cast<unsigned>(std::min(rows, gemv_grid_ctas() * 8));
   if (src_bf16)
     rows_to_f16_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(src), rows, K,
-                                                                 n_rows_dev, dst, scale);
+                                                                 n_rows_dev, dst, scale, zero, zero_n);
   else
     rows_to_f16_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(src), rows, K, n_rows_dev, dst,
-                                                         scale);
+                                                         scale, zero, zero_n);
   return cudaGetLastError();
 }
 
 cudaError_t launch_tma_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream) {
-  const unsigned grid = static_cast<unsigned>(gemv_grid_ctas() * 2);  // 2 CTAs (8 warps) per SM
+  const unsigned grid = static_cast<unsigned>(gemv_grid_ctas());  // one 4-warp CTA per SM (216 KiB of rings)
   auto k2 = tma_mma_gemv_kernel<2, kEpiSwiglu>;
   auto k1 = tma_mma_gemv_kernel<1, kEpiStore>;
   if (ns == 2 && epi == kEpiSwiglu) {
@@ -508,9 +545,32 @@ cudaError_t launch_tma_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t 
 
 int read_and_clear_mma_device_error(cudaStream_t stream) { return read_and_clear_local_error(stream); }
 
-cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream) {
-  const int blocks_per_sm = 4;  // register-limited: about 3 resident CTAs of 4 warps
-  const unsigned grid = static_cast<unsigned>(gemv_grid_ctas() * blocks_per_sm);
+// Resident 4-warp CTAs per SM of the register-fed kernel (register-limited).
+static int mma_ctas_per_sm() {
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int a = 0, b = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, mma_gemv_kernel<2, kEpiSwiglu>, kMmaCtaWarps * kWarp, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, mma_gemv_kernel<1, kEpiStore>, kMmaCtaWarps * kWarp, 0);
+    per_sm = std::max(1, std::min(a, b));
+  }
+  return per_sm;
+}
+
+int mma_gemv_ksplit(int64_t tasks_bound, int K) {
+  const int64_t warps = static_cast<int64_t>(gemv_grid_ctas()) * mma_ctas_per_sm() * kMmaCtaWarps;
+  if (tasks_bound <= 0 || tasks_bound >= warps) return 1;
+  const int nkb = K / kBlock;
+  const int64_t want = ceil_div(warps, tasks_bound);
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({want, nkb / 4, kMaxMmaKSplit})));
+}
+
+cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream) {
+  if (a.ksplit < 1 || a.ksplit > kMaxMmaKSplit || (a.ksplit > 1 && (!a.partial || !a.counters)))
+    return cudaErrorInvalidValue;
+  const int64_t full = static_cast<int64_t>(gemv_grid_ctas()) * mma_ctas_per_sm();
+  const int64_t need = ceil_div(std::max<int64_t>(1, tasks_bound) * a.ksplit, kMmaCtaWarps);
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(full, need)));
   if (ns == 2 && epi == kEpiSwiglu) mma_gemv_kernel<2, kEpiSwiglu><<<grid, kMmaCtaWarps * kWarp, 0, stream>>>(a);
   else if (ns == 1 && epi == kEpiStore) mma_gemv_kernel<1, kEpiStore><<<grid, kMmaCtaWarps * kWarp, 0, stream>>>(a);
   else return cudaErrorInvalidValue;

@@ -14,6 +14,7 @@
 #include "router_device.cuh"
 
 #include <algorithm>
+#include <type_traits>
 
 namespace moe {
 
@@ -179,6 +180,123 @@ __global__ void __launch_bounds__(256) router_logits_tiled_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Split-K logits for decode batches: partial[q][t][e] = sum over the q-th
+// k-range of x[t, k] * w[e, k].  The k-ranges are multiples of kSpan long, so
+// every range starts 16-byte aligned.
+// ---------------------------------------------------------------------------
+constexpr int kSpan = 32;
+constexpr int kMmaRouterWarps = 4;
+constexpr int kPartWarps = 8;
+
+template <typename T>
+MOE_D void mma_16816_t(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1);
+
+template <>
+MOE_D void mma_16816_t<__nv_bfloat16>(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                      uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <>
+MOE_D void mma_16816_t<__half>(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// x and w of the same 16-bit type (bf16 or f16): products are exact in fp32
+// as in the reference's fp32 F.linear; the tensor pipe accumulates in fp32.
+// A warp owns 16 experts (A rows) of one k-range and up to 64 tokens (eight
+// 8-column B tiles) at a time.  Lane (g, c) loads 8 consecutive elements
+// [8c, 8c + 8) of a 32-element span for rows g and g + 8 and token g; words
+// 0/1 of those loads feed one m16n8k16 and words 2/3 another: physical
+// k = 8c + {0,1} plays logical k = 2c + {0,1}, 8c + {2,3} plays 2c + 8 + {0,1}
+// (and 8c + 4.. the same in the second MMA), identically in A and B, so each
+// span's 32 products are each summed once.
+template <typename T>
+__global__ void __launch_bounds__(kMmaRouterWarps * kWarp) router_logits_mma_kernel(
+    const T* __restrict__ x, const T* __restrict__ w, float* __restrict__ partial, int tokens, int hidden,
+    int experts, int kpart) {
+  const int lane = threadIdx.x % kWarp, g = lane / 4, c = lane % 4;
+  const int e0 = (blockIdx.x * kMmaRouterWarps + threadIdx.x / kWarp) * 16;
+  if (e0 >= experts) return;
+  const int k_lo = blockIdx.y * kpart, k_hi = min(hidden, k_lo + kpart);
+  const T* wa = w + static_cast<int64_t>(min(e0 + g, experts - 1)) * hidden + 8 * c;
+  const T* wb = w + static_cast<int64_t>(min(e0 + g + 8, experts - 1)) * hidden + 8 * c;
+  float* out = partial + static_cast<int64_t>(blockIdx.y) * tokens * experts;
+  for (int t0 = 0; t0 < tokens; t0 += 64) {
+    const int ntiles = min(8, static_cast<int>(ceil_div(tokens - t0, 8)));
+    float acc[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+#pragma unroll 2
+    for (int k = k_lo; k < k_hi; k += kSpan) {
+      const uint4 a_lo = __ldg(reinterpret_cast<const uint4*>(wa + k));
+      const uint4 a_hi = __ldg(reinterpret_cast<const uint4*>(wb + k));
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        if (n < ntiles) {
+          const int tok = t0 + 8 * n + g;
+          const uint4 b = tok < tokens ? __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(tok) * hidden +
+                                                                             k + 8 * c))
+                                       : make_uint4(0, 0, 0, 0);
+          mma_16816_t<T>(acc[n], a_lo.x, a_hi.x, a_lo.y, a_hi.y, b.x, b.y);
+          mma_16816_t<T>(acc[n], a_lo.z, a_hi.z, a_lo.w, a_hi.w, b.z, b.w);
+        }
+      }
+    }
+    // acc[n]: (expert e0 + g, tokens 2c, 2c + 1), (expert e0 + g + 8, same tokens)
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      if (n >= ntiles) continue;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tok = t0 + 8 * n + 2 * c + (i & 1);
+        const int e = e0 + g + (i >= 2 ? 8 : 0);
+        if (tok < tokens && e < experts) out[static_cast<int64_t>(tok) * experts + e] = acc[n][i];
+      }
+    }
+  }
+}
+
+// Any other dtype pair: one warp per expert and k-range, fp32 FMAs.
+template <typename XT, typename WT>
+__global__ void __launch_bounds__(kPartWarps * kWarp) router_logits_part_kernel(
+    const XT* __restrict__ x, const WT* __restrict__ w, float* __restrict__ partial, int tokens, int hidden,
+    int experts, int kpart, int vec_ok) {
+  const int lane = threadIdx.x % kWarp;
+  const int e = blockIdx.x * kPartWarps + threadIdx.x / kWarp;
+  if (e >= experts) return;
+  const int k_lo = blockIdx.y * kpart, k_hi = min(hidden, k_lo + kpart);
+  const WT* wrow = w + static_cast<int64_t>(e) * hidden;
+  float* out = partial + static_cast<int64_t>(blockIdx.y) * tokens * experts + e;
+  for (int t = 0; t < tokens; ++t) {
+    const XT* xr = x + static_cast<int64_t>(t) * hidden;
+    float acc = 0.0f;
+    if (vec_ok) {
+      for (int k = k_lo + lane * 8; k < k_hi; k += kWarp * 8) {
+        float wv[8], xv[8];
+        load8<WT>(wrow + k, wv);
+        load8<XT>(xr + k, xv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[i], acc);
+      }
+    } else {
+      for (int k = k_lo + lane; k < k_hi; k += kWarp) acc = fmaf(to_float_any(xr[k]), to_float_any(wrow[k]), acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) out[static_cast<int64_t>(t) * experts] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Selection: one warp per token.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kSelectWarps * kWarp) router_select_kernel(
@@ -231,11 +349,23 @@ template <typename XT, typename WT>
 static cudaError_t launch_split_t(const void* x, const void* w, float* partial, int tokens, int hidden, int experts,
                                   cudaStream_t stream) {
   const int parts = router_split_parts(hidden);
-  const int kpart = static_cast<int>(ceil_div(ceil_div(hidden, parts), kTileK)) * kTileK;
-  dim3 grid(static_cast<unsigned>(ceil_div(experts, kTileN)), static_cast<unsigned>(ceil_div(tokens, kTileM)),
-            static_cast<unsigned>(parts));
-  router_logits_tiled_kernel<XT, WT><<<grid, 256, 0, stream>>>(static_cast<const XT*>(x), static_cast<const WT*>(w),
-                                                                partial, tokens, hidden, experts, kpart);
+  const int kpart = router_split_kpart(hidden);
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(w) % 16 == 0);
+  constexpr bool kPair = (std::is_same<XT, __nv_bfloat16>::value && std::is_same<WT, __nv_bfloat16>::value) ||
+                         (std::is_same<XT, __half>::value && std::is_same<WT, __half>::value);
+  if constexpr (kPair) {
+    if (aligned && hidden % kSpan == 0) {
+      dim3 grid(static_cast<unsigned>(ceil_div(ceil_div(experts, 16), kMmaRouterWarps)),
+                static_cast<unsigned>(parts));
+      router_logits_mma_kernel<XT><<<grid, kMmaRouterWarps * kWarp, 0, stream>>>(
+          static_cast<const XT*>(x), static_cast<const XT*>(w), partial, tokens, hidden, experts, kpart);
+      return cudaGetLastError();
+    }
+  }
+  dim3 grid(static_cast<unsigned>(ceil_div(experts, kPartWarps)), static_cast<unsigned>(parts));
+  const bool vec_ok = aligned && hidden % 8 == 0;
+  router_logits_part_kernel<XT, WT><<<grid, kPartWarps * kWarp, 0, stream>>>(
+      static_cast<const XT*>(x), static_cast<const WT*>(w), partial, tokens, hidden, experts, kpart, vec_ok ? 1 : 0);
   return cudaGetLastError();
 }
 
@@ -251,7 +381,11 @@ static cudaError_t launch_split_w(const void* x, int w_dtype, const void* w, flo
 }
 
 int router_split_parts(int hidden) {
-  return static_cast<int>(std::min<int64_t>(kMaxRouterParts, ceil_div(hidden, 448)));
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(kMaxRouterParts, ceil_div(hidden, 448))));
+}
+
+int router_split_kpart(int hidden) {
+  return static_cast<int>(ceil_div(ceil_div(hidden, router_split_parts(hidden)), kSpan) * kSpan);
 }
 
 cudaError_t launch_router_logits_split(const void* x, int x_dtype, const void* w, int w_dtype, float* partial,

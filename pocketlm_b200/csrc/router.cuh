@@ -25,9 +25,11 @@ cudaError_t launch_router_logits(const void* x, int x_dtype, const void* w, int 
                                  int tokens, int hidden, int experts, cudaStream_t stream);
 
 // Split-K logits for decode batches: partial[q][t][e], q < router_split_parts(hidden)
-// (at most kMaxRouterParts); the parts are summed in order by the selection.
+// (at most kMaxRouterParts), each part router_split_kpart(hidden) columns (a
+// multiple of 32); the parts are summed in order by the selection.
 constexpr int kMaxRouterParts = 16;
 int router_split_parts(int hidden);
+int router_split_kpart(int hidden);
 cudaError_t launch_router_logits_split(const void* x, int x_dtype, const void* w, int w_dtype, float* partial,
                                        int tokens, int hidden, int experts, cudaStream_t stream);
 

@@ -60,8 +60,12 @@ class DsMoELayerGPU:
     up, up scale, down, down scale; the shared expert last) that
     moe_ds_moe_layer_fp8 walks, and a reusable workspace."""
 
-    def __init__(self, layer: Fp8MoELayer, layer_index: int = 0):
-        if not layer.is_full:
+    def __init__(self, layer: Fp8MoELayer, layer_index: int = 0, *, allow_partial: bool = False):
+        """allow_partial: accept a layer holding only some experts; the absent
+        ones get null table entries, which the kernels skip (they contribute
+        nothing), so outputs are only right for tokens routed to resident
+        experts.  For small profiling cases; a full layer is the product path."""
+        if not layer.is_full and not allow_partial:
             raise ValueError("the fused layer path needs every expert resident (a full layer)")
         if layer.device.type != "cuda":
             layer = layer.to(native._device())
@@ -71,6 +75,8 @@ class DsMoELayerGPU:
         n = self.cfg.n_routed + 1
         cols = [[0] * n for _ in range(6)]
         for e in range(n):
+            if not layer.is_full and e not in layer.slots:
+                continue
             for j, t in enumerate(layer.expert(e)):
                 cols[j][e] = int(t.data_ptr())
         self.tables = torch.tensor(cols, dtype=torch.int64, device=layer.device)

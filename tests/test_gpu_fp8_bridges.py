@@ -18,16 +18,15 @@ from pocketlm_b200 import native
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["auto", "mma_regs", "stream", "direct"])
+@pytest.fixture(autouse=True, params=["auto", "stream", "direct"])
 def gemv_impl(request):
-    """Run every case on each expert-GEMV kernel: auto (TMA-fed warp-MMA on
-    the layer path), the register-fed warp-MMA one (both fp8_mma.cu), the
-    bulk-copy streaming one (fp8_stream.cu) and the direct-load one
-    (fp8_gemv.cu)."""
+    """Run every case on each expert-GEMV kernel the bridges use: auto and
+    the direct-load one (fp8_gemv.cu), the bulk-copy streaming one
+    (fp8_stream.cu)."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     lib = native.load_library()
-    assert lib.moe_b200_select_gemv({"auto": 0, "stream": 1, "direct": 2, "mma_regs": 3}[request.param]) == 0
+    assert lib.moe_b200_select_gemv({"auto": 0, "stream": 1, "direct": 2, "mma_tma": 4}[request.param]) == 0
     yield request.param
     torch.cuda.synchronize()
     assert lib.moe_b200_device_error(None) == 0, "a bounded wait inside a kernel gave up"
