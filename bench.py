@@ -47,10 +47,11 @@ METRIC = "DS-V3 MoE layer tokens/s @1/2/4/8 B200; % of HBM or FP8 TC roofline"
 L2_FLUSH_BYTES = 256 << 20
 # kernels per layer forward: router logits, route + dispatch + chunk list, then on the warp-MMA path
 # x -> f16, gate/up, activations -> f16, down (else chunk list, gate/up, down), combine
-KERNELS_PER_LAYER = {"auto": 7, "mma_tma": 7, "stream": 6, "direct": 6}
-GEMV_IMPLS = {"auto": 0, "stream": 1, "direct": 2, "mma_tma": 4}
+KERNELS_PER_LAYER = {"auto": 7, "mma_regs": 7, "mma_tma": 7, "stream": 6, "direct": 6}
+GEMV_IMPLS = {"auto": 0, "stream": 1, "direct": 2, "mma_regs": 3, "mma_tma": 4}
 ROOFLINE_KERNEL = {
-    "auto": "mma_gemv_kernel<2, swiglu> gate/up+SwiGLU (fp8_mma.cu)",
+    "auto": "mma_gemv_async_kernel<2, swiglu> gate/up+SwiGLU (fp8_mma.cu)",
+    "mma_regs": "mma_gemv_kernel<2, swiglu> gate/up+SwiGLU (fp8_mma.cu)",
     "mma_tma": "tma_mma_gemv_kernel<2, swiglu> gate/up+SwiGLU (fp8_mma.cu)",
     "stream": "stream_gemv_kernel gate/up+SwiGLU (fp8_stream.cu)",
     "direct": "grouped_gemv_kernel gate/up+SwiGLU (fp8_gemv.cu)",
@@ -195,7 +196,11 @@ def stage_times(gpu_layer, x, steps: int, flush: torch.Tensor) -> list[float]:
     acc = None
     buf = (ctypes.c_float * 8)()
     for _ in range(steps):
-        flush_l2(flush)
+        # a long flush (~4 x 256 MiB of writes) keeps the GPU busy while the
+        # host enqueues the layer, so the stage events time GPU work rather
+        # than host launch latency
+        for _ in range(4):
+            flush_l2(flush)
         gpu_layer.forward(x)
         n = lib.moe_b200_stage_times(buf, 8)
         vals = [buf[i] for i in range(n)]
@@ -333,21 +338,20 @@ def run_profile_case(args) -> dict:
     by the kernels), run eagerly warmup + steps times.  Holds about
     (experts selected + 1) x 44 MB of weights instead of 11.3 GB."""
     from pocketlm_b200 import native, synth
-    import oracle
-    from pocketlm_b200.runtime import DsMoELayerGPU
+    from pocketlm_b200.runtime import DsMoELayerGPU, run_fp8_router
 
     dev = torch.device("cuda", 0)
     native.load_library()
     cfg = synth.C2_DSV3
-    x = synth.make_hidden(args.tokens, cfg.hidden, seed=args.seed)
-    probe = synth.make_fp8_layer(cfg, seed=args.seed, experts=[])
-    route = oracle.route_deepseek(x, probe.router_weight, probe.bias, top_k=cfg.top_k, n_groups=cfg.n_group,
-                                  topk_groups=cfg.topk_group, route_scale=cfg.route_scale)
-    experts = sorted({int(v) for v in route.ids.reshape(-1).tolist()}) + [cfg.n_routed]
+    xd = synth.make_hidden(args.tokens, cfg.hidden, seed=args.seed).to(dev)
+    # route on the GPU with the layer's own (device-generated) router, then
+    # materialise exactly the experts that routing selects
+    probe = synth.make_fp8_layer(cfg, seed=args.seed, device=dev, experts=[])
+    ids = run_fp8_router(probe, xd).indices_tensor
+    experts = sorted({int(v) for v in ids.reshape(-1).tolist()}) + [cfg.n_routed]
     if args.profile_no_experts:
         experts = []  # routing kernels only: every expert absent, the GEMVs skip them
     layer = DsMoELayerGPU(synth.make_fp8_layer(cfg, seed=args.seed, device=dev, experts=experts), allow_partial=True)
-    xd = x.to(dev)
     for _ in range(args.warmup + args.steps):
         layer.forward(xd)
     torch.cuda.synchronize()

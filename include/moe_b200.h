@@ -194,11 +194,148 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t tokens, i
                          int64_t intermediate, const void* router_weight, int router_dtype,
                          const float* router_bias, int64_t n_routed, int64_t n_group, int64_t topk_group,
                          int64_t top_k, int scoring, float route_scale, const uint64_t* tables,
-                         int has_shared, uint16_t* out_bf16, int64_t* out_ids, uint16_t* out_weights_bf16,
-                         void* workspace, int64_t workspace_bytes, void* stream);
+                         int has_shared, const uint8_t* nan_free, uint16_t* out_bf16, int64_t* out_ids,
+                         uint16_t* out_weights_bf16, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Per-expert flags for moe_ds_moe_layer_fp8's `nan_free` argument (no
+ * reference counterpart): flags[e] = 1 when none of expert e's gate, up and
+ * down e4m3 bytes is 0x7F or 0xFF (tables as above, [6][num_experts]; absent
+ * experts count as clean), else 0.  The layer decodes those two codes as +0
+ * like the reference's linear kernels; an expert known to hold neither skips
+ * that per-byte fix-up.  nan_free may be NULL (every expert is fixed up).
+ * Compute the flags once per set of resident weights. */
+int moe_fp8_nan_free_flags(const uint64_t* tables, int64_t num_experts, int64_t intermediate, int64_t hidden_dim,
+                           uint8_t* flags, void* stream);
 
 int64_t moe_ds_moe_layer_workspace_bytes(int64_t tokens, int64_t hidden_dim, int64_t intermediate,
                                          int64_t n_routed, int64_t top_k, int has_shared);
+
+/* ---------------------------------------------------------------------------
+ * Q4 (signed int4, two codes per byte with the even flat index in the low
+ * nibble, one fp16 scale per output row: q4_quantize.py:21-71) and the
+ * 16-bit formats.  Entry points named after a reference C function return
+ * that function's own positive codes for null pointers / bad sizes (listed
+ * beside each); the others use the negative codes above.
+ * ------------------------------------------------------------------------- */
+
+/* replaces q4_dequant_to_fp16, q4_dequant.cpp:171-208 (which returns void):
+ * out[c * channel_size + k] = fp16(code * scales[c]).  1: null pointer,
+ * 2: non-positive sizes. */
+int moe_q4_dequant_to_fp16(const uint8_t* packed, const uint16_t* scales, uint16_t* out, int64_t num_channels,
+                           int64_t channel_size, void* stream);
+
+/* replaces q4_dequant_many_to_fp16, q4_dequant.cpp:210-286: HOST arrays of
+ * device pointers and sizes, one entry per tensor.  1: a null array,
+ * 2: tensor_count <= 0. */
+int moe_q4_dequant_many_to_fp16(const uint8_t* const* packed, const uint16_t* const* scales, uint16_t* const* out,
+                                const int64_t* num_channels, const int64_t* channel_sizes, int64_t tensor_count,
+                                void* stream);
+
+/* replaces q4_moe_selected_forward_u16, q4_dequant.cpp:357-476: one fp16
+ * token through `selected_count` experts (device uint64 tables of packed
+ * gate/up [intermediate, hidden] and down [hidden, intermediate] codes and
+ * their fp16 row scales), out_fp16[h] = fp16(sum_e route[e] * down_e(...)).
+ * 1: null pointer or non-positive size (q4_dequant.cpp:370-378). */
+int moe_q4_moe_selected_forward_u16(const uint16_t* hidden, const uint64_t* gate_packed, const uint64_t* gate_scales,
+                                    const uint64_t* up_packed, const uint64_t* up_scales,
+                                    const uint64_t* down_packed, const uint64_t* down_scales,
+                                    const float* route_weights, uint16_t* out_fp16, int64_t hidden_size,
+                                    int64_t intermediate_size, int64_t selected_count, void* workspace,
+                                    int64_t workspace_bytes, void* stream);
+int64_t moe_q4_moe_selected_workspace_bytes(int64_t hidden_size, int64_t intermediate_size, int64_t selected);
+
+/* A whole Mixtral-style Q4 MoE layer for a batch of tokens: softmax router
+ * over fp32 logits, top-k renormalised (layer_bridge.py:2682-2689), then each
+ * token through q4_moe_selected_forward_u16's arithmetic -- the batch form of
+ * the reference's per-token loop _run_q4_moe_mlp_token_loop
+ * (layer_bridge.py:909-955).  hidden: [tokens, hidden] bf16 (1) or fp16 (2),
+ * converted to fp16 as the reference does; tables: device uint64 [6][E];
+ * out: [tokens, hidden] in hidden's dtype (the fp16 result, re-rounded to
+ * bf16 for a bf16 caller); out_ids int64 / out_weights fp32 [tokens, top_k]
+ * may be NULL. */
+int moe_q4_moe_layer_u16(const void* hidden, int hidden_dtype, int64_t tokens, int64_t hidden_size,
+                         int64_t intermediate_size, const void* router_weight, int router_dtype, int64_t num_experts,
+                         int64_t top_k, const uint64_t* tables, void* out, int64_t* out_ids, float* out_weights,
+                         void* workspace, int64_t workspace_bytes, void* stream);
+int64_t moe_q4_moe_layer_workspace_bytes(int64_t tokens, int64_t hidden_size, int64_t intermediate_size,
+                                         int64_t num_experts, int64_t top_k);
+
+/* replaces native_pack_u16_rows8, fp16_packed_gemv.cpp:52-77:
+ * packed[(blk * cols + c) * 8 + lane] = weight[blk * 8 + lane, c], zero past
+ * the last row.  1: null pointer, 2: negative size. */
+int moe_pack_u16_rows8(const uint16_t* weight, uint16_t* packed, int64_t rows, int64_t cols, void* stream);
+
+/* replaces native_packed_gemv_rows8, fp16_packed_gemv.cpp:79-116:
+ * out[r] = sum_c hidden[c] * W[r, c] (fp32) from the row8 layout; dtype_code
+ * 0 = fp16, 1 = bf16.  1: null pointer, 2: negative size or bad dtype. */
+int moe_packed_gemv_rows8(const uint16_t* hidden, const uint16_t* packed, float* out, int64_t rows, int64_t cols,
+                          int dtype_code, void* stream);
+
+/* replaces native_moe_selected_forward_u16, fp16_moe.cpp:199-267: every token
+ * through every one of `selected_count` experts stacked as gate/up
+ * [selected, intermediate, hidden] and down [selected, hidden, intermediate],
+ * out[t] = sum_s route_weights[t, s] * expert_s(hidden[t]) in fp32, stored in
+ * the 16-bit dtype.  1: null pointer, 2: non-positive size, 3: bad dtype. */
+int moe_moe_selected_forward_u16(const uint16_t* hidden, const uint16_t* gate_weight, const uint16_t* up_weight,
+                                 const uint16_t* down_weight, const float* route_weights, uint16_t* out,
+                                 int64_t seq_len, int64_t hidden_size, int64_t selected_count,
+                                 int64_t intermediate_size, int dtype_code, void* workspace, int64_t workspace_bytes,
+                                 void* stream);
+int64_t moe_moe_selected_forward_workspace_bytes(int64_t seq_len, int64_t hidden_size, int64_t selected_count,
+                                                 int64_t intermediate_size, int dtype_code);
+
+/* replaces native_moe_forward_fp16, fp16_moe.cpp:90-197: fp16 router
+ * (softmax, top-k, ties to the lower id, optional renorm) then the selected
+ * fp16 experts ([E, intermediate, hidden] / [E, hidden, intermediate]).
+ * selected_experts (int64) and selected_weights (fp32) [seq_len, top_k] may
+ * be NULL.  1: null pointer, 2: non-positive size, 3: top_k > num_experts. */
+int moe_moe_forward_fp16(const uint16_t* hidden, const uint16_t* router_weight, const uint16_t* gate_weight,
+                         const uint16_t* up_weight, const uint16_t* down_weight, uint16_t* out,
+                         int64_t* selected_experts, float* selected_weights, int64_t seq_len, int64_t hidden_size,
+                         int64_t num_experts, int64_t top_k, int64_t intermediate_size, int normalize_topk,
+                         void* workspace, int64_t workspace_bytes, void* stream);
+int64_t moe_moe_forward_fp16_workspace_bytes(int64_t seq_len, int64_t hidden_size, int64_t num_experts,
+                                             int64_t top_k, int64_t intermediate_size);
+
+/* ---------------------------------------------------------------------------
+ * Expert parallelism (no reference counterpart: the reference runs on one
+ * host).  Experts are partitioned contiguously over `world` ranks (rank r
+ * owns experts [r * E / world, (r + 1) * E / world)); router and shared
+ * expert are replicated.  One layer step per rank:
+ *   moe_route_topk -> moe_ep_dispatch_pack -> all-to-all of send_offsets'
+ *   counts, rows and expert ids (the caller's collective) ->
+ *   moe_ep_experts_fp8 over the received rows (+ the rank's own rows for
+ *   the shared expert) -> reverse all-to-all of the fp32 outputs ->
+ *   moe_ep_combine.
+ * The arithmetic per (token, expert) pair and the combine order (top-k slot
+ * order, then the shared expert, fp32, one bf16 rounding) are those of
+ * moe_ds_moe_layer_fp8.
+ * ------------------------------------------------------------------------- */
+
+/* Group the (token, slot) entries of ids / weights ([tokens, top_k]) by
+ * destination rank, token order kept inside a rank: send_rows [tokens*top_k,
+ * hidden] bf16 copies of the tokens' hidden rows, send_expert the expert id
+ * local to its rank, send_offsets [world + 1] the rank boundaries,
+ * entry_pos [tokens*top_k] each entry's send position and pos_weight
+ * [tokens*top_k] the weight at each send position. */
+int moe_ep_dispatch_pack(const int64_t* ids, const float* weights, const uint16_t* hidden_bf16, int64_t tokens,
+                         int64_t hidden_dim, int64_t top_k, int64_t num_experts, int64_t world,
+                         uint16_t* send_rows, int32_t* send_expert, int32_t* send_offsets, int32_t* entry_pos,
+                         float* pos_weight, void* workspace, int64_t workspace_bytes, void* stream);
+int64_t moe_ep_dispatch_workspace_bytes(int64_t tokens, int64_t top_k);
+
+/* out[i] = expert_{row_expert[i]}(rows[i]) (fp32 [rows, hidden]) over this
+ * rank's experts (device tables [6][num_local]); a row whose expert id is
+ * out of range comes back zero.  hidden and intermediate: multiples of 128. */
+int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int64_t rows, int64_t hidden_dim,
+                       int64_t intermediate, const uint64_t* tables, int64_t num_local, const uint8_t* nan_free,
+                       float* out, void* workspace, int64_t workspace_bytes, void* stream);
+int64_t moe_ep_experts_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t intermediate, int64_t num_local);
+
+/* out_bf16[t] = bf16(sum_slot pos_weight[p] * y[p] (+ y[tokens*top_k + t]
+ * when has_shared)), p = entry_pos[t * top_k + slot], slots in order. */
+int moe_ep_combine(const float* y, const int32_t* entry_pos, const float* pos_weight, int64_t tokens, int64_t top_k,
+                   int64_t hidden_dim, int has_shared, uint16_t* out_bf16, void* stream);
 
 /* ---------------------------------------------------------------------------
  * DeepSeek session: opaque handle with the reference's observable counters.
@@ -243,12 +380,13 @@ int moe_b200_stage_timing(int enable);
 int moe_b200_stage_times(float* ms, int max_n);
 
 /* Expert-GEMV implementation (no reference counterpart): 0 = auto (default:
- * the register-fed warp-MMA kernel on the whole-layer path when hidden and
+ * the cp.async-fed warp-MMA kernel on the whole-layer path when hidden and
  * intermediate sizes are multiples of 128, the direct-load kernel
  * elsewhere), 1 = the warp-specialised bulk-copy streaming kernel wherever
- * the shape allows, 2 = the direct-load kernel everywhere, 3 = same as 0,
- * 4 = like 0 but the warp-MMA kernel is fed through per-warp TMA bulk-copy
- * rings.  For A/B parity tests and measurements. */
+ * the shape allows, 2 = the direct-load kernel everywhere, 3 = like 0 with
+ * the warp-MMA kernel loading its weights straight into registers, 4 = like
+ * 0 with the warp-MMA kernel fed through per-warp TMA bulk-copy rings, 5 =
+ * same as 0.  For A/B parity tests and measurements. */
 int moe_b200_select_gemv(int impl);
 
 /* Device error word (no reference counterpart): nonzero when a bounded wait

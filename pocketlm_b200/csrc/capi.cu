@@ -12,6 +12,8 @@
 #include "dequant.cuh"
 #include "dispatch.cuh"
 #include "fp8_gemv.cuh"
+#include "plan.cuh"
+#include "route_host.cuh"
 #include "router.cuh"
 #include "status.cuh"
 
@@ -19,50 +21,6 @@ using namespace moe;
 
 namespace {
 
-// Bump allocator over one workspace block; sizes round up to 256 bytes.
-class Plan {
- public:
-  explicit Plan(char* base = nullptr) : base_(base) {}
-  template <typename T>
-  T* take(int64_t count) {
-    const size_t bytes = (static_cast<size_t>(count > 0 ? count : 1) * sizeof(T) + 255) & ~size_t(255);
-    T* p = base_ ? reinterpret_cast<T*>(base_ + used_) : nullptr;
-    used_ += bytes;
-    return p;
-  }
-  size_t used() const { return used_; }
-
- private:
-  char* base_;
-  size_t used_ = 0;
-};
-
-// Either the caller's workspace or a stream-ordered allocation freed at scope end.
-class Scratch {
- public:
-  Scratch(void* workspace, int64_t bytes, size_t need, cudaStream_t stream) : stream_(stream) {
-    if (workspace) {
-      ok_ = bytes >= static_cast<int64_t>(need);
-      base_ = static_cast<char*>(workspace);
-    } else {
-      ok_ = cudaMallocAsync(reinterpret_cast<void**>(&base_), need > 0 ? need : 256, stream) == cudaSuccess;
-      owned_ = ok_;
-    }
-  }
-  ~Scratch() {
-    if (owned_) cudaFreeAsync(base_, stream_);
-  }
-  bool ok() const { return ok_; }
-  char* base() const { return base_; }
-
- private:
-  cudaStream_t stream_;
-  char* base_ = nullptr;
-  bool ok_ = false;
-  bool owned_ = false;
-};
-
-cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 // Optional stage timing of the fused layer (moe_b200_stage_timing): CUDA events
 // recorded on the launching stream between the layer's kernels.
@@ -75,8 +33,9 @@ int g_marks = 0;
 // shapes allow, direct-load elsewhere), 1 = bulk-copy streaming kernel where
 // supported, 2 = direct-load kernel everywhere.
 int g_gemv_impl = 0;
-// Operand feed of the warp-MMA kernel: 0 = register loads (default), 1 = TMA bulk-copy ring per warp.
-int g_mma_feed = 0;
+// Operand feed of the warp-MMA kernel: 0 = register loads, 1 = TMA bulk-copy
+// ring per warp, 2 = cp.async shared-memory ring per warp (default).
+int g_mma_feed = 2;
 
 cudaError_t gemv(const GemvArgs& a, int x_dtype, int ns, int epi, int nt, bool vec, cudaStream_t stream) {
   if (g_gemv_impl == 1 && vec && stream_gemv_supported(a.K, x_dtype, nt))
@@ -219,10 +178,6 @@ __global__ void validate_pairs_kernel(const int64_t* item, const int64_t* row, i
     if (item[i] < 0 || item[i] >= items || row[i] < 0 || row[i] >= rows) atomicExch(bad, 1);
 }
 
-unsigned grid_for(int64_t n, int threads = 256) {
-  return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, threads), 4096)));
-}
-
 // Shared body of the many / weighted / row-weighted MLP entry points.
 // Entry i = (item i / batch, row i % batch) in item-major order; every row's
 // combine then walks its entries in item order, as the reference sums them.
@@ -273,6 +228,70 @@ int mlp_items(const Tables& t, const float* hidden, const float* route, int rout
 }
 
 }  // namespace
+
+int moe::route_impl(const void* hidden, int hd, const void* w, int wd, const float* bias, int64_t T, int64_t H,
+                      int64_t E, int64_t n_group, int64_t topk_group, int64_t k, int scoring, int renorm,
+                      int fp64, float scale, int round_bf16, int64_t* ids64, int32_t* ids32, float* wf32,
+                      uint16_t* wbf16, float* logits, cudaStream_t stream) {
+  MOE_CUDA(launch_router_logits(hidden, hd, w, wd, logits, static_cast<int>(T), static_cast<int>(H),
+                                static_cast<int>(E), stream),
+           "router logits");
+  RouterSelectParams p{};
+  p.tokens = static_cast<int>(T);
+  p.experts = static_cast<int>(E);
+  p.top_k = static_cast<int>(k);
+  p.n_group = static_cast<int>(n_group);
+  p.topk_group = static_cast<int>(topk_group);
+  p.scoring = scoring;
+  p.renorm = renorm || scoring == kScoreSigmoid;
+  p.softmax_fp64 = fp64;
+  p.round_bf16 = round_bf16;
+  p.route_scale = scale;
+  MOE_CUDA(launch_router_select(logits, bias, p, ids64, ids32, wf32, reinterpret_cast<__nv_bfloat16*>(wbf16),
+                                stream),
+           "router select");
+  return kOk;
+}
+
+int moe::check_route(int64_t T, int64_t H, int64_t E, int64_t n_group, int64_t topk_group, int64_t k) {
+  if (T <= 0 || H <= 0 || E <= 0 || k <= 0 || k > E) return fail(kBadDims, "bad dimensions");
+  if (k > 32) return fail(kUnsupported, "top_k > 32");
+  if (E > 2048) return fail(kUnsupported, "more than 2048 experts");
+  if (n_group < 1 || n_group > 32 || E % n_group != 0) return fail(kBadDims, "n_group must divide num_experts (<= 32)");
+  if (topk_group < 1) return fail(kBadDims, "topk_group < 1");
+  return kOk;
+}
+
+// Destination rank of each (token, slot) entry under a contiguous expert
+// partition: rank = expert / experts_per_rank.
+__global__ void ep_rank_keys_kernel(const int64_t* ids, int64_t n, int64_t per_rank, int64_t world, int32_t* keys) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = ids[i] / per_rank;
+    keys[i] = (ids[i] >= 0 && r < world) ? static_cast<int32_t>(r) : -1;
+  }
+}
+
+// send_rows[p] = hidden[pos_token[p]], send_expert[p] = expert id local to its rank; one warp per row.
+__global__ void ep_gather_kernel(const uint16_t* hidden, const int64_t* ids, const int32_t* keys,
+                                 const int32_t* pos_token, const int32_t* pos_entry, int64_t n, int64_t H,
+                                 int64_t per_rank, int64_t vec, uint16_t* send_rows, int32_t* send_expert) {
+  const int lane = threadIdx.x % 32;
+  for (int64_t p = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) / 32; p < n;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
+    const int32_t e = pos_entry[p];
+    if (e < 0) continue;
+    const uint16_t* src = hidden + static_cast<int64_t>(pos_token[p]) * H;
+    uint16_t* dst = send_rows + p * H;
+    if (vec) {
+      for (int64_t i = lane; i < H / 8; i += 32)
+        reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+    } else {
+      for (int64_t i = lane; i < H; i += 32) dst[i] = src[i];
+    }
+    if (lane == 0) send_expert[p] = static_cast<int32_t>(ids[e] - keys[e] * per_rank);
+  }
+}
 
 extern "C" {
 
@@ -526,39 +545,6 @@ int64_t moe_route_topk_workspace_bytes(int64_t tokens, int64_t experts) {
   return static_cast<int64_t>(p.used());
 }
 
-static int route_impl(const void* hidden, int hd, const void* w, int wd, const float* bias, int64_t T, int64_t H,
-                      int64_t E, int64_t n_group, int64_t topk_group, int64_t k, int scoring, int renorm,
-                      int fp64, float scale, int round_bf16, int64_t* ids64, int32_t* ids32, float* wf32,
-                      uint16_t* wbf16, float* logits, cudaStream_t stream) {
-  MOE_CUDA(launch_router_logits(hidden, hd, w, wd, logits, static_cast<int>(T), static_cast<int>(H),
-                                static_cast<int>(E), stream),
-           "router logits");
-  RouterSelectParams p{};
-  p.tokens = static_cast<int>(T);
-  p.experts = static_cast<int>(E);
-  p.top_k = static_cast<int>(k);
-  p.n_group = static_cast<int>(n_group);
-  p.topk_group = static_cast<int>(topk_group);
-  p.scoring = scoring;
-  p.renorm = renorm || scoring == kScoreSigmoid;
-  p.softmax_fp64 = fp64;
-  p.round_bf16 = round_bf16;
-  p.route_scale = scale;
-  MOE_CUDA(launch_router_select(logits, bias, p, ids64, ids32, wf32, reinterpret_cast<__nv_bfloat16*>(wbf16),
-                                stream),
-           "router select");
-  return kOk;
-}
-
-static int check_route(int64_t T, int64_t H, int64_t E, int64_t n_group, int64_t topk_group, int64_t k) {
-  if (T <= 0 || H <= 0 || E <= 0 || k <= 0 || k > E) return fail(kBadDims, "bad dimensions");
-  if (k > 32) return fail(kUnsupported, "top_k > 32");
-  if (E > 2048) return fail(kUnsupported, "more than 2048 experts");
-  if (n_group < 1 || n_group > 32 || E % n_group != 0) return fail(kBadDims, "n_group must divide num_experts (<= 32)");
-  if (topk_group < 1) return fail(kBadDims, "topk_group < 1");
-  return kOk;
-}
-
 int moe_route_topk(const void* hidden, int hidden_dtype, const void* router_weight, int router_dtype,
                    const float* bias, int64_t T, int64_t H, int64_t E, int64_t n_group, int64_t topk_group,
                    int64_t k, int scoring, int renorm, float route_scale, int round_bf16, int64_t* out_ids,
@@ -609,9 +595,11 @@ struct LayerPlan {
   int64_t n_counters;
 };
 
-static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, int shared, int nt) {
+static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, int shared, int nt,
+                            bool router = true) {
   LayerPlan l{};
-  l.logits = p.take<float>(static_cast<int64_t>(std::max(1, router_split_parts(static_cast<int>(H)))) * T * E);
+  if (router)
+    l.logits = p.take<float>(static_cast<int64_t>(std::max(1, router_split_parts(static_cast<int>(H)))) * T * E);
   l.ids32 = p.take<int32_t>(T * k);
   l.wts = p.take<float>(T * k);
   const int64_t pairs = T * k + (shared ? T : 0);
@@ -623,13 +611,20 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
   const int64_t chunks = std::min(pairs, chunk_capacity(pairs, E + (shared ? 1 : 0), 8));
   l.tasks1 = chunks * ceil_div(I, mma_task_rows(2));
   l.tasks2 = chunks * ceil_div(H, mma_task_rows(1));
-  l.ksplit1 = mma_gemv_ksplit(l.tasks1, static_cast<int>(H));
-  l.ksplit2 = mma_gemv_ksplit(l.tasks2, static_cast<int>(I));
+  // the k-split depends on the feed's resident warps; size for either feed
+  const int ks_regs1 = mma_gemv_ksplit(l.tasks1, static_cast<int>(H));
+  const int ks_regs2 = mma_gemv_ksplit(l.tasks2, static_cast<int>(I));
+  const int ks_async1 = async_gemv_ksplit(l.tasks1, static_cast<int>(H));
+  const int ks_async2 = async_gemv_ksplit(l.tasks2, static_cast<int>(I));
+  const bool async = g_mma_feed == 2;
+  l.ksplit1 = async ? ks_async1 : ks_regs1;
+  l.ksplit2 = async ? ks_async2 : ks_regs2;
   const int64_t frag = 32 * 8;
-  const int64_t part = std::max(l.ksplit1 > 1 ? l.tasks1 * l.ksplit1 : 0, l.ksplit2 > 1 ? l.tasks2 * l.ksplit2 : 0);
-  l.partial = part > 0 ? p.take<float>(part * frag) : nullptr;
-  l.n_counters = (l.ksplit1 > 1 ? l.tasks1 : 0) + (l.ksplit2 > 1 ? l.tasks2 : 0);
-  l.counters = l.n_counters > 0 ? p.take<int32_t>(l.n_counters) : nullptr;
+  const int64_t part = std::max({l.tasks1 * std::max(ks_regs1, ks_async1), l.tasks2 * std::max(ks_regs2, ks_async2),
+                                 int64_t{1}});
+  l.partial = p.take<float>(part * frag);
+  l.n_counters = l.tasks1 + l.tasks2;
+  l.counters = p.take<int32_t>(l.n_counters);
   return l;
 }
 
@@ -637,7 +632,7 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
 // staged as f16 rows with power-of-two scales.
 static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, const LayerPlan& l, int64_t T,
                                  int64_t pairs, int64_t n_segments, int64_t I, int64_t H, bool chunks_ready,
-                                 cudaStream_t s) {
+                                 const uint8_t* nan_free, cudaStream_t s) {
   const MlpScratch& m = l.m;
   if (!chunks_ready) {
     ChunkArgs ca{m.seg_offset, static_cast<int>(n_segments), 8, m.chunk_seg, m.chunk_start, m.chunk_len, m.n_chunks};
@@ -653,9 +648,10 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
   g1.chunk_seg = m.chunk_seg; g1.chunk_start = m.chunk_start; g1.chunk_len = m.chunk_len; g1.n_chunks = m.n_chunks;
   g1.out0 = m.act; g1.N = static_cast<int>(I); g1.K = static_cast<int>(H);
   g1.scale_cols = static_cast<int>(ceil_div(H, kBlock)); g1.nanfix = 1;
-  g1.ksplit = l.ksplit1; g1.partial = l.partial; g1.counters = l.counters;
-  MOE_CUDA(g_mma_feed == 1 ? launch_tma_mma_gemv(g1, 2, kEpiSwiglu, s)
-                           : launch_mma_gemv(g1, 2, kEpiSwiglu, l.tasks1, s),
+  g1.ksplit = l.ksplit1; g1.partial = l.partial; g1.counters = l.counters; g1.nan_free = nan_free;
+  MOE_CUDA(g_mma_feed == 1   ? launch_tma_mma_gemv(g1, 2, kEpiSwiglu, s)
+           : g_mma_feed == 2 ? launch_async_mma_gemv(g1, 2, kEpiSwiglu, l.tasks1, s)
+                             : launch_mma_gemv(g1, 2, kEpiSwiglu, l.tasks1, s),
            "gate/up stage");
   stage_mark(s);
   MOE_CUDA(launch_rows_to_f16(m.act, false, static_cast<int>(pairs), static_cast<int>(I), nullptr, l.act16,
@@ -668,9 +664,10 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
   g2.out0 = m.y; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
   g2.scale_cols = static_cast<int>(ceil_div(I, kBlock));
   g2.ksplit = l.ksplit2;
-  g2.counters = l.counters ? l.counters + (l.ksplit1 > 1 ? l.tasks1 : 0) : nullptr;
-  MOE_CUDA(g_mma_feed == 1 ? launch_tma_mma_gemv(g2, 1, kEpiStore, s)
-                           : launch_mma_gemv(g2, 1, kEpiStore, l.tasks2, s),
+  g2.counters = l.counters + l.tasks1;
+  MOE_CUDA(g_mma_feed == 1   ? launch_tma_mma_gemv(g2, 1, kEpiStore, s)
+           : g_mma_feed == 2 ? launch_async_mma_gemv(g2, 1, kEpiStore, l.tasks2, s)
+                             : launch_mma_gemv(g2, 1, kEpiStore, l.tasks2, s),
            "down stage");
   stage_mark(s);
   return kOk;
@@ -685,8 +682,9 @@ int64_t moe_ds_moe_layer_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_
 int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_t H, int64_t I,
                          const void* router_weight, int router_dtype, const float* router_bias, int64_t E,
                          int64_t n_group, int64_t topk_group, int64_t k, int scoring, float route_scale,
-                         const uint64_t* tables, int has_shared, uint16_t* out_bf16, int64_t* out_ids,
-                         uint16_t* out_weights_bf16, void* workspace, int64_t workspace_bytes, void* stream) {
+                         const uint64_t* tables, int has_shared, const uint8_t* nan_free, uint16_t* out_bf16,
+                         int64_t* out_ids, uint16_t* out_weights_bf16, void* workspace, int64_t workspace_bytes,
+                         void* stream) {
   if (!hidden || !router_weight || !tables || !out_bf16) return fail(kNullPointer, "null pointer");
   int code = check_route(T, H, E, n_group, topk_group, k);
   if (code != kOk) return code;
@@ -718,13 +716,20 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
                l.m.n_chunks};
   bool chunks_ready = false;
   if (T <= 256 && route_dispatch_smem_bytes(static_cast<int>(T), static_cast<int>(E)) <= 200 * 1024) {
-    // decode batches: split-K logits, then selection + dispatch + chunk list in one CTA
-    MOE_CUDA(launch_router_logits_split(hidden, hidden_dtype, router_weight, router_dtype, l.logits,
-                                        static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s),
-             "router logits");
+    // decode batches: logits (cluster-reduced, else split-K partials), then
+    // selection + dispatch + chunk list in one CTA
+    int nparts = 1;
+    cudaError_t lerr = launch_router_logits_cluster(hidden, hidden_dtype, router_weight, router_dtype, l.logits,
+                                                    static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s);
+    if (lerr == cudaErrorNotSupported) {
+      lerr = launch_router_logits_split(hidden, hidden_dtype, router_weight, router_dtype, l.logits,
+                                        static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s);
+      nparts = router_split_parts(static_cast<int>(H));
+    }
+    MOE_CUDA(lerr, "router logits");
     RouteDispatchArgs rd{};
     rd.partial = l.logits;
-    rd.nparts = router_split_parts(static_cast<int>(H));
+    rd.nparts = nparts;
     rd.part_stride = T * E;
     rd.bias = router_bias;
     rd.select.tokens = static_cast<int>(T);
@@ -759,7 +764,7 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   const bool vec = H % 16 == 0 && I % 16 == 0 && aligned16(hidden);
   if (use_mma) {
     code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I, H,
-                                 chunks_ready, s);
+                                 chunks_ready, nan_free, s);
   } else {
     code = run_expert_stages(t, hidden, xd, l.m, l.m.y, S, I, H, ceil_div(H, kBlock), ceil_div(I, kBlock), nt, vec, s);
   }
@@ -772,6 +777,104 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   c.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
   MOE_CUDA(launch_combine(c, s), "combine");
   stage_mark(s);
+  return kOk;
+}
+
+// ---------------------------------------------------------------------------
+// Expert parallelism: dispatch packing, grouped experts over received rows,
+// home combine (the exchange itself is the caller's all-to-all)
+// ---------------------------------------------------------------------------
+
+int64_t moe_ep_dispatch_workspace_bytes(int64_t tokens, int64_t top_k) {
+  if (tokens <= 0 || top_k <= 0) return -1;
+  Plan p;
+  p.take<int32_t>(tokens * top_k);
+  p.take<int32_t>(tokens * top_k);
+  p.take<int32_t>(tokens * top_k);
+  return static_cast<int64_t>(p.used());
+}
+
+int moe_ep_dispatch_pack(const int64_t* ids, const float* weights, const uint16_t* hidden_bf16, int64_t tokens,
+                         int64_t hidden_dim, int64_t top_k, int64_t num_experts, int64_t world,
+                         uint16_t* send_rows, int32_t* send_expert, int32_t* send_offsets, int32_t* entry_pos,
+                         float* pos_weight, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!ids || !weights || !hidden_bf16 || !send_rows || !send_expert || !send_offsets || !entry_pos || !pos_weight)
+    return fail(kNullPointer, "null pointer");
+  if (tokens <= 0 || hidden_dim <= 0 || top_k <= 0 || world <= 0 || num_experts <= 0 || num_experts % world != 0)
+    return fail(kBadDims, "bad dimensions (num_experts must be a multiple of world)");
+  if (world > kMaxBuckets) return fail(kUnsupported, "world too large");
+  const int64_t n = tokens * top_k;
+  cudaStream_t s = as_stream(stream);
+  Scratch scratch(workspace, workspace_bytes, moe_ep_dispatch_workspace_bytes(tokens, top_k), s);
+  if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
+  Plan plan(scratch.base());
+  int32_t* keys = plan.take<int32_t>(n);
+  int32_t* pos_token = plan.take<int32_t>(n);
+  int32_t* pos_entry = plan.take<int32_t>(n);
+  ep_rank_keys_kernel<<<grid_for(n), 256, 0, s>>>(ids, n, num_experts / world, world, keys);
+  MOE_CUDA(cudaGetLastError(), "rank keys");
+  BucketArgs ba{};
+  ba.keys = keys; ba.rows = nullptr; ba.weights = weights; ba.n = static_cast<int>(n); ba.k = static_cast<int>(top_k);
+  ba.key_lo = 0; ba.n_buckets = static_cast<int>(world); ba.bucket_offset = send_offsets; ba.pair_row = pos_token;
+  ba.pair_weight = pos_weight; ba.pair_entry = pos_entry; ba.entry_pair = entry_pos; ba.tail = 0;
+  MOE_CUDA(launch_bucket(ba, s), "rank buckets");
+  const int64_t vec = hidden_dim % 8 == 0 && aligned16(hidden_bf16) && aligned16(send_rows) ? 1 : 0;
+  ep_gather_kernel<<<grid_for(n * 32, 256), 256, 0, s>>>(hidden_bf16, ids, keys, pos_token, pos_entry, n, hidden_dim,
+                                                         num_experts / world, vec, send_rows, send_expert);
+  MOE_CUDA(cudaGetLastError(), "gather send rows");
+  return kOk;
+}
+
+int64_t moe_ep_experts_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t intermediate, int64_t num_local) {
+  if (rows <= 0 || hidden_dim <= 0 || intermediate <= 0 || num_local <= 0) return -1;
+  Plan p;
+  plan_layer(p, rows, hidden_dim, intermediate, num_local, 1, 0, 8, false);
+  return static_cast<int64_t>(p.used());
+}
+
+int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int64_t rows, int64_t hidden_dim,
+                       int64_t intermediate, const uint64_t* tables, int64_t num_local, const uint8_t* nan_free,
+                       float* out, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!rows_bf16 || !row_expert || !tables || !out) return fail(kNullPointer, "null pointer");
+  if (rows <= 0 || hidden_dim <= 0 || intermediate <= 0 || num_local <= 0) return fail(kBadDims, "bad dimensions");
+  if (num_local > kMaxBuckets) return fail(kUnsupported, "too many local experts");
+  if (!mma_gemv_supported(static_cast<int>(hidden_dim), static_cast<int>(intermediate)) ||
+      !mma_gemv_supported(static_cast<int>(intermediate), static_cast<int>(hidden_dim)))
+    return fail(kUnsupported, "hidden and intermediate sizes must be multiples of 128");
+  const int64_t H = hidden_dim, I = intermediate, S = num_local, R = rows;
+  cudaStream_t s = as_stream(stream);
+  Plan sizing;
+  plan_layer(sizing, R, H, I, S, 1, 0, 8, false);
+  Scratch scratch(workspace, workspace_bytes, sizing.used(), s);
+  if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
+  Plan plan(scratch.base());
+  LayerPlan l = plan_layer(plan, R, H, I, S, 1, 0, 8, false);
+  BucketArgs ba{};
+  ba.keys = row_expert; ba.rows = nullptr; ba.weights = nullptr; ba.n = static_cast<int>(R); ba.k = 1;
+  ba.key_lo = 0; ba.n_buckets = static_cast<int>(S); ba.bucket_offset = l.m.seg_offset; ba.pair_row = l.m.pair_row;
+  ba.pair_weight = l.m.pair_weight; ba.pair_entry = l.m.pair_entry; ba.entry_pair = l.m.entry_pair; ba.tail = 0;
+  MOE_CUDA(launch_bucket(ba, s), "expert buckets");
+  Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
+  int code = run_expert_stages_mma(t, rows_bf16, true, l, R, R, S, I, H, false, nan_free, s);
+  if (code != kOk) return code;
+  // back to row order (a row routed nowhere -- key out of range -- comes back zero)
+  CombineArgs c{};
+  c.y = l.m.y; c.row_ptr = nullptr; c.stride = 1; c.row_pairs = l.m.entry_pair; c.pair_weight = nullptr;
+  c.extra_base = -1; c.T = static_cast<int>(R); c.H = static_cast<int>(H); c.out_f32 = out;
+  MOE_CUDA(launch_combine(c, s), "row order");
+  return kOk;
+}
+
+int moe_ep_combine(const float* y, const int32_t* entry_pos, const float* pos_weight, int64_t tokens, int64_t top_k,
+                   int64_t hidden_dim, int has_shared, uint16_t* out_bf16, void* stream) {
+  if (!y || !entry_pos || !pos_weight || !out_bf16) return fail(kNullPointer, "null pointer");
+  if (tokens <= 0 || top_k <= 0 || hidden_dim <= 0) return fail(kBadDims, "bad dimensions");
+  CombineArgs c{};
+  c.y = y; c.row_ptr = nullptr; c.stride = static_cast<int>(top_k); c.row_pairs = entry_pos;
+  c.pair_weight = pos_weight; c.extra_base = has_shared ? static_cast<int>(tokens * top_k) : -1;
+  c.T = static_cast<int>(tokens); c.H = static_cast<int>(hidden_dim);
+  c.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
+  MOE_CUDA(launch_combine(c, as_stream(stream)), "combine");
   return kOk;
 }
 
@@ -789,9 +892,19 @@ int moe_b200_stage_timing(int enable) {
 }
 
 int moe_b200_select_gemv(int impl) {
-  if (impl < 0 || impl > 4) return fail(kBadDims, "impl must be 0, 1, 2, 3 or 4");
+  if (impl < 0 || impl > 5) return fail(kBadDims, "impl must be 0 to 5");
   g_gemv_impl = impl >= 3 ? 0 : impl;
-  g_mma_feed = impl == 4 ? 1 : 0;
+  g_mma_feed = impl == 3 ? 0 : impl == 4 ? 1 : 2;
+  return kOk;
+}
+
+int moe_fp8_nan_free_flags(const uint64_t* tables, int64_t num_experts, int64_t intermediate, int64_t hidden_dim,
+                           uint8_t* flags, void* stream) {
+  if (!tables || !flags) return fail(kNullPointer, "null pointer");
+  if (num_experts <= 0 || intermediate <= 0 || hidden_dim <= 0) return fail(kBadDims, "bad dimensions");
+  MOE_CUDA(launch_nan_free_flags(tables, static_cast<int>(num_experts), intermediate, hidden_dim, flags,
+                                 as_stream(stream)),
+           "nan-free scan");
   return kOk;
 }
 

@@ -38,8 +38,12 @@ MOE_HD int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // (fp8_linear.cpp:31-33) where the hardware conversion yields NaN; clearing
 // the byte to 0x00 gives exactly +0.0.
 MOE_D uint32_t e4m3x4_nan_to_zero(uint32_t w) {
-  const uint32_t eq = __vcmpeq4(w & 0x7F7F7F7Fu, 0x7F7F7F7Fu);  // 0xFF where NaN
-  return w & ~eq;
+  // (byte & 0x7F) + 1 reaches bit 7 exactly when byte & 0x7F == 0x7F (no
+  // carry crosses a byte); prmt's sign mode spreads each bit 7 over its byte
+  const uint32_t s = (w & 0x7F7F7F7Fu) + 0x01010101u;
+  uint32_t mask;
+  asm("prmt.b32 %0, %1, 0, 0xBA98;" : "=r"(mask) : "r"(s));
+  return w & ~mask;
 }
 
 // Two e4m3 bytes (low half of `pair`) -> two floats (exact).

@@ -70,10 +70,12 @@ cudaError_t launch_stage_rows(const void* src, int src_dtype, int rows, int K, c
 // Fill table[i] = base + i * stride_bytes for i < n (device).
 cudaError_t launch_fill_table(uint64_t* table, const void* base, int64_t stride_bytes, int n, cudaStream_t stream);
 
-// Q4: out[c * size + k] = fp16(code(c * size + k) * scale[c]) for every item.
-cudaError_t launch_q4_dequant(const uint64_t* packed, const uint64_t* scales, const uint64_t* out,
-                              const int64_t* channels, const int64_t* sizes, int items, int64_t max_elems,
-                              cudaStream_t stream);
+// Q4: out[c * size + k] = fp16(code(c * size + k) * scale[c]), code the
+// signed int4 at flat index c * size + k (even index in the low nibble).
+cudaError_t launch_q4_dequant(const uint8_t* packed, const uint16_t* scales, uint16_t* out, int64_t channels,
+                              int64_t size, cudaStream_t stream);
+// fp32 copy of n elements of a bf16 / f16 / fp32 array (Dtype).
+cudaError_t launch_to_f32(const void* src, int src_dtype, int64_t n, float* dst, cudaStream_t stream);
 
 // row8 layout: packed[(blk * cols + c) * 8 + lane] = w[blk * 8 + lane, c] (0 past rows).
 cudaError_t launch_pack_rows8(const uint16_t* w, uint16_t* packed, int64_t rows, int64_t cols, cudaStream_t stream);

@@ -246,7 +246,9 @@ __global__ void combine_kernel(CombineArgs a) {
   const int64_t o = static_cast<int64_t>(t) * a.H + h;
   for (int i = 0; i < width; ++i) {
     if (a.out_f32) a.out_f32[o + i] = acc[i];
-    if (a.out_bf16) a.out_bf16[o + i] = __float2bfloat16_rn(acc[i]);
+    if (a.out_f16) a.out_f16[o + i] = __float2half_rn(acc[i]);
+    if (a.out_bf16)
+      a.out_bf16[o + i] = __float2bfloat16_rn(a.bf16_via_f16 ? __half2float(__float2half_rn(acc[i])) : acc[i]);
   }
 }
 

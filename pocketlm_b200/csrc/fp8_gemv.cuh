@@ -40,6 +40,8 @@ struct CombineArgs {
   int H;
   float* out_f32;            // [T, H] or null
   __nv_bfloat16* out_bf16;   // [T, H] or null
+  __half* out_f16;           // [T, H] or null
+  int bf16_via_f16;          // out_bf16 = bf16(f16(sum)): an fp16 result handed on as bf16
 };
 
 // Largest supported chunk size (1, 4 or 8 rows) whose staged rows fit in
@@ -74,6 +76,7 @@ struct MmaArgs {
   int K;
   int scale_cols;
   int nanfix;                // decode e4m3 0x7F/0xFF as +0 (the reference's linear semantics)
+  const uint8_t* nan_free;   // [segments] or null: 1 = the expert holds no 0x7F/0xFF code (no fix needed)
   int ksplit;                // register-fed kernel: k-block ranges per task (1: none)
   float* partial;            // [tasks * ksplit, 32, 8] fp32 fragments when ksplit > 1
   int32_t* counters;         // [tasks] arrival counters: zero on entry, left zero on exit
@@ -86,6 +89,15 @@ bool mma_gemv_supported(int K, int N);
 // when the tasks already occupy every resident warp.
 int mma_gemv_ksplit(int64_t tasks_bound, int K);
 cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream);
+// Same computation, weights staged through a per-warp shared-memory ring by
+// cp.async (fp8_mma.cu); tasks_bound as for launch_mma_gemv.
+int async_gemv_ksplit(int64_t tasks_bound, int K);
+cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream);
+// Per-expert flags for MmaArgs::nan_free: flags[s] = 1 when none of the
+// gate / up / down e4m3 weights of expert s (device tables [6][S], absent
+// experts count as clean) is 0x7F or 0xFF.
+cudaError_t launch_nan_free_flags(const uint64_t* tables, int S, int64_t inter, int64_t hidden, uint8_t* flags,
+                                  cudaStream_t stream);
 // Same computation, weights fed to each warp by TMA bulk copies (fp8_mma.cu).
 cudaError_t launch_tma_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream);
 int read_and_clear_mma_device_error(cudaStream_t stream);

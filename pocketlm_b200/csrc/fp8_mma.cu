@@ -316,6 +316,241 @@ __global__ void __launch_bounds__(kMmaCtaWarps * kWarp) mma_gemv_kernel(MmaArgs 
 }
 
 // ---------------------------------------------------------------------------
+// The same tasks with the weights staged through shared memory by cp.async:
+// every warp owns a ring of kAsyncStages k-blocks; lane l copies its own
+// 8 x 16 bytes of a k-block (the bytes it multiplies) to slots
+// (i * 32 + l) * 16 of a stage and later reads exactly those bytes back, so
+// the ring needs no barrier -- only the lane's own cp.async groups
+// (commit / wait_group).  kAsyncStages - 1 k-blocks of every lane stay in
+// flight without holding registers.  Experts flagged NaN-free skip the
+// 0x7F/0xFF fix-up (a warp-uniform choice per task).
+// ---------------------------------------------------------------------------
+constexpr int kAsyncWarps = 4;
+constexpr int kAsyncStages = 4;
+constexpr int kAsyncStageBytes = kWarp * 8 * 16;  // 4 KiB: one k-block of the warp's 32 row streams
+constexpr int kAsyncSmem = kAsyncWarps * kAsyncStages * kAsyncStageBytes;
+
+MOE_D void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+MOE_D void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+MOE_D void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// acc += this lane's share of W[k-blocks kb0..kb1) . x for one task
+template <bool FIX>
+MOE_D void async_accumulate(float (&acc)[2][4], unsigned char* ring, const uint8_t* const (&arow)[2][2],
+                            const float* const (&srow)[2], const __half* xb, bool bvalid, int kb0, int kb1,
+                            int lane, int c) {
+  auto slot = [&](int stage, int i) { return ring + stage * kAsyncStageBytes + (i * kWarp + lane) * 16; };
+  auto issue = [&](int kbi) {
+    const int stage = (kbi - kb0) % kAsyncStages;
+#pragma unroll
+    for (int sp = 0; sp < 2; ++sp)
+#pragma unroll
+      for (int st = 0; st < 2; ++st)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+          cp_async16(slot(stage, (sp * 2 + st) * 2 + rr), arow[st][rr] + kbi * kBlock + sp * 64);
+  };
+#pragma unroll
+  for (int j = 0; j < kAsyncStages - 1; ++j) {
+    if (kb0 + j < kb1) issue(kb0 + j);
+    cp_async_commit();
+  }
+  for (int kbi = kb0; kbi < kb1; ++kbi) {
+    if (kbi + kAsyncStages - 1 < kb1) issue(kbi + kAsyncStages - 1);
+    cp_async_commit();
+    uint4 b[2][2];
+#pragma unroll
+    for (int sp = 0; sp < 2; ++sp) {
+      const int off = kbi * kBlock + sp * 64;
+      b[sp][0] = bvalid ? __ldg(reinterpret_cast<const uint4*>(xb + off)) : make_uint4(0, 0, 0, 0);
+      b[sp][1] = bvalid ? __ldg(reinterpret_cast<const uint4*>(xb + off + 8)) : make_uint4(0, 0, 0, 0);
+    }
+    const float sc0 = __ldg(srow[0] + kbi), sc1 = __ldg(srow[1] + kbi);
+    cp_async_wait<kAsyncStages - 1>();  // this lane's copies of k-block kbi have landed
+    const int stage = (kbi - kb0) % kAsyncStages;
+    float t[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int sp = 0; sp < 2; ++sp) {
+      uint4 av[2][2];
+#pragma unroll
+      for (int st = 0; st < 2; ++st)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+          av[st][rr] = *reinterpret_cast<const uint4*>(slot(stage, (sp * 2 + st) * 2 + rr));
+      const uint32_t bw[8] = {b[sp][0].x, b[sp][0].y, b[sp][0].z, b[sp][0].w,
+                              b[sp][1].x, b[sp][1].y, b[sp][1].z, b[sp][1].w};
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+#pragma unroll
+        for (int st = 0; st < 2; ++st) {
+          uint32_t wg = word_of(av[st][0], s);
+          uint32_t wh = word_of(av[st][1], s);
+          if (FIX) {
+            wg = e4m3x4_nan_to_zero(wg);
+            wh = e4m3x4_nan_to_zero(wh);
+          }
+          mma_16816(t[st], e4m3x2_to_f16x2_bits(wg), e4m3x2_to_f16x2_bits(wh), e4m3x2_to_f16x2_bits(wg >> 16),
+                    e4m3x2_to_f16x2_bits(wh >> 16), bw[2 * s], bw[2 * s + 1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc[0][i] = fmaf(t[0][i], sc0, acc[0][i]);
+      acc[1][i] = fmaf(t[1][i], sc1, acc[1][i]);
+    }
+  }
+  cp_async_wait<0>();  // nothing of this task in flight before the ring is reused
+}
+
+template <int NS, int EPI>
+__global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(MmaArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int g = lane / 4, c = lane % 4;
+  const int K = a.K, N = a.N;
+  unsigned char* ring = smem + warp * kAsyncStages * kAsyncStageBytes;
+  constexpr int kTaskRows = NS == 2 ? 16 : 32;
+  const int row_tiles = static_cast<int>(ceil_div(N, kTaskRows));
+  const int ksplit = a.ksplit;
+  const int64_t tasks = static_cast<int64_t>(*a.n_chunks) * row_tiles;
+  const int64_t units = tasks * ksplit;
+  const int64_t warp_global = static_cast<int64_t>(blockIdx.x) * kAsyncWarps + warp;
+  const int64_t warp_count = static_cast<int64_t>(gridDim.x) * kAsyncWarps;
+  const int nkb = K / kBlock;
+
+  for (int64_t unit = warp_global; unit < units; unit += warp_count) {
+    const int64_t task = unit / ksplit;
+    const int ks = static_cast<int>(unit % ksplit);
+    const int kb0 = static_cast<int>(static_cast<int64_t>(ks) * nkb / ksplit);
+    const int kb1 = static_cast<int>(static_cast<int64_t>(ks + 1) * nkb / ksplit);
+    const int ch = static_cast<int>(task / row_tiles);
+    const int r0 = static_cast<int>(task % row_tiles) * kTaskRows;
+    const int seg = a.chunk_seg[ch], p0 = a.chunk_start[ch], len = a.chunk_len[ch];
+    const uint8_t* w0 = reinterpret_cast<const uint8_t*>(a.w0[seg]);
+    const float* s0 = reinterpret_cast<const float*>(a.s0[seg]);
+    const uint8_t* w1 = NS == 2 ? reinterpret_cast<const uint8_t*>(a.w1[seg]) : w0;
+    const float* s1 = NS == 2 ? reinterpret_cast<const float*>(a.s1[seg]) : s0;
+    const bool present = w0 && s0 && w1 && s1 &&
+                         ((reinterpret_cast<uintptr_t>(w0) | reinterpret_cast<uintptr_t>(w1)) & 15u) == 0;
+    const uint8_t* arow[2][2];
+    const float* srow[2];
+#pragma unroll
+    for (int st = 0; st < 2; ++st) {
+      const int base = NS == 2 ? r0 : r0 + 16 * st;
+      const uint8_t* w = st == 0 ? w0 : w1;
+      const float* sc = st == 0 ? s0 : s1;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int row = min(base + g + 8 * rr, N - 1);
+        arow[st][rr] = present ? w + static_cast<int64_t>(row) * K + 16 * c : nullptr;
+      }
+      srow[st] = present ? sc + static_cast<int64_t>(min(base, N - 1) / kBlock) * a.scale_cols : nullptr;
+    }
+    const bool bvalid = g < len;
+    const int64_t brow = bvalid ? (a.pair_row ? a.pair_row[p0 + g] : static_cast<int64_t>(p0 + g)) : 0;
+    const __half* xb = a.x16 + brow * K + 16 * c;
+
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if (present && kb0 < kb1) {
+      const bool fix = a.nanfix && !(a.nan_free && a.nan_free[seg]);
+      if (fix) async_accumulate<true>(acc, ring, arow, srow, xb, bvalid, kb0, kb1, lane, c);
+      else async_accumulate<false>(acc, ring, arow, srow, xb, bvalid, kb0, kb1, lane, c);
+    }
+
+    if (ksplit > 1) {
+      float4* part = reinterpret_cast<float4*>(a.partial + (task * ksplit + ks) * (kWarp * 8) + lane * 8);
+      __stcg(part, make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]));
+      __stcg(part + 1, make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]));
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(a.counters + task, 1) == ksplit - 1;
+      last = __shfl_sync(0xFFFFFFFFu, last, 0);
+      if (!last) continue;
+      __threadfence();
+#pragma unroll
+      for (int st = 0; st < 2; ++st)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[st][i] = 0.0f;
+      const float4* parts = reinterpret_cast<const float4*>(a.partial + task * ksplit * (kWarp * 8) + lane * 8);
+      for (int r = 0; r < ksplit; ++r) {
+        const float4 v0 = __ldcg(parts + r * (kWarp * 2));
+        const float4 v1 = __ldcg(parts + r * (kWarp * 2) + 1);
+        acc[0][0] += v0.x; acc[0][1] += v0.y; acc[0][2] += v0.z; acc[0][3] += v0.w;
+        acc[1][0] += v1.x; acc[1][1] += v1.y; acc[1][2] += v1.z; acc[1][3] += v1.w;
+      }
+      if (lane == 0) a.counters[task] = 0;
+    }
+
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int tok = 2 * c + j;
+      if (tok >= len) continue;
+      const int64_t tr = a.pair_row ? a.pair_row[p0 + tok] : static_cast<int64_t>(p0 + tok);
+      const float xs = a.xscale[tr];
+      const int64_t p = p0 + tok;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int i = rr * 2 + j;
+        if (NS == 2) {
+          const int row = r0 + g + 8 * rr;
+          if (row < N) {
+            const float gv = acc[0][i] * xs, uv = acc[1][i] * xs;
+            const float silu = gv / (1.0f + expf(-gv));
+            a.out0[p * N + row] = EPI == kEpiSwiglu ? silu * uv : gv;
+          }
+        } else {
+#pragma unroll
+          for (int st = 0; st < 2; ++st) {
+            const int row = r0 + 16 * st + g + 8 * rr;
+            if (row < N) a.out0[p * N + row] = acc[st][i] * xs;
+          }
+        }
+      }
+    }
+  }
+}
+
+// flags[s] = 1 when expert s's three weight matrices hold no 0x7F / 0xFF byte.
+__global__ void nan_free_kernel(const uint64_t* __restrict__ tables, int S, int64_t inter, int64_t hidden,
+                                uint8_t* __restrict__ flags) {
+  __shared__ int found;
+  const int s = blockIdx.y;
+  if (threadIdx.x == 0) found = 0;
+  __syncthreads();
+  const int64_t sizes[3] = {inter * hidden, inter * hidden, hidden * inter};
+  const uint64_t ptrs[3] = {tables[s], tables[2 * S + s], tables[4 * S + s]};
+  int hit = 0;
+  for (int m = 0; m < 3 && !hit; ++m) {
+    const uint8_t* w = reinterpret_cast<const uint8_t*>(ptrs[m]);
+    if (!w) continue;
+    const int64_t n = sizes[m];
+    const bool vec = (reinterpret_cast<uintptr_t>(w) & 15u) == 0;
+    const int64_t n16 = vec ? n / 16 : 0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16 && !hit;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const uint4 v = __ldcs(reinterpret_cast<const uint4*>(w) + i);
+      const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) hit |= (((words[j] & 0x7F7F7F7Fu) + 0x01010101u) & 0x80808080u) != 0;
+    }
+    for (int64_t i = n16 * 16 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+      hit |= (w[i] & 0x7F) == 0x7F;
+  }
+  if (hit) found = 1;
+  __syncthreads();
+  // flags start at 1 (launcher); any CTA that saw a NaN code clears it
+  if (threadIdx.x == 0 && found) flags[s] = 0;
+}
+
+// ---------------------------------------------------------------------------
 // The same tasks fed by TMA: every warp owns a ring of kTmaStages shared-memory
 // stages; lane l bulk-copies (cp.async.bulk) a 512-byte slice (4 k-blocks) of
 // its row-stream l (stream l / 16, row l % 16 of the task) into slot l of a
@@ -544,6 +779,54 @@ cudaError_t launch_tma_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t 
 }
 
 int read_and_clear_mma_device_error(cudaStream_t stream) { return read_and_clear_local_error(stream); }
+
+static int async_ctas_per_sm() {
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int a = 0, b = 0;
+    cudaFuncSetAttribute(mma_gemv_async_kernel<2, kEpiSwiglu>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAsyncSmem);
+    cudaFuncSetAttribute(mma_gemv_async_kernel<1, kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAsyncSmem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, mma_gemv_async_kernel<2, kEpiSwiglu>, kAsyncWarps * kWarp,
+                                                  kAsyncSmem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, mma_gemv_async_kernel<1, kEpiStore>, kAsyncWarps * kWarp,
+                                                  kAsyncSmem);
+    per_sm = std::max(1, std::min(a, b));
+  }
+  return per_sm;
+}
+
+int async_gemv_ksplit(int64_t tasks_bound, int K) {
+  const int64_t warps = static_cast<int64_t>(gemv_grid_ctas()) * async_ctas_per_sm() * kAsyncWarps;
+  if (tasks_bound <= 0 || tasks_bound >= warps) return 1;
+  const int nkb = K / kBlock;
+  const int64_t want = ceil_div(warps, tasks_bound);
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({want, nkb / 4, kMaxMmaKSplit})));
+}
+
+cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream) {
+  if (a.ksplit < 1 || a.ksplit > kMaxMmaKSplit || (a.ksplit > 1 && (!a.partial || !a.counters)))
+    return cudaErrorInvalidValue;
+  const int64_t full = static_cast<int64_t>(gemv_grid_ctas()) * async_ctas_per_sm();
+  const int64_t need = ceil_div(std::max<int64_t>(1, tasks_bound) * a.ksplit, kAsyncWarps);
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(full, need)));
+  auto kernel = ns == 2 ? mma_gemv_async_kernel<2, kEpiSwiglu> : mma_gemv_async_kernel<1, kEpiStore>;
+  if (!((ns == 2 && epi == kEpiSwiglu) || (ns == 1 && epi == kEpiStore))) return cudaErrorInvalidValue;
+  // per device context, so set on every launch (a host-side call; graphs do not record it)
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAsyncSmem);
+  if (err != cudaSuccess) return err;
+  kernel<<<grid, kAsyncWarps * kWarp, kAsyncSmem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_nan_free_flags(const uint64_t* tables, int S, int64_t inter, int64_t hidden, uint8_t* flags,
+                                  cudaStream_t stream) {
+  if (S <= 0) return cudaSuccess;
+  cudaError_t err = cudaMemsetAsync(flags, 1, static_cast<size_t>(S), stream);
+  if (err != cudaSuccess) return err;
+  dim3 grid(64, static_cast<unsigned>(S));
+  nan_free_kernel<<<grid, 256, 0, stream>>>(tables, S, inter, hidden, flags);
+  return cudaGetLastError();
+}
 
 // Resident 4-warp CTAs per SM of the register-fed kernel (register-limited).
 static int mma_ctas_per_sm() {

@@ -13,6 +13,8 @@
 #include "router.cuh"
 #include "router_device.cuh"
 
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <type_traits>
 
@@ -266,6 +268,91 @@ __global__ void __launch_bounds__(kMmaRouterWarps * kWarp) router_logits_mma_ker
   }
 }
 
+// Decode-batch logits in one pass, no partials: a cluster of kClusterParts
+// CTAs shares one 16-expert tile, each CTA a contiguous k-range split over its
+// 4 warps.  Fragments and the lane mapping are those of
+// router_logits_mma_kernel.  Each warp holds up to 8 spans of its weight rows
+// in registers while it walks the token tiles, the warps' sums meet in shared
+// memory, and after a cluster barrier each CTA adds 1/kClusterParts of the
+// tile's (expert, token) sums over the cluster's CTAs in rank order through
+// distributed shared memory -- a fixed order -- and writes the logits.
+constexpr int kClusterParts = 8;
+constexpr int kClusterWarps = 4;
+constexpr int kClusterTokens = 64;
+constexpr int kWarpSpans = 8;
+
+template <typename T>
+__global__ void __cluster_dims__(kClusterParts, 1, 1) __launch_bounds__(kClusterWarps * kWarp)
+    router_logits_cluster_kernel(const T* __restrict__ x, const T* __restrict__ w, float* __restrict__ logits,
+                                 int tokens, int hidden, int experts, int kpart) {
+  __shared__ float red[kClusterWarps][16][kClusterTokens];
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp, g = lane / 4, c = lane % 4;
+  const int e0 = blockIdx.y * 16;
+  const int wpart = kpart / kClusterWarps;
+  const int k_lo = min(hidden, rank * kpart + warp * wpart), k_hi = min(hidden, k_lo + wpart);
+  const T* wa = w + static_cast<int64_t>(min(e0 + g, experts - 1)) * hidden + 8 * c;
+  const T* wb = w + static_cast<int64_t>(min(e0 + g + 8, experts - 1)) * hidden + 8 * c;
+  for (int t0 = 0; t0 < tokens; t0 += kClusterTokens) {
+    const int ntiles = min(kClusterTokens / 8, static_cast<int>(ceil_div(tokens - t0, 8)));
+    float acc[kClusterTokens / 8][4];
+#pragma unroll
+    for (int n = 0; n < kClusterTokens / 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+    for (int kc = k_lo; kc < k_hi; kc += kWarpSpans * kSpan) {
+      uint4 a_lo[kWarpSpans], a_hi[kWarpSpans];
+#pragma unroll
+      for (int s = 0; s < kWarpSpans; ++s) {
+        const int k = kc + s * kSpan;
+        a_lo[s] = k < k_hi ? __ldg(reinterpret_cast<const uint4*>(wa + k)) : make_uint4(0, 0, 0, 0);
+        a_hi[s] = k < k_hi ? __ldg(reinterpret_cast<const uint4*>(wb + k)) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int n = 0; n < kClusterTokens / 8; ++n) {
+        if (n >= ntiles) break;
+        const int tok = t0 + 8 * n + g;
+        const T* xr = x + static_cast<int64_t>(min(tok, tokens - 1)) * hidden + 8 * c;
+        uint4 b[kWarpSpans];
+#pragma unroll
+        for (int s = 0; s < kWarpSpans; ++s) {
+          const int k = kc + s * kSpan;
+          b[s] = (tok < tokens && k < k_hi) ? __ldg(reinterpret_cast<const uint4*>(xr + k)) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int s = 0; s < kWarpSpans; ++s) {
+          mma_16816_t<T>(acc[n], a_lo[s].x, a_hi[s].x, a_lo[s].y, a_hi[s].y, b[s].x, b[s].y);
+          mma_16816_t<T>(acc[n], a_lo[s].z, a_hi[s].z, a_lo[s].w, a_hi[s].w, b[s].z, b[s].w);
+        }
+      }
+    }
+    // acc[n]: (expert e0 + g (+8), tokens 8n + 2c, 8n + 2c + 1)
+#pragma unroll
+    for (int n = 0; n < kClusterTokens / 8; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) red[warp][g + (i >= 2 ? 8 : 0)][8 * n + 2 * c + (i & 1)] = acc[n][i];
+    __syncthreads();
+    for (int j = threadIdx.x; j < 16 * kClusterTokens; j += blockDim.x) {
+      float* cell = &red[0][0][0] + j;
+      float s = cell[0];
+#pragma unroll
+      for (int q = 1; q < kClusterWarps; ++q) s += cell[q * 16 * kClusterTokens];
+      cell[0] = s;
+    }
+    cluster.sync();
+    // this CTA's share of the tile: entries [rank * per, (rank + 1) * per)
+    constexpr int kPer = 16 * kClusterTokens / kClusterParts;
+    for (int j = rank * kPer + threadIdx.x; j < (rank + 1) * kPer; j += blockDim.x) {
+      const int le = j / kClusterTokens, lt = j % kClusterTokens;
+      float s = 0.0f;
+      for (int q = 0; q < kClusterParts; ++q) s += cluster.map_shared_rank(&red[0][0][0], q)[j];
+      const int e = e0 + le, t = t0 + lt;
+      if (e < experts && t < tokens) logits[static_cast<int64_t>(t) * experts + e] = s;
+    }
+    cluster.sync();  // remote reads done before red[] is rewritten or the CTA exits
+  }
+}
+
 // Any other dtype pair: one warp per expert and k-range, fp32 FMAs.
 template <typename XT, typename WT>
 __global__ void __launch_bounds__(kPartWarps * kWarp) router_logits_part_kernel(
@@ -378,6 +465,25 @@ static cudaError_t launch_split_w(const void* x, int w_dtype, const void* w, flo
     case kDtypeF16: return launch_split_t<XT, __half>(x, w, partial, tokens, hidden, experts, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t launch_router_logits_cluster(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
+                                         int tokens, int hidden, int experts, cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(w) % 16 == 0);
+  if (x_dtype != w_dtype || (x_dtype != kDtypeBF16 && x_dtype != kDtypeF16) || !aligned || hidden % kSpan != 0)
+    return cudaErrorNotSupported;
+  const int kpart = static_cast<int>(ceil_div(ceil_div(hidden, kClusterParts), kSpan * kClusterWarps)) *
+                    kSpan * kClusterWarps;
+  dim3 grid(kClusterParts, static_cast<unsigned>(ceil_div(experts, 16)));
+  if (x_dtype == kDtypeBF16)
+    router_logits_cluster_kernel<__nv_bfloat16><<<grid, kClusterWarps * kWarp, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), logits, tokens, hidden, experts,
+        kpart);
+  else
+    router_logits_cluster_kernel<__half><<<grid, kClusterWarps * kWarp, 0, stream>>>(
+        static_cast<const __half*>(x), static_cast<const __half*>(w), logits, tokens, hidden, experts, kpart);
+  return cudaGetLastError();
 }
 
 int router_split_parts(int hidden) {

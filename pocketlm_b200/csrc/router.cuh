@@ -33,6 +33,12 @@ int router_split_kpart(int hidden);
 cudaError_t launch_router_logits_split(const void* x, int x_dtype, const void* w, int w_dtype, float* partial,
                                        int tokens, int hidden, int experts, cudaStream_t stream);
 
+// Decode-batch logits [T, E] in one launch (clusters of 8 CTAs reduce over k
+// in distributed shared memory): bf16 x bf16 or f16 x f16, hidden % 32 == 0,
+// 16-byte aligned operands; cudaErrorNotSupported otherwise.
+cudaError_t launch_router_logits_cluster(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
+                                         int tokens, int hidden, int experts, cudaStream_t stream);
+
 cudaError_t launch_router_select(const float* logits, const float* bias, const RouterSelectParams& p,
                                  int64_t* ids64, int32_t* ids32, float* weights_f32,
                                  __nv_bfloat16* weights_bf16, cudaStream_t stream);

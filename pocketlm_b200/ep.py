@@ -1,0 +1,161 @@
+"""Expert-parallel DeepSeek-V3 MoE layer: one process per GPU, experts
+partitioned over the ranks, tokens exchanged with all-to-all collectives.
+
+Rank r of N owns routed experts [r * E / N, (r + 1) * E / N); the router and
+the shared expert are replicated.  A layer step on each rank, for that rank's
+own tokens (the reference's run_fp8_moe flow, fp8_source.py:1569-1884, with
+the per-expert loop spread over the ranks):
+
+  1. route (sigmoid + bias, group-limited top-k; weights rounded through the
+     hidden dtype as fp8_source.py:1547 does);
+  2. pack the (token, slot) entries by destination rank -- token rows, the
+     expert id local to that rank, and where each entry went;
+  3. all-to-all of the per-rank counts, then of the rows and expert ids;
+  4. grouped FP8 experts over the received rows, plus the shared expert over
+     the rank's own rows in the same launch;
+  5. reverse all-to-all of the fp32 expert outputs;
+  6. combine at home in top-k slot order, then the shared expert, one bf16
+     rounding -- the order of the single-GPU layer.
+
+The counts exchange needs the sizes on the host (NCCL collectives take host
+counts), so a step synchronises once.  The compute steps go through an ops
+object: CudaEPOps calls libmoe_b200's kernels; tests substitute a CPU
+implementation to check the exchange logic with gloo ranks.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from . import native, synth
+
+
+@dataclass
+class Packed:
+    send_rows: torch.Tensor     # bf16 [T*k, H], grouped by destination rank
+    send_expert: torch.Tensor   # int32 [T*k], expert id local to the destination
+    send_offsets: torch.Tensor  # int32 [N + 1]
+    entry_pos: torch.Tensor     # int32 [T*k]: send position of entry t*k + slot
+    pos_weight: torch.Tensor    # fp32 [T*k]: routing weight at each send position
+
+
+class CudaEPOps:
+    """The compute steps on the GPU (libmoe_b200)."""
+
+    def __init__(self, layer: "ExpertParallelLayer"):
+        self.layer = layer
+        self.lib = native.load_library()
+        self._ws = torch.empty((0,), dtype=torch.uint8, device=layer.device)
+
+    def _workspace(self, nbytes: int) -> torch.Tensor:
+        if self._ws.numel() < nbytes:
+            self._ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=self.layer.device)
+        return self._ws
+
+    def route(self, x: torch.Tensor):
+        L = self.layer
+        cfg = L.cfg
+        return native.route_topk(x, L.router_weight, L.bias, top_k=cfg.top_k, n_group=cfg.n_group,
+                                 topk_group=cfg.topk_group, scoring_func=cfg.scoring_func,
+                                 route_scale=cfg.route_scale, round_to_hidden_dtype=True, weights_fp32=True)
+
+    def pack(self, ids: torch.Tensor, w: torch.Tensor, x: torch.Tensor) -> Packed:
+        L = self.layer
+        T, k, H = int(ids.shape[0]), int(ids.shape[1]), L.cfg.hidden
+        dev = x.device
+        p = Packed(torch.empty((T * k, H), dtype=torch.bfloat16, device=dev),
+                   torch.empty((T * k,), dtype=torch.int32, device=dev),
+                   torch.empty((L.world + 1,), dtype=torch.int32, device=dev),
+                   torch.empty((T * k,), dtype=torch.int32, device=dev),
+                   torch.empty((T * k,), dtype=torch.float32, device=dev))
+        ws = self._workspace(int(self.lib.moe_ep_dispatch_workspace_bytes(T, k)))
+        code = self.lib.moe_ep_dispatch_pack(
+            native._ptr(ids), native._ptr(w), native._ptr(x), T, H, k, L.cfg.n_routed, L.world,
+            native._ptr(p.send_rows), native._ptr(p.send_expert), native._ptr(p.send_offsets),
+            native._ptr(p.entry_pos), native._ptr(p.pos_weight), native._ptr(ws), ws.numel(), native._stream())
+        native._check(code, "moe_ep_dispatch_pack")
+        return p
+
+    def experts(self, rows: torch.Tensor, row_expert: torch.Tensor) -> torch.Tensor:
+        L = self.layer
+        R = int(rows.shape[0])
+        out = torch.empty((R, L.cfg.hidden), dtype=torch.float32, device=rows.device)
+        ws = self._workspace(int(self.lib.moe_ep_experts_workspace_bytes(R, L.cfg.hidden, L.cfg.inter, L.n_local + 1)))
+        code = self.lib.moe_ep_experts_fp8(
+            native._ptr(rows), native._ptr(row_expert), R, L.cfg.hidden, L.cfg.inter, native._ptr(L.tables),
+            L.n_local + 1, native._ptr(L.nan_free), native._ptr(out), native._ptr(ws), ws.numel(), native._stream())
+        native._check(code, "moe_ep_experts_fp8")
+        return out
+
+    def combine(self, y: torch.Tensor, p: Packed, T: int) -> torch.Tensor:
+        L = self.layer
+        k = L.cfg.top_k
+        out = torch.empty((T, L.cfg.hidden), dtype=torch.bfloat16, device=y.device)
+        code = self.lib.moe_ep_combine(native._ptr(y), native._ptr(p.entry_pos), native._ptr(p.pos_weight), T, k,
+                                       L.cfg.hidden, 1, native._ptr(out), native._stream())
+        native._check(code, "moe_ep_combine")
+        return out
+
+
+class ExpertParallelLayer:
+    """This rank's share of one expert-parallel DS-V3 MoE layer.
+
+    `layer` may be a full or partial synth.Fp8MoELayer holding at least the
+    router, this rank's experts and the shared expert; by default they are
+    generated from `seed` (identical on every rank)."""
+
+    def __init__(self, cfg: synth.DsMoEConfig, rank: int, world: int, *, group=None, seed: int = 20,
+                 device: torch.device | str | None = None, layer: synth.Fp8MoELayer | None = None, ops=None):
+        if cfg.n_routed % world:
+            raise ValueError("the routed experts must split evenly over the ranks")
+        self.cfg, self.rank, self.world, self.group = cfg, int(rank), int(world), group
+        self.n_local = cfg.n_routed // world
+        self.first = self.rank * self.n_local
+        local = list(range(self.first, self.first + self.n_local)) + [cfg.n_routed]
+        if device is None:
+            device = native._device()
+        self.device = torch.device(device)
+        if layer is None:
+            layer = synth.make_fp8_layer(cfg, seed=seed, device=self.device, experts=local)
+        self.layer = layer
+        self.router_weight = layer.router_weight.to(self.device)
+        self.bias = layer.bias.to(self.device)
+        # local tables [6][n_local + 1]: this rank's experts, then the shared expert
+        self.local_experts = [[t.to(self.device) for t in layer.expert(e)] for e in local]
+        self.tables = torch.tensor([[int(ex[j].data_ptr()) for ex in self.local_experts] for j in range(6)],
+                                   dtype=torch.int64, device=self.device) if self.device.type == "cuda" else None
+        self.nan_free = None
+        if self.device.type == "cuda":
+            self.nan_free = torch.zeros((self.n_local + 1,), dtype=torch.uint8, device=self.device)
+            native._check(native.load_library().moe_fp8_nan_free_flags(
+                native._ptr(self.tables), self.n_local + 1, cfg.inter, cfg.hidden, native._ptr(self.nan_free),
+                native._stream()), "moe_fp8_nan_free_flags")
+        self.ops = ops(self) if ops is not None else CudaEPOps(self)
+
+    def forward(self, x: torch.Tensor):
+        """x [T, H] bf16 (this rank's tokens) -> (out [T, H] bf16, ids [T, k], weights fp32 [T, k])."""
+        cfg, ops = self.cfg, self.ops
+        x = x.reshape(-1, cfg.hidden).contiguous()
+        T, k, H = int(x.shape[0]), cfg.top_k, cfg.hidden
+        ids, w = ops.route(x)
+        p = ops.pack(ids, w, x)
+        send_counts = (p.send_offsets[1:] - p.send_offsets[:-1]).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        counts = torch.stack([send_counts, recv_counts]).cpu()  # the step's one host synchronisation
+        sc, rc = counts[0].tolist(), counts[1].tolist()
+        R = int(sum(rc))
+        rows = torch.empty((R + T, H), dtype=torch.bfloat16, device=x.device)
+        row_expert = torch.empty((R + T,), dtype=torch.int32, device=x.device)
+        dist.all_to_all_single(rows[:R], p.send_rows, rc, sc, group=self.group)
+        dist.all_to_all_single(row_expert[:R], p.send_expert, rc, sc, group=self.group)
+        rows[R:].copy_(x)
+        row_expert[R:].fill_(self.n_local)  # the shared expert, last in the local tables
+        y = ops.experts(rows, row_expert)
+        y_back = torch.empty((T * k + T, H), dtype=torch.float32, device=x.device)
+        dist.all_to_all_single(y_back[:T * k], y[:R], sc, rc, group=self.group)
+        y_back[T * k:].copy_(y[R:])
+        return ops.combine(y_back, p, T), ids, w

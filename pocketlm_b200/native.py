@@ -94,7 +94,8 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
                         _P, _P, _P, _P, _I64, _P], _INT),
     "moe_route_topk_workspace_bytes": ([_I64, _I64], _I64),
     "moe_ds_moe_layer_fp8": ([_P, _INT, _I64, _I64, _I64, _P, _INT, _P, _I64, _I64, _I64, _I64, _INT, _F32, _P,
-                              _INT, _P, _P, _P, _P, _I64, _P], _INT),
+                              _INT, _P, _P, _P, _P, _P, _I64, _P], _INT),
+    "moe_fp8_nan_free_flags": ([_P, _I64, _I64, _I64, _P, _P], _INT),
     "moe_ds_moe_layer_workspace_bytes": ([_I64] * 5 + [_INT], _I64),
     "moe_ds_session_create": ([_I64] * 4, _P),
     "moe_ds_session_destroy": ([_P], None),
@@ -103,6 +104,23 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_ds_layers_executed_count": ([_P], _I64),
     "moe_ds_moe_layer_forward_f32": ([_P, _P, _P, _I64, _I64, _I64, _P, _P], _INT),
     "moe_ds_moe_layer_forward_fp8_f32": ([_P] * 9 + [_I64] * 6 + [_P, _P, _I64, _P], _INT),
+    "moe_q4_dequant_to_fp16": ([_P, _P, _P, _I64, _I64, _P], _INT),
+    "moe_q4_dequant_many_to_fp16": ([_P, _P, _P, _P, _P, _I64, _P], _INT),
+    "moe_q4_moe_selected_forward_u16": ([_P] * 9 + [_I64] * 3 + [_P, _I64, _P], _INT),
+    "moe_q4_moe_selected_workspace_bytes": ([_I64] * 3, _I64),
+    "moe_q4_moe_layer_u16": ([_P, _INT, _I64, _I64, _I64, _P, _INT, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P], _INT),
+    "moe_q4_moe_layer_workspace_bytes": ([_I64] * 5, _I64),
+    "moe_pack_u16_rows8": ([_P, _P, _I64, _I64, _P], _INT),
+    "moe_packed_gemv_rows8": ([_P, _P, _P, _I64, _I64, _INT, _P], _INT),
+    "moe_moe_selected_forward_u16": ([_P] * 6 + [_I64] * 4 + [_INT, _P, _I64, _P], _INT),
+    "moe_moe_selected_forward_workspace_bytes": ([_I64] * 4 + [_INT], _I64),
+    "moe_moe_forward_fp16": ([_P] * 8 + [_I64] * 5 + [_INT, _P, _I64, _P], _INT),
+    "moe_moe_forward_fp16_workspace_bytes": ([_I64] * 5, _I64),
+    "moe_ep_dispatch_pack": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _P], _INT),
+    "moe_ep_dispatch_workspace_bytes": ([_I64, _I64], _I64),
+    "moe_ep_experts_fp8": ([_P, _P, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _I64, _P], _INT),
+    "moe_ep_experts_workspace_bytes": ([_I64] * 4, _I64),
+    "moe_ep_combine": ([_P, _P, _P, _I64, _I64, _I64, _INT, _P, _P], _INT),
     "moe_b200_stage_timing": ([_INT], _INT),
     "moe_b200_stage_times": ([_P, _INT], _INT),
     "moe_b200_select_gemv": ([_INT], _INT),
@@ -578,13 +596,15 @@ def _python_ds_router_topk(hidden: torch.Tensor, router_weights: torch.Tensor, k
 
 def route_topk(hidden: torch.Tensor, router_weight: torch.Tensor, bias: torch.Tensor | None, *, top_k: int,
                n_group: int = 1, topk_group: int = 1, scoring_func: str = "sigmoid", route_scale: float = 1.0,
-               renorm: bool = False, round_to_hidden_dtype: bool = True):
+               renorm: bool = False, round_to_hidden_dtype: bool = True, weights_fp32: bool = False):
     """Batched router on the GPU: the math of run_fp8_router
     (fp8_source.py:1522-1547) or, with scoring_func="softmax" and renorm,
     the Mixtral router (layer_bridge.py:2682-2689).
 
     Returns (ids int64 [T, k], weights [T, k]) with weights in hidden.dtype
-    when round_to_hidden_dtype (the reference casts them), else fp32."""
+    when round_to_hidden_dtype (the reference casts them), else fp32;
+    weights_fp32 returns them as fp32 values (rounded through the hidden
+    dtype when round_to_hidden_dtype)."""
     x = _gpu(hidden.reshape(-1, int(hidden.shape[-1])))
     dt = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}
     if x.dtype not in dt:
@@ -606,7 +626,9 @@ def route_topk(hidden: torch.Tensor, router_weight: torch.Tensor, bias: torch.Te
                               float(route_scale), 1 if (round_to_hidden_dtype and wb is not None) else 0,
                               _ptr(ids), _ptr(wf), _ptr(wb), _ptr(ws), ws.numel(), _stream())
     _check(code, "moe_route_topk")
-    if round_to_hidden_dtype:
+    if weights_fp32:
+        weights = wf
+    elif round_to_hidden_dtype:
         weights = wb if wb is not None else wf.to(hidden.dtype)
     else:
         weights = wf
@@ -716,4 +738,270 @@ def ds_moe_layer_forward_fp8(session: DeepSeekNativeSession, items, hidden: torc
                                                 _ptr(ws), ws.numel(), _stream())
     if code != 0:
         raise RuntimeError(f"ds_moe_layer_forward_fp8_f32 failed with code {code}")
+    return out.to(_out_device(hidden))
+
+
+# ---------------------------------------------------------------------------
+# Q4 (native/__init__.py:204-215, 4025-4155)
+# ---------------------------------------------------------------------------
+
+def native_q4_available() -> bool:
+    return not _native_disabled() and _lib_or_none() is not None and torch.cuda.is_available()
+
+
+def native_q4_load_error() -> Exception | None:
+    _lib_or_none()
+    return _LIB_ERROR
+
+
+def q4_dequant_to_fp16(packed: torch.Tensor, scales: torch.Tensor, num_channels: int,
+                       channel_size: int) -> torch.Tensor:
+    _require(native_q4_available(), "Q4 dequant", _native_disabled())
+    pk = _gpu(packed.reshape(-1), torch.uint8)
+    sc = _gpu(scales.reshape(-1), torch.float16)
+    n = int(num_channels) * int(channel_size)
+    if pk.numel() * 2 < n or sc.numel() < int(num_channels):
+        raise ValueError("packed / scales are too small for num_channels x channel_size")
+    out = torch.empty((n,), dtype=torch.float16, device=pk.device)
+    code = load_library().moe_q4_dequant_to_fp16(_ptr(pk), _ptr(sc), _ptr(out), int(num_channels),
+                                                 int(channel_size), _stream())
+    _check(code, "q4_dequant_to_fp16")
+    return out.to(_out_device(packed))
+
+
+def q4_dequant_many_to_fp16(items: list[tuple[torch.Tensor, torch.Tensor, int, int]]) -> list[torch.Tensor]:
+    _require(native_q4_available(), "Q4 batch dequant", _native_disabled())
+    if not items:
+        return []
+    keep, outs = [], []
+    n = len(items)
+    pk_ptrs, sc_ptrs, out_ptrs = (_P * n)(), (_P * n)(), (_P * n)()
+    channels, sizes = (_I64 * n)(), (_I64 * n)()
+    for i, (packed, scales, num_channels, channel_size) in enumerate(items):
+        pk = _gpu(packed.reshape(-1), torch.uint8)
+        sc = _gpu(scales.reshape(-1), torch.float16)
+        elems = int(num_channels) * int(channel_size)
+        if pk.numel() * 2 < elems or sc.numel() < int(num_channels):
+            raise ValueError("packed / scales are too small for num_channels x channel_size")
+        out = torch.empty((elems,), dtype=torch.float16, device=pk.device)
+        keep += [pk, sc]
+        outs.append(out)
+        pk_ptrs[i], sc_ptrs[i], out_ptrs[i] = _ptr(pk), _ptr(sc), _ptr(out)
+        channels[i], sizes[i] = int(num_channels), int(channel_size)
+    code = load_library().moe_q4_dequant_many_to_fp16(pk_ptrs, sc_ptrs, out_ptrs, channels, sizes, n, _stream())
+    if code != 0:
+        raise RuntimeError(f"Native Q4 batch dequant failed with code {code}")
+    return [o.to(_out_device(items[i][0])) for i, o in enumerate(outs)]
+
+
+def q4_moe_selected_forward_u16(hidden: torch.Tensor, experts: list, route_weights: torch.Tensor, *,
+                                hidden_size: int, intermediate_size: int) -> torch.Tensor:
+    _require(native_q4_available(), "Q4 MoE selected forward", _native_disabled())
+    if not experts:
+        raise ValueError("experts must not be empty")
+    x = _gpu(hidden.reshape(-1), torch.float16)
+    if x.numel() != int(hidden_size):
+        raise ValueError("hidden size mismatch")
+    route = _gpu(route_weights.reshape(-1), torch.float32)
+    if route.numel() != len(experts):
+        raise ValueError("route weight count must match selected experts")
+    dtypes = (torch.uint8, torch.float16) * 3
+    tensors = [[_gpu(t.reshape(-1), dt) for t, dt in zip(item, dtypes)] for item in experts]
+    table = torch.tensor([[int(item[j].data_ptr()) for item in tensors] for j in range(6)], dtype=torch.int64,
+                         device=x.device)
+    S = len(experts)
+    out = torch.empty((int(hidden_size),), dtype=torch.float16, device=x.device)
+    cols = [_P(int(table.data_ptr()) + 8 * S * j) for j in range(6)]
+    code = load_library().moe_q4_moe_selected_forward_u16(_ptr(x), *cols, _ptr(route), _ptr(out), int(hidden_size),
+                                                          int(intermediate_size), S, None, 0, _stream())
+    if code != 0:
+        raise RuntimeError(f"Native Q4 MoE selected forward failed with code {code}")
+    return out.to(_out_device(hidden))
+
+
+# ---------------------------------------------------------------------------
+# row8 packed GEMV (native/__init__.py:1658-1668, 2108-2223)
+# ---------------------------------------------------------------------------
+from collections import OrderedDict  # noqa: E402
+
+_PACKED_GEMV_CACHE: "OrderedDict[str, torch.Tensor]" = OrderedDict()
+_PACKED_GEMV_CACHE_BYTES = 0
+_PACKED_GEMV_CACHE_STATS = {"hits": 0, "misses": 0, "stores": 0, "evictions": 0}
+
+
+def native_fp16_packed_gemv_available() -> bool:
+    return not _native_packed_gemv_disabled() and _lib_or_none() is not None and torch.cuda.is_available()
+
+
+def _packed_gemv_cache_disabled() -> bool:
+    return _flag("PCKETLM_DISABLE_PACKED_GEMV_CACHE")
+
+
+def _packed_gemv_cache_budget_bytes() -> int:
+    raw = os.environ.get("PCKETLM_PACKED_GEMV_CACHE_MB", "").strip()
+    if not raw:
+        return 0
+    try:
+        mb = int(raw)
+    except ValueError:
+        return 0
+    return max(0, mb) * 1024 * 1024
+
+
+def reset_packed_gemv_cache() -> None:
+    global _PACKED_GEMV_CACHE_BYTES
+    _PACKED_GEMV_CACHE.clear()
+    _PACKED_GEMV_CACHE_BYTES = 0
+    for key in _PACKED_GEMV_CACHE_STATS:
+        _PACKED_GEMV_CACHE_STATS[key] = 0
+
+
+def packed_gemv_cache_stats() -> dict[str, int | float]:
+    return {
+        **_PACKED_GEMV_CACHE_STATS,
+        "resident_count": len(_PACKED_GEMV_CACHE),
+        "resident_bytes": _PACKED_GEMV_CACHE_BYTES,
+        "resident_mb": round(_PACKED_GEMV_CACHE_BYTES / 1024 / 1024, 4),
+        "budget_bytes": _packed_gemv_cache_budget_bytes(),
+    }
+
+
+def _u16_storage_dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.float16:
+        return 0
+    if dtype == torch.bfloat16:
+        return 1
+    raise TypeError("native KV kernels require torch.float16 or torch.bfloat16 tensors")
+
+
+def pack_weight_rows8(weight: torch.Tensor) -> torch.Tensor:
+    """[rows, cols] fp16/bf16 -> flat uint16 row8 layout [ceil(rows/8) * cols * 8],
+    packed on the GPU and kept there (device of the result: the current CUDA device)."""
+    _require(native_fp16_packed_gemv_available(), "packed GEMV", _native_packed_gemv_disabled())
+    if weight.dtype not in {torch.float16, torch.bfloat16}:
+        raise TypeError("pack_weight_rows8 requires torch.float16 or torch.bfloat16 weight")
+    if weight.ndim != 2:
+        raise ValueError("weight must have shape [rows, cols]")
+    w = _gpu(weight).view(torch.uint16)
+    rows, cols = int(w.shape[0]), int(w.shape[1])
+    packed = torch.empty((((rows + 7) // 8) * cols * 8,), dtype=torch.uint16, device=w.device)
+    code = load_library().moe_pack_u16_rows8(_ptr(w), _ptr(packed), rows, cols, _stream())
+    if code != 0:
+        raise RuntimeError(f"native_pack_u16_rows8 failed with code {code}")
+    return packed
+
+
+def cached_pack_weight_rows8(cache_key: str, weight: torch.Tensor) -> torch.Tensor:
+    global _PACKED_GEMV_CACHE_BYTES
+    if _packed_gemv_cache_disabled():
+        _PACKED_GEMV_CACHE_STATS["misses"] += 1
+        return pack_weight_rows8(weight)
+    budget = _packed_gemv_cache_budget_bytes()
+    if budget <= 0:
+        _PACKED_GEMV_CACHE_STATS["misses"] += 1
+        return pack_weight_rows8(weight)
+    key = str(cache_key)
+    cached = _PACKED_GEMV_CACHE.get(key)
+    if cached is not None:
+        _PACKED_GEMV_CACHE.move_to_end(key)
+        _PACKED_GEMV_CACHE_STATS["hits"] += 1
+        return cached
+    _PACKED_GEMV_CACHE_STATS["misses"] += 1
+    packed = pack_weight_rows8(weight)
+    packed_bytes = int(packed.numel() * packed.element_size())
+    if packed_bytes > budget:
+        return packed
+    while _PACKED_GEMV_CACHE and _PACKED_GEMV_CACHE_BYTES + packed_bytes > budget:
+        _old, old_value = _PACKED_GEMV_CACHE.popitem(last=False)
+        _PACKED_GEMV_CACHE_BYTES -= int(old_value.numel() * old_value.element_size())
+        _PACKED_GEMV_CACHE_STATS["evictions"] += 1
+    _PACKED_GEMV_CACHE[key] = packed
+    _PACKED_GEMV_CACHE_BYTES += packed_bytes
+    _PACKED_GEMV_CACHE_STATS["stores"] += 1
+    return packed
+
+
+def packed_gemv_rows8(hidden: torch.Tensor, packed_weight: torch.Tensor, *, rows: int, cols: int) -> torch.Tensor:
+    _require(native_fp16_packed_gemv_available(), "packed GEMV", _native_packed_gemv_disabled())
+    if hidden.dtype not in {torch.float16, torch.bfloat16}:
+        raise TypeError("packed_gemv_rows8 requires torch.float16 or torch.bfloat16 hidden")
+    if packed_weight.dtype != torch.uint16:
+        raise TypeError("packed_weight must be a torch.uint16 tensor from pack_weight_rows8")
+    x = _gpu(hidden.reshape(-1))
+    if x.numel() != int(cols):
+        raise ValueError("hidden length does not match packed weight column count")
+    pk = _gpu(packed_weight)
+    if pk.numel() != ((int(rows) + 7) // 8) * int(cols) * 8:
+        raise ValueError("packed weight length does not match rows/cols")
+    out = torch.empty((int(rows),), dtype=torch.float32, device=x.device)
+    code = load_library().moe_packed_gemv_rows8(_ptr(x.view(torch.uint16)), _ptr(pk), _ptr(out), int(rows), int(cols),
+                                                _u16_storage_dtype_code(x.dtype), _stream())
+    if code != 0:
+        raise RuntimeError(f"native_packed_gemv_rows8 failed with code {code}")
+    return out.to(_out_device(hidden))
+
+
+# ---------------------------------------------------------------------------
+# 16-bit dense MoE (native/__init__.py:2465-2574)
+# ---------------------------------------------------------------------------
+
+def native_fp16_moe_available() -> bool:
+    return not _native_moe_disabled() and _lib_or_none() is not None and torch.cuda.is_available()
+
+
+def native_fp16_moe_error() -> Exception | None:
+    _lib_or_none()
+    return _LIB_ERROR
+
+
+def moe_forward_fp16(hidden: torch.Tensor, router_weight: torch.Tensor, gate_weight: torch.Tensor,
+                     up_weight: torch.Tensor, down_weight: torch.Tensor, *, top_k: int,
+                     normalize_topk: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    _require(native_fp16_moe_available(), "fp16 MoE", _native_moe_disabled())
+    tensors = [hidden, router_weight, gate_weight, up_weight, down_weight]
+    if any(t.dtype != torch.float16 for t in tensors):
+        raise TypeError("moe_forward_fp16 requires torch.float16 tensors")
+    if hidden.ndim != 2:
+        raise ValueError("hidden must have shape [seq_len, hidden_size]")
+    if gate_weight.ndim != 3 or up_weight.ndim != 3 or down_weight.ndim != 3:
+        raise ValueError("expert weights must be rank-3 [num_experts, rows, cols]")
+    x, rw, g, u, d = (_gpu(t) for t in tensors)
+    T, H = int(x.shape[0]), int(x.shape[1])
+    E, I, k = int(rw.shape[0]), int(g.shape[1]), int(top_k)
+    out = torch.empty((T, H), dtype=torch.float16, device=x.device)
+    ids = torch.empty((T, k), dtype=torch.int64, device=x.device)
+    wts = torch.empty((T, k), dtype=torch.float32, device=x.device)
+    u16 = lambda t: _ptr(t.view(torch.uint16))  # noqa: E731
+    code = load_library().moe_moe_forward_fp16(u16(x), u16(rw), u16(g), u16(u), u16(d), u16(out), _ptr(ids),
+                                               _ptr(wts), T, H, E, k, I, 1 if normalize_topk else 0, None, 0,
+                                               _stream())
+    if code != 0:
+        raise RuntimeError(f"native_moe_forward_fp16 failed with code {code}")
+    dev = _out_device(hidden)
+    return out.to(dev), ids.to(dev), wts.to(dev)
+
+
+def moe_selected_forward_u16(hidden: torch.Tensor, gate_weight: torch.Tensor, up_weight: torch.Tensor,
+                             down_weight: torch.Tensor, route_weights: torch.Tensor) -> torch.Tensor:
+    _require(native_fp16_moe_available(), "fp16 MoE", _native_moe_disabled())
+    dtype_code = _u16_storage_dtype_code(hidden.dtype)
+    tensors = [hidden, gate_weight, up_weight, down_weight]
+    if any(t.dtype != hidden.dtype for t in tensors):
+        raise TypeError(f"moe_selected_forward_u16 requires all model tensors to share dtype {hidden.dtype}")
+    if hidden.ndim != 2:
+        raise ValueError("hidden must have shape [seq_len, hidden_size]")
+    if gate_weight.ndim != 3 or up_weight.ndim != 3 or down_weight.ndim != 3:
+        raise ValueError("selected expert weights must be rank-3")
+    T, H = int(hidden.shape[0]), int(hidden.shape[1])
+    S, I = int(gate_weight.shape[0]), int(gate_weight.shape[1])
+    if route_weights.shape != (T, S):
+        raise ValueError("route_weights must have shape [seq_len, selected_count]")
+    x, g, u, d = (_gpu(t) for t in tensors)
+    route = _gpu(route_weights, torch.float32)
+    out = torch.empty((T, H), dtype=hidden.dtype, device=x.device)
+    u16 = lambda t: _ptr(t.view(torch.uint16))  # noqa: E731
+    code = load_library().moe_moe_selected_forward_u16(u16(x), u16(g), u16(u), u16(d), _ptr(route), u16(out), T, H,
+                                                       S, I, dtype_code, None, 0, _stream())
+    if code != 0:
+        raise RuntimeError(f"native_moe_selected_forward_u16 failed with code {code}")
     return out.to(_out_device(hidden))

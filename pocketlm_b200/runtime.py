@@ -80,6 +80,11 @@ class DsMoELayerGPU:
             for j, t in enumerate(layer.expert(e)):
                 cols[j][e] = int(t.data_ptr())
         self.tables = torch.tensor(cols, dtype=torch.int64, device=layer.device)
+        # experts with no 0x7F/0xFF byte skip the decoder's NaN-code fix-up (computed once)
+        self.nan_free = torch.zeros((n,), dtype=torch.uint8, device=layer.device)
+        native._check(native.load_library().moe_fp8_nan_free_flags(
+            native._ptr(self.tables), n, self.cfg.inter, self.cfg.hidden, native._ptr(self.nan_free),
+            native._stream()), "moe_fp8_nan_free_flags")
         self._workspace = torch.empty((0,), dtype=torch.uint8, device=layer.device)
 
     def workspace_for(self, tokens: int) -> torch.Tensor:
@@ -113,7 +118,8 @@ class DsMoELayerGPU:
             native._ptr(x), native.DTYPE_BF16 if x.dtype == torch.bfloat16 else native.DTYPE_F32, T, cfg.hidden,
             cfg.inter, native._ptr(rw), rdt[rw.dtype], native._ptr(self.layer.bias), cfg.n_routed, cfg.n_group,
             cfg.topk_group, cfg.top_k, 1 if cfg.scoring_func == "softmax" else 0, float(cfg.route_scale),
-            native._ptr(self.tables), 1, native._ptr(out), native._ptr(ids), native._ptr(weights),
+            native._ptr(self.tables), 1, native._ptr(self.nan_free), native._ptr(out), native._ptr(ids),
+            native._ptr(weights),
             native._ptr(ws), ws.numel(), native._stream())
         native._check(code, "moe_ds_moe_layer_fp8")
         return out
@@ -208,3 +214,49 @@ def run_fp8_moe(layer: DsMoELayerGPU, hidden: torch.Tensor, *, dtype: torch.dtyp
         output_shape=[int(v) for v in output.shape], selected_experts=selected,
         routed_weight_bytes=len(selected) * cfg.expert_bytes, shared_weight_bytes=cfg.expert_bytes,
         router=router, output_tensor=output, total_elapsed_seconds=time.perf_counter() - start, ready=True)
+
+
+class Q4MoELayerGPU:
+    """A Mixtral-shape Q4 MoE layer (pocketlm_b200.synth.Q4MoELayer) resident
+    in HBM for moe_q4_moe_layer_u16: softmax top-k router, then every token
+    through its experts with q4_moe_selected_forward_u16's arithmetic (the
+    batch form of layer_bridge.py:909-955)."""
+
+    def __init__(self, layer):
+        if layer.gate_p.device.type != "cuda":
+            layer = layer.to(native._device())
+        self.layer = layer
+        self.cfg = layer.cfg
+        E = self.cfg.n_experts
+        cols = [[int(t.data_ptr()) for t in (layer.gate_p[e], layer.gate_s[e], layer.up_p[e], layer.up_s[e],
+                                             layer.down_p[e], layer.down_s[e])] for e in range(E)]
+        self.tables = torch.tensor(cols, dtype=torch.int64, device=layer.gate_p.device).t().contiguous()
+        self._workspace = torch.empty((0,), dtype=torch.uint8, device=layer.gate_p.device)
+
+    def workspace_for(self, tokens: int) -> torch.Tensor:
+        cfg = self.cfg
+        need = int(native.load_library().moe_q4_moe_layer_workspace_bytes(tokens, cfg.hidden, cfg.inter,
+                                                                          cfg.n_experts, cfg.top_k))
+        if self._workspace.numel() < need:
+            self._workspace = torch.empty((need,), dtype=torch.uint8, device=self.tables.device)
+        return self._workspace
+
+    def forward(self, hidden: torch.Tensor, *, out: torch.Tensor | None = None, ids: torch.Tensor | None = None,
+                weights: torch.Tensor | None = None) -> torch.Tensor:
+        """hidden [T, H] bf16 or fp16 on the layer's device -> out [T, H] same dtype."""
+        cfg = self.cfg
+        x = hidden.reshape(-1, cfg.hidden).contiguous()
+        if x.dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("hidden must be bf16 or fp16")
+        T = int(x.shape[0])
+        if out is None:
+            out = torch.empty((T, cfg.hidden), dtype=x.dtype, device=x.device)
+        ws = self.workspace_for(T)
+        rw = self.layer.router_weight
+        rdt = {torch.float32: native.DTYPE_F32, torch.bfloat16: native.DTYPE_BF16, torch.float16: native.DTYPE_F16}
+        code = native.load_library().moe_q4_moe_layer_u16(
+            native._ptr(x), rdt[x.dtype], T, cfg.hidden, cfg.inter, native._ptr(rw), rdt[rw.dtype], cfg.n_experts,
+            cfg.top_k, native._ptr(self.tables), native._ptr(out), native._ptr(ids), native._ptr(weights),
+            native._ptr(ws), ws.numel(), native._stream())
+        native._check(code, "moe_q4_moe_layer_u16")
+        return out

@@ -20,16 +20,16 @@ from tests.parity import COS_GATE, REL_L2_GATE, cos_dist, id_mismatches, rel_l2
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["auto", "mma_tma", "stream", "direct"])
+@pytest.fixture(autouse=True, params=["auto", "mma_regs", "mma_tma", "stream", "direct"])
 def gemv_impl(request):
-    """Run every case on each expert-GEMV kernel: auto (the register-fed
-    warp-MMA kernel on the layer path), the TMA-fed warp-MMA one (both
-    fp8_mma.cu), the bulk-copy streaming one (fp8_stream.cu) and the
-    direct-load one (fp8_gemv.cu)."""
+    """Run every case on each expert-GEMV kernel: auto (the cp.async-fed
+    warp-MMA kernel on the layer path), the register-fed and TMA-fed
+    warp-MMA ones (all fp8_mma.cu), the bulk-copy streaming one
+    (fp8_stream.cu) and the direct-load one (fp8_gemv.cu)."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     lib = native.load_library()
-    assert lib.moe_b200_select_gemv({"auto": 0, "stream": 1, "direct": 2, "mma_tma": 4}[request.param]) == 0
+    assert lib.moe_b200_select_gemv({"auto": 0, "stream": 1, "direct": 2, "mma_regs": 3, "mma_tma": 4}[request.param]) == 0
     yield request.param
     torch.cuda.synchronize()
     assert lib.moe_b200_device_error(None) == 0, "a bounded wait inside a kernel gave up"
@@ -133,6 +133,29 @@ def test_dsv3_one_token_layer_is_repeatable(cuda_device):
         assert torch.equal(graphed(x), first)
     expected, _route = oracle.ds_moe_layer(x.cpu(), gpu.layer)
     assert rel_l2(first, expected) <= REL_L2_GATE and cos_dist(first, expected) <= COS_GATE
+
+
+def test_nan_codes_decode_as_zero_on_the_layer_path(cuda_device):
+    """e4m3 codes 0x7F / 0xFF decode as +0 (the reference's linear kernels,
+    fp8_linear.cpp:31-33).  Experts holding such bytes are flagged and take
+    the fix-up path; the others skip it."""
+    cfg = synth.C1_TINY
+    base = synth.make_fp8_layer(cfg, seed=11)
+    w13, w2 = base.w13.clone(), base.w2.clone()
+    w13[3, 0, 5, :40] = 0x7F
+    w13[3, 0, 9, 100:140] = 0xFF
+    w2[3, 7, :64] = 0x7F
+    w13[cfg.n_routed, 1, 2, :20] = 0xFF  # the shared expert
+    layer = synth.Fp8MoELayer(cfg, base.router_weight, base.bias, w13, base.s13, w2, base.s2)
+    gpu = DsMoELayerGPU(layer.to("cuda"))
+    flags = gpu.nan_free.cpu()
+    assert flags[3] == 0 and flags[cfg.n_routed] == 0 and int(flags.sum()) == cfg.n_routed - 1
+    x = synth.make_hidden(16, cfg.hidden, seed=12)
+    out = gpu.forward(x.cuda())
+    assert torch.isfinite(out.float()).all()
+    expected, route = oracle.ds_moe_layer(x, layer)
+    assert 3 in route.ids.reshape(-1).tolist()
+    assert rel_l2(out, expected) <= REL_L2_GATE and cos_dist(out, expected) <= COS_GATE
 
 
 def test_dsv3_router_result_api(cuda_device):
