@@ -21,8 +21,10 @@ on this host (`cpu_baseline`, oracle/_ref), clocks sampled during the run.
 
 --impl reference times the reference's CPU path alone (oracle/_ref kernels
 driven through run_fp8_moe's default flow) on a bounded token sample.
-With --gpus N > 1 (torchrun), each rank runs its own replica of the layer on
-its own tokens (weak scaling); value is the sum over ranks.
+With --gpus N > 1 (torchrun) the layer runs expert-parallel (pocketlm_b200/ep.py):
+each rank holds 256/N routed experts plus the shared expert and router, routes
+its own --tokens tokens and exchanges them with NCCL all-to-alls (weak
+scaling); value is N * tokens / the slowest rank's step time.
 """
 
 from __future__ import annotations
@@ -332,6 +334,97 @@ def run_ours(args, rank: int, world: int) -> dict | None:
     }
 
 
+def run_ours_ep(args, rank: int, world: int) -> dict | None:
+    """N > 1: expert parallelism.  Rank r holds routed experts
+    [r * 256 / N, (r + 1) * 256 / N) plus the shared expert and router, and
+    routes its own --tokens tokens; a step is one layer forward on every rank
+    (route, pack, NCCL all-to-alls, local grouped experts, reverse exchange,
+    combine).  Timed per rank with CUDA events between barriers; the max over
+    ranks is the step time; value = N * tokens / step time."""
+    import torch.distributed as dist
+
+    from pocketlm_b200 import synth
+    from pocketlm_b200.ep import ExpertParallelLayer
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    cfg = synth.C2_DSV3
+    T = args.tokens
+    ep = ExpertParallelLayer(cfg, rank, world, seed=args.seed, device=dev)
+    flush = torch.zeros((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
+    x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 100 * rank + T, device=dev)
+    peaks = measured_peaks()
+
+    def timed(fn) -> float:
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        stream = torch.cuda.current_stream()
+        times = []
+        for _ in range(args.steps):
+            flush_l2(flush)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            fn()
+            e.record(stream)
+            e.synchronize()
+            times.append(s.elapsed_time(e))
+        dist.barrier()
+        t = torch.tensor([statistics.mean(times)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with ClockSampler(dev.index) as clocks:
+        ms = timed(lambda: ep.forward(x))
+        x_host = x.cpu().pin_memory()
+        out_host = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
+
+        def e2e():
+            xd = x_host.to(dev, non_blocking=True)
+            out, _ids, _w = ep.forward(xd)
+            out_host.copy_(out, non_blocking=True)
+
+        e2e_ms = timed(e2e)
+    _out, ids, _w = ep.forward(x)
+    gathered = [torch.empty_like(ids) for _ in range(world)]
+    dist.all_gather(gathered, ids)
+    clock_info = clocks.summary()
+    if rank != 0:
+        return None
+    all_ids = torch.cat(gathered).cpu()
+    per_rank = cfg.n_routed // world
+    # bytes streamed by the busiest rank: its experts hit by any token (+ the shared expert)
+    hit = sorted({int(v) for v in all_ids.reshape(-1).tolist()})
+    busiest = max(sum(1 for e in hit if r * per_rank <= e < (r + 1) * per_rank) for r in range(world)) + 1
+    gs, ds = cfg.gate_scale_shape, cfg.down_scale_shape
+    expert_bytes = 3 * cfg.inter * cfg.hidden + 4 * (2 * gs[0] * gs[1] + ds[0] * ds[1])
+    rank_bytes = busiest * expert_bytes + cfg.n_routed * cfg.hidden * 2
+    achieved = rank_bytes / (ms / 1e3) / 1e9
+    return {
+        "metric": METRIC, "value": world * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (e4m3 weights decoded exactly, bf16 activations, fp32 accumulate)",
+        "data": "synthetic (seeded random DS-V3-shape weights and activations; no checkpoint)",
+        "config": {"workload": f"c2-dsv3-decode-T{T}", "tokens_per_gpu": T, "hidden": cfg.hidden,
+                   "moe_intermediate": cfg.inter, "experts": f"{cfg.n_routed}+1", "top_k": cfg.top_k,
+                   "n_group": cfg.n_group, "topk_group": cfg.topk_group, "parallelism": f"ep{world}",
+                   "l2": "256 MiB L2 flush between timed steps"},
+        "roofline": {"bound": "hbm", "kernel": "whole EP layer step on the busiest rank",
+                     "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} hbm_gbs",
+                     "algorithmic_bytes_per_launch": rank_bytes, "traffic": None,
+                     "experts_on_busiest_rank": busiest},
+        "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * cfg.hidden * 2,
+                "d2h_bytes_per_step": T * cfg.hidden * 2},
+        # route (logits, select), pack (rank keys, bucket, gather), experts (bucket, chunk list,
+        # x staging, gate/up, activation staging, down, row order), combine
+        "gpu_launches": 13 * args.steps,
+        "cpu_baseline": None,
+        "clocks": clock_info,
+    }
+
+
 def run_profile_case(args) -> dict:
     """A small case for ncu: the config-2 layer with only the experts that
     `--tokens` tokens select materialised (the others are absent and skipped
@@ -422,7 +515,12 @@ def main() -> None:
         if args.profile:
             result = run_profile_case(args)
         else:
-            result = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world)
+            if args.impl == "reference":
+                result = run_reference(args, rank, world)
+            elif world > 1:
+                result = run_ours_ep(args, rank, world)
+            else:
+                result = run_ours(args, rank, world)
         if result is not None:
             print(json.dumps(result), flush=True)
     finally:

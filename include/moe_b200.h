@@ -187,15 +187,28 @@ int64_t moe_route_topk_workspace_bytes(int64_t tokens, int64_t num_experts);
  * (fp8_source.py:1569-1884).  hidden: [tokens, hidden_dim] bf16 (dtype 1) or
  * fp32 (dtype 0).  tables: device uint64 array [6][n_routed + has_shared]
  * (gate w, gate scale, up w, up scale, down w, down scale; the shared expert
- * is the last entry).  out_bf16: [tokens, hidden_dim] bf16.  out_ids (int64)
+ * is the last entry).  nan_free: moe_fp8_nan_free_flags' per-expert flags or
+ * NULL.  weight_layout: 0 = row-major weights (the reference's), 1 = the
+ * tiled layout below.  out_bf16: [tokens, hidden_dim] bf16.  out_ids (int64)
  * and out_weights_bf16 ([tokens, top_k]) may be NULL.
  * ------------------------------------------------------------------------- */
 int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t tokens, int64_t hidden_dim,
                          int64_t intermediate, const void* router_weight, int router_dtype,
                          const float* router_bias, int64_t n_routed, int64_t n_group, int64_t topk_group,
                          int64_t top_k, int scoring, float route_scale, const uint64_t* tables,
-                         int has_shared, const uint8_t* nan_free, uint16_t* out_bf16, int64_t* out_ids,
-                         uint16_t* out_weights_bf16, void* workspace, int64_t workspace_bytes, void* stream);
+                         int has_shared, const uint8_t* nan_free, int weight_layout, uint16_t* out_bf16,
+                         int64_t* out_ids, uint16_t* out_weights_bf16, void* workspace, int64_t workspace_bytes,
+                         void* stream);
+
+/* Fragment-native weight layout (no reference counterpart), weight_layout 1
+ * of moe_ds_moe_layer_fp8: moe_fp8_tile_weights copies a row-major e4m3
+ * [rows, cols] matrix (cols % 128 == 0) into moe_fp8_tiled_bytes(rows, cols)
+ * bytes laid out so that each 16-row x 128-column block sits in 2 KiB in the
+ * order the decode GEMV's lanes read it -- every warp then streams one
+ * contiguous range per matrix.  Same bytes, same results; the block scales
+ * keep their layout.  Tables for weight_layout 1 point at tiled copies. */
+int64_t moe_fp8_tiled_bytes(int64_t rows, int64_t cols);
+int moe_fp8_tile_weights(const uint8_t* weight, uint8_t* tiled, int64_t rows, int64_t cols, void* stream);
 
 /* Per-expert flags for moe_ds_moe_layer_fp8's `nan_free` argument (no
  * reference counterpart): flags[e] = 1 when none of expert e's gate, up and
@@ -388,6 +401,8 @@ int moe_b200_stage_times(float* ms, int max_n);
  * 0 with the warp-MMA kernel fed through per-warp TMA bulk-copy rings, 5 =
  * same as 0.  For A/B parity tests and measurements. */
 int moe_b200_select_gemv(int impl);
+/* The current selection (0 for the default, else 1 to 4). */
+int moe_b200_selected_gemv(void);
 
 /* Device error word (no reference counterpart): nonzero when a bounded wait
  * inside a kernel gave up (1: producer, 2: consumer, 4: drain, 8: misaligned

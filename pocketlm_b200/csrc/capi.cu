@@ -632,7 +632,7 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
 // staged as f16 rows with power-of-two scales.
 static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, const LayerPlan& l, int64_t T,
                                  int64_t pairs, int64_t n_segments, int64_t I, int64_t H, bool chunks_ready,
-                                 const uint8_t* nan_free, cudaStream_t s) {
+                                 const uint8_t* nan_free, cudaStream_t s, int tiled = 0) {
   const MlpScratch& m = l.m;
   if (!chunks_ready) {
     ChunkArgs ca{m.seg_offset, static_cast<int>(n_segments), 8, m.chunk_seg, m.chunk_start, m.chunk_len, m.n_chunks};
@@ -649,6 +649,7 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
   g1.out0 = m.act; g1.N = static_cast<int>(I); g1.K = static_cast<int>(H);
   g1.scale_cols = static_cast<int>(ceil_div(H, kBlock)); g1.nanfix = 1;
   g1.ksplit = l.ksplit1; g1.partial = l.partial; g1.counters = l.counters; g1.nan_free = nan_free;
+  g1.tiled = tiled;
   MOE_CUDA(g_mma_feed == 1   ? launch_tma_mma_gemv(g1, 2, kEpiSwiglu, s)
            : g_mma_feed == 2 ? launch_async_mma_gemv(g1, 2, kEpiSwiglu, l.tasks1, s)
                              : launch_mma_gemv(g1, 2, kEpiSwiglu, l.tasks1, s),
@@ -682,10 +683,11 @@ int64_t moe_ds_moe_layer_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_
 int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_t H, int64_t I,
                          const void* router_weight, int router_dtype, const float* router_bias, int64_t E,
                          int64_t n_group, int64_t topk_group, int64_t k, int scoring, float route_scale,
-                         const uint64_t* tables, int has_shared, const uint8_t* nan_free, uint16_t* out_bf16,
-                         int64_t* out_ids, uint16_t* out_weights_bf16, void* workspace, int64_t workspace_bytes,
-                         void* stream) {
+                         const uint64_t* tables, int has_shared, const uint8_t* nan_free, int weight_layout,
+                         uint16_t* out_bf16, int64_t* out_ids, uint16_t* out_weights_bf16, void* workspace,
+                         int64_t workspace_bytes, void* stream) {
   if (!hidden || !router_weight || !tables || !out_bf16) return fail(kNullPointer, "null pointer");
+  if (weight_layout != 0 && weight_layout != 1) return fail(kBadDims, "weight_layout must be 0 or 1");
   int code = check_route(T, H, E, n_group, topk_group, k);
   if (code != kOk) return code;
   if (I <= 0) return fail(kBadDims, "bad dimensions");
@@ -706,6 +708,8 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   const int64_t S = E + (has_shared ? 1 : 0);
   const bool use_mma = g_gemv_impl == 0 && mma_gemv_supported(static_cast<int>(H), static_cast<int>(I)) &&
                        mma_gemv_supported(static_cast<int>(I), static_cast<int>(H));
+  if (weight_layout == 1 && !(use_mma && g_mma_feed == 2))
+    return fail(kUnsupported, "tiled weights need the cp.async warp-MMA GEMV (hidden, intermediate % 128 == 0)");
   const int chunk = use_mma ? 8 : nt;
   BucketArgs ba{};
   ba.keys = l.ids32; ba.rows = nullptr; ba.weights = l.wts; ba.n = static_cast<int>(T * k);
@@ -764,7 +768,7 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   const bool vec = H % 16 == 0 && I % 16 == 0 && aligned16(hidden);
   if (use_mma) {
     code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I, H,
-                                 chunks_ready, nan_free, s);
+                                 chunks_ready, nan_free, s, weight_layout);
   } else {
     code = run_expert_stages(t, hidden, xd, l.m, l.m.y, S, I, H, ceil_div(H, kBlock), ceil_div(I, kBlock), nt, vec, s);
   }
@@ -891,10 +895,25 @@ int moe_b200_stage_timing(int enable) {
   return kOk;
 }
 
+int moe_b200_selected_gemv(void) { return g_gemv_impl != 0 ? g_gemv_impl : (g_mma_feed == 0 ? 3 : g_mma_feed == 1 ? 4 : 0); }
+
 int moe_b200_select_gemv(int impl) {
   if (impl < 0 || impl > 5) return fail(kBadDims, "impl must be 0 to 5");
   g_gemv_impl = impl >= 3 ? 0 : impl;
   g_mma_feed = impl == 3 ? 0 : impl == 4 ? 1 : 2;
+  return kOk;
+}
+
+int64_t moe_fp8_tiled_bytes(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0 || cols % kBlock != 0) return -1;
+  return fp8_tiled_bytes(rows, cols);
+}
+
+int moe_fp8_tile_weights(const uint8_t* weight, uint8_t* tiled, int64_t rows, int64_t cols, void* stream) {
+  if (!weight || !tiled) return fail(kNullPointer, "null pointer");
+  if (rows <= 0 || cols <= 0 || cols % kBlock != 0) return fail(kBadDims, "cols must be a positive multiple of 128");
+  if (!aligned16(weight) || !aligned16(tiled)) return fail(kUnsupported, "weights must be 16-byte aligned");
+  MOE_CUDA(launch_fp8_tile(weight, tiled, rows, cols, as_stream(stream)), "tile weights");
   return kOk;
 }
 

@@ -77,6 +77,7 @@ struct MmaArgs {
   int scale_cols;
   int nanfix;                // decode e4m3 0x7F/0xFF as +0 (the reference's linear semantics)
   const uint8_t* nan_free;   // [segments] or null: 1 = the expert holds no 0x7F/0xFF code (no fix needed)
+  int tiled;                 // cp.async kernel: weights in the fragment-native tiled layout (launch_fp8_tile)
   int ksplit;                // register-fed kernel: k-block ranges per task (1: none)
   float* partial;            // [tasks * ksplit, 32, 8] fp32 fragments when ksplit > 1
   int32_t* counters;         // [tasks] arrival counters: zero on entry, left zero on exit
@@ -93,6 +94,11 @@ cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bou
 // cp.async (fp8_mma.cu); tasks_bound as for launch_mma_gemv.
 int async_gemv_ksplit(int64_t tasks_bound, int K);
 cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream);
+// Fragment-native weight layout for the cp.async kernel: bytes of the tiled
+// copy of a row-major e4m3 [rows, cols] matrix (cols % 128 == 0; rows padded
+// to a multiple of 32 with zeros), and the repacking launch.
+int64_t fp8_tiled_bytes(int64_t rows, int64_t cols);
+cudaError_t launch_fp8_tile(const uint8_t* src, uint8_t* dst, int64_t rows, int64_t cols, cudaStream_t stream);
 // Per-expert flags for MmaArgs::nan_free: flags[s] = 1 when none of the
 // gate / up / down e4m3 weights of expert s (device tables [6][S], absent
 // experts count as clean) is 0x7F or 0xFF.

@@ -316,22 +316,35 @@ __global__ void __launch_bounds__(kMmaCtaWarps * kWarp) mma_gemv_kernel(MmaArgs 
 }
 
 // ---------------------------------------------------------------------------
-// The same tasks with the weights staged through shared memory by cp.async:
+// The same tasks with the operands staged through shared memory by cp.async:
 // every warp owns a ring of kAsyncStages k-blocks; lane l copies its own
-// 8 x 16 bytes of a k-block (the bytes it multiplies) to slots
-// (i * 32 + l) * 16 of a stage and later reads exactly those bytes back, so
-// the ring needs no barrier -- only the lane's own cp.async groups
-// (commit / wait_group).  kAsyncStages - 1 k-blocks of every lane stay in
-// flight without holding registers.  Experts flagged NaN-free skip the
-// 0x7F/0xFF fix-up (a warp-uniform choice per task).
+// 8 x 16 bytes of weights and 4 x 16 bytes of activations of a k-block (the
+// bytes it multiplies) to slots (i * 32 + l) * 16 of a stage and later reads
+// exactly those bytes back, so the ring needs no barrier -- only the lane's
+// own cp.async groups (commit / wait_group).  kAsyncStages - 1 k-blocks of
+// every lane stay in flight without holding registers, and the block scales
+// are loaded one k-block ahead.  Experts flagged NaN-free skip the 0x7F/0xFF
+// fix-up (a warp-uniform choice per task).
 // ---------------------------------------------------------------------------
 constexpr int kAsyncWarps = 4;
-constexpr int kAsyncStages = 4;
-constexpr int kAsyncStageBytes = kWarp * 8 * 16;  // 4 KiB: one k-block of the warp's 32 row streams
+constexpr int kAsyncStages = 3;
+constexpr int kAsyncStageBytes = kWarp * 12 * 16;  // 6 KiB: a k-block of the warp's 32 row streams + its activations
 constexpr int kAsyncSmem = kAsyncWarps * kAsyncStages * kAsyncStageBytes;
+// Fragment-native ("tiled") weight layout: for every 16-row tile and 128-column
+// k-block, 2 KiB holding the 16-byte pieces in the order the lanes take them:
+// piece p (row g + 8 (p / 2), columns 64 (p % 2) + 16 c, lane (g, c)) of all
+// 32 lanes, then the next piece -- so each warp-wide cp.async reads 512
+// contiguous bytes and a warp-task's weights are one contiguous stream per
+// matrix.
+constexpr int kTileKBlockBytes = kWarp * 64;
 
 MOE_D void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+// src_bytes < 16 zero-fills the rest of the 16-byte destination (0: all zeros, nothing read)
+MOE_D void cp_async16_zfill(void* smem, const void* gmem, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
 }
 MOE_D void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
@@ -340,37 +353,44 @@ MOE_D void cp_async_wait() {
 }
 
 // acc += this lane's share of W[k-blocks kb0..kb1) . x for one task
-template <bool FIX>
+// TILED: the weights are in the fragment-native layout of fp8_tile_kernel
+// (tbase[st] = this lane's first piece of k-block 0 of stream st's 16-row
+// tile); otherwise row-major (arow[st][rr] = row g + 8 rr at column 16 c).
+template <bool FIX, bool TILED>
 MOE_D void async_accumulate(float (&acc)[2][4], unsigned char* ring, const uint8_t* const (&arow)[2][2],
-                            const float* const (&srow)[2], const __half* xb, bool bvalid, int kb0, int kb1,
-                            int lane, int c) {
+                            const uint8_t* const (&tbase)[2], const float* const (&srow)[2], const __half* xb,
+                            bool bvalid, int kb0, int kb1, int lane, int c) {
   auto slot = [&](int stage, int i) { return ring + stage * kAsyncStageBytes + (i * kWarp + lane) * 16; };
+  // slots 0-7: this lane's weight pieces (span, stream, row half); 8-11: its
+  // activation pieces (span, half); an absent token row is zero-filled
   auto issue = [&](int kbi) {
     const int stage = (kbi - kb0) % kAsyncStages;
 #pragma unroll
-    for (int sp = 0; sp < 2; ++sp)
+    for (int sp = 0; sp < 2; ++sp) {
 #pragma unroll
       for (int st = 0; st < 2; ++st)
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr)
-          cp_async16(slot(stage, (sp * 2 + st) * 2 + rr), arow[st][rr] + kbi * kBlock + sp * 64);
+          cp_async16(slot(stage, (sp * 2 + st) * 2 + rr),
+                     TILED ? tbase[st] + static_cast<int64_t>(kbi) * kTileKBlockBytes + (rr * 2 + sp) * (kWarp * 16)
+                           : arow[st][rr] + kbi * kBlock + sp * 64);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        cp_async16_zfill(slot(stage, 8 + sp * 2 + h), xb + kbi * kBlock + sp * 64 + h * 8, bvalid ? 16 : 0);
+    }
   };
 #pragma unroll
   for (int j = 0; j < kAsyncStages - 1; ++j) {
     if (kb0 + j < kb1) issue(kb0 + j);
     cp_async_commit();
   }
+  float sc0 = __ldg(srow[0] + kb0), sc1 = __ldg(srow[1] + kb0);
   for (int kbi = kb0; kbi < kb1; ++kbi) {
     if (kbi + kAsyncStages - 1 < kb1) issue(kbi + kAsyncStages - 1);
     cp_async_commit();
-    uint4 b[2][2];
-#pragma unroll
-    for (int sp = 0; sp < 2; ++sp) {
-      const int off = kbi * kBlock + sp * 64;
-      b[sp][0] = bvalid ? __ldg(reinterpret_cast<const uint4*>(xb + off)) : make_uint4(0, 0, 0, 0);
-      b[sp][1] = bvalid ? __ldg(reinterpret_cast<const uint4*>(xb + off + 8)) : make_uint4(0, 0, 0, 0);
-    }
-    const float sc0 = __ldg(srow[0] + kbi), sc1 = __ldg(srow[1] + kbi);
+    // next k-block's scales load while this one is multiplied
+    const int kn = min(kbi + 1, kb1 - 1);
+    const float nsc0 = __ldg(srow[0] + kn), nsc1 = __ldg(srow[1] + kn);
     cp_async_wait<kAsyncStages - 1>();  // this lane's copies of k-block kbi have landed
     const int stage = (kbi - kb0) % kAsyncStages;
     float t[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -382,8 +402,9 @@ MOE_D void async_accumulate(float (&acc)[2][4], unsigned char* ring, const uint8
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr)
           av[st][rr] = *reinterpret_cast<const uint4*>(slot(stage, (sp * 2 + st) * 2 + rr));
-      const uint32_t bw[8] = {b[sp][0].x, b[sp][0].y, b[sp][0].z, b[sp][0].w,
-                              b[sp][1].x, b[sp][1].y, b[sp][1].z, b[sp][1].w};
+      const uint4 b0 = *reinterpret_cast<const uint4*>(slot(stage, 8 + sp * 2));
+      const uint4 b1 = *reinterpret_cast<const uint4*>(slot(stage, 8 + sp * 2 + 1));
+      const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
 #pragma unroll
@@ -404,11 +425,13 @@ MOE_D void async_accumulate(float (&acc)[2][4], unsigned char* ring, const uint8
       acc[0][i] = fmaf(t[0][i], sc0, acc[0][i]);
       acc[1][i] = fmaf(t[1][i], sc1, acc[1][i]);
     }
+    sc0 = nsc0;
+    sc1 = nsc1;
   }
   cp_async_wait<0>();  // nothing of this task in flight before the ring is reused
 }
 
-template <int NS, int EPI>
+template <int NS, int EPI, bool TILED>
 __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(MmaArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
@@ -452,6 +475,12 @@ __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(Mma
       }
       srow[st] = present ? sc + static_cast<int64_t>(min(base, N - 1) / kBlock) * a.scale_cols : nullptr;
     }
+    const uint8_t* tbase[2];
+#pragma unroll
+    for (int st = 0; st < 2; ++st) {
+      const int64_t tile = NS == 2 ? r0 / 16 : r0 / 16 + st;
+      tbase[st] = present ? (st == 0 ? w0 : w1) + tile * 16 * static_cast<int64_t>(K) + lane * 16 : nullptr;
+    }
     const bool bvalid = g < len;
     const int64_t brow = bvalid ? (a.pair_row ? a.pair_row[p0 + g] : static_cast<int64_t>(p0 + g)) : 0;
     const __half* xb = a.x16 + brow * K + 16 * c;
@@ -459,8 +488,8 @@ __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(Mma
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     if (present && kb0 < kb1) {
       const bool fix = a.nanfix && !(a.nan_free && a.nan_free[seg]);
-      if (fix) async_accumulate<true>(acc, ring, arow, srow, xb, bvalid, kb0, kb1, lane, c);
-      else async_accumulate<false>(acc, ring, arow, srow, xb, bvalid, kb0, kb1, lane, c);
+      if (fix) async_accumulate<true, TILED>(acc, ring, arow, tbase, srow, xb, bvalid, kb0, kb1, lane, c);
+      else async_accumulate<false, TILED>(acc, ring, arow, tbase, srow, xb, bvalid, kb0, kb1, lane, c);
     }
 
     if (ksplit > 1) {
@@ -548,6 +577,28 @@ __global__ void nan_free_kernel(const uint64_t* __restrict__ tables, int S, int6
   __syncthreads();
   // flags start at 1 (launcher); any CTA that saw a NaN code clears it
   if (threadIdx.x == 0 && found) flags[s] = 0;
+}
+
+// row-major e4m3 [rows, cols] -> fragment-native tiles (kTileKBlockBytes per
+// 16-row tile and k-block); rows past `rows` (up to a multiple of 32) are zero.
+__global__ void fp8_tile_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t rows,
+                                int64_t cols) {
+  const int64_t nkb = cols / kBlock;
+  const int64_t tiles = ceil_div(rows, 32) * 2;
+  const int64_t pieces = tiles * nkb * kWarp * 4;
+  for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < pieces;
+       q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int piece = static_cast<int>(q % 4);
+    const int lane = static_cast<int>((q / 4) % kWarp);
+    const int64_t kb = (q / (4 * kWarp)) % nkb;
+    const int64_t tile = q / (4 * kWarp * nkb);
+    const int g = lane / 4, c = lane % 4, rr = piece / 2, sp = piece % 2;
+    const int64_t row = tile * 16 + g + 8 * rr;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < rows) v = *reinterpret_cast<const uint4*>(src + row * cols + kb * kBlock + sp * 64 + 16 * c);
+    // piece-major inside the block: one warp-wide 16-byte access per piece is 512 contiguous bytes
+    *reinterpret_cast<uint4*>(dst + (((tile * nkb + kb) * 4 + piece) * kWarp + lane) * 16) = v;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -784,12 +835,14 @@ static int async_ctas_per_sm() {
   static int per_sm = 0;
   if (per_sm == 0) {
     int a = 0, b = 0;
-    cudaFuncSetAttribute(mma_gemv_async_kernel<2, kEpiSwiglu>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAsyncSmem);
-    cudaFuncSetAttribute(mma_gemv_async_kernel<1, kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAsyncSmem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, mma_gemv_async_kernel<2, kEpiSwiglu>, kAsyncWarps * kWarp,
-                                                  kAsyncSmem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, mma_gemv_async_kernel<1, kEpiStore>, kAsyncWarps * kWarp,
-                                                  kAsyncSmem);
+    cudaFuncSetAttribute(mma_gemv_async_kernel<2, kEpiSwiglu, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kAsyncSmem);
+    cudaFuncSetAttribute(mma_gemv_async_kernel<1, kEpiStore, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kAsyncSmem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, mma_gemv_async_kernel<2, kEpiSwiglu, false>,
+                                                  kAsyncWarps * kWarp, kAsyncSmem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, mma_gemv_async_kernel<1, kEpiStore, false>,
+                                                  kAsyncWarps * kWarp, kAsyncSmem);
     per_sm = std::max(1, std::min(a, b));
   }
   return per_sm;
@@ -809,12 +862,25 @@ cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tas
   const int64_t full = static_cast<int64_t>(gemv_grid_ctas()) * async_ctas_per_sm();
   const int64_t need = ceil_div(std::max<int64_t>(1, tasks_bound) * a.ksplit, kAsyncWarps);
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(full, need)));
-  auto kernel = ns == 2 ? mma_gemv_async_kernel<2, kEpiSwiglu> : mma_gemv_async_kernel<1, kEpiStore>;
+  auto kernel = ns == 2 ? (a.tiled ? mma_gemv_async_kernel<2, kEpiSwiglu, true> : mma_gemv_async_kernel<2, kEpiSwiglu, false>)
+                        : (a.tiled ? mma_gemv_async_kernel<1, kEpiStore, true> : mma_gemv_async_kernel<1, kEpiStore, false>);
   if (!((ns == 2 && epi == kEpiSwiglu) || (ns == 1 && epi == kEpiStore))) return cudaErrorInvalidValue;
   // per device context, so set on every launch (a host-side call; graphs do not record it)
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAsyncSmem);
   if (err != cudaSuccess) return err;
   kernel<<<grid, kAsyncWarps * kWarp, kAsyncSmem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+int64_t fp8_tiled_bytes(int64_t rows, int64_t cols) { return ceil_div(rows, 32) * 32 * cols; }
+
+cudaError_t launch_fp8_tile(const uint8_t* src, uint8_t* dst, int64_t rows, int64_t cols, cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0) return cudaSuccess;
+  if (cols % kBlock != 0 || (reinterpret_cast<uintptr_t>(src) & 15u) || (reinterpret_cast<uintptr_t>(dst) & 15u))
+    return cudaErrorInvalidValue;
+  const int64_t pieces = fp8_tiled_bytes(rows, cols) / 16;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(pieces, 256), gemv_grid_ctas() * 16));
+  fp8_tile_kernel<<<grid, 256, 0, stream>>>(src, dst, rows, cols);
   return cudaGetLastError();
 }
 

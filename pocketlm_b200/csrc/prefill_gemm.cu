@@ -1,0 +1,470 @@
+// Grouped FP8-weight GEMM for prefill batches on the 5th-generation tensor
+// cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+// The per-expert products of run_fp8_moe (fp8_source.py:1569-1884) for large
+// token counts: for every expert e with M_e (token, expert) pairs,
+//   gate/up:  act[p, n] = silu(x_p . gate_e[n]) * (x_p . up_e[n])
+//   down:     y[p, h]   = act_p . down_e[h]
+// with 128 x 128 fp32 block scales on the e4m3 weights (fp8_linear.cpp:103-112).
+//
+// Operands.  A is the pairs' activation rows in fp16, each row divided by a
+// power of two (exact; undone in the epilogue), expert-contiguous [P, K] and
+// loaded by TMA (128B swizzle, 128 rows x 64 columns per box).  B is the
+// expert's weights in the fragment-native tiled layout (fp8_mma.cu), brought
+// in by 1-D bulk copies and converted by a converter warpgroup to fp16 with
+// the k-block's scale folded in -- w * s rounded to fp16, a relative error of
+// at most 2^-11 per weight -- written in the same 128B-swizzled K-major
+// layout.  D accumulates in fp32 in tensor memory: M = 128 pairs,
+// N = 128 weight rows (64 gate + 64 up rows for the fused gate/up GEMM),
+// K = 16 per MMA, 64 per pipeline stage.
+//
+// Warp roles (352 threads): warps 0-3 epilogue (TMEM lanes 32w..32w+31),
+// warps 4-7 converter, warp 8 TMA producer, warp 9 MMA issuer, warp 10 TMEM
+// allocator.  A persistent CTA walks tiles (expert m-tile, n-tile) in order;
+// two TMEM accumulators let the epilogue of one tile overlap the next
+// tile's main loop.  Every wait is bounded (2 s of %globaltimer): on
+// expiry the CTA records an error code, every role leaves its loop, the
+// producer waits (bounded) for the copies it issued, and TMEM is freed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "async_copy.cuh"
+#include "common.cuh"
+#include "fp8_gemv.cuh"
+#include "prefill_gemm.cuh"
+
+namespace moe {
+namespace {
+
+constexpr int kBM = 128;              // pairs per tile
+constexpr int kBN = 128;              // weight rows per tile
+constexpr int kBK = 64;               // k per stage (half a scale block)
+constexpr int kStages = 4;
+constexpr int kATileBytes = kBM * kBK * 2;       // 16 KiB, fp16 swizzled
+constexpr int kBTileBytes = kBN * kBK * 2;       // 16 KiB, fp16 swizzled (converted)
+constexpr int kRawBytes = kBN * kBK;             // 8 KiB e4m3, 16 runs of 512 B
+constexpr int kStageBytes = kATileBytes + kBTileBytes + kRawBytes;
+constexpr int kTmemCols = 2 * kBN;               // two fp32 accumulators
+constexpr int kEpiWarps = 4, kConvWarps = 4;
+constexpr int kProducerWarp = 8, kMmaWarp = 9, kAllocWarp = 10;
+constexpr int kThreads = 11 * kWarp;
+constexpr int kCodeWait = 32;
+
+struct Barriers {
+  uint64_t full[kStages];   // producer -> converter: A + raw weights landed (tx bytes)
+  uint64_t conv[kStages];   // converter -> MMA: fp16 weights written (4 arrivals)
+  uint64_t empty[kStages];  // MMA -> producer: the stage's MMAs completed (tcgen05.commit)
+  uint64_t tfull[2];        // MMA -> epilogue: accumulator complete
+  uint64_t tempty[2];       // epilogue -> MMA: accumulator drained (4 arrivals)
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t kSmemBytes = 1024 /* alignment slack */ + static_cast<size_t>(kStages) * kStageBytes +
+                              sizeof(Barriers);
+
+// ---------------------------------------------------------------- PTX
+MOE_D void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)), "r"(ncols)
+               : "memory");
+}
+MOE_D void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+MOE_D void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+MOE_D void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+MOE_D void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+MOE_D void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+MOE_D void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+MOE_D void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+MOE_D void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_addr(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// K-major, 128B-swizzled operand tile: rows of 128 bytes, 8-row atoms 1024 B apart.
+MOE_D uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(16 >> 4) << 16;    // leading byte offset (unused with 128B swizzle)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;  // stride byte offset: next 8-row atom
+  d |= static_cast<uint64_t>(1) << 46;          // descriptor version for tcgen05
+  d |= static_cast<uint64_t>(2) << 61;          // 128B swizzle
+  return d;
+}
+// kind::f16 instruction descriptor: fp32 D, fp16 A and B, both K-major.
+constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+
+// Bounded wait that also gives up when another role aborted.
+MOE_D bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      atomicOr(&g_device_error, kCodeWait);
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+// ------------------------------------------------------------ tile map
+// tile t -> (segment, first pair, pairs in the segment from there, n-tile)
+struct TileRef {
+  int seg, row0, rows, nt;
+};
+MOE_D TileRef tile_at(int64_t t, const int32_t* mprefix, const int32_t* seg_offset, int n_segments, int n_tiles) {
+  const int m = static_cast<int>(t / n_tiles);
+  TileRef r;
+  r.nt = static_cast<int>(t % n_tiles);
+  int lo = 0, hi = n_segments;  // largest s with mprefix[s] <= m
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) / 2;
+    if (mprefix[mid] <= m) lo = mid;
+    else hi = mid;
+  }
+  r.seg = lo;
+  r.row0 = seg_offset[lo] + (m - mprefix[lo]) * kBM;
+  r.rows = min(kBM, seg_offset[lo + 1] - r.row0);
+  return r;
+}
+
+// mprefix[s] = m-tiles of segments before s; mprefix[n_segments] = all of them.
+__global__ void prefill_tiles_kernel(const int32_t* seg_offset, int n_segments, int32_t* mprefix) {
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  int acc = 0;
+  for (int s = 0; s < n_segments; ++s) {
+    mprefix[s] = acc;
+    const int rows = seg_offset[s + 1] - seg_offset[s];
+    acc += (rows + kBM - 1) / kBM;
+  }
+  mprefix[n_segments] = acc;
+}
+
+// A rows of the gate/up GEMM: xa[p] = x16[pair_row[p]], ascale[p] = xscale[pair_row[p]].
+__global__ void gather_rows_kernel(const __half* x16, const float* xscale, const int32_t* pair_row, int64_t P,
+                                   int64_t K, __half* xa, float* ascale) {
+  const int lane = threadIdx.x % kWarp;
+  for (int64_t p = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / kWarp; p < P;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x / kWarp) {
+    const int64_t r = pair_row[p];
+    const uint4* src = reinterpret_cast<const uint4*>(x16 + r * K);
+    uint4* dst = reinterpret_cast<uint4*>(xa + p * K);
+    for (int64_t i = lane; i < K / 8; i += kWarp) dst[i] = __ldg(src + i);
+    if (lane == 0) ascale[p] = xscale[r];
+  }
+}
+
+// --------------------------------------------------------------- kernel
+template <bool GATEUP>
+__global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                                    PrefillArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kStageBytes);
+  auto a_tile = [&](int s) { return smem + s * kStageBytes; };
+  auto b_tile = [&](int s) { return smem + s * kStageBytes + kATileBytes; };
+  auto raw_tile = [&](int s) { return smem + s * kStageBytes + kATileBytes + kBTileBytes; };
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  volatile int* abort = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->conv[s], kConvWarps);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->tfull[i], 1);
+      mbar_init(&bars->tempty[i], kEpiWarps);
+    }
+    bars->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kAllocWarp) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  const int K = a.K, N = a.N;
+  const int n_tiles = GATEUP ? N / (kBN / 2) : N / kBN;
+  const int64_t tiles = static_cast<int64_t>(a.mprefix[a.n_segments]) * n_tiles;
+  const int nkh = K / kBK;  // pipeline stages per tile
+  const int nkb = K / 128;  // k-blocks (scale columns, tiled-layout blocks)
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+        const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
+        const uint8_t* wbase[2];
+        int tile0[2];
+        if (GATEUP) {
+          wbase[0] = reinterpret_cast<const uint8_t*>(a.w0[tr.seg]);
+          wbase[1] = reinterpret_cast<const uint8_t*>(a.w1[tr.seg]);
+          tile0[0] = tile0[1] = tr.nt * 4;  // 64 rows = 4 tiles of 16 in each matrix
+        } else {
+          wbase[0] = wbase[1] = reinterpret_cast<const uint8_t*>(a.w0[tr.seg]);
+          tile0[0] = tr.nt * 8;
+          tile0[1] = tr.nt * 8 + 4;
+        }
+        for (int kh = 0; kh < nkh && !*abort; ++kh, ++it) {
+          const int s = it % kStages;
+          if (it >= kStages && !wait_or_abort(&bars->empty[s], ((it / kStages) - 1) & 1, abort)) break;
+          mbar_arrive_expect_tx(&bars->full[s], kATileBytes + kRawBytes);
+          tma_load_2d(a_tile(s), &tmap_a, kh * kBK, tr.row0, &bars->full[s]);
+          const int kb = kh / 2, sp = kh % 2;
+          // 8 row tiles of 16 (4 from each half) x rows g / g + 8: 16 runs of 512 B
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int half = i / 4;
+            const uint8_t* blk =
+                wbase[half] + (static_cast<int64_t>(tile0[half] + i % 4) * nkb + kb) * 2048;
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr)
+              bulk_copy_g2s(raw_tile(s) + (i * 2 + rr) * 512, blk + (rr * 2 + sp) * 512, 512, &bars->full[s]);
+          }
+        }
+      }
+      // drain: every copy issued must land before the CTA may exit
+      for (uint32_t j = it > kStages ? it - kStages : 0; j < it; ++j)
+        mbar_wait(&bars->full[j % kStages], (j / kStages) & 1, kCodeWait);
+    }
+  } else if (warp >= kEpiWarps && warp < kEpiWarps + kConvWarps) {
+    // converter: e4m3 runs -> fp16 * block scale, 128B-swizzled K-major
+    const int ct = threadIdx.x - kEpiWarps * kWarp;  // 0..127
+    uint32_t it = 0;
+    for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+      const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
+      const float* sb[2];
+      int srow[2];
+      if (GATEUP) {
+        sb[0] = reinterpret_cast<const float*>(a.s0[tr.seg]);
+        sb[1] = reinterpret_cast<const float*>(a.s1[tr.seg]);
+        srow[0] = srow[1] = (tr.nt * 64) / 128;
+      } else {
+        sb[0] = sb[1] = reinterpret_cast<const float*>(a.s0[tr.seg]);
+        srow[0] = srow[1] = tr.nt;  // 128 rows = one scale row
+      }
+      for (int kh = 0; kh < nkh; ++kh, ++it) {
+        const int s = it % kStages;
+        if (!wait_or_abort(&bars->full[s], (it / kStages) & 1, abort)) break;
+        const int kb = kh / 2;
+        const float sc[2] = {__ldg(sb[0] + srow[0] * a.scale_cols + kb), __ldg(sb[1] + srow[1] * a.scale_cols + kb)};
+        const unsigned char* raw = raw_tile(s);
+        unsigned char* bt = b_tile(s);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int u = ct + q * 128;        // 16-byte unit: run u / 32, lane u % 32
+          const int run = u / kWarp, ul = u % kWarp;
+          const int i = run / 2, rr = run % 2;
+          const int g = ul / 4, c = ul % 4;
+          const int n = 16 * i + g + 8 * rr;  // tile row 0..127
+          uint4 v = *reinterpret_cast<const uint4*>(raw + u * 16);
+          const float scale = sc[i / 4];
+          if (a.nanfix) {
+            v.x = e4m3x4_nan_to_zero(v.x);
+            v.y = e4m3x4_nan_to_zero(v.y);
+            v.z = e4m3x4_nan_to_zero(v.z);
+            v.w = e4m3x4_nan_to_zero(v.w);
+          }
+          const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+          uint32_t h[8];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const float2 f = e4m3x2_to_float2(static_cast<uint16_t>(words[w] >> (16 * half)));
+              const __half2 hv = __floats2half2_rn(f.x * scale, f.y * scale);
+              h[w * 2 + half] = *reinterpret_cast<const uint32_t*>(&hv);
+            }
+          }
+          // k 16c .. 16c + 15 of this stage = 16-byte chunks 2c, 2c + 1 of row n
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int chunk = 2 * c + j;
+            unsigned char* dst = bt + (n / 8) * 1024 + (n % 8) * 128 + ((chunk ^ (n % 8)) * 16);
+            *reinterpret_cast<uint4*>(dst) = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+          }
+        }
+        fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor core (async proxy)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->conv[s]);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      uint32_t it = 0, ti = 0;
+      for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x, ++ti) {
+        const int acc = ti % 2;
+        if (ti >= 2 && !wait_or_abort(&bars->tempty[acc], ((ti / 2) - 1) & 1, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * kBN;
+        bool ok = true;
+        for (int kh = 0; kh < nkh; ++kh, ++it) {
+          const int s = it % kStages;
+          if (!wait_or_abort(&bars->conv[s], (it / kStages) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_addr(a_tile(s)), sbt = smem_addr(b_tile(s));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_f16(d_tmem, sw128_desc(sa + k * 32), sw128_desc(sbt + k * 32), kIdesc, (kh | k) != 0);
+          umma_commit(&bars->empty[s]);  // frees the stage when these MMAs complete
+        }
+        if (!ok) break;
+        umma_commit(&bars->tfull[acc]);
+      }
+    }
+  } else if (warp < kEpiWarps) {
+    uint32_t ti = 0;
+    const int row_in_tile = warp * kWarp + lane;  // TMEM lane
+    for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x, ++ti) {
+      const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
+      const int acc = ti % 2;
+      if (!wait_or_abort(&bars->tfull[acc], (ti / 2) & 1, abort)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + acc * kBN + (static_cast<uint32_t>(warp * kWarp) << 16);
+      const bool valid = row_in_tile < tr.rows;
+      const int64_t p = tr.row0 + row_in_tile;
+      const float xs = valid ? a.ascale[p] : 0.0f;
+      if (GATEUP) {
+        float* out = a.out + p * N + tr.nt * 64;
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 16) {
+          float g[16], u[16];
+          tmem_ld16(taddr + c0, g);
+          tmem_ld16(taddr + 64 + c0, u);
+          if (valid) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              float4 o;
+              float* op = &o.x;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float gv = g[j + q] * xs, uv = u[j + q] * xs;
+                op[q] = gv / (1.0f + expf(-gv)) * uv;
+              }
+              *reinterpret_cast<float4*>(out + c0 + j) = o;
+            }
+          }
+        }
+      } else {
+        float* out = a.out + p * N + tr.nt * kBN;
+#pragma unroll
+        for (int c0 = 0; c0 < kBN; c0 += 16) {
+          float d[16];
+          tmem_ld16(taddr + c0, d);
+          if (valid) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<float4*>(out + c0 + j) =
+                  make_float4(d[j] * xs, d[j + 1] * xs, d[j + 2] * xs, d[j + 3] * xs);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->tempty[acc]);
+    }
+  }
+
+  // all roles done: the last tcgen05 ops are complete once their commits
+  // arrived (the epilogue waited for every tfull it consumed)
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kAllocWarp) tmem_dealloc(tmem, kTmemCols);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+size_t prefill_smem_bytes() { return kSmemBytes; }
+
+bool prefill_supported(int64_t K, int64_t N, bool gateup) {
+  return K > 0 && N > 0 && K % 128 == 0 && (gateup ? N % 64 == 0 : N % kBN == 0);
+}
+
+cudaError_t launch_prefill_tiles(const int32_t* seg_offset, int n_segments, int32_t* mprefix, cudaStream_t stream) {
+  prefill_tiles_kernel<<<1, 32, 0, stream>>>(seg_offset, n_segments, mprefix);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const __half* x16, const float* xscale, const int32_t* pair_row, int64_t P, int64_t K,
+                               __half* xa, float* ascale, cudaStream_t stream) {
+  if (P <= 0) return cudaSuccess;
+  if (K % 8 != 0) return cudaErrorInvalidValue;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(P * kWarp, 256), gemv_grid_ctas() * 16));
+  gather_rows_kernel<<<grid, 256, 0, stream>>>(x16, xscale, pair_row, P, K, xa, ascale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_gemm(const PrefillArgs& a, bool gateup, int64_t max_tiles, cudaStream_t stream) {
+  if (!prefill_supported(a.K, a.N, gateup) || a.rows_a <= 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(a.a16) & 15u) != 0) return cudaErrorInvalidValue;
+  auto encode = encode_fn();
+  if (!encode) return cudaErrorNotSupported;
+  CUtensorMap tmap;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.K), static_cast<cuuint64_t>(a.rows_a)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.K) * 2};
+  const cuuint32_t box[2] = {kBK, kBM};
+  const cuuint32_t estr[2] = {1, 1};
+  if (encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(a.a16), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  auto kernel = gateup ? prefill_gemm_kernel<true> : prefill_gemm_kernel<false>;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+  if (err != cudaSuccess) return err;
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(gemv_grid_ctas(), max_tiles)));
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmap, a);
+  return cudaGetLastError();
+}
+
+int read_and_clear_prefill_device_error(cudaStream_t stream) { return read_and_clear_local_error(stream); }
+
+}  // namespace moe

@@ -94,7 +94,9 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
                         _P, _P, _P, _P, _I64, _P], _INT),
     "moe_route_topk_workspace_bytes": ([_I64, _I64], _I64),
     "moe_ds_moe_layer_fp8": ([_P, _INT, _I64, _I64, _I64, _P, _INT, _P, _I64, _I64, _I64, _I64, _INT, _F32, _P,
-                              _INT, _P, _P, _P, _P, _P, _I64, _P], _INT),
+                              _INT, _P, _INT, _P, _P, _P, _P, _I64, _P], _INT),
+    "moe_fp8_tiled_bytes": ([_I64, _I64], _I64),
+    "moe_fp8_tile_weights": ([_P, _P, _I64, _I64, _P], _INT),
     "moe_fp8_nan_free_flags": ([_P, _I64, _I64, _I64, _P, _P], _INT),
     "moe_ds_moe_layer_workspace_bytes": ([_I64] * 5 + [_INT], _I64),
     "moe_ds_session_create": ([_I64] * 4, _P),
@@ -124,6 +126,7 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_b200_stage_timing": ([_INT], _INT),
     "moe_b200_stage_times": ([_P, _INT], _INT),
     "moe_b200_select_gemv": ([_INT], _INT),
+    "moe_b200_selected_gemv": ([], _INT),
     "moe_b200_device_error": ([_P], _INT),
 }
 

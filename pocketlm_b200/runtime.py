@@ -60,11 +60,16 @@ class DsMoELayerGPU:
     up, up scale, down, down scale; the shared expert last) that
     moe_ds_moe_layer_fp8 walks, and a reusable workspace."""
 
-    def __init__(self, layer: Fp8MoELayer, layer_index: int = 0, *, allow_partial: bool = False):
+    def __init__(self, layer: Fp8MoELayer, layer_index: int = 0, *, allow_partial: bool = False,
+                 tiled: bool = True):
         """allow_partial: accept a layer holding only some experts; the absent
         ones get null table entries, which the kernels skip (they contribute
         nothing), so outputs are only right for tokens routed to resident
-        experts.  For small profiling cases; a full layer is the product path."""
+        experts.  For small profiling cases; a full layer is the product path.
+
+        tiled: also keep the expert weights in the decode GEMV's
+        fragment-native layout (moe_fp8_tile_weights; same bytes, one
+        contiguous stream per warp), used whenever the default GEMV runs."""
         if not layer.is_full and not allow_partial:
             raise ValueError("the fused layer path needs every expert resident (a full layer)")
         if layer.device.type != "cuda":
@@ -85,6 +90,28 @@ class DsMoELayerGPU:
         native._check(native.load_library().moe_fp8_nan_free_flags(
             native._ptr(self.tables), n, self.cfg.inter, self.cfg.hidden, native._ptr(self.nan_free),
             native._stream()), "moe_fp8_nan_free_flags")
+        self.tables_tiled = None
+        cfg = self.cfg
+        lib = native.load_library()
+        if tiled and cfg.hidden % 128 == 0 and cfg.inter % 128 == 0:
+            tb13 = int(lib.moe_fp8_tiled_bytes(cfg.inter, cfg.hidden))
+            tb2 = int(lib.moe_fp8_tiled_bytes(cfg.hidden, cfg.inter))
+            self._tiled13 = torch.empty((n, 2, tb13), dtype=torch.uint8, device=layer.device)
+            self._tiled2 = torch.empty((n, tb2), dtype=torch.uint8, device=layer.device)
+            tcols = [list(c) for c in cols]
+            for e in range(n):
+                if cols[0][e] == 0:
+                    continue
+                g, _gs, u, _us, d, _ds = layer.expert(e)
+                for src, dst, rows, k in ((g, self._tiled13[e, 0], cfg.inter, cfg.hidden),
+                                          (u, self._tiled13[e, 1], cfg.inter, cfg.hidden),
+                                          (d, self._tiled2[e], cfg.hidden, cfg.inter)):
+                    native._check(lib.moe_fp8_tile_weights(native._ptr(src), native._ptr(dst), rows, k,
+                                                           native._stream()), "moe_fp8_tile_weights")
+                tcols[0][e] = int(self._tiled13[e, 0].data_ptr())
+                tcols[2][e] = int(self._tiled13[e, 1].data_ptr())
+                tcols[4][e] = int(self._tiled2[e].data_ptr())
+            self.tables_tiled = torch.tensor(tcols, dtype=torch.int64, device=layer.device)
         self._workspace = torch.empty((0,), dtype=torch.uint8, device=layer.device)
 
     def workspace_for(self, tokens: int) -> torch.Tensor:
@@ -114,11 +141,15 @@ class DsMoELayerGPU:
         ws = self.workspace_for(T)
         rw = self.layer.router_weight
         rdt = {torch.float32: native.DTYPE_F32, torch.bfloat16: native.DTYPE_BF16, torch.float16: native.DTYPE_F16}
-        code = native.load_library().moe_ds_moe_layer_fp8(
+        lib = native.load_library()
+        # the tiled copy serves the default GEMV; the other selections read row-major weights
+        layout = 1 if self.tables_tiled is not None and lib.moe_b200_selected_gemv() == 0 else 0
+        tables = self.tables_tiled if layout else self.tables
+        code = lib.moe_ds_moe_layer_fp8(
             native._ptr(x), native.DTYPE_BF16 if x.dtype == torch.bfloat16 else native.DTYPE_F32, T, cfg.hidden,
             cfg.inter, native._ptr(rw), rdt[rw.dtype], native._ptr(self.layer.bias), cfg.n_routed, cfg.n_group,
             cfg.topk_group, cfg.top_k, 1 if cfg.scoring_func == "softmax" else 0, float(cfg.route_scale),
-            native._ptr(self.tables), 1, native._ptr(self.nan_free), native._ptr(out), native._ptr(ids),
+            native._ptr(tables), 1, native._ptr(self.nan_free), layout, native._ptr(out), native._ptr(ids),
             native._ptr(weights),
             native._ptr(ws), ws.numel(), native._stream())
         native._check(code, "moe_ds_moe_layer_fp8")

@@ -158,6 +158,21 @@ def test_nan_codes_decode_as_zero_on_the_layer_path(cuda_device):
     assert rel_l2(out, expected) <= REL_L2_GATE and cos_dist(out, expected) <= COS_GATE
 
 
+@pytest.mark.parametrize("cfg,tokens", [(synth.C1_TINY, 9), (synth.C2_DSV3, 4)])
+def test_tiled_weights_give_the_same_bits(cuda_device, cfg, tokens):
+    """The fragment-native weight copy only reorders bytes: the layer's
+    output is bit-identical to the row-major run of the same GEMV (and the
+    other selections read the row-major copy)."""
+    layer = synth.make_fp8_layer(cfg, seed=21, device="cuda")
+    x = synth.make_hidden(tokens, cfg.hidden, seed=22, device="cuda")
+    tiled = DsMoELayerGPU(layer)
+    assert tiled.tables_tiled is not None
+    a = tiled.forward(x).clone()
+    del tiled
+    b = DsMoELayerGPU(layer, tiled=False).forward(x)
+    assert torch.equal(a, b)
+
+
 def test_dsv3_router_result_api(cuda_device):
     cfg = synth.C2_DSV3
     layer = synth.make_fp8_layer(cfg, seed=5, device="cuda", experts=[])
