@@ -1,0 +1,39 @@
+// Prefill grouped GEMM on tcgen05 (prefill_gemm.cu).
+#pragma once
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace moe {
+
+struct PrefillArgs {
+  // per-segment device tables: weights in the fragment-native tiled layout
+  // (launch_fp8_tile) and fp32 block scales [ceil(N/128), scale_cols]
+  const uint64_t* w0;      // gate (gate/up GEMM) or down
+  const uint64_t* s0;
+  const uint64_t* w1;      // up (gate/up GEMM only)
+  const uint64_t* s1;
+  const __half* a16;       // [rows_a, K] pair-ordered activations / ascale
+  const float* ascale;     // [rows_a] power-of-two row scales
+  int64_t rows_a;          // pairs (TMA bound; rows past it read as zero)
+  const int32_t* seg_offset;  // [n_segments + 1] pair ranges per expert
+  const int32_t* mprefix;     // [n_segments + 1] from launch_prefill_tiles
+  int n_segments;
+  float* out;              // [rows_a, N] fp32 (gate/up: SwiGLU activations)
+  int N;                   // output columns (gate/up: intermediate size)
+  int K;
+  int scale_cols;          // ceil(K / 128)
+  int nanfix;              // decode e4m3 0x7F / 0xFF as +0
+};
+
+size_t prefill_smem_bytes();
+// K % 128 == 0; N % 64 (gate/up) or % 128 (down) == 0.
+bool prefill_supported(int64_t K, int64_t N, bool gateup);
+cudaError_t launch_prefill_tiles(const int32_t* seg_offset, int n_segments, int32_t* mprefix, cudaStream_t stream);
+cudaError_t launch_gather_rows(const __half* x16, const float* xscale, const int32_t* pair_row, int64_t P, int64_t K,
+                               __half* xa, float* ascale, cudaStream_t stream);
+// max_tiles: an upper bound on the tiles (grid size); the kernel reads the real count.
+cudaError_t launch_prefill_gemm(const PrefillArgs& a, bool gateup, int64_t max_tiles, cudaStream_t stream);
+int read_and_clear_prefill_device_error(cudaStream_t stream);
+
+}  // namespace moe
