@@ -406,7 +406,8 @@ int moe_b200_selected_gemv(void);
 
 /* Device error word (no reference counterpart): nonzero when a bounded wait
  * inside a kernel gave up (1: producer, 2: consumer, 4: drain, 8: misaligned
- * weights refused by the streaming kernel, 16: warp-MMA ring).  Synchronises
+ * weights refused by the streaming kernel, 16: warp-MMA ring, 32: prefill
+ * tensor-core GEMM pipeline).  Synchronises
  * `stream`, returns the word (-1 if it cannot be read) and clears it. */
 int moe_b200_device_error(void* stream);
 

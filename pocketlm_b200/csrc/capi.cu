@@ -13,6 +13,7 @@
 #include "dispatch.cuh"
 #include "fp8_gemv.cuh"
 #include "plan.cuh"
+#include "prefill_gemm.cuh"
 #include "route_host.cuh"
 #include "router.cuh"
 #include "status.cuh"
@@ -593,7 +594,18 @@ struct LayerPlan {
   float* partial;
   int32_t* counters;       // [tasks1] gate/up then [tasks2] down (only the split stages)
   int64_t n_counters;
+  // prefill (tcgen05 grouped GEMM): pair-ordered fp16 activations, their
+  // scales, and the per-expert m-tile prefix
+  __half* a16;
+  float* a16scale;
+  int32_t* mprefix;
 };
+
+// Token counts from which the whole-layer call runs the prefill GEMM (when
+// the weights are tiled and the shapes allow): from ~16 pairs per expert on,
+// one 128-row tile of tensor-core work beats re-streaming the weights per
+// chunk of 8 pairs.
+constexpr int64_t kPrefillMinTokens = 512;
 
 static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, int shared, int nt,
                             bool router = true) {
@@ -625,7 +637,46 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
   l.partial = p.take<float>(part * frag);
   l.n_counters = l.tasks1 + l.tasks2;
   l.counters = p.take<int32_t>(l.n_counters);
+  if (router && T >= kPrefillMinTokens) {
+    l.a16 = p.take<__half>(pairs * H);
+    l.a16scale = p.take<float>(pairs);
+    l.mprefix = p.take<int32_t>(E + 2);
+  }
   return l;
+}
+
+// The expert stages on the tcgen05 grouped GEMM (tiled weights): gather the
+// pairs' fp16 rows, gate/up + SwiGLU, stage the activations, down.
+static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16, const LayerPlan& l, int64_t T,
+                                     int64_t pairs, int64_t n_segments, int64_t I, int64_t H, cudaStream_t s) {
+  const MlpScratch& m = l.m;
+  MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.x16, l.xscale, nullptr,
+                              0, s),
+           "stage x");
+  MOE_CUDA(launch_gather_rows(l.x16, l.xscale, m.pair_row, pairs, H, l.a16, l.a16scale, s), "gather pairs");
+  MOE_CUDA(launch_prefill_tiles(m.seg_offset, static_cast<int>(n_segments), l.mprefix, s), "tile map");
+  stage_mark(s);
+  const int64_t mtiles_bound = pairs / 128 + n_segments;
+  PrefillArgs g1{};
+  g1.w0 = t.gw; g1.s0 = t.gs; g1.w1 = t.uw; g1.s1 = t.us;
+  g1.a16 = l.a16; g1.ascale = l.a16scale; g1.rows_a = pairs;
+  g1.seg_offset = m.seg_offset; g1.mprefix = l.mprefix; g1.n_segments = static_cast<int>(n_segments);
+  g1.out = m.act; g1.N = static_cast<int>(I); g1.K = static_cast<int>(H);
+  g1.scale_cols = static_cast<int>(ceil_div(H, kBlock)); g1.nanfix = 1;
+  MOE_CUDA(launch_prefill_gemm(g1, true, mtiles_bound * (I / 64), s), "gate/up GEMM");
+  stage_mark(s);
+  MOE_CUDA(launch_rows_to_f16(m.act, false, static_cast<int>(pairs), static_cast<int>(I), nullptr, l.act16, l.ascale,
+                              nullptr, 0, s),
+           "stage activations");
+  stage_mark(s);
+  PrefillArgs g2 = g1;
+  g2.w0 = t.dw; g2.s0 = t.ds; g2.w1 = nullptr; g2.s1 = nullptr;
+  g2.a16 = l.act16; g2.ascale = l.ascale;
+  g2.out = m.y; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
+  g2.scale_cols = static_cast<int>(ceil_div(I, kBlock));
+  MOE_CUDA(launch_prefill_gemm(g2, false, mtiles_bound * (H / 128), s), "down GEMM");
+  stage_mark(s);
+  return kOk;
 }
 
 // The expert stages on the warp-MMA kernel: x and the SwiGLU activations are
@@ -766,7 +817,12 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   // 3. experts
   Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
   const bool vec = H % 16 == 0 && I % 16 == 0 && aligned16(hidden);
-  if (use_mma) {
+  const bool prefill = weight_layout == 1 && T >= kPrefillMinTokens && l.a16 != nullptr &&
+                       prefill_supported(H, I, true) && prefill_supported(I, H, false);
+  if (prefill) {
+    code = run_expert_stages_prefill(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I,
+                                     H, s);
+  } else if (use_mma) {
     code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I, H,
                                  chunks_ready, nan_free, s, weight_layout);
   } else {
@@ -930,7 +986,8 @@ int moe_fp8_nan_free_flags(const uint64_t* tables, int64_t num_experts, int64_t 
 int moe_b200_device_error(void* stream) {
   const int a = read_and_clear_device_error(as_stream(stream));
   const int b = read_and_clear_mma_device_error(as_stream(stream));
-  return (a < 0 || b < 0) ? -1 : (a | b);
+  const int c = read_and_clear_prefill_device_error(as_stream(stream));
+  return (a < 0 || b < 0 || c < 0) ? -1 : (a | b | c);
 }
 
 int moe_b200_stage_times(float* ms, int max_n) {

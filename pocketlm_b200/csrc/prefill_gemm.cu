@@ -59,6 +59,7 @@ struct Barriers {
   uint64_t empty[kStages];  // MMA -> producer: the stage's MMAs completed (tcgen05.commit)
   uint64_t tfull[2];        // MMA -> epilogue: accumulator complete
   uint64_t tempty[2];       // epilogue -> MMA: accumulator drained (4 arrivals)
+  uint64_t drain;           // MMA issuer's last commit: all of its MMAs complete
   uint32_t tmem_base;
   int abort;
 };
@@ -204,6 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       mbar_init(&bars->tfull[i], 1);
       mbar_init(&bars->tempty[i], kEpiWarps);
     }
+    mbar_init(&bars->drain, 1);
     bars->abort = 0;
     fence_barrier_init();
   }
@@ -333,7 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         bool ok = true;
         for (int kh = 0; kh < nkh; ++kh, ++it) {
           const int s = it % kStages;
-          if (!wait_or_abort(&bars->conv[s], (it / kStages) & 1, abort)) {
+          // the A tile (TMA) and the converted weights of this stage have landed
+          if (!wait_or_abort(&bars->full[s], (it / kStages) & 1, abort) ||
+              !wait_or_abort(&bars->conv[s], (it / kStages) & 1, abort)) {
             ok = false;
             break;
           }
@@ -347,6 +351,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         if (!ok) break;
         umma_commit(&bars->tfull[acc]);
       }
+      // every MMA this thread issued has completed before TMEM is released
+      umma_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, kCodeWait);
     }
   } else if (warp < kEpiWarps) {
     uint32_t ti = 0;
@@ -401,8 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
     }
   }
 
-  // all roles done: the last tcgen05 ops are complete once their commits
-  // arrived (the epilogue waited for every tfull it consumed)
+  // all roles done; the MMA issuer saw its last commit arrive (drain)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

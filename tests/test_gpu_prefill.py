@@ -1,0 +1,72 @@
+"""Prefill-sized batches (>= 512 tokens) on the tcgen05 grouped GEMM
+(prefill_gemm.cu) against the oracle's run_fp8_moe flow and against the
+decode GEMV path on the same layer.
+
+The prefill GEMM folds each 128 x 128 block scale into the weights as it
+converts them to fp16 (w * s rounded to fp16), so it agrees with the exact
+GEMV path to a few parts in 1e4 rather than bit for bit."""
+
+import pytest
+import torch
+
+import oracle
+from pocketlm_b200 import native, synth
+from pocketlm_b200.runtime import DsMoELayerGPU
+from tests.parity import COS_GATE, REL_L2_GATE, cos_dist, id_mismatches, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+C_MID = synth.DsMoEConfig("mid", hidden=1024, inter=512, n_routed=32, top_k=4, n_group=4, topk_group=2,
+                          route_scale=2.5)
+
+
+@pytest.fixture(autouse=True)
+def _clean_error_word():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    lib = native.load_library()
+    lib.moe_b200_select_gemv(0)
+    yield
+    torch.cuda.synchronize()
+    assert lib.moe_b200_device_error(None) == 0, "a bounded wait inside a kernel gave up"
+
+
+def _run(cfg, tokens, seed, bias="uniform"):
+    layer = synth.make_fp8_layer(cfg, seed=seed, device="cuda", bias_kind=bias)
+    x = synth.make_hidden(tokens, cfg.hidden, seed=seed + 1, device="cuda")
+    gpu = DsMoELayerGPU(layer)
+    ids = torch.empty((tokens, cfg.top_k), dtype=torch.int64, device="cuda")
+    out = gpu.forward(x, ids=ids).clone()
+    gemv = DsMoELayerGPU(layer, tiled=False).forward(x).clone()  # row-major weights: the decode GEMV
+    torch.cuda.synchronize()
+    return layer, x, out, ids, gemv
+
+
+@pytest.mark.parametrize("cfg,tokens", [(synth.C1_TINY, 512), (synth.C1_TINY, 2048), (C_MID, 1024)])
+def test_prefill_matches_oracle_and_gemv(cuda_device, cfg, tokens):
+    layer, x, out, ids, gemv = _run(cfg, tokens, seed=40 + tokens)
+    assert rel_l2(out, gemv) <= 2e-3 and cos_dist(out, gemv) <= 1e-5
+    expected, route = oracle.ds_moe_layer(x.cpu(), layer)
+    bad, excused = id_mismatches(ids, route)
+    assert bad == excused
+    assert rel_l2(out, expected) <= REL_L2_GATE and cos_dist(out, expected) <= COS_GATE
+
+
+def test_prefill_zipf_routing_uneven_experts(cuda_device):
+    """Zipf-biased routing (config 3's distribution): a few experts take most
+    pairs (many m-tiles), others none (empty segments)."""
+    layer, x, out, ids, gemv = _run(C_MID, 1536, seed=77, bias="zipf")
+    counts = torch.bincount(ids.reshape(-1).cpu(), minlength=C_MID.n_routed)
+    assert counts.max() > 4 * counts.float().mean()
+    assert rel_l2(out, gemv) <= 2e-3
+
+
+def test_prefill_dsv3_shape(cuda_device):
+    cfg = synth.C2_DSV3
+    layer, x, out, ids, gemv = _run(cfg, 512, seed=91)
+    assert rel_l2(out, gemv) <= 2e-3 and cos_dist(out, gemv) <= 1e-5
+    n = 48  # the oracle on a slice of the batch: every token is computed independently
+    expected, route = oracle.ds_moe_layer(x[:n].cpu(), layer)
+    bad, excused = id_mismatches(ids[:n], route)
+    assert bad == excused
+    assert rel_l2(out[:n], expected) <= REL_L2_GATE and cos_dist(out[:n], expected) <= COS_GATE
