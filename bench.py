@@ -293,6 +293,12 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                 "gateup_gbs": (b["gateup"] / (gateup_ms / 1e3) / 1e9) if gateup_ms else None,
                 "down_gbs": (b["down"] / (down_ms / 1e3) / 1e9) if down_ms else None,
             }
+        prefill = {}
+        if args.prefill_tokens != "none":
+            del gpu_layer, layer, graphed
+            torch.cuda.empty_cache()
+            prefill = run_prefill(args, dev, flush, peaks,
+                                  [int(v) for v in args.prefill_tokens.split(",") if v])
     clock_info = clocks.summary()
     if rank != 0:
         return None
@@ -331,7 +337,52 @@ def run_ours(args, rank: int, world: int) -> dict | None:
         "clocks": clock_info,
         "sweep": {str(T): {k: v for k, v in r.items() if k != "stage_ms"} | {"stage_ms": r["stage_ms"]}
                   for T, r in sorted(results.items())},
+        "prefill": prefill,
     }
+
+
+def run_prefill(args, dev, flush, peaks, token_list) -> dict:
+    """Config 3 on one GPU: the DS-V3 layer with the Zipf-skewed router bias,
+    prefill batches on the tcgen05 grouped GEMM (prefill_gemm.cu).  Each step
+    is one eager layer forward (7 + 4 launches; launch cost is negligible at
+    these sizes), CUDA-event timed after warm-up with an L2 flush between
+    steps.  FLOPs are the layer's algorithmic ones: T * (k + 1) * 3 * 2 * H * I
+    for the experts + T * 2 * H * E for the router."""
+    from pocketlm_b200 import synth
+    from pocketlm_b200.runtime import DsMoELayerGPU
+
+    cfg = synth.C2_DSV3
+    layer = synth.make_fp8_layer(cfg, seed=args.seed + 1, device=dev, bias_kind="zipf")
+    gpu_layer = DsMoELayerGPU(layer)
+    bf16_peak = peaks.get("bf16_tflops", 1590.0)
+    out = {}
+    for T in token_list:
+        x = synth.make_hidden(T, cfg.hidden, seed=args.seed + T, device=dev)
+        ids = torch.empty((T, cfg.top_k), dtype=torch.int64, device=dev)
+        gpu_layer.forward(x, ids=ids)
+        torch.cuda.synchronize()
+        steps = max(3, min(args.steps, 10))
+        ms = statistics.mean(time_steps(lambda: gpu_layer.forward(x), steps, args.warmup, flush))
+        stages = stage_times(gpu_layer, x, 3, flush)
+        flops = T * (cfg.top_k + 1) * 3 * 2 * cfg.hidden * cfg.inter + T * 2 * cfg.hidden * cfg.n_routed
+        pairs = T * (cfg.top_k + 1)
+        gu_flops = pairs * 2 * 2 * cfg.hidden * cfg.inter
+        gu_ms = stages[1] if len(stages) > 1 else None
+        counts = torch.bincount(ids.reshape(-1), minlength=cfg.n_routed)
+        out[str(T)] = {
+            "tokens": T, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
+            "tflops": flops / (ms / 1e3) / 1e12,
+            "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / bf16_peak,
+            "frac_of_fp8_nominal": flops / (ms / 1e3) / 1e12 / 4500.0,
+            "gateup_tflops": (gu_flops / (gu_ms / 1e3) / 1e12) if gu_ms else None,
+            "stage_ms": stages, "max_pairs_per_expert": int(counts.max()),
+            "mma_kind": "tcgen05.mma kind::f16 (fp16 A/B, fp32 accumulate in TMEM)",
+        }
+        del x, ids
+    del gpu_layer, layer
+    torch.cuda.empty_cache()
+    return {"workload": "c3-dsv3-prefill-zipf", "peak_bf16_tflops": bf16_peak,
+            "peak_source": f"{peaks['source']} bf16_tflops", "sweep": out}
 
 
 def run_ours_ep(args, rank: int, world: int) -> dict | None:
@@ -452,6 +503,25 @@ def run_profile_case(args) -> dict:
             "launches": args.warmup + args.steps}
 
 
+def run_profile_prefill(args) -> dict:
+    """A small prefill case for ncu: DS-V3 expert shapes (hidden 7168,
+    intermediate 2048, top-8) with 32 routed experts + shared (about 2.9 GB
+    with the tiled copy), --tokens tokens on the tcgen05 GEMM."""
+    from pocketlm_b200 import native, synth
+    from pocketlm_b200.runtime import DsMoELayerGPU
+
+    dev = torch.device("cuda", 0)
+    native.load_library()
+    cfg = synth.DsMoEConfig("c3-profile", hidden=7168, inter=2048, n_routed=32, top_k=8, n_group=8, topk_group=4,
+                            route_scale=2.5)
+    layer = DsMoELayerGPU(synth.make_fp8_layer(cfg, seed=args.seed, device=dev, bias_kind="zipf"))
+    x = synth.make_hidden(args.tokens, cfg.hidden, seed=args.seed + 1, device=dev)
+    for _ in range(args.warmup + args.steps):
+        layer.forward(x)
+    torch.cuda.synchronize()
+    return {"profile_case": f"c3-shape-32-experts-T{args.tokens}", "launches": args.warmup + args.steps}
+
+
 def run_reference(args, rank: int, world: int) -> dict | None:
     if rank != 0:
         return None
@@ -493,8 +563,12 @@ def main() -> None:
                         help="comma-separated extra batch sizes measured after --tokens, or 'none'")
     parser.add_argument("--gemv", choices=list(GEMV_IMPLS), default="auto",
                         help="expert GEMV kernel (moe_b200_select_gemv); auto is the product default")
+    parser.add_argument("--prefill-tokens", default="2048,8192,16384",
+                        help="config-3 prefill batch sizes measured after the decode sweep, or 'none'")
     parser.add_argument("--profile", action="store_true",
                         help="run the small ncu case (selected experts only) instead of the benchmark")
+    parser.add_argument("--profile-prefill", action="store_true",
+                        help="run the small prefill ncu case (DS-V3 expert shapes, 32 experts) instead")
     parser.add_argument("--profile-no-experts", action="store_true",
                         help="with --profile: materialise no expert (for captures of the routing kernels)")
     args = parser.parse_args()
@@ -512,7 +586,9 @@ def main() -> None:
 
         native.load_library().moe_b200_select_gemv(GEMV_IMPLS[args.gemv])
     try:
-        if args.profile:
+        if args.profile_prefill:
+            result = run_profile_prefill(args)
+        elif args.profile:
             result = run_profile_case(args)
         else:
             if args.impl == "reference":
