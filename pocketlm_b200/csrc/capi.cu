@@ -234,9 +234,19 @@ int moe::route_impl(const void* hidden, int hd, const void* w, int wd, const flo
                       int64_t E, int64_t n_group, int64_t topk_group, int64_t k, int scoring, int renorm,
                       int fp64, float scale, int round_bf16, int64_t* ids64, int32_t* ids32, float* wf32,
                       uint16_t* wbf16, float* logits, cudaStream_t stream) {
-  MOE_CUDA(launch_router_logits(hidden, hd, w, wd, logits, static_cast<int>(T), static_cast<int>(H),
-                                static_cast<int>(E), stream),
-           "router logits");
+  // prefill-sized batches on the tensor cores (split-K partials, summed in
+  // part order by the selection); otherwise the fp32 GEMV / tiled kernels
+  int nparts = 1;
+  if (T > 256 && router_split_is_mma(hidden, hd, w, wd, static_cast<int>(H))) {
+    MOE_CUDA(launch_router_logits_split(hidden, hd, w, wd, logits, static_cast<int>(T), static_cast<int>(H),
+                                        static_cast<int>(E), stream),
+             "router logits");
+    nparts = router_split_parts(static_cast<int>(H));
+  } else {
+    MOE_CUDA(launch_router_logits(hidden, hd, w, wd, logits, static_cast<int>(T), static_cast<int>(H),
+                                  static_cast<int>(E), stream),
+             "router logits");
+  }
   RouterSelectParams p{};
   p.tokens = static_cast<int>(T);
   p.experts = static_cast<int>(E);
@@ -249,7 +259,7 @@ int moe::route_impl(const void* hidden, int hd, const void* w, int wd, const flo
   p.round_bf16 = round_bf16;
   p.route_scale = scale;
   MOE_CUDA(launch_router_select(logits, bias, p, ids64, ids32, wf32, reinterpret_cast<__nv_bfloat16*>(wbf16),
-                                stream),
+                                stream, nparts, T * E),
            "router select");
   return kOk;
 }
@@ -542,7 +552,8 @@ int moe_fp8_e4m3_dequant_to_bf16(const uint8_t* w, const float* s, uint16_t* out
 
 int64_t moe_route_topk_workspace_bytes(int64_t tokens, int64_t experts) {
   Plan p;
-  p.take<float>(tokens * experts);
+  // above 256 tokens the logits may come as up to kMaxRouterParts split-K partials
+  p.take<float>((tokens > 256 ? kMaxRouterParts : 1) * tokens * experts);
   return static_cast<int64_t>(p.used());
 }
 
@@ -648,7 +659,8 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
 // The expert stages on the tcgen05 grouped GEMM (tiled weights): gather the
 // pairs' fp16 rows, gate/up + SwiGLU, stage the activations, down.
 static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16, const LayerPlan& l, int64_t T,
-                                     int64_t pairs, int64_t n_segments, int64_t I, int64_t H, cudaStream_t s) {
+                                     int64_t pairs, int64_t n_segments, int64_t I, int64_t H, const uint8_t* nan_free,
+                                     cudaStream_t s) {
   const MlpScratch& m = l.m;
   MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.x16, l.xscale, nullptr,
                               0, s),
@@ -662,8 +674,8 @@ static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16
   g1.a16 = l.a16; g1.ascale = l.a16scale; g1.rows_a = pairs;
   g1.seg_offset = m.seg_offset; g1.mprefix = l.mprefix; g1.n_segments = static_cast<int>(n_segments);
   g1.out = m.act; g1.N = static_cast<int>(I); g1.K = static_cast<int>(H);
-  g1.scale_cols = static_cast<int>(ceil_div(H, kBlock)); g1.nanfix = 1;
-  MOE_CUDA(launch_prefill_gemm(g1, true, mtiles_bound * (I / 64), s), "gate/up GEMM");
+  g1.scale_cols = static_cast<int>(ceil_div(H, kBlock)); g1.nanfix = 1; g1.nan_free = nan_free;
+  MOE_CUDA(launch_prefill_gemm(g1, true, mtiles_bound * (I / 128), s), "gate/up GEMM");
   stage_mark(s);
   MOE_CUDA(launch_rows_to_f16(m.act, false, static_cast<int>(pairs), static_cast<int>(I), nullptr, l.act16, l.ascale,
                               nullptr, 0, s),
@@ -674,7 +686,7 @@ static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16
   g2.a16 = l.act16; g2.ascale = l.ascale;
   g2.out = m.y; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
   g2.scale_cols = static_cast<int>(ceil_div(I, kBlock));
-  MOE_CUDA(launch_prefill_gemm(g2, false, mtiles_bound * (H / 128), s), "down GEMM");
+  MOE_CUDA(launch_prefill_gemm(g2, false, mtiles_bound * (H / 256), s), "down GEMM");
   stage_mark(s);
   return kOk;
 }
@@ -821,7 +833,7 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
                        prefill_supported(H, I, true) && prefill_supported(I, H, false);
   if (prefill) {
     code = run_expert_stages_prefill(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I,
-                                     H, s);
+                                     H, nan_free, s);
   } else if (use_mma) {
     code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I, H,
                                  chunks_ready, nan_free, s, weight_layout);

@@ -72,7 +72,8 @@ DensePlan plan_dense(Plan& p, int kind, int64_t rows_x, int64_t pairs, int64_t s
   if (router_logits > 0) {
     d.ids32 = p.take<int32_t>(entries);
     d.wts = p.take<float>(entries);
-    d.logits = p.take<float>(router_logits);
+    // above 256 tokens the router may produce up to kMaxRouterParts split-K partials
+    d.logits = p.take<float>((rows_x > 256 ? kMaxRouterParts : 1) * router_logits);
   }
   if (tables) d.tables = p.take<uint64_t>(6 * segments);
   d.mma = dense_mma_supported(kind, static_cast<int>(H)) && dense_mma_supported(kind, static_cast<int>(I));

@@ -332,10 +332,10 @@ constexpr int kAsyncStageBytes = kWarp * 12 * 16;  // 6 KiB: a k-block of the wa
 constexpr int kAsyncSmem = kAsyncWarps * kAsyncStages * kAsyncStageBytes;
 // Fragment-native ("tiled") weight layout: for every 16-row tile and 128-column
 // k-block, 2 KiB holding the 16-byte pieces in the order the lanes take them:
-// piece p (row g + 8 (p / 2), columns 64 (p % 2) + 16 c, lane (g, c)) of all
+// piece p (row g + 8 (p % 2), columns 64 (p / 2) + 16 c, lane (g, c)) of all
 // 32 lanes, then the next piece -- so each warp-wide cp.async reads 512
-// contiguous bytes and a warp-task's weights are one contiguous stream per
-// matrix.
+// contiguous bytes, a warp-task's weights are one contiguous stream per
+// matrix, and each 64-column half of a block is 1 KiB contiguous.
 constexpr int kTileKBlockBytes = kWarp * 64;
 
 MOE_D void cp_async16(void* smem, const void* gmem) {
@@ -372,7 +372,7 @@ MOE_D void async_accumulate(float (&acc)[2][4], unsigned char* ring, const uint8
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr)
           cp_async16(slot(stage, (sp * 2 + st) * 2 + rr),
-                     TILED ? tbase[st] + static_cast<int64_t>(kbi) * kTileKBlockBytes + (rr * 2 + sp) * (kWarp * 16)
+                     TILED ? tbase[st] + static_cast<int64_t>(kbi) * kTileKBlockBytes + (sp * 2 + rr) * (kWarp * 16)
                            : arow[st][rr] + kbi * kBlock + sp * 64);
 #pragma unroll
       for (int h = 0; h < 2; ++h)
@@ -592,7 +592,7 @@ __global__ void fp8_tile_kernel(const uint8_t* __restrict__ src, uint8_t* __rest
     const int lane = static_cast<int>((q / 4) % kWarp);
     const int64_t kb = (q / (4 * kWarp)) % nkb;
     const int64_t tile = q / (4 * kWarp * nkb);
-    const int g = lane / 4, c = lane % 4, rr = piece / 2, sp = piece % 2;
+    const int g = lane / 4, c = lane % 4, sp = piece / 2, rr = piece % 2;
     const int64_t row = tile * 16 + g + 8 * rr;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (row < rows) v = *reinterpret_cast<const uint4*>(src + row * cols + kb * kBlock + sp * 64 + 16 * c);

@@ -11,18 +11,19 @@
 // power of two (exact; undone in the epilogue), expert-contiguous [P, K] and
 // loaded by TMA (128B swizzle, 128 rows x 64 columns per box).  B is the
 // expert's weights in the fragment-native tiled layout (fp8_mma.cu), brought
-// in by 1-D bulk copies and converted by a converter warpgroup to fp16 with
-// the k-block's scale folded in -- w * s rounded to fp16, a relative error of
-// at most 2^-11 per weight -- written in the same 128B-swizzled K-major
-// layout.  D accumulates in fp32 in tensor memory: M = 128 pairs,
-// N = 128 weight rows (64 gate + 64 up rows for the fused gate/up GEMM),
-// K = 16 per MMA, 64 per pipeline stage.
+// in by 1-D bulk copies of 1 KiB runs and converted by a converter warpgroup
+// to fp16 with the k-block's scale folded in -- w * s rounded to fp16, a
+// relative error of at most 2^-11 per weight -- written in the same
+// 128B-swizzled K-major layout.  D accumulates in fp32 in tensor memory:
+// M = 128 pairs, N = 256 weight rows (128 gate + 128 up rows for the fused
+// gate/up GEMM), K = 16 per MMA, 64 per pipeline stage; five load stages
+// (A + raw weights) feed two converted-weight buffers.
 //
 // Warp roles (352 threads): warps 0-3 epilogue (TMEM lanes 32w..32w+31),
 // warps 4-7 converter, warp 8 TMA producer, warp 9 MMA issuer, warp 10 TMEM
 // allocator.  A persistent CTA walks tiles (expert m-tile, n-tile) in order;
-// two TMEM accumulators let the epilogue of one tile overlap the next
-// tile's main loop.  Every wait is bounded (2 s of %globaltimer): on
+// two TMEM accumulators (2 x 256 columns) let the epilogue of one tile
+// overlap the next tile's main loop.  Every wait is bounded (2 s of %globaltimer): on
 // expiry the CTA records an error code, every role leaves its loop, the
 // producer waits (bounded) for the copies it issued, and TMEM is freed.
 #include <cuda.h>
@@ -40,33 +41,41 @@ namespace moe {
 namespace {
 
 constexpr int kBM = 128;              // pairs per tile
-constexpr int kBN = 128;              // weight rows per tile
+constexpr int kBN = 256;              // weight rows per tile (128 gate + 128 up for the gate/up GEMM)
 constexpr int kBK = 64;               // k per stage (half a scale block)
-constexpr int kStages = 4;
-constexpr int kATileBytes = kBM * kBK * 2;       // 16 KiB, fp16 swizzled
-constexpr int kBTileBytes = kBN * kBK * 2;       // 16 KiB, fp16 swizzled (converted)
-constexpr int kRawBytes = kBN * kBK;             // 8 KiB e4m3, 16 runs of 512 B
-constexpr int kStageBytes = kATileBytes + kBTileBytes + kRawBytes;
-constexpr int kTmemCols = 2 * kBN;               // two fp32 accumulators
+constexpr int kStages = 5;            // load stages: A tile + raw e4m3 weights
+constexpr int kConvBufs = 2;          // converted fp16 weight buffers
+constexpr int kATileBytes = kBM * kBK * 2;       // 16 KiB, fp16, 128B-swizzled (TMA)
+constexpr int kRawBytes = kBN * kBK;             // 16 KiB e4m3: 16 row tiles x 1 KiB runs
+constexpr int kLoadBytes = kATileBytes + kRawBytes;
+constexpr int kBTileBytes = kBN * kBK * 2;       // 32 KiB, fp16, 128B-swizzled (converter)
+constexpr int kTmemCols = 2 * kBN;               // two tile accumulators (512 columns)
 constexpr int kEpiWarps = 4, kConvWarps = 4;
 constexpr int kProducerWarp = 8, kMmaWarp = 9, kAllocWarp = 10;
 constexpr int kThreads = 11 * kWarp;
 constexpr int kCodeWait = 32;
 
 struct Barriers {
-  uint64_t full[kStages];   // producer -> converter: A + raw weights landed (tx bytes)
-  uint64_t conv[kStages];   // converter -> MMA: fp16 weights written (4 arrivals)
-  uint64_t empty[kStages];  // MMA -> producer: the stage's MMAs completed (tcgen05.commit)
-  uint64_t tfull[2];        // MMA -> epilogue: accumulator complete
-  uint64_t tempty[2];       // epilogue -> MMA: accumulator drained (4 arrivals)
-  uint64_t drain;           // MMA issuer's last commit: all of its MMAs complete
+  uint64_t full[kStages];      // producer -> converter, MMA: A + raw weights landed (tx bytes)
+  uint64_t empty[kStages];     // MMA -> producer: the stage's MMAs completed (tcgen05.commit)
+  uint64_t cfull[kConvBufs];   // converter -> MMA: fp16 weights written (4 arrivals)
+  uint64_t cempty[kConvBufs];  // MMA -> converter: buffer consumed (tcgen05.commit)
+  uint64_t tfull[2];           // MMA -> epilogue: tile accumulator complete
+  uint64_t tempty[2];          // epilogue -> MMA: accumulator drained (4 arrivals)
+  uint64_t drain;              // MMA issuer's last commit: all of its MMAs complete
   uint32_t tmem_base;
   int abort;
 };
-constexpr size_t kSmemBytes = 1024 /* alignment slack */ + static_cast<size_t>(kStages) * kStageBytes +
-                              sizeof(Barriers);
+constexpr size_t kSmemBytes = 1024 /* alignment slack */ + static_cast<size_t>(kStages) * kLoadBytes +
+                              static_cast<size_t>(kConvBufs) * kBTileBytes + sizeof(Barriers);
+static_assert(kSmemBytes <= 232448, "shared memory per block");
 
 // ---------------------------------------------------------------- PTX
+MOE_D uint32_t e4m3x2_to_f16x2_raw(uint32_t pair) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair), __NV_E4M3);
+  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+}
+
 MOE_D void tmem_alloc(uint32_t* dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)), "r"(ncols)
                : "memory");
@@ -188,18 +197,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
                                                                     PrefillArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kStageBytes);
-  auto a_tile = [&](int s) { return smem + s * kStageBytes; };
-  auto b_tile = [&](int s) { return smem + s * kStageBytes + kATileBytes; };
-  auto raw_tile = [&](int s) { return smem + s * kStageBytes + kATileBytes + kBTileBytes; };
+  auto a_tile = [&](int s) { return smem + s * kLoadBytes; };
+  auto raw_tile = [&](int s) { return smem + s * kLoadBytes + kATileBytes; };
+  auto b_tile = [&](int b) { return smem + kStages * kLoadBytes + b * kBTileBytes; };
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kLoadBytes + kConvBufs * kBTileBytes);
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   volatile int* abort = &bars->abort;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->conv[s], kConvWarps);
       mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < kConvBufs; ++b) {
+      mbar_init(&bars->cfull[b], kConvWarps);
+      mbar_init(&bars->cempty[b], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->tfull[i], 1);
@@ -229,86 +241,90 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       uint32_t it = 0;
       for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
         const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
+        // 16 row tiles of 16 rows: gate/up = 8 from each matrix, down = 16 consecutive
         const uint8_t* wbase[2];
         int tile0[2];
         if (GATEUP) {
           wbase[0] = reinterpret_cast<const uint8_t*>(a.w0[tr.seg]);
           wbase[1] = reinterpret_cast<const uint8_t*>(a.w1[tr.seg]);
-          tile0[0] = tile0[1] = tr.nt * 4;  // 64 rows = 4 tiles of 16 in each matrix
+          tile0[0] = tile0[1] = tr.nt * 8;
         } else {
           wbase[0] = wbase[1] = reinterpret_cast<const uint8_t*>(a.w0[tr.seg]);
-          tile0[0] = tr.nt * 8;
-          tile0[1] = tr.nt * 8 + 4;
+          tile0[0] = tr.nt * 16;
+          tile0[1] = tr.nt * 16 + 8;
         }
         for (int kh = 0; kh < nkh && !*abort; ++kh, ++it) {
           const int s = it % kStages;
           if (it >= kStages && !wait_or_abort(&bars->empty[s], ((it / kStages) - 1) & 1, abort)) break;
-          mbar_arrive_expect_tx(&bars->full[s], kATileBytes + kRawBytes);
+          mbar_arrive_expect_tx(&bars->full[s], kLoadBytes);
           tma_load_2d(a_tile(s), &tmap_a, kh * kBK, tr.row0, &bars->full[s]);
           const int kb = kh / 2, sp = kh % 2;
-          // 8 row tiles of 16 (4 from each half) x rows g / g + 8: 16 runs of 512 B
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int half = i / 4;
-            const uint8_t* blk =
-                wbase[half] + (static_cast<int64_t>(tile0[half] + i % 4) * nkb + kb) * 2048;
-#pragma unroll
-            for (int rr = 0; rr < 2; ++rr)
-              bulk_copy_g2s(raw_tile(s) + (i * 2 + rr) * 512, blk + (rr * 2 + sp) * 512, 512, &bars->full[s]);
+          for (int i = 0; i < 16; ++i) {
+            const int half = i / 8;
+            const uint8_t* blk = wbase[half] + (static_cast<int64_t>(tile0[half] + i % 8) * nkb + kb) * 2048;
+            bulk_copy_g2s(raw_tile(s) + i * 1024, blk + sp * 1024, 1024, &bars->full[s]);
           }
         }
       }
-      // drain: every copy issued must land before the CTA may exit
+      // every copy issued lands before the CTA may exit
       for (uint32_t j = it > kStages ? it - kStages : 0; j < it; ++j)
         mbar_wait(&bars->full[j % kStages], (j / kStages) & 1, kCodeWait);
     }
   } else if (warp >= kEpiWarps && warp < kEpiWarps + kConvWarps) {
-    // converter: e4m3 runs -> fp16 * block scale, 128B-swizzled K-major
+    // converter: e4m3 runs x block scale -> fp16, 128B-swizzled K-major
     const int ct = threadIdx.x - kEpiWarps * kWarp;  // 0..127
     uint32_t it = 0;
     for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
       const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
+      const bool fix = a.nanfix && !(a.nan_free && a.nan_free[tr.seg]);
+      // scale rows of the two 128-row halves of the tile
       const float* sb[2];
       int srow[2];
       if (GATEUP) {
         sb[0] = reinterpret_cast<const float*>(a.s0[tr.seg]);
         sb[1] = reinterpret_cast<const float*>(a.s1[tr.seg]);
-        srow[0] = srow[1] = (tr.nt * 64) / 128;
+        srow[0] = srow[1] = tr.nt;
       } else {
         sb[0] = sb[1] = reinterpret_cast<const float*>(a.s0[tr.seg]);
-        srow[0] = srow[1] = tr.nt;  // 128 rows = one scale row
+        srow[0] = 2 * tr.nt;
+        srow[1] = 2 * tr.nt + 1;
       }
+      bool ok = true;
       for (int kh = 0; kh < nkh; ++kh, ++it) {
-        const int s = it % kStages;
-        if (!wait_or_abort(&bars->full[s], (it / kStages) & 1, abort)) break;
+        const int s = it % kStages, b = it % kConvBufs;
         const int kb = kh / 2;
         const float sc[2] = {__ldg(sb[0] + srow[0] * a.scale_cols + kb), __ldg(sb[1] + srow[1] * a.scale_cols + kb)};
+        if (!wait_or_abort(&bars->full[s], (it / kStages) & 1, abort) ||
+            (it >= kConvBufs && !wait_or_abort(&bars->cempty[b], ((it / kConvBufs) - 1) & 1, abort))) {
+          ok = false;
+          break;
+        }
         const unsigned char* raw = raw_tile(s);
-        unsigned char* bt = b_tile(s);
+        unsigned char* bt = b_tile(b);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int u = ct + q * 128;        // 16-byte unit: run u / 32, lane u % 32
-          const int run = u / kWarp, ul = u % kWarp;
-          const int i = run / 2, rr = run % 2;
+        for (int q = 0; q < 8; ++q) {
+          const int u = ct + q * 128;           // 16-byte unit: run u / 64, row half, lane
+          const int run = u / 64, rr = (u / kWarp) % 2, ul = u % kWarp;
           const int g = ul / 4, c = ul % 4;
-          const int n = 16 * i + g + 8 * rr;  // tile row 0..127
+          const int n = 16 * run + g + 8 * rr;  // tile row 0..255
           uint4 v = *reinterpret_cast<const uint4*>(raw + u * 16);
-          const float scale = sc[i / 4];
-          if (a.nanfix) {
+          if (fix) {
             v.x = e4m3x4_nan_to_zero(v.x);
             v.y = e4m3x4_nan_to_zero(v.y);
             v.z = e4m3x4_nan_to_zero(v.z);
             v.w = e4m3x4_nan_to_zero(v.w);
           }
+          const float scale = sc[run / 8];
           const uint32_t words[4] = {v.x, v.y, v.z, v.w};
           uint32_t h[8];
 #pragma unroll
           for (int w = 0; w < 4; ++w) {
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              const float2 f = e4m3x2_to_float2(static_cast<uint16_t>(words[w] >> (16 * half)));
+            for (int hh = 0; hh < 2; ++hh) {
+              const float2 f = e4m3x2_to_float2(static_cast<uint16_t>(words[w] >> (16 * hh)));
               const __half2 hv = __floats2half2_rn(f.x * scale, f.y * scale);
-              h[w * 2 + half] = *reinterpret_cast<const uint32_t*>(&hv);
+              h[w * 2 + hh] = *reinterpret_cast<const uint32_t*>(&hv);
             }
           }
           // k 16c .. 16c + 15 of this stage = 16-byte chunks 2c, 2c + 1 of row n
@@ -321,35 +337,35 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         }
         fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor core (async proxy)
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->conv[s]);
+        if (lane == 0) mbar_arrive(&bars->cfull[b]);
       }
+      if (!ok) break;
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       uint32_t it = 0, ti = 0;
-      for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x, ++ti) {
-        const int acc = ti % 2;
-        if (ti >= 2 && !wait_or_abort(&bars->tempty[acc], ((ti / 2) - 1) & 1, abort)) break;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok && !*abort; t += gridDim.x, ++ti) {
+        const int slot = ti % 2;
+        if (ti >= 2 && !wait_or_abort(&bars->tempty[slot], ((ti / 2) - 1) & 1, abort)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + acc * kBN;
-        bool ok = true;
+        const uint32_t d_tmem = tmem + slot * kBN;
         for (int kh = 0; kh < nkh; ++kh, ++it) {
-          const int s = it % kStages;
-          // the A tile (TMA) and the converted weights of this stage have landed
+          const int s = it % kStages, b = it % kConvBufs;
           if (!wait_or_abort(&bars->full[s], (it / kStages) & 1, abort) ||
-              !wait_or_abort(&bars->conv[s], (it / kStages) & 1, abort)) {
+              !wait_or_abort(&bars->cfull[b], (it / kConvBufs) & 1, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_addr(a_tile(s)), sbt = smem_addr(b_tile(s));
+          const uint32_t sa = smem_addr(a_tile(s)), sbt = smem_addr(b_tile(b));
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
             umma_f16(d_tmem, sw128_desc(sa + k * 32), sw128_desc(sbt + k * 32), kIdesc, (kh | k) != 0);
-          umma_commit(&bars->empty[s]);  // frees the stage when these MMAs complete
+          umma_commit(&bars->empty[s]);   // A + raw stage free once these MMAs complete
+          umma_commit(&bars->cempty[b]);  // and the converted buffer
         }
-        if (!ok) break;
-        umma_commit(&bars->tfull[acc]);
+        if (ok) umma_commit(&bars->tfull[slot]);
       }
       // every MMA this thread issued has completed before TMEM is released
       umma_commit(&bars->drain);
@@ -358,22 +374,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
   } else if (warp < kEpiWarps) {
     uint32_t ti = 0;
     const int row_in_tile = warp * kWarp + lane;  // TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(warp * kWarp) << 16;
     for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x, ++ti) {
       const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
-      const int acc = ti % 2;
-      if (!wait_or_abort(&bars->tfull[acc], (ti / 2) & 1, abort)) break;
+      const int slot = ti % 2;
+      if (!wait_or_abort(&bars->tfull[slot], (ti / 2) & 1, abort)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem + acc * kBN + (static_cast<uint32_t>(warp * kWarp) << 16);
+      const uint32_t taddr = tmem + slot * kBN + lane_off;
       const bool valid = row_in_tile < tr.rows;
       const int64_t p = tr.row0 + row_in_tile;
       const float xs = valid ? a.ascale[p] : 0.0f;
       if (GATEUP) {
-        float* out = a.out + p * N + tr.nt * 64;
-#pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 16) {
-          float g[16], u[16];
-          tmem_ld16(taddr + c0, g);
-          tmem_ld16(taddr + 64 + c0, u);
+        float* out = a.out + p * N + tr.nt * (kBN / 2);
+#pragma unroll 1
+        for (int c0 = 0; c0 < kBN / 2; c0 += 16) {
+          float gv[16], uv[16];
+          tmem_ld16(taddr + c0, gv);
+          tmem_ld16(taddr + kBN / 2 + c0, uv);
           if (valid) {
 #pragma unroll
             for (int j = 0; j < 16; j += 4) {
@@ -381,8 +398,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
               float* op = &o.x;
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                const float gv = g[j + q] * xs, uv = u[j + q] * xs;
-                op[q] = gv / (1.0f + expf(-gv)) * uv;
+                const float g = gv[j + q] * xs, u = uv[j + q] * xs;
+                op[q] = g / (1.0f + expf(-g)) * u;
               }
               *reinterpret_cast<float4*>(out + c0 + j) = o;
             }
@@ -390,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         }
       } else {
         float* out = a.out + p * N + tr.nt * kBN;
-#pragma unroll
+#pragma unroll 1
         for (int c0 = 0; c0 < kBN; c0 += 16) {
           float d[16];
           tmem_ld16(taddr + c0, d);
@@ -404,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->tempty[acc]);
+      if (lane == 0) mbar_arrive(&bars->tempty[slot]);
     }
   }
 
@@ -432,7 +449,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 size_t prefill_smem_bytes() { return kSmemBytes; }
 
 bool prefill_supported(int64_t K, int64_t N, bool gateup) {
-  return K > 0 && N > 0 && K % 128 == 0 && (gateup ? N % 64 == 0 : N % kBN == 0);
+  return K > 0 && N > 0 && K % 128 == 0 && (gateup ? N % (kBN / 2) == 0 : N % kBN == 0);
 }
 
 cudaError_t launch_prefill_tiles(const int32_t* seg_offset, int n_segments, int32_t* mprefix, cudaStream_t stream) {

@@ -24,10 +24,11 @@ struct PrefillArgs {
   int K;
   int scale_cols;          // ceil(K / 128)
   int nanfix;              // decode e4m3 0x7F / 0xFF as +0
+  const uint8_t* nan_free; // [n_segments] or null: 1 = the expert holds no such code
 };
 
 size_t prefill_smem_bytes();
-// K % 128 == 0; N % 64 (gate/up) or % 128 (down) == 0.
+// K % 128 == 0; N % 128 (gate/up) or % 256 (down) == 0.
 bool prefill_supported(int64_t K, int64_t N, bool gateup);
 cudaError_t launch_prefill_tiles(const int32_t* seg_offset, int n_segments, int32_t* mprefix, cudaStream_t stream);
 cudaError_t launch_gather_rows(const __half* x16, const float* xscale, const int32_t* pair_row, int64_t P, int64_t K,

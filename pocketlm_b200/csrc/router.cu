@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(kMmaRouterWarps * kWarp) router_logits_mma_ker
   const T* wa = w + static_cast<int64_t>(min(e0 + g, experts - 1)) * hidden + 8 * c;
   const T* wb = w + static_cast<int64_t>(min(e0 + g + 8, experts - 1)) * hidden + 8 * c;
   float* out = partial + static_cast<int64_t>(blockIdx.y) * tokens * experts;
-  for (int t0 = 0; t0 < tokens; t0 += 64) {
+  for (int t0 = blockIdx.z * 64; t0 < tokens; t0 += gridDim.z * 64) {
     const int ntiles = min(8, static_cast<int>(ceil_div(tokens - t0, 8)));
     float acc[8][4];
 #pragma unroll
@@ -443,7 +443,7 @@ static cudaError_t launch_split_t(const void* x, const void* w, float* partial, 
   if constexpr (kPair) {
     if (aligned && hidden % kSpan == 0) {
       dim3 grid(static_cast<unsigned>(ceil_div(ceil_div(experts, 16), kMmaRouterWarps)),
-                static_cast<unsigned>(parts));
+                static_cast<unsigned>(parts), static_cast<unsigned>(std::min<int64_t>(ceil_div(tokens, 64), 1024)));
       router_logits_mma_kernel<XT><<<grid, kMmaRouterWarps * kWarp, 0, stream>>>(
           static_cast<const XT*>(x), static_cast<const XT*>(w), partial, tokens, hidden, experts, kpart);
       return cudaGetLastError();
@@ -486,6 +486,11 @@ cudaError_t launch_router_logits_cluster(const void* x, int x_dtype, const void*
   return cudaGetLastError();
 }
 
+bool router_split_is_mma(const void* x, int x_dtype, const void* w, int w_dtype, int hidden) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(w) % 16 == 0);
+  return aligned && hidden % kSpan == 0 && x_dtype == w_dtype && (x_dtype == kDtypeBF16 || x_dtype == kDtypeF16);
+}
+
 int router_split_parts(int hidden) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(kMaxRouterParts, ceil_div(hidden, 448))));
 }
@@ -518,7 +523,7 @@ cudaError_t launch_router_logits(const void* x, int x_dtype, const void* w, int 
 
 cudaError_t launch_router_select(const float* logits, const float* bias, const RouterSelectParams& p,
                                  int64_t* ids64, int32_t* ids32, float* weights_f32,
-                                 __nv_bfloat16* weights_bf16, cudaStream_t stream) {
+                                 __nv_bfloat16* weights_bf16, cudaStream_t stream, int nparts, int64_t part_stride) {
   if (p.tokens <= 0) return cudaSuccess;
   const size_t smem = static_cast<size_t>(kSelectWarps) * 2 * p.experts * sizeof(float);
   const unsigned grid = static_cast<unsigned>(ceil_div(p.tokens, kSelectWarps));
@@ -527,8 +532,8 @@ cudaError_t launch_router_select(const float* logits, const float* bias, const R
                                            static_cast<int>(smem));
     if (err != cudaSuccess) return err;
   }
-  router_select_kernel<<<grid, kSelectWarps * kWarp, smem, stream>>>(logits, 1, 0, bias, p, ids64, ids32,
-                                                                      weights_f32, weights_bf16);
+  router_select_kernel<<<grid, kSelectWarps * kWarp, smem, stream>>>(logits, nparts, part_stride, bias, p, ids64,
+                                                                      ids32, weights_f32, weights_bf16);
   return cudaGetLastError();
 }
 

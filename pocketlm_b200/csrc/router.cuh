@@ -39,8 +39,13 @@ cudaError_t launch_router_logits_split(const void* x, int x_dtype, const void* w
 cudaError_t launch_router_logits_cluster(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
                                          int tokens, int hidden, int experts, cudaStream_t stream);
 
+// logits: nparts partial [T, E] matrices part_stride floats apart, summed in part order.
 cudaError_t launch_router_select(const float* logits, const float* bias, const RouterSelectParams& p,
                                  int64_t* ids64, int32_t* ids32, float* weights_f32,
-                                 __nv_bfloat16* weights_bf16, cudaStream_t stream);
+                                 __nv_bfloat16* weights_bf16, cudaStream_t stream, int nparts = 1,
+                                 int64_t part_stride = 0);
+// Whether launch_router_logits_split runs on the tensor cores for these operands
+// (bf16 x bf16 or f16 x f16, 16-byte aligned, hidden % 32 == 0).
+bool router_split_is_mma(const void* x, int x_dtype, const void* w, int w_dtype, int hidden);
 
 }  // namespace moe
