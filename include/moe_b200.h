@@ -338,11 +338,12 @@ int moe_ep_dispatch_pack(const int64_t* ids, const float* weights, const uint16_
 int64_t moe_ep_dispatch_workspace_bytes(int64_t tokens, int64_t top_k);
 
 /* out[i] = expert_{row_expert[i]}(rows[i]) (fp32 [rows, hidden]) over this
- * rank's experts (device tables [6][num_local]); a row whose expert id is
- * out of range comes back zero.  hidden and intermediate: multiples of 128. */
+ * rank's experts (device tables [6][num_local]; nan_free and weight_layout as
+ * for moe_ds_moe_layer_fp8); a row whose expert id is out of range comes
+ * back zero.  hidden and intermediate: multiples of 128. */
 int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int64_t rows, int64_t hidden_dim,
                        int64_t intermediate, const uint64_t* tables, int64_t num_local, const uint8_t* nan_free,
-                       float* out, void* workspace, int64_t workspace_bytes, void* stream);
+                       int weight_layout, float* out, void* workspace, int64_t workspace_bytes, void* stream);
 int64_t moe_ep_experts_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t intermediate, int64_t num_local);
 
 /* out_bf16[t] = bf16(sum_slot pos_weight[p] * y[p] (+ y[tokens*top_k + t]

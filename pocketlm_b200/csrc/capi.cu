@@ -237,7 +237,16 @@ int moe::route_impl(const void* hidden, int hd, const void* w, int wd, const flo
   // prefill-sized batches on the tensor cores (split-K partials, summed in
   // part order by the selection); otherwise the fp32 GEMV / tiled kernels
   int nparts = 1;
-  if (T > 256 && router_split_is_mma(hidden, hd, w, wd, static_cast<int>(H))) {
+  cudaError_t cerr = cudaErrorNotSupported;
+  if (T <= 256) {
+    // decode-sized batches: one cluster-reduced tensor-core pass when the operands allow it
+    cerr = launch_router_logits_cluster(hidden, hd, w, wd, logits, static_cast<int>(T), static_cast<int>(H),
+                                        static_cast<int>(E), stream);
+    if (cerr != cudaErrorNotSupported) MOE_CUDA(cerr, "router logits");
+  }
+  if (cerr != cudaErrorNotSupported) {
+    // done
+  } else if (T > 256 && router_split_is_mma(hidden, hd, w, wd, static_cast<int>(H))) {
     MOE_CUDA(launch_router_logits_split(hidden, hd, w, wd, logits, static_cast<int>(T), static_cast<int>(H),
                                         static_cast<int>(E), stream),
              "router logits");
@@ -906,8 +915,11 @@ int64_t moe_ep_experts_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t
 
 int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int64_t rows, int64_t hidden_dim,
                        int64_t intermediate, const uint64_t* tables, int64_t num_local, const uint8_t* nan_free,
-                       float* out, void* workspace, int64_t workspace_bytes, void* stream) {
+                       int weight_layout, float* out, void* workspace, int64_t workspace_bytes, void* stream) {
   if (!rows_bf16 || !row_expert || !tables || !out) return fail(kNullPointer, "null pointer");
+  if (weight_layout != 0 && weight_layout != 1) return fail(kBadDims, "weight_layout must be 0 or 1");
+  if (weight_layout == 1 && !(g_gemv_impl == 0 && g_mma_feed == 2))
+    return fail(kUnsupported, "tiled weights need the cp.async warp-MMA GEMV");
   if (rows <= 0 || hidden_dim <= 0 || intermediate <= 0 || num_local <= 0) return fail(kBadDims, "bad dimensions");
   if (num_local > kMaxBuckets) return fail(kUnsupported, "too many local experts");
   if (!mma_gemv_supported(static_cast<int>(hidden_dim), static_cast<int>(intermediate)) ||
@@ -927,7 +939,7 @@ int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int
   ba.pair_weight = l.m.pair_weight; ba.pair_entry = l.m.pair_entry; ba.entry_pair = l.m.entry_pair; ba.tail = 0;
   MOE_CUDA(launch_bucket(ba, s), "expert buckets");
   Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
-  int code = run_expert_stages_mma(t, rows_bf16, true, l, R, R, S, I, H, false, nan_free, s);
+  int code = run_expert_stages_mma(t, rows_bf16, true, l, R, R, S, I, H, false, nan_free, s, weight_layout);
   if (code != kOk) return code;
   // back to row order (a row routed nowhere -- key out of range -- comes back zero)
   CombineArgs c{};

@@ -84,9 +84,12 @@ class CudaEPOps:
         R = int(rows.shape[0])
         out = torch.empty((R, L.cfg.hidden), dtype=torch.float32, device=rows.device)
         ws = self._workspace(int(self.lib.moe_ep_experts_workspace_bytes(R, L.cfg.hidden, L.cfg.inter, L.n_local + 1)))
+        layout = 1 if L.tables_tiled is not None and self.lib.moe_b200_selected_gemv() == 0 else 0
+        tables = L.tables_tiled if layout else L.tables
         code = self.lib.moe_ep_experts_fp8(
-            native._ptr(rows), native._ptr(row_expert), R, L.cfg.hidden, L.cfg.inter, native._ptr(L.tables),
-            L.n_local + 1, native._ptr(L.nan_free), native._ptr(out), native._ptr(ws), ws.numel(), native._stream())
+            native._ptr(rows), native._ptr(row_expert), R, L.cfg.hidden, L.cfg.inter, native._ptr(tables),
+            L.n_local + 1, native._ptr(L.nan_free), layout, native._ptr(out), native._ptr(ws), ws.numel(),
+            native._stream())
         native._check(code, "moe_ep_experts_fp8")
         return out
 
@@ -128,11 +131,31 @@ class ExpertParallelLayer:
         self.tables = torch.tensor([[int(ex[j].data_ptr()) for ex in self.local_experts] for j in range(6)],
                                    dtype=torch.int64, device=self.device) if self.device.type == "cuda" else None
         self.nan_free = None
+        self.tables_tiled = None
         if self.device.type == "cuda":
-            self.nan_free = torch.zeros((self.n_local + 1,), dtype=torch.uint8, device=self.device)
-            native._check(native.load_library().moe_fp8_nan_free_flags(
-                native._ptr(self.tables), self.n_local + 1, cfg.inter, cfg.hidden, native._ptr(self.nan_free),
+            lib = native.load_library()
+            n = self.n_local + 1
+            self.nan_free = torch.zeros((n,), dtype=torch.uint8, device=self.device)
+            native._check(lib.moe_fp8_nan_free_flags(
+                native._ptr(self.tables), n, cfg.inter, cfg.hidden, native._ptr(self.nan_free),
                 native._stream()), "moe_fp8_nan_free_flags")
+            if cfg.hidden % 128 == 0 and cfg.inter % 128 == 0:
+                # the decode GEMV's fragment-native copy of the local experts (moe_fp8_tile_weights)
+                tb13 = int(lib.moe_fp8_tiled_bytes(cfg.inter, cfg.hidden))
+                tb2 = int(lib.moe_fp8_tiled_bytes(cfg.hidden, cfg.inter))
+                self._tiled13 = torch.empty((n, 2, tb13), dtype=torch.uint8, device=self.device)
+                self._tiled2 = torch.empty((n, tb2), dtype=torch.uint8, device=self.device)
+                cols = [[int(ex[j].data_ptr()) for ex in self.local_experts] for j in range(6)]
+                for i, (g, _gs, u, _us, d, _ds) in enumerate(self.local_experts):
+                    for src, dst, rows, k in ((g, self._tiled13[i, 0], cfg.inter, cfg.hidden),
+                                              (u, self._tiled13[i, 1], cfg.inter, cfg.hidden),
+                                              (d, self._tiled2[i], cfg.hidden, cfg.inter)):
+                        native._check(lib.moe_fp8_tile_weights(native._ptr(src), native._ptr(dst), rows, k,
+                                                               native._stream()), "moe_fp8_tile_weights")
+                    cols[0][i] = int(self._tiled13[i, 0].data_ptr())
+                    cols[2][i] = int(self._tiled13[i, 1].data_ptr())
+                    cols[4][i] = int(self._tiled2[i].data_ptr())
+                self.tables_tiled = torch.tensor(cols, dtype=torch.int64, device=self.device)
         self.ops = ops(self) if ops is not None else CudaEPOps(self)
 
     def forward(self, x: torch.Tensor):

@@ -120,7 +120,7 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_moe_forward_fp16_workspace_bytes": ([_I64] * 5, _I64),
     "moe_ep_dispatch_pack": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _P], _INT),
     "moe_ep_dispatch_workspace_bytes": ([_I64, _I64], _I64),
-    "moe_ep_experts_fp8": ([_P, _P, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _I64, _P], _INT),
+    "moe_ep_experts_fp8": ([_P, _P, _I64, _I64, _I64, _P, _I64, _P, _INT, _P, _P, _I64, _P], _INT),
     "moe_ep_experts_workspace_bytes": ([_I64] * 4, _I64),
     "moe_ep_combine": ([_P, _P, _P, _I64, _I64, _I64, _INT, _P, _P], _INT),
     "moe_b200_stage_timing": ([_INT], _INT),
