@@ -293,12 +293,15 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                 "gateup_gbs": (b["gateup"] / (gateup_ms / 1e3) / 1e9) if gateup_ms else None,
                 "down_gbs": (b["down"] / (down_ms / 1e3) / 1e9) if down_ms else None,
             }
-        prefill = {}
-        if args.prefill_tokens != "none":
+        prefill, q4 = {}, {}
+        if args.prefill_tokens != "none" or args.q4_tokens != "none":
             del gpu_layer, layer, graphed
             torch.cuda.empty_cache()
+        if args.prefill_tokens != "none":
             prefill = run_prefill(args, dev, flush, peaks,
                                   [int(v) for v in args.prefill_tokens.split(",") if v])
+        if args.q4_tokens != "none":
+            q4 = run_q4(args, dev, flush, peaks, [int(v) for v in args.q4_tokens.split(",") if v])
     clock_info = clocks.summary()
     if rank != 0:
         return None
@@ -338,6 +341,7 @@ def run_ours(args, rank: int, world: int) -> dict | None:
         "sweep": {str(T): {k: v for k, v in r.items() if k != "stage_ms"} | {"stage_ms": r["stage_ms"]}
                   for T, r in sorted(results.items())},
         "prefill": prefill,
+        "q4": q4,
     }
 
 
@@ -383,6 +387,37 @@ def run_prefill(args, dev, flush, peaks, token_list) -> dict:
     torch.cuda.empty_cache()
     return {"workload": "c3-dsv3-prefill-zipf", "peak_bf16_tflops": bf16_peak,
             "peak_source": f"{peaks['source']} bf16_tflops", "sweep": out}
+
+
+def run_q4(args, dev, flush, peaks, token_list) -> dict:
+    """Config 4 on one GPU: the Mixtral-8x7B-shape layer in the reference's Q4
+    format (hidden 4096, ffn 14336, 8 experts, softmax top-2 renormalised),
+    bf16 activations, through moe_q4_moe_layer_u16 (router, dispatch, Q4
+    grouped GEMV on the warp MMA pipe, combine).  Eager forwards,
+    CUDA-event timed, L2 flushed between steps.  Bytes: the experts the batch
+    selects (packed codes + fp16 row scales) + router + activations."""
+    from pocketlm_b200 import synth
+    from pocketlm_b200.runtime import Q4MoELayerGPU
+
+    cfg = synth.C4_MIXTRAL
+    layer = Q4MoELayerGPU(synth.make_q4_layer(cfg, seed=args.seed, device=dev))
+    out = {}
+    for T in token_list:
+        x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 7 * T, device=dev)
+        ids = torch.empty((T, cfg.top_k), dtype=torch.int64, device=dev)
+        layer.forward(x, ids=ids)
+        torch.cuda.synchronize()
+        steps = max(3, min(args.steps, 20))
+        ms = statistics.mean(time_steps(lambda: layer.forward(x), steps, args.warmup, flush))
+        n_exp = len({int(v) for v in ids.reshape(-1).tolist()})
+        nbytes = n_exp * cfg.expert_bytes + cfg.n_experts * cfg.hidden * 2 + T * cfg.hidden * 4
+        out[str(T)] = {"tokens": T, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3), "experts_streamed": n_exp,
+                       "layer_bytes": nbytes,
+                       "layer_hbm_frac": nbytes / (ms / 1e3) / (peaks["hbm_gbs"] * 1e9)}
+        del x, ids
+    del layer
+    torch.cuda.empty_cache()
+    return {"workload": "c4-mixtral-q4", "kernel": "dense_mma_gemv_kernel<Q4> (dense_gemv.cu)", "sweep": out}
 
 
 def run_ours_ep(args, rank: int, world: int) -> dict | None:
@@ -565,6 +600,8 @@ def main() -> None:
                         help="expert GEMV kernel (moe_b200_select_gemv); auto is the product default")
     parser.add_argument("--prefill-tokens", default="2048,8192,16384",
                         help="config-3 prefill batch sizes measured after the decode sweep, or 'none'")
+    parser.add_argument("--q4-tokens", default="1,32,4096",
+                        help="config-4 (Mixtral Q4) batch sizes measured after the prefill sweep, or 'none'")
     parser.add_argument("--profile", action="store_true",
                         help="run the small ncu case (selected experts only) instead of the benchmark")
     parser.add_argument("--profile-prefill", action="store_true",

@@ -11,17 +11,18 @@
 // power of two (exact; undone in the epilogue), expert-contiguous [P, K] and
 // loaded by TMA (128B swizzle, 128 rows x 64 columns per box).  B is the
 // expert's weights in the fragment-native tiled layout (fp8_mma.cu), brought
-// in by 1-D bulk copies of 1 KiB runs and converted by a converter warpgroup
-// to fp16 with the k-block's scale folded in -- w * s rounded to fp16, a
-// relative error of at most 2^-11 per weight -- written in the same
-// 128B-swizzled K-major layout.  D accumulates in fp32 in tensor memory:
+// in by 1-D bulk copies of 1 KiB runs and converted by eight converter warps
+// to fp16 with the k-block's scale folded in -- the exact e4m3 value times
+// the scale rounded to fp16, product rounded to fp16: a relative error of
+// at most about 2^-10 per weight -- written in the same 128B-swizzled
+// K-major layout.  D accumulates in fp32 in tensor memory:
 // M = 128 pairs, N = 256 weight rows (128 gate + 128 up rows for the fused
 // gate/up GEMM), K = 16 per MMA, 64 per pipeline stage; five load stages
 // (A + raw weights) feed two converted-weight buffers.
 //
-// Warp roles (352 threads): warps 0-3 epilogue (TMEM lanes 32w..32w+31),
-// warps 4-7 converter, warp 8 TMA producer, warp 9 MMA issuer, warp 10 TMEM
-// allocator.  A persistent CTA walks tiles (expert m-tile, n-tile) in order;
+// Warp roles (480 threads): warps 0-3 epilogue (TMEM lanes 32w..32w+31),
+// warps 4-11 converter, warp 12 TMA producer, warp 13 MMA issuer, warp 14
+// TMEM allocator.  A persistent CTA walks tiles (expert m-tile, n-tile) in order;
 // two TMEM accumulators (2 x 256 columns) let the epilogue of one tile
 // overlap the next tile's main loop.  Every wait is bounded (2 s of %globaltimer): on
 // expiry the CTA records an error code, every role leaves its loop, the
@@ -50,9 +51,10 @@ constexpr int kRawBytes = kBN * kBK;             // 16 KiB e4m3: 16 row tiles x 
 constexpr int kLoadBytes = kATileBytes + kRawBytes;
 constexpr int kBTileBytes = kBN * kBK * 2;       // 32 KiB, fp16, 128B-swizzled (converter)
 constexpr int kTmemCols = 2 * kBN;               // two tile accumulators (512 columns)
-constexpr int kEpiWarps = 4, kConvWarps = 4;
-constexpr int kProducerWarp = 8, kMmaWarp = 9, kAllocWarp = 10;
-constexpr int kThreads = 11 * kWarp;
+constexpr int kEpiWarps = 4, kConvWarps = 8;
+constexpr int kConvThreads = kConvWarps * kWarp;
+constexpr int kProducerWarp = kEpiWarps + kConvWarps, kMmaWarp = kProducerWarp + 1, kAllocWarp = kProducerWarp + 2;
+constexpr int kThreads = (kAllocWarp + 1) * kWarp;
 constexpr int kCodeWait = 32;
 
 struct Barriers {
@@ -273,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
     }
   } else if (warp >= kEpiWarps && warp < kEpiWarps + kConvWarps) {
     // converter: e4m3 runs x block scale -> fp16, 128B-swizzled K-major
-    const int ct = threadIdx.x - kEpiWarps * kWarp;  // 0..127
+    const int ct = threadIdx.x - kEpiWarps * kWarp;  // 0 .. kConvThreads - 1
     uint32_t it = 0;
     for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
       const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
@@ -294,7 +296,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       for (int kh = 0; kh < nkh; ++kh, ++it) {
         const int s = it % kStages, b = it % kConvBufs;
         const int kb = kh / 2;
-        const float sc[2] = {__ldg(sb[0] + srow[0] * a.scale_cols + kb), __ldg(sb[1] + srow[1] * a.scale_cols + kb)};
+        // the block scales as fp16 pairs: w * s is rounded once more, to fp16
+        const __half2 sc2[2] = {__float2half2_rn(__ldg(sb[0] + srow[0] * a.scale_cols + kb)),
+                                __float2half2_rn(__ldg(sb[1] + srow[1] * a.scale_cols + kb))};
         if (!wait_or_abort(&bars->full[s], (it / kStages) & 1, abort) ||
             (it >= kConvBufs && !wait_or_abort(&bars->cempty[b], ((it / kConvBufs) - 1) & 1, abort))) {
           ok = false;
@@ -303,8 +307,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         const unsigned char* raw = raw_tile(s);
         unsigned char* bt = b_tile(b);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int u = ct + q * 128;           // 16-byte unit: run u / 64, row half, lane
+        for (int q = 0; q < kRawBytes / 16 / kConvThreads; ++q) {
+          const int u = ct + q * kConvThreads;  // 16-byte unit: run u / 64, row half, lane
           const int run = u / 64, rr = (u / kWarp) % 2, ul = u % kWarp;
           const int g = ul / 4, c = ul % 4;
           const int n = 16 * run + g + 8 * rr;  // tile row 0..255
@@ -315,15 +319,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
             v.z = e4m3x4_nan_to_zero(v.z);
             v.w = e4m3x4_nan_to_zero(v.w);
           }
-          const float scale = sc[run / 8];
+          const __half2 scale = sc2[run / 8];
           const uint32_t words[4] = {v.x, v.y, v.z, v.w};
           uint32_t h[8];
 #pragma unroll
           for (int w = 0; w < 4; ++w) {
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-              const float2 f = e4m3x2_to_float2(static_cast<uint16_t>(words[w] >> (16 * hh)));
-              const __half2 hv = __floats2half2_rn(f.x * scale, f.y * scale);
+              const uint32_t e = e4m3x2_to_f16x2_raw((words[w] >> (16 * hh)) & 0xFFFFu);
+              const __half2 hv = __hmul2(*reinterpret_cast<const __half2*>(&e), scale);
               h[w * 2 + hh] = *reinterpret_cast<const uint32_t*>(&hv);
             }
           }
