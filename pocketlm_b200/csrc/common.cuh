@@ -46,6 +46,15 @@ MOE_D uint32_t e4m3x4_nan_to_zero(uint32_t w) {
   return w & ~mask;
 }
 
+// Four e4m3 bytes -> two fp16x2 words (exact): lo = bytes 0, 1; hi = bytes 2, 3.
+// The 32-bit word is split into its 16-bit halves inside the asm, so no
+// extract / repack instructions surround the two conversions.
+MOE_D void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n cvt.rn.f16x2.e4m3x2 %0, l;\n cvt.rn.f16x2.e4m3x2 %1, h;\n}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+
 // Two e4m3 bytes (low half of `pair`) -> two floats (exact).
 MOE_D float2 e4m3x2_to_float2(uint16_t pair) {
   __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair), __NV_E4M3);

@@ -35,11 +35,6 @@ namespace moe {
 
 constexpr int kMmaCtaWarps = 4;
 
-MOE_D uint32_t e4m3x2_to_f16x2_bits(uint32_t pair) {
-  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair & 0xFFFFu), __NV_E4M3);
-  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
-}
-
 MOE_D void mma_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -235,8 +230,10 @@ __global__ void __launch_bounds__(kMmaCtaWarps * kWarp) mma_gemv_kernel(MmaArgs 
                 wg = e4m3x4_nan_to_zero(wg);
                 wh = e4m3x4_nan_to_zero(wh);
               }
-              mma_16816(t[st], e4m3x2_to_f16x2_bits(wg), e4m3x2_to_f16x2_bits(wh),
-                        e4m3x2_to_f16x2_bits(wg >> 16), e4m3x2_to_f16x2_bits(wh >> 16), bw[2 * s], bw[2 * s + 1]);
+              uint32_t g0, g1, h0, h1;
+              e4m3x4_to_f16x2x2(wg, g0, g1);
+              e4m3x4_to_f16x2x2(wh, h0, h1);
+              mma_16816(t[st], g0, h0, g1, h1, bw[2 * s], bw[2 * s + 1]);
             }
           }
         }
@@ -415,8 +412,10 @@ MOE_D void async_accumulate(float (&acc)[2][4], unsigned char* ring, const uint8
             wg = e4m3x4_nan_to_zero(wg);
             wh = e4m3x4_nan_to_zero(wh);
           }
-          mma_16816(t[st], e4m3x2_to_f16x2_bits(wg), e4m3x2_to_f16x2_bits(wh), e4m3x2_to_f16x2_bits(wg >> 16),
-                    e4m3x2_to_f16x2_bits(wh >> 16), bw[2 * s], bw[2 * s + 1]);
+          uint32_t g0, g1, h0, h1;
+          e4m3x4_to_f16x2x2(wg, g0, g1);
+          e4m3x4_to_f16x2x2(wh, h0, h1);
+          mma_16816(t[st], g0, h0, g1, h1, bw[2 * s], bw[2 * s + 1]);
         }
       }
     }
@@ -740,8 +739,10 @@ __global__ void __launch_bounds__(kTmaWarps * kWarp) tma_mma_gemv_kernel(MmaArgs
                   wg = e4m3x4_nan_to_zero(wg);
                   wh = e4m3x4_nan_to_zero(wh);
                 }
-                mma_16816(t[st], e4m3x2_to_f16x2_bits(wg), e4m3x2_to_f16x2_bits(wh),
-                          e4m3x2_to_f16x2_bits(wg >> 16), e4m3x2_to_f16x2_bits(wh >> 16), bw[2 * s], bw[2 * s + 1]);
+                uint32_t g0, g1, h0, h1;
+                e4m3x4_to_f16x2x2(wg, g0, g1);
+                e4m3x4_to_f16x2x2(wh, h0, h1);
+                mma_16816(t[st], g0, h0, g1, h1, bw[2 * s], bw[2 * s + 1]);
               }
             }
           }

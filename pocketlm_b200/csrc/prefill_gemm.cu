@@ -56,6 +56,7 @@ constexpr int kConvThreads = kConvWarps * kWarp;
 constexpr int kProducerWarp = kEpiWarps + kConvWarps, kMmaWarp = kProducerWarp + 1, kAllocWarp = kProducerWarp + 2;
 constexpr int kThreads = (kAllocWarp + 1) * kWarp;
 constexpr int kCodeWait = 32;
+constexpr int kScaleRegs = 4;  // converter scale cache: registers per lane and half
 
 struct Barriers {
   uint64_t full[kStages];      // producer -> converter, MMA: A + raw weights landed (tx bytes)
@@ -73,10 +74,6 @@ constexpr size_t kSmemBytes = 1024 /* alignment slack */ + static_cast<size_t>(k
 static_assert(kSmemBytes <= 232448, "shared memory per block");
 
 // ---------------------------------------------------------------- PTX
-MOE_D uint32_t e4m3x2_to_f16x2_raw(uint32_t pair) {
-  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair), __NV_E4M3);
-  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
-}
 
 MOE_D void tmem_alloc(uint32_t* dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)), "r"(ncols)
@@ -131,11 +128,14 @@ MOE_D uint64_t sw128_desc(uint32_t saddr) {
 // kind::f16 instruction descriptor: fp32 D, fp16 A and B, both K-major.
 constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
 
-// Bounded wait that also gives up when another role aborted.
+// Bounded wait that also gives up when another role aborted.  Between checks
+// the thread sleeps in try_wait (woken when the phase completes), so waiting
+// roles take no issue slots from the converter warps.
+constexpr uint32_t kSuspendHintNs = 20000;
 MOE_D bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) {
     if (*abort) return false;
     if (global_timer_ns() - start > kWaitLimitNs) {
       atomicOr(&g_device_error, kCodeWait);
@@ -281,24 +281,37 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
       const bool fix = a.nanfix && !(a.nan_free && a.nan_free[tr.seg]);
       // scale rows of the two 128-row halves of the tile
-      const float* sb[2];
-      int srow[2];
-      if (GATEUP) {
-        sb[0] = reinterpret_cast<const float*>(a.s0[tr.seg]);
-        sb[1] = reinterpret_cast<const float*>(a.s1[tr.seg]);
-        srow[0] = srow[1] = tr.nt;
-      } else {
-        sb[0] = sb[1] = reinterpret_cast<const float*>(a.s0[tr.seg]);
-        srow[0] = 2 * tr.nt;
-        srow[1] = 2 * tr.nt + 1;
-      }
+      const float* sb0 = reinterpret_cast<const float*>(a.s0[tr.seg]);
+      const float* sb1 = GATEUP ? reinterpret_cast<const float*>(a.s1[tr.seg]) : sb0;
+      sb0 += static_cast<int64_t>(GATEUP ? tr.nt : 2 * tr.nt) * a.scale_cols;
+      sb1 += static_cast<int64_t>(GATEUP ? tr.nt : 2 * tr.nt + 1) * a.scale_cols;
+      // the tile's block scales, k-block kb in lane kb % 32 of register kb / 32
+      // (read once per tile; K up to kScaleRegs * 32 * 128, else per stage)
+      const bool cached = nkb <= kScaleRegs * kWarp;
+      auto scale_at = [&](const float* sb, int i) {
+        const int kbi = lane + i * kWarp;
+        return (cached && kbi < nkb) ? __ldg(sb + kbi) : 0.0f;
+      };
+      // four named registers per half (an indexed array would live in local memory)
+      const float g0 = scale_at(sb0, 0), g1 = scale_at(sb0, 1), g2 = scale_at(sb0, 2), g3 = scale_at(sb0, 3);
+      const float u0 = scale_at(sb1, 0), u1 = scale_at(sb1, 1), u2 = scale_at(sb1, 2), u3 = scale_at(sb1, 3);
       bool ok = true;
       for (int kh = 0; kh < nkh; ++kh, ++it) {
         const int s = it % kStages, b = it % kConvBufs;
         const int kb = kh / 2;
         // the block scales as fp16 pairs: w * s is rounded once more, to fp16
-        const __half2 sc2[2] = {__float2half2_rn(__ldg(sb[0] + srow[0] * a.scale_cols + kb)),
-                                __float2half2_rn(__ldg(sb[1] + srow[1] * a.scale_cols + kb))};
+        float sf0, sf1;
+        if (cached) {
+          const int r = kb / kWarp;
+          const float v0 = r == 0 ? g0 : r == 1 ? g1 : r == 2 ? g2 : g3;
+          const float v1 = r == 0 ? u0 : r == 1 ? u1 : r == 2 ? u2 : u3;
+          sf0 = __shfl_sync(0xffffffffu, v0, kb % kWarp);
+          sf1 = __shfl_sync(0xffffffffu, v1, kb % kWarp);
+        } else {
+          sf0 = __ldg(sb0 + kb);
+          sf1 = __ldg(sb1 + kb);
+        }
+        const __half2 sc_lo = __float2half2_rn(sf0), sc_hi = __float2half2_rn(sf1);
         if (!wait_or_abort(&bars->full[s], (it / kStages) & 1, abort) ||
             (it >= kConvBufs && !wait_or_abort(&bars->cempty[b], ((it / kConvBufs) - 1) & 1, abort))) {
           ok = false;
@@ -319,16 +332,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
             v.z = e4m3x4_nan_to_zero(v.z);
             v.w = e4m3x4_nan_to_zero(v.w);
           }
-          const __half2 scale = sc2[run / 8];
+          const __half2 scale = q * kConvThreads >= kRawBytes / 32 ? sc_hi : sc_lo;  // runs 8-15: second half
           const uint32_t words[4] = {v.x, v.y, v.z, v.w};
           uint32_t h[8];
 #pragma unroll
           for (int w = 0; w < 4; ++w) {
+            e4m3x4_to_f16x2x2(words[w], h[2 * w], h[2 * w + 1]);
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-              const uint32_t e = e4m3x2_to_f16x2_raw((words[w] >> (16 * hh)) & 0xFFFFu);
-              const __half2 hv = __hmul2(*reinterpret_cast<const __half2*>(&e), scale);
-              h[w * 2 + hh] = *reinterpret_cast<const uint32_t*>(&hv);
+              const __half2 hv = __hmul2(*reinterpret_cast<const __half2*>(&h[2 * w + hh]), scale);
+              h[2 * w + hh] = *reinterpret_cast<const uint32_t*>(&hv);
             }
           }
           // k 16c .. 16c + 15 of this stage = 16-byte chunks 2c, 2c + 1 of row n
