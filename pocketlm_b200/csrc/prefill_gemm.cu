@@ -9,22 +9,26 @@
 //
 // Operands.  A is the pairs' activation rows in fp16, each row divided by a
 // power of two (exact; undone in the epilogue), expert-contiguous [P, K] and
-// loaded by TMA (128B swizzle, 128 rows x 64 columns per box).  B is the
+// loaded by TMA (128B swizzle, 128 rows x 64 columns per box, two boxes per
+// 256-pair tile).  B is the
 // expert's weights in the fragment-native tiled layout (fp8_mma.cu), brought
 // in by 1-D bulk copies of 1 KiB runs and converted by eight converter warps
 // to fp16 with the k-block's scale folded in -- the exact e4m3 value times
 // the scale rounded to fp16, product rounded to fp16: a relative error of
 // at most about 2^-10 per weight -- written in the same 128B-swizzled
-// K-major layout.  D accumulates in fp32 in tensor memory:
-// M = 128 pairs, N = 256 weight rows (128 gate + 128 up rows for the fused
-// gate/up GEMM), K = 16 per MMA, 64 per pipeline stage; five load stages
-// (A + raw weights) feed two converted-weight buffers.
+// K-major layout.  A tile is 256 pairs x 256 weight rows (128 gate + 128 up
+// rows for the fused gate/up GEMM): two M = 128 MMAs per K = 16 step share
+// the converted weights, so each converted byte feeds twice the tensor work
+// of a 128-pair tile.  D accumulates in fp32 in tensor memory (2 x 256
+// columns).  K = 64 per pipeline stage; three load stages (two A sub-tiles +
+// raw weights, 48 KiB) feed two converted-weight buffers (32 KiB).  A tile of
+// at most 128 pairs loads and multiplies one sub-tile.
 //
-// Warp roles (480 threads): warps 0-3 epilogue (TMEM lanes 32w..32w+31),
-// warps 4-11 converter, warp 12 TMA producer, warp 13 MMA issuer, warp 14
-// TMEM allocator.  A persistent CTA walks tiles (expert m-tile, n-tile) in order;
-// two TMEM accumulators (2 x 256 columns) let the epilogue of one tile
-// overlap the next tile's main loop.  Every wait is bounded (2 s of %globaltimer): on
+// Warp roles (608 threads): warps 0-7 epilogue (warp w: TMEM lanes
+// 32 (w % 4) .. + 31 of sub-tile w / 4), warps 8-15 converter, warp 16 TMA
+// producer, warp 17 MMA issuer, warp 18 TMEM allocator.  A persistent CTA
+// walks tiles (expert m-tile, n-tile) in order; the epilogue drains a tile's
+// accumulators before the next tile's first MMA.  Every wait is bounded (2 s of %globaltimer): on
 // expiry the CTA records an error code, every role leaves its loop, the
 // producer waits (bounded) for the copies it issued, and TMEM is freed.
 #include <cuda.h>
@@ -41,17 +45,18 @@
 namespace moe {
 namespace {
 
-constexpr int kBM = 128;              // pairs per tile
+constexpr int kBM = 256;              // pairs per tile: two 128-row MMA sub-tiles sharing B
+constexpr int kSubM = 128;            // pairs per MMA (M of tcgen05.mma, cta_group::1)
 constexpr int kBN = 256;              // weight rows per tile (128 gate + 128 up for the gate/up GEMM)
 constexpr int kBK = 64;               // k per stage (half a scale block)
-constexpr int kStages = 5;            // load stages: A tile + raw e4m3 weights
+constexpr int kStages = 3;            // load stages: two A sub-tiles + raw e4m3 weights
 constexpr int kConvBufs = 2;          // converted fp16 weight buffers
-constexpr int kATileBytes = kBM * kBK * 2;       // 16 KiB, fp16, 128B-swizzled (TMA)
+constexpr int kATileBytes = kSubM * kBK * 2;     // 16 KiB per sub-tile, fp16, 128B-swizzled (TMA)
 constexpr int kRawBytes = kBN * kBK;             // 16 KiB e4m3: 16 row tiles x 1 KiB runs
-constexpr int kLoadBytes = kATileBytes + kRawBytes;
+constexpr int kLoadBytes = 2 * kATileBytes + kRawBytes;  // 48 KiB per stage
 constexpr int kBTileBytes = kBN * kBK * 2;       // 32 KiB, fp16, 128B-swizzled (converter)
-constexpr int kTmemCols = 2 * kBN;               // two tile accumulators (512 columns)
-constexpr int kEpiWarps = 4, kConvWarps = 8;
+constexpr int kTmemCols = 2 * kBN;               // the two sub-tiles' accumulators (512 columns)
+constexpr int kEpiWarps = 8, kConvWarps = 8;
 constexpr int kConvThreads = kConvWarps * kWarp;
 constexpr int kProducerWarp = kEpiWarps + kConvWarps, kMmaWarp = kProducerWarp + 1, kAllocWarp = kProducerWarp + 2;
 constexpr int kThreads = (kAllocWarp + 1) * kWarp;
@@ -63,8 +68,8 @@ struct Barriers {
   uint64_t empty[kStages];     // MMA -> producer: the stage's MMAs completed (tcgen05.commit)
   uint64_t cfull[kConvBufs];   // converter -> MMA: fp16 weights written (4 arrivals)
   uint64_t cempty[kConvBufs];  // MMA -> converter: buffer consumed (tcgen05.commit)
-  uint64_t tfull[2];           // MMA -> epilogue: tile accumulator complete
-  uint64_t tempty[2];          // epilogue -> MMA: accumulator drained (4 arrivals)
+  uint64_t tfull;              // MMA -> epilogue: tile accumulators complete
+  uint64_t tempty;             // epilogue -> MMA: accumulators drained (one arrival per epilogue warp)
   uint64_t drain;              // MMA issuer's last commit: all of its MMAs complete
   uint32_t tmem_base;
   int abort;
@@ -97,17 +102,15 @@ MOE_D void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                : "memory");
 }
-MOE_D void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
+// 16 columns of this warp's 32 TMEM lanes; the registers are valid after tmem_ld_wait().
+MOE_D void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+MOE_D void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 MOE_D void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -126,7 +129,7 @@ MOE_D uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 // kind::f16 instruction descriptor: fp32 D, fp16 A and B, both K-major.
-constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kSubM >> 4) << 24);
 
 // Bounded wait that also gives up when another role aborted.  Between checks
 // the thread sleeps in try_wait (woken when the phase completes), so waiting
@@ -199,8 +202,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
                                                                     PrefillArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  auto a_tile = [&](int s) { return smem + s * kLoadBytes; };
-  auto raw_tile = [&](int s) { return smem + s * kLoadBytes + kATileBytes; };
+  auto a_tile = [&](int s, int h) { return smem + s * kLoadBytes + h * kATileBytes; };
+  auto raw_tile = [&](int s) { return smem + s * kLoadBytes + 2 * kATileBytes; };
   auto b_tile = [&](int b) { return smem + kStages * kLoadBytes + b * kBTileBytes; };
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kLoadBytes + kConvBufs * kBTileBytes);
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
@@ -215,10 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       mbar_init(&bars->cfull[b], kConvWarps);
       mbar_init(&bars->cempty[b], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->tfull[i], 1);
-      mbar_init(&bars->tempty[i], kEpiWarps);
-    }
+    mbar_init(&bars->tfull, 1);
+    mbar_init(&bars->tempty, kEpiWarps);
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
     fence_barrier_init();
@@ -258,8 +259,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         for (int kh = 0; kh < nkh && !*abort; ++kh, ++it) {
           const int s = it % kStages;
           if (it >= kStages && !wait_or_abort(&bars->empty[s], ((it / kStages) - 1) & 1, abort)) break;
-          mbar_arrive_expect_tx(&bars->full[s], kLoadBytes);
-          tma_load_2d(a_tile(s), &tmap_a, kh * kBK, tr.row0, &bars->full[s]);
+          // the second sub-tile only when the tile has more than 128 pairs
+          const bool two = tr.rows > kSubM;
+          mbar_arrive_expect_tx(&bars->full[s], two ? kLoadBytes : kLoadBytes - kATileBytes);
+          tma_load_2d(a_tile(s, 0), &tmap_a, kh * kBK, tr.row0, &bars->full[s]);
+          if (two) tma_load_2d(a_tile(s, 1), &tmap_a, kh * kBK, tr.row0 + kSubM, &bars->full[s]);
           const int kb = kh / 2, sp = kh % 2;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -363,10 +367,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       uint32_t it = 0, ti = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < tiles && ok && !*abort; t += gridDim.x, ++ti) {
-        const int slot = ti % 2;
-        if (ti >= 2 && !wait_or_abort(&bars->tempty[slot], ((ti / 2) - 1) & 1, abort)) break;
+        const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
+        const bool two = tr.rows > kSubM;
+        // the epilogue has drained the previous tile's accumulators
+        if (ti >= 1 && !wait_or_abort(&bars->tempty, (ti - 1) & 1, abort)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + slot * kBN;
         for (int kh = 0; kh < nkh; ++kh, ++it) {
           const int s = it % kStages, b = it % kConvBufs;
           if (!wait_or_abort(&bars->full[s], (it / kStages) & 1, abort) ||
@@ -375,39 +380,47 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_addr(a_tile(s)), sbt = smem_addr(b_tile(b));
+          const uint32_t sa0 = smem_addr(a_tile(s, 0)), sa1 = smem_addr(a_tile(s, 1)), sbt = smem_addr(b_tile(b));
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)
-            umma_f16(d_tmem, sw128_desc(sa + k * 32), sw128_desc(sbt + k * 32), kIdesc, (kh | k) != 0);
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t bdesc = sw128_desc(sbt + k * 32);
+            umma_f16(tmem, sw128_desc(sa0 + k * 32), bdesc, kIdesc, (kh | k) != 0);
+            if (two) umma_f16(tmem + kBN, sw128_desc(sa1 + k * 32), bdesc, kIdesc, (kh | k) != 0);
+          }
           umma_commit(&bars->empty[s]);   // A + raw stage free once these MMAs complete
           umma_commit(&bars->cempty[b]);  // and the converted buffer
         }
-        if (ok) umma_commit(&bars->tfull[slot]);
+        if (ok) umma_commit(&bars->tfull);
       }
       // every MMA this thread issued has completed before TMEM is released
       umma_commit(&bars->drain);
       mbar_wait(&bars->drain, 0, kCodeWait);
     }
   } else if (warp < kEpiWarps) {
+    // warp w drains TMEM lanes 32 (w % 4) .. + 31 of sub-tile w / 4 (columns 256 (w / 4) ..)
     uint32_t ti = 0;
-    const int row_in_tile = warp * kWarp + lane;  // TMEM lane
-    const uint32_t lane_off = static_cast<uint32_t>(warp * kWarp) << 16;
+    const int half = warp / 4, quad = warp % 4;
+    const int row_in_tile = half * kSubM + quad * kWarp + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * kWarp) << 16;
     for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x, ++ti) {
       const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
-      const int slot = ti % 2;
-      if (!wait_or_abort(&bars->tfull[slot], (ti / 2) & 1, abort)) break;
+      if (!wait_or_abort(&bars->tfull, ti & 1, abort)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem + slot * kBN + lane_off;
+      // the second sub-tile's accumulator was not written for tiles of <= 128 pairs
+      const bool live = half == 0 || tr.rows > kSubM;
+      const uint32_t taddr = tmem + half * kBN + lane_off;
       const bool valid = row_in_tile < tr.rows;
       const int64_t p = tr.row0 + row_in_tile;
       const float xs = valid ? a.ascale[p] : 0.0f;
-      if (GATEUP) {
+      if (!live) {
+      } else if (GATEUP) {
         float* out = a.out + p * N + tr.nt * (kBN / 2);
 #pragma unroll 1
         for (int c0 = 0; c0 < kBN / 2; c0 += 16) {
-          float gv[16], uv[16];
-          tmem_ld16(taddr + c0, gv);
-          tmem_ld16(taddr + kBN / 2 + c0, uv);
+          uint32_t gr[16], ur[16];
+          tmem_ld16(taddr + c0, gr);
+          tmem_ld16(taddr + kBN / 2 + c0, ur);
+          tmem_ld_wait();
           if (valid) {
 #pragma unroll
             for (int j = 0; j < 16; j += 4) {
@@ -415,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
               float* op = &o.x;
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                const float g = gv[j + q] * xs, u = uv[j + q] * xs;
+                const float g = __uint_as_float(gr[j + q]) * xs, u = __uint_as_float(ur[j + q]) * xs;
                 op[q] = g / (1.0f + expf(-g)) * u;
               }
               *reinterpret_cast<float4*>(out + c0 + j) = o;
@@ -425,20 +438,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       } else {
         float* out = a.out + p * N + tr.nt * kBN;
 #pragma unroll 1
-        for (int c0 = 0; c0 < kBN; c0 += 16) {
-          float d[16];
-          tmem_ld16(taddr + c0, d);
+        for (int c0 = 0; c0 < kBN; c0 += 32) {
+          uint32_t d0[16], d1[16];
+          tmem_ld16(taddr + c0, d0);
+          tmem_ld16(taddr + c0 + 16, d1);
+          tmem_ld_wait();
           if (valid) {
 #pragma unroll
-            for (int j = 0; j < 16; j += 4)
+            for (int j = 0; j < 16; j += 4) {
               *reinterpret_cast<float4*>(out + c0 + j) =
-                  make_float4(d[j] * xs, d[j + 1] * xs, d[j + 2] * xs, d[j + 3] * xs);
+                  make_float4(__uint_as_float(d0[j]) * xs, __uint_as_float(d0[j + 1]) * xs,
+                              __uint_as_float(d0[j + 2]) * xs, __uint_as_float(d0[j + 3]) * xs);
+              *reinterpret_cast<float4*>(out + c0 + 16 + j) =
+                  make_float4(__uint_as_float(d1[j]) * xs, __uint_as_float(d1[j + 1]) * xs,
+                              __uint_as_float(d1[j + 2]) * xs, __uint_as_float(d1[j + 3]) * xs);
+            }
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->tempty[slot]);
+      if (lane == 0) mbar_arrive(&bars->tempty);
     }
   }
 
@@ -491,7 +511,7 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, bool gateup, int64_t max_t
   CUtensorMap tmap;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.K), static_cast<cuuint64_t>(a.rows_a)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.K) * 2};
-  const cuuint32_t box[2] = {kBK, kBM};
+  const cuuint32_t box[2] = {kBK, kSubM};
   const cuuint32_t estr[2] = {1, 1};
   if (encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(a.a16), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
