@@ -94,9 +94,25 @@ cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bou
 // cp.async (fp8_mma.cu); tasks_bound as for launch_mma_gemv.
 int async_gemv_ksplit(int64_t tasks_bound, int K);
 cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream);
-// Fragment-native weight layout for the cp.async kernel: bytes of the tiled
-// copy of a row-major e4m3 [rows, cols] matrix (cols % 128 == 0; rows padded
-// to a multiple of 32 with zeros), and the repacking launch.
+// Fragment-native ("tiled") weight layout, read by the cp.async decode GEMV
+// and the prefill GEMM.  Row tile t = rows 16t .. 16t + 15; group = 8 row
+// tiles (128 rows).  For every (group, 128-column k-block kb, 64-column half
+// sp) an 8 KiB block holds the group's 8 row tiles in order, 1 KiB each; a
+// row tile's 1 KiB is two 512-byte pieces (rr = 0: rows g, rr = 1: rows
+// g + 8) of 32 lanes x 16 bytes, lane l = 4g + c holding columns
+// 64 sp + 16 c .. + 15 of row 16t + g + 8 rr.  So a warp-wide 16-byte
+// access is 512 contiguous bytes (decode), and 128 rows x 64 columns of a
+// matrix are one 8 KiB run (one bulk copy of the prefill GEMM).
+constexpr int64_t kTileGroupRows = 128;
+constexpr int64_t kTileRunBytes = 8192;  // one (group, kb, sp) block
+MOE_HD int64_t tiled_offset(int64_t tile, int64_t kb, int sp, int nkb) {
+  return (((tile / 8) * nkb + kb) * 2 + sp) * kTileRunBytes + (tile % 8) * 1024;
+}
+MOE_HD int64_t fp8_tiled_bytes_dev(int64_t rows, int64_t cols) {
+  return (rows + kTileGroupRows - 1) / kTileGroupRows * kTileGroupRows * cols;
+}
+// Bytes of the tiled copy of a row-major e4m3 [rows, cols] matrix (cols %
+// 128 == 0; rows padded to a multiple of 128 with zeros), and the repacking launch.
 int64_t fp8_tiled_bytes(int64_t rows, int64_t cols);
 cudaError_t launch_fp8_tile(const uint8_t* src, uint8_t* dst, int64_t rows, int64_t cols, cudaStream_t stream);
 // Per-expert flags for MmaArgs::nan_free: flags[s] = 1 when none of the

@@ -327,13 +327,10 @@ constexpr int kAsyncWarps = 4;
 constexpr int kAsyncStages = 3;
 constexpr int kAsyncStageBytes = kWarp * 12 * 16;  // 6 KiB: a k-block of the warp's 32 row streams + its activations
 constexpr int kAsyncSmem = kAsyncWarps * kAsyncStages * kAsyncStageBytes;
-// Fragment-native ("tiled") weight layout: for every 16-row tile and 128-column
-// k-block, 2 KiB holding the 16-byte pieces in the order the lanes take them:
-// piece p (row g + 8 (p % 2), columns 64 (p / 2) + 16 c, lane (g, c)) of all
-// 32 lanes, then the next piece -- so each warp-wide cp.async reads 512
-// contiguous bytes, a warp-task's weights are one contiguous stream per
-// matrix, and each 64-column half of a block is 1 KiB contiguous.
-constexpr int kTileKBlockBytes = kWarp * 64;
+// Fragment-native ("tiled") weight layout: tiled_offset (fp8_gemv.cuh).  A
+// row tile's k-block is two 1 KiB halves (sp) 8 KiB apart; consecutive
+// k-blocks of a row tile are 16 KiB apart.
+constexpr int kTileKBlockStride = 2 * kTileRunBytes;
 
 MOE_D void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
@@ -351,8 +348,9 @@ MOE_D void cp_async_wait() {
 
 // acc += this lane's share of W[k-blocks kb0..kb1) . x for one task
 // TILED: the weights are in the fragment-native layout of fp8_tile_kernel
-// (tbase[st] = this lane's first piece of k-block 0 of stream st's 16-row
-// tile); otherwise row-major (arow[st][rr] = row g + 8 rr at column 16 c).
+// (tbase[st] = this lane's 16 bytes of piece rr = 0, half sp = 0 of k-block 0
+// of stream st's 16-row tile); otherwise row-major (arow[st][rr] = row
+// g + 8 rr at column 16 c).
 template <bool FIX, bool TILED>
 MOE_D void async_accumulate(float (&acc)[2][4], unsigned char* ring, const uint8_t* const (&arow)[2][2],
                             const uint8_t* const (&tbase)[2], const float* const (&srow)[2], const __half* xb,
@@ -369,7 +367,7 @@ MOE_D void async_accumulate(float (&acc)[2][4], unsigned char* ring, const uint8
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr)
           cp_async16(slot(stage, (sp * 2 + st) * 2 + rr),
-                     TILED ? tbase[st] + static_cast<int64_t>(kbi) * kTileKBlockBytes + (sp * 2 + rr) * (kWarp * 16)
+                     TILED ? tbase[st] + static_cast<int64_t>(kbi) * kTileKBlockStride + sp * kTileRunBytes + rr * (kWarp * 16)
                            : arow[st][rr] + kbi * kBlock + sp * 64);
 #pragma unroll
       for (int h = 0; h < 2; ++h)
@@ -478,7 +476,7 @@ __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(Mma
 #pragma unroll
     for (int st = 0; st < 2; ++st) {
       const int64_t tile = NS == 2 ? r0 / 16 : r0 / 16 + st;
-      tbase[st] = present ? (st == 0 ? w0 : w1) + tile * 16 * static_cast<int64_t>(K) + lane * 16 : nullptr;
+      tbase[st] = present ? (st == 0 ? w0 : w1) + tiled_offset(tile, 0, 0, nkb) + lane * 16 : nullptr;
     }
     const bool bvalid = g < len;
     const int64_t brow = bvalid ? (a.pair_row ? a.pair_row[p0 + g] : static_cast<int64_t>(p0 + g)) : 0;
@@ -578,25 +576,26 @@ __global__ void nan_free_kernel(const uint64_t* __restrict__ tables, int S, int6
   if (threadIdx.x == 0 && found) flags[s] = 0;
 }
 
-// row-major e4m3 [rows, cols] -> fragment-native tiles (kTileKBlockBytes per
-// 16-row tile and k-block); rows past `rows` (up to a multiple of 32) are zero.
+// row-major e4m3 [rows, cols] -> fragment-native tiles (tiled_offset); rows
+// past `rows` (up to a multiple of 128) are zero.  Thread q writes the q-th
+// 16 bytes of the destination: (group, kb, sp, row tile j, piece rr, lane).
 __global__ void fp8_tile_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t rows,
                                 int64_t cols) {
   const int64_t nkb = cols / kBlock;
-  const int64_t tiles = ceil_div(rows, 32) * 2;
-  const int64_t pieces = tiles * nkb * kWarp * 4;
-  for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < pieces;
+  const int64_t units = fp8_tiled_bytes_dev(rows, cols) / 16;
+  for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < units;
        q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int piece = static_cast<int>(q % 4);
-    const int lane = static_cast<int>((q / 4) % kWarp);
-    const int64_t kb = (q / (4 * kWarp)) % nkb;
-    const int64_t tile = q / (4 * kWarp * nkb);
-    const int g = lane / 4, c = lane % 4, sp = piece / 2, rr = piece % 2;
-    const int64_t row = tile * 16 + g + 8 * rr;
+    const int lane = static_cast<int>(q % kWarp);
+    const int rr = static_cast<int>((q / kWarp) % 2);
+    const int j = static_cast<int>((q / (2 * kWarp)) % 8);
+    const int sp = static_cast<int>((q / (16 * kWarp)) % 2);
+    const int64_t kb = (q / (32 * kWarp)) % nkb;
+    const int64_t group = q / (32 * kWarp * nkb);
+    const int g = lane / 4, c = lane % 4;
+    const int64_t row = group * kTileGroupRows + j * 16 + g + 8 * rr;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (row < rows) v = *reinterpret_cast<const uint4*>(src + row * cols + kb * kBlock + sp * 64 + 16 * c);
-    // piece-major inside the block: one warp-wide 16-byte access per piece is 512 contiguous bytes
-    *reinterpret_cast<uint4*>(dst + (((tile * nkb + kb) * 4 + piece) * kWarp + lane) * 16) = v;
+    *reinterpret_cast<uint4*>(dst + q * 16) = v;
   }
 }
 
@@ -873,7 +872,7 @@ cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tas
   return cudaGetLastError();
 }
 
-int64_t fp8_tiled_bytes(int64_t rows, int64_t cols) { return ceil_div(rows, 32) * 32 * cols; }
+int64_t fp8_tiled_bytes(int64_t rows, int64_t cols) { return fp8_tiled_bytes_dev(rows, cols); }
 
 cudaError_t launch_fp8_tile(const uint8_t* src, uint8_t* dst, int64_t rows, int64_t cols, cudaStream_t stream) {
   if (rows <= 0 || cols <= 0) return cudaSuccess;

@@ -12,7 +12,7 @@
 // loaded by TMA (128B swizzle, 128 rows x 64 columns per box, two boxes per
 // 256-pair tile).  B is the
 // expert's weights in the fragment-native tiled layout (fp8_mma.cu), brought
-// in by 1-D bulk copies of 1 KiB runs and converted by eight converter warps
+// in by 1-D bulk copies of 8 KiB runs and converted by eight converter warps
 // to fp16 with the k-block's scale folded in -- the exact e4m3 value times
 // the scale rounded to fp16, product rounded to fp16: a relative error of
 // at most about 2^-10 per weight -- written in the same 128B-swizzled
@@ -52,7 +52,7 @@ constexpr int kBK = 64;               // k per stage (half a scale block)
 constexpr int kStages = 3;            // load stages: two A sub-tiles + raw e4m3 weights
 constexpr int kConvBufs = 2;          // converted fp16 weight buffers
 constexpr int kATileBytes = kSubM * kBK * 2;     // 16 KiB per sub-tile, fp16, 128B-swizzled (TMA)
-constexpr int kRawBytes = kBN * kBK;             // 16 KiB e4m3: 16 row tiles x 1 KiB runs
+constexpr int kRawBytes = kBN * kBK;             // 16 KiB e4m3: two 8 KiB runs of 8 row tiles
 constexpr int kLoadBytes = 2 * kATileBytes + kRawBytes;  // 48 KiB per stage
 constexpr int kBTileBytes = kBN * kBK * 2;       // 32 KiB, fp16, 128B-swizzled (converter)
 constexpr int kTmemCols = 2 * kBN;               // the two sub-tiles' accumulators (512 columns)
@@ -109,6 +109,15 @@ MOE_D void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+// explicit shared-space accesses (the aligned smem base is a generic pointer)
+MOE_D uint4 ld_shared_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(smem_addr(p)));
+  return v;
+}
+MOE_D void st_shared_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(smem_addr(p)), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 MOE_D void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 MOE_D void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint64_t* bar) {
@@ -244,18 +253,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       uint32_t it = 0;
       for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
         const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
-        // 16 row tiles of 16 rows: gate/up = 8 from each matrix, down = 16 consecutive
-        const uint8_t* wbase[2];
-        int tile0[2];
-        if (GATEUP) {
-          wbase[0] = reinterpret_cast<const uint8_t*>(a.w0[tr.seg]);
-          wbase[1] = reinterpret_cast<const uint8_t*>(a.w1[tr.seg]);
-          tile0[0] = tile0[1] = tr.nt * 8;
-        } else {
-          wbase[0] = wbase[1] = reinterpret_cast<const uint8_t*>(a.w0[tr.seg]);
-          tile0[0] = tr.nt * 16;
-          tile0[1] = tr.nt * 16 + 8;
-        }
+        // two 128-row groups (8 row tiles each, one 8 KiB run per k-step):
+        // gate/up = group nt of each matrix, down = groups 2 nt, 2 nt + 1
+        const uint8_t* w0 = reinterpret_cast<const uint8_t*>(a.w0[tr.seg]);
+        const uint8_t* wbase[2] = {w0, GATEUP ? reinterpret_cast<const uint8_t*>(a.w1[tr.seg]) : w0};
+        const int64_t tile0[2] = {GATEUP ? tr.nt * 8 : tr.nt * 16, GATEUP ? tr.nt * 8 : tr.nt * 16 + 8};
         for (int kh = 0; kh < nkh && !*abort; ++kh, ++it) {
           const int s = it % kStages;
           if (it >= kStages && !wait_or_abort(&bars->empty[s], ((it / kStages) - 1) & 1, abort)) break;
@@ -266,11 +268,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
           if (two) tma_load_2d(a_tile(s, 1), &tmap_a, kh * kBK, tr.row0 + kSubM, &bars->full[s]);
           const int kb = kh / 2, sp = kh % 2;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int half = i / 8;
-            const uint8_t* blk = wbase[half] + (static_cast<int64_t>(tile0[half] + i % 8) * nkb + kb) * 2048;
-            bulk_copy_g2s(raw_tile(s) + i * 1024, blk + sp * 1024, 1024, &bars->full[s]);
-          }
+          for (int h = 0; h < 2; ++h)
+            bulk_copy_g2s(raw_tile(s) + h * kTileRunBytes, wbase[h] + tiled_offset(tile0[h], kb, sp, nkb),
+                          kTileRunBytes, &bars->full[s]);
         }
       }
       // every copy issued lands before the CTA may exit
@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
           const int run = u / 64, rr = (u / kWarp) % 2, ul = u % kWarp;
           const int g = ul / 4, c = ul % 4;
           const int n = 16 * run + g + 8 * rr;  // tile row 0..255
-          uint4 v = *reinterpret_cast<const uint4*>(raw + u * 16);
+          uint4 v = ld_shared_v4(raw + u * 16);
           if (fix) {
             v.x = e4m3x4_nan_to_zero(v.x);
             v.y = e4m3x4_nan_to_zero(v.y);
@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
           for (int j = 0; j < 2; ++j) {
             const int chunk = 2 * c + j;
             unsigned char* dst = bt + (n / 8) * 1024 + (n % 8) * 128 + ((chunk ^ (n % 8)) * 16);
-            *reinterpret_cast<uint4*>(dst) = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+            st_shared_v4(dst, h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
           }
         }
         fence_proxy_async_shared();  // generic-proxy writes -> visible to the tensor core (async proxy)
