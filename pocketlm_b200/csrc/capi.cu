@@ -244,6 +244,11 @@ int moe::route_impl(const void* hidden, int hd, const void* w, int wd, const flo
                                         static_cast<int>(E), stream);
     if (cerr != cudaErrorNotSupported) MOE_CUDA(cerr, "router logits");
   }
+  if (T > 256) {
+    // prefill-sized batches: the tcgen05 GEMM when both operands are 16-bit of one type
+    cerr = launch_router_logits_tc(hidden, hd, w, wd, logits, T, H, E, &nparts, stream);
+    if (cerr != cudaErrorNotSupported) MOE_CUDA(cerr, "router logits");
+  }
   if (cerr != cudaErrorNotSupported) {
     // done
   } else if (T > 256 && router_split_is_mma(hidden, hd, w, wd, static_cast<int>(H))) {
@@ -619,6 +624,7 @@ struct LayerPlan {
   __half* a16;
   float* a16scale;
   int32_t* mprefix;
+  int32_t* bucket_scratch;  // multi-CTA dispatch: per-block bucket counts
 };
 
 // Token counts from which the whole-layer call runs the prefill GEMM (when
@@ -634,6 +640,7 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
     l.logits = p.take<float>(static_cast<int64_t>(std::max(1, router_split_parts(static_cast<int>(H)))) * T * E);
   l.ids32 = p.take<int32_t>(T * k);
   l.wts = p.take<float>(T * k);
+  l.bucket_scratch = p.take<int32_t>(bucket_scratch_ints(T * k, static_cast<int>(E)));
   const int64_t pairs = T * k + (shared ? T : 0);
   l.m = plan_mlp(p, pairs, E + 1, T * k, I, H, nt, true);
   l.x16 = p.take<__half>(T * H);
@@ -788,6 +795,7 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   ba.k = static_cast<int>(k); ba.key_lo = 0; ba.n_buckets = static_cast<int>(E);
   ba.bucket_offset = l.m.seg_offset; ba.pair_row = l.m.pair_row; ba.pair_weight = l.m.pair_weight;
   ba.pair_entry = l.m.pair_entry; ba.entry_pair = l.m.entry_pair; ba.tail = has_shared ? static_cast<int>(T) : 0;
+  ba.block_counts = l.bucket_scratch;
   ChunkArgs ca{l.m.seg_offset, static_cast<int>(S), chunk, l.m.chunk_seg, l.m.chunk_start, l.m.chunk_len,
                l.m.n_chunks};
   bool chunks_ready = false;
@@ -866,12 +874,16 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
 // home combine (the exchange itself is the caller's all-to-all)
 // ---------------------------------------------------------------------------
 
+// ranks up to which the dispatch workspace holds the multi-CTA bucket counts
+constexpr int kEpMaxScratchRanks = 64;
+
 int64_t moe_ep_dispatch_workspace_bytes(int64_t tokens, int64_t top_k) {
   if (tokens <= 0 || top_k <= 0) return -1;
   Plan p;
   p.take<int32_t>(tokens * top_k);
   p.take<int32_t>(tokens * top_k);
   p.take<int32_t>(tokens * top_k);
+  p.take<int32_t>(bucket_scratch_ints(tokens * top_k, kEpMaxScratchRanks));
   return static_cast<int64_t>(p.used());
 }
 
@@ -892,12 +904,14 @@ int moe_ep_dispatch_pack(const int64_t* ids, const float* weights, const uint16_
   int32_t* keys = plan.take<int32_t>(n);
   int32_t* pos_token = plan.take<int32_t>(n);
   int32_t* pos_entry = plan.take<int32_t>(n);
+  int32_t* block_counts = plan.take<int32_t>(bucket_scratch_ints(n, kEpMaxScratchRanks));
   ep_rank_keys_kernel<<<grid_for(n), 256, 0, s>>>(ids, n, num_experts / world, world, keys);
   MOE_CUDA(cudaGetLastError(), "rank keys");
   BucketArgs ba{};
   ba.keys = keys; ba.rows = nullptr; ba.weights = weights; ba.n = static_cast<int>(n); ba.k = static_cast<int>(top_k);
   ba.key_lo = 0; ba.n_buckets = static_cast<int>(world); ba.bucket_offset = send_offsets; ba.pair_row = pos_token;
   ba.pair_weight = pos_weight; ba.pair_entry = pos_entry; ba.entry_pair = entry_pos; ba.tail = 0;
+  ba.block_counts = world <= kEpMaxScratchRanks ? block_counts : nullptr;
   MOE_CUDA(launch_bucket(ba, s), "rank buckets");
   const int64_t vec = hidden_dim % 8 == 0 && aligned16(hidden_bf16) && aligned16(send_rows) ? 1 : 0;
   ep_gather_kernel<<<grid_for(n * 32, 256), 256, 0, s>>>(hidden_bf16, ids, keys, pos_token, pos_entry, n, hidden_dim,
@@ -937,6 +951,7 @@ int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int
   ba.keys = row_expert; ba.rows = nullptr; ba.weights = nullptr; ba.n = static_cast<int>(R); ba.k = 1;
   ba.key_lo = 0; ba.n_buckets = static_cast<int>(S); ba.bucket_offset = l.m.seg_offset; ba.pair_row = l.m.pair_row;
   ba.pair_weight = l.m.pair_weight; ba.pair_entry = l.m.pair_entry; ba.entry_pair = l.m.entry_pair; ba.tail = 0;
+  ba.block_counts = l.bucket_scratch;
   MOE_CUDA(launch_bucket(ba, s), "expert buckets");
   Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
   int code = run_expert_stages_mma(t, rows_bf16, true, l, R, R, S, I, H, false, nan_free, s, weight_layout);

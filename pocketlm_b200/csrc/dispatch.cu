@@ -76,6 +76,116 @@ cudaError_t launch_route_dispatch(const RouteDispatchArgs& a, cudaStream_t strea
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- multi-CTA
+// The same stable bucketing for large n in three launches: every block of
+// kBucketThreads consecutive entries counts its keys; one CTA turns the
+// counts into bucket offsets and per-block starting slots (bucket-major, so
+// entries keep their order inside a bucket); every block then places its
+// entries with the shared-memory bitmask rank of the one-CTA kernel.
+
+__global__ void __launch_bounds__(kBucketThreads) bucket_count_kernel(BucketArgs a) {
+  extern __shared__ int32_t cnt[];
+  for (int b = threadIdx.x; b < a.n_buckets; b += kBucketThreads) cnt[b] = 0;
+  __syncthreads();
+  const int i = blockIdx.x * kBucketThreads + threadIdx.x;
+  if (i < a.n) {
+    const int key = a.keys[i] - a.key_lo;
+    if (key >= 0 && key < a.n_buckets) atomicAdd(&cnt[key], 1);
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < a.n_buckets; b += kBucketThreads)
+    a.block_counts[static_cast<int64_t>(blockIdx.x) * a.n_buckets + b] = cnt[b];
+}
+
+// One CTA: bucket totals -> offsets; block_counts[blk][b] -> the slot where
+// block blk's first entry of bucket b goes.
+__global__ void __launch_bounds__(kBucketThreads) bucket_offsets_kernel(BucketArgs a, int blocks) {
+  extern __shared__ int32_t tot[];
+  const int tid = threadIdx.x;
+  for (int b = tid; b < a.n_buckets; b += kBucketThreads) {
+    int s = 0;
+    for (int blk = 0; blk < blocks; ++blk) s += a.block_counts[static_cast<int64_t>(blk) * a.n_buckets + b];
+    tot[b] = s;
+  }
+  __syncthreads();
+  const int per = static_cast<int>(ceil_div(a.n_buckets, kBucketThreads));
+  const int b_lo = min(a.n_buckets, tid * per), b_hi = min(a.n_buckets, b_lo + per);
+  int mine = 0;
+  for (int b = b_lo; b < b_hi; ++b) mine += tot[b];
+  int running = 0;
+  int off = block_exclusive_scan(mine, &running);
+  for (int b = b_lo; b < b_hi; ++b) {
+    a.bucket_offset[b] = off;
+    if (a.counts) a.counts[b] = tot[b];
+    int slot = off;
+    for (int blk = 0; blk < blocks; ++blk) {
+      int32_t* c = a.block_counts + static_cast<int64_t>(blk) * a.n_buckets + b;
+      const int n = *c;
+      *c = slot;
+      slot += n;
+    }
+    off += tot[b];
+  }
+  if (tid == 0) {
+    a.bucket_offset[a.n_buckets] = running;
+    if (a.tail > 0) a.bucket_offset[a.n_buckets + 1] = running + a.tail;
+    if (a.total) *a.total = running + (a.tail > 0 ? a.tail : 0);
+  }
+}
+
+__global__ void __launch_bounds__(kBucketThreads) bucket_scatter_kernel(BucketArgs a) {
+  extern __shared__ uint32_t mask[];  // [n_buckets][kWindowWords]
+  const int tid = threadIdx.x;
+  for (int j = tid; j < a.n_buckets * kWindowWords; j += kBucketThreads) mask[j] = 0;
+  __syncthreads();
+  const int i = blockIdx.x * kBucketThreads + tid;
+  int key = -1;
+  if (i < a.n) {
+    key = a.keys[i] - a.key_lo;
+    if (key >= 0 && key < a.n_buckets) atomicOr(&mask[key * kWindowWords + tid / 32], 1u << (tid % 32));
+    else key = -1;
+  }
+  __syncthreads();
+  if (key >= 0) {
+    const uint32_t* mk = mask + key * kWindowWords;
+    int rank = __popc(mk[tid / 32] & ((1u << (tid % 32)) - 1u));
+    for (int wd = 0; wd < tid / 32; ++wd) rank += __popc(mk[wd]);
+    const int p = a.block_counts[static_cast<int64_t>(blockIdx.x) * a.n_buckets + key] + rank;
+    a.pair_row[p] = a.rows ? a.rows[i] : i / a.k;
+    if (a.pair_weight) a.pair_weight[p] = a.weights ? a.weights[i] : 1.0f;
+    if (a.pair_entry) a.pair_entry[p] = i;
+    if (a.entry_pair) a.entry_pair[i] = p;
+  } else if (i < a.n && a.entry_pair) {
+    a.entry_pair[i] = -1;
+  }
+}
+
+// the appended bucket (rows 0 .. tail - 1) after the kept entries
+__global__ void bucket_tail_kernel(BucketArgs a) {
+  const int first = a.bucket_offset[a.n_buckets];
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < a.tail; r += gridDim.x * blockDim.x) {
+    a.pair_row[first + r] = r;
+    if (a.pair_weight) a.pair_weight[first + r] = 1.0f;
+    if (a.pair_entry) a.pair_entry[first + r] = -1;
+  }
+}
+
+int64_t bucket_scratch_ints(int64_t n, int n_buckets) { return ceil_div(n, kBucketThreads) * n_buckets; }
+
+static cudaError_t launch_bucket_multi(const BucketArgs& a, cudaStream_t stream) {
+  const int blocks = static_cast<int>(ceil_div(a.n, kBucketThreads));
+  const size_t cnt_smem = static_cast<size_t>(a.n_buckets) * sizeof(int32_t);
+  const size_t mask_smem = static_cast<size_t>(a.n_buckets) * kWindowWords * sizeof(uint32_t);
+  cudaError_t err = cudaFuncSetAttribute(bucket_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(mask_smem));
+  if (err != cudaSuccess) return err;
+  bucket_count_kernel<<<blocks, kBucketThreads, cnt_smem, stream>>>(a);
+  bucket_offsets_kernel<<<1, kBucketThreads, cnt_smem, stream>>>(a, blocks);
+  bucket_scatter_kernel<<<blocks, kBucketThreads, mask_smem, stream>>>(a);
+  if (a.tail > 0) bucket_tail_kernel<<<static_cast<unsigned>(ceil_div(a.tail, 256)), 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
 size_t bucket_smem_bytes(int n_buckets) {
   return static_cast<size_t>(n_buckets) * kWindowWords * sizeof(uint32_t) +
          static_cast<size_t>(2 * n_buckets + 1) * sizeof(int32_t);
@@ -84,6 +194,7 @@ size_t bucket_smem_bytes(int n_buckets) {
 cudaError_t launch_bucket(const BucketArgs& a, cudaStream_t stream) {
   const size_t smem = bucket_smem_bytes(a.n_buckets);
   if (a.n_buckets <= 0 || a.n_buckets > kMaxBuckets) return cudaErrorInvalidValue;
+  if (a.block_counts && a.n > 2 * kBucketThreads) return launch_bucket_multi(a, stream);
   cudaError_t err = cudaFuncSetAttribute(bucket_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return err;

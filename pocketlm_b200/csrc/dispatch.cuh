@@ -24,7 +24,11 @@ struct BucketArgs {
   int32_t* total;          // [1] or null
   int tail;                // > 0: append one more bucket holding rows 0..tail-1, weight 1
                            // (the shared expert); bucket_offset then has n_buckets + 2 entries
+  int32_t* block_counts;   // or null: bucket_scratch_ints(n, n_buckets) ints of workspace for
+                           // the multi-CTA path (large n); null keeps the one-CTA kernel
 };
+// Workspace ints of BucketArgs::block_counts: per-block bucket counts.
+int64_t bucket_scratch_ints(int64_t n, int n_buckets);
 
 struct ChunkArgs {
   const int32_t* seg_offset;  // [n_segments + 1]

@@ -41,6 +41,7 @@
 #include "common.cuh"
 #include "fp8_gemv.cuh"
 #include "prefill_gemm.cuh"
+#include "router.cuh"
 
 namespace moe {
 namespace {
@@ -481,6 +482,136 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// ------------------------------------------------------- router logits
+// Prefill-sized router GEMM on tcgen05: partial[z][t][e] = sum over the z-th
+// k-range of x[t, k] * w[e, k], x and w both bf16 or both f16 (products
+// exact in fp32, fp32 accumulation in tensor memory) -- the reference's fp32
+// F.linear of the gate (fp8_source.py:1547) up to the order of the sums.
+// One CTA per (128-token tile, expert tile of <= 256, k-range): TMA loads
+// both operands (128B swizzle, 64 columns per stage, four stages), one
+// thread issues M = 128 x N MMAs, four warps drain TMEM to the partials.
+constexpr int kRStages = 4;
+constexpr int kRATile = 128 * 64 * 2;   // 16 KiB
+constexpr int kRBTile = 256 * 64 * 2;   // 32 KiB (up to 256 experts)
+constexpr int kRThreads = 6 * kWarp;    // warps 0-3 epilogue, 4 producer, 5 MMA + TMEM
+struct RBarriers {
+  uint64_t full[kRStages];
+  uint64_t empty[kRStages];
+  uint64_t tfull;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t kRSmemBytes = 1024 + static_cast<size_t>(kRStages) * (kRATile + kRBTile) + sizeof(RBarriers);
+static_assert(kRSmemBytes <= 232448, "shared memory per block");
+
+template <bool BF16>
+__global__ void __launch_bounds__(kRThreads, 1) router_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                                 const __grid_constant__ CUtensorMap tmap_w,
+                                                                 float* partial, int tokens, int experts, int ncols,
+                                                                 int n_tiles, int nkh, int parts) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  auto a_tile = [&](int s) { return smem + s * (kRATile + kRBTile); };
+  auto b_tile = [&](int s) { return smem + s * (kRATile + kRBTile) + kRATile; };
+  RBarriers* bars = reinterpret_cast<RBarriers*>(smem + kRStages * (kRATile + kRBTile));
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  volatile int* abort = &bars->abort;
+  const int m0 = (blockIdx.x / n_tiles) * 128, n0 = (blockIdx.x % n_tiles) * ncols;
+  const int z = blockIdx.y;
+  const int kh0 = static_cast<int>(static_cast<int64_t>(z) * nkh / parts);
+  const int kh1 = static_cast<int>(static_cast<int64_t>(z + 1) * nkh / parts);
+  const uint32_t b_bytes = static_cast<uint32_t>(ncols) * 64 * 2;
+  const uint32_t idesc = (1u << 4) | (BF16 ? (1u << 7) | (1u << 10) : 0u) |
+                         (static_cast<uint32_t>(ncols >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->tfull, 1);
+    mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(&bars->tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int kh = kh0; kh < kh1 && !*abort; ++kh, ++it) {
+        const int s = it % kRStages;
+        if (it >= kRStages && !wait_or_abort(&bars->empty[s], ((it / kRStages) - 1) & 1, abort)) break;
+        mbar_arrive_expect_tx(&bars->full[s], kRATile + b_bytes);
+        tma_load_2d(a_tile(s), &tmap_x, kh * 64, m0, &bars->full[s]);
+        tma_load_2d(b_tile(s), &tmap_w, kh * 64, n0, &bars->full[s]);
+      }
+      for (uint32_t j = it > kRStages ? it - kRStages : 0; j < it; ++j)
+        mbar_wait(&bars->full[j % kRStages], (j / kRStages) & 1, kCodeWait);
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int kh = kh0; kh < kh1; ++kh, ++it) {
+        const int s = it % kRStages;
+        if (!wait_or_abort(&bars->full[s], (it / kRStages) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_addr(a_tile(s)), sb = smem_addr(b_tile(s));
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_f16(tmem, sw128_desc(sa + k * 32), sw128_desc(sb + k * 32), idesc, (it | k) != 0);
+        umma_commit(&bars->empty[s]);
+      }
+      if (ok) umma_commit(&bars->tfull);
+      umma_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, kCodeWait);
+    }
+  } else {
+    // epilogue: warp w drains TMEM lanes 32w .. 32w + 31 (tokens m0 + 32w + lane)
+    if (wait_or_abort(&bars->tfull, 0, abort)) {
+      tc_fence_after();
+      const int t = m0 + warp * kWarp + lane;
+      float* row = partial + (static_cast<int64_t>(z) * tokens + t) * experts + n0;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * kWarp) << 16);
+      const bool vec = experts % 4 == 0;
+#pragma unroll 1
+      for (int c0 = 0; c0 < ncols; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + c0, r);
+        tmem_ld_wait();
+        if (t < tokens) {
+          if (vec && n0 + c0 + 16 <= experts) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<float4*>(row + c0 + j) = make_float4(
+                  __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (n0 + c0 + j < experts) row[c0 + j] = __uint_as_float(r[j]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc(tmem, 256);
+}
+
 }  // namespace
 
 size_t prefill_smem_bytes() { return kSmemBytes; }
@@ -522,6 +653,56 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, bool gateup, int64_t max_t
   if (err != cudaSuccess) return err;
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(gemv_grid_ctas(), max_tiles)));
   kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmap, a);
+  return cudaGetLastError();
+}
+
+int router_tc_parts(int64_t tokens, int64_t hidden, int64_t experts) {
+  const int64_t ncols = experts >= 256 ? 256 : (experts + 15) / 16 * 16;
+  const int64_t tiles = ceil_div(tokens, 128) * ceil_div(experts, ncols);
+  const int64_t nkh = hidden / 64;
+  // fill the SMs with k-ranges of at least eight stages, at most kMaxRouterTcParts ranges
+  int64_t parts = std::max<int64_t>(1, gemv_grid_ctas() / std::max<int64_t>(1, tiles));
+  // (and no more than the split-K router's parts, which size the callers' partial buffers)
+  parts = std::min<int64_t>({parts, kMaxRouterTcParts, std::max<int64_t>(1, nkh / 8),
+                             std::max<int64_t>(1, router_split_parts(static_cast<int>(hidden)))});
+  return static_cast<int>(parts);
+}
+
+cudaError_t launch_router_logits_tc(const void* x, int xdtype, const void* w, int wdtype, float* partial,
+                                    int64_t tokens, int64_t hidden, int64_t experts, int* nparts,
+                                    cudaStream_t stream) {
+  // both operands bf16 or both f16, 16-byte aligned rows, whole 64-column stages
+  if (xdtype != wdtype || (xdtype != kDtypeBF16 && xdtype != kDtypeF16)) return cudaErrorNotSupported;
+  if (hidden % 64 != 0 || tokens <= 0 || experts <= 0 || experts > 2048) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15u) return cudaErrorNotSupported;
+  auto encode = encode_fn();
+  if (!encode) return cudaErrorNotSupported;
+  const bool bf16 = xdtype == kDtypeBF16;
+  const int ncols = experts >= 256 ? 256 : static_cast<int>((experts + 15) / 16 * 16);
+  const int n_tiles = static_cast<int>(ceil_div(experts, ncols));
+  const int parts = router_tc_parts(tokens, hidden, experts);
+  const CUtensorMapDataType dt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tx, tw;
+  const cuuint32_t estr[2] = {1, 1};
+  const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(hidden), static_cast<cuuint64_t>(tokens)};
+  const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(hidden), static_cast<cuuint64_t>(experts)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(hidden) * 2};
+  const cuuint32_t xbox[2] = {64, 128};
+  const cuuint32_t wbox[2] = {64, static_cast<cuuint32_t>(ncols)};
+  if (encode(&tx, dt, 2, const_cast<void*>(x), xdims, strides, xbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+          CUDA_SUCCESS ||
+      encode(&tw, dt, 2, const_cast<void*>(w), wdims, strides, wbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+          CUDA_SUCCESS)
+    return cudaErrorNotSupported;
+  auto kernel = bf16 ? router_tc_kernel<true> : router_tc_kernel<false>;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kRSmemBytes));
+  if (err != cudaSuccess) return err;
+  dim3 grid(static_cast<unsigned>(ceil_div(tokens, 128) * n_tiles), static_cast<unsigned>(parts));
+  kernel<<<grid, kRThreads, kRSmemBytes, stream>>>(tx, tw, partial, static_cast<int>(tokens), static_cast<int>(experts),
+                                                   ncols, n_tiles, static_cast<int>(hidden / 64), parts);
+  *nparts = parts;
   return cudaGetLastError();
 }
 

@@ -37,4 +37,14 @@ cudaError_t launch_gather_rows(const __half* x16, const float* xscale, const int
 cudaError_t launch_prefill_gemm(const PrefillArgs& a, bool gateup, int64_t max_tiles, cudaStream_t stream);
 int read_and_clear_prefill_device_error(cudaStream_t stream);
 
+// Router logits of prefill-sized batches on tcgen05 (prefill_gemm.cu):
+// *nparts k-range partials [nparts][tokens][experts] (summed in part order by
+// the selection).  cudaErrorNotSupported unless x and w are both bf16 or both
+// f16 (dtype codes of router.cuh), 16-byte aligned, hidden % 64 == 0.
+constexpr int kMaxRouterTcParts = 16;
+int router_tc_parts(int64_t tokens, int64_t hidden, int64_t experts);
+cudaError_t launch_router_logits_tc(const void* x, int xdtype, const void* w, int wdtype, float* partial,
+                                    int64_t tokens, int64_t hidden, int64_t experts, int* nparts,
+                                    cudaStream_t stream);
+
 }  // namespace moe

@@ -57,6 +57,9 @@ def test_sigmoid_bias_router_known_answer(cuda_device):
     (synth.C1_TINY, 64, 0, "uniform"),
     (synth.C2_DSV3, 64, 3, "uniform"),
     (synth.C2_DSV3, 512, 4, "zipf"),
+    # prefill-sized batches take the tcgen05 router: ragged token tiles, 16 experts (N = 16)
+    (synth.C2_DSV3, 1000, 6, "uniform"),
+    (synth.C1_TINY, 700, 5, "zipf"),
 ])
 def test_grouped_router_matches_oracle(cuda_device, cfg, tokens, seed, bias):
     layer = synth.make_fp8_layer(cfg, seed=seed, device="cuda", bias_kind=bias, experts=[])
