@@ -75,8 +75,10 @@ struct Barriers {
   uint32_t tmem_base;
   int abort;
 };
+constexpr int kStageBytes = kWarp * 16 * 4;  // epilogue staging per warp: 32 rows x 16 fp32
 constexpr size_t kSmemBytes = 1024 /* alignment slack */ + static_cast<size_t>(kStages) * kLoadBytes +
-                              static_cast<size_t>(kConvBufs) * kBTileBytes + sizeof(Barriers);
+                              static_cast<size_t>(kConvBufs) * kBTileBytes +
+                              static_cast<size_t>(kEpiWarps) * kStageBytes + sizeof(Barriers);
 static_assert(kSmemBytes <= 232448, "shared memory per block");
 
 // ---------------------------------------------------------------- PTX
@@ -215,7 +217,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
   auto a_tile = [&](int s, int h) { return smem + s * kLoadBytes + h * kATileBytes; };
   auto raw_tile = [&](int s) { return smem + s * kLoadBytes + 2 * kATileBytes; };
   auto b_tile = [&](int b) { return smem + kStages * kLoadBytes + b * kBTileBytes; };
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kLoadBytes + kConvBufs * kBTileBytes);
+  unsigned char* stage_buf = smem + kStages * kLoadBytes + kConvBufs * kBTileBytes;  // epilogue staging
+  Barriers* bars = reinterpret_cast<Barriers*>(stage_buf + kEpiWarps * kStageBytes);
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   volatile int* abort = &bars->abort;
 
@@ -248,12 +251,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
   const int64_t tiles = static_cast<int64_t>(a.mprefix[a.n_segments]) * n_tiles;
   const int nkh = K / kBK;  // pipeline stages per tile
   const int nkb = K / 128;  // k-blocks (scale columns, tiled-layout blocks)
+  // an expert without (16-byte aligned) weights and scales is skipped by every
+  // role alike; the epilogue writes its pairs' rows as zeros
+  auto present = [&](int seg) {
+    const uint64_t w0 = a.w0[seg], w1 = GATEUP ? a.w1[seg] : w0;
+    return w0 && w1 && a.s0[seg] && (!GATEUP || a.s1[seg]) && ((w0 | w1) & 15u) == 0;
+  };
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
       uint32_t it = 0;
       for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
         const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
+        if (!present(tr.seg)) continue;
         // two 128-row groups (8 row tiles each, one 8 KiB run per k-step):
         // gate/up = group nt of each matrix, down = groups 2 nt, 2 nt + 1
         const uint8_t* w0 = reinterpret_cast<const uint8_t*>(a.w0[tr.seg]);
@@ -284,6 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
     uint32_t it = 0;
     for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
       const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
+      if (!present(tr.seg)) continue;
       const bool fix = a.nanfix && !(a.nan_free && a.nan_free[tr.seg]);
       // scale rows of the two 128-row halves of the tile
       const float* sb0 = reinterpret_cast<const float*>(a.s0[tr.seg]);
@@ -367,8 +378,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
     if (lane == 0) {
       uint32_t it = 0, ti = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < tiles && ok && !*abort; t += gridDim.x, ++ti) {
+      for (int64_t t = blockIdx.x; t < tiles && ok && !*abort; t += gridDim.x) {
         const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
+        if (!present(tr.seg)) continue;
         const bool two = tr.rows > kSubM;
         // the epilogue has drained the previous tile's accumulators
         if (ti >= 1 && !wait_or_abort(&bars->tempty, (ti - 1) & 1, abort)) break;
@@ -392,6 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
           umma_commit(&bars->cempty[b]);  // and the converted buffer
         }
         if (ok) umma_commit(&bars->tfull);
+        ++ti;
       }
       // every MMA this thread issued has completed before TMEM is released
       umma_commit(&bars->drain);
@@ -401,10 +414,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
     // warp w drains TMEM lanes 32 (w % 4) .. + 31 of sub-tile w / 4 (columns 256 (w / 4) ..)
     uint32_t ti = 0;
     const int half = warp / 4, quad = warp % 4;
+    unsigned char* stage = stage_buf + warp * kStageBytes;
     const int row_in_tile = half * kSubM + quad * kWarp + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quad * kWarp) << 16;
-    for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x, ++ti) {
+    for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
       const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
+      if (!present(tr.seg)) {
+        // absent expert: its pairs' output rows are zero
+        if (row_in_tile < tr.rows) {
+          float4* out = reinterpret_cast<float4*>(a.out + (tr.row0 + row_in_tile) * static_cast<int64_t>(N) +
+                                                  tr.nt * (GATEUP ? kBN / 2 : kBN));
+          for (int j = 0; j < (GATEUP ? kBN / 2 : kBN) / 4; ++j) out[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        continue;
+      }
       if (!wait_or_abort(&bars->tfull, ti & 1, abort)) break;
       tc_fence_after();
       // the second sub-tile's accumulator was not written for tiles of <= 128 pairs
@@ -413,8 +436,30 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       const bool valid = row_in_tile < tr.rows;
       const int64_t p = tr.row0 + row_in_tile;
       const float xs = valid ? a.ascale[p] : 0.0f;
+      // down (256 fp32 per row): 16 columns of the warp's 32 rows at a time
+      // leave through its 2 KiB staging buffer -- lane = row on the way in,
+      // four lanes per row (64 contiguous bytes) on the way out; 16-byte
+      // slots XOR-swizzled by row so both phases are free of bank conflicts
+      const int row_base = half * kSubM + quad * kWarp;  // the warp's first row in the tile
+      float* out_base = a.out + (tr.row0 + row_base) * static_cast<int64_t>(N) + tr.nt * (GATEUP ? kBN / 2 : kBN);
+      auto emit16 = [&](const float (&v)[16], int c0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          st_shared_v4(stage + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16), __float_as_uint(v[4 * j]),
+                       __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rr = lane / 4 + 8 * i, j = lane % 4;
+          const uint4 w = ld_shared_v4(stage + rr * 64 + ((j ^ ((rr >> 1) & 3)) * 16));
+          if (row_base + rr < tr.rows)
+            *reinterpret_cast<uint4*>(out_base + rr * static_cast<int64_t>(N) + c0 + 4 * j) = w;
+        }
+        __syncwarp();
+      };
       if (!live) {
       } else if (GATEUP) {
+        // 128 SwiGLU outputs per row: direct 16-byte stores from each row's lane
         float* out = a.out + p * N + tr.nt * (kBN / 2);
 #pragma unroll 1
         for (int c0 = 0; c0 < kBN / 2; c0 += 16) {
@@ -437,29 +482,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
           }
         }
       } else {
-        float* out = a.out + p * N + tr.nt * kBN;
 #pragma unroll 1
         for (int c0 = 0; c0 < kBN; c0 += 32) {
           uint32_t d0[16], d1[16];
           tmem_ld16(taddr + c0, d0);
           tmem_ld16(taddr + c0 + 16, d1);
           tmem_ld_wait();
-          if (valid) {
+          float o[16];
 #pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              *reinterpret_cast<float4*>(out + c0 + j) =
-                  make_float4(__uint_as_float(d0[j]) * xs, __uint_as_float(d0[j + 1]) * xs,
-                              __uint_as_float(d0[j + 2]) * xs, __uint_as_float(d0[j + 3]) * xs);
-              *reinterpret_cast<float4*>(out + c0 + 16 + j) =
-                  make_float4(__uint_as_float(d1[j]) * xs, __uint_as_float(d1[j + 1]) * xs,
-                              __uint_as_float(d1[j + 2]) * xs, __uint_as_float(d1[j + 3]) * xs);
-            }
-          }
+          for (int q = 0; q < 16; ++q) o[q] = __uint_as_float(d0[q]) * xs;
+          emit16(o, c0);
+#pragma unroll
+          for (int q = 0; q < 16; ++q) o[q] = __uint_as_float(d1[q]) * xs;
+          emit16(o, c0 + 16);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tempty);
+      ++ti;
     }
   }
 

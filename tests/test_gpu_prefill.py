@@ -70,3 +70,18 @@ def test_prefill_dsv3_shape(cuda_device):
     bad, excused = id_mismatches(ids[:n], route)
     assert bad == excused
     assert rel_l2(out[:n], expected) <= REL_L2_GATE and cos_dist(out[:n], expected) <= COS_GATE
+
+
+def test_prefill_skips_absent_experts_like_the_gemv(cuda_device):
+    """A partial layer (some experts not resident, null table entries): the
+    prefill GEMM skips their tiles in every role and writes their pairs'
+    rows as zeros, as the GEMV path leaves them -- same output."""
+    cfg = C_MID
+    resident = [e for e in range(cfg.n_routed) if e % 3 != 1] + [cfg.n_routed]
+    layer = synth.make_fp8_layer(cfg, seed=55, device="cuda", experts=resident)
+    x = synth.make_hidden(1024, cfg.hidden, seed=56, device="cuda")
+    out = DsMoELayerGPU(layer, allow_partial=True).forward(x).clone()
+    gemv = DsMoELayerGPU(layer, allow_partial=True, tiled=False).forward(x).clone()
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    assert rel_l2(out, gemv) <= 2e-3 and cos_dist(out, gemv) <= 1e-5
