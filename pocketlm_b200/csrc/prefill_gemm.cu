@@ -62,6 +62,7 @@ constexpr int kConvThreads = kConvWarps * kWarp;
 constexpr int kProducerWarp = kEpiWarps + kConvWarps, kMmaWarp = kProducerWarp + 1, kAllocWarp = kProducerWarp + 2;
 constexpr int kThreads = (kAllocWarp + 1) * kWarp;
 constexpr int kCodeWait = 32;
+constexpr int kPrefetchStages = 4;  // weight runs requested into L2 this many stages ahead
 constexpr int kScaleRegs = 4;  // converter scale cache: registers per lane and half
 
 struct Barriers {
@@ -121,6 +122,10 @@ MOE_D uint4 ld_shared_v4(const void* p) {
 }
 MOE_D void st_shared_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(smem_addr(p)), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+// warm L2 with a weight run a few stages ahead of its bulk copy (no shared memory held)
+MOE_D void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 MOE_D void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 MOE_D void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint64_t* bar) {
@@ -269,8 +274,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         const uint8_t* w0 = reinterpret_cast<const uint8_t*>(a.w0[tr.seg]);
         const uint8_t* wbase[2] = {w0, GATEUP ? reinterpret_cast<const uint8_t*>(a.w1[tr.seg]) : w0};
         const int64_t tile0[2] = {GATEUP ? tr.nt * 8 : tr.nt * 16, GATEUP ? tr.nt * 8 : tr.nt * 16 + 8};
+        auto prefetch = [&](int kq) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            bulk_prefetch_l2(wbase[h] + tiled_offset(tile0[h], kq / 2, kq % 2, nkb), kTileRunBytes);
+        };
+        for (int kq = 0; kq < kPrefetchStages && kq < nkh; ++kq) prefetch(kq);
         for (int kh = 0; kh < nkh && !*abort; ++kh, ++it) {
           const int s = it % kStages;
+          if (kh + kPrefetchStages < nkh) prefetch(kh + kPrefetchStages);
           if (it >= kStages && !wait_or_abort(&bars->empty[s], ((it / kStages) - 1) & 1, abort)) break;
           // the second sub-tile only when the tile has more than 128 pairs
           const bool two = tr.rows > kSubM;
