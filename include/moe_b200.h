@@ -203,10 +203,13 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t tokens, i
 /* Fragment-native weight layout (no reference counterpart), weight_layout 1
  * of moe_ds_moe_layer_fp8: moe_fp8_tile_weights copies a row-major e4m3
  * [rows, cols] matrix (cols % 128 == 0) into moe_fp8_tiled_bytes(rows, cols)
- * bytes laid out so that each 16-row x 128-column block sits in 2 KiB in the
- * order the decode GEMV's lanes read it -- every warp then streams one
- * contiguous range per matrix.  Same bytes, same results; the block scales
- * keep their layout.  Tables for weight_layout 1 point at tiled copies. */
+ * bytes (rows padded to a multiple of 128 with zeros).  For every 128-row
+ * group, 128-column k-block and 64-column half, an 8 KiB run holds the
+ * group's eight 16-row tiles, each as two 512-byte pieces in the order the
+ * decode GEMV's lanes read them (a warp-wide access is 512 contiguous bytes);
+ * the prefill GEMM brings a whole run into shared memory with one bulk copy.
+ * Same bytes, same results; the block scales keep their layout.  Tables for
+ * weight_layout 1 point at tiled copies. */
 int64_t moe_fp8_tiled_bytes(int64_t rows, int64_t cols);
 int moe_fp8_tile_weights(const uint8_t* weight, uint8_t* tiled, int64_t rows, int64_t cols, void* stream);
 
