@@ -23,7 +23,8 @@ namespace moe {
 
 __global__ void __launch_bounds__(kBucketThreads) bucket_kernel(BucketArgs a) {
   extern __shared__ uint32_t sm[];
-  bucket_body(a, sm);
+  if (a.n <= kBucketThreads) bucket_body_small(a, sm);
+  else bucket_body(a, sm);
 }
 
 __global__ void __launch_bounds__(kBucketThreads) chunk_kernel(ChunkArgs a) {
@@ -55,7 +56,8 @@ __global__ void __launch_bounds__(kBucketThreads) route_dispatch_kernel(RouteDis
     select_token(logits, 1, 0, a.bias, a.select, t, scratch, scratch + E, a.ids64, a.bucket.keys_out,
                  a.bucket.weights_out, a.weights_bf16);
   __syncthreads();
-  bucket_body(a.bucket.args, sm);
+  if (a.bucket.args.n <= kBucketThreads) bucket_body_small(a.bucket.args, sm);
+  else bucket_body(a.bucket.args, sm);
   __syncthreads();
   chunk_body(a.chunks);
 }
@@ -187,8 +189,10 @@ static cudaError_t launch_bucket_multi(const BucketArgs& a, cudaStream_t stream)
 }
 
 size_t bucket_smem_bytes(int n_buckets) {
-  return static_cast<size_t>(n_buckets) * kWindowWords * sizeof(uint32_t) +
-         static_cast<size_t>(2 * n_buckets + 1) * sizeof(int32_t);
+  // the bitmask window (bucket_body) or the staged keys (bucket_body_small)
+  return std::max(static_cast<size_t>(n_buckets) * kWindowWords * sizeof(uint32_t) +
+                      static_cast<size_t>(2 * n_buckets + 1) * sizeof(int32_t),
+                  static_cast<size_t>(kBucketThreads + n_buckets) * sizeof(int32_t));
 }
 
 cudaError_t launch_bucket(const BucketArgs& a, cudaStream_t stream) {

@@ -126,6 +126,72 @@ static __device__ void bucket_body(const BucketArgs& a, uint32_t* sm) {
   }
 }
 
+// bucket_body for at most kBucketThreads entries (decode batches): thread i
+// owns entry i; its rank inside its bucket is the number of earlier entries
+// with the same key (keys staged in shared memory, four per load) -- no
+// per-bucket bitmask window to clear and count.  Same outputs as bucket_body.
+static __device__ void bucket_body_small(const BucketArgs& a, uint32_t* sm) {
+  int32_t* keys_s = reinterpret_cast<int32_t*>(sm);  // [kBucketThreads]
+  int32_t* start = keys_s + kBucketThreads;         // [n_buckets]: counts, then first slots
+  const int tid = threadIdx.x;
+  for (int b = tid; b < a.n_buckets; b += kBucketThreads) start[b] = 0;
+  int key = -1;
+  if (tid < a.n) {
+    key = a.keys[tid] - a.key_lo;
+    if (key < 0 || key >= a.n_buckets) key = -1;
+  }
+  keys_s[tid] = key;
+  __syncthreads();
+  if (key >= 0) atomicAdd(&start[key], 1);
+  __syncthreads();
+  {
+    const int per = static_cast<int>(ceil_div(a.n_buckets, kBucketThreads));
+    const int b_lo = min(a.n_buckets, tid * per), b_hi = min(a.n_buckets, b_lo + per);
+    int mine = 0;
+    for (int b = b_lo; b < b_hi; ++b) mine += start[b];
+    int running = 0;
+    int off = block_exclusive_scan(mine, &running);
+    for (int b = b_lo; b < b_hi; ++b) {
+      const int c = start[b];
+      if (a.counts) a.counts[b] = c;
+      a.bucket_offset[b] = off;
+      start[b] = off;
+      off += c;
+    }
+    if (tid == 0) {
+      a.bucket_offset[a.n_buckets] = running;
+      if (a.tail > 0) a.bucket_offset[a.n_buckets + 1] = running + a.tail;
+      if (a.total) *a.total = running + (a.tail > 0 ? a.tail : 0);
+    }
+  }
+  __syncthreads();
+  if (key >= 0) {
+    int rank = 0;
+    const int4* k4 = reinterpret_cast<const int4*>(keys_s);
+    for (int j = 0; j < tid / 4; ++j) {
+      const int4 q = k4[j];
+      rank += (q.x == key) + (q.y == key) + (q.z == key) + (q.w == key);
+    }
+    for (int j = tid & ~3; j < tid; ++j) rank += keys_s[j] == key;
+    const int p = start[key] + rank;
+    a.pair_row[p] = a.rows ? a.rows[tid] : tid / a.k;
+    if (a.pair_weight) a.pair_weight[p] = a.weights ? a.weights[tid] : 1.0f;
+    if (a.pair_entry) a.pair_entry[p] = tid;
+    if (a.entry_pair) a.entry_pair[tid] = p;
+  } else if (tid < a.n && a.entry_pair) {
+    a.entry_pair[tid] = -1;
+  }
+  if (a.tail > 0) {
+    const int first = a.bucket_offset[a.n_buckets];
+    for (int r = tid; r < a.tail; r += kBucketThreads) {
+      a.pair_row[first + r] = r;
+      if (a.pair_weight) a.pair_weight[first + r] = 1.0f;
+      if (a.pair_entry) a.pair_entry[first + r] = -1;
+    }
+  }
+  __syncthreads();
+}
+
 // One CTA: segments -> chunks of at most `chunk` consecutive pairs.
 static __device__ void chunk_body(const ChunkArgs& a) {
   const int tid = threadIdx.x;

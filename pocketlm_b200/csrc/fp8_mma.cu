@@ -848,12 +848,24 @@ static int async_ctas_per_sm() {
   return per_sm;
 }
 
+// K-split of the warp tasks when there are fewer tasks than resident warps:
+// enough k-ranges to cover the warps (at least four k-blocks each), then one
+// more if that packs the round-robin (task, k-range) units into fewer
+// rounds per task (1152 tasks on 1776 warps: 2 -> 2 rounds of half a task,
+// 3 -> 2 rounds of a third).  Each k-range costs a partial write and a
+// reduction, so batches with a task per warp or more are not split.
+static int balanced_ksplit(int64_t tasks, int64_t warps, int K) {
+  if (tasks <= 0 || tasks >= warps) return 1;
+  const int nkb = K / kBlock;
+  const int cap = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(nkb / 4, kMaxMmaKSplit)));
+  const int want = static_cast<int>(std::min<int64_t>(ceil_div(warps, tasks), cap));
+  auto per_task = [&](int ks) { return static_cast<double>(ceil_div(tasks * ks, warps)) / ks; };
+  return (want + 1 <= cap && per_task(want + 1) < per_task(want)) ? want + 1 : std::max(1, want);
+}
+
 int async_gemv_ksplit(int64_t tasks_bound, int K) {
   const int64_t warps = static_cast<int64_t>(gemv_grid_ctas()) * async_ctas_per_sm() * kAsyncWarps;
-  if (tasks_bound <= 0 || tasks_bound >= warps) return 1;
-  const int nkb = K / kBlock;
-  const int64_t want = ceil_div(warps, tasks_bound);
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({want, nkb / 4, kMaxMmaKSplit})));
+  return balanced_ksplit(tasks_bound, warps, K);
 }
 
 cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream) {
@@ -908,10 +920,7 @@ static int mma_ctas_per_sm() {
 
 int mma_gemv_ksplit(int64_t tasks_bound, int K) {
   const int64_t warps = static_cast<int64_t>(gemv_grid_ctas()) * mma_ctas_per_sm() * kMmaCtaWarps;
-  if (tasks_bound <= 0 || tasks_bound >= warps) return 1;
-  const int nkb = K / kBlock;
-  const int64_t want = ceil_div(warps, tasks_bound);
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({want, nkb / 4, kMaxMmaKSplit})));
+  return balanced_ksplit(tasks_bound, warps, K);
 }
 
 cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream) {
