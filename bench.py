@@ -539,22 +539,25 @@ def run_profile_case(args) -> dict:
 
 
 def run_profile_prefill(args) -> dict:
-    """A small prefill case for ncu: DS-V3 expert shapes (hidden 7168,
-    intermediate 2048, top-8) with 32 routed experts + shared (about 2.9 GB
-    with the tiled copy), --tokens tokens on the tcgen05 GEMM."""
+    """A prefill case for ncu: DS-V3 expert shapes (hidden 7168,
+    intermediate 2048, top-8) with --profile-prefill-experts routed experts
+    + shared (32: about 2.9 GB with the tiled copy, the small case for
+    multi-pass captures; 256: the full config-3 layer, for single-pass launch
+    lists), --tokens tokens on the tcgen05 GEMM."""
     from pocketlm_b200 import native, synth
     from pocketlm_b200.runtime import DsMoELayerGPU
 
     dev = torch.device("cuda", 0)
     native.load_library()
-    cfg = synth.DsMoEConfig("c3-profile", hidden=7168, inter=2048, n_routed=32, top_k=8, n_group=8, topk_group=4,
+    E = args.profile_prefill_experts
+    cfg = synth.DsMoEConfig("c3-profile", hidden=7168, inter=2048, n_routed=E, top_k=8, n_group=8, topk_group=4,
                             route_scale=2.5)
     layer = DsMoELayerGPU(synth.make_fp8_layer(cfg, seed=args.seed, device=dev, bias_kind="zipf"))
     x = synth.make_hidden(args.tokens, cfg.hidden, seed=args.seed + 1, device=dev)
     for _ in range(args.warmup + args.steps):
         layer.forward(x)
     torch.cuda.synchronize()
-    return {"profile_case": f"c3-shape-32-experts-T{args.tokens}", "launches": args.warmup + args.steps}
+    return {"profile_case": f"c3-shape-{E}-experts-T{args.tokens}", "launches": args.warmup + args.steps}
 
 
 def run_reference(args, rank: int, world: int) -> dict | None:
@@ -606,6 +609,8 @@ def main() -> None:
                         help="run the small ncu case (selected experts only) instead of the benchmark")
     parser.add_argument("--profile-prefill", action="store_true",
                         help="run the small prefill ncu case (DS-V3 expert shapes, 32 experts) instead")
+    parser.add_argument("--profile-prefill-experts", type=int, default=32,
+                        help="routed experts of the --profile-prefill layer (32 small case, 256 full config 3)")
     parser.add_argument("--profile-no-experts", action="store_true",
                         help="with --profile: materialise no expert (for captures of the routing kernels)")
     args = parser.parse_args()
