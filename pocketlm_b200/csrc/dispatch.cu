@@ -41,14 +41,29 @@ __global__ void __launch_bounds__(kBucketThreads) route_dispatch_kernel(RouteDis
   const int E = a.select.experts, T = a.select.tokens;
   // logits = sum of the split-K partials, in part order, summed by the whole CTA
   float* logits = reinterpret_cast<float*>(sm);
-  for (int i = threadIdx.x; i < T * E; i += kBucketThreads) {
-    float parts[kMaxRouterParts];
+  if (a.nparts == 1) {
+    // one part: eight independent loads in flight per thread
+    for (int i0 = threadIdx.x; i0 < T * E; i0 += 8 * kBucketThreads) {
+      float v[8];
 #pragma unroll
-    for (int q = 0; q < kMaxRouterParts; ++q) parts[q] = q < a.nparts ? a.partial[q * a.part_stride + i] : 0.0f;
-    float v = parts[0];
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kBucketThreads;
+        v[u] = i < T * E ? a.partial[i] : 0.0f;
+      }
 #pragma unroll
-    for (int q = 1; q < kMaxRouterParts; ++q) v += q < a.nparts ? parts[q] : 0.0f;
-    logits[i] = v;
+      for (int u = 0; u < 8; ++u)
+        if (i0 + u * kBucketThreads < T * E) logits[i0 + u * kBucketThreads] = v[u];
+    }
+  } else {
+    for (int i = threadIdx.x; i < T * E; i += kBucketThreads) {
+      float parts[kMaxRouterParts];
+#pragma unroll
+      for (int q = 0; q < kMaxRouterParts; ++q) parts[q] = q < a.nparts ? a.partial[q * a.part_stride + i] : 0.0f;
+      float v = parts[0];
+#pragma unroll
+      for (int q = 1; q < kMaxRouterParts; ++q) v += q < a.nparts ? parts[q] : 0.0f;
+      logits[i] = v;
+    }
   }
   __syncthreads();
   float* scratch = logits + static_cast<size_t>(T) * E + static_cast<size_t>(warp) * 2 * E;
