@@ -393,9 +393,11 @@ def run_q4(args, dev, flush, peaks, token_list) -> dict:
     """Config 4 on one GPU: the Mixtral-8x7B-shape layer in the reference's Q4
     format (hidden 4096, ffn 14336, 8 experts, softmax top-2 renormalised),
     bf16 activations, through moe_q4_moe_layer_u16 (router, dispatch, Q4
-    grouped GEMV on the warp MMA pipe, combine).  Eager forwards,
-    CUDA-event timed, L2 flushed between steps.  Bytes: the experts the batch
-    selects (packed codes + fp16 row scales) + router + activations."""
+    experts, combine): batches of 32+ pairs per expert on the tcgen05 grouped
+    GEMM (int4 codes in the Q4 tiled layout, converted exactly to fp16), smaller
+    ones on the warp-MMA GEMV.  Eager forwards, CUDA-event timed, L2 flushed
+    between steps.  Bytes: the experts the batch selects (packed codes + fp16
+    row scales) + router + activations; FLOPs: T * k * 3 * 2 * H * I."""
     from pocketlm_b200 import synth
     from pocketlm_b200.runtime import Q4MoELayerGPU
 
@@ -411,13 +413,18 @@ def run_q4(args, dev, flush, peaks, token_list) -> dict:
         ms = statistics.mean(time_steps(lambda: layer.forward(x), steps, args.warmup, flush))
         n_exp = len({int(v) for v in ids.reshape(-1).tolist()})
         nbytes = n_exp * cfg.expert_bytes + cfg.n_experts * cfg.hidden * 2 + T * cfg.hidden * 4
+        gemm = layer.tables_tiled is not None and T * cfg.top_k >= layer.prefill_pairs * cfg.n_experts
+        flops = T * cfg.top_k * 3 * 2 * cfg.hidden * cfg.inter
         out[str(T)] = {"tokens": T, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3), "experts_streamed": n_exp,
-                       "layer_bytes": nbytes,
-                       "layer_hbm_frac": nbytes / (ms / 1e3) / (peaks["hbm_gbs"] * 1e9)}
+                       "path": "tcgen05 GEMM" if gemm else "warp-MMA GEMV", "layer_bytes": nbytes,
+                       "layer_hbm_frac": nbytes / (ms / 1e3) / (peaks["hbm_gbs"] * 1e9),
+                       "tflops": flops / (ms / 1e3) / 1e12,
+                       "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peaks.get("bf16_tflops", 1590.0)}
         del x, ids
     del layer
     torch.cuda.empty_cache()
-    return {"workload": "c4-mixtral-q4", "kernel": "dense_mma_gemv_kernel<Q4> (dense_gemv.cu)", "sweep": out}
+    return {"workload": "c4-mixtral-q4", "kernel": "dense_mma_gemv_kernel<Q4> (dense_gemv.cu) / "
+            "prefill_gemm_kernel<*, Q4> (prefill_gemm.cu)", "sweep": out}
 
 
 def run_ours_ep(args, rank: int, world: int) -> dict | None:
@@ -603,7 +610,7 @@ def main() -> None:
                         help="expert GEMV kernel (moe_b200_select_gemv); auto is the product default")
     parser.add_argument("--prefill-tokens", default="2048,8192,16384",
                         help="config-3 prefill batch sizes measured after the decode sweep, or 'none'")
-    parser.add_argument("--q4-tokens", default="1,32,4096",
+    parser.add_argument("--q4-tokens", default="1,32,512,4096",
                         help="config-4 (Mixtral Q4) batch sizes measured after the prefill sweep, or 'none'")
     parser.add_argument("--profile", action="store_true",
                         help="run the small ncu case (selected experts only) instead of the benchmark")

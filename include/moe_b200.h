@@ -268,13 +268,24 @@ int64_t moe_q4_moe_selected_workspace_bytes(int64_t hidden_size, int64_t interme
  * converted to fp16 as the reference does; tables: device uint64 [6][E];
  * out: [tokens, hidden] in hidden's dtype (the fp16 result, re-rounded to
  * bf16 for a bf16 caller); out_ids int64 / out_weights fp32 [tokens, top_k]
- * may be NULL. */
+ * may be NULL.  weight_layout 0: tables point at the row-major packed codes
+ * (warp-MMA GEMV, any batch); 1: at copies in the Q4 tiled layout
+ * (moe_q4_tile_weights) -- the tcgen05 grouped GEMM for prefill-sized
+ * batches, hidden % 256 == 0 and intermediate % 128 == 0; scales as given. */
 int moe_q4_moe_layer_u16(const void* hidden, int hidden_dtype, int64_t tokens, int64_t hidden_size,
                          int64_t intermediate_size, const void* router_weight, int router_dtype, int64_t num_experts,
-                         int64_t top_k, const uint64_t* tables, void* out, int64_t* out_ids, float* out_weights,
-                         void* workspace, int64_t workspace_bytes, void* stream);
+                         int64_t top_k, const uint64_t* tables, int weight_layout, void* out, int64_t* out_ids,
+                         float* out_weights, void* workspace, int64_t workspace_bytes, void* stream);
 int64_t moe_q4_moe_layer_workspace_bytes(int64_t tokens, int64_t hidden_size, int64_t intermediate_size,
                                          int64_t num_experts, int64_t top_k);
+/* Q4 tiled layout (no reference counterpart), weight_layout 1 of
+ * moe_q4_moe_layer_u16: moe_q4_tile_weights copies packed int4 codes [rows,
+ * cols / 2] (cols % 64 == 0) into moe_q4_tiled_bytes(rows, cols) bytes: for
+ * every 128-row group and 64-column block a 4 KiB run of the group's rows (32
+ * bytes each), rows padded to a multiple of 128 with zeros -- one bulk copy
+ * per matrix and pipeline stage of the prefill GEMM.  Same bytes reordered. */
+int64_t moe_q4_tiled_bytes(int64_t rows, int64_t cols);
+int moe_q4_tile_weights(const uint8_t* packed, uint8_t* tiled, int64_t rows, int64_t cols, void* stream);
 
 /* replaces native_pack_u16_rows8, fp16_packed_gemv.cpp:52-77:
  * packed[(blk * cols + c) * 8 + lane] = weight[blk * 8 + lane, c], zero past

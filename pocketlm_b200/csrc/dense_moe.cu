@@ -15,6 +15,7 @@
 #include "dispatch.cuh"
 #include "fp8_gemv.cuh"
 #include "plan.cuh"
+#include "prefill_gemm.cuh"
 #include "route_host.cuh"
 #include "router.cuh"
 #include "status.cuh"
@@ -54,10 +55,20 @@ struct DensePlan {
   int32_t* counters;
   int64_t n_counters;
   bool mma;
+  // tensor-core prefill (Q4 tiled weights): natural-order fp16 rows with
+  // power-of-two scales, the pair-ordered A rows and the m-tile map
+  __half* x16;
+  float* x16scale;
+  __half* a16;
+  float* a16scale;
+  __half* act16;
+  float* act16scale;
+  int32_t* mprefix;
+  int32_t* bucket_scratch;  // multi-CTA dispatch of large batches
 };
 
 DensePlan plan_dense(Plan& p, int kind, int64_t rows_x, int64_t pairs, int64_t segments, int64_t entries,
-                     int64_t H, int64_t I, int64_t router_logits, bool tables) {
+                     int64_t H, int64_t I, int64_t router_logits, bool tables, bool prefill = false) {
   DensePlan d{};
   d.seg_offset = p.take<int32_t>(segments + 2);
   d.pair_row = p.take<int32_t>(pairs);
@@ -98,7 +109,23 @@ DensePlan plan_dense(Plan& p, int kind, int64_t rows_x, int64_t pairs, int64_t s
   }
   d.act = p.take<float>(pairs * I);
   d.y = p.take<float>(pairs * H);
+  if (prefill) {
+    d.x16 = p.take<__half>(rows_x * H);
+    d.x16scale = p.take<float>(rows_x);
+    d.a16 = p.take<__half>(pairs * H);
+    d.a16scale = p.take<float>(pairs);
+    d.act16 = p.take<__half>(pairs * I);
+    d.act16scale = p.take<float>(pairs);
+    d.mprefix = p.take<int32_t>(segments + 2);
+    d.bucket_scratch = p.take<int32_t>(bucket_scratch_ints(entries, static_cast<int>(segments)));
+  }
   return d;
+}
+
+// Q4 shapes the tensor-core prefill GEMM takes (Q4 tiled weights: K % 64; the
+// GEMM's tiles: K % 128, gate/up rows % 128, down rows % 256).
+bool q4_prefill_supported(int64_t H, int64_t I) {
+  return prefill_supported(H, I, true) && prefill_supported(I, H, false);
 }
 
 // Dense route matrix [T, S]: pair p = s * T + t (expert-major), weight
@@ -184,6 +211,7 @@ int bucket_routes(const DensePlan& d, int64_t T, int64_t k, int64_t E, cudaStrea
   ba.k = static_cast<int>(k); ba.key_lo = 0; ba.n_buckets = static_cast<int>(E);
   ba.bucket_offset = d.seg_offset; ba.pair_row = d.pair_row; ba.pair_weight = d.pair_weight;
   ba.pair_entry = d.pair_entry; ba.entry_pair = d.row_pairs; ba.tail = 0;
+  ba.block_counts = d.bucket_scratch;
   MOE_CUDA(launch_bucket(ba, s), "dispatch");
   return kOk;
 }
@@ -222,10 +250,44 @@ int selected_forward(int kind, const DenseTables* given, const void* gate, const
   return dense_combine(d, T, H, S, out, out_dtype, false, s);
 }
 
-size_t routed_need(int kind, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, bool tables) {
+size_t routed_need(int kind, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, bool tables,
+                   bool prefill = false) {
   Plan p;
-  plan_dense(p, kind, T, T * k, E, T * k, H, I, T * E, tables);
+  plan_dense(p, kind, T, T * k, E, T * k, H, I, T * E, tables, prefill);
   return p.used();
+}
+
+// The Q4 expert stages on the tcgen05 grouped GEMM (prefill_gemm.cu, int4
+// weights in the Q4 tiled layout): stage x as fp16 rows, gather the pairs'
+// rows, gate/up + SwiGLU, stage the activations, down.  d.y gets every
+// pair's output as the GEMV path leaves it.
+int run_q4_prefill(const DenseTables& t, const void* x, int x_dtype, int64_t T, int64_t pairs, int64_t E, int64_t H,
+                   int64_t I, const DensePlan& d, cudaStream_t s) {
+  if (x_dtype == kDtypeF16)
+    MOE_CUDA(launch_f16_rows_to_f16(x, static_cast<int>(T), static_cast<int>(H), d.x16, d.x16scale, s), "stage x");
+  else
+    MOE_CUDA(launch_rows_to_f16(x, true, static_cast<int>(T), static_cast<int>(H), nullptr, d.x16, d.x16scale, nullptr,
+                                0, s),
+             "stage x");
+  MOE_CUDA(launch_gather_rows(d.x16, d.x16scale, d.pair_row, pairs, H, d.a16, d.a16scale, s), "gather pairs");
+  MOE_CUDA(launch_prefill_tiles(d.seg_offset, static_cast<int>(E), d.mprefix, s), "tile map");
+  const int64_t mtiles_bound = pairs / 128 + E;
+  PrefillArgs g1{};
+  g1.w0 = t.gw; g1.s0 = t.gs; g1.w1 = t.uw; g1.s1 = t.us;
+  g1.a16 = d.a16; g1.ascale = d.a16scale; g1.rows_a = pairs;
+  g1.seg_offset = d.seg_offset; g1.mprefix = d.mprefix; g1.n_segments = static_cast<int>(E);
+  g1.out = d.act; g1.N = static_cast<int>(I); g1.K = static_cast<int>(H);
+  g1.scale_cols = 0; g1.nanfix = 0; g1.nan_free = nullptr; g1.wformat = kPrefillQ4Row;
+  MOE_CUDA(launch_prefill_gemm(g1, true, mtiles_bound * (I / 128), s), "gate/up GEMM");
+  MOE_CUDA(launch_rows_to_f16(d.act, false, static_cast<int>(pairs), static_cast<int>(I), nullptr, d.act16,
+                              d.act16scale, nullptr, 0, s),
+           "stage activations");
+  PrefillArgs g2 = g1;
+  g2.w0 = t.dw; g2.s0 = t.ds; g2.w1 = nullptr; g2.s1 = nullptr;
+  g2.a16 = d.act16; g2.ascale = d.act16scale;
+  g2.out = d.y; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
+  MOE_CUDA(launch_prefill_gemm(g2, false, mtiles_bound * (H / 256), s), "down GEMM");
+  return kOk;
 }
 
 }  // namespace
@@ -280,25 +342,31 @@ int moe_q4_moe_selected_forward_u16(const uint16_t* hidden, const uint64_t* gate
 int64_t moe_q4_moe_layer_workspace_bytes(int64_t tokens, int64_t hidden_size, int64_t intermediate_size,
                                          int64_t num_experts, int64_t top_k) {
   if (tokens <= 0 || hidden_size <= 0 || intermediate_size <= 0 || num_experts <= 0 || top_k <= 0) return -1;
-  return static_cast<int64_t>(routed_need(kWQ4, tokens, hidden_size, intermediate_size, num_experts, top_k, false));
+  // room for the tensor-core path too (weight_layout 1) where the shapes allow it
+  return static_cast<int64_t>(routed_need(kWQ4, tokens, hidden_size, intermediate_size, num_experts, top_k, false,
+                                          q4_prefill_supported(hidden_size, intermediate_size)));
 }
 
 int moe_q4_moe_layer_u16(const void* hidden, int hidden_dtype, int64_t tokens, int64_t hidden_size,
                          int64_t intermediate_size, const void* router_weight, int router_dtype, int64_t num_experts,
-                         int64_t top_k, const uint64_t* tables, void* out, int64_t* out_ids, float* out_weights,
-                         void* workspace, int64_t workspace_bytes, void* stream) {
+                         int64_t top_k, const uint64_t* tables, int weight_layout, void* out, int64_t* out_ids,
+                         float* out_weights, void* workspace, int64_t workspace_bytes, void* stream) {
   if (!hidden || !router_weight || !tables || !out) return fail(kNullPointer, "null pointer");
   if (hidden_dtype != kDtypeBF16 && hidden_dtype != kDtypeF16) return fail(kUnsupported, "hidden must be bf16 or fp16");
+  if (weight_layout != 0 && weight_layout != 1) return fail(kBadDims, "weight_layout must be 0 or 1");
+  if (weight_layout == 1 && !q4_prefill_supported(hidden_size, intermediate_size))
+    return fail(kUnsupported, "Q4 tiled weights need hidden % 256 == 0 and intermediate % 128 == 0");
   int code = check_route(tokens, hidden_size, num_experts, 1, 1, top_k);
   if (code != kOk) return code;
   if (intermediate_size <= 0) return fail(kBadDims, "bad dimensions");
   if (num_experts > kMaxBuckets) return fail(kUnsupported, "too many experts");
   const int64_t T = tokens, H = hidden_size, I = intermediate_size, E = num_experts, k = top_k;
   cudaStream_t s = as_stream(stream);
-  Scratch scratch(workspace, workspace_bytes, routed_need(kWQ4, T, H, I, E, k, false), s);
+  const bool prefill = q4_prefill_supported(H, I);
+  Scratch scratch(workspace, workspace_bytes, routed_need(kWQ4, T, H, I, E, k, false, prefill), s);
   if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
   Plan plan(scratch.base());
-  const DensePlan d = plan_dense(plan, kWQ4, T, T * k, E, T * k, H, I, T * E, false);
+  const DensePlan d = plan_dense(plan, kWQ4, T, T * k, E, T * k, H, I, T * E, false, prefill);
   // softmax over fp32 logits, top-k, renormalised (layer_bridge.py:2682-2689)
   code = route_impl(hidden, hidden_dtype, router_weight, router_dtype, nullptr, T, H, E, 1, 1, k, kScoreSoftmax, 1,
                     0, 1.0f, 0, out_ids, d.ids32, d.wts, nullptr, d.logits, s);
@@ -308,10 +376,23 @@ int moe_q4_moe_layer_u16(const void* hidden, int hidden_dtype, int64_t tokens, i
   code = bucket_routes(d, T, k, E, s);
   if (code != kOk) return code;
   const DenseTables t{tables, tables + E, tables + 2 * E, tables + 3 * E, tables + 4 * E, tables + 5 * E};
-  code = run_dense_pipeline(kWQ4, t, hidden, hidden_dtype, T, T * k, E, H, I, d, s);
+  code = weight_layout == 1 ? run_q4_prefill(t, hidden, hidden_dtype, T, T * k, E, H, I, d, s)
+                            : run_dense_pipeline(kWQ4, t, hidden, hidden_dtype, T, T * k, E, H, I, d, s);
   if (code != kOk) return code;
   // q4_moe_selected_forward_u16 returns fp16 per token; a bf16 caller gets that value as bf16
   return dense_combine(d, T, H, k, out, hidden_dtype, hidden_dtype == kDtypeBF16, s);
+}
+
+int64_t moe_q4_tiled_bytes(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0 || cols % 64 != 0) return -1;
+  return q4_tiled_bytes(rows, cols);
+}
+
+int moe_q4_tile_weights(const uint8_t* packed, uint8_t* tiled, int64_t rows, int64_t cols, void* stream) {
+  if (!packed || !tiled) return fail(kNullPointer, "null pointer");
+  if (rows <= 0 || cols <= 0 || cols % 64 != 0) return fail(kBadDims, "cols must be a positive multiple of 64");
+  MOE_CUDA(launch_q4_tile(packed, tiled, rows, cols, as_stream(stream)), "q4 tile");
+  return kOk;
 }
 
 // ---------------------------------------------------------------------------

@@ -123,6 +123,8 @@ cudaError_t launch_nan_free_flags(const uint64_t* tables, int S, int64_t inter, 
 // Same computation, weights fed to each warp by TMA bulk copies (fp8_mma.cu).
 cudaError_t launch_tma_mma_gemv(const MmaArgs& a, int ns, int epi, cudaStream_t stream);
 int read_and_clear_mma_device_error(cudaStream_t stream);
+// the rows_to_f16 staging of fp16 rows (dst = src / power-of-two scale, exact)
+cudaError_t launch_f16_rows_to_f16(const void* src, int rows, int K, __half* dst, float* scale, cudaStream_t stream);
 // Also zeroes zero[0, zero_n) (the k-split counters of the stages that follow).
 cudaError_t launch_rows_to_f16(const void* src, bool src_bf16, int rows, int K, const int32_t* n_rows_dev,
                                __half* dst, float* scale, int32_t* zero, int64_t zero_n, cudaStream_t stream);

@@ -77,6 +77,17 @@ MOE_D void unpack16<__nv_bfloat16>(const uint4& v, float* out) {
   }
 }
 
+template <>
+MOE_D void unpack16<__half>(const uint4& v, float* out) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
+  }
+}
+
 // Activation rows -> f16 with a per-row power-of-two scale:
 // dst[r, k] = src[r, k] / scale[r], scale = 2^(floor(log2(amax)) - 13) so the
 // largest magnitude lands in [2^13, 2^14) (1 for an all-zero row).  One CTA
@@ -796,6 +807,14 @@ __global__ void __launch_bounds__(kTmaWarps * kWarp) tma_mma_gemv_kernel(MmaArgs
 // ---------------------------------------------------------------------------
 
 bool mma_gemv_supported(int K, int N) { return K % kBlock == 0 && K > 0 && N > 0; }
+
+cudaError_t launch_f16_rows_to_f16(const void* src, int rows, int K, __half* dst, float* scale, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  const unsigned grid = static_cast<unsigned>(std::min(rows, gemv_grid_ctas() * 8));
+  rows_to_f16_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(src), rows, K, nullptr, dst, scale,
+                                                       nullptr, 0);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_rows_to_f16(const void* src, bool src_bf16, int rows, int K, const int32_t* n_rows_dev,
                                __half* dst, float* scale, int32_t* zero, int64_t zero_n, cudaStream_t stream) {

@@ -213,8 +213,25 @@ __global__ void gather_rows_kernel(const __half* x16, const float* xscale, const
   }
 }
 
+// Row-major packed int4 [rows, K / 2] -> the Q4 tiled layout; thread q writes
+// the q-th 16 bytes of the destination (run, row, half of its 32 bytes).
+__global__ void q4_tile_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t rows, int64_t K) {
+  const int64_t nkblk = K / 64, row_bytes = K / 2;
+  const int64_t units = (rows + 127) / 128 * nkblk * 256;
+  for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < units;
+       q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t run = q / 256;
+    const int w = static_cast<int>(q % 256);
+    const int64_t group = run / nkblk, kblk = run % nkblk;
+    const int64_t row = group * 128 + w / 2;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < rows) v = *reinterpret_cast<const uint4*>(src + row * row_bytes + kblk * 32 + (w % 2) * 16);
+    *reinterpret_cast<uint4*>(dst + q * 16) = v;
+  }
+}
+
 // --------------------------------------------------------------- kernel
-template <bool GATEUP>
+template <bool GATEUP, int WF>
 __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                                     PrefillArgs a) {
   extern __shared__ unsigned char smem_raw[];
@@ -256,6 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
   const int64_t tiles = static_cast<int64_t>(a.mprefix[a.n_segments]) * n_tiles;
   const int nkh = K / kBK;  // pipeline stages per tile
   const int nkb = K / 128;  // k-blocks (scale columns, tiled-layout blocks)
+  constexpr uint32_t kRunBytes = WF == kPrefillQ4Row ? 4096 : kTileRunBytes;  // per matrix half and stage
   // an expert without (16-byte aligned) weights and scales is skipped by every
   // role alike; the epilogue writes its pairs' rows as zeros
   auto present = [&](int seg) {
@@ -274,10 +292,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         const uint8_t* w0 = reinterpret_cast<const uint8_t*>(a.w0[tr.seg]);
         const uint8_t* wbase[2] = {w0, GATEUP ? reinterpret_cast<const uint8_t*>(a.w1[tr.seg]) : w0};
         const int64_t tile0[2] = {GATEUP ? tr.nt * 8 : tr.nt * 16, GATEUP ? tr.nt * 8 : tr.nt * 16 + 8};
+        // the stage's run of matrix half h: 8 KiB of e4m3 (k-block kq / 2, half kq % 2)
+        // or 4 KiB of int4 codes (64-code k-block kq)
+        auto run_at = [&](int h, int kq) {
+          return WF == kPrefillQ4Row ? wbase[h] + q4_tiled_offset(tile0[h] / 8, kq, nkh)
+                                     : wbase[h] + tiled_offset(tile0[h], kq / 2, kq % 2, nkb);
+        };
         auto prefetch = [&](int kq) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-            bulk_prefetch_l2(wbase[h] + tiled_offset(tile0[h], kq / 2, kq % 2, nkb), kTileRunBytes);
+          for (int h = 0; h < 2; ++h) bulk_prefetch_l2(run_at(h, kq), kRunBytes);
         };
         for (int kq = 0; kq < kPrefetchStages && kq < nkh; ++kq) prefetch(kq);
         for (int kh = 0; kh < nkh && !*abort; ++kh, ++it) {
@@ -286,21 +309,63 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
           if (it >= kStages && !wait_or_abort(&bars->empty[s], ((it / kStages) - 1) & 1, abort)) break;
           // the second sub-tile only when the tile has more than 128 pairs
           const bool two = tr.rows > kSubM;
-          mbar_arrive_expect_tx(&bars->full[s], two ? kLoadBytes : kLoadBytes - kATileBytes);
+          mbar_arrive_expect_tx(&bars->full[s], (two ? 2 : 1) * kATileBytes + 2 * kRunBytes);
           tma_load_2d(a_tile(s, 0), &tmap_a, kh * kBK, tr.row0, &bars->full[s]);
           if (two) tma_load_2d(a_tile(s, 1), &tmap_a, kh * kBK, tr.row0 + kSubM, &bars->full[s]);
-          const int kb = kh / 2, sp = kh % 2;
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-            bulk_copy_g2s(raw_tile(s) + h * kTileRunBytes, wbase[h] + tiled_offset(tile0[h], kb, sp, nkb),
-                          kTileRunBytes, &bars->full[s]);
+          for (int h = 0; h < 2; ++h) bulk_copy_g2s(raw_tile(s) + h * kRunBytes, run_at(h, kh), kRunBytes, &bars->full[s]);
         }
       }
       // every copy issued lands before the CTA may exit
       for (uint32_t j = it > kStages ? it - kStages : 0; j < it; ++j)
         mbar_wait(&bars->full[j % kStages], (j / kStages) & 1, kCodeWait);
     }
-  } else if (warp >= kEpiWarps && warp < kEpiWarps + kConvWarps) {
+  } else if (WF == kPrefillQ4Row && warp >= kEpiWarps && warp < kEpiWarps + kConvWarps) {
+    // converter, int4 codes: thread ct owns tile row n = ct (run n / 128, row
+    // n % 128 of it): its 32 bytes hold k 0..63 of the stage, converted
+    // exactly to fp16 integers -8..7 (the row scale is applied in the
+    // epilogue) and written as one 128-byte swizzled row
+    const int n = threadIdx.x - kEpiWarps * kWarp;  // 0 .. 255
+    const __half2 mul = __halves2half2(__float2half(1.0f), __float2half(0.0625f));
+    const __half2 add = __halves2half2(__float2half(-1032.0f), __float2half(-72.0f));
+    uint32_t it = 0;
+    for (int64_t t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+      const TileRef tr = tile_at(t, a.mprefix, a.seg_offset, a.n_segments, n_tiles);
+      if (!present(tr.seg)) continue;
+      bool ok = true;
+      for (int kh = 0; kh < nkh; ++kh, ++it) {
+        const int s = it % kStages, b = it % kConvBufs;
+        if (!wait_or_abort(&bars->full[s], (it / kStages) & 1, abort) ||
+            (it >= kConvBufs && !wait_or_abort(&bars->cempty[b], ((it / kConvBufs) - 1) & 1, abort))) {
+          ok = false;
+          break;
+        }
+        const unsigned char* src = raw_tile(s) + (n / 128) * kRunBytes + (n % 128) * 32;
+        unsigned char* bt = b_tile(b);
+        const uint4 lo = ld_shared_v4(src), hi = ld_shared_v4(src + 16);
+        const uint32_t words[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          // word c = codes k 8c .. 8c + 7, two per byte (even k low): byte j -> (k 8c+2j, 8c+2j+1)
+          uint32_t h[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t v;
+            asm("prmt.b32 %0, %1, 0, %2;" : "=r"(v) : "r"(words[c]), "r"(0x4040 + 0x0101 * j));
+            // halves 1024 + (lo ^ 8) and 1024 + 16 (hi ^ 8), then x (1, 1/16) - (1032, 72): the signed codes
+            v = (v & 0x00F0000Fu) ^ 0x64806408u;
+            const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&v), mul, add);
+            h[j] = *reinterpret_cast<const uint32_t*>(&r);
+          }
+          st_shared_v4(bt + (n / 8) * 1024 + (n % 8) * 128 + ((c ^ (n % 8)) * 16), h[0], h[1], h[2], h[3]);
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->cfull[b]);
+      }
+      if (!ok) break;
+    }
+  } else if (WF == kPrefillFp8Block && warp >= kEpiWarps && warp < kEpiWarps + kConvWarps) {
     // converter: e4m3 runs x block scale -> fp16, 128B-swizzled K-major
     const int ct = threadIdx.x - kEpiWarps * kWarp;  // 0 .. kConvThreads - 1
     uint32_t it = 0;
@@ -448,6 +513,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       const bool valid = row_in_tile < tr.rows;
       const int64_t p = tr.row0 + row_in_tile;
       const float xs = valid ? a.ascale[p] : 0.0f;
+      // int4 weights: fp16 scale of each output column (weight row), else none
+      const __half* csc0 = WF == kPrefillQ4Row ? reinterpret_cast<const __half*>(a.s0[tr.seg]) +
+                                                     static_cast<int64_t>(tr.nt) * (GATEUP ? kBN / 2 : kBN)
+                                               : nullptr;
+      const __half* csc1 = WF == kPrefillQ4Row && GATEUP
+                               ? reinterpret_cast<const __half*>(a.s1[tr.seg]) + static_cast<int64_t>(tr.nt) * (kBN / 2)
+                               : nullptr;
       // down (256 fp32 per row): 16 columns of the warp's 32 rows at a time
       // leave through its 2 KiB staging buffer -- lane = row on the way in,
       // four lanes per row (64 contiguous bytes) on the way out; 16-byte
@@ -486,7 +558,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
               float* op = &o.x;
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                const float g = __uint_as_float(gr[j + q]) * xs, u = __uint_as_float(ur[j + q]) * xs;
+                float g = __uint_as_float(gr[j + q]) * xs, u = __uint_as_float(ur[j + q]) * xs;
+                if (WF == kPrefillQ4Row) {
+                  g *= __half2float(csc0[c0 + j + q]);
+                  u *= __half2float(csc1[c0 + j + q]);
+                }
                 op[q] = g / (1.0f + expf(-g)) * u;
               }
               *reinterpret_cast<float4*>(out + c0 + j) = o;
@@ -502,10 +578,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
           tmem_ld_wait();
           float o[16];
 #pragma unroll
-          for (int q = 0; q < 16; ++q) o[q] = __uint_as_float(d0[q]) * xs;
+          for (int q = 0; q < 16; ++q)
+            o[q] = __uint_as_float(d0[q]) * xs * (WF == kPrefillQ4Row ? __half2float(csc0[c0 + q]) : 1.0f);
           emit16(o, c0);
 #pragma unroll
-          for (int q = 0; q < 16; ++q) o[q] = __uint_as_float(d1[q]) * xs;
+          for (int q = 0; q < 16; ++q)
+            o[q] = __uint_as_float(d1[q]) * xs * (WF == kPrefillQ4Row ? __half2float(csc0[c0 + 16 + q]) : 1.0f);
           emit16(o, c0 + 16);
         }
       }
@@ -701,7 +779,9 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, bool gateup, int64_t max_t
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  auto kernel = gateup ? prefill_gemm_kernel<true> : prefill_gemm_kernel<false>;
+  const bool q4 = a.wformat == kPrefillQ4Row;
+  auto kernel = gateup ? (q4 ? prefill_gemm_kernel<true, kPrefillQ4Row> : prefill_gemm_kernel<true, kPrefillFp8Block>)
+                       : (q4 ? prefill_gemm_kernel<false, kPrefillQ4Row> : prefill_gemm_kernel<false, kPrefillFp8Block>);
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
   if (err != cudaSuccess) return err;
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(gemv_grid_ctas(), max_tiles)));
@@ -756,6 +836,18 @@ cudaError_t launch_router_logits_tc(const void* x, int xdtype, const void* w, in
   kernel<<<grid, kRThreads, kRSmemBytes, stream>>>(tx, tw, partial, static_cast<int>(tokens), static_cast<int>(experts),
                                                    ncols, n_tiles, static_cast<int>(hidden / 64), parts);
   *nparts = parts;
+  return cudaGetLastError();
+}
+
+int64_t q4_tiled_bytes(int64_t rows, int64_t K) { return (rows + 127) / 128 * 128 * (K / 2); }
+
+cudaError_t launch_q4_tile(const uint8_t* packed, uint8_t* tiled, int64_t rows, int64_t K, cudaStream_t stream) {
+  if (rows <= 0 || K <= 0) return cudaSuccess;
+  if (K % 64 != 0 || (reinterpret_cast<uintptr_t>(packed) & 15u) || (reinterpret_cast<uintptr_t>(tiled) & 15u))
+    return cudaErrorInvalidValue;
+  const int64_t units = q4_tiled_bytes(rows, K) / 16;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(units, 256), gemv_grid_ctas() * 16));
+  q4_tile_kernel<<<grid, 256, 0, stream>>>(packed, tiled, rows, K);
   return cudaGetLastError();
 }
 

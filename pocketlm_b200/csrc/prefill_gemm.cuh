@@ -25,7 +25,22 @@ struct PrefillArgs {
   int scale_cols;          // ceil(K / 128)
   int nanfix;              // decode e4m3 0x7F / 0xFF as +0
   const uint8_t* nan_free; // [n_segments] or null: 1 = the expert holds no such code
+  int wformat;             // kPrefillFp8Block or kPrefillQ4Row
 };
+
+// Weight formats of the prefill GEMM: e4m3 with 128 x 128 fp32 block scales
+// in the fragment-native tiled layout (fp8_gemv.cuh), or signed int4 codes
+// (two per byte, even k in the low nibble) with one fp16 scale per output
+// row, in the Q4 tiled layout below.
+constexpr int kPrefillFp8Block = 0;
+constexpr int kPrefillQ4Row = 1;
+
+// Q4 tiled layout: for every 128-row group and 64-code k-block, a 4 KiB run
+// holding the group's rows in order, 32 bytes (64 codes) each.  Rows padded to
+// a multiple of 128 with zero bytes; K % 64 == 0.
+MOE_HD int64_t q4_tiled_offset(int64_t group, int64_t kblk, int64_t nkblk) { return (group * nkblk + kblk) * 4096; }
+int64_t q4_tiled_bytes(int64_t rows, int64_t K);
+cudaError_t launch_q4_tile(const uint8_t* packed, uint8_t* tiled, int64_t rows, int64_t K, cudaStream_t stream);
 
 size_t prefill_smem_bytes();
 // K % 128 == 0; N % 128 (gate/up) or % 256 (down) == 0.

@@ -110,7 +110,10 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_q4_dequant_many_to_fp16": ([_P, _P, _P, _P, _P, _I64, _P], _INT),
     "moe_q4_moe_selected_forward_u16": ([_P] * 9 + [_I64] * 3 + [_P, _I64, _P], _INT),
     "moe_q4_moe_selected_workspace_bytes": ([_I64] * 3, _I64),
-    "moe_q4_moe_layer_u16": ([_P, _INT, _I64, _I64, _I64, _P, _INT, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P], _INT),
+    "moe_q4_moe_layer_u16": ([_P, _INT, _I64, _I64, _I64, _P, _INT, _I64, _I64, _P, _INT, _P, _P, _P, _P, _I64, _P],
+                             _INT),
+    "moe_q4_tiled_bytes": ([_I64, _I64], _I64),
+    "moe_q4_tile_weights": ([_P, _P, _I64, _I64, _P], _INT),
     "moe_q4_moe_layer_workspace_bytes": ([_I64] * 5, _I64),
     "moe_pack_u16_rows8": ([_P, _P, _I64, _I64, _P], _INT),
     "moe_packed_gemv_rows8": ([_P, _P, _P, _I64, _I64, _INT, _P], _INT),

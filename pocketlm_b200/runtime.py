@@ -251,9 +251,16 @@ class Q4MoELayerGPU:
     """A Mixtral-shape Q4 MoE layer (pocketlm_b200.synth.Q4MoELayer) resident
     in HBM for moe_q4_moe_layer_u16: softmax top-k router, then every token
     through its experts with q4_moe_selected_forward_u16's arithmetic (the
-    batch form of layer_bridge.py:909-955)."""
+    batch form of layer_bridge.py:909-955).
 
-    def __init__(self, layer):
+    tiled: also keep the codes in the Q4 tiled layout (moe_q4_tile_weights,
+    +1x the packed bytes) so that batches of at least `prefill_pairs`
+    (token, expert) pairs per expert run on the tcgen05 grouped GEMM; smaller
+    batches stream the row-major codes through the warp-MMA GEMV."""
+
+    prefill_pairs = 32
+
+    def __init__(self, layer, *, tiled: bool = True):
         if layer.gate_p.device.type != "cuda":
             layer = layer.to(native._device())
         self.layer = layer
@@ -262,6 +269,26 @@ class Q4MoELayerGPU:
         cols = [[int(t.data_ptr()) for t in (layer.gate_p[e], layer.gate_s[e], layer.up_p[e], layer.up_s[e],
                                              layer.down_p[e], layer.down_s[e])] for e in range(E)]
         self.tables = torch.tensor(cols, dtype=torch.int64, device=layer.gate_p.device).t().contiguous()
+        self.tables_tiled = None
+        cfg = self.cfg
+        if tiled and cfg.hidden % 256 == 0 and cfg.inter % 128 == 0:
+            lib = native.load_library()
+            dev = layer.gate_p.device
+            tb13 = int(lib.moe_q4_tiled_bytes(cfg.inter, cfg.hidden))
+            tb2 = int(lib.moe_q4_tiled_bytes(cfg.hidden, cfg.inter))
+            self._tiled13 = torch.empty((E, 2, tb13), dtype=torch.uint8, device=dev)
+            self._tiled2 = torch.empty((E, tb2), dtype=torch.uint8, device=dev)
+            tcols = [list(c) for c in cols]
+            for e in range(E):
+                for src, dst, rows, k in ((layer.gate_p[e], self._tiled13[e, 0], cfg.inter, cfg.hidden),
+                                          (layer.up_p[e], self._tiled13[e, 1], cfg.inter, cfg.hidden),
+                                          (layer.down_p[e], self._tiled2[e], cfg.hidden, cfg.inter)):
+                    native._check(lib.moe_q4_tile_weights(native._ptr(src), native._ptr(dst), rows, k,
+                                                          native._stream()), "moe_q4_tile_weights")
+                tcols[e][0] = int(self._tiled13[e, 0].data_ptr())
+                tcols[e][2] = int(self._tiled13[e, 1].data_ptr())
+                tcols[e][4] = int(self._tiled2[e].data_ptr())
+            self.tables_tiled = torch.tensor(tcols, dtype=torch.int64, device=dev).t().contiguous()
         self._workspace = torch.empty((0,), dtype=torch.uint8, device=layer.gate_p.device)
 
     def workspace_for(self, tokens: int) -> torch.Tensor:
@@ -273,13 +300,21 @@ class Q4MoELayerGPU:
         return self._workspace
 
     def forward(self, hidden: torch.Tensor, *, out: torch.Tensor | None = None, ids: torch.Tensor | None = None,
-                weights: torch.Tensor | None = None) -> torch.Tensor:
-        """hidden [T, H] bf16 or fp16 on the layer's device -> out [T, H] same dtype."""
+                weights: torch.Tensor | None = None, layout: int | None = None) -> torch.Tensor:
+        """hidden [T, H] bf16 or fp16 on the layer's device -> out [T, H] same dtype.
+
+        layout: 0 (GEMV, row-major codes) or 1 (tcgen05 GEMM, tiled codes);
+        by default 1 from prefill_pairs pairs per expert on, when tiled."""
         cfg = self.cfg
         x = hidden.reshape(-1, cfg.hidden).contiguous()
         if x.dtype not in (torch.bfloat16, torch.float16):
             raise ValueError("hidden must be bf16 or fp16")
         T = int(x.shape[0])
+        if layout is None:
+            layout = int(self.tables_tiled is not None and T * cfg.top_k >= self.prefill_pairs * cfg.n_experts)
+        if layout == 1 and self.tables_tiled is None:
+            raise ValueError("layout 1 needs the tiled copy (tiled=True and hidden % 256, intermediate % 128 == 0)")
+        tables = self.tables_tiled if layout == 1 else self.tables
         if out is None:
             out = torch.empty((T, cfg.hidden), dtype=x.dtype, device=x.device)
         ws = self.workspace_for(T)
@@ -287,7 +322,7 @@ class Q4MoELayerGPU:
         rdt = {torch.float32: native.DTYPE_F32, torch.bfloat16: native.DTYPE_BF16, torch.float16: native.DTYPE_F16}
         code = native.load_library().moe_q4_moe_layer_u16(
             native._ptr(x), rdt[x.dtype], T, cfg.hidden, cfg.inter, native._ptr(rw), rdt[rw.dtype], cfg.n_experts,
-            cfg.top_k, native._ptr(self.tables), native._ptr(out), native._ptr(ids), native._ptr(weights),
+            cfg.top_k, native._ptr(tables), int(layout), native._ptr(out), native._ptr(ids), native._ptr(weights),
             native._ptr(ws), ws.numel(), native._stream())
         native._check(code, "moe_q4_moe_layer_u16")
         return out
