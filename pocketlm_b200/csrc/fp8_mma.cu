@@ -357,20 +357,36 @@ MOE_D void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// acc += this lane's share of W[k-blocks kb0..kb1) . x for one task
-// TILED: the weights are in the fragment-native layout of fp8_tile_kernel
-// (tbase[st] = this lane's 16 bytes of piece rr = 0, half sp = 0 of k-block 0
-// of stream st's 16-row tile); otherwise row-major (arow[st][rr] = row
-// g + 8 rr at column 16 c).
+// One warp unit's operand addresses: a task's k-range [kb0, kb1) (empty when
+// the expert is absent).  TILED: the weights are in the fragment-native layout
+// of fp8_tile_kernel (tbase[st] = this lane's 16 bytes of piece rr = 0, half
+// sp = 0 of k-block 0 of stream st's 16-row tile); otherwise row-major
+// (arow[st][rr] = row g + 8 rr at column 16 c).
+struct UnitOperands {
+  const uint8_t* arow[2][2];
+  const uint8_t* tbase[2];
+  const float* srow[2];
+  const __half* xb;
+  bool bvalid;
+  int kb0, kb1;
+};
+
+// acc += this lane's share of W[k-blocks kb0..kb1) . x for unit u.  The warp's
+// ring is one pipeline across its units: step j of u sits in stage (step0 + j)
+// % kAsyncStages, the first `primed` steps of u were issued by the previous
+// unit, and in its last k-blocks this unit issues the first steps of the next
+// unit `nx` (returned: how many), so the ring does not drain between units.
+// Every iteration commits one cp.async group (possibly empty) and the prologue
+// kAsyncStages - 1 - primed, so kAsyncStages - 1 newer groups always follow
+// the one being waited for.  Each lane reads only its own ring slots.
 template <bool FIX, bool TILED>
-MOE_D void async_accumulate(float (&acc)[2][4], unsigned char* ring, const uint8_t* const (&arow)[2][2],
-                            const uint8_t* const (&tbase)[2], const float* const (&srow)[2], const __half* xb,
-                            bool bvalid, int kb0, int kb1, int lane, int c) {
-  auto slot = [&](int stage, int i) { return ring + stage * kAsyncStageBytes + (i * kWarp + lane) * 16; };
+MOE_D int async_accumulate(float (&acc)[2][4], unsigned char* ring, const UnitOperands& u, const UnitOperands& nx,
+                           uint32_t step0, int primed, int lane) {
+  auto slot = [&](uint32_t stage, int i) { return ring + stage * kAsyncStageBytes + (i * kWarp + lane) * 16; };
   // slots 0-7: this lane's weight pieces (span, stream, row half); 8-11: its
   // activation pieces (span, half); an absent token row is zero-filled
-  auto issue = [&](int kbi) {
-    const int stage = (kbi - kb0) % kAsyncStages;
+  auto issue = [&](const UnitOperands& o, int kbi, uint32_t step) {
+    const uint32_t stage = step % kAsyncStages;
 #pragma unroll
     for (int sp = 0; sp < 2; ++sp) {
 #pragma unroll
@@ -378,27 +394,35 @@ MOE_D void async_accumulate(float (&acc)[2][4], unsigned char* ring, const uint8
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr)
           cp_async16(slot(stage, (sp * 2 + st) * 2 + rr),
-                     TILED ? tbase[st] + static_cast<int64_t>(kbi) * kTileKBlockStride + sp * kTileRunBytes + rr * (kWarp * 16)
-                           : arow[st][rr] + kbi * kBlock + sp * 64);
+                     TILED ? o.tbase[st] + static_cast<int64_t>(kbi) * kTileKBlockStride + sp * kTileRunBytes + rr * (kWarp * 16)
+                           : o.arow[st][rr] + kbi * kBlock + sp * 64);
 #pragma unroll
       for (int h = 0; h < 2; ++h)
-        cp_async16_zfill(slot(stage, 8 + sp * 2 + h), xb + kbi * kBlock + sp * 64 + h * 8, bvalid ? 16 : 0);
+        cp_async16_zfill(slot(stage, 8 + sp * 2 + h), o.xb + kbi * kBlock + sp * 64 + h * 8, o.bvalid ? 16 : 0);
     }
   };
-#pragma unroll
-  for (int j = 0; j < kAsyncStages - 1; ++j) {
-    if (kb0 + j < kb1) issue(kb0 + j);
+  const int kb0 = u.kb0, kb1 = u.kb1, n = kb1 - kb0;
+  const int nx_steps = nx.kb1 - nx.kb0;
+  int nx_issued = 0;
+  for (int j = primed; j < kAsyncStages - 1; ++j) {
+    if (j < n) issue(u, kb0 + j, step0 + j);
     cp_async_commit();
   }
-  float sc0 = __ldg(srow[0] + kb0), sc1 = __ldg(srow[1] + kb0);
+  float sc0 = __ldg(u.srow[0] + kb0), sc1 = __ldg(u.srow[1] + kb0);
   for (int kbi = kb0; kbi < kb1; ++kbi) {
-    if (kbi + kAsyncStages - 1 < kb1) issue(kbi + kAsyncStages - 1);
+    const int ahead = kbi - kb0 + kAsyncStages - 1;  // step of u (or beyond: of nx) to issue now
+    if (ahead < n) {
+      issue(u, kb0 + ahead, step0 + ahead);
+    } else if (nx_issued < nx_steps && nx_issued < kAsyncStages - 1) {
+      issue(nx, nx.kb0 + nx_issued, step0 + n + nx_issued);
+      ++nx_issued;
+    }
     cp_async_commit();
     // next k-block's scales load while this one is multiplied
     const int kn = min(kbi + 1, kb1 - 1);
-    const float nsc0 = __ldg(srow[0] + kn), nsc1 = __ldg(srow[1] + kn);
+    const float nsc0 = __ldg(u.srow[0] + kn), nsc1 = __ldg(u.srow[1] + kn);
     cp_async_wait<kAsyncStages - 1>();  // this lane's copies of k-block kbi have landed
-    const int stage = (kbi - kb0) % kAsyncStages;
+    const uint32_t stage = (step0 + kbi - kb0) % kAsyncStages;
     float t[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int sp = 0; sp < 2; ++sp) {
@@ -436,7 +460,7 @@ MOE_D void async_accumulate(float (&acc)[2][4], unsigned char* ring, const uint8
     sc0 = nsc0;
     sc1 = nsc1;
   }
-  cp_async_wait<0>();  // nothing of this task in flight before the ring is reused
+  return nx_issued;
 }
 
 template <int NS, int EPI, bool TILED>
@@ -455,11 +479,13 @@ __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(Mma
   const int64_t warp_count = static_cast<int64_t>(gridDim.x) * kAsyncWarps;
   const int nkb = K / kBlock;
 
-  for (int64_t unit = warp_global; unit < units; unit += warp_count) {
+  // operand addresses of a unit (an empty k-range when out of range or the expert is absent)
+  auto operands = [&](int64_t unit, UnitOperands& o, bool& fix) {
+    o.kb0 = o.kb1 = 0;
+    fix = false;
+    if (unit >= units) return;
     const int64_t task = unit / ksplit;
     const int ks = static_cast<int>(unit % ksplit);
-    const int kb0 = static_cast<int>(static_cast<int64_t>(ks) * nkb / ksplit);
-    const int kb1 = static_cast<int>(static_cast<int64_t>(ks + 1) * nkb / ksplit);
     const int ch = static_cast<int>(task / row_tiles);
     const int r0 = static_cast<int>(task % row_tiles) * kTaskRows;
     const int seg = a.chunk_seg[ch], p0 = a.chunk_start[ch], len = a.chunk_len[ch];
@@ -469,8 +495,7 @@ __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(Mma
     const float* s1 = NS == 2 ? reinterpret_cast<const float*>(a.s1[seg]) : s0;
     const bool present = w0 && s0 && w1 && s1 &&
                          ((reinterpret_cast<uintptr_t>(w0) | reinterpret_cast<uintptr_t>(w1)) & 15u) == 0;
-    const uint8_t* arow[2][2];
-    const float* srow[2];
+    if (!present) return;
 #pragma unroll
     for (int st = 0; st < 2; ++st) {
       const int base = NS == 2 ? r0 : r0 + 16 * st;
@@ -479,26 +504,44 @@ __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(Mma
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
         const int row = min(base + g + 8 * rr, N - 1);
-        arow[st][rr] = present ? w + static_cast<int64_t>(row) * K + 16 * c : nullptr;
+        o.arow[st][rr] = w + static_cast<int64_t>(row) * K + 16 * c;
       }
-      srow[st] = present ? sc + static_cast<int64_t>(min(base, N - 1) / kBlock) * a.scale_cols : nullptr;
-    }
-    const uint8_t* tbase[2];
-#pragma unroll
-    for (int st = 0; st < 2; ++st) {
+      o.srow[st] = sc + static_cast<int64_t>(min(base, N - 1) / kBlock) * a.scale_cols;
       const int64_t tile = NS == 2 ? r0 / 16 : r0 / 16 + st;
-      tbase[st] = present ? (st == 0 ? w0 : w1) + tiled_offset(tile, 0, 0, nkb) + lane * 16 : nullptr;
+      o.tbase[st] = w + tiled_offset(tile, 0, 0, nkb) + lane * 16;
     }
-    const bool bvalid = g < len;
-    const int64_t brow = bvalid ? (a.pair_row ? a.pair_row[p0 + g] : static_cast<int64_t>(p0 + g)) : 0;
-    const __half* xb = a.x16 + brow * K + 16 * c;
+    o.bvalid = g < len;
+    const int64_t brow = o.bvalid ? (a.pair_row ? a.pair_row[p0 + g] : static_cast<int64_t>(p0 + g)) : 0;
+    o.xb = a.x16 + brow * K + 16 * c;
+    o.kb0 = static_cast<int>(static_cast<int64_t>(ks) * nkb / ksplit);
+    o.kb1 = static_cast<int>(static_cast<int64_t>(ks + 1) * nkb / ksplit);
+    fix = a.nanfix && !(a.nan_free && a.nan_free[seg]);
+  };
+
+  UnitOperands cur, nxt;
+  bool cur_fix, nxt_fix;
+  operands(warp_global, cur, cur_fix);
+  uint32_t step0 = 0;  // ring steps (k-blocks) of this warp's earlier units
+  int primed = 0;      // k-blocks of `cur` already issued by the previous unit
+  for (int64_t unit = warp_global; unit < units; unit += warp_count) {
+    const int64_t task = unit / ksplit;
+    const int ks = static_cast<int>(unit % ksplit);
+    const int ch = static_cast<int>(task / row_tiles);
+    const int r0 = static_cast<int>(task % row_tiles) * kTaskRows;
+    const int p0 = a.chunk_start[ch], len = a.chunk_len[ch];
+    operands(unit + warp_count, nxt, nxt_fix);
 
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    if (present && kb0 < kb1) {
-      const bool fix = a.nanfix && !(a.nan_free && a.nan_free[seg]);
-      if (fix) async_accumulate<true, TILED>(acc, ring, arow, tbase, srow, xb, bvalid, kb0, kb1, lane, c);
-      else async_accumulate<false, TILED>(acc, ring, arow, tbase, srow, xb, bvalid, kb0, kb1, lane, c);
+    const int n = cur.kb1 - cur.kb0;
+    int nx_primed = 0;
+    if (n > 0) {
+      nx_primed = cur_fix ? async_accumulate<true, TILED>(acc, ring, cur, nxt, step0, primed, lane)
+                          : async_accumulate<false, TILED>(acc, ring, cur, nxt, step0, primed, lane);
     }
+    step0 += n;
+    primed = nx_primed;
+    cur = nxt;
+    cur_fix = nxt_fix;
 
     if (ksplit > 1) {
       float4* part = reinterpret_cast<float4*>(a.partial + (task * ksplit + ks) * (kWarp * 8) + lane * 8);
@@ -552,6 +595,7 @@ __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(Mma
       }
     }
   }
+  cp_async_wait<0>();  // no copy of this warp in flight when it exits
 }
 
 // flags[s] = 1 when expert s's three weight matrices hold no 0x7F / 0xFF byte.
