@@ -233,6 +233,8 @@ __global__ void q4_tile_kernel(const uint8_t* __restrict__ src, uint8_t* __restr
 // --------------------------------------------------------------- kernel
 template <bool GATEUP, int WF>
 __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                                    const __grid_constant__ CUtensorMap tmap_a64,
+                                                                    const __grid_constant__ CUtensorMap tmap_a32,
                                                                     PrefillArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -309,9 +311,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
           if (it >= kStages && !wait_or_abort(&bars->empty[s], ((it / kStages) - 1) & 1, abort)) break;
           // the second sub-tile only when the tile has more than 128 pairs
           const bool two = tr.rows > kSubM;
-          mbar_arrive_expect_tx(&bars->full[s], (two ? 2 : 1) * kATileBytes + 2 * kRunBytes);
-          tma_load_2d(a_tile(s, 0), &tmap_a, kh * kBK, tr.row0, &bars->full[s]);
-          if (two) tma_load_2d(a_tile(s, 1), &tmap_a, kh * kBK, tr.row0 + kSubM, &bars->full[s]);
+          // a sub-tile of <= 32 / 64 pairs loads that many rows (the rest of the
+          // 128-row tile keeps stale data; its results are never stored)
+          const int rows0 = min(tr.rows, kSubM), rows1 = tr.rows - kSubM;
+          auto a_box = [&](int rows) { return rows <= 32 ? &tmap_a32 : rows <= 64 ? &tmap_a64 : &tmap_a; };
+          auto a_bytes = [&](int rows) { return rows <= 32 ? kATileBytes / 4 : rows <= 64 ? kATileBytes / 2 : kATileBytes; };
+          mbar_arrive_expect_tx(&bars->full[s], a_bytes(rows0) + (two ? a_bytes(rows1) : 0) + 2 * kRunBytes);
+          tma_load_2d(a_tile(s, 0), a_box(rows0), kh * kBK, tr.row0, &bars->full[s]);
+          if (two) tma_load_2d(a_tile(s, 1), a_box(rows1), kh * kBK, tr.row0 + kSubM, &bars->full[s]);
 #pragma unroll
           for (int h = 0; h < 2; ++h) bulk_copy_g2s(raw_tile(s) + h * kRunBytes, run_at(h, kh), kRunBytes, &bars->full[s]);
         }
@@ -770,22 +777,25 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, bool gateup, int64_t max_t
   if ((reinterpret_cast<uintptr_t>(a.a16) & 15u) != 0) return cudaErrorInvalidValue;
   auto encode = encode_fn();
   if (!encode) return cudaErrorNotSupported;
-  CUtensorMap tmap;
+  // A boxes of 128, 64 and 32 rows (the smaller ones for small tiles)
+  CUtensorMap tmap[3];
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.K), static_cast<cuuint64_t>(a.rows_a)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.K) * 2};
-  const cuuint32_t box[2] = {kBK, kSubM};
   const cuuint32_t estr[2] = {1, 1};
-  if (encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(a.a16), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return cudaErrorInvalidValue;
+  for (int i = 0; i < 3; ++i) {
+    const cuuint32_t box[2] = {kBK, static_cast<cuuint32_t>(kSubM >> i)};
+    if (encode(&tmap[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(a.a16), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
   const bool q4 = a.wformat == kPrefillQ4Row;
   auto kernel = gateup ? (q4 ? prefill_gemm_kernel<true, kPrefillQ4Row> : prefill_gemm_kernel<true, kPrefillFp8Block>)
                        : (q4 ? prefill_gemm_kernel<false, kPrefillQ4Row> : prefill_gemm_kernel<false, kPrefillFp8Block>);
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
   if (err != cudaSuccess) return err;
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(gemv_grid_ctas(), max_tiles)));
-  kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmap, a);
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmap[0], tmap[1], tmap[2], a);
   return cudaGetLastError();
 }
 
