@@ -674,14 +674,22 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
 
 // The expert stages on the tcgen05 grouped GEMM (tiled weights): gather the
 // pairs' fp16 rows, gate/up + SwiGLU, stage the activations, down.
-static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16, const LayerPlan& l, int64_t T,
+static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16, int64_t k, bool shared,
+                                     const LayerPlan& l, int64_t T,
                                      int64_t pairs, int64_t n_segments, int64_t I, int64_t H, const uint8_t* nan_free,
                                      cudaStream_t s) {
   const MlpScratch& m = l.m;
-  MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.x16, l.xscale, nullptr,
-                              0, s),
-           "stage x");
-  MOE_CUDA(launch_gather_rows(l.x16, l.xscale, m.pair_row, pairs, H, l.a16, l.a16scale, s), "gather pairs");
+  // each token's row staged once and written to its pairs' rows (the shared pairs follow the routed ones)
+  cudaError_t serr = launch_scatter_rows(x, x_bf16 ? kDtypeBF16 : kDtypeF32, T, H, m.entry_pair, static_cast<int>(k),
+                                         shared ? m.seg_offset + (n_segments - 1) : nullptr, l.a16, l.a16scale, s);
+  if (serr == cudaErrorNotSupported) {
+    MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.x16, l.xscale,
+                                nullptr, 0, s),
+             "stage x");
+    MOE_CUDA(launch_gather_rows(l.x16, l.xscale, m.pair_row, pairs, H, l.a16, l.a16scale, s), "gather pairs");
+  } else {
+    MOE_CUDA(serr, "stage pairs");
+  }
   MOE_CUDA(launch_prefill_tiles(m.seg_offset, static_cast<int>(n_segments), l.mprefix, s), "tile map");
   stage_mark(s);
   const int64_t mtiles_bound = pairs / 128 + n_segments;
@@ -849,7 +857,8 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   const bool prefill = weight_layout == 1 && T >= kPrefillMinTokens && l.a16 != nullptr &&
                        prefill_supported(H, I, true) && prefill_supported(I, H, false);
   if (prefill) {
-    code = run_expert_stages_prefill(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I,
+    code = run_expert_stages_prefill(t, hidden, hidden_dtype == kDtypeBF16, k, has_shared != 0, l, T,
+                                     T * k + (has_shared ? T : 0), S, I,
                                      H, nan_free, s);
   } else if (use_mma) {
     code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I, H,

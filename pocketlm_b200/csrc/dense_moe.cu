@@ -263,13 +263,20 @@ size_t routed_need(int kind, int64_t T, int64_t H, int64_t I, int64_t E, int64_t
 // pair's output as the GEMV path leaves it.
 int run_q4_prefill(const DenseTables& t, const void* x, int x_dtype, int64_t T, int64_t pairs, int64_t E, int64_t H,
                    int64_t I, const DensePlan& d, cudaStream_t s) {
-  if (x_dtype == kDtypeF16)
-    MOE_CUDA(launch_f16_rows_to_f16(x, static_cast<int>(T), static_cast<int>(H), d.x16, d.x16scale, s), "stage x");
-  else
-    MOE_CUDA(launch_rows_to_f16(x, true, static_cast<int>(T), static_cast<int>(H), nullptr, d.x16, d.x16scale, nullptr,
-                                0, s),
-             "stage x");
-  MOE_CUDA(launch_gather_rows(d.x16, d.x16scale, d.pair_row, pairs, H, d.a16, d.a16scale, s), "gather pairs");
+  // each token's row staged once and written to its pairs' rows
+  const cudaError_t serr = launch_scatter_rows(x, x_dtype, T, H, d.row_pairs, static_cast<int>(pairs / T), nullptr,
+                                               d.a16, d.a16scale, s);
+  if (serr == cudaErrorNotSupported) {
+    if (x_dtype == kDtypeF16)
+      MOE_CUDA(launch_f16_rows_to_f16(x, static_cast<int>(T), static_cast<int>(H), d.x16, d.x16scale, s), "stage x");
+    else
+      MOE_CUDA(launch_rows_to_f16(x, true, static_cast<int>(T), static_cast<int>(H), nullptr, d.x16, d.x16scale,
+                                  nullptr, 0, s),
+               "stage x");
+    MOE_CUDA(launch_gather_rows(d.x16, d.x16scale, d.pair_row, pairs, H, d.a16, d.a16scale, s), "gather pairs");
+  } else {
+    MOE_CUDA(serr, "stage pairs");
+  }
   MOE_CUDA(launch_prefill_tiles(d.seg_offset, static_cast<int>(E), d.mprefix, s), "tile map");
   const int64_t mtiles_bound = pairs / 128 + E;
   PrefillArgs g1{};

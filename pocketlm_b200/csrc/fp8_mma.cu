@@ -92,6 +92,69 @@ MOE_D void unpack16<__half>(const uint4& v, float* out) {
 // dst[r, k] = src[r, k] / scale[r], scale = 2^(floor(log2(amax)) - 13) so the
 // largest magnitude lands in [2^13, 2^14) (1 for an all-zero row).  One CTA
 // per row, 16-byte loads (K * sizeof(T) must be a multiple of 16).
+// The same for rows of at most 256 x 16 bytes (K <= 2048 fp32 or 4096 16-bit
+// values): each thread keeps its 16-byte pieces in registers between the
+// max and the conversion, so a row is read once.
+template <typename T, int P>
+__global__ void __launch_bounds__(256) rows_to_f16_regs_kernel(const T* __restrict__ src, int rows, int K,
+                                                               const int32_t* __restrict__ n_rows_dev,
+                                                               __half* __restrict__ dst, float* __restrict__ scale,
+                                                               int32_t* __restrict__ zero, int64_t zero_n) {
+  constexpr int V = 16 / sizeof(T);
+  __shared__ float red[8];
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < zero_n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    zero[i] = 0;
+  const int n_rows = n_rows_dev ? min(rows, *n_rows_dev) : rows;
+  const int n16 = K / V;
+  for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
+    const uint4* s = reinterpret_cast<const uint4*>(src + static_cast<int64_t>(r) * K);
+    uint4 v[P];
+    float amax = 0.0f;
+#pragma unroll
+    for (int q = 0; q < P; ++q) {
+      const int i = threadIdx.x + q * 256;
+      v[q] = i < n16 ? __ldg(s + i) : make_uint4(0, 0, 0, 0);
+      float f[V];
+      unpack16<T>(v[q], f);
+#pragma unroll
+      for (int j = 0; j < V; ++j) amax = fmaxf(amax, fabsf(f[j]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+    if (threadIdx.x % kWarp == 0) red[threadIdx.x / kWarp] = amax;
+    __syncthreads();
+    if (threadIdx.x < kWarp) {
+      float w = threadIdx.x < blockDim.x / kWarp ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) w = fmaxf(w, __shfl_xor_sync(0xFFFFFFFFu, w, o));
+      if (threadIdx.x == 0) red[0] = w;
+    }
+    __syncthreads();
+    amax = red[0];
+    const float sc = (amax > 0.0f && isfinite(amax)) ? ldexpf(1.0f, ilogbf(amax) - 13) : 1.0f;
+    const float inv = 1.0f / sc;  // exact: power of two
+    __half* d = dst + static_cast<int64_t>(r) * K;
+#pragma unroll
+    for (int q = 0; q < P; ++q) {
+      const int i = threadIdx.x + q * 256;
+      if (i >= n16) continue;
+      float f[V];
+      unpack16<T>(v[q], f);
+      __align__(16) __half h[V];
+#pragma unroll
+      for (int j = 0; j < V; ++j) h[j] = __float2half_rn(f[j] * inv);
+      if (V == 8) {
+        *reinterpret_cast<uint4*>(d + i * V) = *reinterpret_cast<const uint4*>(h);
+      } else {
+        *reinterpret_cast<uint2*>(d + i * V) = *reinterpret_cast<const uint2*>(h);
+      }
+    }
+    if (threadIdx.x == 0) scale[r] = sc;
+    __syncthreads();
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) rows_to_f16_kernel(const T* __restrict__ src, int rows, int K,
                                                           const int32_t* __restrict__ n_rows_dev,
@@ -852,11 +915,25 @@ __global__ void __launch_bounds__(kTmaWarps * kWarp) tma_mma_gemv_kernel(MmaArgs
 
 bool mma_gemv_supported(int K, int N) { return K % kBlock == 0 && K > 0 && N > 0; }
 
+// rows of at most 4 x 256 16-byte pieces go through the single-read kernel
+template <typename T>
+static void launch_rows_to_f16_t(const T* src, int rows, int K, const int32_t* n_rows_dev, __half* dst, float* scale,
+                                 int32_t* zero, int64_t zero_n, unsigned grid, cudaStream_t stream) {
+  const int pieces = static_cast<int>(ceil_div(static_cast<int64_t>(K) * sizeof(T), 16));
+  if (pieces <= 256)
+    rows_to_f16_regs_kernel<T, 1><<<grid, 256, 0, stream>>>(src, rows, K, n_rows_dev, dst, scale, zero, zero_n);
+  else if (pieces <= 512)
+    rows_to_f16_regs_kernel<T, 2><<<grid, 256, 0, stream>>>(src, rows, K, n_rows_dev, dst, scale, zero, zero_n);
+  else if (pieces <= 1024)
+    rows_to_f16_regs_kernel<T, 4><<<grid, 256, 0, stream>>>(src, rows, K, n_rows_dev, dst, scale, zero, zero_n);
+  else
+    rows_to_f16_kernel<T><<<grid, 256, 0, stream>>>(src, rows, K, n_rows_dev, dst, scale, zero, zero_n);
+}
+
 cudaError_t launch_f16_rows_to_f16(const void* src, int rows, int K, __half* dst, float* scale, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   const unsigned grid = static_cast<unsigned>(std::min(rows, gemv_grid_ctas() * 8));
-  rows_to_f16_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(src), rows, K, nullptr, dst, scale,
-                                                       nullptr, 0);
+  launch_rows_to_f16_t(static_cast<const __half*>(src), rows, K, nullptr, dst, scale, nullptr, 0, grid, stream);
   return cudaGetLastError();
 }
 
@@ -866,11 +943,10 @@ cudaError_t launch_rows_to_f16(const void* src, bool src_bf16, int rows, int K, 
   if (zero_n > 0 && !zero) return cudaErrorInvalidValue;
   const unsigned grid = static_cast<unsigned>(std::min(rows, gemv_grid_ctas() * 8));
   if (src_bf16)
-    rows_to_f16_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(src), rows, K,
-                                                                 n_rows_dev, dst, scale, zero, zero_n);
+    launch_rows_to_f16_t(static_cast<const __nv_bfloat16*>(src), rows, K, n_rows_dev, dst, scale, zero, zero_n, grid,
+                         stream);
   else
-    rows_to_f16_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(src), rows, K, n_rows_dev, dst,
-                                                         scale, zero, zero_n);
+    launch_rows_to_f16_t(static_cast<const float*>(src), rows, K, n_rows_dev, dst, scale, zero, zero_n, grid, stream);
   return cudaGetLastError();
 }
 

@@ -230,6 +230,103 @@ __global__ void q4_tile_kernel(const uint8_t* __restrict__ src, uint8_t* __restr
   }
 }
 
+// 16 bytes of activations -> floats
+template <typename T>
+MOE_D void piece_to_float(const uint4& v, float* out);
+template <>
+MOE_D void piece_to_float<float>(const uint4& v, float* out) {
+  out[0] = __uint_as_float(v.x); out[1] = __uint_as_float(v.y);
+  out[2] = __uint_as_float(v.z); out[3] = __uint_as_float(v.w);
+}
+template <>
+MOE_D void piece_to_float<__nv_bfloat16>(const uint4& v, float* out) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(w[i] << 16);
+    out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+template <>
+MOE_D void piece_to_float<__half>(const uint4& v, float* out) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
+  }
+}
+
+// The pairs' A rows straight from the tokens: token t's row (read once, kept
+// in registers) -> fp16 / power-of-two scale (the rows_to_f16 staging:
+// 2^(floor(log2 amax) - 13), 1 for an all-zero row), written to the row of
+// each of its pairs: entry_pair[t * k + j] (>= 0), then, with a shared
+// expert, pair *tail_first + t.  One CTA per token.
+template <typename T, int P>
+__global__ void __launch_bounds__(256) scatter_rows_kernel(const T* __restrict__ x, int T_, int K,
+                                                           const int32_t* __restrict__ entry_pair, int k,
+                                                           const int32_t* __restrict__ tail_first,
+                                                           __half* __restrict__ a16, float* __restrict__ ascale) {
+  constexpr int V = 16 / sizeof(T);
+  __shared__ float red[8];
+  const int n16 = K / V;
+  for (int t = blockIdx.x; t < T_; t += gridDim.x) {
+    const uint4* s = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * K);
+    uint4 v[P];
+    float amax = 0.0f;
+#pragma unroll
+    for (int q = 0; q < P; ++q) {
+      const int i = threadIdx.x + q * 256;
+      v[q] = i < n16 ? __ldg(s + i) : make_uint4(0, 0, 0, 0);
+      float f[V];
+      piece_to_float<T>(v[q], f);
+#pragma unroll
+      for (int j = 0; j < V; ++j) amax = fmaxf(amax, fabsf(f[j]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+    if (threadIdx.x % kWarp == 0) red[threadIdx.x / kWarp] = amax;
+    __syncthreads();
+    if (threadIdx.x < kWarp) {
+      float w = threadIdx.x < blockDim.x / kWarp ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) w = fmaxf(w, __shfl_xor_sync(0xFFFFFFFFu, w, o));
+      if (threadIdx.x == 0) red[0] = w;
+    }
+    __syncthreads();
+    amax = red[0];
+    const float sc = (amax > 0.0f && isfinite(amax)) ? ldexpf(1.0f, ilogbf(amax) - 13) : 1.0f;
+    const float inv = 1.0f / sc;  // exact: power of two
+    // fp16 pieces: V values each (8 halves = 16 bytes, or 4 halves = 8 bytes for fp32 input)
+    uint4 h16[P];
+#pragma unroll
+    for (int q = 0; q < P; ++q) {
+      float f[V];
+      piece_to_float<T>(v[q], f);
+      __align__(16) __half h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(j < V ? f[j] * inv : 0.0f);
+      h16[q] = *reinterpret_cast<const uint4*>(h);
+    }
+    const int n_out = k + (tail_first ? 1 : 0);
+    for (int j = 0; j < n_out; ++j) {
+      const int p = j < k ? entry_pair[static_cast<int64_t>(t) * k + j] : *tail_first + t;
+      if (p < 0) continue;
+      __half* d = a16 + static_cast<int64_t>(p) * K;
+#pragma unroll
+      for (int q = 0; q < P; ++q) {
+        const int i = threadIdx.x + q * 256;
+        if (i >= n16) continue;
+        if (V == 8) *reinterpret_cast<uint4*>(d + i * V) = h16[q];
+        else *reinterpret_cast<uint2*>(d + i * V) = make_uint2(h16[q].x, h16[q].y);
+      }
+      if (threadIdx.x == 0) ascale[p] = sc;
+    }
+    __syncthreads();
+  }
+}
+
 // --------------------------------------------------------------- kernel
 template <bool GATEUP, int WF>
 __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -859,6 +956,38 @@ cudaError_t launch_q4_tile(const uint8_t* packed, uint8_t* tiled, int64_t rows, 
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(units, 256), gemv_grid_ctas() * 16));
   q4_tile_kernel<<<grid, 256, 0, stream>>>(packed, tiled, rows, K);
   return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_scatter_t(const void* x, int64_t T_, int64_t K, const int32_t* entry_pair, int k,
+                                    const int32_t* tail_first, __half* a16, float* ascale, cudaStream_t stream) {
+  const int64_t pieces = K * static_cast<int64_t>(sizeof(T)) / 16;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(T_, gemv_grid_ctas() * 8));
+  const T* xs = static_cast<const T*>(x);
+  if (pieces <= 256)
+    scatter_rows_kernel<T, 1><<<grid, 256, 0, stream>>>(xs, static_cast<int>(T_), static_cast<int>(K), entry_pair, k,
+                                                        tail_first, a16, ascale);
+  else if (pieces <= 512)
+    scatter_rows_kernel<T, 2><<<grid, 256, 0, stream>>>(xs, static_cast<int>(T_), static_cast<int>(K), entry_pair, k,
+                                                        tail_first, a16, ascale);
+  else if (pieces <= 1024)
+    scatter_rows_kernel<T, 4><<<grid, 256, 0, stream>>>(xs, static_cast<int>(T_), static_cast<int>(K), entry_pair, k,
+                                                        tail_first, a16, ascale);
+  else
+    return cudaErrorNotSupported;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_rows(const void* x, int x_dtype, int64_t T_, int64_t K, const int32_t* entry_pair, int k,
+                                const int32_t* tail_first, __half* a16, float* ascale, cudaStream_t stream) {
+  if (T_ <= 0) return cudaSuccess;
+  if (K % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15u)) return cudaErrorNotSupported;
+  switch (x_dtype) {
+    case kDtypeBF16: return launch_scatter_t<__nv_bfloat16>(x, T_, K, entry_pair, k, tail_first, a16, ascale, stream);
+    case kDtypeF16: return launch_scatter_t<__half>(x, T_, K, entry_pair, k, tail_first, a16, ascale, stream);
+    case kDtypeF32: return launch_scatter_t<float>(x, T_, K, entry_pair, k, tail_first, a16, ascale, stream);
+    default: return cudaErrorNotSupported;
+  }
 }
 
 int read_and_clear_prefill_device_error(cudaStream_t stream) { return read_and_clear_local_error(stream); }

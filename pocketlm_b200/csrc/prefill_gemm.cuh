@@ -48,6 +48,12 @@ bool prefill_supported(int64_t K, int64_t N, bool gateup);
 cudaError_t launch_prefill_tiles(const int32_t* seg_offset, int n_segments, int32_t* mprefix, cudaStream_t stream);
 cudaError_t launch_gather_rows(const __half* x16, const float* xscale, const int32_t* pair_row, int64_t P, int64_t K,
                                __half* xa, float* ascale, cudaStream_t stream);
+// Stage the tokens' rows as fp16 / power-of-two scale straight into their pairs'
+// A rows (entry_pair [T, k], -1 = dropped; with tail_first, the shared pair of
+// token t is *tail_first + t): the staging plus gather_rows in one read of x.
+// cudaErrorNotSupported when a row exceeds 16 KiB or is not 16-byte aligned.
+cudaError_t launch_scatter_rows(const void* x, int x_dtype, int64_t T, int64_t K, const int32_t* entry_pair, int k,
+                                const int32_t* tail_first, __half* a16, float* ascale, cudaStream_t stream);
 // max_tiles: an upper bound on the tiles (grid size); the kernel reads the real count.
 cudaError_t launch_prefill_gemm(const PrefillArgs& a, bool gateup, int64_t max_tiles, cudaStream_t stream);
 int read_and_clear_prefill_device_error(cudaStream_t stream);
