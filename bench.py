@@ -567,6 +567,22 @@ def run_profile_prefill(args) -> dict:
     return {"profile_case": f"c3-shape-{E}-experts-T{args.tokens}", "launches": args.warmup + args.steps}
 
 
+def run_profile_q4(args) -> dict:
+    """A Q4 case for ncu: the config-4 Mixtral layer (8 experts, 2.1 GB of
+    packed codes + the tiled copy), --tokens tokens, eager forwards."""
+    from pocketlm_b200 import native, synth
+    from pocketlm_b200.runtime import Q4MoELayerGPU
+
+    dev = torch.device("cuda", 0)
+    native.load_library()
+    layer = Q4MoELayerGPU(synth.make_q4_layer(synth.C4_MIXTRAL, seed=args.seed, device=dev))
+    x = synth.make_hidden(args.tokens, synth.C4_MIXTRAL.hidden, seed=args.seed + 1, device=dev)
+    for _ in range(args.warmup + args.steps):
+        layer.forward(x)
+    torch.cuda.synchronize()
+    return {"profile_case": f"c4-mixtral-q4-T{args.tokens}", "launches": args.warmup + args.steps}
+
+
 def run_reference(args, rank: int, world: int) -> dict | None:
     if rank != 0:
         return None
@@ -618,6 +634,8 @@ def main() -> None:
                         help="run the small prefill ncu case (DS-V3 expert shapes, 32 experts) instead")
     parser.add_argument("--profile-prefill-experts", type=int, default=32,
                         help="routed experts of the --profile-prefill layer (32 small case, 256 full config 3)")
+    parser.add_argument("--profile-q4", action="store_true",
+                        help="run the config-4 Q4 layer for --tokens tokens (an ncu case)")
     parser.add_argument("--profile-no-experts", action="store_true",
                         help="with --profile: materialise no expert (for captures of the routing kernels)")
     args = parser.parse_args()
@@ -637,6 +655,8 @@ def main() -> None:
     try:
         if args.profile_prefill:
             result = run_profile_prefill(args)
+        elif args.profile_q4:
+            result = run_profile_q4(args)
         elif args.profile:
             result = run_profile_case(args)
         else:

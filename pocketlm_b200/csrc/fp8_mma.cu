@@ -92,9 +92,9 @@ MOE_D void unpack16<__half>(const uint4& v, float* out) {
 // dst[r, k] = src[r, k] / scale[r], scale = 2^(floor(log2(amax)) - 13) so the
 // largest magnitude lands in [2^13, 2^14) (1 for an all-zero row).  One CTA
 // per row, 16-byte loads (K * sizeof(T) must be a multiple of 16).
-// The same for rows of at most 256 x 16 bytes (K <= 2048 fp32 or 4096 16-bit
-// values): each thread keeps its 16-byte pieces in registers between the
-// max and the conversion, so a row is read once.
+// The same for rows of at most P x 256 x 16 bytes (P <= 16: K <= 16384 fp32 or
+// 32768 16-bit values): each thread keeps its P 16-byte pieces in registers
+// between the max and the conversion, so a row is read once.
 template <typename T, int P>
 __global__ void __launch_bounds__(256) rows_to_f16_regs_kernel(const T* __restrict__ src, int rows, int K,
                                                                const int32_t* __restrict__ n_rows_dev,
@@ -926,6 +926,10 @@ static void launch_rows_to_f16_t(const T* src, int rows, int K, const int32_t* n
     rows_to_f16_regs_kernel<T, 2><<<grid, 256, 0, stream>>>(src, rows, K, n_rows_dev, dst, scale, zero, zero_n);
   else if (pieces <= 1024)
     rows_to_f16_regs_kernel<T, 4><<<grid, 256, 0, stream>>>(src, rows, K, n_rows_dev, dst, scale, zero, zero_n);
+  else if (pieces <= 2048)
+    rows_to_f16_regs_kernel<T, 8><<<grid, 256, 0, stream>>>(src, rows, K, n_rows_dev, dst, scale, zero, zero_n);
+  else if (pieces <= 4096)
+    rows_to_f16_regs_kernel<T, 16><<<grid, 256, 0, stream>>>(src, rows, K, n_rows_dev, dst, scale, zero, zero_n);
   else
     rows_to_f16_kernel<T><<<grid, 256, 0, stream>>>(src, rows, K, n_rows_dev, dst, scale, zero, zero_n);
 }
