@@ -431,8 +431,8 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
     """N > 1: expert parallelism.  Rank r holds routed experts
     [r * 256 / N, (r + 1) * 256 / N) plus the shared expert and router, and
     routes its own --tokens tokens; a step is one layer forward on every rank
-    (route, pack, NCCL all-to-alls, local grouped experts, reverse exchange,
-    combine).  Timed per rank with CUDA events between barriers; the max over
+    (route, rows written straight into their experts' ranks over NVLink,
+    local grouped experts, outputs written back, combine; ep.PeerExchange).  Timed per rank with CUDA events between barriers; the max over
     ranks is the step time; value = N * tokens / step time."""
     import torch.distributed as dist
 
@@ -510,9 +510,12 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
                      "experts_on_busiest_rank": busiest},
         "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * cfg.hidden * 2,
                 "d2h_bytes_per_step": T * cfg.hidden * 2},
-        # route (logits, select), pack (rank keys, bucket, gather), experts (bucket, chunk list,
-        # x staging, gate/up, activation staging, down, row order), combine
-        "gpu_launches": 13 * args.steps,
+        # peer exchange: route (logits, select), rank counts, dispatch (rank keys, bucket, scatter to
+        # peers), experts (bucket: 1 kernel, 3 above 2048 rows; chunk list, x staging, gate/up, activation
+        # staging, down, row order), return to peers, combine; all-to-all exchange: 13
+        "gpu_launches": (15 + (2 if ep.peer is not None and ep.peer.capacity + T > 2048 else 0)
+                         if ep.peer is not None else 13) * args.steps,
+        "exchange": "peer-memory (symmetric memory, NVLink stores)" if ep.peer is not None else "NCCL all-to-all",
         "cpu_baseline": None,
         "clocks": clock_info,
     }

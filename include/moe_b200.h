@@ -365,6 +365,33 @@ int64_t moe_ep_experts_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t
 int moe_ep_combine(const float* y, const int32_t* entry_pos, const float* pos_weight, int64_t tokens, int64_t top_k,
                    int64_t hidden_dim, int has_shared, uint16_t* out_bf16, void* stream);
 
+/* The exchange without collectives on the data path: every rank keeps
+ * receive buffers in peer-accessible memory (e.g. torch symmetric memory) --
+ * rows [capacity (+ own rows), hidden] bf16, expert int32 [capacity] (-1 =
+ * empty, reset before each step), src int32 [capacity], and a return buffer
+ * [src_stride + tokens, hidden] fp32 -- whose addresses on every rank the
+ * caller passes as device arrays uint64 [world].  A step:
+ *   moe_ep_count_ranks -> all-gather of the [world] counts into
+ *   count_matrix [world][world] (row = source rank) -> moe_ep_dispatch_p2p
+ *   (this rank's rows written into each destination's buffers, token order
+ *   kept, ranks in order) -> barrier -> moe_ep_experts_fp8 over the local
+ *   buffer -> moe_ep_return_p2p (each output row written into row e of its
+ *   source rank's return buffer, e = the entry t * top_k + slot) -> barrier
+ *   -> moe_ep_combine with entry_pos = identity.  src = rank * src_stride +
+ *   entry; src_stride >= the entries of any rank; capacity >= the rows any
+ *   rank receives (world * src_stride suffices).  The barriers are the
+ *   caller's (any stream-ordered collective).  Same arithmetic and combine
+ *   order as the all-to-all exchange above. */
+int moe_ep_count_ranks(const int64_t* ids, int64_t tokens, int64_t top_k, int64_t num_experts, int64_t world,
+                       int32_t* counts, void* stream);
+int moe_ep_dispatch_p2p(const int64_t* ids, const uint16_t* hidden_bf16, int64_t tokens, int64_t hidden_dim,
+                        int64_t top_k, int64_t num_experts, int64_t world, int64_t rank, const int32_t* count_matrix,
+                        int64_t capacity, int64_t src_stride, const uint64_t* peer_rows, const uint64_t* peer_expert,
+                        const uint64_t* peer_src, void* workspace, int64_t workspace_bytes, void* stream);
+int64_t moe_ep_dispatch_p2p_workspace_bytes(int64_t tokens, int64_t top_k, int64_t world);
+int moe_ep_return_p2p(const float* y, int64_t rows, const int32_t* recv_expert, const int32_t* recv_src,
+                      int64_t hidden_dim, int64_t src_stride, const uint64_t* peer_yback, void* stream);
+
 /* ---------------------------------------------------------------------------
  * DeepSeek session: opaque handle with the reference's observable counters.
  * ------------------------------------------------------------------------- */

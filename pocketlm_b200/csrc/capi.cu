@@ -318,6 +318,78 @@ __global__ void ep_gather_kernel(const uint16_t* hidden, const int64_t* ids, con
   }
 }
 
+// Expert-parallel exchange over NVLink peer memory.  Per-destination-rank
+// entry counts of this rank's (token, slot) entries.
+__global__ void ep_count_kernel(const int64_t* ids, int64_t n, int64_t per_rank, int world, int32_t* counts) {
+  extern __shared__ int32_t c[];
+  for (int r = threadIdx.x; r < world; r += blockDim.x) c[r] = 0;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const int64_t r = ids[i] / per_rank;
+    if (ids[i] >= 0 && r < world) atomicAdd(&c[r], 1);
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < world; r += blockDim.x) counts[r] = c[r];
+}
+
+// Rows to their experts' ranks: send position p (grouped by destination q,
+// token order inside) goes to row O(q) + p - send_offset[q] of rank q's
+// receive buffers, O(q) = the entries of ranks before this one bound for q
+// (count_matrix [world][world], row = source rank).  One warp per entry;
+// 16-byte stores straight into the peer's memory.
+__global__ void ep_p2p_scatter_kernel(const uint16_t* hidden, const int64_t* ids, const int32_t* keys,
+                                      const int32_t* pos_token, const int32_t* pos_entry, const int32_t* send_offset,
+                                      const int32_t* count_matrix, int64_t n, int64_t H, int64_t per_rank, int world,
+                                      int rank, int64_t capacity, int64_t src_stride, const uint64_t* peer_rows,
+                                      const uint64_t* peer_expert, const uint64_t* peer_src, int vec) {
+  const int lane = threadIdx.x % 32;
+  for (int64_t p = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) / 32; p < n;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
+    const int32_t e = pos_entry[p];
+    if (e < 0) continue;
+    const int q = keys[e];
+    int64_t slot = p - send_offset[q];
+    for (int r = 0; r < rank; ++r) slot += count_matrix[r * world + q];
+    if (slot >= capacity) continue;  // cannot happen with capacity >= the entries all ranks send to q
+    const uint16_t* src = hidden + static_cast<int64_t>(pos_token[p]) * H;
+    uint16_t* dst = reinterpret_cast<uint16_t*>(peer_rows[q]) + slot * H;
+    if (vec) {
+      for (int64_t i = lane; i < H / 8; i += 32)
+        reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+    } else {
+      for (int64_t i = lane; i < H; i += 32) dst[i] = src[i];
+    }
+    if (lane == 0) {
+      reinterpret_cast<int32_t*>(peer_expert[q])[slot] = static_cast<int32_t>(ids[e] - q * per_rank);
+      reinterpret_cast<int32_t*>(peer_src[q])[slot] = static_cast<int32_t>(rank * src_stride + e);
+    }
+  }
+  __threadfence_system();
+}
+
+// Expert outputs home: received row j (valid: expert >= 0) came from entry
+// e of rank r (src = r * src_stride + e); its fp32 output row goes to row e
+// of rank r's return buffer.  One warp per row.
+__global__ void ep_p2p_return_kernel(const float* y, int64_t rows, const int32_t* recv_expert, const int32_t* recv_src,
+                                     int64_t H, int64_t src_stride, const uint64_t* peer_yback, int vec) {
+  const int lane = threadIdx.x % 32;
+  for (int64_t j = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) / 32; j < rows;
+       j += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
+    if (recv_expert[j] < 0) continue;
+    const int32_t s = recv_src[j];
+    const int64_t r = s / src_stride, e = s % src_stride;
+    const float* src = y + j * H;
+    float* dst = reinterpret_cast<float*>(peer_yback[r]) + e * H;
+    if (vec) {
+      for (int64_t i = lane; i < H / 4; i += 32)
+        reinterpret_cast<float4*>(dst)[i] = __ldcs(reinterpret_cast<const float4*>(src) + i);
+    } else {
+      for (int64_t i = lane; i < H; i += 32) dst[i] = src[i];
+    }
+  }
+  __threadfence_system();
+}
+
 extern "C" {
 
 int moe_b200_abi_version(void) { return MOE_B200_ABI_VERSION; }
@@ -926,6 +998,82 @@ int moe_ep_dispatch_pack(const int64_t* ids, const float* weights, const uint16_
   ep_gather_kernel<<<grid_for(n * 32, 256), 256, 0, s>>>(hidden_bf16, ids, keys, pos_token, pos_entry, n, hidden_dim,
                                                          num_experts / world, vec, send_rows, send_expert);
   MOE_CUDA(cudaGetLastError(), "gather send rows");
+  return kOk;
+}
+
+int moe_ep_count_ranks(const int64_t* ids, int64_t tokens, int64_t top_k, int64_t num_experts, int64_t world,
+                       int32_t* counts, void* stream) {
+  if (!ids || !counts) return fail(kNullPointer, "null pointer");
+  if (tokens <= 0 || top_k <= 0 || world <= 0 || num_experts <= 0 || num_experts % world != 0 || world > 1024)
+    return fail(kBadDims, "bad dimensions (num_experts must be a multiple of world)");
+  ep_count_kernel<<<1, 256, static_cast<size_t>(world) * sizeof(int32_t), as_stream(stream)>>>(
+      ids, tokens * top_k, num_experts / world, static_cast<int>(world), counts);
+  MOE_CUDA(cudaGetLastError(), "count ranks");
+  return kOk;
+}
+
+int moe_ep_dispatch_p2p(const int64_t* ids, const uint16_t* hidden_bf16, int64_t tokens, int64_t hidden_dim,
+                        int64_t top_k, int64_t num_experts, int64_t world, int64_t rank, const int32_t* count_matrix,
+                        int64_t capacity, int64_t src_stride, const uint64_t* peer_rows, const uint64_t* peer_expert,
+                        const uint64_t* peer_src, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!ids || !hidden_bf16 || !count_matrix || !peer_rows || !peer_expert || !peer_src)
+    return fail(kNullPointer, "null pointer");
+  if (tokens <= 0 || hidden_dim <= 0 || top_k <= 0 || world <= 0 || num_experts <= 0 || num_experts % world != 0 ||
+      rank < 0 || rank >= world || capacity <= 0 || src_stride < tokens * top_k)
+    return fail(kBadDims, "bad dimensions");
+  if (world > kMaxBuckets) return fail(kUnsupported, "world too large");
+  const int64_t n = tokens * top_k;
+  cudaStream_t s = as_stream(stream);
+  Plan sizing;
+  sizing.take<int32_t>(n);
+  sizing.take<int32_t>(n);
+  sizing.take<int32_t>(n);
+  sizing.take<int32_t>(bucket_scratch_ints(n, kEpMaxScratchRanks));
+  sizing.take<int32_t>(world + 1);
+  Scratch scratch(workspace, workspace_bytes, static_cast<int64_t>(sizing.used()), s);
+  if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
+  Plan plan(scratch.base());
+  int32_t* keys = plan.take<int32_t>(n);
+  int32_t* pos_token = plan.take<int32_t>(n);
+  int32_t* pos_entry = plan.take<int32_t>(n);
+  int32_t* block_counts = plan.take<int32_t>(bucket_scratch_ints(n, kEpMaxScratchRanks));
+  int32_t* offsets = plan.take<int32_t>(world + 1);
+  ep_rank_keys_kernel<<<grid_for(n), 256, 0, s>>>(ids, n, num_experts / world, world, keys);
+  MOE_CUDA(cudaGetLastError(), "rank keys");
+  BucketArgs ba{};
+  ba.keys = keys; ba.rows = nullptr; ba.weights = nullptr; ba.n = static_cast<int>(n); ba.k = static_cast<int>(top_k);
+  ba.key_lo = 0; ba.n_buckets = static_cast<int>(world); ba.bucket_offset = offsets; ba.pair_row = pos_token;
+  ba.pair_weight = nullptr; ba.pair_entry = pos_entry; ba.entry_pair = nullptr; ba.tail = 0;
+  ba.block_counts = world <= kEpMaxScratchRanks ? block_counts : nullptr;
+  MOE_CUDA(launch_bucket(ba, s), "rank buckets");
+  const int vec = hidden_dim % 8 == 0 && aligned16(hidden_bf16) ? 1 : 0;
+  ep_p2p_scatter_kernel<<<grid_for(n * 32, 256), 256, 0, s>>>(
+      hidden_bf16, ids, keys, pos_token, pos_entry, offsets, count_matrix, n, hidden_dim, num_experts / world,
+      static_cast<int>(world), static_cast<int>(rank), capacity, src_stride, peer_rows, peer_expert, peer_src, vec);
+  MOE_CUDA(cudaGetLastError(), "scatter to peers");
+  return kOk;
+}
+
+int64_t moe_ep_dispatch_p2p_workspace_bytes(int64_t tokens, int64_t top_k, int64_t world) {
+  if (tokens <= 0 || top_k <= 0 || world <= 0) return -1;
+  const int64_t n = tokens * top_k;
+  Plan p;
+  p.take<int32_t>(n);
+  p.take<int32_t>(n);
+  p.take<int32_t>(n);
+  p.take<int32_t>(bucket_scratch_ints(n, kEpMaxScratchRanks));
+  p.take<int32_t>(world + 1);
+  return static_cast<int64_t>(p.used());
+}
+
+int moe_ep_return_p2p(const float* y, int64_t rows, const int32_t* recv_expert, const int32_t* recv_src,
+                      int64_t hidden_dim, int64_t src_stride, const uint64_t* peer_yback, void* stream) {
+  if (!y || !recv_expert || !recv_src || !peer_yback) return fail(kNullPointer, "null pointer");
+  if (rows <= 0 || hidden_dim <= 0 || src_stride <= 0) return fail(kBadDims, "bad dimensions");
+  const int vec = hidden_dim % 4 == 0 && aligned16(y) ? 1 : 0;
+  ep_p2p_return_kernel<<<grid_for(rows * 32, 256), 256, 0, as_stream(stream)>>>(y, rows, recv_expert, recv_src,
+                                                                              hidden_dim, src_stride, peer_yback, vec);
+  MOE_CUDA(cudaGetLastError(), "return to peers");
   return kOk;
 }
 

@@ -21,6 +21,14 @@ The counts exchange needs the sizes on the host (NCCL collectives take host
 counts), so a step synchronises once.  The compute steps go through an ops
 object: CudaEPOps calls libmoe_b200's kernels; tests substitute a CPU
 implementation to check the exchange logic with gloo ranks.
+
+On GPUs the default exchange (PeerExchange) has no host synchronisation and
+no collective on the data path: receive and return buffers live in torch
+symmetric memory, the dispatch kernel writes each row straight into its
+destination rank's buffer over NVLink and the return kernel writes each
+output row back into its source rank's buffer; only the [world] entry counts
+go through an NCCL all-gather, and two one-element NCCL all-reduces order
+the steps across ranks (no device-side waiting of our own).
 """
 
 from __future__ import annotations
@@ -103,6 +111,71 @@ class CudaEPOps:
         return out
 
 
+class PeerExchange:
+    """Symmetric-memory buffers for a layer's peer-to-peer exchange, sized for
+    up to `max_tokens` tokens per rank and step."""
+
+    def __init__(self, layer: "ExpertParallelLayer", max_tokens: int):
+        import torch.distributed._symmetric_memory as symm
+
+        L = layer
+        cfg = L.cfg
+        dev = L.device
+        self.max_tokens = int(max_tokens)
+        self.stride = self.max_tokens * cfg.top_k            # entries of one rank (src encoding)
+        self.capacity = L.world * self.stride                 # rows one rank can receive
+        H = cfg.hidden
+        group = L.group if L.group is not None else dist.group.WORLD
+        self.rows = symm.empty((self.capacity + self.max_tokens, H), dtype=torch.bfloat16, device=dev)
+        self.expert = symm.empty((self.capacity + self.max_tokens,), dtype=torch.int32, device=dev)
+        self.src = symm.empty((self.capacity,), dtype=torch.int32, device=dev)
+        self.yback = symm.empty((self.stride + self.max_tokens, H), dtype=torch.float32, device=dev)
+        self.handles = [symm.rendezvous(t, group) for t in (self.rows, self.expert, self.src, self.yback)]
+        self.peers = [torch.tensor([int(p) for p in h.buffer_ptrs], dtype=torch.int64, device=dev)
+                      for h in self.handles]
+        self.flag = torch.zeros((1,), dtype=torch.int32, device=dev)
+        self.counts = torch.empty((L.world,), dtype=torch.int32, device=dev)
+        self.matrix = torch.empty((L.world * L.world,), dtype=torch.int32, device=dev)
+        self.identity = torch.arange(self.stride, dtype=torch.int32, device=dev)
+        self.lib = native.load_library()
+        self._ws = torch.empty((0,), dtype=torch.uint8, device=dev)
+
+    def forward(self, L: "ExpertParallelLayer", x: torch.Tensor):
+        cfg, lib = L.cfg, self.lib
+        T, k, H = int(x.shape[0]), cfg.top_k, cfg.hidden
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the exchange's {self.max_tokens}")
+        ids, w = L.ops.route(x)
+        native._check(lib.moe_ep_count_ranks(native._ptr(ids), T, k, cfg.n_routed, L.world, native._ptr(self.counts),
+                                             native._stream()), "moe_ep_count_ranks")
+        # empty receive slots; peers write only after the all-gather, which this rank joins after the reset
+        self.expert.fill_(-1)
+        dist.all_gather_into_tensor(self.matrix, self.counts, group=L.group)
+        need = int(lib.moe_ep_dispatch_p2p_workspace_bytes(T, k, L.world))
+        if self._ws.numel() < need:
+            self._ws = torch.empty((need,), dtype=torch.uint8, device=x.device)
+        native._check(lib.moe_ep_dispatch_p2p(
+            native._ptr(ids), native._ptr(x), T, H, k, cfg.n_routed, L.world, L.rank, native._ptr(self.matrix),
+            self.capacity, self.stride, native._ptr(self.peers[0]), native._ptr(self.peers[1]),
+            native._ptr(self.peers[2]), native._ptr(self._ws), self._ws.numel(), native._stream()),
+            "moe_ep_dispatch_p2p")
+        dist.all_reduce(self.flag, group=L.group)  # every rank's rows have landed
+        C = self.capacity
+        self.rows[C:C + T].copy_(x)
+        self.expert[C:C + T].fill_(L.n_local)      # the shared expert, last in the local tables
+        y = L.ops.experts(self.rows[:C + T], self.expert[:C + T])
+        native._check(lib.moe_ep_return_p2p(native._ptr(y), C, native._ptr(self.expert), native._ptr(self.src), H,
+                                            self.stride, native._ptr(self.peers[3]), native._stream()),
+                      "moe_ep_return_p2p")
+        self.yback[T * k:T * k + T].copy_(y[C:C + T])
+        dist.all_reduce(self.flag, group=L.group)  # every output row is home
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+        native._check(lib.moe_ep_combine(native._ptr(self.yback), native._ptr(self.identity),
+                                         native._ptr(w.reshape(-1).contiguous()), T, k, H, 1, native._ptr(out),
+                                         native._stream()), "moe_ep_combine")
+        return out, ids, w
+
+
 class ExpertParallelLayer:
     """This rank's share of one expert-parallel DS-V3 MoE layer.
 
@@ -111,7 +184,8 @@ class ExpertParallelLayer:
     generated from `seed` (identical on every rank)."""
 
     def __init__(self, cfg: synth.DsMoEConfig, rank: int, world: int, *, group=None, seed: int = 20,
-                 device: torch.device | str | None = None, layer: synth.Fp8MoELayer | None = None, ops=None):
+                 device: torch.device | str | None = None, layer: synth.Fp8MoELayer | None = None, ops=None,
+                 exchange: str = "auto", max_tokens: int = 64):
         if cfg.n_routed % world:
             raise ValueError("the routed experts must split evenly over the ranks")
         self.cfg, self.rank, self.world, self.group = cfg, int(rank), int(world), group
@@ -157,11 +231,19 @@ class ExpertParallelLayer:
                     cols[4][i] = int(self._tiled2[i].data_ptr())
                 self.tables_tiled = torch.tensor(cols, dtype=torch.int64, device=self.device)
         self.ops = ops(self) if ops is not None else CudaEPOps(self)
+        # "p2p": PeerExchange (GPUs, NCCL group); "nccl": all-to-alls with host counts; "auto": p2p when possible
+        if exchange not in ("auto", "p2p", "nccl"):
+            raise ValueError("exchange must be auto, p2p or nccl")
+        use_p2p = exchange == "p2p" or (exchange == "auto" and ops is None and self.device.type == "cuda"
+                                        and dist.is_initialized() and dist.get_backend(group) == "nccl")
+        self.peer = PeerExchange(self, max_tokens) if use_p2p else None
 
     def forward(self, x: torch.Tensor):
         """x [T, H] bf16 (this rank's tokens) -> (out [T, H] bf16, ids [T, k], weights fp32 [T, k])."""
         cfg, ops = self.cfg, self.ops
         x = x.reshape(-1, cfg.hidden).contiguous()
+        if self.peer is not None:
+            return self.peer.forward(self, x)
         T, k, H = int(x.shape[0]), cfg.top_k, cfg.hidden
         ids, w = ops.route(x)
         p = ops.pack(ids, w, x)

@@ -36,13 +36,21 @@ def _rank_main(rank, world, port, outdir):
         dev = torch.device("cuda", rank)
         full = synth.make_fp8_layer(cfg, seed=13, device=dev)
         x = synth.make_hidden(6 + 5 * rank, cfg.hidden, seed=70 + rank, device=dev)
-        ep = ExpertParallelLayer(cfg, rank, world, layer=full, device=dev)
+        ep = ExpertParallelLayer(cfg, rank, world, layer=full, device=dev, exchange="nccl")
         out, ids, _w = ep.forward(x)
+        # the peer-memory exchange, two steps in a row (buffers reused) on different tokens
+        peer = ExpertParallelLayer(cfg, rank, world, layer=full, device=dev, exchange="p2p", max_tokens=16)
+        x2 = synth.make_hidden(3 + 7 * rank, cfg.hidden, seed=90 + rank, device=dev)
+        out_p2p, ids_p2p, _ = peer.forward(x)
+        out_p2p2, _, _ = peer.forward(x2)
+        out_nccl2, _, _ = ep.forward(x2)
         single = DsMoELayerGPU(full)
         ref_ids = torch.empty_like(ids)
         ref = single.forward(x, ids=ref_ids)
         torch.cuda.synchronize()
-        torch.save({"out": out.cpu(), "ids": ids.cpu(), "ref": ref.cpu(), "ref_ids": ref_ids.cpu(), "x": x.cpu()},
+        torch.save({"out": out.cpu(), "ids": ids.cpu(), "ref": ref.cpu(), "ref_ids": ref_ids.cpu(), "x": x.cpu(),
+                    "out_p2p": out_p2p.cpu(), "ids_p2p": ids_p2p.cpu(), "out_p2p2": out_p2p2.cpu(),
+                    "out_nccl2": out_nccl2.cpu()},
                    os.path.join(outdir, f"rank{rank}.pt"))
         dist.barrier()
     finally:
@@ -67,3 +75,7 @@ def test_ep_two_gpus_matches_single_gpu_layer_and_oracle():
             # same routing -> same per-pair arithmetic and combine order as the fused layer
             assert rel_l2(r["out"][same], r["ref"][same]) <= 1e-3
             assert rel_l2(r["out"], expected) <= REL_L2_GATE and cos_dist(r["out"], expected) <= COS_GATE
+            # the peer-memory exchange: the same rows reach the same experts in the same order
+            assert torch.equal(r["ids_p2p"], r["ids"])
+            assert torch.equal(r["out_p2p"], r["out"])
+            assert torch.equal(r["out_p2p2"], r["out_nccl2"])
