@@ -467,17 +467,21 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    # the peer exchange's step replays as one CUDA graph (kernels + NCCL), like the 1-GPU layer
+    graphed = ep.capture(T) if ep.peer is not None else None
+    step = (lambda: graphed(x)) if graphed is not None else (lambda: ep.forward(x))
     with ClockSampler(dev.index) as clocks:
-        ms = timed(lambda: ep.forward(x))
+        ms = timed(step)
         x_host = x.cpu().pin_memory()
         out_host = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
 
         def e2e():
             xd = x_host.to(dev, non_blocking=True)
-            out, _ids, _w = ep.forward(xd)
+            out = graphed(xd) if graphed is not None else ep.forward(xd)[0]
             out_host.copy_(out, non_blocking=True)
 
         e2e_ms = timed(e2e)
+    del graphed  # a graph holding NCCL calls goes before the process group
     _out, ids, _w = ep.forward(x)
     gathered = [torch.empty_like(ids) for _ in range(world)]
     dist.all_gather(gathered, ids)

@@ -176,6 +176,39 @@ class PeerExchange:
         return out, ids, w
 
 
+class GraphedExpertParallelLayer:
+    """An ExpertParallelLayer step with the peer exchange for one token count,
+    captured as a CUDA graph (its kernels, memsets and the NCCL all-gather and
+    all-reduces).  Every rank captures and replays in step.  Write the tokens
+    into `.input` (or pass them to __call__), replay, read `.output`.
+    Release it (del) before destroying the process group."""
+
+    def __init__(self, layer: "ExpertParallelLayer", tokens: int):
+        if layer.peer is None:
+            raise ValueError("graph capture needs the peer exchange (no host-synchronised counts)")
+        cfg, dev = layer.cfg, layer.device
+        self.input = torch.zeros((tokens, cfg.hidden), dtype=torch.bfloat16, device=dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):  # kernel attributes, workspaces, NCCL set-up outside the capture
+                layer.forward(self.input)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.output, self.ids, self.weights = layer.forward(self.input)
+        torch.cuda.synchronize(dev)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.output
+
+    def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
+        self.input.copy_(hidden.reshape(self.input.shape), non_blocking=True)
+        return self.replay()
+
+
 class ExpertParallelLayer:
     """This rank's share of one expert-parallel DS-V3 MoE layer.
 
@@ -237,6 +270,10 @@ class ExpertParallelLayer:
         use_p2p = exchange == "p2p" or (exchange == "auto" and ops is None and self.device.type == "cuda"
                                         and dist.is_initialized() and dist.get_backend(group) == "nccl")
         self.peer = PeerExchange(self, max_tokens) if use_p2p else None
+
+    def capture(self, tokens: int) -> GraphedExpertParallelLayer:
+        """A CUDA graph of one step for `tokens` tokens per rank (peer exchange only)."""
+        return GraphedExpertParallelLayer(self, tokens)
 
     def forward(self, x: torch.Tensor):
         """x [T, H] bf16 (this rank's tokens) -> (out [T, H] bf16, ids [T, k], weights fp32 [T, k])."""

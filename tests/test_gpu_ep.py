@@ -44,13 +44,19 @@ def _rank_main(rank, world, port, outdir):
         out_p2p, ids_p2p, _ = peer.forward(x)
         out_p2p2, _, _ = peer.forward(x2)
         out_nccl2, _, _ = ep.forward(x2)
+        # the same step replayed from a CUDA graph
+        graphed = peer.capture(int(x2.shape[0]))
+        out_graph = graphed(x2).clone()
+        out_graph2 = graphed(x2).clone()
+        torch.cuda.synchronize()
+        del graphed
         single = DsMoELayerGPU(full)
         ref_ids = torch.empty_like(ids)
         ref = single.forward(x, ids=ref_ids)
         torch.cuda.synchronize()
         torch.save({"out": out.cpu(), "ids": ids.cpu(), "ref": ref.cpu(), "ref_ids": ref_ids.cpu(), "x": x.cpu(),
                     "out_p2p": out_p2p.cpu(), "ids_p2p": ids_p2p.cpu(), "out_p2p2": out_p2p2.cpu(),
-                    "out_nccl2": out_nccl2.cpu()},
+                    "out_nccl2": out_nccl2.cpu(), "out_graph": out_graph.cpu(), "out_graph2": out_graph2.cpu()},
                    os.path.join(outdir, f"rank{rank}.pt"))
         dist.barrier()
     finally:
@@ -79,3 +85,4 @@ def test_ep_two_gpus_matches_single_gpu_layer_and_oracle():
             assert torch.equal(r["ids_p2p"], r["ids"])
             assert torch.equal(r["out_p2p"], r["out"])
             assert torch.equal(r["out_p2p2"], r["out_nccl2"])
+            assert torch.equal(r["out_graph"], r["out_nccl2"]) and torch.equal(r["out_graph2"], r["out_nccl2"])
