@@ -447,14 +447,14 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
     x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 100 * rank + T, device=dev)
     peaks = measured_peaks()
 
-    def timed(fn) -> float:
+    def timed(fn, steps: int | None = None) -> float:
         for _ in range(args.warmup):
             fn()
         torch.cuda.synchronize()
         dist.barrier()
         stream = torch.cuda.current_stream()
         times = []
-        for _ in range(args.steps):
+        for _ in range(args.steps if steps is None else steps):
             flush_l2(flush)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
@@ -486,6 +486,7 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
     gathered = [torch.empty_like(ids) for _ in range(world)]
     dist.all_gather(gathered, ids)
     clock_info = clocks.summary()
+    prefill = run_ep_prefill(args, rank, world, ep, timed, peaks)
     if rank != 0:
         return None
     all_ids = torch.cat(gathered).cpu()
@@ -520,9 +521,53 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
         "gpu_launches": (15 + (2 if ep.peer is not None and ep.peer.capacity + T > 2048 else 0)
                          if ep.peer is not None else 13) * args.steps,
         "exchange": "peer-memory (symmetric memory, NVLink stores)" if ep.peer is not None else "NCCL all-to-all",
+        "ep_prefill": prefill,
         "cpu_baseline": None,
         "clocks": clock_info,
     }
+
+
+def run_ep_prefill(args, rank: int, world: int, ep, timed, peaks) -> dict | None:
+    """Config 3 at N > 1: the Zipf-biased DS-V3 layer split expert-parallel
+    (256 / N routed experts per rank), --ep-prefill-tokens tokens per rank,
+    exchanged by NCCL all-to-alls with host-read counts (the step's one host
+    synchronisation); each rank's received rows run on the tcgen05 grouped
+    GEMM.  Step time = max over ranks; value = N * tokens / step time.  The
+    busiest rank's rows (routed pairs received + its own shared-expert rows)
+    set the step, so its FLOP rate is reported against the bf16 peak."""
+    import torch.distributed as dist
+
+    from pocketlm_b200 import synth
+    from pocketlm_b200.ep import ExpertParallelLayer
+
+    if args.ep_prefill_tokens == "none":
+        return None
+    cfg, dev = ep.cfg, ep.device
+    local = list(range(ep.first, ep.first + ep.n_local)) + [cfg.n_routed]
+    zipf = synth.make_fp8_layer(cfg, seed=args.seed + 1, device=dev, bias_kind="zipf", experts=local)
+    pre = ExpertParallelLayer(cfg, rank, world, layer=zipf, device=dev, exchange="nccl")
+    bf16_peak = peaks.get("bf16_tflops", 1590.0)
+    sweep = {}
+    for T in [int(v) for v in args.ep_prefill_tokens.split(",")]:
+        x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 100 * rank + T, device=dev)
+        ms = timed(lambda: pre.forward(x), steps=max(3, min(args.steps, 10)))
+        _out, ids, _w = pre.forward(x)
+        per_rank = torch.bincount(ids.reshape(-1) // ep.n_local, minlength=world).to(torch.int64)
+        dist.all_reduce(per_rank)
+        rows = per_rank.cpu() + T  # each rank also runs its own tokens' shared expert
+        flops = int(rows.max()) * 3 * 2 * cfg.hidden * cfg.inter
+        sweep[str(T)] = {
+            "tokens_per_gpu": T, "ms_per_step": ms, "tokens_per_s": world * T / (ms / 1e3),
+            "rows_per_rank": [int(v) for v in rows], "busiest_rank_tflops": flops / (ms / 1e3) / 1e12,
+            "busiest_rank_frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / bf16_peak,
+        }
+        del x, ids, _out, _w
+    del pre, zipf
+    torch.cuda.empty_cache()
+    return {"workload": "c3-dsv3-prefill-zipf", "parallelism": f"ep{world}",
+            "exchange": "NCCL all-to-all (counts read on the host)",
+            "expert_kernel": "tcgen05 grouped GEMM (prefill_gemm.cu) when a rank receives >= 16 rows per expert",
+            "peak_bf16_tflops": bf16_peak, "peak_source": f"{peaks['source']} bf16_tflops", "sweep": sweep}
 
 
 def run_profile_case(args) -> dict:
@@ -635,6 +680,9 @@ def main() -> None:
                         help="config-3 prefill batch sizes measured after the decode sweep, or 'none'")
     parser.add_argument("--q4-tokens", default="1,32,512,4096",
                         help="config-4 (Mixtral Q4) batch sizes measured after the prefill sweep, or 'none'")
+    parser.add_argument("--ep-prefill-tokens", default="8192",
+                        help="config-3 expert-parallel prefill tokens per rank measured after the decode step "
+                             "at N > 1, or 'none'")
     parser.add_argument("--profile", action="store_true",
                         help="run the small ncu case (selected experts only) instead of the benchmark")
     parser.add_argument("--profile-prefill", action="store_true",

@@ -736,7 +736,8 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
   l.partial = p.take<float>(part * frag);
   l.n_counters = l.tasks1 + l.tasks2;
   l.counters = p.take<int32_t>(l.n_counters);
-  if (router && T >= kPrefillMinTokens) {
+  // the tcgen05 GEMM's pair rows: layers (router) and expert-parallel experts (rows) alike
+  if (T >= kPrefillMinTokens) {
     l.a16 = p.take<__half>(pairs * H);
     l.a16scale = p.take<float>(pairs);
     l.mprefix = p.take<int32_t>(E + 2);
@@ -773,8 +774,9 @@ static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16
   g1.scale_cols = static_cast<int>(ceil_div(H, kBlock)); g1.nanfix = 1; g1.nan_free = nan_free;
   MOE_CUDA(launch_prefill_gemm(g1, true, mtiles_bound * (I / 128), s), "gate/up GEMM");
   stage_mark(s);
-  MOE_CUDA(launch_rows_to_f16(m.act, false, static_cast<int>(pairs), static_cast<int>(I), nullptr, l.act16, l.ascale,
-                              nullptr, 0, s),
+  // rows past the last segment (pairs routed nowhere) are neither staged nor read
+  MOE_CUDA(launch_rows_to_f16(m.act, false, static_cast<int>(pairs), static_cast<int>(I),
+                              m.seg_offset + n_segments, l.act16, l.ascale, nullptr, 0, s),
            "stage activations");
   stage_mark(s);
   PrefillArgs g2 = g1;
@@ -1111,7 +1113,11 @@ int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int
   ba.block_counts = l.bucket_scratch;
   MOE_CUDA(launch_bucket(ba, s), "expert buckets");
   Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
-  int code = run_expert_stages_mma(t, rows_bf16, true, l, R, R, S, I, H, false, nan_free, s, weight_layout);
+  // tiled weights and ~16 rows per expert or more (the layer's prefill threshold): the tcgen05 grouped GEMM
+  const bool gemm = weight_layout == 1 && R >= kPrefillMinTokens && R >= 16 * S && l.a16 != nullptr &&
+                    prefill_supported(H, I, true) && prefill_supported(I, H, false);
+  int code = gemm ? run_expert_stages_prefill(t, rows_bf16, true, 1, false, l, R, R, S, I, H, nan_free, s)
+                  : run_expert_stages_mma(t, rows_bf16, true, l, R, R, S, I, H, false, nan_free, s, weight_layout);
   if (code != kOk) return code;
   // back to row order (a row routed nowhere -- key out of range -- comes back zero)
   CombineArgs c{};

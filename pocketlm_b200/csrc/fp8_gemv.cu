@@ -215,40 +215,41 @@ __global__ void __launch_bounds__(kGemvThreads, 1) grouped_gemv_kernel(GemvArgs 
 // table order, :964-975 for pair order).
 // ---------------------------------------------------------------------------
 __global__ void combine_kernel(CombineArgs a) {
-  const int t = blockIdx.y;
-  const int lo = a.row_ptr ? a.row_ptr[t] : t * a.stride;
-  const int hi = a.row_ptr ? a.row_ptr[t + 1] : lo + a.stride;
   const bool vec = (a.H % 4) == 0;
   const int h = (blockIdx.x * blockDim.x + threadIdx.x) * (vec ? 4 : 1);
   if (h >= a.H) return;
-  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   const int width = vec ? 4 : 1;
+  for (int t = blockIdx.y; t < a.T; t += gridDim.y) {  // rows past grid.y's limit of 65535 loop
+    const int lo = a.row_ptr ? a.row_ptr[t] : t * a.stride;
+    const int hi = a.row_ptr ? a.row_ptr[t + 1] : lo + a.stride;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 8
-  for (int j = lo; j < hi; ++j) {
-    const int p = a.row_pairs ? a.row_pairs[j] : j;
-    if (p < 0) continue;
-    const float w = a.pair_weight ? a.pair_weight[p] : 1.0f;
-    const float* yp = a.y + static_cast<int64_t>(p) * a.H + h;
-    if (vec) {
-      const float4 v = *reinterpret_cast<const float4*>(yp);
-      acc[0] = fmaf(w, v.x, acc[0]);
-      acc[1] = fmaf(w, v.y, acc[1]);
-      acc[2] = fmaf(w, v.z, acc[2]);
-      acc[3] = fmaf(w, v.w, acc[3]);
-    } else {
-      acc[0] = fmaf(w, yp[0], acc[0]);
+    for (int j = lo; j < hi; ++j) {
+      const int p = a.row_pairs ? a.row_pairs[j] : j;
+      if (p < 0) continue;
+      const float w = a.pair_weight ? a.pair_weight[p] : 1.0f;
+      const float* yp = a.y + static_cast<int64_t>(p) * a.H + h;
+      if (vec) {
+        const float4 v = *reinterpret_cast<const float4*>(yp);
+        acc[0] = fmaf(w, v.x, acc[0]);
+        acc[1] = fmaf(w, v.y, acc[1]);
+        acc[2] = fmaf(w, v.z, acc[2]);
+        acc[3] = fmaf(w, v.w, acc[3]);
+      } else {
+        acc[0] = fmaf(w, yp[0], acc[0]);
+      }
     }
-  }
-  if (a.extra_base >= 0) {
-    const float* yp = a.y + static_cast<int64_t>(a.extra_base + t) * a.H + h;
-    for (int i = 0; i < width; ++i) acc[i] += yp[i];
-  }
-  const int64_t o = static_cast<int64_t>(t) * a.H + h;
-  for (int i = 0; i < width; ++i) {
-    if (a.out_f32) a.out_f32[o + i] = acc[i];
-    if (a.out_f16) a.out_f16[o + i] = __float2half_rn(acc[i]);
-    if (a.out_bf16)
-      a.out_bf16[o + i] = __float2bfloat16_rn(a.bf16_via_f16 ? __half2float(__float2half_rn(acc[i])) : acc[i]);
+    if (a.extra_base >= 0) {
+      const float* yp = a.y + static_cast<int64_t>(a.extra_base + t) * a.H + h;
+      for (int i = 0; i < width; ++i) acc[i] += yp[i];
+    }
+    const int64_t o = static_cast<int64_t>(t) * a.H + h;
+    for (int i = 0; i < width; ++i) {
+      if (a.out_f32) a.out_f32[o + i] = acc[i];
+      if (a.out_f16) a.out_f16[o + i] = __float2half_rn(acc[i]);
+      if (a.out_bf16)
+        a.out_bf16[o + i] = __float2bfloat16_rn(a.bf16_via_f16 ? __half2float(__float2half_rn(acc[i])) : acc[i]);
+    }
   }
 }
 
@@ -314,7 +315,8 @@ cudaError_t launch_combine(const CombineArgs& a, cudaStream_t stream) {
   if (a.T <= 0) return cudaSuccess;
   const int per_thread = (a.H % 4) == 0 ? 4 : 1;
   const int threads = 64;
-  dim3 grid(static_cast<unsigned>(ceil_div(ceil_div(a.H, per_thread), threads)), static_cast<unsigned>(a.T));
+  dim3 grid(static_cast<unsigned>(ceil_div(ceil_div(a.H, per_thread), threads)),
+            static_cast<unsigned>(std::min(a.T, 65535)));
   combine_kernel<<<grid, threads, 0, stream>>>(a);
   return cudaGetLastError();
 }

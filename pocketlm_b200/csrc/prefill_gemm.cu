@@ -262,7 +262,8 @@ MOE_D void piece_to_float<__half>(const uint4& v, float* out) {
 // in registers) -> fp16 / power-of-two scale (the rows_to_f16 staging:
 // 2^(floor(log2 amax) - 13), 1 for an all-zero row), written to the row of
 // each of its pairs: entry_pair[t * k + j] (>= 0), then, with a shared
-// expert, pair *tail_first + t.  One CTA per token.
+// expert, pair *tail_first + t.  One CTA per token; a token with no pair is
+// not read.
 template <typename T, int P>
 __global__ void __launch_bounds__(256) scatter_rows_kernel(const T* __restrict__ x, int T_, int K,
                                                            const int32_t* __restrict__ entry_pair, int k,
@@ -272,6 +273,9 @@ __global__ void __launch_bounds__(256) scatter_rows_kernel(const T* __restrict__
   __shared__ float red[8];
   const int n16 = K / V;
   for (int t = blockIdx.x; t < T_; t += gridDim.x) {
+    bool any = tail_first != nullptr;  // the same for every thread of the CTA
+    for (int j = 0; j < k; ++j) any |= entry_pair[static_cast<int64_t>(t) * k + j] >= 0;
+    if (!any) continue;
     const uint4* s = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * K);
     uint4 v[P];
     float amax = 0.0f;

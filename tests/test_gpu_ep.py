@@ -50,13 +50,22 @@ def _rank_main(rank, world, port, outdir):
         out_graph2 = graphed(x2).clone()
         torch.cuda.synchronize()
         del graphed
+        # prefill-sized steps: ~1200 rows per rank reach the tcgen05 grouped GEMM
+        xp = synth.make_hidden(600 + 40 * rank, cfg.hidden, seed=110 + rank, device=dev)
+        out_pre, ids_pre, _ = ep.forward(xp)
+        big = ExpertParallelLayer(cfg, rank, world, layer=full, device=dev, exchange="p2p", max_tokens=1024)
+        out_pre_p2p, _, _ = big.forward(xp)
         single = DsMoELayerGPU(full)
         ref_ids = torch.empty_like(ids)
         ref = single.forward(x, ids=ref_ids)
+        ref_pre_ids = torch.empty_like(ids_pre)
+        ref_pre = single.forward(xp, ids=ref_pre_ids)
         torch.cuda.synchronize()
         torch.save({"out": out.cpu(), "ids": ids.cpu(), "ref": ref.cpu(), "ref_ids": ref_ids.cpu(), "x": x.cpu(),
                     "out_p2p": out_p2p.cpu(), "ids_p2p": ids_p2p.cpu(), "out_p2p2": out_p2p2.cpu(),
-                    "out_nccl2": out_nccl2.cpu(), "out_graph": out_graph.cpu(), "out_graph2": out_graph2.cpu()},
+                    "out_nccl2": out_nccl2.cpu(), "out_graph": out_graph.cpu(), "out_graph2": out_graph2.cpu(),
+                    "xp": xp.cpu(), "out_pre": out_pre.cpu(), "ids_pre": ids_pre.cpu(),
+                    "out_pre_p2p": out_pre_p2p.cpu(), "ref_pre": ref_pre.cpu(), "ref_pre_ids": ref_pre_ids.cpu()},
                    os.path.join(outdir, f"rank{rank}.pt"))
         dist.barrier()
     finally:
@@ -86,3 +95,12 @@ def test_ep_two_gpus_matches_single_gpu_layer_and_oracle():
             assert torch.equal(r["out_p2p"], r["out"])
             assert torch.equal(r["out_p2p2"], r["out_nccl2"])
             assert torch.equal(r["out_graph"], r["out_nccl2"]) and torch.equal(r["out_graph2"], r["out_nccl2"])
+            # prefill: the received rows run on the grouped GEMM, as the fused layer's pairs do
+            same = (torch.sort(r["ids_pre"], 1).values == torch.sort(r["ref_pre_ids"], 1).values).all(dim=1)
+            assert same.float().mean() > 0.99
+            assert rel_l2(r["out_pre"][same], r["ref_pre"][same]) <= 1e-3
+            assert torch.equal(r["out_pre_p2p"], r["out_pre"])
+            expected, route = oracle.ds_moe_layer(r["xp"], layer)
+            bad, excused = id_mismatches(r["ids_pre"], route)
+            assert bad == excused
+            assert rel_l2(r["out_pre"], expected) <= REL_L2_GATE and cos_dist(r["out_pre"], expected) <= COS_GATE
