@@ -516,8 +516,8 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
         "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * cfg.hidden * 2,
                 "d2h_bytes_per_step": T * cfg.hidden * 2},
         # peer exchange: route (logits, select), rank counts, dispatch (rank keys, bucket, scatter to
-        # peers), experts (bucket: 1 kernel, 3 above 2048 rows; chunk list, x staging, gate/up, activation
-        # staging, down, row order), return to peers, combine; all-to-all exchange: 13
+        # peers), experts (bucket: 1 kernel, 3 above 2048 rows; home rows, chunk list, x staging, gate/up,
+        # activation staging, down, rows home to their ranks), combine; all-to-all exchange: 13
         "gpu_launches": (15 + (2 if ep.peer is not None and ep.peer.capacity + T > 2048 else 0)
                          if ep.peer is not None else 13) * args.steps,
         "exchange": "peer-memory (symmetric memory, NVLink stores)" if ep.peer is not None else "NCCL all-to-all",
@@ -530,11 +530,14 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
 def run_ep_prefill(args, rank: int, world: int, ep, timed, peaks) -> dict | None:
     """Config 3 at N > 1: the Zipf-biased DS-V3 layer split expert-parallel
     (256 / N routed experts per rank), --ep-prefill-tokens tokens per rank,
-    exchanged by NCCL all-to-alls with host-read counts (the step's one host
-    synchronisation); each rank's received rows run on the tcgen05 grouped
-    GEMM.  Step time = max over ranks; value = N * tokens / step time.  The
-    busiest rank's rows (routed pairs received + its own shared-expert rows)
-    set the step, so its FLOP rate is reported against the bf16 peak."""
+    with either exchange: "nccl" = all-to-alls with host-read counts (the
+    step's one host synchronisation); "p2p" = ep.PeerExchange (rows stored
+    into the experts' ranks by our dispatch kernel, outputs stored home by the
+    down GEMM's epilogue over NVLink).  Each rank's received rows run on the
+    tcgen05 grouped GEMM.  Step time = max over ranks; value = N * tokens /
+    step time.  The busiest rank's rows (routed pairs received + its own
+    shared-expert rows) set the step, so its FLOP rate is reported against the
+    bf16 peak."""
     import torch.distributed as dist
 
     from pocketlm_b200 import synth
@@ -543,31 +546,39 @@ def run_ep_prefill(args, rank: int, world: int, ep, timed, peaks) -> dict | None
     if args.ep_prefill_tokens == "none":
         return None
     cfg, dev = ep.cfg, ep.device
+    tokens = [int(v) for v in args.ep_prefill_tokens.split(",")]
     local = list(range(ep.first, ep.first + ep.n_local)) + [cfg.n_routed]
     zipf = synth.make_fp8_layer(cfg, seed=args.seed + 1, device=dev, bias_kind="zipf", experts=local)
-    pre = ExpertParallelLayer(cfg, rank, world, layer=zipf, device=dev, exchange="nccl")
     bf16_peak = peaks.get("bf16_tflops", 1590.0)
-    sweep = {}
-    for T in [int(v) for v in args.ep_prefill_tokens.split(",")]:
-        x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 100 * rank + T, device=dev)
-        ms = timed(lambda: pre.forward(x), steps=max(3, min(args.steps, 10)))
-        _out, ids, _w = pre.forward(x)
-        per_rank = torch.bincount(ids.reshape(-1) // ep.n_local, minlength=world).to(torch.int64)
-        dist.all_reduce(per_rank)
-        rows = per_rank.cpu() + T  # each rank also runs its own tokens' shared expert
-        flops = int(rows.max()) * 3 * 2 * cfg.hidden * cfg.inter
-        sweep[str(T)] = {
-            "tokens_per_gpu": T, "ms_per_step": ms, "tokens_per_s": world * T / (ms / 1e3),
-            "rows_per_rank": [int(v) for v in rows], "busiest_rank_tflops": flops / (ms / 1e3) / 1e12,
-            "busiest_rank_frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / bf16_peak,
-        }
-        del x, ids, _out, _w
-    del pre, zipf
+    sweeps = {}
+    for exchange in ("nccl", "p2p"):
+        pre = ExpertParallelLayer(cfg, rank, world, layer=zipf, device=dev, exchange=exchange,
+                                  max_tokens=max(tokens))
+        sweep = {}
+        for T in tokens:
+            x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 100 * rank + T, device=dev)
+            ms = timed(lambda: pre.forward(x), steps=max(3, min(args.steps, 10)))
+            _out, ids, _w = pre.forward(x)
+            per_rank = torch.bincount(ids.reshape(-1) // ep.n_local, minlength=world).to(torch.int64)
+            dist.all_reduce(per_rank)
+            rows = per_rank.cpu() + T  # each rank also runs its own tokens' shared expert
+            flops = int(rows.max()) * 3 * 2 * cfg.hidden * cfg.inter
+            sweep[str(T)] = {
+                "tokens_per_gpu": T, "ms_per_step": ms, "tokens_per_s": world * T / (ms / 1e3),
+                "rows_per_rank": [int(v) for v in rows], "busiest_rank_tflops": flops / (ms / 1e3) / 1e12,
+                "busiest_rank_frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / bf16_peak,
+            }
+            del x, ids, _out, _w
+        sweeps[exchange] = sweep
+        del pre
+        torch.cuda.empty_cache()
+    del zipf
     torch.cuda.empty_cache()
     return {"workload": "c3-dsv3-prefill-zipf", "parallelism": f"ep{world}",
-            "exchange": "NCCL all-to-all (counts read on the host)",
+            "exchanges": {"nccl": "NCCL all-to-all (counts read on the host)",
+                          "p2p": "peer memory: dispatch kernel stores rows, down-GEMM epilogue stores outputs home"},
             "expert_kernel": "tcgen05 grouped GEMM (prefill_gemm.cu) when a rank receives >= 16 rows per expert",
-            "peak_bf16_tflops": bf16_peak, "peak_source": f"{peaks['source']} bf16_tflops", "sweep": sweep}
+            "peak_bf16_tflops": bf16_peak, "peak_source": f"{peaks['source']} bf16_tflops", "sweep": sweeps}
 
 
 def run_profile_case(args) -> dict:

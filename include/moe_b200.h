@@ -391,6 +391,21 @@ int moe_ep_dispatch_p2p(const int64_t* ids, const uint16_t* hidden_bf16, int64_t
 int64_t moe_ep_dispatch_p2p_workspace_bytes(int64_t tokens, int64_t top_k, int64_t world);
 int moe_ep_return_p2p(const float* y, int64_t rows, const int32_t* recv_expert, const int32_t* recv_src,
                       int64_t hidden_dim, int64_t src_stride, const uint64_t* peer_yback, void* stream);
+/* moe_ep_experts_fp8 and moe_ep_return_p2p in one call: received row j's fp32
+ * output goes straight to row (row_src[j] % src_stride) of the return buffer
+ * of rank row_src[j] / src_stride (peer_yback [world], as above), stored over
+ * NVLink by the down GEMM's epilogue (prefill-sized batches: tiled weights,
+ * >= 512 rows and >= 16 per expert) or by a copy kernel after the warp-MMA
+ * experts.  Rows whose expert id is out of range are neither computed nor
+ * sent, so a receive buffer with empty slots costs no expert work.  The
+ * caller may route its own tokens' shared-expert rows through the same call
+ * (src = rank * src_stride + their return row).  hidden % 4 == 0. */
+int moe_ep_experts_return_p2p(const uint16_t* rows_bf16, const int32_t* row_expert, const int32_t* row_src,
+                              int64_t rows, int64_t hidden_dim, int64_t intermediate, const uint64_t* tables,
+                              int64_t num_local, const uint8_t* nan_free, int weight_layout, int64_t src_stride,
+                              const uint64_t* peer_yback, void* workspace, int64_t workspace_bytes, void* stream);
+int64_t moe_ep_experts_return_p2p_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t intermediate,
+                                                  int64_t num_local);
 
 /* ---------------------------------------------------------------------------
  * DeepSeek session: opaque handle with the reference's observable counters.

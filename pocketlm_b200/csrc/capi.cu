@@ -390,6 +390,41 @@ __global__ void ep_p2p_return_kernel(const float* y, int64_t rows, const int32_t
   __threadfence_system();
 }
 
+// Home rows of the received rows' outputs: pair p (received row j =
+// pair_entry[p], sent by rank r as its entry e: row_src[j] = r * src_stride +
+// e) -> row e of rank r's return buffer.
+__global__ void ep_pair_home_kernel(const int32_t* pair_entry, const int32_t* n_pairs, const int32_t* row_src,
+                                    int64_t src_stride, const uint64_t* peer_yback, int64_t H, uint64_t* pair_dst,
+                                    int64_t cap) {
+  const int64_t n = min(static_cast<int64_t>(*n_pairs), cap);
+  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < n;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t s = row_src[pair_entry[p]];
+    const int64_t r = s / src_stride, e = s % src_stride;
+    pair_dst[p] = peer_yback[r] + static_cast<uint64_t>(e * H) * sizeof(float);
+  }
+}
+
+// Pair p's fp32 output row y[p] to its home row pair_dst[p] (another GPU's
+// memory or this one's).  One warp per pair.
+__global__ void ep_pairs_home_kernel(const float* y, const int32_t* n_pairs, const uint64_t* pair_dst, int64_t H,
+                                     int64_t cap, int vec) {
+  const int lane = threadIdx.x % 32;
+  const int64_t n = min(static_cast<int64_t>(*n_pairs), cap);
+  for (int64_t p = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) / 32; p < n;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
+    const float* src = y + p * H;
+    float* dst = reinterpret_cast<float*>(pair_dst[p]);
+    if (vec) {
+      for (int64_t i = lane; i < H / 4; i += 32)
+        reinterpret_cast<float4*>(dst)[i] = __ldcs(reinterpret_cast<const float4*>(src) + i);
+    } else {
+      for (int64_t i = lane; i < H; i += 32) dst[i] = src[i];
+    }
+  }
+  __threadfence_system();
+}
+
 extern "C" {
 
 int moe_b200_abi_version(void) { return MOE_B200_ABI_VERSION; }
@@ -750,7 +785,7 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
 static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16, int64_t k, bool shared,
                                      const LayerPlan& l, int64_t T,
                                      int64_t pairs, int64_t n_segments, int64_t I, int64_t H, const uint8_t* nan_free,
-                                     cudaStream_t s) {
+                                     cudaStream_t s, const uint64_t* out_row = nullptr) {
   const MlpScratch& m = l.m;
   // each token's row staged once and written to its pairs' rows (the shared pairs follow the routed ones)
   cudaError_t serr = launch_scatter_rows(x, x_bf16 ? kDtypeBF16 : kDtypeF32, T, H, m.entry_pair, static_cast<int>(k),
@@ -782,7 +817,7 @@ static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16
   PrefillArgs g2 = g1;
   g2.w0 = t.dw; g2.s0 = t.ds; g2.w1 = nullptr; g2.s1 = nullptr;
   g2.a16 = l.act16; g2.ascale = l.ascale;
-  g2.out = m.y; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
+  g2.out = m.y; g2.out_row = out_row; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
   g2.scale_cols = static_cast<int>(ceil_div(I, kBlock));
   MOE_CUDA(launch_prefill_gemm(g2, false, mtiles_bound * (H / 256), s), "down GEMM");
   stage_mark(s);
@@ -1086,10 +1121,28 @@ int64_t moe_ep_experts_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t
   return static_cast<int64_t>(p.used());
 }
 
-int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int64_t rows, int64_t hidden_dim,
-                       int64_t intermediate, const uint64_t* tables, int64_t num_local, const uint8_t* nan_free,
-                       int weight_layout, float* out, void* workspace, int64_t workspace_bytes, void* stream) {
-  if (!rows_bf16 || !row_expert || !tables || !out) return fail(kNullPointer, "null pointer");
+// The local experts over received rows (moe_ep_experts_fp8 and
+// moe_ep_experts_return_p2p): outputs either in row order (out) or, with
+// home != null, straight to their home rows.
+struct EpHome {
+  const int32_t* row_src;
+  int64_t src_stride;
+  const uint64_t* peer_yback;
+};
+
+static void plan_ep_experts(Plan& p, int64_t R, int64_t H, int64_t I, int64_t S, bool home, LayerPlan* l,
+                            uint64_t** pair_dst) {
+  LayerPlan lp = plan_layer(p, R, H, I, S, 1, 0, 8, false);
+  uint64_t* pd = home ? p.take<uint64_t>(R) : nullptr;
+  if (l) *l = lp;
+  if (pair_dst) *pair_dst = pd;
+}
+
+static int ep_experts(const uint16_t* rows_bf16, const int32_t* row_expert, int64_t rows, int64_t hidden_dim,
+                      int64_t intermediate, const uint64_t* tables, int64_t num_local, const uint8_t* nan_free,
+                      int weight_layout, float* out, const EpHome* home, void* workspace, int64_t workspace_bytes,
+                      void* stream) {
+  if (!rows_bf16 || !row_expert || !tables || (!out && !home)) return fail(kNullPointer, "null pointer");
   if (weight_layout != 0 && weight_layout != 1) return fail(kBadDims, "weight_layout must be 0 or 1");
   if (weight_layout == 1 && !(g_gemv_impl == 0 && g_mma_feed == 2))
     return fail(kUnsupported, "tiled weights need the cp.async warp-MMA GEMV");
@@ -1101,30 +1154,75 @@ int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int
   const int64_t H = hidden_dim, I = intermediate, S = num_local, R = rows;
   cudaStream_t s = as_stream(stream);
   Plan sizing;
-  plan_layer(sizing, R, H, I, S, 1, 0, 8, false);
+  plan_ep_experts(sizing, R, H, I, S, home != nullptr, nullptr, nullptr);
   Scratch scratch(workspace, workspace_bytes, sizing.used(), s);
   if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
   Plan plan(scratch.base());
-  LayerPlan l = plan_layer(plan, R, H, I, S, 1, 0, 8, false);
+  LayerPlan l{};
+  uint64_t* pair_dst = nullptr;
+  plan_ep_experts(plan, R, H, I, S, home != nullptr, &l, &pair_dst);
   BucketArgs ba{};
   ba.keys = row_expert; ba.rows = nullptr; ba.weights = nullptr; ba.n = static_cast<int>(R); ba.k = 1;
   ba.key_lo = 0; ba.n_buckets = static_cast<int>(S); ba.bucket_offset = l.m.seg_offset; ba.pair_row = l.m.pair_row;
   ba.pair_weight = l.m.pair_weight; ba.pair_entry = l.m.pair_entry; ba.entry_pair = l.m.entry_pair; ba.tail = 0;
   ba.block_counts = l.bucket_scratch;
   MOE_CUDA(launch_bucket(ba, s), "expert buckets");
+  const int32_t* n_pairs = l.m.seg_offset + S;  // rows routed to a local expert
+  if (home) {
+    ep_pair_home_kernel<<<grid_for(R), 256, 0, s>>>(l.m.pair_entry, n_pairs, home->row_src, home->src_stride,
+                                                    home->peer_yback, H, pair_dst, R);
+    MOE_CUDA(cudaGetLastError(), "home rows");
+  }
   Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
-  // tiled weights and ~16 rows per expert or more (the layer's prefill threshold): the tcgen05 grouped GEMM
+  // tiled weights and ~16 rows per expert or more (the layer's prefill threshold): the tcgen05 grouped GEMM,
+  // whose down epilogue can store each row at its home
   const bool gemm = weight_layout == 1 && R >= kPrefillMinTokens && R >= 16 * S && l.a16 != nullptr &&
                     prefill_supported(H, I, true) && prefill_supported(I, H, false);
-  int code = gemm ? run_expert_stages_prefill(t, rows_bf16, true, 1, false, l, R, R, S, I, H, nan_free, s)
+  int code = gemm ? run_expert_stages_prefill(t, rows_bf16, true, 1, false, l, R, R, S, I, H, nan_free, s, pair_dst)
                   : run_expert_stages_mma(t, rows_bf16, true, l, R, R, S, I, H, false, nan_free, s, weight_layout);
   if (code != kOk) return code;
+  if (home) {
+    if (!gemm) {
+      const int vec = H % 4 == 0;
+      ep_pairs_home_kernel<<<grid_for(R * 32, 256), 256, 0, s>>>(l.m.y, n_pairs, pair_dst, H, R, vec);
+      MOE_CUDA(cudaGetLastError(), "rows home");
+    }
+    return kOk;
+  }
   // back to row order (a row routed nowhere -- key out of range -- comes back zero)
   CombineArgs c{};
   c.y = l.m.y; c.row_ptr = nullptr; c.stride = 1; c.row_pairs = l.m.entry_pair; c.pair_weight = nullptr;
   c.extra_base = -1; c.T = static_cast<int>(R); c.H = static_cast<int>(H); c.out_f32 = out;
   MOE_CUDA(launch_combine(c, s), "row order");
   return kOk;
+}
+
+int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int64_t rows, int64_t hidden_dim,
+                       int64_t intermediate, const uint64_t* tables, int64_t num_local, const uint8_t* nan_free,
+                       int weight_layout, float* out, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!out) return fail(kNullPointer, "null pointer");
+  return ep_experts(rows_bf16, row_expert, rows, hidden_dim, intermediate, tables, num_local, nan_free, weight_layout,
+                    out, nullptr, workspace, workspace_bytes, stream);
+}
+
+int64_t moe_ep_experts_return_p2p_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t intermediate,
+                                                  int64_t num_local) {
+  if (rows <= 0 || hidden_dim <= 0 || intermediate <= 0 || num_local <= 0) return -1;
+  Plan p;
+  plan_ep_experts(p, rows, hidden_dim, intermediate, num_local, true, nullptr, nullptr);
+  return static_cast<int64_t>(p.used());
+}
+
+int moe_ep_experts_return_p2p(const uint16_t* rows_bf16, const int32_t* row_expert, const int32_t* row_src,
+                              int64_t rows, int64_t hidden_dim, int64_t intermediate, const uint64_t* tables,
+                              int64_t num_local, const uint8_t* nan_free, int weight_layout, int64_t src_stride,
+                              const uint64_t* peer_yback, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!row_src || !peer_yback) return fail(kNullPointer, "null pointer");
+  if (src_stride <= 0) return fail(kBadDims, "bad dimensions");
+  if (hidden_dim % 4 != 0) return fail(kUnsupported, "hidden size must be a multiple of 4");
+  const EpHome home{row_src, src_stride, peer_yback};
+  return ep_experts(rows_bf16, row_expert, rows, hidden_dim, intermediate, tables, num_local, nan_free, weight_layout,
+                    nullptr, &home, workspace, workspace_bytes, stream);
 }
 
 int moe_ep_combine(const float* y, const int32_t* entry_pos, const float* pos_weight, int64_t tokens, int64_t top_k,

@@ -607,8 +607,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       if (!present(tr.seg)) {
         // absent expert: its pairs' output rows are zero
         if (row_in_tile < tr.rows) {
-          float4* out = reinterpret_cast<float4*>(a.out + (tr.row0 + row_in_tile) * static_cast<int64_t>(N) +
-                                                  tr.nt * (GATEUP ? kBN / 2 : kBN));
+          const int64_t pz = tr.row0 + row_in_tile;
+          float* row = !GATEUP && a.out_row ? reinterpret_cast<float*>(a.out_row[pz]) : a.out + pz * N;
+          float4* out = reinterpret_cast<float4*>(row + tr.nt * (GATEUP ? kBN / 2 : kBN));
           for (int j = 0; j < (GATEUP ? kBN / 2 : kBN) / 4; ++j) out[j] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
         continue;
@@ -633,7 +634,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       // four lanes per row (64 contiguous bytes) on the way out; 16-byte
       // slots XOR-swizzled by row so both phases are free of bank conflicts
       const int row_base = half * kSubM + quad * kWarp;  // the warp's first row in the tile
-      float* out_base = a.out + (tr.row0 + row_base) * static_cast<int64_t>(N) + tr.nt * (GATEUP ? kBN / 2 : kBN);
+      // the output rows this lane stores in emit16: rows lane / 4 + 8 i of the warp's 32
+      float* out_row[4] = {nullptr, nullptr, nullptr, nullptr};
+      if (!GATEUP) {
+        float* mine = nullptr;
+        if (valid) mine = (a.out_row ? reinterpret_cast<float*>(a.out_row[p]) : a.out + p * N) + tr.nt * kBN;
+        const uint64_t m64 = reinterpret_cast<uint64_t>(mine);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int src = lane / 4 + 8 * i;
+          const uint32_t lo = __shfl_sync(0xFFFFFFFFu, static_cast<uint32_t>(m64), src);
+          const uint32_t hi = __shfl_sync(0xFFFFFFFFu, static_cast<uint32_t>(m64 >> 32), src);
+          out_row[i] = reinterpret_cast<float*>((static_cast<uint64_t>(hi) << 32) | lo);
+        }
+      }
       auto emit16 = [&](const float (&v)[16], int c0) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -644,8 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         for (int i = 0; i < 4; ++i) {
           const int rr = lane / 4 + 8 * i, j = lane % 4;
           const uint4 w = ld_shared_v4(stage + rr * 64 + ((j ^ ((rr >> 1) & 3)) * 16));
-          if (row_base + rr < tr.rows)
-            *reinterpret_cast<uint4*>(out_base + rr * static_cast<int64_t>(N) + c0 + 4 * j) = w;
+          if (row_base + rr < tr.rows) *reinterpret_cast<uint4*>(out_row[i] + c0 + 4 * j) = w;
         }
         __syncwarp();
       };
@@ -702,6 +715,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
     }
   }
 
+  // rows stored to another GPU's memory are visible there once this grid ends
+  if (!GATEUP && a.out_row && warp < kEpiWarps) __threadfence_system();
   // all roles done; the MMA issuer saw its last commit arrive (drain)
   tc_fence_before();
   __syncthreads();

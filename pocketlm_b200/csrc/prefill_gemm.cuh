@@ -20,6 +20,9 @@ struct PrefillArgs {
   const int32_t* mprefix;     // [n_segments + 1] from launch_prefill_tiles
   int n_segments;
   float* out;              // [rows_a, N] fp32 (gate/up: SwiGLU activations)
+  // down GEMM only, or null: pair p's output row goes to out_row[p] (N fp32,
+  // 16-byte aligned; may be another GPU's memory) instead of out + p * N
+  const uint64_t* out_row;
   int N;                   // output columns (gate/up: intermediate size)
   int K;
   int scale_cols;          // ceil(K / 128)

@@ -101,6 +101,22 @@ class CudaEPOps:
         native._check(code, "moe_ep_experts_fp8")
         return out
 
+    def experts_home(self, rows: torch.Tensor, row_expert: torch.Tensor, row_src: torch.Tensor, src_stride: int,
+                     peer_yback: torch.Tensor) -> None:
+        """experts() with each output row written into its source rank's
+        return buffer (moe_ep_experts_return_p2p)."""
+        L = self.layer
+        R = int(rows.shape[0])
+        ws = self._workspace(int(self.lib.moe_ep_experts_return_p2p_workspace_bytes(R, L.cfg.hidden, L.cfg.inter,
+                                                                                    L.n_local + 1)))
+        layout = 1 if L.tables_tiled is not None and self.lib.moe_b200_selected_gemv() == 0 else 0
+        tables = L.tables_tiled if layout else L.tables
+        code = self.lib.moe_ep_experts_return_p2p(
+            native._ptr(rows), native._ptr(row_expert), native._ptr(row_src), R, L.cfg.hidden, L.cfg.inter,
+            native._ptr(tables), L.n_local + 1, native._ptr(L.nan_free), layout, src_stride, native._ptr(peer_yback),
+            native._ptr(ws), ws.numel(), native._stream())
+        native._check(code, "moe_ep_experts_return_p2p")
+
     def combine(self, y: torch.Tensor, p: Packed, T: int) -> torch.Tensor:
         L = self.layer
         k = L.cfg.top_k
@@ -122,13 +138,14 @@ class PeerExchange:
         cfg = L.cfg
         dev = L.device
         self.max_tokens = int(max_tokens)
-        self.stride = self.max_tokens * cfg.top_k            # entries of one rank (src encoding)
+        self.stride = self.max_tokens * cfg.top_k            # routed entries of one rank
+        self.src_stride = self.stride + self.max_tokens       # return rows of one rank (src encoding)
         self.capacity = L.world * self.stride                 # rows one rank can receive
         H = cfg.hidden
         group = L.group if L.group is not None else dist.group.WORLD
         self.rows = symm.empty((self.capacity + self.max_tokens, H), dtype=torch.bfloat16, device=dev)
         self.expert = symm.empty((self.capacity + self.max_tokens,), dtype=torch.int32, device=dev)
-        self.src = symm.empty((self.capacity,), dtype=torch.int32, device=dev)
+        self.src = symm.empty((self.capacity + self.max_tokens,), dtype=torch.int32, device=dev)
         self.yback = symm.empty((self.stride + self.max_tokens, H), dtype=torch.float32, device=dev)
         self.handles = [symm.rendezvous(t, group) for t in (self.rows, self.expert, self.src, self.yback)]
         self.peers = [torch.tensor([int(p) for p in h.buffer_ptrs], dtype=torch.int64, device=dev)
@@ -137,6 +154,7 @@ class PeerExchange:
         self.counts = torch.empty((L.world,), dtype=torch.int32, device=dev)
         self.matrix = torch.empty((L.world * L.world,), dtype=torch.int32, device=dev)
         self.identity = torch.arange(self.stride, dtype=torch.int32, device=dev)
+        self._shared_src = {}  # tokens -> src codes of this rank's shared-expert rows
         self.lib = native.load_library()
         self._ws = torch.empty((0,), dtype=torch.uint8, device=dev)
 
@@ -156,18 +174,20 @@ class PeerExchange:
             self._ws = torch.empty((need,), dtype=torch.uint8, device=x.device)
         native._check(lib.moe_ep_dispatch_p2p(
             native._ptr(ids), native._ptr(x), T, H, k, cfg.n_routed, L.world, L.rank, native._ptr(self.matrix),
-            self.capacity, self.stride, native._ptr(self.peers[0]), native._ptr(self.peers[1]),
+            self.capacity, self.src_stride, native._ptr(self.peers[0]), native._ptr(self.peers[1]),
             native._ptr(self.peers[2]), native._ptr(self._ws), self._ws.numel(), native._stream()),
             "moe_ep_dispatch_p2p")
         dist.all_reduce(self.flag, group=L.group)  # every rank's rows have landed
         C = self.capacity
         self.rows[C:C + T].copy_(x)
         self.expert[C:C + T].fill_(L.n_local)      # the shared expert, last in the local tables
-        y = L.ops.experts(self.rows[:C + T], self.expert[:C + T])
-        native._check(lib.moe_ep_return_p2p(native._ptr(y), C, native._ptr(self.expert), native._ptr(self.src), H,
-                                            self.stride, native._ptr(self.peers[3]), native._stream()),
-                      "moe_ep_return_p2p")
-        self.yback[T * k:T * k + T].copy_(y[C:C + T])
+        if T not in self._shared_src:              # its outputs go to this rank's return rows T*k + t
+            self._shared_src[T] = (torch.arange(T, dtype=torch.int32, device=x.device)
+                                   + (L.rank * self.src_stride + T * k))
+        self.src[C:C + T].copy_(self._shared_src[T])
+        # the local experts; every output row is stored straight into its source rank's return buffer
+        L.ops.experts_home(self.rows[:C + T], self.expert[:C + T], self.src[:C + T], self.src_stride,
+                           self.peers[3])
         dist.all_reduce(self.flag, group=L.group)  # every output row is home
         out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
         native._check(lib.moe_ep_combine(native._ptr(self.yback), native._ptr(self.identity),
