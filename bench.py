@@ -85,9 +85,16 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        # the sampler is running (first line written) before the timed region starts
+        deadline = time.monotonic() + 10.0
+        while time.monotonic() < deadline and self.proc.poll() is None:
+            if self.path.exists() and self.path.stat().st_size > 0:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
@@ -486,7 +493,10 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
     gathered = [torch.empty_like(ids) for _ in range(world)]
     dist.all_gather(gathered, ids)
     clock_info = clocks.summary()
-    prefill = run_ep_prefill(args, rank, world, ep, timed, peaks)
+    with ClockSampler(dev.index) as prefill_clocks:
+        prefill = run_ep_prefill(args, rank, world, ep, timed, peaks)
+    if prefill is not None:
+        prefill["clocks"] = prefill_clocks.summary()
     if rank != 0:
         return None
     all_ids = torch.cat(gathered).cpu()

@@ -405,7 +405,7 @@ int moe_ep_experts_return_p2p(const uint16_t* rows_bf16, const int32_t* row_expe
                               int64_t num_local, const uint8_t* nan_free, int weight_layout, int64_t src_stride,
                               const uint64_t* peer_yback, void* workspace, int64_t workspace_bytes, void* stream);
 int64_t moe_ep_experts_return_p2p_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t intermediate,
-                                                  int64_t num_local);
+                                                  int64_t num_local, int weight_layout);
 
 /* ---------------------------------------------------------------------------
  * DeepSeek session: opaque handle with the reference's observable counters.

@@ -740,8 +740,10 @@ struct LayerPlan {
 // chunk of 8 pairs.
 constexpr int64_t kPrefillMinTokens = 512;
 
+// lean: the caller runs the tcgen05 GEMM with its outputs stored through a
+// row table -- no warp-MMA buffers (x16, k-split partials) and no pair-order y.
 static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, int shared, int nt,
-                            bool router = true) {
+                            bool router = true, bool lean = false) {
   LayerPlan l{};
   if (router)
     l.logits = p.take<float>(static_cast<int64_t>(std::max(1, router_split_parts(static_cast<int>(H)))) * T * E);
@@ -749,9 +751,11 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
   l.wts = p.take<float>(T * k);
   l.bucket_scratch = p.take<int32_t>(bucket_scratch_ints(T * k, static_cast<int>(E)));
   const int64_t pairs = T * k + (shared ? T : 0);
-  l.m = plan_mlp(p, pairs, E + 1, T * k, I, H, nt, true);
-  l.x16 = p.take<__half>(T * H);
-  l.xscale = p.take<float>(T);
+  l.m = plan_mlp(p, pairs, E + 1, T * k, I, H, nt, !lean);
+  if (!lean) {
+    l.x16 = p.take<__half>(T * H);
+    l.xscale = p.take<float>(T);
+  }
   l.act16 = p.take<__half>(pairs * I);
   l.ascale = p.take<float>(pairs);
   const int64_t chunks = std::min(pairs, chunk_capacity(pairs, E + (shared ? 1 : 0), 8));
@@ -768,9 +772,11 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
   const int64_t frag = 32 * 8;
   const int64_t part = std::max({l.tasks1 * std::max(ks_regs1, ks_async1), l.tasks2 * std::max(ks_regs2, ks_async2),
                                  int64_t{1}});
-  l.partial = p.take<float>(part * frag);
-  l.n_counters = l.tasks1 + l.tasks2;
-  l.counters = p.take<int32_t>(l.n_counters);
+  if (!lean) {
+    l.partial = p.take<float>(part * frag);
+    l.n_counters = l.tasks1 + l.tasks2;
+    l.counters = p.take<int32_t>(l.n_counters);
+  }
   // the tcgen05 GEMM's pair rows: layers (router) and expert-parallel experts (rows) alike
   if (T >= kPrefillMinTokens) {
     l.a16 = p.take<__half>(pairs * H);
@@ -791,6 +797,7 @@ static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16
   cudaError_t serr = launch_scatter_rows(x, x_bf16 ? kDtypeBF16 : kDtypeF32, T, H, m.entry_pair, static_cast<int>(k),
                                          shared ? m.seg_offset + (n_segments - 1) : nullptr, l.a16, l.a16scale, s);
   if (serr == cudaErrorNotSupported) {
+    if (!l.x16) return fail(kUnsupported, "rows must be 16-byte aligned and at most 16 KiB");
     MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.x16, l.xscale,
                                 nullptr, 0, s),
              "stage x");
@@ -1130,9 +1137,15 @@ struct EpHome {
   const uint64_t* peer_yback;
 };
 
-static void plan_ep_experts(Plan& p, int64_t R, int64_t H, int64_t I, int64_t S, bool home, LayerPlan* l,
+// tiled weights and ~16 rows per expert or more (the layer's prefill threshold): the tcgen05 grouped GEMM
+static bool ep_use_gemm(int weight_layout, int64_t R, int64_t H, int64_t I, int64_t S) {
+  return weight_layout == 1 && R >= kPrefillMinTokens && R >= 16 * S && prefill_supported(H, I, true) &&
+         prefill_supported(I, H, false);
+}
+
+static void plan_ep_experts(Plan& p, int64_t R, int64_t H, int64_t I, int64_t S, bool home, bool gemm, LayerPlan* l,
                             uint64_t** pair_dst) {
-  LayerPlan lp = plan_layer(p, R, H, I, S, 1, 0, 8, false);
+  LayerPlan lp = plan_layer(p, R, H, I, S, 1, 0, 8, false, home && gemm);
   uint64_t* pd = home ? p.take<uint64_t>(R) : nullptr;
   if (l) *l = lp;
   if (pair_dst) *pair_dst = pd;
@@ -1153,14 +1166,15 @@ static int ep_experts(const uint16_t* rows_bf16, const int32_t* row_expert, int6
     return fail(kUnsupported, "hidden and intermediate sizes must be multiples of 128");
   const int64_t H = hidden_dim, I = intermediate, S = num_local, R = rows;
   cudaStream_t s = as_stream(stream);
+  const bool gemm = ep_use_gemm(weight_layout, R, H, I, S);
   Plan sizing;
-  plan_ep_experts(sizing, R, H, I, S, home != nullptr, nullptr, nullptr);
+  plan_ep_experts(sizing, R, H, I, S, home != nullptr, gemm, nullptr, nullptr);
   Scratch scratch(workspace, workspace_bytes, sizing.used(), s);
   if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
   Plan plan(scratch.base());
   LayerPlan l{};
   uint64_t* pair_dst = nullptr;
-  plan_ep_experts(plan, R, H, I, S, home != nullptr, &l, &pair_dst);
+  plan_ep_experts(plan, R, H, I, S, home != nullptr, gemm, &l, &pair_dst);
   BucketArgs ba{};
   ba.keys = row_expert; ba.rows = nullptr; ba.weights = nullptr; ba.n = static_cast<int>(R); ba.k = 1;
   ba.key_lo = 0; ba.n_buckets = static_cast<int>(S); ba.bucket_offset = l.m.seg_offset; ba.pair_row = l.m.pair_row;
@@ -1174,10 +1188,7 @@ static int ep_experts(const uint16_t* rows_bf16, const int32_t* row_expert, int6
     MOE_CUDA(cudaGetLastError(), "home rows");
   }
   Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
-  // tiled weights and ~16 rows per expert or more (the layer's prefill threshold): the tcgen05 grouped GEMM,
-  // whose down epilogue can store each row at its home
-  const bool gemm = weight_layout == 1 && R >= kPrefillMinTokens && R >= 16 * S && l.a16 != nullptr &&
-                    prefill_supported(H, I, true) && prefill_supported(I, H, false);
+  // the GEMM's down epilogue stores each row at its home
   int code = gemm ? run_expert_stages_prefill(t, rows_bf16, true, 1, false, l, R, R, S, I, H, nan_free, s, pair_dst)
                   : run_expert_stages_mma(t, rows_bf16, true, l, R, R, S, I, H, false, nan_free, s, weight_layout);
   if (code != kOk) return code;
@@ -1206,10 +1217,11 @@ int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int
 }
 
 int64_t moe_ep_experts_return_p2p_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t intermediate,
-                                                  int64_t num_local) {
+                                                  int64_t num_local, int weight_layout) {
   if (rows <= 0 || hidden_dim <= 0 || intermediate <= 0 || num_local <= 0) return -1;
   Plan p;
-  plan_ep_experts(p, rows, hidden_dim, intermediate, num_local, true, nullptr, nullptr);
+  plan_ep_experts(p, rows, hidden_dim, intermediate, num_local, true,
+                  ep_use_gemm(weight_layout, rows, hidden_dim, intermediate, num_local), nullptr, nullptr);
   return static_cast<int64_t>(p.used());
 }
 

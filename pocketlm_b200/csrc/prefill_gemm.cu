@@ -891,6 +891,8 @@ cudaError_t launch_gather_rows(const __half* x16, const float* xscale, const int
 cudaError_t launch_prefill_gemm(const PrefillArgs& a, bool gateup, int64_t max_tiles, cudaStream_t stream) {
   if (!prefill_supported(a.K, a.N, gateup) || a.rows_a <= 0) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(a.a16) & 15u) != 0) return cudaErrorInvalidValue;
+  // outputs: rows of out, or (down GEMM only) the row table
+  if (gateup ? (!a.out || a.out_row) : (!a.out && !a.out_row)) return cudaErrorInvalidValue;
   auto encode = encode_fn();
   if (!encode) return cudaErrorNotSupported;
   // A boxes of 128, 64 and 32 rows (the smaller ones for small tiles)

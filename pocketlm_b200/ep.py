@@ -107,9 +107,9 @@ class CudaEPOps:
         return buffer (moe_ep_experts_return_p2p)."""
         L = self.layer
         R = int(rows.shape[0])
-        ws = self._workspace(int(self.lib.moe_ep_experts_return_p2p_workspace_bytes(R, L.cfg.hidden, L.cfg.inter,
-                                                                                    L.n_local + 1)))
         layout = 1 if L.tables_tiled is not None and self.lib.moe_b200_selected_gemv() == 0 else 0
+        ws = self._workspace(int(self.lib.moe_ep_experts_return_p2p_workspace_bytes(R, L.cfg.hidden, L.cfg.inter,
+                                                                                    L.n_local + 1, layout)))
         tables = L.tables_tiled if layout else L.tables
         code = self.lib.moe_ep_experts_return_p2p(
             native._ptr(rows), native._ptr(row_expert), native._ptr(row_src), R, L.cfg.hidden, L.cfg.inter,
