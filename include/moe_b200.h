@@ -394,18 +394,21 @@ int moe_ep_return_p2p(const float* y, int64_t rows, const int32_t* recv_expert, 
 /* moe_ep_experts_fp8 and moe_ep_return_p2p in one call: received row j's fp32
  * output goes straight to row (row_src[j] % src_stride) of the return buffer
  * of rank row_src[j] / src_stride (peer_yback [world], as above), stored over
- * NVLink by the down GEMM's epilogue (prefill-sized batches: tiled weights,
- * >= 512 rows and >= 16 per expert) or by a copy kernel after the warp-MMA
+ * NVLink by the down GEMM's epilogue or by a copy kernel after the warp-MMA
  * experts.  Rows whose expert id is out of range are neither computed nor
- * sent, so a receive buffer with empty slots costs no expert work.  The
- * caller may route its own tokens' shared-expert rows through the same call
- * (src = rank * src_stride + their return row).  hidden % 4 == 0. */
+ * sent, so a receive buffer with empty slots costs no expert work.
+ * valid_rows: the rows the caller expects to carry a local expert (0 = all);
+ * it only picks the kernel -- the GEMM for tiled weights and >= 512 rows, >= 16
+ * per local expert -- and the workspace, so any value gives the same result.
+ * The caller may route its own tokens' shared-expert rows through the same
+ * call (src = rank * src_stride + their return row).  hidden % 4 == 0. */
 int moe_ep_experts_return_p2p(const uint16_t* rows_bf16, const int32_t* row_expert, const int32_t* row_src,
-                              int64_t rows, int64_t hidden_dim, int64_t intermediate, const uint64_t* tables,
-                              int64_t num_local, const uint8_t* nan_free, int weight_layout, int64_t src_stride,
-                              const uint64_t* peer_yback, void* workspace, int64_t workspace_bytes, void* stream);
-int64_t moe_ep_experts_return_p2p_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t intermediate,
-                                                  int64_t num_local, int weight_layout);
+                              int64_t rows, int64_t valid_rows, int64_t hidden_dim, int64_t intermediate,
+                              const uint64_t* tables, int64_t num_local, const uint8_t* nan_free, int weight_layout,
+                              int64_t src_stride, const uint64_t* peer_yback, void* workspace,
+                              int64_t workspace_bytes, void* stream);
+int64_t moe_ep_experts_return_p2p_workspace_bytes(int64_t rows, int64_t valid_rows, int64_t hidden_dim,
+                                                  int64_t intermediate, int64_t num_local, int weight_layout);
 
 /* ---------------------------------------------------------------------------
  * DeepSeek session: opaque handle with the reference's observable counters.

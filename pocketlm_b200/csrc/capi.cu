@@ -1137,9 +1137,13 @@ struct EpHome {
   const uint64_t* peer_yback;
 };
 
-// tiled weights and ~16 rows per expert or more (the layer's prefill threshold): the tcgen05 grouped GEMM
-static bool ep_use_gemm(int weight_layout, int64_t R, int64_t H, int64_t I, int64_t S) {
-  return weight_layout == 1 && R >= kPrefillMinTokens && R >= 16 * S && prefill_supported(H, I, true) &&
+// Tiled weights and ~16 valid rows per expert or more (the layer's prefill
+// threshold): the tcgen05 grouped GEMM.  `valid` = the rows expected to carry a
+// local expert (a receive buffer sized for the worst case holds far fewer);
+// 0 or more than R means all R.
+static bool ep_use_gemm(int weight_layout, int64_t R, int64_t valid, int64_t H, int64_t I, int64_t S) {
+  const int64_t v = valid > 0 ? std::min(valid, R) : R;
+  return weight_layout == 1 && v >= kPrefillMinTokens && v >= 16 * S && prefill_supported(H, I, true) &&
          prefill_supported(I, H, false);
 }
 
@@ -1151,7 +1155,8 @@ static void plan_ep_experts(Plan& p, int64_t R, int64_t H, int64_t I, int64_t S,
   if (pair_dst) *pair_dst = pd;
 }
 
-static int ep_experts(const uint16_t* rows_bf16, const int32_t* row_expert, int64_t rows, int64_t hidden_dim,
+static int ep_experts(const uint16_t* rows_bf16, const int32_t* row_expert, int64_t rows, int64_t valid_rows,
+                      int64_t hidden_dim,
                       int64_t intermediate, const uint64_t* tables, int64_t num_local, const uint8_t* nan_free,
                       int weight_layout, float* out, const EpHome* home, void* workspace, int64_t workspace_bytes,
                       void* stream) {
@@ -1166,7 +1171,7 @@ static int ep_experts(const uint16_t* rows_bf16, const int32_t* row_expert, int6
     return fail(kUnsupported, "hidden and intermediate sizes must be multiples of 128");
   const int64_t H = hidden_dim, I = intermediate, S = num_local, R = rows;
   cudaStream_t s = as_stream(stream);
-  const bool gemm = ep_use_gemm(weight_layout, R, H, I, S);
+  const bool gemm = ep_use_gemm(weight_layout, R, valid_rows, H, I, S);
   Plan sizing;
   plan_ep_experts(sizing, R, H, I, S, home != nullptr, gemm, nullptr, nullptr);
   Scratch scratch(workspace, workspace_bytes, sizing.used(), s);
@@ -1212,29 +1217,29 @@ int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int
                        int64_t intermediate, const uint64_t* tables, int64_t num_local, const uint8_t* nan_free,
                        int weight_layout, float* out, void* workspace, int64_t workspace_bytes, void* stream) {
   if (!out) return fail(kNullPointer, "null pointer");
-  return ep_experts(rows_bf16, row_expert, rows, hidden_dim, intermediate, tables, num_local, nan_free, weight_layout,
-                    out, nullptr, workspace, workspace_bytes, stream);
+  return ep_experts(rows_bf16, row_expert, rows, rows, hidden_dim, intermediate, tables, num_local, nan_free,
+                    weight_layout, out, nullptr, workspace, workspace_bytes, stream);
 }
 
-int64_t moe_ep_experts_return_p2p_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t intermediate,
-                                                  int64_t num_local, int weight_layout) {
+int64_t moe_ep_experts_return_p2p_workspace_bytes(int64_t rows, int64_t valid_rows, int64_t hidden_dim,
+                                                  int64_t intermediate, int64_t num_local, int weight_layout) {
   if (rows <= 0 || hidden_dim <= 0 || intermediate <= 0 || num_local <= 0) return -1;
   Plan p;
   plan_ep_experts(p, rows, hidden_dim, intermediate, num_local, true,
-                  ep_use_gemm(weight_layout, rows, hidden_dim, intermediate, num_local), nullptr, nullptr);
+                  ep_use_gemm(weight_layout, rows, valid_rows, hidden_dim, intermediate, num_local), nullptr, nullptr);
   return static_cast<int64_t>(p.used());
 }
 
 int moe_ep_experts_return_p2p(const uint16_t* rows_bf16, const int32_t* row_expert, const int32_t* row_src,
-                              int64_t rows, int64_t hidden_dim, int64_t intermediate, const uint64_t* tables,
+                              int64_t rows, int64_t valid_rows, int64_t hidden_dim, int64_t intermediate, const uint64_t* tables,
                               int64_t num_local, const uint8_t* nan_free, int weight_layout, int64_t src_stride,
                               const uint64_t* peer_yback, void* workspace, int64_t workspace_bytes, void* stream) {
   if (!row_src || !peer_yback) return fail(kNullPointer, "null pointer");
   if (src_stride <= 0) return fail(kBadDims, "bad dimensions");
   if (hidden_dim % 4 != 0) return fail(kUnsupported, "hidden size must be a multiple of 4");
   const EpHome home{row_src, src_stride, peer_yback};
-  return ep_experts(rows_bf16, row_expert, rows, hidden_dim, intermediate, tables, num_local, nan_free, weight_layout,
-                    nullptr, &home, workspace, workspace_bytes, stream);
+  return ep_experts(rows_bf16, row_expert, rows, valid_rows, hidden_dim, intermediate, tables, num_local, nan_free,
+                    weight_layout, nullptr, &home, workspace, workspace_bytes, stream);
 }
 
 int moe_ep_combine(const float* y, const int32_t* entry_pos, const float* pos_weight, int64_t tokens, int64_t top_k,

@@ -102,17 +102,19 @@ class CudaEPOps:
         return out
 
     def experts_home(self, rows: torch.Tensor, row_expert: torch.Tensor, row_src: torch.Tensor, src_stride: int,
-                     peer_yback: torch.Tensor) -> None:
+                     peer_yback: torch.Tensor, valid_rows: int = 0) -> None:
         """experts() with each output row written into its source rank's
-        return buffer (moe_ep_experts_return_p2p)."""
+        return buffer (moe_ep_experts_return_p2p); valid_rows: the rows
+        expected to carry a local expert (picks the kernel; 0 = all)."""
         L = self.layer
         R = int(rows.shape[0])
         layout = 1 if L.tables_tiled is not None and self.lib.moe_b200_selected_gemv() == 0 else 0
-        ws = self._workspace(int(self.lib.moe_ep_experts_return_p2p_workspace_bytes(R, L.cfg.hidden, L.cfg.inter,
-                                                                                    L.n_local + 1, layout)))
+        ws = self._workspace(int(self.lib.moe_ep_experts_return_p2p_workspace_bytes(
+            R, valid_rows, L.cfg.hidden, L.cfg.inter, L.n_local + 1, layout)))
         tables = L.tables_tiled if layout else L.tables
         code = self.lib.moe_ep_experts_return_p2p(
-            native._ptr(rows), native._ptr(row_expert), native._ptr(row_src), R, L.cfg.hidden, L.cfg.inter,
+            native._ptr(rows), native._ptr(row_expert), native._ptr(row_src), R, valid_rows, L.cfg.hidden,
+            L.cfg.inter,
             native._ptr(tables), L.n_local + 1, native._ptr(L.nan_free), layout, src_stride, native._ptr(peer_yback),
             native._ptr(ws), ws.numel(), native._stream())
         native._check(code, "moe_ep_experts_return_p2p")
@@ -185,9 +187,10 @@ class PeerExchange:
             self._shared_src[T] = (torch.arange(T, dtype=torch.int32, device=x.device)
                                    + (L.rank * self.src_stride + T * k))
         self.src[C:C + T].copy_(self._shared_src[T])
-        # the local experts; every output row is stored straight into its source rank's return buffer
+        # the local experts; every output row is stored straight into its source rank's return buffer.
+        # Rows expected: T * k routed (a rank receives about what it sends) + T shared
         L.ops.experts_home(self.rows[:C + T], self.expert[:C + T], self.src[:C + T], self.src_stride,
-                           self.peers[3])
+                           self.peers[3], valid_rows=T * (k + 1))
         dist.all_reduce(self.flag, group=L.group)  # every output row is home
         out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
         native._check(lib.moe_ep_combine(native._ptr(self.yback), native._ptr(self.identity),

@@ -131,9 +131,9 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
                             _INT),
     "moe_ep_dispatch_p2p_workspace_bytes": ([_I64, _I64, _I64], _I64),
     "moe_ep_return_p2p": ([_P, _I64, _P, _P, _I64, _I64, _P, _P], _INT),
-    "moe_ep_experts_return_p2p": ([_P, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _INT, _I64, _P, _P, _I64, _P],
-                                  _INT),
-    "moe_ep_experts_return_p2p_workspace_bytes": ([_I64] * 4 + [_INT], _I64),
+    "moe_ep_experts_return_p2p": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _INT, _I64, _P, _P, _I64,
+                                   _P], _INT),
+    "moe_ep_experts_return_p2p_workspace_bytes": ([_I64] * 5 + [_INT], _I64),
     "moe_b200_stage_timing": ([_INT], _INT),
     "moe_b200_stage_times": ([_P, _INT], _INT),
     "moe_b200_select_gemv": ([_INT], _INT),
