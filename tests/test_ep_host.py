@@ -1,0 +1,41 @@
+"""Host-side behaviour of the expert-parallel experts entry points
+(include/moe_b200.h): argument checks and the workspace each kernel choice
+needs.  Pure host arithmetic and early returns -- no device work."""
+
+from pocketlm_b200 import native
+
+H, I = 7168, 2048
+
+
+def test_workspace_follows_the_kernel_choice():
+    lib = native.load_library()
+    S = 256 // 8 + 1                       # one of 8 ranks: 32 routed experts + the shared one
+    T = 8192
+    R = 8 * T * 8 + T                      # receive buffer sized for every rank's worst case
+    lean = lib.moe_ep_experts_return_p2p_workspace_bytes(R, T * 9, H, I, S, 1)     # grouped GEMM
+    gemv = lib.moe_ep_experts_return_p2p_workspace_bytes(R, 16 * 9, H, I, S, 1)    # ~4 rows per expert
+    rowmajor = lib.moe_ep_experts_return_p2p_workspace_bytes(R, T * 9, H, I, S, 0)  # untiled: no GEMM
+    assert 0 < lean < gemv
+    assert rowmajor == gemv
+    # 64 tokens per rank at 8 ranks: 576 rows, ~16 per local expert -- the GEMM's threshold
+    assert lib.moe_ep_experts_return_p2p_workspace_bytes(R, 64 * 9, H, I, S, 1) == lean
+    # the GEMM path keeps no warp-MMA buffers and no pair-order outputs: well under half
+    assert lean < gemv // 2
+    # valid_rows 0 means every row, and more than rows is clamped
+    assert lib.moe_ep_experts_return_p2p_workspace_bytes(R, 0, H, I, S, 1) == lean
+    assert lib.moe_ep_experts_return_p2p_workspace_bytes(R, 10 * R, H, I, S, 1) == lean
+
+
+def test_workspace_rejects_bad_sizes():
+    lib = native.load_library()
+    for args in ((0, 0, H, I, 9), (100, 0, 0, I, 9), (100, 0, H, 0, 9), (100, 0, H, I, 0)):
+        assert lib.moe_ep_experts_return_p2p_workspace_bytes(*args, 1) == -1
+    assert lib.moe_ep_experts_workspace_bytes(0, H, I, 9) == -1
+
+
+def test_entry_points_check_pointers_before_any_device_work():
+    lib = native.load_library()
+    code = lib.moe_ep_experts_return_p2p(None, None, None, 16, 0, H, I, None, 9, None, 1, 16, None, None, 0, None)
+    assert code == -1 and b"null" in lib.moe_b200_last_error()
+    code = lib.moe_ep_experts_fp8(None, None, 16, H, I, None, 9, None, 1, None, None, 0, None)
+    assert code == -1 and b"null" in lib.moe_b200_last_error()
