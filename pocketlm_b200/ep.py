@@ -165,20 +165,25 @@ class PeerExchange:
         T, k, H = int(x.shape[0]), cfg.top_k, cfg.hidden
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens exceed the exchange's {self.max_tokens}")
-        ids, w = L.ops.route(x)
-        native._check(lib.moe_ep_count_ranks(native._ptr(ids), T, k, cfg.n_routed, L.world, native._ptr(self.counts),
-                                             native._stream()), "moe_ep_count_ranks")
+        if T == 0:  # nothing to send; this rank still takes every step (it may receive rows)
+            ids, w = L._no_routes(x)
+            self.counts.zero_()
+        else:
+            ids, w = L.ops.route(x)
+            native._check(lib.moe_ep_count_ranks(native._ptr(ids), T, k, cfg.n_routed, L.world,
+                                                 native._ptr(self.counts), native._stream()), "moe_ep_count_ranks")
         # empty receive slots; peers write only after the all-gather, which this rank joins after the reset
         self.expert.fill_(-1)
         dist.all_gather_into_tensor(self.matrix, self.counts, group=L.group)
-        need = int(lib.moe_ep_dispatch_p2p_workspace_bytes(T, k, L.world))
-        if self._ws.numel() < need:
-            self._ws = torch.empty((need,), dtype=torch.uint8, device=x.device)
-        native._check(lib.moe_ep_dispatch_p2p(
-            native._ptr(ids), native._ptr(x), T, H, k, cfg.n_routed, L.world, L.rank, native._ptr(self.matrix),
-            self.capacity, self.src_stride, native._ptr(self.peers[0]), native._ptr(self.peers[1]),
-            native._ptr(self.peers[2]), native._ptr(self._ws), self._ws.numel(), native._stream()),
-            "moe_ep_dispatch_p2p")
+        if T > 0:
+            need = int(lib.moe_ep_dispatch_p2p_workspace_bytes(T, k, L.world))
+            if self._ws.numel() < need:
+                self._ws = torch.empty((need,), dtype=torch.uint8, device=x.device)
+            native._check(lib.moe_ep_dispatch_p2p(
+                native._ptr(ids), native._ptr(x), T, H, k, cfg.n_routed, L.world, L.rank,
+                native._ptr(self.matrix), self.capacity, self.src_stride, native._ptr(self.peers[0]),
+                native._ptr(self.peers[1]), native._ptr(self.peers[2]), native._ptr(self._ws), self._ws.numel(),
+                native._stream()), "moe_ep_dispatch_p2p")
         dist.all_reduce(self.flag, group=L.group)  # every rank's rows have landed
         C = self.capacity
         self.rows[C:C + T].copy_(x)
@@ -190,9 +195,11 @@ class PeerExchange:
         # the local experts; every output row is stored straight into its source rank's return buffer.
         # Rows expected: T * k routed (a rank receives about what it sends) + T shared
         L.ops.experts_home(self.rows[:C + T], self.expert[:C + T], self.src[:C + T], self.src_stride,
-                           self.peers[3], valid_rows=T * (k + 1))
+                           self.peers[3], valid_rows=max(T, 1) * (k + 1))
         dist.all_reduce(self.flag, group=L.group)  # every output row is home
         out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+        if T == 0:
+            return out, ids, w
         native._check(lib.moe_ep_combine(native._ptr(self.yback), native._ptr(self.identity),
                                          native._ptr(w.reshape(-1).contiguous()), T, k, H, 1, native._ptr(out),
                                          native._stream()), "moe_ep_combine")
@@ -305,8 +312,16 @@ class ExpertParallelLayer:
         if self.peer is not None:
             return self.peer.forward(self, x)
         T, k, H = int(x.shape[0]), cfg.top_k, cfg.hidden
-        ids, w = ops.route(x)
-        p = ops.pack(ids, w, x)
+        if T == 0:  # nothing to route; this rank still exchanges (it may receive rows) in step with the others
+            ids, w = self._no_routes(x)
+            p = Packed(torch.empty((0, H), dtype=torch.bfloat16, device=x.device),
+                       torch.empty((0,), dtype=torch.int32, device=x.device),
+                       torch.zeros((self.world + 1,), dtype=torch.int32, device=x.device),
+                       torch.empty((0,), dtype=torch.int32, device=x.device),
+                       torch.empty((0,), dtype=torch.float32, device=x.device))
+        else:
+            ids, w = ops.route(x)
+            p = ops.pack(ids, w, x)
         send_counts = (p.send_offsets[1:] - p.send_offsets[:-1]).to(torch.int64)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
@@ -319,8 +334,16 @@ class ExpertParallelLayer:
         dist.all_to_all_single(row_expert[:R], p.send_expert, rc, sc, group=self.group)
         rows[R:].copy_(x)
         row_expert[R:].fill_(self.n_local)  # the shared expert, last in the local tables
-        y = ops.experts(rows, row_expert)
+        y = ops.experts(rows, row_expert) if R + T > 0 else torch.empty((0, H), dtype=torch.float32,
+                                                                        device=x.device)
         y_back = torch.empty((T * k + T, H), dtype=torch.float32, device=x.device)
         dist.all_to_all_single(y_back[:T * k], y[:R], sc, rc, group=self.group)
         y_back[T * k:].copy_(y[R:])
+        if T == 0:
+            return torch.empty((0, H), dtype=torch.bfloat16, device=x.device), ids, w
         return ops.combine(y_back, p, T), ids, w
+
+    def _no_routes(self, x: torch.Tensor):
+        k = self.cfg.top_k
+        return (torch.empty((0, k), dtype=torch.int64, device=x.device),
+                torch.empty((0, k), dtype=torch.float32, device=x.device))
