@@ -434,6 +434,31 @@ def run_q4(args, dev, flush, peaks, token_list) -> dict:
             "prefill_gemm_kernel<*, Q4> (prefill_gemm.cu)", "sweep": out}
 
 
+def timed_max_over_ranks(fn, steps: int, warmup: int, flush: torch.Tensor, dev: torch.device) -> float:
+    """Mean CUDA-event time of `steps` calls of fn on this rank (L2 flushed
+    before each, warm-up first, barriers around), then the max over ranks."""
+    import torch.distributed as dist
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    stream = torch.cuda.current_stream()
+    times = []
+    for _ in range(steps):
+        flush_l2(flush)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        fn()
+        e.record(stream)
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    dist.barrier()
+    t = torch.tensor([statistics.mean(times)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def run_ours_ep(args, rank: int, world: int) -> dict | None:
     """N > 1: expert parallelism.  Rank r holds routed experts
     [r * 256 / N, (r + 1) * 256 / N) plus the shared expert and router, and
@@ -455,24 +480,7 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
     peaks = measured_peaks()
 
     def timed(fn, steps: int | None = None) -> float:
-        for _ in range(args.warmup):
-            fn()
-        torch.cuda.synchronize()
-        dist.barrier()
-        stream = torch.cuda.current_stream()
-        times = []
-        for _ in range(args.steps if steps is None else steps):
-            flush_l2(flush)
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record(stream)
-            fn()
-            e.record(stream)
-            e.synchronize()
-            times.append(s.elapsed_time(e))
-        dist.barrier()
-        t = torch.tensor([statistics.mean(times)], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return timed_max_over_ranks(fn, args.steps if steps is None else steps, args.warmup, flush, dev)
 
     # the peer exchange's step replays as one CUDA graph (kernels + NCCL), like the 1-GPU layer
     graphed = ep.capture(T) if ep.peer is not None else None
@@ -534,6 +542,120 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
         "ep_prefill": prefill,
         "cpu_baseline": None,
         "clocks": clock_info,
+    }
+
+
+def stack_share(batch: int, rank: int, world: int) -> int:
+    """Tokens of a decode batch on `rank`: the batch spread over the ranks in
+    order (data-parallel attention replicas), so a 1-token batch lives on
+    rank 0 and the other ranks only serve experts."""
+    return batch // world + (1 if rank < batch % world else 0)
+
+
+def stack_critical_bytes(ids_by_rank: list, per_rank: int, expert_bytes: int, router_bytes: int) -> int:
+    """Weight bytes on the stack's critical path: ids_by_rank[r][l] = rank
+    r's expert ids [T_r, k] in layer l.  Layer l waits for its busiest rank:
+    the routed experts in that rank's range hit by any token, plus, on a rank
+    with tokens, its shared expert and the router.  Summed over the layers."""
+    world = len(ids_by_rank)
+    total = 0
+    for li in range(len(ids_by_rank[0])):
+        hit = {int(v) for r in range(world) for v in ids_by_rank[r][li].reshape(-1).tolist()}
+        worst = 0
+        for r in range(world):
+            has_tokens = ids_by_rank[r][li].numel() > 0
+            n = sum(1 for e in hit if r * per_rank <= e < (r + 1) * per_rank) + (1 if has_tokens else 0)
+            worst = max(worst, n * expert_bytes + (router_bytes if has_tokens else 0))
+        total += worst
+    return total
+
+
+def run_stack(args, rank: int, world: int) -> dict | None:
+    """Config 5: the routed-expert stack of DS-V3 decode, --stack-layers
+    layers (58 for the full model) of the config-2 shape with random weights,
+    experts split expert-parallel over the N ranks (256 / N per rank per
+    layer, tiled copy only: 84 GB per GPU at 58 layers and N = 8), attention
+    replaced by the identity (h <- h + moe_l(h)).  For each batch of
+    --stack-tokens (spread over the ranks, stack_share), one step = the whole
+    stack for the batch, replayed as ONE CUDA graph per rank (every layer's
+    route, peer exchange, experts, combine and residual add).  Step time =
+    max over ranks = the end-to-end latency of every token of the batch.
+    Roofline: per layer, the busiest rank's expert bytes (experts hit there +
+    its shared expert + router) bound the layer; their sum over the layers ÷
+    the step time, against measured HBM bandwidth."""
+    import torch.distributed as dist
+
+    from pocketlm_b200 import synth
+    from pocketlm_b200.ep import ExpertParallelStack
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    cfg = synth.C2_DSV3
+    L = args.stack_layers
+    batches = [int(v) for v in args.stack_tokens.split(",")]
+    max_tokens = max(max(stack_share(b, 0, world), 1) for b in batches)
+    stack = ExpertParallelStack(cfg, rank, world, L, seed=args.seed, device=dev, max_tokens=max_tokens)
+    flush = torch.zeros((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
+    peaks = measured_peaks()
+    gs, ds = cfg.gate_scale_shape, cfg.down_scale_shape
+    expert_bytes = 3 * cfg.inter * cfg.hidden + 4 * (2 * gs[0] * gs[1] + ds[0] * ds[1])
+    router_bytes = cfg.n_routed * cfg.hidden * 2
+    per_rank = cfg.n_routed // world
+    steps = max(3, min(args.steps, 20))
+    sweep = {}
+    with ClockSampler(dev.index) as clocks:
+        for B in batches:
+            T = stack_share(B, rank, world)
+            x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 100 * rank + B, device=dev)
+            graphed = stack.capture(T) if stack.peer is not None else None
+            step = (lambda: graphed(x)) if graphed is not None else (lambda: stack.forward(x))
+            ms = timed_max_over_ranks(step, steps, args.warmup, flush, dev)
+            x_host = x.cpu().pin_memory()
+            out_host = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
+
+            def e2e():
+                xd = x_host.to(dev, non_blocking=True)
+                out = graphed(xd) if graphed is not None else stack.forward(xd)
+                out_host.copy_(out, non_blocking=True)
+
+            e2e_ms = timed_max_over_ranks(e2e, steps, args.warmup, flush, dev)
+            del graphed  # graphs holding NCCL calls go before the process group
+            # routing of one eager step: per layer, the experts each rank serves
+            ids_per_layer: list = []
+            stack.forward(x, ids_out=ids_per_layer)
+            gathered = [None] * world
+            dist.all_gather_object(gathered, [i.cpu() for i in ids_per_layer])
+            crit = stack_critical_bytes(gathered, per_rank, expert_bytes, router_bytes)
+            achieved = crit / (ms / 1e3) / 1e9
+            sweep[str(B)] = {
+                "batch": B, "tokens_per_rank": [stack_share(B, r, world) for r in range(world)],
+                "ms_per_step": ms, "per_token_latency_ms": ms, "tokens_per_s": B / (ms / 1e3),
+                "e2e_ms": e2e_ms, "e2e_tokens_per_s": B / (e2e_ms / 1e3),
+                "critical_path_expert_bytes": crit, "achieved_gbs": achieved,
+                "frac_of_hbm": achieved / peaks["hbm_gbs"],
+            }
+            del x, x_host, out_host
+    clock_info = clocks.summary()
+    if rank != 0:
+        return None
+    head = sweep[str(batches[0])]
+    return {
+        "metric": METRIC, "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 (e4m3 weights decoded exactly, bf16 activations, fp32 accumulate)",
+        "data": "synthetic (seeded random DS-V3-shape weights and activations; no checkpoint)",
+        "config": {"workload": f"c5-dsv3-stack{L}-decode-B{batches[0]}", "layers": L, "batches": batches,
+                   "hidden": cfg.hidden, "moe_intermediate": cfg.inter, "experts": f"{cfg.n_routed}+1",
+                   "top_k": cfg.top_k, "parallelism": f"ep{world}", "attention": "identity residual",
+                   "l2": "256 MiB L2 flush between timed steps"},
+        "roofline": {"bound": "hbm", "kernel": "whole stack step, busiest rank per layer",
+                     "achieved": head["achieved_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": head["frac_of_hbm"], "peak_source": f"{peaks['source']} hbm_gbs",
+                     "algorithmic_bytes_per_launch": head["critical_path_expert_bytes"], "traffic": None},
+        "e2e": {"value": head["e2e_tokens_per_s"], "unit": "tokens/s",
+                "h2d_bytes_per_step": stack_share(batches[0], 0, world) * cfg.hidden * 2,
+                "d2h_bytes_per_step": stack_share(batches[0], 0, world) * cfg.hidden * 2},
+        "exchange": "peer-memory (symmetric memory, NVLink stores), one buffer set for all layers",
+        "sweep": sweep, "cpu_baseline": None, "clocks": clock_info,
     }
 
 
@@ -704,6 +826,11 @@ def main() -> None:
     parser.add_argument("--ep-prefill-tokens", default="8192",
                         help="config-3 expert-parallel prefill tokens per rank measured after the decode step "
                              "at N > 1, or 'none'")
+    parser.add_argument("--stack-layers", type=int, default=0,
+                        help="config 5: time the expert-parallel stack of this many layers (58 = DS-V3) "
+                             "instead of the one-layer bench; needs N GPUs with room for layers * 257 / N experts")
+    parser.add_argument("--stack-tokens", default="1,2,32",
+                        help="config-5 decode batches (spread over the ranks)")
     parser.add_argument("--profile", action="store_true",
                         help="run the small ncu case (selected experts only) instead of the benchmark")
     parser.add_argument("--profile-prefill", action="store_true",
@@ -719,11 +846,16 @@ def main() -> None:
         args.warmup = 3
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    if world > 1 and args.impl == "ours":
+    # a process group for N > 1, and for the stack at N = 1 too (its exchange steps are collectives)
+    use_pg = args.impl == "ours" and (world > 1 or args.stack_layers > 0)
+    if use_pg:
         import datetime
 
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29571")
+        torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
+                                             timeout=datetime.timedelta(seconds=120))
     if args.impl == "ours":
         from pocketlm_b200 import native
 
@@ -738,6 +870,8 @@ def main() -> None:
         else:
             if args.impl == "reference":
                 result = run_reference(args, rank, world)
+            elif args.stack_layers > 0:
+                result = run_stack(args, rank, world)
             elif world > 1:
                 result = run_ours_ep(args, rank, world)
             else:
@@ -745,7 +879,7 @@ def main() -> None:
         if result is not None:
             print(json.dumps(result), flush=True)
     finally:
-        if world > 1 and args.impl == "ours":
+        if use_pg:
             torch.distributed.destroy_process_group()
 
 

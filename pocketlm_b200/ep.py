@@ -248,7 +248,8 @@ class ExpertParallelLayer:
 
     def __init__(self, cfg: synth.DsMoEConfig, rank: int, world: int, *, group=None, seed: int = 20,
                  device: torch.device | str | None = None, layer: synth.Fp8MoELayer | None = None, ops=None,
-                 exchange: str = "auto", max_tokens: int = 64):
+                 exchange: str = "auto", max_tokens: int = 64, peer: "PeerExchange | None" = None,
+                 row_major: bool = True):
         if cfg.n_routed % world:
             raise ValueError("the routed experts must split evenly over the ranks")
         self.cfg, self.rank, self.world, self.group = cfg, int(rank), int(world), group
@@ -297,9 +298,22 @@ class ExpertParallelLayer:
         # "p2p": PeerExchange (GPUs, NCCL group); "nccl": all-to-alls with host counts; "auto": p2p when possible
         if exchange not in ("auto", "p2p", "nccl"):
             raise ValueError("exchange must be auto, p2p or nccl")
+        if not row_major:
+            # keep only the tiled copy the default GEMV and the GEMM read (half the memory): drop the
+            # row-major codes and the source layer; the scales stay
+            if self.tables_tiled is None:
+                raise ValueError("row_major=False needs the tiled copy (CUDA, hidden and intermediate % 128 == 0)")
+            self.local_experts = [[None, ex[1], None, ex[3], None, ex[5]] for ex in self.local_experts]
+            self.tables = None
+            self.layer = layer = None
         use_p2p = exchange == "p2p" or (exchange == "auto" and ops is None and self.device.type == "cuda"
                                         and dist.is_initialized() and dist.get_backend(group) == "nccl")
-        self.peer = PeerExchange(self, max_tokens) if use_p2p else None
+        if peer is not None:  # layers run one after another, so one set of exchange buffers serves them all
+            if not use_p2p:
+                raise ValueError("a shared peer exchange needs exchange='p2p' or 'auto' on an NCCL group")
+            self.peer = peer
+        else:
+            self.peer = PeerExchange(self, max_tokens) if use_p2p else None
 
     def capture(self, tokens: int) -> GraphedExpertParallelLayer:
         """A CUDA graph of one step for `tokens` tokens per rank (peer exchange only)."""
@@ -347,3 +361,80 @@ class ExpertParallelLayer:
         k = self.cfg.top_k
         return (torch.empty((0, k), dtype=torch.int64, device=x.device),
                 torch.empty((0, k), dtype=torch.float32, device=x.device))
+
+
+class ExpertParallelStack:
+    """A stack of expert-parallel DS-V3 MoE layers with the attention blocks
+    replaced by the identity: h <- h + moe_l(h) for l = 0 .. n_layers - 1, in
+    bf16 (the routed-expert stack of a decode step).  Layer l is generated
+    from seed + l unless `layers` gives it; every layer keeps only the tiled
+    copy of its experts on GPUs (row_major=False), and the layers share one
+    peer exchange, whose buffers serve one layer after the other."""
+
+    def __init__(self, cfg: synth.DsMoEConfig, rank: int, world: int, n_layers: int, *, group=None,
+                 seed: int = 20, device: torch.device | str | None = None,
+                 layers: list[synth.Fp8MoELayer] | None = None, ops=None, exchange: str = "auto",
+                 max_tokens: int = 64, row_major: bool | None = None):
+        if n_layers < 1 or (layers is not None and len(layers) != n_layers):
+            raise ValueError("n_layers must be >= 1 and match `layers`")
+        self.cfg, self.world = cfg, int(world)
+        self.layers: list[ExpertParallelLayer] = []
+        peer = None
+        for li in range(n_layers):
+            given = layers[li] if layers is not None else None
+            keep = row_major if row_major is not None else (ops is not None or torch.device(
+                device if device is not None else native._device()).type != "cuda")
+            ep = ExpertParallelLayer(cfg, rank, world, group=group, seed=seed + li, device=device, layer=given,
+                                     ops=ops, exchange=exchange, max_tokens=max_tokens, peer=peer, row_major=keep)
+            peer = ep.peer
+            self.layers.append(ep)
+            del given, ep
+        self.device = self.layers[0].device
+        self.peer = peer
+
+    def forward(self, x: torch.Tensor, ids_out: list | None = None) -> torch.Tensor:
+        """x [T, H] bf16 (this rank's tokens, T may be 0) -> h [T, H] bf16 after
+        every layer; ids_out, when given, receives each layer's expert ids."""
+        h = x.reshape(-1, self.cfg.hidden).to(torch.bfloat16)
+        for ep in self.layers:
+            out, ids, _w = ep.forward(h)
+            if ids_out is not None:
+                ids_out.append(ids)
+            h = h + out
+        return h
+
+    def capture(self, tokens: int) -> "GraphedExpertParallelStack":
+        """One CUDA graph of the whole stack for `tokens` tokens on this rank (peer exchange only)."""
+        return GraphedExpertParallelStack(self, tokens)
+
+
+class GraphedExpertParallelStack:
+    """ExpertParallelStack.forward for one token count captured as one CUDA
+    graph (every layer's kernels, memsets, residual adds and NCCL calls).
+    Every rank captures and replays in step; release it (del) before
+    destroying the process group."""
+
+    def __init__(self, stack: ExpertParallelStack, tokens: int):
+        if stack.peer is None:
+            raise ValueError("graph capture needs the peer exchange (no host-synchronised counts)")
+        dev = stack.device
+        self.input = torch.zeros((tokens, stack.cfg.hidden), dtype=torch.bfloat16, device=dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):  # kernel attributes, workspaces, NCCL set-up outside the capture
+                stack.forward(self.input)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.output = stack.forward(self.input)
+        torch.cuda.synchronize(dev)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.output
+
+    def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
+        self.input.copy_(hidden.reshape(self.input.shape), non_blocking=True)
+        return self.replay()

@@ -109,3 +109,43 @@ def test_ep_world2_matches_one_rank_and_oracle(tokens):
                 continue
             assert rel_l2(r["out"], r["expected"]) <= REL_L2_GATE
             assert cos_dist(r["out"], r["expected"]) <= COS_GATE
+
+
+def _stack_main(rank, world, port, tokens, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from pocketlm_b200.ep import ExpertParallelStack
+
+        cfg = synth.C1_TINY
+        layers = [synth.make_fp8_layer(cfg, seed=30 + li) for li in range(3)]
+        x = synth.make_hidden(tokens[rank], cfg.hidden, seed=80 + rank)
+        stack = ExpertParallelStack(cfg, rank, world, 3, layers=layers, device="cpu", ops=OracleEPOps)
+        out = stack.forward(x)
+        solo_groups = [dist.new_group([r]) for r in range(world)]
+        solo = ExpertParallelStack(cfg, 0, 1, 3, group=solo_groups[rank], layers=layers, device="cpu",
+                                   ops=OracleEPOps)
+        ref = solo.forward(x)
+        h = x.clone()
+        for layer in layers:  # the oracle's layer flow, layer after layer, residual in bf16
+            if h.shape[0]:
+                h = h + oracle.ds_moe_layer(h, layer)[0]
+        torch.save({"out": out, "ref": ref, "expected": h}, os.path.join(outdir, f"rank{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("tokens", [(4, 5), (3, 0)])
+def test_ep_stack_world2_matches_one_rank_and_oracle(tokens):
+    """Three layers with residuals (the routed-expert stack of a decode step),
+    a rank with no tokens included."""
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_stack_main, args=(2, _free_port(), tokens, d), nprocs=2, join=True, start_method="spawn")
+        for rank in range(2):
+            r = torch.load(os.path.join(d, f"rank{rank}.pt"))
+            assert r["out"].shape == (tokens[rank], synth.C1_TINY.hidden) and r["out"].dtype == torch.bfloat16
+            assert torch.equal(r["out"].view(torch.int16), r["ref"].view(torch.int16))
+            if tokens[rank]:
+                assert rel_l2(r["out"], r["expected"]) <= REL_L2_GATE
+                assert cos_dist(r["out"], r["expected"]) <= COS_GATE
