@@ -464,6 +464,21 @@ int moe_b200_select_gemv(int impl);
 /* The current selection (0 for the default, else 1 to 4). */
 int moe_b200_selected_gemv(void);
 
+/* ---------------------------------------------------------------------------
+ * Pack-file reads (host only): the FP8 pack loader's byte ranges.
+ * ------------------------------------------------------------------------- */
+
+/* replaces native_read_tensor_bytes, native/fp16_loader.cpp:33-67 (POSIX
+ * pread instead of ReadFile): nbytes at absolute_offset of the file into
+ * out.  0 ok, 1 null argument, 2 the file cannot be opened, 3 the range ends
+ * past the file, 4 short read. */
+int moe_read_tensor_bytes(const char* path, uint64_t absolute_offset, uint64_t nbytes, uint8_t* out);
+/* n ranges of one file, range i into outs[i] (host memory, pinned or not),
+ * read in pieces of >= 8 MiB by `threads` threads (0: up to 8).  Codes as
+ * above. */
+int moe_read_spans(const char* path, int64_t n, const uint64_t* offsets, const uint64_t* lengths,
+                   uint8_t* const* outs, int64_t threads);
+
 /* Device error word (no reference counterpart): nonzero when a bounded wait
  * inside a kernel gave up (1: producer, 2: consumer, 4: drain, 8: misaligned
  * weights refused by the streaming kernel, 16: warp-MMA ring, 32: prefill

@@ -78,6 +78,8 @@ def _native_moe_disabled() -> bool:
 _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_b200_abi_version": ([], _INT),
     "moe_b200_last_error": ([], ctypes.c_char_p),
+    "moe_read_tensor_bytes": ([ctypes.c_char_p, ctypes.c_uint64, ctypes.c_uint64, _P], _INT),
+    "moe_read_spans": ([ctypes.c_char_p, _I64, _P, _P, _P, _I64], _INT),
     "moe_fp8_e4m3_block_linear_f32": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P], _INT),
     "moe_fp8_e4m3_block_dual_linear_f32": ([_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P], _INT),
     "moe_fp8_e4m3_block_mlp_f32": ([_P] * 8 + [_I64] * 5 + [_P, _I64, _P], _INT),
@@ -206,6 +208,41 @@ def _gpu(t: torch.Tensor, dtype: torch.dtype | None = None) -> torch.Tensor:
 
 def _ptr(t: torch.Tensor | None) -> _P:
     return _P(0 if t is None else int(t.data_ptr()))
+
+
+def native_read_tensor_bytes(path: str | Path, absolute_offset: int, nbytes: int, out: torch.Tensor) -> None:
+    """Read nbytes at absolute_offset of `path` into the host tensor `out`
+    (moe_read_tensor_bytes; the reference's checks and errors,
+    native/__init__.py:3314-3331)."""
+    lib = load_library()
+    if out.device.type != "cpu":
+        raise ValueError("native_read_tensor_bytes reads into host memory")
+    if not out.is_contiguous():
+        raise ValueError("native_read_tensor_bytes requires a contiguous output tensor")
+    if out.nelement() * out.element_size() != int(nbytes):
+        raise ValueError("output tensor byte size does not match requested native read size")
+    code = lib.moe_read_tensor_bytes(str(Path(path)).encode("utf-8"), int(absolute_offset), int(nbytes),
+                                     _P(int(out.data_ptr())))
+    if code != 0:
+        raise OSError(f"native_read_tensor_bytes failed with code {code} for {path}")
+
+
+def read_spans(path: str | Path, spans: list[tuple[int, int]], outs: list[torch.Tensor], threads: int = 0) -> None:
+    """Byte ranges (offset, length) of one file into contiguous host tensors of
+    exactly those lengths, several threads at once (moe_read_spans)."""
+    if len(spans) != len(outs):
+        raise ValueError("one output tensor per span")
+    for (_off, n), out in zip(spans, outs):
+        if out.device.type != "cpu" or not out.is_contiguous() or out.nelement() * out.element_size() != int(n):
+            raise ValueError("span outputs must be contiguous host tensors of the span's length")
+    k = len(spans)
+    offs = (ctypes.c_uint64 * max(k, 1))(*[int(o) for o, _ in spans])
+    lens = (ctypes.c_uint64 * max(k, 1))(*[int(n) for _, n in spans])
+    ptrs = (ctypes.c_void_p * max(k, 1))(*[int(t.data_ptr()) for t in outs])
+    code = load_library().moe_read_spans(str(Path(path)).encode("utf-8"), k, ctypes.cast(offs, _P),
+                                         ctypes.cast(lens, _P), ctypes.cast(ptrs, _P), int(threads))
+    if code != 0:
+        raise OSError(f"moe_read_spans failed with code {code} for {path}")
 
 
 def _check(code: int, name: str) -> None:
