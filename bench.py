@@ -161,6 +161,104 @@ def cpu_reference_sample(tokens: int, seed: int, reps: int = 1) -> dict:
                        f"shared expert); {len(experts)} routed experts; OMP threads {os.environ['OMP_NUM_THREADS']}")}
 
 
+def cpu_fp8_layer_sample(layer, x: torch.Tensor, reps: int = 1) -> dict:
+    """run_fp8_moe's default flow (fp8_source.py:1569-1884) on the host cores
+    for the host tokens `x`, with `layer`'s own weights (any device) copied to
+    the host for the experts those tokens select: torch CPU router, the
+    reference's compiled fp8_e4m3_block_mlp_f32 per expert (oracle/_ref),
+    bf16 combine, shared expert."""
+    import oracle
+    from oracle import ref
+    from pocketlm_b200 import synth
+
+    if not ref.available():
+        raise RuntimeError("reference build oracle/_ref missing")
+    cfg = layer.cfg
+    rw = layer.router_weight.cpu()
+    bias = None if layer.bias is None else layer.bias.cpu()
+    route = oracle.route_deepseek(x, rw, bias, top_k=cfg.top_k, n_groups=cfg.n_group, topk_groups=cfg.topk_group,
+                                  route_scale=cfg.route_scale)
+    experts = sorted({int(v) for v in route.ids.reshape(-1).tolist()})
+    ids = experts + [cfg.n_routed]
+    idx = torch.tensor([e if layer.slots is None else layer.slots[e] for e in ids], device=layer.w13.device)
+    host = synth.Fp8MoELayer(cfg, rw, bias, *(t.index_select(0, idx).cpu() for t in (layer.w13, layer.s13,
+                                                                                     layer.w2, layer.s2)),
+                             {e: i for i, e in enumerate(ids)})
+    times = []
+    for _ in range(max(1, reps)):
+        t0 = time.perf_counter()
+        oracle.ds_moe_layer(x, host, route=None, mlp_fn=ref.fp8_mlp)
+        times.append(time.perf_counter() - t0)
+    per = statistics.median(times)
+    return {"value": x.shape[0] / per, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)),
+            "kind": "reference", "seconds_per_sample": per, "routed_experts": len(experts)}
+
+
+def cpu_prefill_expert_sample(layer, x: torch.Tensor, ids: torch.Tensor, n_experts: int = 4) -> dict:
+    """The reference's CPU cost of a prefill batch, from a bounded sample:
+    run_fp8_moe's default flow calls the compiled fp8_e4m3_block_mlp_f32 once
+    per selected expert on all of that expert's rows (fp8_source.py:1600-1660),
+    and at prefill sizes those calls are the whole cost.  Time those calls
+    (oracle/_ref) for the `n_experts` experts around the median load of this
+    batch -- their full row sets, the layer's own weights copied to the host --
+    and scale the per-row time to the batch's T * (k + 1) pairs."""
+    from oracle import ref
+
+    if not ref.available():
+        raise RuntimeError("reference build oracle/_ref missing")
+    cfg = layer.cfg
+    T = int(ids.shape[0])
+    counts = torch.bincount(ids.reshape(-1).cpu(), minlength=cfg.n_routed)
+    order = [int(e) for e in torch.argsort(counts, stable=True).tolist() if int(counts[e]) > 0]
+    mid = len(order) // 2
+    chosen = order[max(0, mid - n_experts // 2):max(0, mid - n_experts // 2) + n_experts]
+    flat = ids.reshape(-1)
+    rows_total, seconds = 0, 0.0
+    for e in chosen:
+        rows = (flat == e).nonzero().reshape(-1) // cfg.top_k
+        xe = x.index_select(0, rows.to(x.device)).cpu().float()
+        i = e if layer.slots is None else layer.slots[e]
+        w = [t.cpu() for t in (layer.w13[i, 0], layer.s13[i, 0], layer.w13[i, 1], layer.s13[i, 1], layer.w2[i],
+                               layer.s2[i])]
+        t0 = time.perf_counter()
+        ref.fp8_mlp(*w, xe)
+        seconds += time.perf_counter() - t0
+        rows_total += int(rows.numel())
+    per_row = seconds / max(1, rows_total)
+    batch_seconds = per_row * T * (cfg.top_k + 1)
+    return {"value": T / batch_seconds, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)),
+            "kind": "reference", "seconds_per_sample": seconds, "sampled_rows": rows_total,
+            "sampled_experts": chosen, "estimated_batch_seconds": batch_seconds}
+
+
+def cpu_q4_layer_sample(layer, x: torch.Tensor, reps: int = 1) -> dict:
+    """The reference's Q4 token loop (layer_bridge.py:909-955: softmax top-k
+    router in torch, then q4_moe_selected_forward_u16 per token,
+    q4_dequant.cpp:357-476, compiled in oracle/_ref) on the host cores for the
+    host tokens `x`, with `layer`'s own weights copied to the host."""
+    import oracle
+    from oracle import ref
+
+    if not ref.available():
+        raise RuntimeError("reference build oracle/_ref missing")
+    cfg = layer.cfg
+    rw = layer.router_weight.cpu()
+    probe = oracle.route_softmax_topk(x, rw, top_k=cfg.top_k, normalize=True)
+    host = {e: tuple(t.cpu() for t in layer.expert(e)) for e in sorted({int(v) for v in probe.ids.reshape(-1)})}
+    times = []
+    for _ in range(max(1, reps)):
+        t0 = time.perf_counter()
+        route = oracle.route_softmax_topk(x, rw, top_k=cfg.top_k, normalize=True)
+        x16 = x.to(torch.float16)
+        for t in range(x.shape[0]):
+            ref.q4_moe_selected_forward(x16[t], [host[int(e)] for e in route.ids[t].tolist()],
+                                        route.weights[t].float(), cfg.hidden, cfg.inter)
+        times.append(time.perf_counter() - t0)
+    per = statistics.median(times)
+    return {"value": x.shape[0] / per, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)),
+            "kind": "reference", "seconds_per_sample": per, "experts": len(host)}
+
+
 # ---------------------------------------------------------------------------
 # GPU measurement
 # ---------------------------------------------------------------------------
@@ -390,10 +488,26 @@ def run_prefill(args, dev, flush, peaks, token_list) -> dict:
             "mma_kind": "tcgen05.mma kind::f16 (fp16 A/B, fp32 accumulate in TMEM)",
         }
         del x, ids
+    cpu = None
+    if not args.no_cpu_baseline and token_list:
+        # the reference's per-expert CPU calls on the 8192-token batch (or the largest), same weights
+        T = 8192 if 8192 in token_list else max(token_list)
+        x = synth.make_hidden(T, cfg.hidden, seed=args.seed + T, device=dev)
+        ids = torch.empty((T, cfg.top_k), dtype=torch.int64, device=dev)
+        gpu_layer.forward(x, ids=ids)
+        try:
+            cpu = cpu_prefill_expert_sample(layer, x, ids, n_experts=max(1, args.cpu_prefill_experts))
+            cpu["sample"] = (f"the reference's fp8_e4m3_block_mlp_f32 (oracle/_ref) on the full row sets of "
+                             f"{len(cpu['sampled_experts'])} median-load experts of the {T}-token config-3 batch "
+                             f"({cpu['sampled_rows']} rows, same weights); per-row time scaled to the batch's "
+                             f"{T * (cfg.top_k + 1)} pairs; OMP threads {os.environ.get('OMP_NUM_THREADS')}")
+        except RuntimeError as exc:
+            cpu = {"unavailable": str(exc)}
+        del x, ids
     del gpu_layer, layer
     torch.cuda.empty_cache()
     return {"workload": "c3-dsv3-prefill-zipf", "peak_bf16_tflops": bf16_peak,
-            "peak_source": f"{peaks['source']} bf16_tflops", "sweep": out}
+            "peak_source": f"{peaks['source']} bf16_tflops", "sweep": out, "cpu_baseline": cpu}
 
 
 def run_q4(args, dev, flush, peaks, token_list) -> dict:
@@ -428,10 +542,21 @@ def run_q4(args, dev, flush, peaks, token_list) -> dict:
                        "tflops": flops / (ms / 1e3) / 1e12,
                        "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peaks.get("bf16_tflops", 1590.0)}
         del x, ids
+    cpu = None
+    if not args.no_cpu_baseline and token_list:
+        n = max(1, args.cpu_q4_tokens)
+        T = max(token_list)
+        x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 7 * T, device=dev)[:n].cpu()
+        try:
+            cpu = cpu_q4_layer_sample(layer.layer, x)
+            cpu["sample"] = (f"first {n} tokens of the {T}-token config-4 batch, same weights, through the "
+                             f"reference's token loop with oracle/_ref's q4_moe_selected_forward_u16")
+        except RuntimeError as exc:
+            cpu = {"unavailable": str(exc)}
     del layer
     torch.cuda.empty_cache()
     return {"workload": "c4-mixtral-q4", "kernel": "dense_mma_gemv_kernel<Q4> (dense_gemv.cu) / "
-            "prefill_gemm_kernel<*, Q4> (prefill_gemm.cu)", "sweep": out}
+            "prefill_gemm_kernel<*, Q4> (prefill_gemm.cu)", "sweep": out, "cpu_baseline": cpu}
 
 
 def timed_max_over_ranks(fn, steps: int, warmup: int, flush: torch.Tensor, dev: torch.device) -> float:
@@ -815,6 +940,10 @@ def main() -> None:
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--cpu-sample-tokens", type=int, default=4)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--cpu-prefill-experts", type=int, default=4,
+                        help="experts of the config-3 batch whose rows are timed through the reference's CPU kernel")
+    parser.add_argument("--cpu-q4-tokens", type=int, default=4,
+                        help="tokens of the config-4 batch timed through the reference's CPU token loop")
     parser.add_argument("--sweep", default="1,4,16,64",
                         help="comma-separated extra batch sizes measured after --tokens, or 'none'")
     parser.add_argument("--gemv", choices=list(GEMV_IMPLS), default="auto",
