@@ -763,6 +763,16 @@ def run_stack(args, rank: int, world: int) -> dict | None:
     if rank != 0:
         return None
     head = sweep[str(batches[0])]
+    cpu = None
+    if not args.no_cpu_baseline:
+        # derived, as the reference runs one layer after another: its per-layer time x the layers
+        try:
+            s = cpu_reference_sample(max(1, batches[0]), seed=args.seed, reps=1)
+            cpu = {"value": max(1, batches[0]) / (s["seconds_per_sample"] * L), "unit": "tokens/s",
+                   "cores": s["cores"], "kind": "reference",
+                   "sample": f"derived: the reference's time for one config-2 layer ({s['sample']}) x {L} layers"}
+        except RuntimeError as exc:
+            cpu = {"unavailable": str(exc)}
     return {
         "metric": METRIC, "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "strong",
@@ -780,7 +790,7 @@ def run_stack(args, rank: int, world: int) -> dict | None:
                 "h2d_bytes_per_step": stack_share(batches[0], 0, world) * cfg.hidden * 2,
                 "d2h_bytes_per_step": stack_share(batches[0], 0, world) * cfg.hidden * 2},
         "exchange": "peer-memory (symmetric memory, NVLink stores), one buffer set for all layers",
-        "sweep": sweep, "cpu_baseline": None, "clocks": clock_info,
+        "sweep": sweep, "cpu_baseline": cpu, "clocks": clock_info,
     }
 
 
