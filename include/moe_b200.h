@@ -374,14 +374,16 @@ int moe_ep_combine(const float* y, const int32_t* entry_pos, const float* pos_we
  *   moe_ep_count_ranks -> all-gather of the [world] counts into
  *   count_matrix [world][world] (row = source rank) -> moe_ep_dispatch_p2p
  *   (this rank's rows written into each destination's buffers, token order
- *   kept, ranks in order) -> barrier -> moe_ep_experts_fp8 over the local
- *   buffer -> moe_ep_return_p2p (each output row written into row e of its
- *   source rank's return buffer, e = the entry t * top_k + slot) -> barrier
- *   -> moe_ep_combine with entry_pos = identity.  src = rank * src_stride +
- *   entry; src_stride >= the entries of any rank; capacity >= the rows any
- *   rank receives (world * src_stride suffices).  The barriers are the
- *   caller's (any stream-ordered collective).  Same arithmetic and combine
- *   order as the all-to-all exchange above. */
+ *   kept, ranks in order) -> barrier -> moe_ep_experts_return_p2p over the
+ *   local buffer (or moe_ep_experts_fp8 then moe_ep_return_p2p): each output
+ *   row is written into row e of its source rank's return buffer, e = the
+ *   entry t * top_k + slot -> barrier -> moe_ep_combine with entry_pos =
+ *   identity.  src = rank * src_stride + e; src_stride > every return row
+ *   (tokens * top_k, or tokens * (top_k + 1) when the rank's own shared-expert
+ *   rows go through the same call with e = tokens * top_k + t); capacity >=
+ *   the rows any rank receives (world * tokens * top_k suffices).  The
+ *   barriers are the caller's (any stream-ordered collective).  Same
+ *   arithmetic and combine order as the all-to-all exchange above. */
 int moe_ep_count_ranks(const int64_t* ids, int64_t tokens, int64_t top_k, int64_t num_experts, int64_t world,
                        int32_t* counts, void* stream);
 int moe_ep_dispatch_p2p(const int64_t* ids, const uint16_t* hidden_bf16, int64_t tokens, int64_t hidden_dim,
