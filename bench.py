@@ -130,24 +130,33 @@ class ClockSampler:
 # CPU baseline: the reference's own kernels (oracle/_ref) in run_fp8_moe's flow
 # ---------------------------------------------------------------------------
 
-def cpu_reference_sample(tokens: int, seed: int, reps: int = 1) -> dict:
-    """Time run_fp8_moe's default flow (fp8_source.py:1569-1884) on the host
-    cores with the reference's compiled fp8_e4m3_block_mlp_f32 on a bounded
-    sample of `tokens` tokens of the config-2 workload (weights generated on
-    the CPU for exactly the experts those tokens select)."""
+def cpu_decode_sample_inputs(tokens: int, seed: int):
+    """A bounded sample of the config-2 decode workload for the reference's
+    CPU flow: `tokens` tokens and the layer's weights generated on the CPU for
+    exactly the experts those tokens select (plus the shared one)."""
     import oracle
-    from oracle import ref
     from pocketlm_b200 import synth
 
-    if not ref.available():
-        raise RuntimeError("reference build oracle/_ref missing")
     cfg = synth.C2_DSV3
     x = synth.make_hidden(tokens, cfg.hidden, seed=seed)
     probe = synth.make_fp8_layer(cfg, seed=seed, experts=[])
     route = oracle.route_deepseek(x, probe.router_weight, probe.bias, top_k=cfg.top_k, n_groups=cfg.n_group,
                                   topk_groups=cfg.topk_group, route_scale=cfg.route_scale)
     experts = sorted({int(v) for v in route.ids.reshape(-1).tolist()})
-    layer = synth.make_fp8_layer(cfg, seed=seed, experts=experts + [cfg.n_routed])
+    return x, synth.make_fp8_layer(cfg, seed=seed, experts=experts + [cfg.n_routed]), experts
+
+
+def cpu_reference_sample(tokens: int, seed: int, reps: int = 1, inputs=None) -> dict:
+    """Time run_fp8_moe's default flow (fp8_source.py:1569-1884) on the host
+    cores with the reference's compiled fp8_e4m3_block_mlp_f32 on a bounded
+    sample of `tokens` tokens of the config-2 workload (cpu_decode_sample_inputs,
+    or `inputs` made by it once for several timings)."""
+    import oracle
+    from oracle import ref
+
+    if not ref.available():
+        raise RuntimeError("reference build oracle/_ref missing")
+    x, layer, experts = inputs if inputs is not None else cpu_decode_sample_inputs(tokens, seed)
     times = []
     for _ in range(max(1, reps)):
         t0 = time.perf_counter()
@@ -921,8 +930,9 @@ def run_reference(args, rank: int, world: int) -> dict | None:
     if not ref.available():
         return {"impl": "reference", "unavailable": "reference CPU build (oracle/_ref) missing"}
     samples = []
+    inputs = cpu_decode_sample_inputs(args.cpu_sample_tokens, args.seed)  # generated once, timed per step
     for i in range(args.warmup + args.steps):
-        s = cpu_reference_sample(args.cpu_sample_tokens, seed=args.seed, reps=1)
+        s = cpu_reference_sample(args.cpu_sample_tokens, seed=args.seed, reps=1, inputs=inputs)
         if i >= args.warmup:
             samples.append(s["seconds_per_sample"])
     per = statistics.mean(samples)
