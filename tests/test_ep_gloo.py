@@ -96,11 +96,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("tokens", [(8, 8), (5, 11), (0, 7)])
+@pytest.mark.parametrize("tokens", [(8, 8), (5, 11), (0, 7), (3, 0, 5, 2)])
 def test_ep_world2_matches_one_rank_and_oracle(tokens):
+    """World 2, and world 4 (each rank exchanging with three peers, one of
+    them empty) against one rank and the oracle."""
+    world = len(tokens)
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_rank_main, args=(2, _free_port(), tokens, d), nprocs=2, join=True, start_method="spawn")
-        for rank in range(2):
+        mp.start_processes(_rank_main, args=(world, _free_port(), tokens, d), nprocs=world, join=True,
+                           start_method="spawn")
+        for rank in range(world):
             r = torch.load(os.path.join(d, f"rank{rank}.pt"))
             assert torch.equal(r["ids"], r["ref_ids"])
             assert r["out"].shape == (tokens[rank], synth.C1_TINY.hidden)
