@@ -19,8 +19,15 @@ copies inside the timed region (`e2e`), the HBM roofline of the dominant
 kernel (the grouped GEMV gate/up stage), the reference's own CPU path timed
 on this host (`cpu_baseline`, oracle/_ref), clocks sampled during the run.
 
---impl reference times the reference's CPU path alone (oracle/_ref kernels
-driven through run_fp8_moe's default flow) on a bounded token sample.
+Every run also checks what it timed (`parity`, after the timed regions):
+each batch's expert ids against the oracle's router (ties within 1e-6
+excused) and its outputs against the oracle's run_fp8_moe flow on the same
+weights -- all tokens of the decode batches, a slice of the prefill ones --
+with the north star's gate (rel-L2 <= 2e-2, cosine distance <= 1e-3).
+
+--impl reference times the reference's CPU path alone (its own compiled
+kernels, oracle/_ref, driven through run_fp8_moe's default flow) on the same
+workload: the full 64-token batch, with every expert it selects.
 With --gpus N > 1 (torchrun) the layer runs expert-parallel (pocketlm_b200/ep.py):
 each rank holds 256/N routed experts plus the shared expert and router, routes
 its own --tokens tokens and exchanges them with NCCL all-to-alls (weak
@@ -143,7 +150,9 @@ def cpu_decode_sample_inputs(tokens: int, seed: int):
     route = oracle.route_deepseek(x, probe.router_weight, probe.bias, top_k=cfg.top_k, n_groups=cfg.n_group,
                                   topk_groups=cfg.topk_group, route_scale=cfg.route_scale)
     experts = sorted({int(v) for v in route.ids.reshape(-1).tolist()})
-    return x, synth.make_fp8_layer(cfg, seed=seed, experts=experts + [cfg.n_routed]), experts
+    layer = synth.make_fp8_layer(cfg, seed=seed, experts=experts + [cfg.n_routed],
+                                 threads=len(os.sched_getaffinity(0)))
+    return x, layer, experts
 
 
 def cpu_reference_sample(tokens: int, seed: int, reps: int = 1, inputs=None) -> dict:
@@ -165,9 +174,10 @@ def cpu_reference_sample(tokens: int, seed: int, reps: int = 1, inputs=None) -> 
     per_step = statistics.median(times)
     return {"value": tokens / per_step, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)),
             "kind": "reference", "seconds_per_sample": per_step,
-            "sample": (f"{tokens} tokens of the config-2 decode batch through run_fp8_moe's default flow "
+            "sample": (f"the whole {tokens}-token config-2 decode batch through run_fp8_moe's default flow "
                        f"(torch CPU router, per-expert fp8_e4m3_block_mlp_f32 from oracle/_ref, bf16 combine, "
-                       f"shared expert); {len(experts)} routed experts; OMP threads {os.environ['OMP_NUM_THREADS']}")}
+                       f"shared expert); {len(experts)} routed experts; OMP threads {os.environ['OMP_NUM_THREADS']}; "
+                       f"weights drawn on the host from the same seeded distributions")}
 
 
 def cpu_fp8_layer_sample(layer, x: torch.Tensor, reps: int = 1) -> dict:
@@ -188,11 +198,14 @@ def cpu_fp8_layer_sample(layer, x: torch.Tensor, reps: int = 1) -> dict:
     route = oracle.route_deepseek(x, rw, bias, top_k=cfg.top_k, n_groups=cfg.n_group, topk_groups=cfg.topk_group,
                                   route_scale=cfg.route_scale)
     experts = sorted({int(v) for v in route.ids.reshape(-1).tolist()})
-    ids = experts + [cfg.n_routed]
-    idx = torch.tensor([e if layer.slots is None else layer.slots[e] for e in ids], device=layer.w13.device)
-    host = synth.Fp8MoELayer(cfg, rw, bias, *(t.index_select(0, idx).cpu() for t in (layer.w13, layer.s13,
-                                                                                     layer.w2, layer.s2)),
-                             {e: i for i, e in enumerate(ids)})
+    if layer.w13.device.type == "cpu":
+        host = layer  # already on the host (a full copy made once for the parity checks)
+    else:
+        ids = experts + [cfg.n_routed]
+        idx = torch.tensor([e if layer.slots is None else layer.slots[e] for e in ids], device=layer.w13.device)
+        host = synth.Fp8MoELayer(cfg, rw, bias, *(t.index_select(0, idx).cpu() for t in (layer.w13, layer.s13,
+                                                                                         layer.w2, layer.s2)),
+                                 {e: i for i, e in enumerate(ids)})
     times = []
     for _ in range(max(1, reps)):
         t0 = time.perf_counter()
@@ -238,6 +251,16 @@ def cpu_prefill_expert_sample(layer, x: torch.Tensor, ids: torch.Tensor, n_exper
     return {"value": T / batch_seconds, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)),
             "kind": "reference", "seconds_per_sample": seconds, "sampled_rows": rows_total,
             "sampled_experts": chosen, "estimated_batch_seconds": batch_seconds}
+
+
+def cpu_prefill_full_batch(host_layer, x: torch.Tensor) -> dict:
+    """The reference's CPU flow timed on a whole prefill batch (one run):
+    run_fp8_moe's default flow with the compiled fp8_e4m3_block_mlp_f32 on
+    every selected expert's full row set, the layer's own weights on the host."""
+    s = cpu_fp8_layer_sample(host_layer, x, reps=1)
+    s["sample"] = (f"the whole {int(x.shape[0])}-token config-3 batch through run_fp8_moe's default flow "
+                   f"(oracle/_ref kernels, {s['routed_experts']} routed experts, same weights and tokens), measured")
+    return s
 
 
 def cpu_q4_layer_sample(layer, x: torch.Tensor, reps: int = 1) -> dict:
@@ -338,6 +361,17 @@ def read_traffic(name: str):
     return None
 
 
+def parity_leg(fn, *a, **kw) -> dict:
+    """The checker on a timed batch (oracle/parity.py), after its timing; a
+    checker that cannot run is reported, never silently passed."""
+    try:
+        from oracle import parity
+
+        return getattr(parity, fn)(*a, **kw)
+    except Exception as exc:  # noqa: BLE001 -- reported in the JSON line
+        return {"pass": False, "error": f"{type(exc).__name__}: {exc}"}
+
+
 def run_ours(args, rank: int, world: int) -> dict | None:
     from pocketlm_b200 import native, synth
     from pocketlm_b200.runtime import DsMoELayerGPU
@@ -351,6 +385,7 @@ def run_ours(args, rank: int, world: int) -> dict | None:
     flush = torch.zeros((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
     peaks = measured_peaks()
     results = {}
+    checked = {}  # T -> (x, out, ids) of the timed batch, for the parity leg
     sweep = [] if args.sweep == "none" else [int(v) for v in args.sweep.split(",") if v]
     token_list = [args.tokens] + [t for t in sweep if t != args.tokens]
     with ClockSampler(dev.index) as clocks:
@@ -396,6 +431,9 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                 t = torch.tensor([e2e_ms], device=dev)
                 torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
                 e2e_ms = float(t.item())
+            torch.cuda.synchronize()
+            # what the timed graph replays produced for this batch, for the parity leg
+            checked[T] = (x.cpu(), graphed.output.cpu(), graphed.ids.cpu())
             results[T] = {
                 "tokens": T, "ms_per_step": ms, "tokens_per_s": T * world / (ms / 1e3),
                 "eager_ms_per_step": eager_ms,
@@ -407,6 +445,26 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                 "gateup_gbs": (b["gateup"] / (gateup_ms / 1e3) / 1e9) if gateup_ms else None,
                 "down_gbs": (b["down"] / (down_ms / 1e3) / 1e9) if down_ms else None,
             }
+        # the checker on every decode batch (all tokens), and the reference's CPU path on the headline batch,
+        # both on one host copy of this layer's weights
+        host_layer = layer.to("cpu") if not args.no_parity or not args.no_cpu_baseline else None
+        parity = {}
+        if not args.no_parity:
+            for T, (xc, oc, ic) in sorted(checked.items()):
+                parity[f"c2-dsv3-decode-T{T}"] = parity_leg("fp8_layer_parity", host_layer, xc, oc, ic)
+        cpu = None
+        if not args.no_cpu_baseline and rank == 0:
+            try:
+                cpu = cpu_fp8_layer_sample(host_layer, checked[args.tokens][0], reps=2)
+                cpu["sample"] = (f"the whole {args.tokens}-token config-2 batch of the GPU run (same weights and "
+                                 f"tokens) through run_fp8_moe's default flow: torch CPU router, the reference's "
+                                 f"compiled fp8_e4m3_block_mlp_f32 (oracle/_ref) per selected expert "
+                                 f"({cpu['routed_experts']}), bf16 combine, shared expert; OMP threads "
+                                 f"{os.environ['OMP_NUM_THREADS']}")
+            except Exception as exc:  # the baseline is reported, not required
+                cpu = {"value": None, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)),
+                       "kind": "reference", "sample": f"unavailable: {type(exc).__name__}: {exc}"}
+        del host_layer
         prefill, q4 = {}, {}
         if args.prefill_tokens != "none" or args.q4_tokens != "none":
             del gpu_layer, layer, graphed
@@ -422,13 +480,13 @@ def run_ours(args, rank: int, world: int) -> dict | None:
     head = results[args.tokens]
     peak = peaks["hbm_gbs"]
     achieved = head["gateup_gbs"]
-    cpu = None
-    if not args.no_cpu_baseline:
-        try:
-            cpu = cpu_reference_sample(args.cpu_sample_tokens, seed=args.seed, reps=2)
-        except Exception as exc:  # the baseline is reported, not required
-            cpu = {"value": None, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)), "kind": "reference",
-                   "sample": f"unavailable: {exc}"}
+    for block in (prefill, q4):
+        for key, rep in (block.pop("parity", None) or {}).items():
+            parity[key] = rep
+    parity_summary = {"gate": {"rel_l2": 2e-2, "cos_dist": 1e-3, "ids": "bit-exact, ties within 1e-6 excused"},
+                      "all_pass": bool(parity) and all(r.get("pass") for r in parity.values()),
+                      "cases": parity} if not args.no_parity else None
+    t1 = results.get(1)
     return {
         "metric": METRIC, "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
@@ -452,6 +510,11 @@ def run_ours(args, rank: int, world: int) -> dict | None:
         "gpu_launches": KERNELS_PER_LAYER[args.gemv] * args.steps,
         "cpu_baseline": cpu,
         "clocks": clock_info,
+        "parity": parity_summary,
+        "decode_T1": None if t1 is None else {
+            "ms_per_step": t1["ms_per_step"], "tokens_per_s": t1["tokens_per_s"],
+            "layer_bytes": t1["layer_bytes"], "layer_hbm_frac": t1["layer_hbm_frac"],
+            "stage_ms": t1["stage_ms"], "target_hbm_frac": 0.70},
         "sweep": {str(T): {k: v for k, v in r.items() if k != "stage_ms"} | {"stage_ms": r["stage_ms"]}
                   for T, r in sorted(results.items())},
         "prefill": prefill,
@@ -474,13 +537,18 @@ def run_prefill(args, dev, flush, peaks, token_list) -> dict:
     gpu_layer = DsMoELayerGPU(layer)
     bf16_peak = peaks.get("bf16_tflops", 1590.0)
     out = {}
+    checked = {}
     for T in token_list:
         x = synth.make_hidden(T, cfg.hidden, seed=args.seed + T, device=dev)
         ids = torch.empty((T, cfg.top_k), dtype=torch.int64, device=dev)
         gpu_layer.forward(x, ids=ids)
         torch.cuda.synchronize()
         steps = max(3, min(args.steps, 10))
-        ms = statistics.mean(time_steps(lambda: gpu_layer.forward(x), steps, args.warmup, flush))
+        y = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=dev)
+        ms = statistics.mean(time_steps(lambda: gpu_layer.forward(x, out=y), steps, args.warmup, flush))
+        torch.cuda.synchronize()
+        checked[T] = (x.cpu(), y.cpu(), ids.cpu())  # the last timed forward's output
+        del y
         stages = stage_times(gpu_layer, x, 3, flush)
         flops = T * (cfg.top_k + 1) * 3 * 2 * cfg.hidden * cfg.inter + T * 2 * cfg.hidden * cfg.n_routed
         pairs = T * (cfg.top_k + 1)
@@ -497,26 +565,37 @@ def run_prefill(args, dev, flush, peaks, token_list) -> dict:
             "mma_kind": "tcgen05.mma kind::f16 (fp16 A/B, fp32 accumulate in TMEM)",
         }
         del x, ids
+    host_layer = layer.to("cpu") if checked and (not args.no_parity or not args.no_cpu_baseline) else None
+    parity = {}
+    if not args.no_parity:
+        from oracle.parity import slice_tokens
+
+        for T, (xc, yc, ic) in sorted(checked.items()):
+            parity[f"c3-dsv3-prefill-zipf-T{T}"] = parity_leg("fp8_layer_parity", host_layer, xc, yc, ic,
+                                                              slice_tokens(ic))
     cpu = None
     if not args.no_cpu_baseline and token_list:
         # the reference's per-expert CPU calls on the 8192-token batch (or the largest), same weights
-        T = 8192 if 8192 in token_list else max(token_list)
-        x = synth.make_hidden(T, cfg.hidden, seed=args.seed + T, device=dev)
-        ids = torch.empty((T, cfg.top_k), dtype=torch.int64, device=dev)
-        gpu_layer.forward(x, ids=ids)
+        T = 8192 if 8192 in checked else max(checked)
+        xc, _y, ic = checked[T]
         try:
-            cpu = cpu_prefill_expert_sample(layer, x, ids, n_experts=max(1, args.cpu_prefill_experts))
+            cpu = cpu_prefill_expert_sample(host_layer, xc, ic, n_experts=max(1, args.cpu_prefill_experts))
             cpu["sample"] = (f"the reference's fp8_e4m3_block_mlp_f32 (oracle/_ref) on the full row sets of "
                              f"{len(cpu['sampled_experts'])} median-load experts of the {T}-token config-3 batch "
                              f"({cpu['sampled_rows']} rows, same weights); per-row time scaled to the batch's "
                              f"{T * (cfg.top_k + 1)} pairs; OMP threads {os.environ.get('OMP_NUM_THREADS')}")
         except Exception as exc:  # a baseline that cannot run must not cost the GPU numbers
             cpu = {"unavailable": f"{type(exc).__name__}: {exc}"}
-        del x, ids
-    del gpu_layer, layer
+        if args.cpu_prefill_full and args.cpu_prefill_full in checked:
+            xf = checked[args.cpu_prefill_full][0]
+            try:
+                cpu["measured_full_batch"] = cpu_prefill_full_batch(host_layer, xf)
+            except Exception as exc:  # noqa: BLE001
+                cpu["measured_full_batch"] = {"unavailable": f"{type(exc).__name__}: {exc}"}
+    del gpu_layer, layer, host_layer
     torch.cuda.empty_cache()
     return {"workload": "c3-dsv3-prefill-zipf", "peak_bf16_tflops": bf16_peak,
-            "peak_source": f"{peaks['source']} bf16_tflops", "sweep": out, "cpu_baseline": cpu}
+            "peak_source": f"{peaks['source']} bf16_tflops", "sweep": out, "cpu_baseline": cpu, "parity": parity}
 
 
 def run_q4(args, dev, flush, peaks, token_list) -> dict:
@@ -534,13 +613,22 @@ def run_q4(args, dev, flush, peaks, token_list) -> dict:
     cfg = synth.C4_MIXTRAL
     layer = Q4MoELayerGPU(synth.make_q4_layer(cfg, seed=args.seed, device=dev))
     out = {}
+    parity = {}
     for T in token_list:
         x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 7 * T, device=dev)
         ids = torch.empty((T, cfg.top_k), dtype=torch.int64, device=dev)
         layer.forward(x, ids=ids)
         torch.cuda.synchronize()
         steps = max(3, min(args.steps, 20))
-        ms = statistics.mean(time_steps(lambda: layer.forward(x), steps, args.warmup, flush))
+        y = torch.empty_like(x)
+        ms = statistics.mean(time_steps(lambda: layer.forward(x, out=y), steps, args.warmup, flush))
+        torch.cuda.synchronize()
+        if not args.no_parity:
+            from oracle.parity import slice_tokens
+
+            sel = None if T <= 64 else slice_tokens(ids, n_spread=32, n_heavy=8)
+            parity[f"c4-mixtral-q4-T{T}"] = parity_leg("q4_layer_parity", layer.layer, x, y, ids, sel)
+        del y
         n_exp = len({int(v) for v in ids.reshape(-1).tolist()})
         nbytes = n_exp * cfg.expert_bytes + cfg.n_experts * cfg.hidden * 2 + T * cfg.hidden * 4
         gemm = layer.tables_tiled is not None and T * cfg.top_k >= layer.prefill_pairs * cfg.n_experts
@@ -565,7 +653,7 @@ def run_q4(args, dev, flush, peaks, token_list) -> dict:
     del layer
     torch.cuda.empty_cache()
     return {"workload": "c4-mixtral-q4", "kernel": "dense_mma_gemv_kernel<Q4> (dense_gemv.cu) / "
-            "prefill_gemm_kernel<*, Q4> (prefill_gemm.cu)", "sweep": out, "cpu_baseline": cpu}
+            "prefill_gemm_kernel<*, Q4> (prefill_gemm.cu)", "sweep": out, "cpu_baseline": cpu, "parity": parity}
 
 
 def timed_max_over_ranks(fn, steps: int, warmup: int, flush: torch.Tensor, dev: torch.device) -> float:
@@ -631,16 +719,30 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
 
         e2e_ms = timed(e2e)
     del graphed  # a graph holding NCCL calls goes before the process group
-    _out, ids, _w = ep.forward(x)
+    out_ep, ids, _w = ep.forward(x)
     gathered = [torch.empty_like(ids) for _ in range(world)]
     dist.all_gather(gathered, ids)
     clock_info = clocks.summary()
+    parity = None
+    if not args.no_parity:
+        # the checker on this rank's batch: the experts its tokens selected, regenerated here from their own
+        # seeded generators (identical to the copies on the ranks that own them), against the oracle's flow
+        need = sorted({int(v) for v in ids.reshape(-1).tolist()}) + [cfg.n_routed]
+        ref_layer = synth.make_fp8_layer(cfg, seed=args.seed, device=dev, experts=need)
+        parity = parity_leg("fp8_layer_parity", ref_layer, x, out_ep, ids)
+        del ref_layer
+        torch.cuda.empty_cache()
+    parity_by_rank = [None] * world
+    dist.all_gather_object(parity_by_rank, parity)
     with ClockSampler(dev.index) as prefill_clocks:
         prefill = run_ep_prefill(args, rank, world, ep, timed, peaks)
     if prefill is not None:
         prefill["clocks"] = prefill_clocks.summary()
     if rank != 0:
         return None
+    cases = {f"c2-dsv3-decode-T{T}-ep{world}-rank{r}": rep for r, rep in enumerate(parity_by_rank) if rep}
+    for key, rep in ((prefill or {}).pop("parity", None) or {}).items():
+        cases[key] = rep
     all_ids = torch.cat(gathered).cpu()
     per_rank = cfg.n_routed // world
     # bytes streamed by the busiest rank: its experts hit by any token (+ the shared expert)
@@ -676,6 +778,9 @@ def run_ours_ep(args, rank: int, world: int) -> dict | None:
         "ep_prefill": prefill,
         "cpu_baseline": None,
         "clocks": clock_info,
+        "parity": None if args.no_parity else {
+            "gate": {"rel_l2": 2e-2, "cos_dist": 1e-3, "ids": "bit-exact, ties within 1e-6 excused"},
+            "all_pass": bool(cases) and all(r.get("pass") for r in cases.values()), "cases": cases},
     }
 
 
@@ -827,6 +932,7 @@ def run_ep_prefill(args, rank: int, world: int, ep, timed, peaks) -> dict | None
     zipf = synth.make_fp8_layer(cfg, seed=args.seed + 1, device=dev, bias_kind="zipf", experts=local)
     bf16_peak = peaks.get("bf16_tflops", 1590.0)
     sweeps = {}
+    parity = {}
     for exchange in ("nccl", "p2p"):
         pre = ExpertParallelLayer(cfg, rank, world, layer=zipf, device=dev, exchange=exchange,
                                   max_tokens=max(tokens))
@@ -835,6 +941,19 @@ def run_ep_prefill(args, rank: int, world: int, ep, timed, peaks) -> dict | None
             x = synth.make_hidden(T, cfg.hidden, seed=args.seed + 100 * rank + T, device=dev)
             ms = timed(lambda: pre.forward(x), steps=max(3, min(args.steps, 10)))
             _out, ids, _w = pre.forward(x)
+            if exchange == "p2p" and not args.no_parity:
+                from oracle.parity import slice_tokens
+
+                sel = slice_tokens(ids, n_spread=32, n_heavy=8)
+                need = sorted({int(v) for v in ids[sel].reshape(-1).tolist()}) + [cfg.n_routed]
+                ref_layer = synth.make_fp8_layer(cfg, seed=args.seed + 1, device=dev, bias_kind="zipf",
+                                                 experts=need)
+                rep = parity_leg("fp8_layer_parity", ref_layer, x, _out, ids, sel)
+                del ref_layer
+                reps = [None] * world
+                dist.all_gather_object(reps, rep)
+                for r, one in enumerate(reps):
+                    parity[f"c3-dsv3-prefill-zipf-T{T}-ep{world}-rank{r}"] = one
             per_rank = torch.bincount(ids.reshape(-1) // ep.n_local, minlength=world).to(torch.int64)
             dist.all_reduce(per_rank)
             rows = per_rank.cpu() + T  # each rank also runs its own tokens' shared expert
@@ -854,7 +973,8 @@ def run_ep_prefill(args, rank: int, world: int, ep, timed, peaks) -> dict | None
             "exchanges": {"nccl": "NCCL all-to-all (counts read on the host)",
                           "p2p": "peer memory: dispatch kernel stores rows, down-GEMM epilogue stores outputs home"},
             "expert_kernel": "tcgen05 grouped GEMM (prefill_gemm.cu) when a rank receives >= 16 rows per expert",
-            "peak_bf16_tflops": bf16_peak, "peak_source": f"{peaks['source']} bf16_tflops", "sweep": sweeps}
+            "peak_bf16_tflops": bf16_peak, "peak_source": f"{peaks['source']} bf16_tflops", "sweep": sweeps,
+            "parity": parity}
 
 
 def run_profile_case(args) -> dict:
@@ -863,7 +983,7 @@ def run_profile_case(args) -> dict:
     by the kernels), run eagerly warmup + steps times.  Holds about
     (experts selected + 1) x 44 MB of weights instead of 11.3 GB."""
     from pocketlm_b200 import native, synth
-    from pocketlm_b200.runtime import DsMoELayerGPU, run_fp8_router
+    from pocketlm_b200.runtime import DsMoELayerGPU, route_resident_layer
 
     dev = torch.device("cuda", 0)
     native.load_library()
@@ -872,7 +992,7 @@ def run_profile_case(args) -> dict:
     # route on the GPU with the layer's own (device-generated) router, then
     # materialise exactly the experts that routing selects
     probe = synth.make_fp8_layer(cfg, seed=args.seed, device=dev, experts=[])
-    ids = run_fp8_router(probe, xd).indices_tensor
+    ids = route_resident_layer(probe, xd).indices_tensor
     experts = sorted({int(v) for v in ids.reshape(-1).tolist()}) + [cfg.n_routed]
     if args.profile_no_experts:
         experts = []  # routing kernels only: every expert absent, the GEMVs skip them
@@ -930,20 +1050,21 @@ def run_reference(args, rank: int, world: int) -> dict | None:
     if not ref.available():
         return {"impl": "reference", "unavailable": "reference CPU build (oracle/_ref) missing"}
     samples = []
-    inputs = cpu_decode_sample_inputs(args.cpu_sample_tokens, args.seed)  # generated once, timed per step
+    inputs = cpu_decode_sample_inputs(args.tokens, args.seed)  # the whole batch, generated once, timed per step
     for i in range(args.warmup + args.steps):
-        s = cpu_reference_sample(args.cpu_sample_tokens, seed=args.seed, reps=1, inputs=inputs)
+        s = cpu_reference_sample(args.tokens, seed=args.seed, reps=1, inputs=inputs)
         if i >= args.warmup:
             samples.append(s["seconds_per_sample"])
     per = statistics.mean(samples)
-    value = args.cpu_sample_tokens / per
+    value = args.tokens / per
     return {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 (reference CPU: e4m3 LUT decode, fp32 accumulate)",
         "data": "synthetic (seeded random DS-V3-shape weights and activations; no checkpoint)",
         "config": {"workload": f"c2-dsv3-decode-T{args.tokens}", "tokens_per_gpu": args.tokens,
-                   "parallelism": "host CPU"},
+                   "hidden": 7168, "moe_intermediate": 2048, "experts": "256+1", "top_k": 8,
+                   "parallelism": "host CPU", "routed_experts_in_batch": len(inputs[2])},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)),
                          "kind": "reference", "sample": s["sample"]},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -958,10 +1079,13 @@ def main() -> None:
     parser.add_argument("--tokens", type=int, default=64)
     parser.add_argument("--seed", type=int, default=20)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--cpu-sample-tokens", type=int, default=4)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-parity", action="store_true",
+                        help="skip the parity leg (the oracle on each timed batch, after its timing)")
     parser.add_argument("--cpu-prefill-experts", type=int, default=4,
                         help="experts of the config-3 batch whose rows are timed through the reference's CPU kernel")
+    parser.add_argument("--cpu-prefill-full", type=int, default=2048,
+                        help="config-3 batch also timed whole through the reference's CPU flow (0: none)")
     parser.add_argument("--cpu-q4-tokens", type=int, default=4,
                         help="tokens of the config-4 batch timed through the reference's CPU token loop")
     parser.add_argument("--sweep", default="1,4,16,64",

@@ -123,7 +123,8 @@ int moe_fp8_e4m3_block_mlp_many_pair_weighted_f32(const uint64_t* gate_weight_pt
  * activations) is a static device array of MOE_B200_NOALLOC_SCRATCH_BYTES
  * (4 MiB) that every GPU loading the library holds until exit.  Calls needing
  * more (roughly batch * intermediate_rows * 4 bytes plus a few KiB) return -3
- * with a message.  All calls share the array, so calls that overlap on the GPU
+ * with a message, checked before any size product is formed; dimensions
+ * beyond int32 are unsupported.  All calls share the array, so calls that overlap on the GPU
  * (different streams or devices' threads racing on one device) race; serialise
  * them.  The first call on a device looks the array's address up and should
  * come before any stream capture.  Same arguments and results as
@@ -378,7 +379,10 @@ int moe_ep_combine(const float* y, const int32_t* entry_pos, const float* pos_we
  *   local buffer (or moe_ep_experts_fp8 then moe_ep_return_p2p): each output
  *   row is written into row e of its source rank's return buffer, e = the
  *   entry t * top_k + slot -> barrier -> moe_ep_combine with entry_pos =
- *   identity.  src = rank * src_stride + e; src_stride > every return row
+ *   identity.  The dispatch checks each row's destination rank and receive
+ *   slot (counts that disagree with the rows sent would place a row outside
+ *   the buffer): such a row is not stored and code 64 is set in
+ *   moe_b200_device_error.  src = rank * src_stride + e; src_stride > every return row
  *   (tokens * top_k, or tokens * (top_k + 1) when the rank's own shared-expert
  *   rows go through the same call with e = tokens * top_k + t); capacity >=
  *   the rows any rank receives (world * tokens * top_k suffices).  The
@@ -391,8 +395,14 @@ int moe_ep_dispatch_p2p(const int64_t* ids, const uint16_t* hidden_bf16, int64_t
                         int64_t capacity, int64_t src_stride, const uint64_t* peer_rows, const uint64_t* peer_expert,
                         const uint64_t* peer_src, void* workspace, int64_t workspace_bytes, void* stream);
 int64_t moe_ep_dispatch_p2p_workspace_bytes(int64_t tokens, int64_t top_k, int64_t world);
+/* Received row j with recv_expert[j] >= 0 goes to row recv_src[j] % src_stride
+ * of rank recv_src[j] / src_stride's return buffer.  Every src code is checked
+ * before the store: a rank outside [0, world) or a row at or past home_rows
+ * (the rows of each rank's return buffer, <= src_stride) is skipped and sets
+ * code 64 in moe_b200_device_error. */
 int moe_ep_return_p2p(const float* y, int64_t rows, const int32_t* recv_expert, const int32_t* recv_src,
-                      int64_t hidden_dim, int64_t src_stride, const uint64_t* peer_yback, void* stream);
+                      int64_t hidden_dim, int64_t src_stride, int64_t world, int64_t home_rows,
+                      const uint64_t* peer_yback, void* stream);
 /* moe_ep_experts_fp8 and moe_ep_return_p2p in one call: received row j's fp32
  * output goes straight to row (row_src[j] % src_stride) of the return buffer
  * of rank row_src[j] / src_stride (peer_yback [world], as above), stored over
@@ -403,12 +413,15 @@ int moe_ep_return_p2p(const float* y, int64_t rows, const int32_t* recv_expert, 
  * it only picks the kernel -- the GEMM for tiled weights and >= 512 rows, >= 16
  * per local expert -- and the workspace, so any value gives the same result.
  * The caller may route its own tokens' shared-expert rows through the same
- * call (src = rank * src_stride + their return row).  hidden % 4 == 0. */
+ * call (src = rank * src_stride + their return row).  hidden % 4 == 0.
+ * The src codes are checked as in moe_ep_return_p2p (world, home_rows): a row
+ * whose home is out of range is computed into this rank's own workspace and
+ * never sent, and sets code 64 in moe_b200_device_error. */
 int moe_ep_experts_return_p2p(const uint16_t* rows_bf16, const int32_t* row_expert, const int32_t* row_src,
                               int64_t rows, int64_t valid_rows, int64_t hidden_dim, int64_t intermediate,
                               const uint64_t* tables, int64_t num_local, const uint8_t* nan_free, int weight_layout,
-                              int64_t src_stride, const uint64_t* peer_yback, void* workspace,
-                              int64_t workspace_bytes, void* stream);
+                              int64_t src_stride, int64_t world, int64_t home_rows, const uint64_t* peer_yback,
+                              void* workspace, int64_t workspace_bytes, void* stream);
 int64_t moe_ep_experts_return_p2p_workspace_bytes(int64_t rows, int64_t valid_rows, int64_t hidden_dim,
                                                   int64_t intermediate, int64_t num_local, int weight_layout);
 
@@ -484,7 +497,9 @@ int moe_read_spans(const char* path, int64_t n, const uint64_t* offsets, const u
 /* Device error word (no reference counterpart): nonzero when a bounded wait
  * inside a kernel gave up (1: producer, 2: consumer, 4: drain, 8: misaligned
  * weights refused by the streaming kernel, 16: warp-MMA ring, 32: prefill
- * tensor-core GEMM pipeline).  Synchronises
+ * tensor-core GEMM pipeline), or when an expert-parallel peer kernel skipped
+ * a store whose rank, slot or row read from exchanged data was out of range
+ * (64).  Synchronises
  * `stream`, returns the word (-1 if it cannot be read) and clears it. */
 int moe_b200_device_error(void* stream);
 

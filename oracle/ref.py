@@ -11,6 +11,7 @@ src/pcketlm/native/__init__.py.
 from __future__ import annotations
 
 import ctypes
+import json
 import os
 import subprocess
 from pathlib import Path
@@ -20,8 +21,27 @@ import torch
 from .kernels import _I64, _INT, _P, _Tables, _check, _f32, _ptr, _rows, _u8
 
 REF_DIR = Path(__file__).resolve().parent / "_ref"
-REFERENCE_SOURCES = Path("/root/reference/src/pcketlm/native")
 _LIBS: dict[str, ctypes.CDLL] = {}
+
+
+def reference_root() -> Path | None:
+    """The reference checkout: $PCKETLM_REFERENCE_ROOT, else BASELINE.json's
+    `reference_path`; None when neither names an existing directory (a
+    machine without the reference tree)."""
+    text = os.environ.get("PCKETLM_REFERENCE_ROOT", "").strip()
+    if not text:
+        baseline = REF_DIR.parent.parent / "BASELINE.json"
+        try:
+            text = str(json.loads(baseline.read_text()).get("reference_path") or "")
+        except (OSError, ValueError):
+            text = ""
+    return Path(text) if text and Path(text).is_dir() else None
+
+
+def reference_sources() -> Path | None:
+    root = reference_root()
+    src = None if root is None else root / "src" / "pcketlm" / "native"
+    return src if src is not None and src.is_dir() else None
 
 
 def build() -> bool:
@@ -31,8 +51,9 @@ def build() -> bool:
     machine without the reference tree (the GPU box) the prebuilt files that
     travelled with the repository are used as they are.
     """
-    if REFERENCE_SOURCES.is_dir():
-        subprocess.run(["make", "-s", "-C", str(REF_DIR.parent), "ref"], check=True)
+    src = reference_sources()
+    if src is not None:
+        subprocess.run(["make", "-s", "-C", str(REF_DIR.parent), "ref", f"REF={src}"], check=True)
     return available()
 
 

@@ -22,6 +22,25 @@ using namespace moe;
 
 namespace {
 
+// Error word of the expert-parallel peer kernels (moe_b200_device_error code
+// 64): a destination rank, receive slot or return row read from exchanged
+// data that lies outside the buffers it indexes.  The access is skipped.
+constexpr int kEpRangeError = 64;
+__device__ int g_ep_error = 0;
+
+int read_and_clear_ep_error(cudaStream_t stream) {
+  int host = 0;
+  if (cudaMemcpyFromSymbolAsync(&host, g_ep_error, sizeof(int), 0, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return -1;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return -1;
+  if (host) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbolAsync(g_ep_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess)
+      return -1;
+  }
+  return host;
+}
 
 // Optional stage timing of the fused layer (moe_b200_stage_timing): CUDA events
 // recorded on the launching stream between the layer's kernels.
@@ -348,9 +367,18 @@ __global__ void ep_p2p_scatter_kernel(const uint16_t* hidden, const int64_t* ids
     const int32_t e = pos_entry[p];
     if (e < 0) continue;
     const int q = keys[e];
+    if (q < 0 || q >= world || e >= n) {  // a destination rank or entry outside this step
+      if (lane == 0) atomicOr(&g_ep_error, kEpRangeError);
+      continue;
+    }
     int64_t slot = p - send_offset[q];
     for (int r = 0; r < rank; ++r) slot += count_matrix[r * world + q];
-    if (slot >= capacity) continue;  // cannot happen with capacity >= the entries all ranks send to q
+    // counts exchanged by the all-gather place every row inside the receive buffer; a slot
+    // outside it (counts that disagree with the rows sent) is recorded, never stored
+    if (slot < 0 || slot >= capacity) {
+      if (lane == 0) atomicOr(&g_ep_error, kEpRangeError);
+      continue;
+    }
     const uint16_t* src = hidden + static_cast<int64_t>(pos_token[p]) * H;
     uint16_t* dst = reinterpret_cast<uint16_t*>(peer_rows[q]) + slot * H;
     if (vec) {
@@ -371,13 +399,19 @@ __global__ void ep_p2p_scatter_kernel(const uint16_t* hidden, const int64_t* ids
 // e of rank r (src = r * src_stride + e); its fp32 output row goes to row e
 // of rank r's return buffer.  One warp per row.
 __global__ void ep_p2p_return_kernel(const float* y, int64_t rows, const int32_t* recv_expert, const int32_t* recv_src,
-                                     int64_t H, int64_t src_stride, const uint64_t* peer_yback, int vec) {
+                                     int64_t H, int64_t src_stride, int world, int64_t home_rows,
+                                     const uint64_t* peer_yback, int vec) {
   const int lane = threadIdx.x % 32;
   for (int64_t j = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) / 32; j < rows;
        j += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
     if (recv_expert[j] < 0) continue;
     const int32_t s = recv_src[j];
     const int64_t r = s / src_stride, e = s % src_stride;
+    // src codes are written by the peers' dispatch: check them before storing into a peer's memory
+    if (s < 0 || r >= world || e >= home_rows) {
+      if (lane == 0) atomicOr(&g_ep_error, kEpRangeError);
+      continue;
+    }
     const float* src = y + j * H;
     float* dst = reinterpret_cast<float*>(peer_yback[r]) + e * H;
     if (vec) {
@@ -393,14 +427,24 @@ __global__ void ep_p2p_return_kernel(const float* y, int64_t rows, const int32_t
 // Home rows of the received rows' outputs: pair p (received row j =
 // pair_entry[p], sent by rank r as its entry e: row_src[j] = r * src_stride +
 // e) -> row e of rank r's return buffer.
+// A src code outside [0, world * src_stride) or a row at or past home_rows is
+// recorded in the error word and its pair is sent to `sink` (one row of this
+// rank's own workspace) instead: the stores that follow -- the down GEMM's
+// epilogue or ep_pairs_home_kernel -- then never leave this GPU for it.
 __global__ void ep_pair_home_kernel(const int32_t* pair_entry, const int32_t* n_pairs, const int32_t* row_src,
-                                    int64_t src_stride, const uint64_t* peer_yback, int64_t H, uint64_t* pair_dst,
-                                    int64_t cap) {
+                                    int64_t src_stride, int world, int64_t home_rows, const uint64_t* peer_yback,
+                                    int64_t H, uint64_t* pair_dst, int64_t cap, float* sink) {
   const int64_t n = min(static_cast<int64_t>(*n_pairs), cap);
   for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < n;
        p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int32_t s = row_src[pair_entry[p]];
+    const int32_t j = pair_entry[p];
+    const int32_t s = (j >= 0 && j < cap) ? row_src[j] : -1;
     const int64_t r = s / src_stride, e = s % src_stride;
+    if (s < 0 || r >= world || e >= home_rows) {
+      atomicOr(&g_ep_error, kEpRangeError);
+      pair_dst[p] = reinterpret_cast<uint64_t>(sink);
+      continue;
+    }
     pair_dst[p] = peer_yback[r] + static_cast<uint64_t>(e * H) * sizeof(float);
   }
 }
@@ -497,7 +541,10 @@ static int check_mlp_dims(int64_t E, int64_t B, int64_t I, int64_t H, int64_t gs
   if (gsc != ceil_div(H, kBlock) || dsc != ceil_div(I, kBlock))
     return fail(kBadDims, "scale columns do not match the 128x128 block layout");
   if (E > kMaxBuckets) return fail(kUnsupported, "too many experts in one call");
+  if (B > INT32_MAX || I > INT32_MAX || H > INT32_MAX) return fail(kUnsupported, "dimension beyond int32");
   if (E * B > (int64_t(1) << 30)) return fail(kUnsupported, "too many (expert, row) pairs");
+  // keeps every workspace size (pairs x max(I, H) x 4 bytes and the like) far from int64 overflow
+  if (E * B * std::max(I, H) > (int64_t(1) << 50)) return fail(kUnsupported, "problem too large");
   return kOk;
 }
 
@@ -1066,6 +1113,7 @@ int moe_ep_dispatch_p2p(const int64_t* ids, const uint16_t* hidden_bf16, int64_t
       rank < 0 || rank >= world || capacity <= 0 || src_stride < tokens * top_k)
     return fail(kBadDims, "bad dimensions");
   if (world > kMaxBuckets) return fail(kUnsupported, "world too large");
+  if (world * src_stride > INT32_MAX) return fail(kUnsupported, "world * src_stride must fit in int32 src codes");
   const int64_t n = tokens * top_k;
   cudaStream_t s = as_stream(stream);
   Plan sizing;
@@ -1111,12 +1159,15 @@ int64_t moe_ep_dispatch_p2p_workspace_bytes(int64_t tokens, int64_t top_k, int64
 }
 
 int moe_ep_return_p2p(const float* y, int64_t rows, const int32_t* recv_expert, const int32_t* recv_src,
-                      int64_t hidden_dim, int64_t src_stride, const uint64_t* peer_yback, void* stream) {
+                      int64_t hidden_dim, int64_t src_stride, int64_t world, int64_t home_rows,
+                      const uint64_t* peer_yback, void* stream) {
   if (!y || !recv_expert || !recv_src || !peer_yback) return fail(kNullPointer, "null pointer");
-  if (rows <= 0 || hidden_dim <= 0 || src_stride <= 0) return fail(kBadDims, "bad dimensions");
+  if (rows <= 0 || hidden_dim <= 0 || src_stride <= 0 || world <= 0 || world > kMaxBuckets || home_rows <= 0 ||
+      home_rows > src_stride)
+    return fail(kBadDims, "bad dimensions");
   const int vec = hidden_dim % 4 == 0 && aligned16(y) ? 1 : 0;
-  ep_p2p_return_kernel<<<grid_for(rows * 32, 256), 256, 0, as_stream(stream)>>>(y, rows, recv_expert, recv_src,
-                                                                              hidden_dim, src_stride, peer_yback, vec);
+  ep_p2p_return_kernel<<<grid_for(rows * 32, 256), 256, 0, as_stream(stream)>>>(
+      y, rows, recv_expert, recv_src, hidden_dim, src_stride, static_cast<int>(world), home_rows, peer_yback, vec);
   MOE_CUDA(cudaGetLastError(), "return to peers");
   return kOk;
 }
@@ -1134,6 +1185,8 @@ int64_t moe_ep_experts_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t
 struct EpHome {
   const int32_t* row_src;
   int64_t src_stride;
+  int world;
+  int64_t home_rows;  // rows of every rank's return buffer
   const uint64_t* peer_yback;
 };
 
@@ -1148,11 +1201,13 @@ static bool ep_use_gemm(int weight_layout, int64_t R, int64_t valid, int64_t H, 
 }
 
 static void plan_ep_experts(Plan& p, int64_t R, int64_t H, int64_t I, int64_t S, bool home, bool gemm, LayerPlan* l,
-                            uint64_t** pair_dst) {
+                            uint64_t** pair_dst, float** sink) {
   LayerPlan lp = plan_layer(p, R, H, I, S, 1, 0, 8, false, home && gemm);
   uint64_t* pd = home ? p.take<uint64_t>(R) : nullptr;
+  float* sk = home ? p.take<float>(H) : nullptr;  // where a row with a bad home goes
   if (l) *l = lp;
   if (pair_dst) *pair_dst = pd;
+  if (sink) *sink = sk;
 }
 
 static int ep_experts(const uint16_t* rows_bf16, const int32_t* row_expert, int64_t rows, int64_t valid_rows,
@@ -1173,13 +1228,14 @@ static int ep_experts(const uint16_t* rows_bf16, const int32_t* row_expert, int6
   cudaStream_t s = as_stream(stream);
   const bool gemm = ep_use_gemm(weight_layout, R, valid_rows, H, I, S);
   Plan sizing;
-  plan_ep_experts(sizing, R, H, I, S, home != nullptr, gemm, nullptr, nullptr);
+  plan_ep_experts(sizing, R, H, I, S, home != nullptr, gemm, nullptr, nullptr, nullptr);
   Scratch scratch(workspace, workspace_bytes, sizing.used(), s);
   if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
   Plan plan(scratch.base());
   LayerPlan l{};
   uint64_t* pair_dst = nullptr;
-  plan_ep_experts(plan, R, H, I, S, home != nullptr, gemm, &l, &pair_dst);
+  float* sink = nullptr;
+  plan_ep_experts(plan, R, H, I, S, home != nullptr, gemm, &l, &pair_dst, &sink);
   BucketArgs ba{};
   ba.keys = row_expert; ba.rows = nullptr; ba.weights = nullptr; ba.n = static_cast<int>(R); ba.k = 1;
   ba.key_lo = 0; ba.n_buckets = static_cast<int>(S); ba.bucket_offset = l.m.seg_offset; ba.pair_row = l.m.pair_row;
@@ -1189,7 +1245,8 @@ static int ep_experts(const uint16_t* rows_bf16, const int32_t* row_expert, int6
   const int32_t* n_pairs = l.m.seg_offset + S;  // rows routed to a local expert
   if (home) {
     ep_pair_home_kernel<<<grid_for(R), 256, 0, s>>>(l.m.pair_entry, n_pairs, home->row_src, home->src_stride,
-                                                    home->peer_yback, H, pair_dst, R);
+                                                    home->world, home->home_rows, home->peer_yback, H, pair_dst, R,
+                                                    sink);
     MOE_CUDA(cudaGetLastError(), "home rows");
   }
   Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
@@ -1226,18 +1283,21 @@ int64_t moe_ep_experts_return_p2p_workspace_bytes(int64_t rows, int64_t valid_ro
   if (rows <= 0 || hidden_dim <= 0 || intermediate <= 0 || num_local <= 0) return -1;
   Plan p;
   plan_ep_experts(p, rows, hidden_dim, intermediate, num_local, true,
-                  ep_use_gemm(weight_layout, rows, valid_rows, hidden_dim, intermediate, num_local), nullptr, nullptr);
+                  ep_use_gemm(weight_layout, rows, valid_rows, hidden_dim, intermediate, num_local), nullptr, nullptr,
+                  nullptr);
   return static_cast<int64_t>(p.used());
 }
 
 int moe_ep_experts_return_p2p(const uint16_t* rows_bf16, const int32_t* row_expert, const int32_t* row_src,
                               int64_t rows, int64_t valid_rows, int64_t hidden_dim, int64_t intermediate, const uint64_t* tables,
                               int64_t num_local, const uint8_t* nan_free, int weight_layout, int64_t src_stride,
-                              const uint64_t* peer_yback, void* workspace, int64_t workspace_bytes, void* stream) {
+                              int64_t world, int64_t home_rows, const uint64_t* peer_yback, void* workspace,
+                              int64_t workspace_bytes, void* stream) {
   if (!row_src || !peer_yback) return fail(kNullPointer, "null pointer");
-  if (src_stride <= 0) return fail(kBadDims, "bad dimensions");
+  if (src_stride <= 0 || world <= 0 || world > kMaxBuckets || home_rows <= 0 || home_rows > src_stride)
+    return fail(kBadDims, "bad dimensions");
   if (hidden_dim % 4 != 0) return fail(kUnsupported, "hidden size must be a multiple of 4");
-  const EpHome home{row_src, src_stride, peer_yback};
+  const EpHome home{row_src, src_stride, static_cast<int>(world), home_rows, peer_yback};
   return ep_experts(rows_bf16, row_expert, rows, valid_rows, hidden_dim, intermediate, tables, num_local, nan_free,
                     weight_layout, nullptr, &home, workspace, workspace_bytes, stream);
 }
@@ -1304,7 +1364,8 @@ int moe_b200_device_error(void* stream) {
   const int a = read_and_clear_device_error(as_stream(stream));
   const int b = read_and_clear_mma_device_error(as_stream(stream));
   const int c = read_and_clear_prefill_device_error(as_stream(stream));
-  return (a < 0 || b < 0 || c < 0) ? -1 : (a | b | c);
+  const int d = read_and_clear_ep_error(as_stream(stream));
+  return (a < 0 || b < 0 || c < 0 || d < 0) ? -1 : (a | b | c | d);
 }
 
 int moe_b200_stage_times(float* ms, int max_n) {

@@ -104,6 +104,17 @@ extern "C" int moe_fp8_e4m3_block_mlp_f32_noalloc(const uint8_t* gate_weight, co
   if (batch <= 0 || I <= 0 || H <= 0 || gsc <= 0 || dsc <= 0) return fail(kBadDims, "bad dimensions");
   if (gsc != ceil_div(H, kBlock) || dsc != ceil_div(I, kBlock))
     return fail(kBadDims, "scale columns do not match the 128x128 block layout");
+  // sizes checked before any product is formed: the kernels take int dimensions, and the activations
+  // (batch x I fp32) alone must fit the static scratch
+  if (I > INT32_MAX || H > INT32_MAX) return fail(kUnsupported, "no-alloc MLP: dimension beyond int32");
+  if (batch > static_cast<int64_t>(kNoAllocBytes / sizeof(float)) / I) {
+    static thread_local char msg[256];
+    std::snprintf(msg, sizeof msg,
+                  "no-alloc MLP needs more than %zu bytes of scratch for batch=%lld intermediate=%lld; the static "
+                  "limit is %zu bytes (MOE_B200_NOALLOC_SCRATCH_BYTES)",
+                  kNoAllocBytes, static_cast<long long>(batch), static_cast<long long>(I), kNoAllocBytes);
+    return fail(kNoMemory, msg);
+  }
   int nt = batch <= 1 ? 1 : (batch <= 4 ? 4 : 8);
   const int cap = std::min(gemv_chunk_tokens(static_cast<int>(H), kXF32), gemv_chunk_tokens(static_cast<int>(I), kXF32));
   if (cap <= 0) return fail(kUnsupported, "hidden/intermediate size too large for the staged GEMV");

@@ -102,10 +102,12 @@ class CudaEPOps:
         return out
 
     def experts_home(self, rows: torch.Tensor, row_expert: torch.Tensor, row_src: torch.Tensor, src_stride: int,
-                     peer_yback: torch.Tensor, valid_rows: int = 0) -> None:
+                     peer_yback: torch.Tensor, valid_rows: int = 0, home_rows: int | None = None) -> None:
         """experts() with each output row written into its source rank's
         return buffer (moe_ep_experts_return_p2p); valid_rows: the rows
-        expected to carry a local expert (picks the kernel; 0 = all)."""
+        expected to carry a local expert (picks the kernel; 0 = all);
+        home_rows: the rows of every rank's return buffer (default
+        src_stride) -- a src code pointing outside them is not stored."""
         L = self.layer
         R = int(rows.shape[0])
         layout = 1 if L.tables_tiled is not None and self.lib.moe_b200_selected_gemv() == 0 else 0
@@ -115,7 +117,8 @@ class CudaEPOps:
         code = self.lib.moe_ep_experts_return_p2p(
             native._ptr(rows), native._ptr(row_expert), native._ptr(row_src), R, valid_rows, L.cfg.hidden,
             L.cfg.inter,
-            native._ptr(tables), L.n_local + 1, native._ptr(L.nan_free), layout, src_stride, native._ptr(peer_yback),
+            native._ptr(tables), L.n_local + 1, native._ptr(L.nan_free), layout, src_stride, L.world,
+            src_stride if home_rows is None else int(home_rows), native._ptr(peer_yback),
             native._ptr(ws), ws.numel(), native._stream())
         native._check(code, "moe_ep_experts_return_p2p")
 

@@ -132,9 +132,9 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_ep_dispatch_p2p": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _P, _P, _I64, _P],
                             _INT),
     "moe_ep_dispatch_p2p_workspace_bytes": ([_I64, _I64, _I64], _I64),
-    "moe_ep_return_p2p": ([_P, _I64, _P, _P, _I64, _I64, _P, _P], _INT),
-    "moe_ep_experts_return_p2p": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _INT, _I64, _P, _P, _I64,
-                                   _P], _INT),
+    "moe_ep_return_p2p": ([_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _P], _INT),
+    "moe_ep_experts_return_p2p": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _INT, _I64, _I64, _I64, _P,
+                                   _P, _I64, _P], _INT),
     "moe_ep_experts_return_p2p_workspace_bytes": ([_I64] * 5 + [_INT], _I64),
     "moe_b200_stage_timing": ([_INT], _INT),
     "moe_b200_stage_times": ([_P, _INT], _INT),
@@ -873,56 +873,82 @@ def q4_moe_selected_forward_u16(hidden: torch.Tensor, experts: list, route_weigh
 # ---------------------------------------------------------------------------
 # row8 packed GEMV (native/__init__.py:1658-1668, 2108-2223)
 # ---------------------------------------------------------------------------
-from collections import OrderedDict  # noqa: E402
+_U16_STORAGE_CODES = {torch.float16: 0, torch.bfloat16: 1}
 
-_PACKED_GEMV_CACHE: "OrderedDict[str, torch.Tensor]" = OrderedDict()
-_PACKED_GEMV_CACHE_BYTES = 0
-_PACKED_GEMV_CACHE_STATS = {"hits": 0, "misses": 0, "stores": 0, "evictions": 0}
+
+class _Row8PackCache:
+    """Device-resident row8 packs keyed by the caller's cache key, bounded
+    by PCKETLM_PACKED_GEMV_CACHE_MB (unset, unparsable or <= 0: no caching;
+    PCKETLM_DISABLE_PACKED_GEMV_CACHE: no caching).  The least recently used
+    packs leave first when a new pack would exceed the budget; a pack larger
+    than the whole budget is returned without being kept.  The statistics
+    keys are the ones the reference's callers read
+    (native/__init__.py:2110-2193)."""
+
+    def __init__(self) -> None:
+        self._packs: dict[str, tuple[torch.Tensor, int, int]] = {}  # key -> (pack, bytes, last use)
+        self._clock = 0
+        self._bytes = 0
+        self.counts = dict.fromkeys(("hits", "misses", "stores", "evictions"), 0)
+
+    @staticmethod
+    def budget() -> int:
+        try:
+            return max(0, int(os.environ.get("PCKETLM_PACKED_GEMV_CACHE_MB", ""))) << 20
+        except ValueError:
+            return 0
+
+    def clear(self) -> None:
+        self._packs.clear()
+        self._bytes = 0
+        self.counts = dict.fromkeys(self.counts, 0)
+
+    def stats(self) -> dict[str, int | float]:
+        return {**self.counts, "resident_count": len(self._packs), "resident_bytes": self._bytes,
+                "resident_mb": round(self._bytes / (1 << 20), 4), "budget_bytes": self.budget()}
+
+    def get(self, key: str, weight: torch.Tensor) -> torch.Tensor:
+        self._clock += 1
+        limit = 0 if _flag("PCKETLM_DISABLE_PACKED_GEMV_CACHE") else self.budget()
+        entry = self._packs.get(key) if limit else None
+        if entry is not None:
+            self.counts["hits"] += 1
+            self._packs[key] = (entry[0], entry[1], self._clock)
+            return entry[0]
+        self.counts["misses"] += 1
+        packed = pack_weight_rows8(weight)
+        size = packed.numel() * packed.element_size()
+        if not limit or size > limit:
+            return packed
+        while self._packs and self._bytes + size > limit:
+            stalest = min(self._packs, key=lambda k: self._packs[k][2])
+            self._bytes -= self._packs.pop(stalest)[1]
+            self.counts["evictions"] += 1
+        self._packs[key] = (packed, size, self._clock)
+        self._bytes += size
+        self.counts["stores"] += 1
+        return packed
+
+
+_ROW8_CACHE = _Row8PackCache()
 
 
 def native_fp16_packed_gemv_available() -> bool:
     return not _native_packed_gemv_disabled() and _lib_or_none() is not None and torch.cuda.is_available()
 
 
-def _packed_gemv_cache_disabled() -> bool:
-    return _flag("PCKETLM_DISABLE_PACKED_GEMV_CACHE")
-
-
-def _packed_gemv_cache_budget_bytes() -> int:
-    raw = os.environ.get("PCKETLM_PACKED_GEMV_CACHE_MB", "").strip()
-    if not raw:
-        return 0
-    try:
-        mb = int(raw)
-    except ValueError:
-        return 0
-    return max(0, mb) * 1024 * 1024
-
-
 def reset_packed_gemv_cache() -> None:
-    global _PACKED_GEMV_CACHE_BYTES
-    _PACKED_GEMV_CACHE.clear()
-    _PACKED_GEMV_CACHE_BYTES = 0
-    for key in _PACKED_GEMV_CACHE_STATS:
-        _PACKED_GEMV_CACHE_STATS[key] = 0
+    _ROW8_CACHE.clear()
 
 
 def packed_gemv_cache_stats() -> dict[str, int | float]:
-    return {
-        **_PACKED_GEMV_CACHE_STATS,
-        "resident_count": len(_PACKED_GEMV_CACHE),
-        "resident_bytes": _PACKED_GEMV_CACHE_BYTES,
-        "resident_mb": round(_PACKED_GEMV_CACHE_BYTES / 1024 / 1024, 4),
-        "budget_bytes": _packed_gemv_cache_budget_bytes(),
-    }
+    return _ROW8_CACHE.stats()
 
 
 def _u16_storage_dtype_code(dtype: torch.dtype) -> int:
-    if dtype == torch.float16:
-        return 0
-    if dtype == torch.bfloat16:
-        return 1
-    raise TypeError("native KV kernels require torch.float16 or torch.bfloat16 tensors")
+    if dtype not in _U16_STORAGE_CODES:
+        raise TypeError("native KV kernels require torch.float16 or torch.bfloat16 tensors")
+    return _U16_STORAGE_CODES[dtype]
 
 
 def pack_weight_rows8(weight: torch.Tensor) -> torch.Tensor:
@@ -943,33 +969,8 @@ def pack_weight_rows8(weight: torch.Tensor) -> torch.Tensor:
 
 
 def cached_pack_weight_rows8(cache_key: str, weight: torch.Tensor) -> torch.Tensor:
-    global _PACKED_GEMV_CACHE_BYTES
-    if _packed_gemv_cache_disabled():
-        _PACKED_GEMV_CACHE_STATS["misses"] += 1
-        return pack_weight_rows8(weight)
-    budget = _packed_gemv_cache_budget_bytes()
-    if budget <= 0:
-        _PACKED_GEMV_CACHE_STATS["misses"] += 1
-        return pack_weight_rows8(weight)
-    key = str(cache_key)
-    cached = _PACKED_GEMV_CACHE.get(key)
-    if cached is not None:
-        _PACKED_GEMV_CACHE.move_to_end(key)
-        _PACKED_GEMV_CACHE_STATS["hits"] += 1
-        return cached
-    _PACKED_GEMV_CACHE_STATS["misses"] += 1
-    packed = pack_weight_rows8(weight)
-    packed_bytes = int(packed.numel() * packed.element_size())
-    if packed_bytes > budget:
-        return packed
-    while _PACKED_GEMV_CACHE and _PACKED_GEMV_CACHE_BYTES + packed_bytes > budget:
-        _old, old_value = _PACKED_GEMV_CACHE.popitem(last=False)
-        _PACKED_GEMV_CACHE_BYTES -= int(old_value.numel() * old_value.element_size())
-        _PACKED_GEMV_CACHE_STATS["evictions"] += 1
-    _PACKED_GEMV_CACHE[key] = packed
-    _PACKED_GEMV_CACHE_BYTES += packed_bytes
-    _PACKED_GEMV_CACHE_STATS["stores"] += 1
-    return packed
+    """pack_weight_rows8 through the process-wide LRU of device packs."""
+    return _ROW8_CACHE.get(str(cache_key), weight)
 
 
 def packed_gemv_rows8(hidden: torch.Tensor, packed_weight: torch.Tensor, *, rows: int, cols: int) -> torch.Tensor:

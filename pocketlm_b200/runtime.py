@@ -1,12 +1,16 @@
 """Layer-level entry points: the GPU counterparts of run_fp8_router and
 run_fp8_moe (src/pcketlm/core/runtime/fp8_source.py:1500-1884).
 
-The reference resolves a layer's tensors through its model catalog
-(model_id, layer_index); here the caller hands in an HBM-resident layer
-(pocketlm_b200.synth.Fp8MoELayer or any object with the same tensors), since
-the catalog / pack loaders are outside this path.  Results carry the fields
-of the reference's FP8RouterResult / FP8MoEResult that describe the
-computation (selected experts, shapes, weight bytes, timings, blockers).
+`run_fp8_router(model_id, layer_index, hidden)` and
+`run_fp8_moe(model_id, layer_index, hidden, *, dtype, router)` keep the
+reference's signatures and result types: the layer is found by model id
+(pocketlm_b200.models: config.json + FP8 pack or safetensors shards) and
+kept resident in HBM, so a caller swaps one import for the other.
+`route_resident_layer` / `moe_resident_layer` take an HBM-resident layer
+object directly (DsMoELayerGPU, or a synth.Fp8MoELayer for the router).
+Results carry the fields of the reference's FP8RouterResult /
+FP8MoEResult; problems finding the layer are reported as blockers with
+ready=False, as the reference does.
 """
 
 from __future__ import annotations
@@ -22,6 +26,7 @@ from .synth import Fp8MoELayer
 
 @dataclass
 class FP8RouterResult:
+    model_id: str
     layer_index: int
     hidden_shape: list[int]
     weights_shape: list[int]
@@ -32,25 +37,54 @@ class FP8RouterResult:
     n_groups: int
     topk_groups: int
     bias_loaded: bool
-    weights_tensor: torch.Tensor | None
-    indices_tensor: torch.Tensor | None
+    weights_tensor: torch.Tensor | None = None
+    indices_tensor: torch.Tensor | None = None
     blockers: list[str] = field(default_factory=list)
     ready: bool = False
+
+    def to_dict(self) -> dict:
+        return {"model_id": self.model_id, "layer_index": self.layer_index, "hidden_shape": list(self.hidden_shape),
+                "weights_shape": list(self.weights_shape), "indices_shape": list(self.indices_shape),
+                "selected_experts": list(self.selected_experts), "scoring_func": self.scoring_func,
+                "route_scale": self.route_scale, "n_groups": self.n_groups, "topk_groups": self.topk_groups,
+                "bias_loaded": self.bias_loaded, "weights_materialized": self.weights_tensor is not None,
+                "indices_materialized": self.indices_tensor is not None, "blockers": list(self.blockers),
+                "ready": self.ready}
 
 
 @dataclass
 class FP8MoEResult:
+    model_id: str
     layer_index: int
     hidden_shape: list[int]
     output_shape: list[int]
     selected_experts: list[int]
     routed_weight_bytes: int
     shared_weight_bytes: int
-    router: FP8RouterResult | None
-    output_tensor: torch.Tensor | None
+    dequantized_weight_bytes: int = 0
+    router: FP8RouterResult | None = None
+    output_tensor: torch.Tensor | None = None
+    router_elapsed_seconds: float = 0.0
+    preload_elapsed_seconds: float = 0.0
+    routed_elapsed_seconds: float = 0.0
+    shared_elapsed_seconds: float = 0.0
     total_elapsed_seconds: float = 0.0
     blockers: list[str] = field(default_factory=list)
     ready: bool = False
+
+    def to_dict(self) -> dict:
+        return {"model_id": self.model_id, "layer_index": self.layer_index, "hidden_shape": list(self.hidden_shape),
+                "output_shape": list(self.output_shape), "selected_experts": list(self.selected_experts),
+                "routed_weight_bytes": self.routed_weight_bytes, "shared_weight_bytes": self.shared_weight_bytes,
+                "dequantized_weight_bytes": self.dequantized_weight_bytes,
+                "router": None if self.router is None else self.router.to_dict(),
+                "output_materialized": self.output_tensor is not None,
+                "router_elapsed_seconds": float(self.router_elapsed_seconds),
+                "preload_elapsed_seconds": float(self.preload_elapsed_seconds),
+                "routed_elapsed_seconds": float(self.routed_elapsed_seconds),
+                "shared_elapsed_seconds": float(self.shared_elapsed_seconds),
+                "total_elapsed_seconds": float(self.total_elapsed_seconds), "blockers": list(self.blockers),
+                "ready": self.ready}
 
 
 class DsMoELayerGPU:
@@ -156,6 +190,54 @@ class DsMoELayerGPU:
         return out
 
 
+    def forward_routed(self, hidden: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, *,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+        """The layer for a routing the caller already has (a router result
+        passed to run_fp8_moe): ids int64 [T, k], weights [T, k] (any float
+        dtype; used as fp32).  Rows are bucketed per expert, the routed
+        experts and the shared expert run as one grouped launch, and the
+        combine adds them in slot order, then the shared expert, rounding
+        once to bf16 -- the fused layer's arithmetic for the same routing."""
+        cfg = self.cfg
+        x = hidden.reshape(-1, cfg.hidden).to(torch.bfloat16).contiguous()
+        T, k, H = int(x.shape[0]), int(ids.shape[-1]), cfg.hidden
+        dev = x.device
+        ids = ids.reshape(T, k).to(device=dev, dtype=torch.int64).contiguous()
+        if T and (int(ids.min()) < 0 or int(ids.max()) >= cfg.n_routed):
+            raise ValueError("router indices must be routed expert ids")
+        w = weights.reshape(T, k).to(device=dev, dtype=torch.float32).contiguous()
+        if out is None:
+            out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        if T == 0:
+            return out
+        lib = native.load_library()
+        n = T * k
+        rows = torch.empty((n + T, H), dtype=torch.bfloat16, device=dev)
+        row_expert = torch.empty((n + T,), dtype=torch.int32, device=dev)
+        offsets = torch.empty((2,), dtype=torch.int32, device=dev)
+        entry_pos = torch.empty((n,), dtype=torch.int32, device=dev)
+        pos_weight = torch.empty((n,), dtype=torch.float32, device=dev)
+        ws = torch.empty((int(lib.moe_ep_dispatch_workspace_bytes(T, k)),), dtype=torch.uint8, device=dev)
+        native._check(lib.moe_ep_dispatch_pack(
+            native._ptr(ids), native._ptr(w), native._ptr(x), T, H, k, cfg.n_routed, 1, native._ptr(rows),
+            native._ptr(row_expert), native._ptr(offsets), native._ptr(entry_pos), native._ptr(pos_weight),
+            native._ptr(ws), ws.numel(), native._stream()), "moe_ep_dispatch_pack")
+        rows[n:].copy_(x)
+        row_expert[n:].fill_(cfg.n_routed)  # the shared expert, last in the tables
+        R, S = n + T, cfg.n_routed + 1
+        y = torch.empty((R, H), dtype=torch.float32, device=dev)
+        layout = 1 if self.tables_tiled is not None and lib.moe_b200_selected_gemv() == 0 else 0
+        tables = self.tables_tiled if layout else self.tables
+        ws = torch.empty((int(lib.moe_ep_experts_workspace_bytes(R, H, cfg.inter, S)),), dtype=torch.uint8,
+                         device=dev)
+        native._check(lib.moe_ep_experts_fp8(
+            native._ptr(rows), native._ptr(row_expert), R, H, cfg.inter, native._ptr(tables), S,
+            native._ptr(self.nan_free), layout, native._ptr(y), native._ptr(ws), ws.numel(), native._stream()),
+            "moe_ep_experts_fp8")
+        native._check(lib.moe_ep_combine(native._ptr(y), native._ptr(entry_pos), native._ptr(pos_weight), T, k, H, 1,
+                                         native._ptr(out), native._stream()), "moe_ep_combine")
+        return out
+
     def capture(self, tokens: int, *, input_dtype: torch.dtype = torch.bfloat16) -> "GraphedDsMoELayer":
         """Record the whole layer (7 kernels) for a fixed token count into a
         CUDA graph; replaying it removes the per-kernel host launch cost,
@@ -200,51 +282,110 @@ class GraphedDsMoELayer:
         return self.replay()
 
 
-def run_fp8_router(layer: Fp8MoELayer | DsMoELayerGPU, hidden: torch.Tensor, layer_index: int = 0) -> FP8RouterResult:
-    """The router of fp8_source.py:1500-1566 on the GPU."""
+def _router_result(model_id: str, layer_index: int, hidden: torch.Tensor, cfg, bias_loaded: bool, ids, weights,
+                   blockers: list[str] | None = None) -> FP8RouterResult:
+    selected = [] if ids is None else sorted({int(v) for v in ids.reshape(-1).tolist()})
+    blockers = list(blockers or [])
+    return FP8RouterResult(
+        model_id=str(model_id), layer_index=int(layer_index), hidden_shape=[int(v) for v in hidden.shape],
+        weights_shape=[] if weights is None else [int(v) for v in weights.shape],
+        indices_shape=[] if ids is None else [int(v) for v in ids.shape], selected_experts=selected,
+        scoring_func=cfg.scoring_func if cfg else "", route_scale=float(cfg.route_scale) if cfg else 0.0,
+        n_groups=int(cfg.n_group) if cfg else 0, topk_groups=int(cfg.topk_group) if cfg else 0,
+        bias_loaded=bool(bias_loaded), weights_tensor=weights, indices_tensor=ids, blockers=blockers,
+        ready=not blockers and ids is not None and weights is not None)
+
+
+def route_resident_layer(layer: Fp8MoELayer | DsMoELayerGPU, hidden: torch.Tensor, layer_index: int | None = None,
+                         *, model_id: str = "") -> FP8RouterResult:
+    """The router of fp8_source.py:1500-1566 on the GPU for a resident layer:
+    ids int64 [T, k] and weights [T, k] in hidden's dtype, on hidden's device."""
     base = layer.layer if isinstance(layer, DsMoELayerGPU) else layer
+    if layer_index is None:
+        layer_index = layer.layer_index if isinstance(layer, DsMoELayerGPU) else 0
     cfg = base.cfg
     ids, weights = native.route_topk(hidden, base.router_weight, base.bias, top_k=cfg.top_k, n_group=cfg.n_group,
                                      topk_group=cfg.topk_group, scoring_func=cfg.scoring_func,
                                      route_scale=cfg.route_scale, round_to_hidden_dtype=True)
-    selected = sorted({int(v) for v in ids.reshape(-1).tolist()})
-    return FP8RouterResult(
-        layer_index=int(layer_index), hidden_shape=[int(v) for v in hidden.shape],
-        weights_shape=[int(v) for v in weights.shape], indices_shape=[int(v) for v in ids.shape],
-        selected_experts=selected, scoring_func=cfg.scoring_func, route_scale=float(cfg.route_scale),
-        n_groups=cfg.n_group, topk_groups=cfg.topk_group, bias_loaded=base.bias is not None,
-        weights_tensor=weights, indices_tensor=ids, blockers=[], ready=True)
+    return _router_result(model_id, layer_index, hidden, cfg, base.bias is not None, ids.to(hidden.device),
+                          weights.to(hidden.device))
 
 
-def run_fp8_moe(layer: DsMoELayerGPU, hidden: torch.Tensor, *, dtype: torch.dtype = torch.bfloat16,
-                layer_index: int | None = None) -> FP8MoEResult:
-    """One MoE layer (routed experts + shared expert) on the GPU, the
-    counterpart of fp8_source.py:1569-1884.  Output in bf16 (the reference's
-    default dtype); fp32 inputs are accepted and rounded once at the end."""
-    if dtype != torch.bfloat16:
-        raise ValueError("the fused GPU layer produces bf16 output")
+def moe_resident_layer(layer: DsMoELayerGPU, hidden: torch.Tensor, *, dtype: torch.dtype = torch.bfloat16,
+                       router: FP8RouterResult | None = None, layer_index: int | None = None,
+                       model_id: str = "") -> FP8MoEResult:
+    """One MoE layer (routed experts + shared expert) on the GPU for a
+    resident layer, the counterpart of fp8_source.py:1569-1884.  Without
+    `router` the fused path routes, dispatches, runs the experts and combines
+    in one launch sequence; with it, its indices and weights are used.  The
+    combine rounds once to bf16; another `dtype` is a cast of that result."""
     start = time.perf_counter()
     cfg = layer.cfg
     dev = layer.layer.device
+    index = int(layer.layer_index if layer_index is None else layer_index)
     flat = hidden.reshape(-1, cfg.hidden)
     x = flat.to(dev).to(torch.bfloat16) if flat.dtype != torch.float32 else flat.to(dev)
     T = int(x.shape[0])
-    ids = torch.empty((T, cfg.top_k), dtype=torch.int64, device=dev)
-    weights = torch.empty((T, cfg.top_k), dtype=torch.bfloat16, device=dev)
-    out = layer.forward(x, ids=ids, weights=weights)
+    if router is not None:
+        if router.indices_tensor is None or router.weights_tensor is None:
+            return FP8MoEResult(
+                model_id=str(model_id), layer_index=index, hidden_shape=[int(v) for v in hidden.shape],
+                output_shape=[], selected_experts=[], routed_weight_bytes=0, shared_weight_bytes=0, router=router,
+                blockers=list(router.blockers) + ["Router did not produce selected experts and route weights."])
+        r0 = time.perf_counter()
+        out = layer.forward_routed(x, router.indices_tensor, router.weights_tensor)
+        router_result, router_s = router, 0.0
+        ids = router.indices_tensor
+    else:
+        ids = torch.empty((T, cfg.top_k), dtype=torch.int64, device=dev)
+        weights = torch.empty((T, cfg.top_k), dtype=torch.bfloat16, device=dev)
+        r0 = time.perf_counter()
+        out = layer.forward(x, ids=ids, weights=weights)
+        router_s = 0.0
+        w_out = weights if hidden.dtype == torch.bfloat16 else weights.to(hidden.dtype)
+        router_result = _router_result(model_id, index, hidden, cfg, layer.layer.bias is not None,
+                                       ids.to(hidden.device), w_out.to(hidden.device))
+    output = out.reshape(hidden.shape).to(device=hidden.device, dtype=dtype)
+    routed_s = time.perf_counter() - r0
     selected = sorted({int(v) for v in ids.reshape(-1).tolist()})
-    router = FP8RouterResult(
-        layer_index=int(layer.layer_index if layer_index is None else layer_index),
-        hidden_shape=[int(v) for v in hidden.shape], weights_shape=[T, cfg.top_k], indices_shape=[T, cfg.top_k],
-        selected_experts=selected, scoring_func=cfg.scoring_func, route_scale=float(cfg.route_scale),
-        n_groups=cfg.n_group, topk_groups=cfg.topk_group, bias_loaded=layer.layer.bias is not None,
-        weights_tensor=weights.to(hidden.device), indices_tensor=ids.to(hidden.device), ready=True)
-    output = out.reshape(hidden.shape).to(hidden.device)
     return FP8MoEResult(
-        layer_index=router.layer_index, hidden_shape=[int(v) for v in hidden.shape],
+        model_id=str(model_id), layer_index=index, hidden_shape=[int(v) for v in hidden.shape],
         output_shape=[int(v) for v in output.shape], selected_experts=selected,
         routed_weight_bytes=len(selected) * cfg.expert_bytes, shared_weight_bytes=cfg.expert_bytes,
-        router=router, output_tensor=output, total_elapsed_seconds=time.perf_counter() - start, ready=True)
+        dequantized_weight_bytes=0, router=router_result, output_tensor=output, router_elapsed_seconds=router_s,
+        routed_elapsed_seconds=routed_s, total_elapsed_seconds=time.perf_counter() - start, ready=True)
+
+
+def run_fp8_router(model_id: str, layer_index: int, hidden: torch.Tensor) -> FP8RouterResult:
+    """DeepSeek-V3 sigmoid (or softmax) group-limited top-k routing for one
+    layer of `model_id` (fp8_source.py:1500-1566), on the GPU."""
+    from . import models
+
+    try:
+        layer = models.resident_layer(model_id, layer_index)
+    except (FileNotFoundError, KeyError, ValueError) as exc:
+        return _router_result(model_id, layer_index, hidden, None, False, None, None, [str(exc)])
+    return route_resident_layer(layer, hidden, layer_index, model_id=model_id)
+
+
+def run_fp8_moe(model_id: str, layer_index: int, hidden: torch.Tensor, *, dtype: torch.dtype = torch.bfloat16,
+                router: FP8RouterResult | None = None) -> FP8MoEResult:
+    """Routed experts plus the shared expert for one MoE layer of `model_id`
+    (fp8_source.py:1569-1884), on the GPU; `router` reuses a routing result."""
+    from . import models
+
+    start = time.perf_counter()
+    try:
+        layer = models.resident_layer(model_id, layer_index)
+    except (FileNotFoundError, KeyError, ValueError) as exc:
+        return FP8MoEResult(model_id=str(model_id), layer_index=int(layer_index),
+                            hidden_shape=[int(v) for v in hidden.shape], output_shape=[], selected_experts=[],
+                            routed_weight_bytes=0, shared_weight_bytes=0, router=router, blockers=[str(exc)])
+    preload = time.perf_counter() - start
+    res = moe_resident_layer(layer, hidden, dtype=dtype, router=router, layer_index=layer_index, model_id=model_id)
+    res.preload_elapsed_seconds = preload
+    res.total_elapsed_seconds = time.perf_counter() - start
+    return res
 
 
 class Q4MoELayerGPU:

@@ -191,10 +191,12 @@ def make_router_bias(cfg: DsMoEConfig, seed: int, device, kind: str = "uniform")
 
 
 def make_fp8_layer(cfg: DsMoEConfig, seed: int = 0, device="cpu", bias_kind: str = "uniform",
-                   experts: list[int] | None = None) -> Fp8MoELayer:
+                   experts: list[int] | None = None, threads: int = 1) -> Fp8MoELayer:
     """Generate a layer.  `experts` (ids; the shared expert is id
     cfg.n_routed) limits which experts are generated and stored: such a
-    partial layer holds only those, in the order given."""
+    partial layer holds only those, in the order given.  `threads` > 1
+    generates CPU experts concurrently (same values: each expert has its
+    own generator)."""
     device = torch.device(device)
     H, I = cfg.hidden, cfg.inter
     ids = list(range(cfg.n_routed + 1)) if experts is None else list(experts)
@@ -206,7 +208,8 @@ def make_fp8_layer(cfg: DsMoEConfig, seed: int = 0, device="cpu", bias_kind: str
     s13 = torch.ones((E1, 2, *cfg.gate_scale_shape), dtype=torch.float32, device=device)
     w2 = torch.zeros((E1, H, I), dtype=torch.uint8, device=device)
     s2 = torch.ones((E1, *cfg.down_scale_shape), dtype=torch.float32, device=device)
-    for slot, e in enumerate(ids):
+
+    def fill(slot: int, e: int) -> None:
         for proj in range(3):
             gen = _generator(device, _expert_seed(seed, e + 1, 2 + proj))
             shape = (H, I) if proj == 2 else (I, H)
@@ -219,6 +222,20 @@ def make_fp8_layer(cfg: DsMoEConfig, seed: int = 0, device="cpu", bias_kind: str
                 w13[slot, proj].copy_(q)
                 s13[slot, proj].copy_(s)
             del w, q, s
+
+    if threads > 1 and device.type == "cpu":
+        from concurrent.futures import ThreadPoolExecutor
+
+        intra = torch.get_num_threads()
+        torch.set_num_threads(1)  # one expert per thread; torch's own threads would oversubscribe the cores
+        try:
+            with ThreadPoolExecutor(max_workers=threads) as pool:
+                list(pool.map(lambda se: fill(*se), enumerate(ids)))
+        finally:
+            torch.set_num_threads(intra)
+    else:
+        for slot, e in enumerate(ids):
+            fill(slot, e)
     slots = None if experts is None else {e: i for i, e in enumerate(ids)}
     return Fp8MoELayer(cfg, router_weight, bias, w13, s13, w2, s2, slots)
 

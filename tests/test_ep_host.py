@@ -35,7 +35,25 @@ def test_workspace_rejects_bad_sizes():
 
 def test_entry_points_check_pointers_before_any_device_work():
     lib = native.load_library()
-    code = lib.moe_ep_experts_return_p2p(None, None, None, 16, 0, H, I, None, 9, None, 1, 16, None, None, 0, None)
+    code = lib.moe_ep_experts_return_p2p(None, None, None, 16, 0, H, I, None, 9, None, 1, 16, 2, 16, None, None, 0,
+                                         None)
     assert code == -1 and b"null" in lib.moe_b200_last_error()
+    code = lib.moe_ep_return_p2p(None, 16, None, None, H, 16, 2, 16, None, None)
+    assert code == -1 and b"null" in lib.moe_b200_last_error()
+
+
+def test_peer_entry_points_check_world_and_return_rows():
+    """The return buffer's rows must lie within src_stride and the world in
+    range; both are checked on the host before anything is launched."""
+    import ctypes
+
+    lib = native.load_library()
+    fake = ctypes.c_void_p(16)  # never dereferenced: the calls return before any launch
+    for world, home_rows in ((0, 16), (2, 0), (2, 17), (4096, 16)):
+        code = lib.moe_ep_return_p2p(fake, 16, fake, fake, H, 16, world, home_rows, fake, None)
+        assert code == -2, (world, home_rows)
+        code = lib.moe_ep_experts_return_p2p(fake, fake, fake, 16, 0, H, I, fake, 9, fake, 1, 16, world, home_rows,
+                                             fake, None, 0, None)
+        assert code == -2, (world, home_rows)
     code = lib.moe_ep_experts_fp8(None, None, 16, H, I, None, 9, None, 1, None, None, 0, None)
     assert code == -1 and b"null" in lib.moe_b200_last_error()

@@ -14,7 +14,7 @@ import torch
 import oracle
 from oracle import kernels as orc
 from pocketlm_b200 import native, synth
-from pocketlm_b200.runtime import DsMoELayerGPU, run_fp8_moe, run_fp8_router
+from pocketlm_b200.runtime import DsMoELayerGPU, moe_resident_layer, route_resident_layer
 from tests.parity import COS_GATE, REL_L2_GATE, cos_dist, id_mismatches, rel_l2
 
 pytestmark = pytest.mark.gpu
@@ -104,7 +104,7 @@ def test_tiny_layer_matches_reference_golden(cuda_device, golden_dir):
     cfg = synth.C1_TINY
     layer = synth.make_fp8_layer(cfg, seed=g["seed"]).to("cuda")
     x = synth.make_hidden(g["tokens"], cfg.hidden, seed=g["seed"]).to("cuda")
-    res = run_fp8_moe(DsMoELayerGPU(layer), x)
+    res = moe_resident_layer(DsMoELayerGPU(layer), x)
     assert res.ready
     assert torch.equal(torch.sort(res.router.indices_tensor.cpu(), 1).values, torch.sort(g["ids"], 1).values)
     assert rel_l2(res.output_tensor, g["out"]) <= REL_L2_GATE
@@ -180,7 +180,7 @@ def test_dsv3_router_result_api(cuda_device):
     cfg = synth.C2_DSV3
     layer = synth.make_fp8_layer(cfg, seed=5, device="cuda", experts=[])
     x = synth.make_hidden(4, cfg.hidden, seed=5, device="cuda")
-    res = run_fp8_router(layer, x)
+    res = route_resident_layer(layer, x)
     assert res.ready and res.indices_tensor.shape == (4, 8) and res.weights_tensor.dtype == torch.bfloat16
     assert res.scoring_func == "sigmoid" and res.n_groups == 8 and res.topk_groups == 4
     sums = res.weights_tensor.float().sum(dim=1)

@@ -55,7 +55,10 @@ def _close(actual, expected, rel=1e-5):
     assert err <= rel * scale + 1e-6, f"max abs err {err} vs scale {scale}"
 
 
-@pytest.mark.parametrize("hidden,inter,batches", [(1024, 512, (3, 5)), (7168, 2048, (1, 2))])
+# growing and shrinking batches (a smaller call after a larger one runs on the chunk list and activations
+# the larger one left in the shared scratch), and 1000 columns, which are not a multiple of 16 (scalar loads)
+@pytest.mark.parametrize("hidden,inter,batches", [(1024, 512, (3, 5)), (7168, 2048, (1, 2)),
+                                                  (1024, 512, (5, 3, 1)), (1000, 384, (4, 2))])
 def test_noalloc_mlp_matches_allocating_entry_point_twice(cuda_device, hidden, inter, batches):
     lib = native.load_library()
     for call, batch in enumerate(batches):
@@ -66,6 +69,25 @@ def test_noalloc_mlp_matches_allocating_entry_point_twice(cuda_device, hidden, i
         torch.cuda.synchronize()
         assert torch.isfinite(got).all()
         _close(got, want)
+
+
+def test_noalloc_call_takes_no_device_memory(cuda_device):
+    """After a first call (which loads the kernels), further calls change
+    neither the device's free memory nor torch's allocator."""
+    lib = native.load_library()
+    item = _expert(300, 1024, 512)
+    x = torch.randn((4, 1024), generator=torch.Generator().manual_seed(301)).cuda()
+    out = torch.empty((4, 1024), device="cuda")
+    args = [ctypes.c_void_p(t.data_ptr()) for t in item] + [ctypes.c_void_p(x.data_ptr()),
+                                                             ctypes.c_void_p(out.data_ptr())]
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert lib.moe_fp8_e4m3_block_mlp_f32_noalloc(*args, 4, 512, 1024, 8, 4, stream) == 0
+    torch.cuda.synchronize()
+    free0, torch0 = torch.cuda.mem_get_info()[0], torch.cuda.memory_allocated()
+    for _ in range(3):
+        assert lib.moe_fp8_e4m3_block_mlp_f32_noalloc(*args, 4, 512, 1024, 8, 4, stream) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0 and torch.cuda.memory_allocated() == torch0
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(cuda_device):
@@ -80,3 +102,9 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(cuda_device):
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert code == -3
     assert b"static limit" in lib.moe_b200_last_error()
+    # a batch whose activations alone overflow any size product is refused the same way
+    code = lib.moe_fp8_e4m3_block_mlp_f32_noalloc(
+        *[ctypes.c_void_p(t.data_ptr()) for t in item], ctypes.c_void_p(x.data_ptr()),
+        ctypes.c_void_p(out.data_ptr()), 1 << 62, inter, hidden, 2, 16,
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert code == -3
