@@ -203,9 +203,9 @@ class PeerExchange:
         out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
         if T == 0:
             return out, ids, w
-        native._check(lib.moe_ep_combine(native._ptr(self.yback), native._ptr(self.identity),
-                                         native._ptr(w.reshape(-1).contiguous()), T, k, H, 1, native._ptr(out),
-                                         native._stream()), "moe_ep_combine")
+        w_flat = w.reshape(-1).contiguous()  # referenced until the launch (a temporary could be freed first)
+        native._check(lib.moe_ep_combine(native._ptr(self.yback), native._ptr(self.identity), native._ptr(w_flat),
+                                         T, k, H, 1, native._ptr(out), native._stream()), "moe_ep_combine")
         return out, ids, w
 
 

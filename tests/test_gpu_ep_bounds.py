@@ -67,9 +67,11 @@ def test_dispatch_p2p_skips_slots_past_capacity(cuda_device):
     srcs = [torch.full((12,), -5, dtype=torch.int32, device=cuda_device) for _ in range(world)]
     need = int(_lib().moe_ep_dispatch_p2p_workspace_bytes(T, k, world))
     ws = torch.empty((need,), dtype=torch.uint8, device=cuda_device)
+    # the device tables stay referenced until the kernel has run (a freed one could be reused by the next)
+    peer_rows, peer_expert, peer_src = _table(*rows), _table(*expert), _table(*srcs)
     code = _lib().moe_ep_dispatch_p2p(
         native._ptr(ids), native._ptr(x), T, H, k, E, world, rank, native._ptr(matrix), capacity, src_stride,
-        native._ptr(_table(*rows)), native._ptr(_table(*expert)), native._ptr(_table(*srcs)), native._ptr(ws),
+        native._ptr(peer_rows), native._ptr(peer_expert), native._ptr(peer_src), native._ptr(ws),
         ws.numel(), native._stream())
     native._check(code, "moe_ep_dispatch_p2p")
     assert _device_error() == EP_RANGE_ERROR
