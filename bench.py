@@ -9,8 +9,11 @@ expert resident in HBM (11.3 GB of e4m3 weights + fp32 block scales,
 synthetic, seeded).  The weights streamed per step exceed the 126 MB L2, and
 L2 is additionally flushed (256 MiB write) between timed steps; each step is
 timed with CUDA events on the launching stream.  The layer runs as one CUDA
-graph replay (GraphedDsMoELayer: 7 kernels); the plain per-call path is
-timed too (eager_ms_per_step).  The same measurement is repeated for
+graph replay (GraphedDsMoELayer: 7 kernels -- router logits, route + dispatch,
+x staging, gate/up, activation staging, down, combine; 5 with --fused-decode);
+the plain per-call path is timed too
+(eager_ms_per_step), and the other decode-experts variant (one fused launch
+or three) beside the one run (alt_ms_per_step).  The same measurement is repeated for
 T = 1, 4, 16 ("sweep").
 
 Printed (rank 0, one JSON line): tokens/s with inputs resident in HBM
@@ -57,8 +60,11 @@ L2_FLUSH_BYTES = 256 << 20
 # kernels per layer forward: router logits, route + dispatch + chunk list, then on the warp-MMA path
 # x -> f16, gate/up, activations -> f16, down (else chunk list, gate/up, down), combine
 KERNELS_PER_LAYER = {"auto": 7, "mma_regs": 7, "mma_tma": 7, "stream": 6, "direct": 6}
+# with the fused decode experts: router logits, route + dispatch + chunk list, x -> f16, fused experts, combine
+KERNELS_PER_LAYER_FUSED = 5
 GEMV_IMPLS = {"auto": 0, "stream": 1, "direct": 2, "mma_regs": 3, "mma_tma": 4}
 ROOFLINE_KERNEL = {
+    "fused": "decode_fused_kernel<tiled>: gate/up+SwiGLU, activation staging and down (fp8_mma.cu)",
     "auto": "mma_gemv_async_kernel<2, swiglu> gate/up+SwiGLU (fp8_mma.cu)",
     "mma_regs": "mma_gemv_kernel<2, swiglu> gate/up+SwiGLU (fp8_mma.cu)",
     "mma_tma": "tma_mma_gemv_kernel<2, swiglu> gate/up+SwiGLU (fp8_mma.cu)",
@@ -384,6 +390,9 @@ def run_ours(args, rank: int, world: int) -> dict | None:
     gpu_layer = DsMoELayerGPU(layer)
     flush = torch.zeros((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
     peaks = measured_peaks()
+    lib = native.load_library()
+    lib.moe_b200_fused_decode(1 if args.fused_decode else 0)
+    fused = bool(lib.moe_b200_fused_decode_enabled()) and args.gemv == "auto"
     results = {}
     checked = {}  # T -> (x, out, ids) of the timed batch, for the parity leg
     sweep = [] if args.sweep == "none" else [int(v) for v in args.sweep.split(",") if v]
@@ -413,10 +422,20 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                 ms = float(t.item())
             stages = stage_times(gpu_layer, x, max(5, min(args.steps, 50)), flush)
             b = layer_bytes(cfg, ids, T)
-            # stage intervals: [route + dispatch + chunk list (+ x to f16), gate/up,
-            # (activations to f16 on the MMA path,) down, combine]
-            gateup_ms = stages[1] if len(stages) >= 2 else None
-            down_ms = (stages[3] if len(stages) >= 5 else stages[2]) if len(stages) >= 3 else None
+            # stage intervals: [route + dispatch + chunk list + x to f16, then either the fused experts
+            # or gate/up, (activations to f16 on the MMA path,) down; then combine]
+            fused_ms = stages[1] if fused and len(stages) == 3 else None
+            gateup_ms = stages[1] if not fused and len(stages) >= 2 else None
+            down_ms = (stages[3] if len(stages) >= 5 else stages[2]) if not fused and len(stages) >= 3 else None
+            # the other decode-experts variant on the same batch (fused vs three launches), for comparison
+            alt_ms = None
+            if args.gemv == "auto" and not args.no_alt_compare:
+                lib.moe_b200_fused_decode(0 if fused else 1)
+                g3 = gpu_layer.capture(T)
+                g3.input.copy_(x)
+                alt_ms = statistics.mean(time_steps(g3.replay, args.steps, args.warmup, flush))
+                del g3
+                lib.moe_b200_fused_decode(1 if fused else 0)
             # end to end through the public API: pinned host in, pinned host out
             x_host = x.cpu().pin_memory()
             out_host = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
@@ -441,9 +460,13 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                 "experts_streamed": b["experts"], "layer_bytes": b["total"],
                 "layer_hbm_frac": (b["total"] / (ms / 1e3)) / (peaks["hbm_gbs"] * 1e9),
                 "gateup_ms": gateup_ms, "down_ms": down_ms, "stage_ms": stages,
-                "gateup_bytes": b["gateup"],
+                "gateup_bytes": b["gateup"], "down_bytes": b["down"],
                 "gateup_gbs": (b["gateup"] / (gateup_ms / 1e3) / 1e9) if gateup_ms else None,
                 "down_gbs": (b["down"] / (down_ms / 1e3) / 1e9) if down_ms else None,
+                "fused_experts_ms": fused_ms,
+                "fused_experts_gbs": ((b["gateup"] + b["down"]) / (fused_ms / 1e3) / 1e9) if fused_ms else None,
+                "alt_variant": None if alt_ms is None else ("three launches" if fused else "fused experts"),
+                "alt_ms_per_step": alt_ms,
             }
         # the checker on every decode batch (all tokens), and the reference's CPU path on the headline batch,
         # both on one host copy of this layer's weights
@@ -479,7 +502,8 @@ def run_ours(args, rank: int, world: int) -> dict | None:
         return None
     head = results[args.tokens]
     peak = peaks["hbm_gbs"]
-    achieved = head["gateup_gbs"]
+    achieved = head["fused_experts_gbs"] if fused else head["gateup_gbs"]
+    roofline_bytes = head["gateup_bytes"] + head["down_bytes"] if fused else head["gateup_bytes"]
     for block in (prefill, q4):
         for key, rep in (block.pop("parity", None) or {}).items():
             parity[key] = rep
@@ -498,23 +522,26 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                    "top_k": cfg.top_k, "n_group": cfg.n_group, "topk_group": cfg.topk_group,
                    "parallelism": "single GPU" if world == 1 else f"replicas x{world}",
                    "l2": "weights streamed per step exceed L2; 256 MiB L2 flush between timed steps"},
-        "roofline": {"bound": "hbm", "kernel": ROOFLINE_KERNEL[args.gemv],
+        "roofline": {"bound": "hbm", "kernel": ROOFLINE_KERNEL["fused" if fused else args.gemv],
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None,
                      "peak_source": f"{peaks['source']} hbm_gbs",
-                     "algorithmic_bytes_per_launch": head["gateup_bytes"],
-                     "traffic": read_traffic(f"grouped_gemv_gateup_c2_decode_T{args.tokens}.md"),
+                     "algorithmic_bytes_per_launch": roofline_bytes,
+                     "traffic": read_traffic(f"decode_fused_c2_decode_T{args.tokens}.md" if fused else
+                                             f"grouped_gemv_gateup_c2_decode_T{args.tokens}.md"),
                      "layer_frac": head["layer_hbm_frac"]},
         "e2e": {"value": head["e2e_tokens_per_s"], "unit": "tokens/s",
                 "h2d_bytes_per_step": args.tokens * cfg.hidden * 2, "d2h_bytes_per_step": args.tokens * cfg.hidden * 2},
-        "gpu_launches": KERNELS_PER_LAYER[args.gemv] * args.steps,
+        "gpu_launches": (KERNELS_PER_LAYER_FUSED if fused else KERNELS_PER_LAYER[args.gemv]) * args.steps,
         "cpu_baseline": cpu,
         "clocks": clock_info,
         "parity": parity_summary,
         "decode_T1": None if t1 is None else {
             "ms_per_step": t1["ms_per_step"], "tokens_per_s": t1["tokens_per_s"],
             "layer_bytes": t1["layer_bytes"], "layer_hbm_frac": t1["layer_hbm_frac"],
-            "stage_ms": t1["stage_ms"], "target_hbm_frac": 0.70},
+            "stage_ms": t1["stage_ms"], "fused_experts_ms": t1["fused_experts_ms"],
+            "fused_experts_gbs": t1["fused_experts_gbs"],
+            "alt_variant": t1["alt_variant"], "alt_ms_per_step": t1["alt_ms_per_step"], "target_hbm_frac": 0.70},
         "sweep": {str(T): {k: v for k, v in r.items() if k != "stage_ms"} | {"stage_ms": r["stage_ms"]}
                   for T, r in sorted(results.items())},
         "prefill": prefill,
@@ -1080,6 +1107,10 @@ def main() -> None:
     parser.add_argument("--seed", type=int, default=20)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--fused-decode", action="store_true",
+                        help="run decode experts as one fused launch (decode_fused_kernel) instead of three")
+    parser.add_argument("--no-alt-compare", action="store_true",
+                        help="skip timing the other decode-experts variant (fused / three launches) beside the run one")
     parser.add_argument("--no-parity", action="store_true",
                         help="skip the parity leg (the oracle on each timed batch, after its timing)")
     parser.add_argument("--cpu-prefill-experts", type=int, default=4,
@@ -1133,6 +1164,7 @@ def main() -> None:
         from pocketlm_b200 import native
 
         native.load_library().moe_b200_select_gemv(GEMV_IMPLS[args.gemv])
+        native.load_library().moe_b200_fused_decode(1 if args.fused_decode else 0)
     try:
         if args.profile_prefill:
             result = run_profile_prefill(args)

@@ -478,6 +478,27 @@ int moe_b200_stage_times(float* ms, int max_n);
 int moe_b200_select_gemv(int impl);
 /* The current selection (0 for the default, else 1 to 4). */
 int moe_b200_selected_gemv(void);
+/* No reference counterpart.  Decode-sized layers on the default GEMV run
+ * their experts as one persistent launch -- gate/up + SwiGLU, the f16 staging
+ * of the activations and the down projection, each phase's weight bytes cut
+ * into equal per-warp ranges, down work of an expert waiting (bounded) for that
+ * expert's gate/up -- when enabled (1); 0 (the default) runs the three
+ * launches.  Same results to fp32 rounding of the partial-sum grouping. */
+int moe_b200_fused_decode(int enable);
+int moe_b200_fused_decode_enabled(void);
+/* No reference counterpart.  A/B knob: k-ranges per task of the decode
+ * warp-MMA stages (0, the default: chosen per batch; 1-8: forced).  It sizes
+ * the layer workspace too, so set it before querying the workspace. */
+int moe_b200_force_ksplit(int ksplit);
+/* No reference counterpart.  Decode batches of at most 8 tokens (and 256
+ * (token, slot) entries) run selection, dispatch, the chunk list and the f16
+ * staging of x in one 256-thread launch (1, the default) or in two launches
+ * (0).  Same results bit for bit. */
+int moe_b200_decode_prologue(int enable);
+/* No reference counterpart.  A/B knob: decode warp-MMA units walk their
+ * k-blocks from a unit-dependent offset (1) or in order (0, the default);
+ * same results to fp32 rounding of the summation order. */
+int moe_b200_kb_rotate(int enable);
 
 /* ---------------------------------------------------------------------------
  * Pack-file reads (host only): the FP8 pack loader's byte ranges.
@@ -497,9 +518,10 @@ int moe_read_spans(const char* path, int64_t n, const uint64_t* offsets, const u
 /* Device error word (no reference counterpart): nonzero when a bounded wait
  * inside a kernel gave up (1: producer, 2: consumer, 4: drain, 8: misaligned
  * weights refused by the streaming kernel, 16: warp-MMA ring, 32: prefill
- * tensor-core GEMM pipeline), or when an expert-parallel peer kernel skipped
- * a store whose rank, slot or row read from exchanged data was out of range
- * (64).  Synchronises
+ * tensor-core GEMM pipeline, 128: fused decode experts -- a down piece gave
+ * up waiting for its expert's activations), or when an expert-parallel peer
+ * kernel skipped a store whose rank, slot or row read from exchanged data was
+ * out of range (64).  Synchronises
  * `stream`, returns the word (-1 if it cannot be read) and clears it. */
 int moe_b200_device_error(void* stream);
 

@@ -56,6 +56,19 @@ int g_gemv_impl = 0;
 // Operand feed of the warp-MMA kernel: 0 = register loads, 1 = TMA bulk-copy
 // ring per warp, 2 = cp.async shared-memory ring per warp (default).
 int g_mma_feed = 2;
+// Decode experts on the cp.async feed as one fused launch (decode_fused_kernel:
+// gate/up, activation staging and down) rather than three launches (off by
+// default: measured slower than the three launches at 1-64 tokens).
+bool g_fused_decode = false;
+// K-split of the cp.async warp-MMA stages: 0 = chosen per batch (async_gemv_ksplit), else this many
+// k-ranges per task (capped at kMaxMmaKSplit); sizes the workspace too, so it must not change between
+// a workspace query and the call it sizes.
+int g_force_ksplit = 0;
+// Decode batches of <= 256 (token, slot) entries: selection, dispatch, chunk list and x staging in one
+// CTA (decode_prologue_kernel) instead of route_dispatch_kernel + rows_to_f16_kernel.
+bool g_decode_prologue = true;
+// Staggered k-block walks in the cp.async warp-MMA stages (MmaArgs::kb_rotate).
+int g_kb_rotate = 0;
 
 cudaError_t gemv(const GemvArgs& a, int x_dtype, int ns, int epi, int nt, bool vec, cudaStream_t stream) {
   if (g_gemv_impl == 1 && vec && stream_gemv_supported(a.K, x_dtype, nt))
@@ -771,8 +784,12 @@ struct LayerPlan {
   int ksplit1, ksplit2;    // gate/up, down
   int64_t tasks1, tasks2;  // upper bounds on tasks (chunks x row tiles)
   float* partial;
-  int32_t* counters;       // [tasks1] gate/up then [tasks2] down (only the split stages)
+  int32_t* counters;       // [tasks1] gate/up then [tasks2] down, then [2 x chunks] (fused decode); zeroed by
+                           // the x staging of every forward
   int64_t n_counters;
+  int64_t chunks;          // upper bound on the chunk list's length
+  float* partial_fused;    // fused decode: [2 phases][2 x fused_warps][32 x 8] piece slots
+  int fused_warps;
   // prefill (tcgen05 grouped GEMM): pair-ordered fp16 activations, their
   // scales, and the per-expert m-tile prefix
   __half* a16;
@@ -811,18 +828,22 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
   // the k-split depends on the feed's resident warps; size for either feed
   const int ks_regs1 = mma_gemv_ksplit(l.tasks1, static_cast<int>(H));
   const int ks_regs2 = mma_gemv_ksplit(l.tasks2, static_cast<int>(I));
-  const int ks_async1 = async_gemv_ksplit(l.tasks1, static_cast<int>(H));
-  const int ks_async2 = async_gemv_ksplit(l.tasks2, static_cast<int>(I));
+  const int forced = std::min(g_force_ksplit, kMaxMmaKSplit);
+  const int ks_async1 = forced > 0 ? forced : async_gemv_ksplit(l.tasks1, static_cast<int>(H));
+  const int ks_async2 = forced > 0 ? forced : async_gemv_ksplit(l.tasks2, static_cast<int>(I));
   const bool async = g_mma_feed == 2;
   l.ksplit1 = async ? ks_async1 : ks_regs1;
   l.ksplit2 = async ? ks_async2 : ks_regs2;
   const int64_t frag = 32 * 8;
   const int64_t part = std::max({l.tasks1 * std::max(ks_regs1, ks_async1), l.tasks2 * std::max(ks_regs2, ks_async2),
                                  int64_t{1}});
+  l.chunks = chunks;
   if (!lean) {
     l.partial = p.take<float>(part * frag);
-    l.n_counters = l.tasks1 + l.tasks2;
+    l.n_counters = l.tasks1 + l.tasks2 + 2 * chunks;
     l.counters = p.take<int32_t>(l.n_counters);
+    l.fused_warps = decode_fused_warps();
+    l.partial_fused = p.take<float>(static_cast<int64_t>(2) * 2 * l.fused_warps * frag);
   }
   // the tcgen05 GEMM's pair rows: layers (router) and expert-parallel experts (rows) alike
   if (T >= kPrefillMinTokens) {
@@ -880,17 +901,20 @@ static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16
 
 // The expert stages on the warp-MMA kernel: x and the SwiGLU activations are
 // staged as f16 rows with power-of-two scales.
+// x_staged: l.x16 / l.xscale already hold the staged rows and the counters are
+// zero (the decode prologue did both).
 static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, const LayerPlan& l, int64_t T,
                                  int64_t pairs, int64_t n_segments, int64_t I, int64_t H, bool chunks_ready,
-                                 const uint8_t* nan_free, cudaStream_t s, int tiled = 0) {
+                                 const uint8_t* nan_free, cudaStream_t s, int tiled = 0, bool x_staged = false) {
   const MlpScratch& m = l.m;
   if (!chunks_ready) {
     ChunkArgs ca{m.seg_offset, static_cast<int>(n_segments), 8, m.chunk_seg, m.chunk_start, m.chunk_len, m.n_chunks};
     MOE_CUDA(launch_chunks(ca, s), "chunk list");
   }
-  MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.x16, l.xscale,
-                              l.counters, l.n_counters, s),
-           "stage x");
+  if (!x_staged)
+    MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.x16, l.xscale,
+                                l.counters, l.n_counters, s),
+             "stage x");
   stage_mark(s);
   MmaArgs g1{};
   g1.w0 = t.gw; g1.s0 = t.gs; g1.w1 = t.uw; g1.s1 = t.us;
@@ -900,6 +924,27 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
   g1.scale_cols = static_cast<int>(ceil_div(H, kBlock)); g1.nanfix = 1;
   g1.ksplit = l.ksplit1; g1.partial = l.partial; g1.counters = l.counters; g1.nan_free = nan_free;
   g1.tiled = tiled;
+  g1.kb_rotate = g_kb_rotate;
+  if (g_fused_decode && g_mma_feed == 2 && l.partial_fused && l.fused_warps > 0) {
+    // one persistent launch: gate/up + SwiGLU, activation staging, down
+    DecodeFusedArgs f{};
+    f.up = g1;
+    f.up.ksplit = 1;
+    f.down = g1;
+    f.down.w0 = t.dw; f.down.s0 = t.ds; f.down.w1 = nullptr; f.down.s1 = nullptr;
+    f.down.x16 = l.act16; f.down.xscale = l.ascale; f.down.pair_row = nullptr;
+    f.down.out0 = m.y; f.down.N = static_cast<int>(H); f.down.K = static_cast<int>(I);
+    f.down.scale_cols = static_cast<int>(ceil_div(I, kBlock)); f.down.ksplit = 1;
+    f.partial = l.partial_fused;
+    f.partial_warps = l.fused_warps;
+    f.cnt_up = l.counters;
+    f.cnt_down = l.counters + l.tasks1;
+    f.chunk_up = l.counters + l.tasks1 + l.tasks2;
+    f.chunk_ready = f.chunk_up + l.chunks;
+    MOE_CUDA(launch_decode_fused(f, s), "fused decode experts");
+    stage_mark(s);
+    return kOk;
+  }
   MOE_CUDA(g_mma_feed == 1   ? launch_tma_mma_gemv(g1, 2, kEpiSwiglu, s)
            : g_mma_feed == 2 ? launch_async_mma_gemv(g1, 2, kEpiSwiglu, l.tasks1, s)
                              : launch_mma_gemv(g1, 2, kEpiSwiglu, l.tasks1, s),
@@ -969,7 +1014,7 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   ba.block_counts = l.bucket_scratch;
   ChunkArgs ca{l.m.seg_offset, static_cast<int>(S), chunk, l.m.chunk_seg, l.m.chunk_start, l.m.chunk_len,
                l.m.n_chunks};
-  bool chunks_ready = false;
+  bool chunks_ready = false, x_staged = false;
   if (T <= 256 && route_dispatch_smem_bytes(static_cast<int>(T), static_cast<int>(E)) <= 200 * 1024) {
     // decode batches: logits (cluster-reduced, else split-K partials), then
     // selection + dispatch + chunk list in one CTA
@@ -1003,7 +1048,23 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
     rd.bucket.weights_out = l.wts;
     rd.bucket.args = ba;
     rd.chunks = ca;
-    MOE_CUDA(launch_route_dispatch(rd, s), "route + dispatch");
+    if (g_decode_prologue && use_mma && nparts == 1 && l.x16 &&
+        decode_prologue_supported(static_cast<int>(T), static_cast<int>(E), static_cast<int>(k), static_cast<int>(H),
+                                  hidden_dtype, hidden, static_cast<int>(S))) {
+      // selection, dispatch, chunk list, x staging and counter reset in one CTA
+      DecodePrologueArgs dp{};
+      dp.rd = rd;
+      dp.x = hidden;
+      dp.hidden = static_cast<int>(H);
+      dp.x16 = l.x16;
+      dp.xscale = l.xscale;
+      dp.zero = l.counters;
+      dp.zero_n = l.n_counters;
+      MOE_CUDA(launch_decode_prologue(dp, hidden_dtype, s), "decode prologue");
+      x_staged = true;
+    } else {
+      MOE_CUDA(launch_route_dispatch(rd, s), "route + dispatch");
+    }
     chunks_ready = true;
   } else {
     // 1. route (weights rounded through bf16 like fp8_source.py:1547 when hidden is bf16)
@@ -1025,7 +1086,7 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
                                      H, nan_free, s);
   } else if (use_mma) {
     code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I, H,
-                                 chunks_ready, nan_free, s, weight_layout);
+                                 chunks_ready, nan_free, s, weight_layout, x_staged);
   } else {
     code = run_expert_stages(t, hidden, xd, l.m, l.m.y, S, I, H, ceil_div(H, kBlock), ceil_div(I, kBlock), nt, vec, s);
   }
@@ -1325,6 +1386,32 @@ int moe_b200_stage_timing(int enable) {
   }
   g_timing = enable != 0;
   g_marks = 0;
+  return kOk;
+}
+
+int moe_b200_fused_decode(int enable) {
+  if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
+  g_fused_decode = enable != 0;
+  return kOk;
+}
+
+int moe_b200_fused_decode_enabled(void) { return g_fused_decode ? 1 : 0; }
+
+int moe_b200_decode_prologue(int enable) {
+  if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
+  g_decode_prologue = enable != 0;
+  return kOk;
+}
+
+int moe_b200_kb_rotate(int enable) {
+  if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
+  g_kb_rotate = enable;
+  return kOk;
+}
+
+int moe_b200_force_ksplit(int ksplit) {
+  if (ksplit < 0 || ksplit > kMaxMmaKSplit) return fail(kBadDims, "ksplit must be 0 to 8");
+  g_force_ksplit = ksplit;
   return kOk;
 }
 

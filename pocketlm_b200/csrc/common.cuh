@@ -153,4 +153,37 @@ MOE_D void warp_argmax(float& v, int& idx) {
   }
 }
 
+// 16 bytes of activations -> floats (4 fp32, or 8 bf16 / f16 values), exactly.
+template <typename T>
+MOE_D void unpack16(const uint4& v, float* out);
+
+template <>
+MOE_D void unpack16<float>(const uint4& v, float* out) {
+  out[0] = __uint_as_float(v.x);
+  out[1] = __uint_as_float(v.y);
+  out[2] = __uint_as_float(v.z);
+  out[3] = __uint_as_float(v.w);
+}
+
+template <>
+MOE_D void unpack16<__nv_bfloat16>(const uint4& v, float* out) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(w[i] << 16);
+    out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+template <>
+MOE_D void unpack16<__half>(const uint4& v, float* out) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
+  }
+}
+
 }  // namespace moe

@@ -64,6 +64,23 @@ struct RouteDispatchArgs {
 size_t route_dispatch_smem_bytes(int tokens, int experts);
 cudaError_t launch_route_dispatch(const RouteDispatchArgs& a, cudaStream_t stream);
 
+// route_dispatch_kernel's work plus the x staging (rows_to_f16_kernel) and the
+// zeroing of `zero` in one 256-thread CTA, for up to 8 tokens, tokens x top_k <=
+// 256 entries and <= 256 routed experts (decode_prologue_supported); rd.nparts must be 1.
+constexpr int kPrologueThreads = 256;
+struct DecodePrologueArgs {
+  RouteDispatchArgs rd;
+  const void* x;       // [tokens, hidden] bf16 or fp32, 16-byte aligned rows
+  int hidden;
+  __half* x16;         // [tokens, hidden] x / xscale
+  float* xscale;       // [tokens]
+  int32_t* zero;       // [zero_n] set to 0
+  int64_t zero_n;
+};
+bool decode_prologue_supported(int tokens, int experts, int top_k, int hidden, int x_dtype, const void* x,
+                               int n_segments);
+cudaError_t launch_decode_prologue(const DecodePrologueArgs& a, int x_dtype, cudaStream_t stream);
+
 size_t bucket_smem_bytes(int n_buckets);
 cudaError_t launch_bucket(const BucketArgs& a, cudaStream_t stream);
 cudaError_t launch_chunks(const ChunkArgs& a, cudaStream_t stream);

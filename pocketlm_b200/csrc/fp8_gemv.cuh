@@ -81,6 +81,7 @@ struct MmaArgs {
   int ksplit;                // register-fed kernel: k-block ranges per task (1: none)
   float* partial;            // [tasks * ksplit, 32, 8] fp32 fragments when ksplit > 1
   int32_t* counters;         // [tasks] arrival counters: zero on entry, left zero on exit
+  int kb_rotate;             // cp.async kernels: start each unit's k-block walk at a unit-dependent offset
 };
 constexpr int kMaxMmaKSplit = 8;
 // Rows of one warp task of the MMA kernels: 16 (gate + up) or 32 (one matrix).
@@ -94,6 +95,25 @@ cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bou
 // cp.async (fp8_mma.cu); tasks_bound as for launch_mma_gemv.
 int async_gemv_ksplit(int64_t tasks_bound, int K);
 cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream);
+// Fused decode experts (decode_fused_kernel, tiled or row-major weights): the
+// gate/up + SwiGLU stage (up), the f16 staging of its activations and the down
+// stage (down) in one persistent launch.  up.out0 = act fp32 [P, I]; down.x16 /
+// down.xscale = where the activations are staged ([P, I] f16, [P]); down.out0
+// = y.  partial: [2][2 * partial_warps][32 * 8] fp32; cnt_up [up tasks],
+// cnt_down [down tasks], chunk_up / chunk_ready [chunks]: zero on entry.
+struct DecodeFusedArgs {
+  MmaArgs up;
+  MmaArgs down;
+  float* partial;
+  int partial_warps;
+  int32_t* cnt_up;
+  int32_t* cnt_down;
+  int32_t* chunk_up;
+  int32_t* chunk_ready;
+};
+// Warps of the fused launch (all resident at once): sizes `partial`.
+int decode_fused_warps();
+cudaError_t launch_decode_fused(const DecodeFusedArgs& a, cudaStream_t stream);
 // Fragment-native ("tiled") weight layout, read by the cp.async decode GEMV
 // and the prefill GEMM.  Row tile t = rows 16t .. 16t + 15; group = 8 row
 // tiles (128 rows).  For every (group, 128-column k-block kb, 64-column half

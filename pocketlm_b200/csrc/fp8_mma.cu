@@ -56,37 +56,6 @@ struct KBlock {
 // Activation rows -> f16 with a per-row power-of-two scale:
 // dst[r, k] = src[r, k] / scale[r], scale = 2^(floor(log2(amax)) - 13) so the
 // largest magnitude lands in [2^13, 2^14) (1 for an all-zero row).
-template <typename T>
-MOE_D void unpack16(const uint4& v, float* out);
-
-template <>
-MOE_D void unpack16<float>(const uint4& v, float* out) {
-  out[0] = __uint_as_float(v.x);
-  out[1] = __uint_as_float(v.y);
-  out[2] = __uint_as_float(v.z);
-  out[3] = __uint_as_float(v.w);
-}
-
-template <>
-MOE_D void unpack16<__nv_bfloat16>(const uint4& v, float* out) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    out[2 * i] = __uint_as_float(w[i] << 16);
-    out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-  }
-}
-
-template <>
-MOE_D void unpack16<__half>(const uint4& v, float* out) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-    out[2 * i] = f.x;
-    out[2 * i + 1] = f.y;
-  }
-}
 
 // Activation rows -> f16 with a per-row power-of-two scale:
 // dst[r, k] = src[r, k] / scale[r], scale = 2^(floor(log2(amax)) - 13) so the
@@ -432,6 +401,7 @@ struct UnitOperands {
   const __half* xb;
   bool bvalid;
   int kb0, kb1;
+  int rot;  // the unit's k-blocks are streamed from kb0 + rot, wrapping to kb0 (0: in order)
 };
 
 // acc += this lane's share of W[k-blocks kb0..kb1) . x for unit u.  The warp's
@@ -466,26 +436,32 @@ MOE_D int async_accumulate(float (&acc)[2][4], unsigned char* ring, const UnitOp
   };
   const int kb0 = u.kb0, kb1 = u.kb1, n = kb1 - kb0;
   const int nx_steps = nx.kb1 - nx.kb0;
+  // k-block of step j of a unit (its rotation applied)
+  auto kb_of = [](const UnitOperands& o, int j) {
+    const int m = o.kb1 - o.kb0;
+    const int r = j + o.rot;
+    return o.kb0 + (r >= m ? r - m : r);
+  };
   int nx_issued = 0;
   for (int j = primed; j < kAsyncStages - 1; ++j) {
-    if (j < n) issue(u, kb0 + j, step0 + j);
+    if (j < n) issue(u, kb_of(u, j), step0 + j);
     cp_async_commit();
   }
-  float sc0 = __ldg(u.srow[0] + kb0), sc1 = __ldg(u.srow[1] + kb0);
-  for (int kbi = kb0; kbi < kb1; ++kbi) {
-    const int ahead = kbi - kb0 + kAsyncStages - 1;  // step of u (or beyond: of nx) to issue now
+  float sc0 = __ldg(u.srow[0] + kb_of(u, 0)), sc1 = __ldg(u.srow[1] + kb_of(u, 0));
+  for (int j = 0; j < n; ++j) {
+    const int ahead = j + kAsyncStages - 1;  // step of u (or beyond: of nx) to issue now
     if (ahead < n) {
-      issue(u, kb0 + ahead, step0 + ahead);
+      issue(u, kb_of(u, ahead), step0 + ahead);
     } else if (nx_issued < nx_steps && nx_issued < kAsyncStages - 1) {
-      issue(nx, nx.kb0 + nx_issued, step0 + n + nx_issued);
+      issue(nx, kb_of(nx, nx_issued), step0 + n + nx_issued);
       ++nx_issued;
     }
     cp_async_commit();
     // next k-block's scales load while this one is multiplied
-    const int kn = min(kbi + 1, kb1 - 1);
+    const int kn = kb_of(u, min(j + 1, n - 1));
     const float nsc0 = __ldg(u.srow[0] + kn), nsc1 = __ldg(u.srow[1] + kn);
-    cp_async_wait<kAsyncStages - 1>();  // this lane's copies of k-block kbi have landed
-    const uint32_t stage = (step0 + kbi - kb0) % kAsyncStages;
+    cp_async_wait<kAsyncStages - 1>();  // this lane's copies of step j have landed
+    const uint32_t stage = (step0 + j) % kAsyncStages;
     float t[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int sp = 0; sp < 2; ++sp) {
@@ -545,6 +521,7 @@ __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(Mma
   // operand addresses of a unit (an empty k-range when out of range or the expert is absent)
   auto operands = [&](int64_t unit, UnitOperands& o, bool& fix) {
     o.kb0 = o.kb1 = 0;
+    o.rot = 0;
     fix = false;
     if (unit >= units) return;
     const int64_t task = unit / ksplit;
@@ -578,6 +555,8 @@ __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(Mma
     o.xb = a.x16 + brow * K + 16 * c;
     o.kb0 = static_cast<int>(static_cast<int64_t>(ks) * nkb / ksplit);
     o.kb1 = static_cast<int>(static_cast<int64_t>(ks + 1) * nkb / ksplit);
+    // staggered start: concurrent units do not walk the k-blocks in lockstep
+    if (a.kb_rotate && o.kb1 > o.kb0) o.rot = static_cast<int>((unit * 37) % (o.kb1 - o.kb0));
     fix = a.nanfix && !(a.nan_free && a.nan_free[seg]);
   };
 
@@ -657,6 +636,369 @@ __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(Mma
         }
       }
     }
+  }
+  cp_async_wait<0>();  // no copy of this warp in flight when it exits
+}
+
+// ---------------------------------------------------------------------------
+// Fused decode experts (tiled weights): gate/up + SwiGLU, the f16 staging of
+// the SwiGLU activations and the down projection in ONE persistent launch of
+// every resident warp -- the work of mma_gemv_async_kernel<2>,
+// rows_to_f16_kernel<float> and mma_gemv_async_kernel<1> without two launch
+// gaps and without the ramp and tail of three grids.
+//
+// Work split (per phase, "stream-K"): a phase's work is tasks x k-blocks
+// "steps" (a task = chunk of <= 8 pairs x 16 rows of gate + up, or x 32 rows
+// of down); warp w of the W used takes steps [w S / W, (w + 1) S / W), so every
+// warp streams the same weight bytes.  A task whose steps fall to several
+// warps has each piece written to a partial slot of its warp (2 per warp and
+// phase: its first task, its last) and the warp adding the last piece sums
+// the pieces in warp order -- the same order whoever arrives last -- then runs
+// the epilogue.  Every warp does its gate/up range, then its down range.
+//
+// Dependency: when a chunk's last gate/up task is written, the warp that
+// wrote it stages the chunk's activation rows to f16 with a power-of-two row
+// scale (rows_to_f16_kernel's arithmetic, so the staged rows are the same
+// bits) and publishes the chunk's ready flag (release).  A down piece of a
+// chunk waits for that flag (acquire; bounded by kWaitLimitNs, after which
+// the piece is skipped and kDecodeWaitError is recorded).  The wait always
+// ends: every CTA is resident (the grid is the occupancy of this kernel),
+// gate/up pieces never wait, and every warp finishes its gate/up range first.
+// The counters and flags must be zero on entry (the x staging kernel clears
+// them each forward).
+// ---------------------------------------------------------------------------
+constexpr int kDecodeWaitError = 128;
+
+MOE_D int ld_acquire_gpu(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+MOE_D void st_release_gpu(int32_t* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// One phase's geometry on the device.
+struct DecodePhase {
+  int rows, row_tiles, nkb;
+  int64_t tasks, steps, warps;  // warps: W used by this phase (0: no work)
+  MOE_D int64_t lo(int64_t w) const { return w * steps / warps; }
+  MOE_D int64_t hi(int64_t w) const { return (w + 1) * steps / warps; }
+  // the warp whose range holds step s
+  MOE_D int64_t warp_of(int64_t s) const { return ((s + 1) * warps - 1) / steps; }
+};
+
+MOE_D DecodePhase decode_phase(int N, int K, int ns, int n_chunks, int64_t W) {
+  DecodePhase p;
+  p.rows = ns == 2 ? 16 : 32;
+  p.row_tiles = static_cast<int>(ceil_div(N, p.rows));
+  p.nkb = K / kBlock;
+  p.tasks = static_cast<int64_t>(n_chunks) * p.row_tiles;
+  p.steps = p.tasks * p.nkb;
+  // at least a quarter of a task per warp keeps the pieces of a task to five or fewer, and at most one
+  // warp per step keeps every warp's range non-empty (a task's pieces then come from every warp between
+  // the first and the last that hold its steps, which is what the arrival count expects)
+  p.warps = p.steps > 0 ? max(int64_t{1}, min(min(W, p.steps), 4 * p.steps / max(p.nkb, 1))) : 0;
+  return p;
+}
+
+// A warp's piece: task `task` of phase `ph`, k-blocks [kb0, kb1).
+struct DecodeSeg {
+  int ph;
+  int64_t task;
+  int kb0, kb1;
+};
+
+template <int PH>
+MOE_D const MmaArgs& decode_args(const DecodeFusedArgs& a) {
+  if constexpr (PH == 0) return a.up;
+  else return a.down;
+}
+
+// Operand addresses of a piece of phase PH (an empty k-range when the expert is absent).
+template <int PH>
+MOE_D void decode_operands(const DecodeFusedArgs& a, const DecodePhase& P, const DecodeSeg& sg, int lane,
+                           UnitOperands& o, bool& fix) {
+  constexpr int NS = PH == 0 ? 2 : 1;
+  const MmaArgs& m = decode_args<PH>(a);
+  const int g = lane / 4, c = lane % 4;
+  o.kb0 = o.kb1 = 0;
+  o.rot = 0;
+  fix = false;
+  const int ch = static_cast<int>(sg.task / P.row_tiles);
+  const int r0 = static_cast<int>(sg.task % P.row_tiles) * P.rows;
+  const int seg = m.chunk_seg[ch], p0 = m.chunk_start[ch], len = m.chunk_len[ch];
+  const uint8_t* w0 = reinterpret_cast<const uint8_t*>(m.w0[seg]);
+  const float* s0 = reinterpret_cast<const float*>(m.s0[seg]);
+  const uint8_t* w1 = NS == 2 ? reinterpret_cast<const uint8_t*>(m.w1[seg]) : w0;
+  const float* s1 = NS == 2 ? reinterpret_cast<const float*>(m.s1[seg]) : s0;
+  const bool present = w0 && s0 && w1 && s1 &&
+                       ((reinterpret_cast<uintptr_t>(w0) | reinterpret_cast<uintptr_t>(w1)) & 15u) == 0;
+  if (!present) return;
+#pragma unroll
+  for (int st = 0; st < 2; ++st) {
+    const int base = NS == 2 ? r0 : r0 + 16 * st;
+    const uint8_t* w = st == 0 ? w0 : w1;
+    const float* sc = st == 0 ? s0 : s1;
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int row = min(base + g + 8 * rr, m.N - 1);
+      o.arow[st][rr] = w + static_cast<int64_t>(row) * m.K + 16 * c;
+    }
+    o.srow[st] = sc + static_cast<int64_t>(min(base, m.N - 1) / kBlock) * m.scale_cols;
+    const int64_t tile = NS == 2 ? r0 / 16 : r0 / 16 + st;
+    o.tbase[st] = w + tiled_offset(tile, 0, 0, P.nkb) + lane * 16;
+  }
+  o.bvalid = g < len;
+  const int64_t brow = o.bvalid ? (m.pair_row ? m.pair_row[p0 + g] : static_cast<int64_t>(p0 + g)) : 0;
+  o.xb = m.x16 + brow * m.K + 16 * c;
+  o.kb0 = sg.kb0;
+  o.kb1 = sg.kb1;
+  if (m.kb_rotate && sg.kb1 > sg.kb0) o.rot = static_cast<int>((sg.task * 37) % (sg.kb1 - sg.kb0));
+  fix = m.nanfix && !(m.nan_free && m.nan_free[seg]);
+}
+
+// A finished task's outputs: SwiGLU of gate and up (PH 0, act) or the down rows (PH 1, y).
+template <int PH>
+MOE_D void decode_epilogue(const DecodeFusedArgs& a, const DecodePhase& P, const DecodeSeg& sg, int lane,
+                           const float (&acc)[2][4], bool known_staged) {
+  const MmaArgs& m = decode_args<PH>(a);
+  const int g = lane / 4, c = lane % 4;
+  const int ch = static_cast<int>(sg.task / P.row_tiles);
+  const int r0 = static_cast<int>(sg.task % P.row_tiles) * P.rows;
+  const int p0 = m.chunk_start[ch], len = m.chunk_len[ch];
+  // the down phase's row scales are written in this launch: read from L2 once the chunk is published
+  // (never, after a timed-out wait: its outputs are then written as zeros)
+  int staged = 1;
+  if (PH == 1 && !known_staged) {
+    if (lane == 0) staged = ld_acquire_gpu(a.chunk_ready + ch);
+    staged = __shfl_sync(0xFFFFFFFFu, staged, 0);
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int tok = 2 * c + j;
+    if (tok >= len) continue;
+    const int64_t tr = m.pair_row ? m.pair_row[p0 + tok] : static_cast<int64_t>(p0 + tok);
+    const float xs = PH == 0 ? m.xscale[tr] : (staged ? __ldcg(m.xscale + tr) : 0.0f);
+    const int64_t p = p0 + tok;
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int i = rr * 2 + j;
+      if (PH == 0) {
+        const int row = r0 + g + 8 * rr;
+        if (row < m.N) {
+          const float gv = acc[0][i] * xs, uv = acc[1][i] * xs;
+          m.out0[p * m.N + row] = gv / (1.0f + expf(-gv)) * uv;
+        }
+      } else {
+#pragma unroll
+        for (int st = 0; st < 2; ++st) {
+          const int row = r0 + 16 * st + g + 8 * rr;
+          if (row < m.N) m.out0[p * m.N + row] = acc[st][i] * xs;
+        }
+      }
+    }
+  }
+}
+
+// Chunk ch's activation rows -> f16 with a power-of-two row scale, by one
+// warp (rows_to_f16_kernel's arithmetic: the same bits).
+MOE_D void decode_stage_chunk(const DecodeFusedArgs& a, int ch, int lane) {
+  const int p0 = a.up.chunk_start[ch], len = a.up.chunk_len[ch];
+  const int I = a.up.N;
+  const int n4 = I / 4;
+  for (int p = p0; p < p0 + len; ++p) {
+    const float4* row = reinterpret_cast<const float4*>(a.up.out0 + static_cast<int64_t>(p) * I);
+    float amax = 0.0f;
+    for (int i0 = lane; i0 < n4; i0 += 8 * kWarp) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = i0 + u * kWarp < n4 ? __ldcg(row + i0 + u * kWarp) : make_float4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+    const float sc = (amax > 0.0f && isfinite(amax)) ? ldexpf(1.0f, ilogbf(amax) - 13) : 1.0f;
+    const float inv = 1.0f / sc;  // exact: power of two
+    __half* dst = const_cast<__half*>(a.down.x16) + static_cast<int64_t>(p) * I;
+    for (int i = lane; i < n4; i += kWarp) {
+      const float4 v = __ldcg(row + i);
+      __align__(8) __half h[4] = {__float2half_rn(v.x * inv), __float2half_rn(v.y * inv),
+                                  __float2half_rn(v.z * inv), __float2half_rn(v.w * inv)};
+      *reinterpret_cast<uint2*>(dst + 4 * i) = *reinterpret_cast<const uint2*>(h);
+    }
+    if (lane == 0) const_cast<float*>(a.down.xscale)[p] = sc;
+  }
+}
+
+template <bool TILED>
+__global__ void __launch_bounds__(kAsyncWarps * kWarp) decode_fused_kernel(DecodeFusedArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  unsigned char* ring = smem + warp * kAsyncStages * kAsyncStageBytes;
+  const int64_t W = min(static_cast<int64_t>(gridDim.x) * kAsyncWarps, static_cast<int64_t>(a.partial_warps));
+  const int64_t wg = static_cast<int64_t>(blockIdx.x) * kAsyncWarps + warp;
+  if (wg >= W) return;
+  const int n_chunks = *a.up.n_chunks;
+  const DecodePhase ph0 = decode_phase(a.up.N, a.up.K, 2, n_chunks, W);
+  const DecodePhase ph1 = decode_phase(a.down.N, a.down.K, 1, n_chunks, W);
+
+  // the warp's pieces in order: its gate/up range, then its down range
+  int cur_ph = 0;
+  int64_t s_at = 0, s_end = 0;
+  if (wg < ph0.warps) {
+    s_at = ph0.lo(wg);
+    s_end = ph0.hi(wg);
+  }
+  auto next_seg = [&](DecodeSeg& sg) -> bool {
+    while (s_at >= s_end) {
+      if (cur_ph == 1) return false;
+      cur_ph = 1;
+      s_at = s_end = 0;
+      if (wg < ph1.warps) {
+        s_at = ph1.lo(wg);
+        s_end = ph1.hi(wg);
+      }
+    }
+    const int nkb = cur_ph ? ph1.nkb : ph0.nkb;
+    sg.ph = cur_ph;
+    sg.task = s_at / nkb;
+    sg.kb0 = static_cast<int>(s_at - sg.task * nkb);
+    sg.kb1 = static_cast<int>(min(s_end - sg.task * nkb, static_cast<int64_t>(nkb)));
+    s_at = (sg.task + 1) * nkb;
+    return true;
+  };
+  auto operands = [&](const DecodeSeg& sg, UnitOperands& o, bool& fix) {
+    if (sg.ph == 0) decode_operands<0>(a, ph0, sg, lane, o, fix);
+    else decode_operands<1>(a, ph1, sg, lane, o, fix);
+  };
+  auto chunk_of = [&](const DecodeSeg& sg) {
+    return static_cast<int>(sg.task / (sg.ph ? ph1.row_tiles : ph0.row_tiles));
+  };
+  // the last chunk this warp saw published (flags only go from 0 to 1 within a launch)
+  int known_ready = -1;
+  // whether a down piece's activations are staged (gate/up pieces need nothing)
+  auto ready = [&](const DecodeSeg& sg) -> bool {
+    if (sg.ph == 0) return true;
+    const int ch = chunk_of(sg);
+    if (ch == known_ready) return true;
+    int v = 0;
+    if (lane == 0) v = ld_acquire_gpu(a.chunk_ready + ch);
+    v = __shfl_sync(0xFFFFFFFFu, v, 0);
+    if (v) known_ready = ch;
+    return v != 0;
+  };
+  auto wait_ready = [&](const DecodeSeg& sg) -> bool {
+    if (chunk_of(sg) == known_ready) return true;
+    int ok = 0;
+    if (lane == 0) {
+      const int32_t* flag = a.chunk_ready + chunk_of(sg);
+      const uint64_t t0 = global_timer_ns();
+      while (true) {
+        if (ld_acquire_gpu(flag)) {
+          ok = 1;
+          break;
+        }
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(&g_device_error, kDecodeWaitError);
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+    if (ok) known_ready = chunk_of(sg);
+    return ok != 0;
+  };
+  // a gate/up task is complete: count it; the chunk's last one stages and publishes the activations
+  auto complete_up = [&](const DecodeSeg& sg) {
+    const int ch = chunk_of(sg);
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(a.chunk_up + ch, 1) == ph0.row_tiles - 1;
+    if (!__shfl_sync(0xFFFFFFFFu, last, 0)) return;
+    __threadfence();
+    decode_stage_chunk(a, ch, lane);
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) st_release_gpu(a.chunk_ready + ch, 1);
+  };
+  auto finish = [&](const DecodeSeg& sg, const float (&acc)[2][4]) {
+    if (sg.ph == 0) {
+      decode_epilogue<0>(a, ph0, sg, lane, acc, true);
+      complete_up(sg);
+    } else {
+      decode_epilogue<1>(a, ph1, sg, lane, acc, chunk_of(sg) == known_ready);
+    }
+  };
+
+  DecodeSeg cur, nxt;
+  bool have = next_seg(cur);
+  UnitOperands cu, nu;
+  bool cfix = false, nfix = false;
+  if (have) operands(cur, cu, cfix);
+  uint32_t step0 = 0;
+  int primed = 0;
+  while (have) {
+    const bool have_n = next_seg(nxt);
+    UnitOperands nx_issue;  // what may be prefetched of the next piece: nothing until its activations exist
+    nx_issue.kb0 = nx_issue.kb1 = 0;
+    nx_issue.rot = 0;
+    if (have_n) {
+      operands(nxt, nu, nfix);
+      if (ready(nxt)) nx_issue = nu;
+    }
+    // a down piece waits for its chunk's activations (absent experts too: their zero rows need the
+    // chunk's scale); after a timeout it is skipped and its rows come out zero (error recorded)
+    bool run = cu.kb1 > cu.kb0;
+    if (cur.ph == 1 && primed == 0 && !wait_ready(cur)) run = false;
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    int nx_primed = 0;
+    if (run) {
+      nx_primed = cfix ? async_accumulate<true, TILED>(acc, ring, cu, nx_issue, step0, primed, lane)
+                       : async_accumulate<false, TILED>(acc, ring, cu, nx_issue, step0, primed, lane);
+      step0 += cu.kb1 - cu.kb0;
+    }
+    primed = nx_primed;
+
+    const DecodePhase P = cur.ph ? ph1 : ph0;
+    if (cur.kb0 == 0 && cur.kb1 == P.nkb) {
+      finish(cur, acc);
+    } else {
+      // a piece: park it in this warp's slot; the last arriving piece sums them in warp order
+      const int64_t first_task = P.lo(wg) / P.nkb;
+      float* slots = a.partial + static_cast<int64_t>(cur.ph) * 2 * a.partial_warps * (kWarp * 8);
+      float4* mine = reinterpret_cast<float4*>(slots + (2 * wg + (cur.task == first_task ? 0 : 1)) * (kWarp * 8) +
+                                               lane * 8);
+      __stcg(mine, make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]));
+      __stcg(mine + 1, make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]));
+      __threadfence();
+      __syncwarp();
+      const int64_t w_lo = P.warp_of(cur.task * P.nkb), w_hi = P.warp_of((cur.task + 1) * P.nkb - 1);
+      int32_t* counter = (cur.ph ? a.cnt_down : a.cnt_up) + cur.task;
+      int last = 0;
+      if (lane == 0) last = atomicAdd(counter, 1) == static_cast<int>(w_hi - w_lo);
+      if (__shfl_sync(0xFFFFFFFFu, last, 0)) {
+        __threadfence();
+        float sum[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        for (int64_t w = w_lo; w <= w_hi; ++w) {
+          const int64_t wf = P.lo(w) / P.nkb;
+          const float4* part = reinterpret_cast<const float4*>(
+              slots + (2 * w + (cur.task == wf ? 0 : 1)) * (kWarp * 8) + lane * 8);
+          const float4 v0 = __ldcg(part), v1 = __ldcg(part + 1);
+          sum[0][0] += v0.x; sum[0][1] += v0.y; sum[0][2] += v0.z; sum[0][3] += v0.w;
+          sum[1][0] += v1.x; sum[1][1] += v1.y; sum[1][2] += v1.z; sum[1][3] += v1.w;
+        }
+        finish(cur, sum);
+      }
+    }
+    cur = nxt;
+    cu = nu;
+    cfix = nfix;
+    have = have_n;
   }
   cp_async_wait<0>();  // no copy of this warp in flight when it exits
 }
@@ -1024,6 +1366,35 @@ cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tas
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAsyncSmem);
   if (err != cudaSuccess) return err;
   kernel<<<grid, kAsyncWarps * kWarp, kAsyncSmem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+static int decode_fused_ctas_per_sm() {
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int a = 0, b = 0;
+    cudaFuncSetAttribute(decode_fused_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAsyncSmem);
+    cudaFuncSetAttribute(decode_fused_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAsyncSmem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, decode_fused_kernel<true>, kAsyncWarps * kWarp, kAsyncSmem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, decode_fused_kernel<false>, kAsyncWarps * kWarp, kAsyncSmem);
+    per_sm = std::max(1, std::min(a, b));
+  }
+  return per_sm;
+}
+
+int decode_fused_warps() { return gemv_grid_ctas() * decode_fused_ctas_per_sm() * kAsyncWarps; }
+
+cudaError_t launch_decode_fused(const DecodeFusedArgs& a, cudaStream_t stream) {
+  if (!a.partial || a.partial_warps <= 0 || !a.cnt_up || !a.cnt_down || !a.chunk_up || !a.chunk_ready ||
+      a.up.tiled != a.down.tiled || a.up.K % kBlock != 0 || a.down.K % kBlock != 0)
+    return cudaErrorInvalidValue;
+  // every CTA resident at once: the down pieces wait for gate/up pieces of other CTAs
+  const int ctas = std::min(gemv_grid_ctas() * decode_fused_ctas_per_sm(),
+                            static_cast<int>(ceil_div(a.partial_warps, kAsyncWarps)));
+  auto kernel = a.up.tiled ? decode_fused_kernel<true> : decode_fused_kernel<false>;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAsyncSmem);
+  if (err != cudaSuccess) return err;
+  kernel<<<static_cast<unsigned>(std::max(1, ctas)), kAsyncWarps * kWarp, kAsyncSmem, stream>>>(a);
   return cudaGetLastError();
 }
 

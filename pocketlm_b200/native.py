@@ -136,6 +136,11 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_ep_experts_return_p2p": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _INT, _I64, _I64, _I64, _P,
                                    _P, _I64, _P], _INT),
     "moe_ep_experts_return_p2p_workspace_bytes": ([_I64] * 5 + [_INT], _I64),
+    "moe_b200_fused_decode": ([_INT], _INT),
+    "moe_b200_fused_decode_enabled": ([], _INT),
+    "moe_b200_force_ksplit": ([_INT], _INT),
+    "moe_b200_decode_prologue": ([_INT], _INT),
+    "moe_b200_kb_rotate": ([_INT], _INT),
     "moe_b200_stage_timing": ([_INT], _INT),
     "moe_b200_stage_times": ([_P, _INT], _INT),
     "moe_b200_select_gemv": ([_INT], _INT),
