@@ -499,6 +499,12 @@ int moe_b200_decode_prologue(int enable);
  * k-blocks from a unit-dependent offset (1) or in order (0, the default);
  * same results to fp32 rounding of the summation order. */
 int moe_b200_kb_rotate(int enable);
+/* No reference counterpart.  Decode layers on the default GEMV stage the
+ * SwiGLU activations inside the gate/up launch and combine the tokens inside
+ * the down launch, by the warp that finishes the last piece each needs (1),
+ * or run the staging and the combine as launches of their own (0, the
+ * default).  Same results bit for bit. */
+int moe_b200_fold_epilogues(int enable);
 
 /* ---------------------------------------------------------------------------
  * Pack-file reads (host only): the FP8 pack loader's byte ranges.

@@ -69,6 +69,10 @@ int g_force_ksplit = 0;
 bool g_decode_prologue = true;
 // Staggered k-block walks in the cp.async warp-MMA stages (MmaArgs::kb_rotate).
 int g_kb_rotate = 0;
+// cp.async decode stages: the activation staging folded into the gate/up GEMV and the combine into the
+// down GEMV (their last-arriving warps), instead of two launches.  Off by default: measured slower from
+// 4 tokens on (a fence and an arrival after every task; 64 tokens: 1.86 against 1.59 ms).
+bool g_fold_epilogues = false;
 
 cudaError_t gemv(const GemvArgs& a, int x_dtype, int ns, int epi, int nt, bool vec, cudaStream_t stream) {
   if (g_gemv_impl == 1 && vec && stream_gemv_supported(a.K, x_dtype, nt))
@@ -788,6 +792,7 @@ struct LayerPlan {
                            // the x staging of every forward
   int64_t n_counters;
   int64_t chunks;          // upper bound on the chunk list's length
+  int64_t comb_tiles;      // 32-column tiles of a hidden row (the folded combine's counters)
   float* partial_fused;    // fused decode: [2 phases][2 x fused_warps][32 x 8] piece slots
   int fused_warps;
   // prefill (tcgen05 grouped GEMM): pair-ordered fp16 activations, their
@@ -840,7 +845,9 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
   l.chunks = chunks;
   if (!lean) {
     l.partial = p.take<float>(part * frag);
-    l.n_counters = l.tasks1 + l.tasks2 + 2 * chunks;
+    // + the combine's per-(token, 32-column tile) arrivals when this is a whole layer
+    l.comb_tiles = ceil_div(H, 32);
+    l.n_counters = l.tasks1 + l.tasks2 + 2 * chunks + (router ? T * l.comb_tiles : 0);
     l.counters = p.take<int32_t>(l.n_counters);
     l.fused_warps = decode_fused_warps();
     l.partial_fused = p.take<float>(static_cast<int64_t>(2) * 2 * l.fused_warps * frag);
@@ -901,11 +908,20 @@ static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16
 
 // The expert stages on the warp-MMA kernel: x and the SwiGLU activations are
 // staged as f16 rows with power-of-two scales.
+// The whole layer's combine, for the down stage to fold in.
+struct LayerCombine {
+  __nv_bfloat16* out;
+  int64_t tokens, k;
+  bool shared;
+};
+
 // x_staged: l.x16 / l.xscale already hold the staged rows and the counters are
-// zero (the decode prologue did both).
+// zero (the decode prologue did both).  comb: the layer's combine, folded into
+// the down stage when the epilogue folds are on (*combined set true then).
 static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, const LayerPlan& l, int64_t T,
                                  int64_t pairs, int64_t n_segments, int64_t I, int64_t H, bool chunks_ready,
-                                 const uint8_t* nan_free, cudaStream_t s, int tiled = 0, bool x_staged = false) {
+                                 const uint8_t* nan_free, cudaStream_t s, int tiled = 0, bool x_staged = false,
+                                 const LayerCombine* comb = nullptr, bool* combined = nullptr) {
   const MlpScratch& m = l.m;
   if (!chunks_ready) {
     ChunkArgs ca{m.seg_offset, static_cast<int>(n_segments), 8, m.chunk_seg, m.chunk_start, m.chunk_len, m.n_chunks};
@@ -945,15 +961,24 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
     stage_mark(s);
     return kOk;
   }
+  // the cp.async kernel can stage the activations and combine the tokens itself (last-arriving warps)
+  const bool fold = g_fold_epilogues && g_mma_feed == 2 && l.counters;
+  if (fold) {
+    g1.stage_x16 = l.act16;
+    g1.stage_scale = l.ascale;
+    g1.chunk_done = l.counters + l.tasks1 + l.tasks2;
+  }
   MOE_CUDA(g_mma_feed == 1   ? launch_tma_mma_gemv(g1, 2, kEpiSwiglu, s)
            : g_mma_feed == 2 ? launch_async_mma_gemv(g1, 2, kEpiSwiglu, l.tasks1, s)
                              : launch_mma_gemv(g1, 2, kEpiSwiglu, l.tasks1, s),
            "gate/up stage");
   stage_mark(s);
-  MOE_CUDA(launch_rows_to_f16(m.act, false, static_cast<int>(pairs), static_cast<int>(I), nullptr, l.act16,
-                              l.ascale, nullptr, 0, s),
-           "stage activations");
-  stage_mark(s);
+  if (!fold) {
+    MOE_CUDA(launch_rows_to_f16(m.act, false, static_cast<int>(pairs), static_cast<int>(I), nullptr, l.act16,
+                                l.ascale, nullptr, 0, s),
+             "stage activations");
+    stage_mark(s);
+  }
   MmaArgs g2 = g1;
   g2.w0 = t.dw; g2.s0 = t.ds; g2.w1 = nullptr; g2.s1 = nullptr;
   g2.x16 = l.act16; g2.xscale = l.ascale; g2.pair_row = nullptr;
@@ -961,6 +986,19 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
   g2.scale_cols = static_cast<int>(ceil_div(I, kBlock));
   g2.ksplit = l.ksplit2;
   g2.counters = l.counters + l.tasks1;
+  g2.stage_x16 = nullptr; g2.stage_scale = nullptr; g2.chunk_done = nullptr;
+  if (fold && comb && comb->out && l.comb_tiles > 0 &&
+      l.n_counters >= l.tasks1 + l.tasks2 + 2 * l.chunks + comb->tokens * l.comb_tiles) {
+    g2.comb_out = comb->out;
+    g2.comb_cnt = l.counters + l.tasks1 + l.tasks2 + 2 * l.chunks;
+    g2.pair_token = m.pair_row;
+    g2.entry_pair = m.entry_pair;
+    g2.pair_weight = m.pair_weight;
+    g2.comb_k = static_cast<int>(comb->k);
+    g2.comb_shared_base = comb->shared ? static_cast<int>(comb->tokens * comb->k) : -1;
+    g2.comb_need = static_cast<int>(comb->k) + (comb->shared ? 1 : 0);
+    if (combined) *combined = true;
+  }
   MOE_CUDA(g_mma_feed == 1   ? launch_tma_mma_gemv(g2, 1, kEpiStore, s)
            : g_mma_feed == 2 ? launch_async_mma_gemv(g2, 1, kEpiStore, l.tasks2, s)
                              : launch_mma_gemv(g2, 1, kEpiStore, l.tasks2, s),
@@ -1014,7 +1052,7 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   ba.block_counts = l.bucket_scratch;
   ChunkArgs ca{l.m.seg_offset, static_cast<int>(S), chunk, l.m.chunk_seg, l.m.chunk_start, l.m.chunk_len,
                l.m.n_chunks};
-  bool chunks_ready = false, x_staged = false;
+  bool chunks_ready = false, x_staged = false, combined = false;
   if (T <= 256 && route_dispatch_smem_bytes(static_cast<int>(T), static_cast<int>(E)) <= 200 * 1024) {
     // decode batches: logits (cluster-reduced, else split-K partials), then
     // selection + dispatch + chunk list in one CTA
@@ -1085,12 +1123,14 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
                                      T * k + (has_shared ? T : 0), S, I,
                                      H, nan_free, s);
   } else if (use_mma) {
+    const LayerCombine lc{reinterpret_cast<__nv_bfloat16*>(out_bf16), T, k, has_shared != 0};
     code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I, H,
-                                 chunks_ready, nan_free, s, weight_layout, x_staged);
+                                 chunks_ready, nan_free, s, weight_layout, x_staged, &lc, &combined);
   } else {
     code = run_expert_stages(t, hidden, xd, l.m, l.m.y, S, I, H, ceil_div(H, kBlock), ceil_div(I, kBlock), nt, vec, s);
   }
   if (code != kOk) return code;
+  if (combined) return kOk;  // the down stage combined the tokens
   // 4. combine: routed slots in top-k order, then the shared expert; one bf16 rounding
   CombineArgs c{};
   c.y = l.m.y; c.row_ptr = nullptr; c.stride = static_cast<int>(k); c.row_pairs = l.m.entry_pair;
@@ -1406,6 +1446,12 @@ int moe_b200_decode_prologue(int enable) {
 int moe_b200_kb_rotate(int enable) {
   if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
   g_kb_rotate = enable;
+  return kOk;
+}
+
+int moe_b200_fold_epilogues(int enable) {
+  if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
+  g_fold_epilogues = enable != 0;
   return kOk;
 }
 

@@ -82,6 +82,23 @@ struct MmaArgs {
   float* partial;            // [tasks * ksplit, 32, 8] fp32 fragments when ksplit > 1
   int32_t* counters;         // [tasks] arrival counters: zero on entry, left zero on exit
   int kb_rotate;             // cp.async kernels: start each unit's k-block walk at a unit-dependent offset
+  // cp.async kernel, gate/up (NS 2) -- fold the activation staging in: the
+  // warp completing a chunk's last task stages its pairs' rows out0 -> f16
+  // (rows_to_f16_kernel's arithmetic).  Null: no staging.
+  __half* stage_x16;         // [P, N]
+  float* stage_scale;        // [P]
+  int32_t* chunk_done;       // [chunks] completed tasks; zero on entry
+  // cp.async kernel, down (NS 1) -- fold the combine in: the warp adding a
+  // token's last pair row to a 32-column tile combines that tile (combine_kernel's
+  // arithmetic: slots in order, then the shared row, one bf16 rounding).  Null: no combine.
+  __nv_bfloat16* comb_out;   // [T, N]
+  int32_t* comb_cnt;         // [T, ceil(N / 32)] arrivals; zero on entry
+  const int32_t* pair_token; // [P] token of each pair
+  const int32_t* entry_pair; // [T * comb_k] pair of each (token, slot), -1 = none
+  const float* pair_weight;  // [P]
+  int comb_k;                // routed slots per token
+  int comb_shared_base;      // >= 0: token t's shared row is pair comb_shared_base + t
+  int comb_need;             // pair rows per token (routed slots kept + the shared one)
 };
 constexpr int kMaxMmaKSplit = 8;
 // Rows of one warp task of the MMA kernels: 16 (gate + up) or 32 (one matrix).

@@ -502,6 +502,53 @@ MOE_D int async_accumulate(float (&acc)[2][4], unsigned char* ring, const UnitOp
   return nx_issued;
 }
 
+// Rows [p0, p0 + len) of src (N fp32 each) -> f16 with a power-of-two row
+// scale, by one warp: rows_to_f16_kernel's arithmetic (the same bits).  The
+// rows were written by other warps of this launch: read from L2.
+MOE_D void stage_rows_f16_warp(const float* src, int p0, int len, int N, __half* dst16, float* scale, int lane) {
+  const int n4 = N / 4;
+  for (int p = p0; p < p0 + len; ++p) {
+    const float4* row = reinterpret_cast<const float4*>(src + static_cast<int64_t>(p) * N);
+    float amax = 0.0f;
+    for (int i0 = lane; i0 < n4; i0 += 8 * kWarp) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = i0 + u * kWarp < n4 ? __ldcg(row + i0 + u * kWarp) : make_float4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+    const float sc = (amax > 0.0f && isfinite(amax)) ? ldexpf(1.0f, ilogbf(amax) - 13) : 1.0f;
+    const float inv = 1.0f / sc;  // exact: power of two
+    __half* dst = dst16 + static_cast<int64_t>(p) * N;
+    for (int i = lane; i < n4; i += kWarp) {
+      const float4 v = __ldcg(row + i);
+      __align__(8) __half h[4] = {__float2half_rn(v.x * inv), __float2half_rn(v.y * inv),
+                                  __float2half_rn(v.z * inv), __float2half_rn(v.w * inv)};
+      *reinterpret_cast<uint2*>(dst + 4 * i) = *reinterpret_cast<const uint2*>(h);
+    }
+    if (lane == 0) scale[p] = sc;
+  }
+}
+
+// Columns [c0, c0 + 32) of token t's combined row, one column per lane:
+// combine_kernel's arithmetic.  The pair rows were written by other warps of
+// this launch: read from L2.
+MOE_D void combine_tile_warp(const MmaArgs& a, const float* y, int t, int c0, int lane) {
+  const int col = c0 + lane;
+  if (col >= a.N) return;
+  float acc = 0.0f;
+  for (int s = 0; s < a.comb_k; ++s) {
+    const int p = a.entry_pair[static_cast<int64_t>(t) * a.comb_k + s];
+    if (p < 0) continue;
+    acc = fmaf(a.pair_weight[p], __ldcg(y + static_cast<int64_t>(p) * a.N + col), acc);
+  }
+  if (a.comb_shared_base >= 0) acc += __ldcg(y + static_cast<int64_t>(a.comb_shared_base + t) * a.N + col);
+  a.comb_out[static_cast<int64_t>(t) * a.N + col] = __float2bfloat16_rn(acc);
+}
+
 template <int NS, int EPI, bool TILED>
 __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(MmaArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -633,6 +680,31 @@ __global__ void __launch_bounds__(kAsyncWarps * kWarp) mma_gemv_async_kernel(Mma
             const int row = r0 + 16 * st + g + 8 * rr;
             if (row < N) a.out0[p * N + row] = acc[st][i] * xs;
           }
+        }
+      }
+    }
+    // folded follow-ups: the activation staging of a finished chunk (gate/up), the combine of
+    // the token tiles this task completed (down)
+    if (NS == 2 && a.chunk_done) {
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(a.chunk_done + ch, 1) == row_tiles - 1;
+      if (__shfl_sync(0xFFFFFFFFu, last, 0)) {
+        __threadfence();
+        stage_rows_f16_warp(a.out0, p0, len, N, a.stage_x16, a.stage_scale, lane);
+      }
+    } else if (NS == 1 && a.comb_out) {
+      __threadfence();
+      __syncwarp();
+      const int tile = r0 / 32, tiles = static_cast<int>(ceil_div(N, 32));
+      for (int j = 0; j < len; ++j) {
+        const int t = a.pair_token[p0 + j];
+        int last = 0;
+        if (lane == 0) last = atomicAdd(a.comb_cnt + static_cast<int64_t>(t) * tiles + tile, 1) == a.comb_need - 1;
+        if (__shfl_sync(0xFFFFFFFFu, last, 0)) {
+          __threadfence();
+          combine_tile_warp(a, a.out0, t, r0, lane);
         }
       }
     }

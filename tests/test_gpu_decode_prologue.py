@@ -74,3 +74,27 @@ def test_rotated_kblock_walk_matches(cuda_device, tokens):
         rotated = _run(gpu, x)[0]
         assert rel_l2(rotated, plain) <= 1e-3
     lib.moe_b200_fused_decode(0)
+
+
+@pytest.mark.parametrize("cfg_name,tokens", [("c1", 1), ("c1", 9), ("c1", 200), ("c2", 1), ("c2", 16), ("c2", 64)])
+def test_folded_staging_and_combine_are_bit_identical(cuda_device, cfg_name, tokens):
+    """The activation staging folded into the gate/up launch and the combine
+    into the down launch (moe_b200_fold_epilogues(1)) against their own
+    launches (0, the default): the same bits, eager and graph-replayed."""
+    cfg = synth.C1_TINY if cfg_name == "c1" else synth.C2_DSV3
+    layer = synth.make_fp8_layer(cfg, seed=700 + tokens, device="cuda")
+    gpu = DsMoELayerGPU(layer)
+    lib = native.load_library()
+    x = synth.make_hidden(tokens, cfg.hidden, seed=701 + tokens, device="cuda")
+    try:
+        lib.moe_b200_fold_epilogues(1)
+        a = _run(gpu, x)
+        graphed = gpu.capture(tokens)
+        replayed = graphed(x).clone()
+        lib.moe_b200_fold_epilogues(0)
+        b = _run(gpu, x)
+    finally:
+        lib.moe_b200_fold_epilogues(0)
+    for u, v in zip(a, b):
+        assert torch.equal(u, v)
+    assert torch.equal(replayed, a[0])
