@@ -889,6 +889,7 @@ def run_stack(args, rank: int, world: int) -> dict | None:
     per_rank = cfg.n_routed // world
     steps = max(3, min(args.steps, 20))
     sweep = {}
+    stack_parity: dict = {}
     with ClockSampler(dev.index) as clocks:
         for B in batches:
             T = stack_share(B, rank, world)
@@ -911,6 +912,20 @@ def run_stack(args, rank: int, world: int) -> dict | None:
             stack.forward(x, ids_out=ids_per_layer)
             gathered = [None] * world
             dist.all_gather_object(gathered, [i.cpu() for i in ids_per_layer])
+            # the checker on layer 0 (every rank takes its collective steps; ranks with tokens check them):
+            # the experts its tokens selected, regenerated from their own seeded generators, against the oracle
+            out0, ids0, _w0 = stack.layers[0].forward(x)
+            rep = None
+            if not args.no_parity and T > 0:
+                need = sorted({int(v) for v in ids0.reshape(-1).tolist()}) + [cfg.n_routed]
+                ref_layer = synth.make_fp8_layer(cfg, seed=args.seed, device=dev, experts=need)
+                rep = parity_leg("fp8_layer_parity", ref_layer, x, out0, ids0)
+                del ref_layer
+            reps = [None] * world
+            dist.all_gather_object(reps, rep)
+            for r, one in enumerate(reps):
+                if one is not None:
+                    stack_parity[f"c5-stack-layer0-B{B}-rank{r}"] = one
             crit = stack_critical_bytes(gathered, per_rank, expert_bytes, router_bytes)
             achieved = crit / (ms / 1e3) / 1e9
             sweep[str(B)] = {
@@ -953,6 +968,12 @@ def run_stack(args, rank: int, world: int) -> dict | None:
                 "d2h_bytes_per_step": stack_share(batches[0], 0, world) * cfg.hidden * 2},
         "exchange": "peer-memory (symmetric memory, NVLink stores), one buffer set for all layers",
         "sweep": sweep, "cpu_baseline": cpu, "clocks": clock_info,
+        "parity": None if args.no_parity else {
+            "gate": {"rel_l2": 2e-2, "cos_dist": 1e-3, "ids": "bit-exact, ties within 1e-6 excused"},
+            "scope": "layer 0 of the stack on each rank's tokens (the whole stack is checked layer by layer "
+                     "against the oracle in tests/test_gpu_stack.py)",
+            "all_pass": bool(stack_parity) and all(r.get("pass") for r in stack_parity.values()),
+            "cases": stack_parity},
     }
 
 

@@ -505,6 +505,16 @@ int moe_b200_kb_rotate(int enable);
  * or run the staging and the combine as launches of their own (0, the
  * default).  Same results bit for bit. */
 int moe_b200_fold_epilogues(int enable);
+/* No reference counterpart.  Decode layers (tiled weights, the default GEMV)
+ * run the shared expert -- which needs no routing -- on a side stream that
+ * forks where the layer starts and joins before the combine, on two CTAs per
+ * SM, while the router and the dispatch run (1); 0, the default, runs it
+ * with the routed experts.  Same results to fp32 rounding (the side launches split
+ * the shared expert's k-blocks for their smaller grid).  The side stream of a
+ * device is created by its first such call, which should come before any
+ * stream capture; layers captured in a graph must not run concurrently with
+ * eager layers on the same device (they share the side stream). */
+int moe_b200_shared_side(int enable);
 
 /* ---------------------------------------------------------------------------
  * Pack-file reads (host only): the FP8 pack loader's byte ranges.

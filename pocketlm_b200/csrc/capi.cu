@@ -5,6 +5,7 @@
 // plans its scratch memory, and enqueues the kernels on the caller's stream.
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "../../include/moe_b200.h"
@@ -73,6 +74,15 @@ int g_kb_rotate = 0;
 // down GEMV (their last-arriving warps), instead of two launches.  Off by default: measured slower from
 // 4 tokens on (a fence and an arrival after every task; 64 tokens: 1.86 against 1.59 ms).
 bool g_fold_epilogues = false;
+// Decode layers (warp-MMA experts, tiled weights): the shared expert -- which needs no routing -- runs on
+// a side stream while the router and the dispatch run, on part of the GPU, instead of with the routed
+// experts.  Off by default: at one token the routed stages got 6 us faster but the router and dispatch,
+// sharing the SMs with the side launches, 11 us slower; the shared expert's own k-split also makes the
+// output differ from the one-stream layer in the last bf16 bit.
+bool g_shared_side = false;
+// CTAs per SM the side stream's expert launches may take (the router's clusters and the dispatch CTA
+// keep the rest).
+constexpr int kSharedSideCtasPerSm = 2;
 
 cudaError_t gemv(const GemvArgs& a, int x_dtype, int ns, int epi, int nt, bool vec, cudaStream_t stream) {
   if (g_gemv_impl == 1 && vec && stream_gemv_supported(a.K, x_dtype, nt))
@@ -486,6 +496,49 @@ __global__ void ep_pairs_home_kernel(const float* y, const int32_t* n_pairs, con
   __threadfence_system();
 }
 
+namespace {
+
+// The shared expert's chunk list for the side stream: its pairs first .. first
+// + T - 1 (token t's is first + t) in chunks of <= 8, and their token rows.
+__global__ void shared_chunks_kernel(int32_t* seg, int32_t* start, int32_t* len, int32_t* n, int32_t* rows,
+                                     int shared_index, int first, int T) {
+  const int nch = (T + 7) / 8;
+  for (int i = threadIdx.x; i < nch; i += blockDim.x) {
+    seg[i] = shared_index;
+    start[i] = first + 8 * i;
+    len[i] = min(8, T - 8 * i);
+  }
+  for (int i = threadIdx.x; i < T; i += blockDim.x) rows[i] = i;
+  if (threadIdx.x == 0) *n = nch;
+}
+
+// A non-blocking side stream and its fork / join events, one set per device,
+// created on first use (the first call on a device should come before any
+// stream capture).
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_side_mutex;
+SideStream g_side[64];
+
+int side_stream(SideStream** out) {
+  int dev = 0;
+  MOE_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(kUnsupported, "side stream: device index beyond 64");
+  std::lock_guard<std::mutex> lock(g_side_mutex);
+  SideStream& sd = g_side[dev];
+  if (!sd.s) {
+    MOE_CUDA(cudaStreamCreateWithFlags(&sd.s, cudaStreamNonBlocking), "side stream");
+    MOE_CUDA(cudaEventCreateWithFlags(&sd.fork, cudaEventDisableTiming), "fork event");
+    MOE_CUDA(cudaEventCreateWithFlags(&sd.join, cudaEventDisableTiming), "join event");
+  }
+  *out = &sd;
+  return kOk;
+}
+
+}  // namespace
+
 extern "C" {
 
 int moe_b200_abi_version(void) { return MOE_B200_ABI_VERSION; }
@@ -793,6 +846,19 @@ struct LayerPlan {
   int64_t n_counters;
   int64_t chunks;          // upper bound on the chunk list's length
   int64_t comb_tiles;      // 32-column tiles of a hidden row (the folded combine's counters)
+  // the shared expert on a side stream (decode layers): its staged x rows, chunk list, split-K state
+  __half* sh_x16;
+  float* sh_xscale;
+  int32_t* sh_rows;        // [T] token of the shared pair first + t: t
+  int32_t* sh_chunk_seg;
+  int32_t* sh_chunk_start;
+  int32_t* sh_chunk_len;
+  int32_t* sh_n_chunks;
+  float* sh_partial;
+  int32_t* sh_counters;    // [sh_tasks1 + sh_tasks2], zeroed by the side stream's x staging
+  int64_t sh_tasks1, sh_tasks2, sh_n_counters;
+  int sh_ks1, sh_ks2;
+  int64_t sh_ctas;
   float* partial_fused;    // fused decode: [2 phases][2 x fused_warps][32 x 8] piece slots
   int fused_warps;
   // prefill (tcgen05 grouped GEMM): pair-ordered fp16 activations, their
@@ -851,6 +917,25 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
     l.counters = p.take<int32_t>(l.n_counters);
     l.fused_warps = decode_fused_warps();
     l.partial_fused = p.take<float>(static_cast<int64_t>(2) * 2 * l.fused_warps * frag);
+    if (router && shared) {
+      const int64_t sh_chunks = ceil_div(T, 8);
+      l.sh_x16 = p.take<__half>(T * H);
+      l.sh_xscale = p.take<float>(T);
+      l.sh_rows = p.take<int32_t>(T);
+      l.sh_chunk_seg = p.take<int32_t>(sh_chunks);
+      l.sh_chunk_start = p.take<int32_t>(sh_chunks);
+      l.sh_chunk_len = p.take<int32_t>(sh_chunks);
+      l.sh_n_chunks = p.take<int32_t>(1);
+      l.sh_tasks1 = sh_chunks * ceil_div(I, mma_task_rows(2));
+      l.sh_tasks2 = sh_chunks * ceil_div(H, mma_task_rows(1));
+      l.sh_ctas = static_cast<int64_t>(gemv_grid_ctas()) *
+                  std::min(kSharedSideCtasPerSm, std::max(1, async_gemv_ctas_per_sm() - 1));
+      l.sh_ks1 = async_gemv_ksplit_for(l.sh_tasks1, static_cast<int>(H), l.sh_ctas);
+      l.sh_ks2 = async_gemv_ksplit_for(l.sh_tasks2, static_cast<int>(I), l.sh_ctas);
+      l.sh_partial = p.take<float>(std::max(l.sh_tasks1 * l.sh_ks1, l.sh_tasks2 * l.sh_ks2) * frag);
+      l.sh_n_counters = l.sh_tasks1 + l.sh_tasks2;
+      l.sh_counters = p.take<int32_t>(l.sh_n_counters);
+    }
   }
   // the tcgen05 GEMM's pair rows: layers (router) and expert-parallel experts (rows) alike
   if (T >= kPrefillMinTokens) {
@@ -1007,6 +1092,57 @@ static int run_expert_stages_mma(const Tables& t, const void* x, bool x_bf16, co
   return kOk;
 }
 
+// The shared expert of a decode layer on the side stream: x staging, its chunk
+// list, gate/up + SwiGLU, activation staging and down for its pairs
+// T*k .. T*k + T - 1, on kSharedSideCtasPerSm CTAs per SM, with a k-split
+// sized for that grid (so its sums group the k-blocks differently from a
+// launch over the whole GPU).  It forks from `s` where the layer starts and is
+// joined before the combine.  Concurrent layers on one device share the side
+// stream: their shared-expert work runs in the order the layers forked.
+static int run_shared_side(const Tables& t, const void* x, bool x_bf16, const LayerPlan& l, int64_t T, int64_t k,
+                           int64_t E, int64_t I, int64_t H, const uint8_t* nan_free, int tiled, cudaStream_t s,
+                           SideStream* side) {
+  const MlpScratch& m = l.m;
+  const int64_t first = T * k;
+  {
+    // record and wait as one step: another host thread's layer records the same fork event
+    std::lock_guard<std::mutex> lock(g_side_mutex);
+    MOE_CUDA(cudaEventRecord(side->fork, s), "fork");
+    MOE_CUDA(cudaStreamWaitEvent(side->s, side->fork, 0), "fork wait");
+  }
+  cudaStream_t ss = side->s;
+  MOE_CUDA(launch_rows_to_f16(x, x_bf16, static_cast<int>(T), static_cast<int>(H), nullptr, l.sh_x16, l.sh_xscale,
+                              l.sh_counters, l.sh_n_counters, ss),
+           "shared x");
+  shared_chunks_kernel<<<1, 64, 0, ss>>>(l.sh_chunk_seg, l.sh_chunk_start, l.sh_chunk_len, l.sh_n_chunks, l.sh_rows,
+                                         static_cast<int>(E), static_cast<int>(first), static_cast<int>(T));
+  MOE_CUDA(cudaGetLastError(), "shared chunks");
+  MmaArgs g1{};
+  g1.w0 = t.gw; g1.s0 = t.gs; g1.w1 = t.uw; g1.s1 = t.us;
+  // pair first + t reads x row t: the pair-row table is indexed from `first` on (only valid pairs read it)
+  g1.x16 = l.sh_x16; g1.xscale = l.sh_xscale;
+  g1.pair_row = reinterpret_cast<const int32_t*>(reinterpret_cast<uintptr_t>(l.sh_rows) - first * sizeof(int32_t));
+  g1.chunk_seg = l.sh_chunk_seg; g1.chunk_start = l.sh_chunk_start; g1.chunk_len = l.sh_chunk_len;
+  g1.n_chunks = l.sh_n_chunks;
+  g1.out0 = m.act; g1.N = static_cast<int>(I); g1.K = static_cast<int>(H);
+  g1.scale_cols = static_cast<int>(ceil_div(H, kBlock)); g1.nanfix = 1;
+  g1.ksplit = l.sh_ks1; g1.partial = l.sh_partial; g1.counters = l.sh_counters; g1.nan_free = nan_free;
+  g1.tiled = tiled;
+  MOE_CUDA(launch_async_mma_gemv(g1, 2, kEpiSwiglu, l.sh_tasks1, ss, l.sh_ctas), "shared gate/up");
+  MOE_CUDA(launch_rows_to_f16(m.act + first * I, false, static_cast<int>(T), static_cast<int>(I), nullptr,
+                              l.act16 + first * I, l.ascale + first, nullptr, 0, ss),
+           "shared activations");
+  MmaArgs g2 = g1;
+  g2.w0 = t.dw; g2.s0 = t.ds; g2.w1 = nullptr; g2.s1 = nullptr;
+  g2.x16 = l.act16; g2.xscale = l.ascale; g2.pair_row = nullptr;
+  g2.out0 = m.y; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
+  g2.scale_cols = static_cast<int>(ceil_div(I, kBlock));
+  g2.ksplit = l.sh_ks2; g2.counters = l.sh_counters + l.sh_tasks1;
+  MOE_CUDA(launch_async_mma_gemv(g2, 1, kEpiStore, l.sh_tasks2, ss, l.sh_ctas), "shared down");
+  MOE_CUDA(cudaEventRecord(side->join, ss), "join");
+  return kOk;
+}
+
 int64_t moe_ds_moe_layer_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, int shared) {
   Plan p;
   plan_layer(p, T, H, I, E, k, shared, 1);
@@ -1044,13 +1180,25 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   if (weight_layout == 1 && !(use_mma && g_mma_feed == 2))
     return fail(kUnsupported, "tiled weights need the cp.async warp-MMA GEMV (hidden, intermediate % 128 == 0)");
   const int chunk = use_mma ? 8 : nt;
+  // the shared expert on the side stream (decode batches on the cp.async warp-MMA GEMV)
+  SideStream* side = nullptr;
+  if (g_shared_side && !g_fused_decode && !g_fold_epilogues && use_mma && g_mma_feed == 2 && weight_layout == 1 &&
+      has_shared && l.sh_x16 && T < kPrefillMinTokens && (hidden_dtype == kDtypeBF16 || hidden_dtype == kDtypeF32)) {
+    code = side_stream(&side);
+    if (code != kOk) return code;
+    Tables st{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
+    code = run_shared_side(st, hidden, hidden_dtype == kDtypeBF16, l, T, k, E, I, H, nan_free, weight_layout, s, side);
+    if (code != kOk) return code;
+  }
+  // the main stream's expert segments: the routed experts, plus the shared one unless the side stream has it
+  const int64_t S_main = side ? S - 1 : S;
   BucketArgs ba{};
   ba.keys = l.ids32; ba.rows = nullptr; ba.weights = l.wts; ba.n = static_cast<int>(T * k);
   ba.k = static_cast<int>(k); ba.key_lo = 0; ba.n_buckets = static_cast<int>(E);
   ba.bucket_offset = l.m.seg_offset; ba.pair_row = l.m.pair_row; ba.pair_weight = l.m.pair_weight;
   ba.pair_entry = l.m.pair_entry; ba.entry_pair = l.m.entry_pair; ba.tail = has_shared ? static_cast<int>(T) : 0;
   ba.block_counts = l.bucket_scratch;
-  ChunkArgs ca{l.m.seg_offset, static_cast<int>(S), chunk, l.m.chunk_seg, l.m.chunk_start, l.m.chunk_len,
+  ChunkArgs ca{l.m.seg_offset, static_cast<int>(S_main), chunk, l.m.chunk_seg, l.m.chunk_start, l.m.chunk_len,
                l.m.n_chunks};
   bool chunks_ready = false, x_staged = false, combined = false;
   if (T <= 256 && route_dispatch_smem_bytes(static_cast<int>(T), static_cast<int>(E)) <= 200 * 1024) {
@@ -1088,7 +1236,7 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
     rd.chunks = ca;
     if (g_decode_prologue && use_mma && nparts == 1 && l.x16 &&
         decode_prologue_supported(static_cast<int>(T), static_cast<int>(E), static_cast<int>(k), static_cast<int>(H),
-                                  hidden_dtype, hidden, static_cast<int>(S))) {
+                                  hidden_dtype, hidden, static_cast<int>(S_main))) {
       // selection, dispatch, chunk list, x staging and counter reset in one CTA
       DecodePrologueArgs dp{};
       dp.rd = rd;
@@ -1124,13 +1272,16 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
                                      H, nan_free, s);
   } else if (use_mma) {
     const LayerCombine lc{reinterpret_cast<__nv_bfloat16*>(out_bf16), T, k, has_shared != 0};
-    code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T, T * k + (has_shared ? T : 0), S, I, H,
-                                 chunks_ready, nan_free, s, weight_layout, x_staged, &lc, &combined);
+    // with the side stream, the main stream stages only the routed pairs' activations
+    code = run_expert_stages_mma(t, hidden, hidden_dtype == kDtypeBF16, l, T,
+                                 T * k + (has_shared && !side ? T : 0), S_main, I, H, chunks_ready, nan_free, s,
+                                 weight_layout, x_staged, &lc, &combined);
   } else {
     code = run_expert_stages(t, hidden, xd, l.m, l.m.y, S, I, H, ceil_div(H, kBlock), ceil_div(I, kBlock), nt, vec, s);
   }
   if (code != kOk) return code;
   if (combined) return kOk;  // the down stage combined the tokens
+  if (side) MOE_CUDA(cudaStreamWaitEvent(s, side->join, 0), "join wait");  // the shared expert's rows
   // 4. combine: routed slots in top-k order, then the shared expert; one bf16 rounding
   CombineArgs c{};
   c.y = l.m.y; c.row_ptr = nullptr; c.stride = static_cast<int>(k); c.row_pairs = l.m.entry_pair;
@@ -1452,6 +1603,12 @@ int moe_b200_kb_rotate(int enable) {
 int moe_b200_fold_epilogues(int enable) {
   if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
   g_fold_epilogues = enable != 0;
+  return kOk;
+}
+
+int moe_b200_shared_side(int enable) {
+  if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
+  g_shared_side = enable != 0;
   return kOk;
 }
 

@@ -42,25 +42,6 @@ namespace moe {
 
 constexpr int kDenseCtaWarps = 4;
 constexpr int kDenseSpanBytes = 64;  // bytes of one row per 4 lanes c
-// Activations of the MMA GEMV go through a per-warp shared-memory ring of
-// cp.async copies, issued with the weight loads of the same spans one buffer
-// ahead: 4 span slots x 32 lanes x 64 bytes (int4: 32 activations of token g;
-// 16-bit weights: 8, plus 8 of the bf16 lo plane).
-constexpr int kDenseActSlots = 4;
-constexpr int kDenseActLaneBytes = 64;
-constexpr int kDenseActSmem = kDenseCtaWarps * kDenseActSlots * kWarp * kDenseActLaneBytes;
-
-MOE_D void dense_cp_async16(void* smem, const void* gmem, int src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
-                   static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
-               "l"(gmem), "r"(src_bytes)
-               : "memory");
-}
-MOE_D void dense_cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-MOE_D void dense_cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 // weights per row span: 32 16-bit values or 128 int4 codes
 inline int span_weights(int kind) { return kind == kWQ4 ? 128 : 32; }
@@ -105,9 +86,7 @@ MOE_D uint4 ld_weights(const uint8_t* p) { return __ldcs(reinterpret_cast<const 
 
 template <int KIND, int NS, int EPI>
 __global__ void __launch_bounds__(kDenseCtaWarps * kWarp) dense_mma_gemv_kernel(DenseArgs a) {
-  __shared__ __align__(16) unsigned char act_smem[kDenseActSmem];
   constexpr int kMmaType = KIND == kWBF16 ? 1 : 0;
-  unsigned char* const act_ring = act_smem + (threadIdx.x / kWarp) * (kDenseActSlots * kWarp * kDenseActLaneBytes);
   constexpr int kTaskRows = NS == 2 ? 16 : 32;
   const int lane = threadIdx.x % kWarp;
   const int g = lane / 4, c = lane % 4;
@@ -153,11 +132,6 @@ __global__ void __launch_bounds__(kDenseCtaWarps * kWarp) dense_mma_gemv_kernel(
 
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     if (present && sp0 < sp1) {
-      // this lane's activation slot of span sp in the warp's ring
-      auto act_slot = [&](int sp) {
-        return act_ring + ((sp % kDenseActSlots) * kWarp + lane) * kDenseActLaneBytes;
-      };
-      // weights of spans sp, sp + 1 into registers, their activations into the ring (one cp.async group)
       auto load = [&](uint4 (&buf)[2][2][2], int sp) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -166,28 +140,15 @@ __global__ void __launch_bounds__(kDenseCtaWarps * kWarp) dense_mma_gemv_kernel(
           for (int st = 0; st < 2; ++st)
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr) buf[h][st][rr] = ld_weights(arow[st][rr] + s * kDenseSpanBytes);
-          if (sp + h < sp1) {
-            unsigned char* dst = act_slot(sp + h);
-            const int bytes = bvalid ? 16 : 0;  // an absent token row reads nothing and is zero-filled
-            if (KIND == kWQ4) {
-              const uint16_t* src = xb + (sp + h) * 128 + 32 * c;
-#pragma unroll
-              for (int j = 0; j < 4; ++j) dense_cp_async16(dst + 16 * j, src + 8 * j, bytes);
-            } else {
-              const int k0 = (sp + h) * 32;
-              dense_cp_async16(dst, xb + k0 + 8 * c, bytes);
-              if (KIND == kWBF16) dense_cp_async16(dst + 16, xb + a.plane + k0 + 8 * c, bytes);
-            }
-          }
         }
-        dense_cp_async_commit();
       };
       auto compute = [&](const uint4 (&a4)[2][2], int sp) {
-        const unsigned char* slot = act_slot(sp);
+        const int k0 = sp * (KIND == kWQ4 ? 128 : 32);
         if (KIND == kWQ4) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint4 b = *reinterpret_cast<const uint4*>(slot + 16 * j);
+            const uint4 b = bvalid ? __ldg(reinterpret_cast<const uint4*>(xb + k0 + 32 * c + 8 * j))
+                                   : make_uint4(0, 0, 0, 0);
 #pragma unroll
             for (int st = 0; st < 2; ++st) {
               uint32_t hg[4], hh[4];
@@ -198,14 +159,15 @@ __global__ void __launch_bounds__(kDenseCtaWarps * kWarp) dense_mma_gemv_kernel(
             }
           }
         } else {
-          const uint4 b = *reinterpret_cast<const uint4*>(slot);
+          const uint4 b = bvalid ? __ldg(reinterpret_cast<const uint4*>(xb + k0 + 8 * c)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
           for (int st = 0; st < 2; ++st) {
             mma_m16n8k16<kMmaType>(acc[st], a4[st][0].x, a4[st][1].x, a4[st][0].y, a4[st][1].y, b.x, b.y);
             mma_m16n8k16<kMmaType>(acc[st], a4[st][0].z, a4[st][1].z, a4[st][0].w, a4[st][1].w, b.z, b.w);
           }
           if (KIND == kWBF16) {
-            const uint4 lo = *reinterpret_cast<const uint4*>(slot + 16);
+            const uint4 lo = bvalid ? __ldg(reinterpret_cast<const uint4*>(xb + a.plane + k0 + 8 * c))
+                                    : make_uint4(0, 0, 0, 0);
 #pragma unroll
             for (int st = 0; st < 2; ++st) {
               mma_m16n8k16<kMmaType>(acc[st], a4[st][0].x, a4[st][1].x, a4[st][0].y, a4[st][1].y, lo.x, lo.y);
@@ -215,29 +177,19 @@ __global__ void __launch_bounds__(kDenseCtaWarps * kWarp) dense_mma_gemv_kernel(
         }
       };
       // ping-pong buffers of two spans each: the next two spans' weight loads
-      // and activation copies are in flight while the current two are multiplied
+      // are in flight while the current two are multiplied
       uint4 bufA[2][2][2], bufB[2][2][2];
       load(bufA, sp0);
       for (int sp = sp0; sp < sp1; sp += 4) {
-        const bool more = sp + 2 < sp1;
-        if (more) load(bufB, sp + 2);
-        // bufA's activation group has landed (bufB's may still be in flight)
-        if (more) dense_cp_async_wait<1>(); else dense_cp_async_wait<0>();
-        __syncwarp();
+        if (sp + 2 < sp1) load(bufB, sp + 2);
         compute(bufA[0], sp);
         if (sp + 1 < sp1) compute(bufA[1], sp + 1);
-        if (more) {
-          __syncwarp();  // the ring slots of spans sp, sp + 1 are free before the next group reuses them
-          const bool more2 = sp + 4 < sp1;
-          if (more2) load(bufA, sp + 4);
-          if (more2) dense_cp_async_wait<1>(); else dense_cp_async_wait<0>();
-          __syncwarp();
+        if (sp + 2 < sp1) {
+          if (sp + 4 < sp1) load(bufA, sp + 4);
           compute(bufB[0], sp + 2);
           if (sp + 3 < sp1) compute(bufB[1], sp + 3);
-          __syncwarp();
         }
       }
-      dense_cp_async_wait<0>();
     }
 
     if (ksplit > 1) {

@@ -111,7 +111,12 @@ cudaError_t launch_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bou
 // Same computation, weights staged through a per-warp shared-memory ring by
 // cp.async (fp8_mma.cu); tasks_bound as for launch_mma_gemv.
 int async_gemv_ksplit(int64_t tasks_bound, int K);
-cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream);
+// Resident CTAs per SM of the cp.async kernel, and its k-split for a grid of `ctas` CTAs.
+int async_gemv_ctas_per_sm();
+int async_gemv_ksplit_for(int64_t tasks_bound, int K, int64_t ctas);
+// max_ctas > 0 caps the grid (a launch that shares the GPU with another stream's kernels).
+cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream,
+                                  int64_t max_ctas = 0);
 // Fused decode experts (decode_fused_kernel, tiled or row-major weights): the
 // gate/up + SwiGLU stage (up), the f16 staging of its activations and the down
 // stage (down) in one persistent launch.  up.out0 = act fp32 [P, I]; down.x16 /

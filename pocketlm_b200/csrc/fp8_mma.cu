@@ -1425,10 +1425,18 @@ int async_gemv_ksplit(int64_t tasks_bound, int K) {
   return balanced_ksplit(tasks_bound, warps, K);
 }
 
-cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream) {
+int async_gemv_ctas_per_sm() { return async_ctas_per_sm(); }
+
+int async_gemv_ksplit_for(int64_t tasks_bound, int K, int64_t ctas) {
+  return balanced_ksplit(tasks_bound, std::max<int64_t>(1, ctas) * kAsyncWarps, K);
+}
+
+cudaError_t launch_async_mma_gemv(const MmaArgs& a, int ns, int epi, int64_t tasks_bound, cudaStream_t stream,
+                                  int64_t max_ctas) {
   if (a.ksplit < 1 || a.ksplit > kMaxMmaKSplit || (a.ksplit > 1 && (!a.partial || !a.counters)))
     return cudaErrorInvalidValue;
-  const int64_t full = static_cast<int64_t>(gemv_grid_ctas()) * async_ctas_per_sm();
+  int64_t full = static_cast<int64_t>(gemv_grid_ctas()) * async_ctas_per_sm();
+  if (max_ctas > 0) full = std::min(full, max_ctas);
   const int64_t need = ceil_div(std::max<int64_t>(1, tasks_bound) * a.ksplit, kAsyncWarps);
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(full, need)));
   auto kernel = ns == 2 ? (a.tiled ? mma_gemv_async_kernel<2, kEpiSwiglu, true> : mma_gemv_async_kernel<2, kEpiSwiglu, false>)

@@ -142,6 +142,7 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_b200_decode_prologue": ([_INT], _INT),
     "moe_b200_kb_rotate": ([_INT], _INT),
     "moe_b200_fold_epilogues": ([_INT], _INT),
+    "moe_b200_shared_side": ([_INT], _INT),
     "moe_b200_stage_timing": ([_INT], _INT),
     "moe_b200_stage_times": ([_P, _INT], _INT),
     "moe_b200_select_gemv": ([_INT], _INT),

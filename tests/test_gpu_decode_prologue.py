@@ -98,3 +98,35 @@ def test_folded_staging_and_combine_are_bit_identical(cuda_device, cfg_name, tok
     for u, v in zip(a, b):
         assert torch.equal(u, v)
     assert torch.equal(replayed, a[0])
+
+
+@pytest.mark.parametrize("cfg_name,tokens", [("c1", 1), ("c1", 12), ("c2", 1), ("c2", 4), ("c2", 64)])
+def test_shared_expert_side_stream(cuda_device, cfg_name, tokens):
+    """The shared expert on the side stream (moe_b200_shared_side(1)) against
+    the one-stream layer (0, the default): the same routing, outputs to
+    bf16 rounding of a different k-split grouping; graph replay with the
+    fork / join captured gives the eager bits; the oracle's gate holds."""
+    import oracle
+    from tests.parity import COS_GATE, REL_L2_GATE, cos_dist, id_mismatches
+
+    cfg = synth.C1_TINY if cfg_name == "c1" else synth.C2_DSV3
+    layer = synth.make_fp8_layer(cfg, seed=800 + tokens, device="cuda")
+    gpu = DsMoELayerGPU(layer)
+    lib = native.load_library()
+    x = synth.make_hidden(tokens, cfg.hidden, seed=801 + tokens, device="cuda")
+    try:
+        lib.moe_b200_shared_side(1)
+        side = _run(gpu, x)
+        graphed = gpu.capture(tokens)
+        replayed = [graphed(x).clone() for _ in range(2)]
+        lib.moe_b200_shared_side(0)
+        single = _run(gpu, x)
+    finally:
+        lib.moe_b200_shared_side(0)
+    assert torch.equal(side[1], single[1]) and torch.equal(side[2], single[2])
+    assert rel_l2(side[0], single[0]) <= 1e-3
+    assert all(torch.equal(r, side[0]) for r in replayed)
+    expected, route = oracle.ds_moe_layer(x.cpu(), layer)
+    bad, excused = id_mismatches(side[1], route)
+    assert bad == excused
+    assert rel_l2(side[0], expected) <= REL_L2_GATE and cos_dist(side[0], expected) <= COS_GATE
