@@ -366,6 +366,23 @@ int64_t moe_ep_experts_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t
 int moe_ep_combine(const float* y, const int32_t* entry_pos, const float* pos_weight, int64_t tokens, int64_t top_k,
                    int64_t hidden_dim, int has_shared, uint16_t* out_bf16, void* stream);
 
+/* No reference counterpart (the reference runs on one host; its ranks do not
+ * exist).  A barrier of the expert-parallel ranks over peer memory, in place
+ * of a collective: peer_sig [world] holds every rank's signal buffer (world
+ * uint32 slots, zero before the first barrier; torch symmetric memory), epoch
+ * this rank's device counter (zero at first; one increment per barrier).  Each
+ * rank stores its epoch into slot [rank] of every peer's buffer after a
+ * system-scope fence -- so everything it stored to peer memory before is
+ * visible first -- and waits for every peer's epoch in its own slots, at most
+ * limit_us microseconds; with payload (payload_n int32, device memory), that
+ * row is first copied into row `rank` of every peer's peer_payload buffer (an
+ * all-gather).  A wait that runs out sets code 256 in moe_b200_device_error,
+ * after which barriers stop waiting until the code is read.  One launch of
+ * one CTA; every rank must call it the same number of times. */
+int moe_ep_barrier_p2p(const uint64_t* peer_sig, int64_t world, int64_t rank, uint32_t* epoch,
+                       const int32_t* payload, int64_t payload_n, const uint64_t* peer_payload, int64_t limit_us,
+                       void* stream);
+
 /* The exchange without collectives on the data path: every rank keeps
  * receive buffers in peer-accessible memory (e.g. torch symmetric memory) --
  * rows [capacity (+ own rows), hidden] bf16, expert int32 [capacity] (-1 =
@@ -386,7 +403,8 @@ int moe_ep_combine(const float* y, const int32_t* entry_pos, const float* pos_we
  *   (tokens * top_k, or tokens * (top_k + 1) when the rank's own shared-expert
  *   rows go through the same call with e = tokens * top_k + t); capacity >=
  *   the rows any rank receives (world * tokens * top_k suffices).  The
- *   barriers are the caller's (any stream-ordered collective).  Same
+ *   barriers are the caller's: moe_ep_barrier_p2p (its payload carrying the
+ *   counts for the all-gather) or any stream-ordered collective.  Same
  *   arithmetic and combine order as the all-to-all exchange above. */
 int moe_ep_count_ranks(const int64_t* ids, int64_t tokens, int64_t top_k, int64_t num_experts, int64_t world,
                        int32_t* counts, void* stream);
@@ -515,6 +533,11 @@ int moe_b200_fold_epilogues(int enable);
  * stream capture; layers captured in a graph must not run concurrently with
  * eager layers on the same device (they share the side stream). */
 int moe_b200_shared_side(int enable);
+/* No reference counterpart.  Decode layers with the one-CTA prologue and bf16
+ * hidden states: the router logits launch stages x as f16 with a row scale in
+ * a cluster of its own, beside the logits clusters (1, the default), or the
+ * prologue stages it (0).  Same results bit for bit. */
+int moe_b200_router_stages_x(int enable);
 
 /* ---------------------------------------------------------------------------
  * Pack-file reads (host only): the FP8 pack loader's byte ranges.

@@ -27,11 +27,11 @@ def cos_dist(actual: torch.Tensor, expected: torch.Tensor) -> float:
     return float(1.0 - torch.dot(a, e) / (a.norm() * e.norm()).clamp_min(1e-30))
 
 
-def id_mismatches(ids: torch.Tensor, route, tol: float = TIE_TOL):
-    """(mismatching tokens, of which excused as ties) against an oracle
-    RouteResult.  Selections compare as sets; a differing set is excused when
-    the oracle's expert boundary gap (k-th pick minus best other) or its group
-    boundary gap is within `tol`."""
+def tie_tokens(ids: torch.Tensor, route, tol: float = TIE_TOL) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per token (bool [T] masks): the GPU's selection differs from the
+    oracle's RouteResult as a set, and such a difference is excused because
+    the oracle's expert boundary gap (k-th pick minus best other) or its
+    group boundary gap is within `tol`."""
     from .router import boundary_gap
 
     a = torch.sort(ids.detach().cpu(), dim=1).values
@@ -40,7 +40,13 @@ def id_mismatches(ids: torch.Tensor, route, tol: float = TIE_TOL):
     near = boundary_gap(route.choice, route.ids) <= tol
     if route.group_gap is not None:
         near = near | (route.group_gap <= tol)
-    excused = bad & near
+    return bad, bad & near
+
+
+def id_mismatches(ids: torch.Tensor, route, tol: float = TIE_TOL):
+    """(mismatching tokens, of which excused as ties) against an oracle
+    RouteResult (tie_tokens, counted)."""
+    bad, excused = tie_tokens(ids, route, tol)
     return int(bad.sum()), int(excused.sum())
 
 
@@ -81,22 +87,32 @@ def fp8_layer_parity(layer, x: torch.Tensor, out: torch.Tensor, ids: torch.Tenso
     (all when None) against the oracle's run_fp8_moe flow, with the layer's
     own weights copied to the host for the experts those tokens select."""
     from .layer import ds_moe_layer
-    from .router import route_deepseek
+    from .router import RouteResult, route_deepseek, route_with_ids
 
     cfg = layer.cfg
     xc = x.detach().cpu()
     route = route_deepseek(xc, layer.router_weight.cpu(), None if layer.bias is None else layer.bias.cpu(),
                            top_k=cfg.top_k, n_groups=cfg.n_group, topk_groups=cfg.topk_group,
                            scoring_func=cfg.scoring_func, route_scale=cfg.route_scale)
-    bad, ties = id_mismatches(ids, route)
+    bad_mask, tie_mask = tie_tokens(ids, route)
+    bad, ties = int(bad_mask.sum()), int(tie_mask.sum())
     sel = list(range(int(xc.shape[0]))) if tokens is None else list(tokens)
-    experts = sorted({int(v) for v in route.ids[sel].reshape(-1).tolist()}) + [cfg.n_routed]
+    # a token whose selection is an excused tie is checked with the experts the GPU picked (either pick is
+    # the reference's answer; its output follows the pick)
+    use_ids = route.ids.clone()
+    use_ids[tie_mask] = ids.detach().cpu().to(torch.int64)[tie_mask]
+    if ties:
+        route = route_with_ids(xc, layer.router_weight.cpu(), use_ids, scoring_func=cfg.scoring_func,
+                               route_scale=cfg.route_scale)
+    experts = sorted({int(v) for v in use_ids[sel].reshape(-1).tolist()}) + [cfg.n_routed]
     host = layer if layer.w13.device.type == "cpu" else host_fp8_sublayer(layer, experts)
-    expected, _ = ds_moe_layer(xc[sel], host)
+    sub = RouteResult(ids=route.ids[sel], weights=route.weights[sel], choice=route.choice[sel],
+                      weights_f32=route.weights_f32[sel])
+    expected, _ = ds_moe_layer(xc[sel], host, route=sub)
     got = out.detach().cpu()[sel]
     rl, cd = rel_l2(got, expected), cos_dist(got, expected)
     return {"tokens_checked": len(sel), "tokens_routed": int(xc.shape[0]), "rel_l2": rl, "cos_dist": cd,
-            "id_mismatches": bad, "ties_excused": ties,
+            "id_mismatches": bad, "ties_excused": ties, "ties_checked_with_gpu_pick": int(tie_mask[sel].sum()),
             "pass": bool(rl <= REL_L2_GATE and cd <= COS_GATE and bad == ties)}
 
 

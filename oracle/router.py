@@ -79,6 +79,29 @@ def route_deepseek(
                        group_gap=group_gap)
 
 
+def route_with_ids(
+    hidden: torch.Tensor,
+    router_weight: torch.Tensor,
+    ids: torch.Tensor,
+    *,
+    scoring_func: str = "sigmoid",
+    route_scale: float = 1.0,
+) -> RouteResult:
+    """The routing weights fp8_source.py:1540-1547 gives a fixed choice of
+    experts `ids` [T, k]: the scores of those experts, renormalised (sigmoid
+    scoring) and scaled.  The checker uses it for tokens whose selection is a
+    score tie, to compute their outputs with the experts the GPU picked."""
+    x = hidden.detach().cpu().reshape(-1, int(hidden.shape[-1])).float()
+    logits = F.linear(x, router_weight.detach().cpu().float())
+    probs = logits.softmax(dim=-1, dtype=torch.float32) if scoring_func == "softmax" else logits.sigmoid()
+    ids = ids.detach().cpu().to(torch.int64)
+    picked = probs.gather(1, ids)
+    if scoring_func == "sigmoid":
+        picked = picked / picked.sum(dim=-1, keepdim=True).clamp_min(1e-12)
+    scaled = picked * float(route_scale)
+    return RouteResult(ids=ids, weights=scaled.to(dtype=hidden.dtype), choice=probs, weights_f32=scaled)
+
+
 def _group_boundary_gap(choice: torch.Tensor, n_groups: int, topk_groups: int, use_bias: bool) -> torch.Tensor:
     """Margin between the last kept group's score and the best dropped one."""
     grouped = choice.view(int(choice.shape[0]), int(n_groups), -1)

@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "../../include/moe_b200.h"
+#include "async_copy.cuh"
 #include "common.cuh"
 #include "dequant.cuh"
 #include "dispatch.cuh"
@@ -27,6 +28,8 @@ namespace {
 // 64): a destination rank, receive slot or return row read from exchanged
 // data that lies outside the buffers it indexes.  The access is skipped.
 constexpr int kEpRangeError = 64;
+// ... and code 256: a wait of the peer-memory barrier (moe_ep_barrier_p2p) ran out.
+constexpr int kEpWaitError = 256;
 __device__ int g_ep_error = 0;
 
 int read_and_clear_ep_error(cudaStream_t stream) {
@@ -68,6 +71,9 @@ int g_force_ksplit = 0;
 // Decode batches of <= 256 (token, slot) entries: selection, dispatch, chunk list and x staging in one
 // CTA (decode_prologue_kernel) instead of route_dispatch_kernel + rows_to_f16_kernel.
 bool g_decode_prologue = true;
+// With the decode prologue and bf16 hidden states: the router logits launch stages x (f16 + row scale) in an
+// extra cluster that runs beside the logits clusters, instead of the prologue's one warp per token.
+bool g_router_stages_x = true;
 // Staggered k-block walks in the cp.async warp-MMA stages (MmaArgs::kb_rotate).
 int g_kb_rotate = 0;
 // cp.async decode stages: the activation staging folded into the gate/up GEMV and the combine into the
@@ -376,6 +382,54 @@ __global__ void ep_count_kernel(const int64_t* ids, int64_t n, int64_t per_rank,
   }
   __syncthreads();
   for (int r = threadIdx.x; r < world; r += blockDim.x) counts[r] = c[r];
+}
+
+// Barrier of the expert-parallel ranks over peer memory.  Each rank's signal
+// buffer holds one 32-bit slot per rank: the last barrier epoch that rank
+// reached (epochs only grow, so one slot per rank serves every barrier).
+// One CTA; thread r < world serves peer r: (optionally) this rank's payload
+// row into row `rank` of peer r's payload buffer, a system-scope fence (every
+// store this rank made to peer memory before, this launch's and earlier
+// launches', is visible first), this rank's epoch into peer r's slot [rank]
+// (release), then a wait for peer r's epoch in this rank's slot [r]
+// (acquire), for at most limit_ns of %globaltimer.  A wait that runs out sets
+// code 256 and gives up; while that code is set, barriers do not wait (the
+// host reads it with moe_b200_device_error).
+MOE_D void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+MOE_D uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__global__ void ep_barrier_kernel(const uint64_t* peer_sig, int world, int rank, uint32_t* epoch, int64_t limit_ns,
+                                  const int32_t* payload, int payload_n, const uint64_t* peer_payload) {
+  __shared__ uint32_t e_s;
+  if (threadIdx.x == 0) e_s = *epoch + 1u;
+  __syncthreads();
+  const uint32_t e = e_s;
+  const int r = threadIdx.x;
+  if (r < world) {
+    if (payload) {
+      int32_t* dst = reinterpret_cast<int32_t*>(peer_payload[r]) + static_cast<int64_t>(rank) * payload_n;
+      for (int i = 0; i < payload_n; ++i) dst[i] = payload[i];
+    }
+    __threadfence_system();
+    st_release_sys_u32(reinterpret_cast<uint32_t*>(peer_sig[r]) + rank, e);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(peer_sig[rank]) + r;
+    const bool skip = (*reinterpret_cast<volatile int*>(&g_ep_error) & kEpWaitError) != 0;
+    const uint64_t start = global_timer_ns();
+    while (!skip && static_cast<int32_t>(ld_acquire_sys_u32(mine) - e) < 0) {
+      if (global_timer_ns() - start > static_cast<uint64_t>(limit_ns)) {
+        atomicOr(&g_ep_error, kEpWaitError);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *epoch = e;
 }
 
 // Rows to their experts' ranks: send position p (grouped by destination q,
@@ -1205,9 +1259,17 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
     // decode batches: logits (cluster-reduced, else split-K partials), then
     // selection + dispatch + chunk list in one CTA
     int nparts = 1;
+    const bool prologue = g_decode_prologue && use_mma && l.x16 &&
+                          decode_prologue_supported(static_cast<int>(T), static_cast<int>(E), static_cast<int>(k),
+                                                    static_cast<int>(H), hidden_dtype, hidden, static_cast<int>(S_main));
+    // the router launch stages x with a cluster of its own, off the prologue's path
+    bool router_staged = prologue && g_router_stages_x && hidden_dtype == kDtypeBF16;
     cudaError_t lerr = launch_router_logits_cluster(hidden, hidden_dtype, router_weight, router_dtype, l.logits,
-                                                    static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s);
+                                                    static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s,
+                                                    router_staged ? l.x16 : nullptr,
+                                                    router_staged ? l.xscale : nullptr);
     if (lerr == cudaErrorNotSupported) {
+      router_staged = false;
       lerr = launch_router_logits_split(hidden, hidden_dtype, router_weight, router_dtype, l.logits,
                                         static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s);
       nparts = router_split_parts(static_cast<int>(H));
@@ -1234,16 +1296,15 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
     rd.bucket.weights_out = l.wts;
     rd.bucket.args = ba;
     rd.chunks = ca;
-    if (g_decode_prologue && use_mma && nparts == 1 && l.x16 &&
-        decode_prologue_supported(static_cast<int>(T), static_cast<int>(E), static_cast<int>(k), static_cast<int>(H),
-                                  hidden_dtype, hidden, static_cast<int>(S_main))) {
-      // selection, dispatch, chunk list, x staging and counter reset in one CTA
+    if (prologue && nparts == 1) {
+      // selection, dispatch, chunk list, x staging (unless the router staged x) and counter reset in one CTA
       DecodePrologueArgs dp{};
       dp.rd = rd;
       dp.x = hidden;
       dp.hidden = static_cast<int>(H);
       dp.x16 = l.x16;
       dp.xscale = l.xscale;
+      dp.stage_x = router_staged ? 0 : 1;
       dp.zero = l.counters;
       dp.zero_n = l.n_counters;
       MOE_CUDA(launch_decode_prologue(dp, hidden_dtype, s), "decode prologue");
@@ -1341,6 +1402,23 @@ int moe_ep_dispatch_pack(const int64_t* ids, const float* weights, const uint16_
   ep_gather_kernel<<<grid_for(n * 32, 256), 256, 0, s>>>(hidden_bf16, ids, keys, pos_token, pos_entry, n, hidden_dim,
                                                          num_experts / world, vec, send_rows, send_expert);
   MOE_CUDA(cudaGetLastError(), "gather send rows");
+  return kOk;
+}
+
+int moe_ep_barrier_p2p(const uint64_t* peer_sig, int64_t world, int64_t rank, uint32_t* epoch,
+                       const int32_t* payload, int64_t payload_n, const uint64_t* peer_payload, int64_t limit_us,
+                       void* stream) {
+  if (!peer_sig || !epoch) return fail(kNullPointer, "null pointer");
+  if (world <= 0 || world > 1024 || rank < 0 || rank >= world || limit_us <= 0 || limit_us > 600000000 ||
+      payload_n < 0 || payload_n > 4096)
+    return fail(kBadDims, "bad dimensions");
+  if ((payload == nullptr) != (peer_payload == nullptr) || (payload && payload_n == 0))
+    return fail(kBadDims, "payload and peer_payload go together, with payload_n > 0");
+  const int threads = static_cast<int>(ceil_div(world, 32) * 32);
+  ep_barrier_kernel<<<1, threads, 0, as_stream(stream)>>>(peer_sig, static_cast<int>(world), static_cast<int>(rank),
+                                                          epoch, limit_us * 1000, payload,
+                                                          static_cast<int>(payload_n), peer_payload);
+  MOE_CUDA(cudaGetLastError(), "ep barrier");
   return kOk;
 }
 
@@ -1603,6 +1681,12 @@ int moe_b200_kb_rotate(int enable) {
 int moe_b200_fold_epilogues(int enable) {
   if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
   g_fold_epilogues = enable != 0;
+  return kOk;
+}
+
+int moe_b200_router_stages_x(int enable) {
+  if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
+  g_router_stages_x = enable != 0;
   return kOk;
 }
 

@@ -144,6 +144,7 @@ __global__ void __launch_bounds__(kPrologueThreads) decode_prologue_kernel(Decod
   for (int t = warp; t < T; t += kPrologueThreads / kWarp) {
     select_token(rd.partial, 1, 0, rd.bias, rd.select, t, scratch, scratch + E, rd.ids64, rd.bucket.keys_out,
                  rd.bucket.weights_out, rd.weights_bf16);
+    if (!a.stage_x) continue;
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const XT*>(a.x) + static_cast<int64_t>(t) * a.hidden);
     float amax = 0.0f;
     for (int i0 = lane; i0 < n16; i0 += 4 * kWarp) {

@@ -74,6 +74,7 @@ struct DecodePrologueArgs {
   int hidden;
   __half* x16;         // [tokens, hidden] x / xscale
   float* xscale;       // [tokens]
+  int stage_x;         // 0: x16 / xscale were staged already (by the router launch)
   int32_t* zero;       // [zero_n] set to 0
   int64_t zero_n;
 };

@@ -281,14 +281,106 @@ constexpr int kClusterWarps = 4;
 constexpr int kClusterTokens = 64;
 constexpr int kWarpSpans = 8;
 
+constexpr int kStageGroup = 8;        // tokens per register batch of the x staging
+constexpr int kStageMaxTokens = 256;
+
+// The staging cluster (the launch's last cluster row, when x16 is given):
+// x rows -> f16 with a power-of-two row scale, the rows_to_f16 staging
+// (2^(floor(log2 amax) - 13); 1 for a row without a finite nonzero maximum),
+// each CTA converting the k-range it would reduce in a logits cluster.  The
+// CTAs' slice maxima meet in distributed shared memory.  `sm` is the CTA's
+// reduction buffer (2 * kStageMaxTokens + kStageGroup * kClusterWarps floats).
+template <typename T>
+MOE_D void cluster_stage_x(cooperative_groups::cluster_group& cluster, int rank, const T* __restrict__ x, int tokens,
+                           int hidden, int kpart, __half* __restrict__ x16, float* __restrict__ xscale, float* sm) {
+  constexpr int V = 16 / sizeof(T);
+  float* part = sm;                          // [kStageMaxTokens] this slice's maxima (read by the peers)
+  float* rowmax = sm + kStageMaxTokens;      // [kStageMaxTokens] the rows' maxima
+  float* wred = sm + 2 * kStageMaxTokens;    // [kStageGroup][kClusterWarps]
+  const int lo = min(hidden, rank * kpart), hi = min(hidden, lo + kpart);
+  const int n = (hi - lo) / V;
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  auto piece = [&](int t, int i) { return reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * hidden + lo) + i; };
+  for (int t0 = 0; t0 < tokens; t0 += kStageGroup) {
+    float m[kStageGroup];
+#pragma unroll
+    for (int g = 0; g < kStageGroup; ++g) m[g] = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      uint4 v[kStageGroup];
+#pragma unroll
+      for (int g = 0; g < kStageGroup; ++g) v[g] = t0 + g < tokens ? __ldg(piece(t0 + g, i)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int g = 0; g < kStageGroup; ++g) {
+        float f[V];
+        unpack16<T>(v[g], f);
+#pragma unroll
+        for (int j = 0; j < V; ++j) m[g] = fmaxf(m[g], fabsf(f[j]));
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kStageGroup; ++g) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m[g] = fmaxf(m[g], __shfl_xor_sync(0xFFFFFFFFu, m[g], o));
+      if (lane == 0) wred[g * kClusterWarps + warp] = m[g];
+    }
+    __syncthreads();
+    if (threadIdx.x < kStageGroup && t0 + static_cast<int>(threadIdx.x) < tokens) {
+      float v = wred[threadIdx.x * kClusterWarps];
+#pragma unroll
+      for (int q = 1; q < kClusterWarps; ++q) v = fmaxf(v, wred[threadIdx.x * kClusterWarps + q]);
+      part[t0 + threadIdx.x] = v;
+    }
+    __syncthreads();  // wred is rewritten by the next group
+  }
+  cluster.sync();  // every slice's maxima are visible to the cluster
+  for (int t = threadIdx.x; t < tokens; t += blockDim.x) {
+    float v = 0.0f;
+    for (int q = 0; q < kClusterParts; ++q) v = fmaxf(v, cluster.map_shared_rank(part, q)[t]);
+    rowmax[t] = v;
+  }
+  __syncthreads();
+  for (int t0 = 0; t0 < tokens; t0 += kStageGroup) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      uint4 v[kStageGroup];
+#pragma unroll
+      for (int g = 0; g < kStageGroup; ++g) v[g] = t0 + g < tokens ? __ldg(piece(t0 + g, i)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int g = 0; g < kStageGroup; ++g) {
+        if (t0 + g >= tokens) break;
+        const float amax = rowmax[t0 + g];
+        const float inv = 1.0f / ((amax > 0.0f && isfinite(amax)) ? ldexpf(1.0f, ilogbf(amax) - 13) : 1.0f);
+        float f[V];
+        unpack16<T>(v[g], f);
+        __align__(16) __half h[V];
+#pragma unroll
+        for (int j = 0; j < V; ++j) h[j] = __float2half_rn(f[j] * inv);
+        __half* dst = x16 + static_cast<int64_t>(t0 + g) * hidden + lo + i * V;
+        if (V == 8) *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(h);
+        else *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(h);
+      }
+    }
+  }
+  if (rank == 0)
+    for (int t = threadIdx.x; t < tokens; t += blockDim.x) {
+      const float amax = rowmax[t];
+      xscale[t] = (amax > 0.0f && isfinite(amax)) ? ldexpf(1.0f, ilogbf(amax) - 13) : 1.0f;
+    }
+  cluster.sync();  // the peers' reads of part[] are done before this CTA exits
+}
+
 template <typename T>
 __global__ void __cluster_dims__(kClusterParts, 1, 1) __launch_bounds__(kClusterWarps * kWarp)
     router_logits_cluster_kernel(const T* __restrict__ x, const T* __restrict__ w, float* __restrict__ logits,
-                                 int tokens, int hidden, int experts, int kpart) {
+                                 int tokens, int hidden, int experts, int kpart, __half* __restrict__ x16,
+                                 float* __restrict__ xscale) {
   __shared__ float red[kClusterWarps][16][kClusterTokens];
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
+  if (x16 != nullptr && blockIdx.y == gridDim.y - 1) {
+    cluster_stage_x<T>(cluster, rank, x, tokens, hidden, kpart, x16, xscale, &red[0][0][0]);
+    return;
+  }
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp, g = lane / 4, c = lane % 4;
   const int e0 = blockIdx.y * 16;
   const int wpart = kpart / kClusterWarps;
@@ -468,21 +560,26 @@ static cudaError_t launch_split_w(const void* x, int w_dtype, const void* w, flo
 }
 
 cudaError_t launch_router_logits_cluster(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
-                                         int tokens, int hidden, int experts, cudaStream_t stream) {
+                                         int tokens, int hidden, int experts, cudaStream_t stream, __half* x16,
+                                         float* xscale) {
   if (tokens <= 0) return cudaSuccess;
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(w) % 16 == 0);
   if (x_dtype != w_dtype || (x_dtype != kDtypeBF16 && x_dtype != kDtypeF16) || !aligned || hidden % kSpan != 0)
     return cudaErrorNotSupported;
+  if (x16 && (!xscale || tokens > kStageMaxTokens || (reinterpret_cast<uintptr_t>(x16) % 16) != 0))
+    return cudaErrorNotSupported;
   const int kpart = static_cast<int>(ceil_div(ceil_div(hidden, kClusterParts), kSpan * kClusterWarps)) *
                     kSpan * kClusterWarps;
-  dim3 grid(kClusterParts, static_cast<unsigned>(ceil_div(experts, 16)));
+  // one more cluster row stages x when asked
+  dim3 grid(kClusterParts, static_cast<unsigned>(ceil_div(experts, 16) + (x16 ? 1 : 0)));
   if (x_dtype == kDtypeBF16)
     router_logits_cluster_kernel<__nv_bfloat16><<<grid, kClusterWarps * kWarp, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), logits, tokens, hidden, experts,
-        kpart);
+        kpart, x16, xscale);
   else
     router_logits_cluster_kernel<__half><<<grid, kClusterWarps * kWarp, 0, stream>>>(
-        static_cast<const __half*>(x), static_cast<const __half*>(w), logits, tokens, hidden, experts, kpart);
+        static_cast<const __half*>(x), static_cast<const __half*>(w), logits, tokens, hidden, experts, kpart, x16,
+        xscale);
   return cudaGetLastError();
 }
 

@@ -1,5 +1,6 @@
 // Router launchers (router.cu).
 #pragma once
+#include <cuda_fp16.h>
 #include "common.cuh"
 
 namespace moe {
@@ -35,9 +36,13 @@ cudaError_t launch_router_logits_split(const void* x, int x_dtype, const void* w
 
 // Decode-batch logits [T, E] in one launch (clusters of 8 CTAs reduce over k
 // in distributed shared memory): bf16 x bf16 or f16 x f16, hidden % 32 == 0,
-// 16-byte aligned operands; cudaErrorNotSupported otherwise.
+// 16-byte aligned operands; cudaErrorNotSupported otherwise.  With x16 (and
+// xscale; tokens <= 256, 16-byte aligned), one more cluster stages x meanwhile:
+// x16 = x / xscale in f16, xscale a power of two per row, exactly the
+// rows_to_f16 staging.
 cudaError_t launch_router_logits_cluster(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
-                                         int tokens, int hidden, int experts, cudaStream_t stream);
+                                         int tokens, int hidden, int experts, cudaStream_t stream,
+                                         __half* x16 = nullptr, float* xscale = nullptr);
 
 // logits: nparts partial [T, E] matrices part_stride floats apart, summed in part order.
 cudaError_t launch_router_select(const float* logits, const float* bias, const RouterSelectParams& p,

@@ -134,10 +134,22 @@ class CudaEPOps:
 
 class PeerExchange:
     """Symmetric-memory buffers for a layer's peer-to-peer exchange, sized for
-    up to `max_tokens` tokens per rank and step."""
+    up to `max_tokens` tokens per rank and step.
 
-    def __init__(self, layer: "ExpertParallelLayer", max_tokens: int):
+    sync: how the ranks order a step's three phases (counts exchanged, rows
+    landed, outputs home) -- "p2p" (default): moe_ep_barrier_p2p, a one-CTA
+    kernel that signals every peer through its symmetric signal buffer and
+    waits (bounded) for theirs, carrying the counts row for the all-gather;
+    "nccl": an NCCL all-gather and two one-element all-reduces."""
+
+    BARRIER_LIMIT_US = 10_000_000  # a peer 10 s late is an error (code 256), not a hang
+
+    def __init__(self, layer: "ExpertParallelLayer", max_tokens: int, sync: str = "p2p"):
         import torch.distributed._symmetric_memory as symm
+
+        if sync not in ("p2p", "nccl"):
+            raise ValueError("sync must be p2p or nccl")
+        self.sync = sync
 
         L = layer
         cfg = L.cfg
@@ -152,16 +164,38 @@ class PeerExchange:
         self.expert = symm.empty((self.capacity + self.max_tokens,), dtype=torch.int32, device=dev)
         self.src = symm.empty((self.capacity + self.max_tokens,), dtype=torch.int32, device=dev)
         self.yback = symm.empty((self.stride + self.max_tokens, H), dtype=torch.float32, device=dev)
-        self.handles = [symm.rendezvous(t, group) for t in (self.rows, self.expert, self.src, self.yback)]
+        # the [world][world] counts (row = source rank) and the barrier's signal slots, peer-written too
+        self.matrix = symm.empty((L.world * L.world,), dtype=torch.int32, device=dev)
+        self.sig = symm.empty((L.world,), dtype=torch.int32, device=dev)
+        self.handles = [symm.rendezvous(t, group) for t in (self.rows, self.expert, self.src, self.yback,
+                                                            self.matrix, self.sig)]
         self.peers = [torch.tensor([int(p) for p in h.buffer_ptrs], dtype=torch.int64, device=dev)
                       for h in self.handles]
         self.flag = torch.zeros((1,), dtype=torch.int32, device=dev)
         self.counts = torch.empty((L.world,), dtype=torch.int32, device=dev)
-        self.matrix = torch.empty((L.world * L.world,), dtype=torch.int32, device=dev)
+        self.sig.zero_()
+        self.epoch = torch.zeros((1,), dtype=torch.int32, device=dev)  # this rank's barrier count
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)  # every rank's signal slots are zero before the first barrier
         self.identity = torch.arange(self.stride, dtype=torch.int32, device=dev)
         self._shared_src = {}  # tokens -> src codes of this rank's shared-expert rows
         self.lib = native.load_library()
         self._ws = torch.empty((0,), dtype=torch.uint8, device=dev)
+
+    def _barrier(self, L: "ExpertParallelLayer", payload: torch.Tensor | None = None) -> None:
+        """Every rank reaches this point before any goes on; with payload (this
+        rank's [world] counts), the counts matrix is all-gathered too."""
+        if self.sync == "nccl":
+            if payload is not None:
+                dist.all_gather_into_tensor(self.matrix, payload, group=L.group)
+            else:
+                dist.all_reduce(self.flag, group=L.group)
+            return
+        has = payload is not None
+        native._check(self.lib.moe_ep_barrier_p2p(
+            native._ptr(self.peers[5]), L.world, L.rank, native._ptr(self.epoch),
+            native._ptr(payload) if has else None, L.world if has else 0, native._ptr(self.peers[4]) if has else None,
+            self.BARRIER_LIMIT_US, native._stream()), "moe_ep_barrier_p2p")
 
     def forward(self, L: "ExpertParallelLayer", x: torch.Tensor):
         cfg, lib = L.cfg, self.lib
@@ -175,9 +209,9 @@ class PeerExchange:
             ids, w = L.ops.route(x)
             native._check(lib.moe_ep_count_ranks(native._ptr(ids), T, k, cfg.n_routed, L.world,
                                                  native._ptr(self.counts), native._stream()), "moe_ep_count_ranks")
-        # empty receive slots; peers write only after the all-gather, which this rank joins after the reset
+        # empty receive slots; peers write only after the counts' all-gather, which this rank joins after the reset
         self.expert.fill_(-1)
-        dist.all_gather_into_tensor(self.matrix, self.counts, group=L.group)
+        self._barrier(L, payload=self.counts)
         if T > 0:
             need = int(lib.moe_ep_dispatch_p2p_workspace_bytes(T, k, L.world))
             if self._ws.numel() < need:
@@ -187,7 +221,7 @@ class PeerExchange:
                 native._ptr(self.matrix), self.capacity, self.src_stride, native._ptr(self.peers[0]),
                 native._ptr(self.peers[1]), native._ptr(self.peers[2]), native._ptr(self._ws), self._ws.numel(),
                 native._stream()), "moe_ep_dispatch_p2p")
-        dist.all_reduce(self.flag, group=L.group)  # every rank's rows have landed
+        self._barrier(L)  # every rank's rows have landed
         C = self.capacity
         self.rows[C:C + T].copy_(x)
         self.expert[C:C + T].fill_(L.n_local)      # the shared expert, last in the local tables
@@ -199,7 +233,7 @@ class PeerExchange:
         # Rows expected: T * k routed (a rank receives about what it sends) + T shared
         L.ops.experts_home(self.rows[:C + T], self.expert[:C + T], self.src[:C + T], self.src_stride,
                            self.peers[3], valid_rows=max(T, 1) * (k + 1))
-        dist.all_reduce(self.flag, group=L.group)  # every output row is home
+        self._barrier(L)  # every output row is home
         out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
         if T == 0:
             return out, ids, w
@@ -211,8 +245,8 @@ class PeerExchange:
 
 class GraphedExpertParallelLayer:
     """An ExpertParallelLayer step with the peer exchange for one token count,
-    captured as a CUDA graph (its kernels, memsets and the NCCL all-gather and
-    all-reduces).  Every rank captures and replays in step.  Write the tokens
+    captured as a CUDA graph (its kernels, memsets and the exchange's barriers:
+    peer-memory kernels, or NCCL collectives with sync="nccl").  Every rank captures and replays in step.  Write the tokens
     into `.input` (or pass them to __call__), replay, read `.output`.
     Release it (del) before destroying the process group."""
 
@@ -252,7 +286,7 @@ class ExpertParallelLayer:
     def __init__(self, cfg: synth.DsMoEConfig, rank: int, world: int, *, group=None, seed: int = 20,
                  device: torch.device | str | None = None, layer: synth.Fp8MoELayer | None = None, ops=None,
                  exchange: str = "auto", max_tokens: int = 64, peer: "PeerExchange | None" = None,
-                 row_major: bool = True):
+                 row_major: bool = True, peer_sync: str = "p2p"):
         if cfg.n_routed % world:
             raise ValueError("the routed experts must split evenly over the ranks")
         self.cfg, self.rank, self.world, self.group = cfg, int(rank), int(world), group
@@ -316,7 +350,7 @@ class ExpertParallelLayer:
                 raise ValueError("a shared peer exchange needs exchange='p2p' or 'auto' on an NCCL group")
             self.peer = peer
         else:
-            self.peer = PeerExchange(self, max_tokens) if use_p2p else None
+            self.peer = PeerExchange(self, max_tokens, sync=peer_sync) if use_p2p else None
 
     def capture(self, tokens: int) -> GraphedExpertParallelLayer:
         """A CUDA graph of one step for `tokens` tokens per rank (peer exchange only)."""
@@ -377,7 +411,7 @@ class ExpertParallelStack:
     def __init__(self, cfg: synth.DsMoEConfig, rank: int, world: int, n_layers: int, *, group=None,
                  seed: int = 20, device: torch.device | str | None = None,
                  layers: list[synth.Fp8MoELayer] | None = None, ops=None, exchange: str = "auto",
-                 max_tokens: int = 64, row_major: bool | None = None):
+                 max_tokens: int = 64, row_major: bool | None = None, peer_sync: str = "p2p"):
         if n_layers < 1 or (layers is not None and len(layers) != n_layers):
             raise ValueError("n_layers must be >= 1 and match `layers`")
         self.cfg, self.world = cfg, int(world)
@@ -388,7 +422,8 @@ class ExpertParallelStack:
             keep = row_major if row_major is not None else (ops is not None or torch.device(
                 device if device is not None else native._device()).type != "cuda")
             ep = ExpertParallelLayer(cfg, rank, world, group=group, seed=seed + li, device=device, layer=given,
-                                     ops=ops, exchange=exchange, max_tokens=max_tokens, peer=peer, row_major=keep)
+                                     ops=ops, exchange=exchange, max_tokens=max_tokens, peer=peer, row_major=keep,
+                                     peer_sync=peer_sync)
             peer = ep.peer
             self.layers.append(ep)
             del given, ep

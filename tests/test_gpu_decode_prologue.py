@@ -24,6 +24,7 @@ def _defaults_and_clean_error_word():
     lib.moe_b200_select_gemv(0)
     yield
     lib.moe_b200_decode_prologue(1)
+    lib.moe_b200_router_stages_x(1)
     lib.moe_b200_kb_rotate(0)
     torch.cuda.synchronize()
     assert lib.moe_b200_device_error(None) == 0, "a bounded wait inside a kernel gave up"
@@ -130,3 +131,33 @@ def test_shared_expert_side_stream(cuda_device, cfg_name, tokens):
     bad, excused = id_mismatches(side[1], route)
     assert bad == excused
     assert rel_l2(side[0], expected) <= REL_L2_GATE and cos_dist(side[0], expected) <= COS_GATE
+
+
+@pytest.mark.parametrize("cfg_name,tokens", [("c1", 1), ("c1", 8), ("c2", 1), ("c2", 2), ("c2", 8)])
+def test_router_staged_x_is_bit_identical(cuda_device, cfg_name, tokens):
+    """x staged by the router launch's extra cluster (moe_b200_router_stages_x(1),
+    the default) against the prologue's own staging (0): the same f16 rows and
+    row scales, so the same bits out -- including a row scaled far up, one far
+    down and an all-zero row (scale 1); eager and graph-replayed."""
+    cfg = synth.C1_TINY if cfg_name == "c1" else synth.C2_DSV3
+    layer = synth.make_fp8_layer(cfg, seed=900 + tokens, device="cuda")
+    gpu = DsMoELayerGPU(layer)
+    lib = native.load_library()
+    x = synth.make_hidden(tokens, cfg.hidden, seed=901 + tokens, device="cuda").float()
+    x[0] *= 3.0e4
+    if tokens > 2:
+        x[1] = 0.0
+        x[2] *= 1.0e-6
+    x = x.to(torch.bfloat16)
+    try:
+        lib.moe_b200_router_stages_x(1)
+        a = _run(gpu, x)
+        graphed = gpu.capture(tokens)
+        replayed = graphed(x).clone()
+        lib.moe_b200_router_stages_x(0)
+        b = _run(gpu, x)
+    finally:
+        lib.moe_b200_router_stages_x(1)
+    for u, v in zip(a, b):
+        assert torch.equal(u, v)
+    assert torch.equal(replayed, a[0])

@@ -44,6 +44,10 @@ def _rank_main(rank, world, port, outdir):
         out_p2p, ids_p2p, _ = peer.forward(x)
         out_p2p2, _, _ = peer.forward(x2)
         out_nccl2, _, _ = ep.forward(x2)
+        # the same exchange ordered by NCCL collectives instead of the peer-memory barrier
+        peer_nccl = ExpertParallelLayer(cfg, rank, world, layer=full, device=dev, exchange="p2p", max_tokens=16,
+                                        peer_sync="nccl")
+        out_sync_nccl, _, _ = peer_nccl.forward(x2)
         # the same step replayed from a CUDA graph
         graphed = peer.capture(int(x2.shape[0]))
         out_graph = graphed(x2).clone()
@@ -61,7 +65,10 @@ def _rank_main(rank, world, port, outdir):
         ref_pre_ids = torch.empty_like(ids_pre)
         ref_pre = single.forward(xp, ids=ref_pre_ids)
         torch.cuda.synchronize()
-        torch.save({"out": out.cpu(), "ids": ids.cpu(), "ref": ref.cpu(), "ref_ids": ref_ids.cpu(), "x": x.cpu(),
+        from pocketlm_b200 import native
+
+        err = int(native.load_library().moe_b200_device_error(None))
+        torch.save({"out": out.cpu(), "device_error": err, "out_sync_nccl": out_sync_nccl.cpu(), "ids": ids.cpu(), "ref": ref.cpu(), "ref_ids": ref_ids.cpu(), "x": x.cpu(),
                     "out_p2p": out_p2p.cpu(), "ids_p2p": ids_p2p.cpu(), "out_p2p2": out_p2p2.cpu(),
                     "out_nccl2": out_nccl2.cpu(), "out_graph": out_graph.cpu(), "out_graph2": out_graph2.cpu(),
                     "xp": xp.cpu(), "out_pre": out_pre.cpu(), "ids_pre": ids_pre.cpu(),
@@ -94,6 +101,8 @@ def test_ep_two_gpus_matches_single_gpu_layer_and_oracle():
             assert torch.equal(r["ids_p2p"], r["ids"])
             assert torch.equal(r["out_p2p"], r["out"])
             assert torch.equal(r["out_p2p2"], r["out_nccl2"])
+            assert torch.equal(r["out_sync_nccl"], r["out_nccl2"])  # barrier kind changes no bits
+            assert r["device_error"] == 0  # no range check fired, no barrier wait ran out
             assert torch.equal(r["out_graph"], r["out_nccl2"]) and torch.equal(r["out_graph2"], r["out_nccl2"])
             # prefill: the received rows run on the grouped GEMM, as the fused layer's pairs do
             same = (torch.sort(r["ids_pre"], 1).values == torch.sort(r["ref_pre_ids"], 1).values).all(dim=1)

@@ -1,5 +1,5 @@
-"""Range checks of the expert-parallel peer kernels, on one GPU with local
-buffers only.
+"""Range checks of the expert-parallel peer kernels and the bounded wait of
+the peer-memory barrier, on one GPU with local buffers only.
 
 The peer kernels store into addresses built from values other ranks wrote
 (src codes, exchanged counts).  Each test declares a buffer smaller than its
@@ -133,3 +133,61 @@ def test_experts_return_p2p_keeps_bad_homes_local(cuda_device, n_rows):
     untouched = torch.ones(big.shape[0], dtype=torch.bool)
     untouched[homes + margin] = False
     assert (big[untouched.to(cuda_device)] == SENTINEL).all()
+
+
+EP_WAIT_ERROR = 256
+
+
+def test_barrier_single_rank_and_payload(cuda_device):
+    """World 1: the rank signals its own slot and passes at once; the payload
+    lands in its own counts row; the epoch counts barriers."""
+    assert _device_error() == 0
+    sig = torch.zeros((1,), dtype=torch.int32, device=cuda_device)
+    matrix = torch.full((1,), -1, dtype=torch.int32, device=cuda_device)
+    epoch = torch.zeros((1,), dtype=torch.int32, device=cuda_device)
+    payload = torch.tensor([7], dtype=torch.int32, device=cuda_device)
+    peers_sig, peers_mat = _table(sig), _table(matrix)
+    lib = _lib()
+    for i in range(3):
+        has = i == 1
+        code = lib.moe_ep_barrier_p2p(native._ptr(peers_sig), 1, 0, native._ptr(epoch),
+                                      native._ptr(payload) if has else None, 1 if has else 0,
+                                      native._ptr(peers_mat) if has else None, 1_000_000, native._stream())
+        native._check(code, "moe_ep_barrier_p2p")
+    assert epoch.item() == 3 and sig.item() == 3 and matrix.item() == 7
+    assert _device_error() == 0
+
+
+def test_barrier_wait_runs_out_and_reports(cuda_device):
+    """World 2 with no second rank: this rank's signal to "rank 1" lands in a
+    local stand-in buffer, and nothing ever writes rank 1's slot here, so the
+    wait runs out after its limit (50 ms), sets code 256 and returns; while the
+    code is set a second barrier does not wait; reading the code clears it."""
+    assert _device_error() == 0
+    sig = torch.zeros((2,), dtype=torch.int32, device=cuda_device)
+    stand_in = torch.zeros((2,), dtype=torch.int32, device=cuda_device)
+    epoch = torch.zeros((1,), dtype=torch.int32, device=cuda_device)
+    payload = torch.tensor([3, 4], dtype=torch.int32, device=cuda_device)
+    matrix = torch.zeros((4,), dtype=torch.int32, device=cuda_device)
+    matrix_stand_in = torch.zeros((4,), dtype=torch.int32, device=cuda_device)
+    peers_sig, peers_mat = _table(sig, stand_in), _table(matrix, matrix_stand_in)
+    lib = _lib()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    native._check(lib.moe_ep_barrier_p2p(native._ptr(peers_sig), 2, 0, native._ptr(epoch), native._ptr(payload), 2,
+                                         native._ptr(peers_mat), 50_000, native._stream()), "moe_ep_barrier_p2p")
+    end.record()
+    torch.cuda.synchronize()
+    assert start.elapsed_time(end) >= 45.0
+    # the payload and the signal reached both "ranks" (row 0 of each counts buffer, slot 0 of each signal buffer)
+    assert matrix[:2].tolist() == [3, 4] and matrix_stand_in[:2].tolist() == [3, 4]
+    assert sig.tolist() == [1, 0] and stand_in.tolist() == [1, 0] and epoch.item() == 1
+    # a second barrier while the code is set: no wait
+    start.record()
+    native._check(lib.moe_ep_barrier_p2p(native._ptr(peers_sig), 2, 0, native._ptr(epoch), None, 0, None, 50_000,
+                                         native._stream()), "moe_ep_barrier_p2p")
+    end.record()
+    torch.cuda.synchronize()
+    assert start.elapsed_time(end) < 40.0 and epoch.item() == 2
+    assert _device_error() == EP_WAIT_ERROR
+    assert _device_error() == 0
