@@ -408,6 +408,33 @@ int moe_ep_barrier_p2p(const uint64_t* peer_sig, int64_t world, int64_t rank, ui
  *   arithmetic and combine order as the all-to-all exchange above. */
 int moe_ep_count_ranks(const int64_t* ids, int64_t tokens, int64_t top_k, int64_t num_experts, int64_t world,
                        int32_t* counts, void* stream);
+/* No reference counterpart.  The send side of one decode step of the
+ * exchange above in two launches (router logits, then one CTA), instead of
+ * routing, count, reset, barrier-with-counts, dispatch, barrier and the
+ * copies of this rank's shared-expert rows: the DS-V3 router (sigmoid,
+ * correction bias, group-limited top-k, renormalised, scaled, weights
+ * rounded through bf16 -- moe_route_topk's results -- into out_ids /
+ * out_weights_f32 [tokens, top_k]), this rank's receive slots reset
+ * (expert -1 for rows 0 .. capacity - 1) and its own tokens' rows appended
+ * at rows capacity + t (expert num_experts / world, the shared expert; src
+ * rank * src_stride + tokens * top_k + t), the counts all-gathered through
+ * the barrier, every routed row written into its expert's rank (token order
+ * kept, ranks in order, slots range-checked: code 64), then the second
+ * barrier.  peer_matrix [world] holds every rank's [world][world] counts
+ * buffer and peer_sig / epoch are the barrier's (moe_ep_barrier_p2p; the
+ * epoch grows by two).  hidden bf16, router_weight bf16 or f16
+ * (router_dtype), tokens <= 128 (0: a rank with no tokens still resets,
+ * sends its zero counts and takes both barriers), tokens * top_k <= 1024,
+ * num_experts <= 256, world <= 32; workspace:
+ * moe_ep_route_dispatch_p2p_workspace_bytes. */
+int64_t moe_ep_route_dispatch_p2p_workspace_bytes(int64_t tokens, int64_t num_experts);
+int moe_ep_route_dispatch_p2p(const uint16_t* hidden_bf16, const void* router_weight, int router_dtype,
+                              const float* bias, int64_t tokens, int64_t hidden_dim, int64_t num_experts,
+                              int64_t n_group, int64_t topk_group, int64_t top_k, float route_scale, int64_t world,
+                              int64_t rank, int64_t capacity, int64_t src_stride, const uint64_t* peer_rows,
+                              const uint64_t* peer_expert, const uint64_t* peer_src, const uint64_t* peer_matrix,
+                              const uint64_t* peer_sig, uint32_t* epoch, int64_t limit_us, int64_t* out_ids,
+                              float* out_weights_f32, void* workspace, int64_t workspace_bytes, void* stream);
 int moe_ep_dispatch_p2p(const int64_t* ids, const uint16_t* hidden_bf16, int64_t tokens, int64_t hidden_dim,
                         int64_t top_k, int64_t num_experts, int64_t world, int64_t rank, const int32_t* count_matrix,
                         int64_t capacity, int64_t src_stride, const uint64_t* peer_rows, const uint64_t* peer_expert,
@@ -538,6 +565,12 @@ int moe_b200_shared_side(int enable);
  * a cluster of its own, beside the logits clusters (1, the default), or the
  * prologue stages it (0).  Same results bit for bit. */
 int moe_b200_router_stages_x(int enable);
+/* No reference counterpart.  With the router staging x (above), decode
+ * layers on tiled weights also request the shared expert's gate/up weights
+ * into L2 from the router launch (no routing needed for them) and list the
+ * shared expert's work first in the gate/up GEMV (1), or not (0, the
+ * default).  Same results bit for bit. */
+int moe_b200_prefetch_shared(int enable);
 
 /* ---------------------------------------------------------------------------
  * Pack-file reads (host only): the FP8 pack loader's byte ranges.

@@ -18,6 +18,7 @@
 #include "prefill_gemm.cuh"
 #include "route_host.cuh"
 #include "router.cuh"
+#include "router_device.cuh"
 #include "status.cuh"
 
 using namespace moe;
@@ -74,6 +75,9 @@ bool g_decode_prologue = true;
 // With the decode prologue and bf16 hidden states: the router logits launch stages x (f16 + row scale) in an
 // extra cluster that runs beside the logits clusters, instead of the prologue's one warp per token.
 bool g_router_stages_x = true;
+// With the router staging x: its staging cluster also requests the shared expert's gate/up weights into L2,
+// and the prologue puts the shared expert's chunks first (A/B knob).
+bool g_prefetch_shared = false;
 // Staggered k-block walks in the cp.async warp-MMA stages (MmaArgs::kb_rotate).
 int g_kb_rotate = 0;
 // cp.async decode stages: the activation staging folded into the gate/up GEMV and the combine into the
@@ -430,6 +434,158 @@ __global__ void ep_barrier_kernel(const uint64_t* peer_sig, int world, int rank,
   }
   __syncthreads();
   if (threadIdx.x == 0) *epoch = e;
+}
+
+// The wait half of a barrier for thread r < world: rank r's epoch >= e in this rank's slot [r].
+MOE_D void ep_wait_peer(const uint64_t* peer_sig, int rank, int r, uint32_t e, int64_t limit_ns) {
+  const uint32_t* mine = reinterpret_cast<const uint32_t*>(peer_sig[rank]) + r;
+  if (*reinterpret_cast<volatile int*>(&g_ep_error) & kEpWaitError) return;
+  const uint64_t start = global_timer_ns();
+  while (static_cast<int32_t>(ld_acquire_sys_u32(mine) - e) < 0) {
+    if (global_timer_ns() - start > static_cast<uint64_t>(limit_ns)) {
+      atomicOr(&g_ep_error, kEpWaitError);
+      return;
+    }
+    __nanosleep(64);
+  }
+}
+MOE_D int32_t ld_relaxed_sys_s32(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.relaxed.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The send side of one decode step of the peer exchange in one CTA, in
+// place of the selection, rank count, receive-slot reset, counts all-gather,
+// rank bucketing, row scatter and the two barriers around it (eleven
+// launches): (1) warp t selects token t's experts from the router logits
+// (select_token, as the router's selection kernel does); (2) this rank's
+// receive slots are reset (expert -1) and its own tokens' shared-expert rows
+// written after them (rows C + t, expert n_local, source entry T * top_k +
+// t); (3) each entry's destination rank and its position among this rank's
+// entries bound there, in entry order (a bitmask per rank); (4) barrier 1,
+// carrying this rank's counts row into every peer's counts matrix; (5) every
+// entry's receive slot = the entries of lower ranks bound for the same rank
+// + its position, range-checked (code 64); warps write each token row and
+// its expert and source codes into the destination's buffers with 16-byte
+// NVLink stores; (6) a system fence, barrier 2.  Barriers as
+// ep_barrier_kernel (the epoch grows by two).  Up to 128 tokens, 1024
+// entries, 256 experts, 32 ranks; 1024 threads.
+constexpr int kEpSendThreads = 1024;
+constexpr int kEpSendWarps = kEpSendThreads / 32;
+constexpr int kEpSendMaxRanks = 32;
+struct EpSendArgs {
+  const float* logits;   // [T, E]
+  const float* bias;
+  RouterSelectParams sel;
+  const uint16_t* x;     // [T, H] bf16
+  int64_t H;
+  int world, rank, n_local;
+  int64_t capacity, src_stride;
+  const uint64_t* peer_rows;
+  const uint64_t* peer_expert;
+  const uint64_t* peer_src;
+  const uint64_t* peer_matrix;
+  const uint64_t* peer_sig;
+  uint32_t* epoch;
+  int64_t limit_ns;
+  int64_t* ids64;
+  float* weights_f32;
+};
+__global__ void __launch_bounds__(kEpSendThreads) ep_send_decode_kernel(EpSendArgs a) {
+  extern __shared__ float sel_scratch[];  // [warps][2 * E]
+  __shared__ uint32_t masks[kEpSendMaxRanks][kEpSendThreads / 32];
+  __shared__ int32_t counts[kEpSendMaxRanks], base[kEpSendMaxRanks];
+  __shared__ int32_t keys[kEpSendThreads], posv[kEpSendThreads];
+  __shared__ uint32_t e_s;
+  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
+  const int T = a.sel.tokens, k = a.sel.top_k, E = a.sel.experts, n = T * k, W = a.world;
+  const int64_t H = a.H, C = a.capacity;
+  if (tid == 0) e_s = *a.epoch;
+  // 1. selection
+  for (int t = warp; t < T; t += kEpSendWarps)
+    select_token(a.logits, 1, 0, a.bias, a.sel, t, sel_scratch + warp * 2 * E, sel_scratch + warp * 2 * E + E,
+                 a.ids64, nullptr, a.weights_f32, nullptr);
+  // 2. this rank's receive slots; its own shared-expert rows after them
+  int32_t* own_expert = reinterpret_cast<int32_t*>(a.peer_expert[a.rank]);
+  int32_t* own_src = reinterpret_cast<int32_t*>(a.peer_src[a.rank]);
+  uint16_t* own_rows = reinterpret_cast<uint16_t*>(a.peer_rows[a.rank]);
+  for (int64_t i = tid; i < C; i += kEpSendThreads) own_expert[i] = -1;
+  for (int t = warp; t < T; t += kEpSendWarps) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(t) * H);
+    uint4* dst = reinterpret_cast<uint4*>(own_rows + (C + t) * H);
+    for (int64_t i = lane; i < H / 8; i += kWarp) dst[i] = __ldg(src + i);
+    if (lane == 0) {
+      own_expert[C + t] = a.n_local;
+      own_src[C + t] = static_cast<int32_t>(a.rank * a.src_stride + n + t);
+    }
+  }
+  for (int i = tid; i < kEpSendMaxRanks * (kEpSendThreads / 32); i += kEpSendThreads) (&masks[0][0])[i] = 0;
+  if (tid < kEpSendMaxRanks) counts[tid] = 0;
+  __syncthreads();  // the selections (global) and the cleared masks are visible to the CTA
+  // 3. destinations and positions
+  int key = -1;
+  if (tid < n) {
+    const int64_t id = a.ids64[tid];
+    const int64_t q = id / a.n_local;
+    key = (id >= 0 && q < W) ? static_cast<int>(q) : -1;
+    if (key < 0) atomicOr(&g_ep_error, kEpRangeError);
+  }
+  keys[tid] = key;
+  if (key >= 0) {
+    atomicOr(&masks[key][tid / 32], 1u << (tid % 32));
+    atomicAdd(&counts[key], 1);
+  }
+  __syncthreads();
+  if (key >= 0) {
+    int pos = __popc(masks[key][tid / 32] & ((1u << (tid % 32)) - 1u));
+    for (int w = 0; w < tid / 32; ++w) pos += __popc(masks[key][w]);
+    posv[tid] = pos;
+  }
+  // 4. barrier 1 with this rank's counts row
+  const uint32_t e1 = e_s + 1u, e2 = e_s + 2u;
+  if (tid < W) {
+    int32_t* dst = reinterpret_cast<int32_t*>(a.peer_matrix[tid]) + static_cast<int64_t>(a.rank) * W;
+    for (int q = 0; q < W; ++q) dst[q] = counts[q];
+    __threadfence_system();  // the reset slots, the own rows and the counts are visible before the signal
+    st_release_sys_u32(reinterpret_cast<uint32_t*>(a.peer_sig[tid]) + a.rank, e1);
+    ep_wait_peer(a.peer_sig, a.rank, tid, e1, a.limit_ns);
+  }
+  __syncthreads();
+  // 5. receive slots, then the rows
+  if (tid < W) {
+    const int32_t* m = reinterpret_cast<const int32_t*>(a.peer_matrix[a.rank]);
+    int b = 0;
+    for (int r = 0; r < a.rank; ++r) b += ld_relaxed_sys_s32(m + static_cast<int64_t>(r) * W + tid);
+    base[tid] = b;
+  }
+  __syncthreads();
+  for (int e = warp; e < n; e += kEpSendWarps) {
+    const int q = keys[e];
+    if (q < 0) continue;
+    const int64_t slot = static_cast<int64_t>(base[q]) + posv[e];
+    if (slot < 0 || slot >= C) {  // counts that disagree with the rows sent: recorded, never stored
+      if (lane == 0) atomicOr(&g_ep_error, kEpRangeError);
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(e / k) * H);
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.peer_rows[q]) + slot * H);
+    for (int64_t i = lane; i < H / 8; i += kWarp) dst[i] = __ldg(src + i);
+    if (lane == 0) {
+      reinterpret_cast<int32_t*>(a.peer_expert[q])[slot] =
+          static_cast<int32_t>(a.ids64[e] - static_cast<int64_t>(q) * a.n_local);
+      reinterpret_cast<int32_t*>(a.peer_src[q])[slot] = static_cast<int32_t>(a.rank * a.src_stride + e);
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  // 6. barrier 2: every rank's rows have landed
+  if (tid < W) {
+    st_release_sys_u32(reinterpret_cast<uint32_t*>(a.peer_sig[tid]) + a.rank, e2);
+    ep_wait_peer(a.peer_sig, a.rank, tid, e2, a.limit_ns);
+  }
+  __syncthreads();
+  if (tid == 0) *a.epoch = e2;
 }
 
 // Rows to their experts' ranks: send position p (grouped by destination q,
@@ -1264,10 +1420,19 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
                                                     static_cast<int>(H), hidden_dtype, hidden, static_cast<int>(S_main));
     // the router launch stages x with a cluster of its own, off the prologue's path
     bool router_staged = prologue && g_router_stages_x && hidden_dtype == kDtypeBF16;
+    // with it, the shared expert's gate/up weights (tiled) go to L2 while the router runs, and its chunks
+    // lead the GEMV's work list
+    const bool prefetch_shared = router_staged && g_prefetch_shared && has_shared && weight_layout == 1 && !side;
+    RouterPrefetch pf{};
+    if (prefetch_shared) {
+      pf.ranges[0] = tables + 0 * S + (S - 1);
+      pf.ranges[1] = tables + 2 * S + (S - 1);
+      pf.bytes = fp8_tiled_bytes(I, H);
+    }
     cudaError_t lerr = launch_router_logits_cluster(hidden, hidden_dtype, router_weight, router_dtype, l.logits,
                                                     static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s,
                                                     router_staged ? l.x16 : nullptr,
-                                                    router_staged ? l.xscale : nullptr);
+                                                    router_staged ? l.xscale : nullptr, pf);
     if (lerr == cudaErrorNotSupported) {
       router_staged = false;
       lerr = launch_router_logits_split(hidden, hidden_dtype, router_weight, router_dtype, l.logits,
@@ -1305,6 +1470,7 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
       dp.x16 = l.x16;
       dp.xscale = l.xscale;
       dp.stage_x = router_staged ? 0 : 1;
+      dp.shared_first = prefetch_shared ? 1 : 0;
       dp.zero = l.counters;
       dp.zero_n = l.n_counters;
       MOE_CUDA(launch_decode_prologue(dp, hidden_dtype, s), "decode prologue");
@@ -1419,6 +1585,83 @@ int moe_ep_barrier_p2p(const uint64_t* peer_sig, int64_t world, int64_t rank, ui
                                                           epoch, limit_us * 1000, payload,
                                                           static_cast<int>(payload_n), peer_payload);
   MOE_CUDA(cudaGetLastError(), "ep barrier");
+  return kOk;
+}
+
+int64_t moe_ep_route_dispatch_p2p_workspace_bytes(int64_t tokens, int64_t num_experts) {
+  return std::max<int64_t>(1, tokens) * std::max<int64_t>(1, num_experts) * static_cast<int64_t>(sizeof(float)) + 256;
+}
+
+int moe_ep_route_dispatch_p2p(const uint16_t* hidden_bf16, const void* router_weight, int router_dtype,
+                              const float* bias, int64_t tokens, int64_t hidden_dim, int64_t num_experts,
+                              int64_t n_group, int64_t topk_group, int64_t top_k, float route_scale, int64_t world,
+                              int64_t rank, int64_t capacity, int64_t src_stride, const uint64_t* peer_rows,
+                              const uint64_t* peer_expert, const uint64_t* peer_src, const uint64_t* peer_matrix,
+                              const uint64_t* peer_sig, uint32_t* epoch, int64_t limit_us, int64_t* out_ids,
+                              float* out_weights_f32, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!router_weight || !peer_rows || !peer_expert || !peer_src || !peer_matrix || !peer_sig || !epoch)
+    return fail(kNullPointer, "null pointer");
+  if (tokens > 0 && (!hidden_bf16 || !out_ids || !out_weights_f32)) return fail(kNullPointer, "null pointer");
+  if (tokens < 0 || hidden_dim <= 0 || hidden_dim % 8 != 0 || world <= 0 || rank < 0 || rank >= world ||
+      num_experts <= 0 || num_experts % world != 0 || capacity <= 0 || limit_us <= 0 || limit_us > 600000000 ||
+      top_k <= 0 || src_stride < tokens * (top_k + 1) || capacity + tokens > INT32_MAX ||
+      world * src_stride > INT32_MAX)
+    return fail(kBadDims, "bad dimensions");
+  if (tokens > 0) {
+    int code = check_route(tokens, hidden_dim, num_experts, n_group, topk_group, top_k);
+    if (code != kOk) return code;
+  }
+  if (tokens > kEpSendThreads / 8 || tokens * top_k > kEpSendThreads || num_experts > 256 ||
+      world > kEpSendMaxRanks)
+    return fail(kUnsupported, "more than 128 tokens, 1024 entries, 256 experts or 32 ranks");
+  if ((reinterpret_cast<uintptr_t>(hidden_bf16) & 15u) != 0) return fail(kUnsupported, "rows must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  Scratch scratch(workspace, workspace_bytes, moe_ep_route_dispatch_p2p_workspace_bytes(tokens, num_experts), s);
+  if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
+  float* logits = reinterpret_cast<float*>(scratch.base());
+  if (tokens > 0) {
+    // the logits as the router's own path computes them for decode sizes (route_impl)
+    cudaError_t cerr = launch_router_logits_cluster(hidden_bf16, kDtypeBF16, router_weight, router_dtype, logits,
+                                                    static_cast<int>(tokens), static_cast<int>(hidden_dim),
+                                                    static_cast<int>(num_experts), s);
+    if (cerr == cudaErrorNotSupported)
+      cerr = launch_router_logits(hidden_bf16, kDtypeBF16, router_weight, router_dtype, logits,
+                                  static_cast<int>(tokens), static_cast<int>(hidden_dim),
+                                  static_cast<int>(num_experts), s);
+    MOE_CUDA(cerr, "router logits");
+  }
+  EpSendArgs a{};
+  a.logits = logits;
+  a.bias = bias;
+  a.sel.tokens = static_cast<int>(tokens);
+  a.sel.experts = static_cast<int>(num_experts);
+  a.sel.top_k = static_cast<int>(top_k);
+  a.sel.n_group = static_cast<int>(n_group);
+  a.sel.topk_group = static_cast<int>(topk_group);
+  a.sel.scoring = kScoreSigmoid;
+  a.sel.renorm = 1;
+  a.sel.softmax_fp64 = 0;
+  a.sel.round_bf16 = 1;
+  a.sel.route_scale = route_scale;
+  a.x = hidden_bf16;
+  a.H = hidden_dim;
+  a.world = static_cast<int>(world);
+  a.rank = static_cast<int>(rank);
+  a.n_local = static_cast<int>(num_experts / world);
+  a.capacity = capacity;
+  a.src_stride = src_stride;
+  a.peer_rows = peer_rows; a.peer_expert = peer_expert; a.peer_src = peer_src;
+  a.peer_matrix = peer_matrix; a.peer_sig = peer_sig;
+  a.epoch = epoch;
+  a.limit_ns = limit_us * 1000;
+  a.ids64 = out_ids;
+  a.weights_f32 = out_weights_f32;
+  const size_t smem = static_cast<size_t>(kEpSendWarps) * 2 * std::max<int64_t>(1, num_experts) * sizeof(float);
+  MOE_CUDA(cudaFuncSetAttribute(ep_send_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(smem)),
+           "send attributes");
+  ep_send_decode_kernel<<<1, kEpSendThreads, smem, s>>>(a);
+  MOE_CUDA(cudaGetLastError(), "ep send");
   return kOk;
 }
 
@@ -1681,6 +1924,12 @@ int moe_b200_kb_rotate(int enable) {
 int moe_b200_fold_epilogues(int enable) {
   if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
   g_fold_epilogues = enable != 0;
+  return kOk;
+}
+
+int moe_b200_prefetch_shared(int enable) {
+  if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
+  g_prefetch_shared = enable != 0;
   return kOk;
 }
 

@@ -197,11 +197,23 @@ class PeerExchange:
             native._ptr(payload) if has else None, L.world if has else 0, native._ptr(self.peers[4]) if has else None,
             self.BARRIER_LIMIT_US, native._stream()), "moe_ep_barrier_p2p")
 
+    def _fused_send(self, L: "ExpertParallelLayer", x: torch.Tensor) -> bool:
+        """Whether this step's send side runs as moe_ep_route_dispatch_p2p (the
+        router logits, then one CTA for selection, dispatch and both barriers)."""
+        cfg = L.cfg
+        return (self.sync == "p2p" and isinstance(L.ops, CudaEPOps) and x.dtype == torch.bfloat16
+                and cfg.scoring_func == "sigmoid" and L.bias is not None
+                and L.router_weight.dtype in (torch.bfloat16, torch.float16)
+                and self.max_tokens <= 128 and self.max_tokens * cfg.top_k <= 1024 and cfg.n_routed <= 256
+                and L.world <= 32 and cfg.hidden % 8 == 0)
+
     def forward(self, L: "ExpertParallelLayer", x: torch.Tensor):
         cfg, lib = L.cfg, self.lib
         T, k, H = int(x.shape[0]), cfg.top_k, cfg.hidden
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens exceed the exchange's {self.max_tokens}")
+        if self._fused_send(L, x):
+            return self._forward_fused(L, x)
         if T == 0:  # nothing to send; this rank still takes every step (it may receive rows)
             ids, w = L._no_routes(x)
             self.counts.zero_()
@@ -238,6 +250,39 @@ class PeerExchange:
         if T == 0:
             return out, ids, w
         w_flat = w.reshape(-1).contiguous()  # referenced until the launch (a temporary could be freed first)
+        native._check(lib.moe_ep_combine(native._ptr(self.yback), native._ptr(self.identity), native._ptr(w_flat),
+                                         T, k, H, 1, native._ptr(out), native._stream()), "moe_ep_combine")
+        return out, ids, w
+
+
+    def _forward_fused(self, L: "ExpertParallelLayer", x: torch.Tensor):
+        """A decode step with the send side fused (moe_ep_route_dispatch_p2p):
+        the same rows, slots, codes and barriers as forward()'s launches, so the
+        same bits."""
+        cfg, lib = L.cfg, self.lib
+        T, k, H = int(x.shape[0]), cfg.top_k, cfg.hidden
+        dev = x.device
+        ids = torch.empty((T, k), dtype=torch.int64, device=dev)
+        w = torch.empty((T, k), dtype=torch.float32, device=dev)
+        need = int(lib.moe_ep_route_dispatch_p2p_workspace_bytes(T, cfg.n_routed))
+        if self._ws.numel() < need:
+            self._ws = torch.empty((need,), dtype=torch.uint8, device=dev)
+        rw_dtype = native.DTYPE_BF16 if L.router_weight.dtype == torch.bfloat16 else native.DTYPE_F16
+        native._check(lib.moe_ep_route_dispatch_p2p(
+            native._ptr(x) if T else None, native._ptr(L.router_weight), rw_dtype, native._ptr(L.bias), T, H,
+            cfg.n_routed, cfg.n_group, cfg.topk_group, k, float(cfg.route_scale), L.world, L.rank, self.capacity,
+            self.src_stride, native._ptr(self.peers[0]), native._ptr(self.peers[1]), native._ptr(self.peers[2]),
+            native._ptr(self.peers[4]), native._ptr(self.peers[5]), native._ptr(self.epoch), self.BARRIER_LIMIT_US,
+            native._ptr(ids) if T else None, native._ptr(w) if T else None, native._ptr(self._ws),
+            self._ws.numel(), native._stream()), "moe_ep_route_dispatch_p2p")
+        C = self.capacity
+        L.ops.experts_home(self.rows[:C + T], self.expert[:C + T], self.src[:C + T], self.src_stride,
+                           self.peers[3], valid_rows=max(T, 1) * (k + 1))
+        self._barrier(L)  # every output row is home
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        if T == 0:
+            return out, ids, w
+        w_flat = w.reshape(-1)  # referenced until the launch
         native._check(lib.moe_ep_combine(native._ptr(self.yback), native._ptr(self.identity), native._ptr(w_flat),
                                          T, k, H, 1, native._ptr(out), native._stream()), "moe_ep_combine")
         return out, ids, w

@@ -130,6 +130,9 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_ep_combine": ([_P, _P, _P, _I64, _I64, _I64, _INT, _P, _P], _INT),
     "moe_ep_count_ranks": ([_P, _I64, _I64, _I64, _I64, _P, _P], _INT),
     "moe_ep_barrier_p2p": ([_P, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _INT),
+    "moe_ep_route_dispatch_p2p_workspace_bytes": ([_I64, _I64], _I64),
+    "moe_ep_route_dispatch_p2p": ([_P, _P, _INT, _P, _I64, _I64, _I64, _I64, _I64, _I64, _F32, _I64, _I64,
+                                   _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _I64, _P], _INT),
     "moe_ep_dispatch_p2p": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _P, _P, _I64, _P],
                             _INT),
     "moe_ep_dispatch_p2p_workspace_bytes": ([_I64, _I64, _I64], _I64),
@@ -144,6 +147,7 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_b200_kb_rotate": ([_INT], _INT),
     "moe_b200_fold_epilogues": ([_INT], _INT),
     "moe_b200_router_stages_x": ([_INT], _INT),
+    "moe_b200_prefetch_shared": ([_INT], _INT),
     "moe_b200_shared_side": ([_INT], _INT),
     "moe_b200_stage_timing": ([_INT], _INT),
     "moe_b200_stage_times": ([_P, _INT], _INT),
