@@ -565,12 +565,6 @@ int moe_b200_shared_side(int enable);
  * a cluster of its own, beside the logits clusters (1, the default), or the
  * prologue stages it (0).  Same results bit for bit. */
 int moe_b200_router_stages_x(int enable);
-/* No reference counterpart.  With the router staging x (above), decode
- * layers on tiled weights also request the shared expert's gate/up weights
- * into L2 from the router launch (no routing needed for them) and list the
- * shared expert's work first in the gate/up GEMV (1), or not (0, the
- * default).  Same results bit for bit. */
-int moe_b200_prefetch_shared(int enable);
 
 /* ---------------------------------------------------------------------------
  * Pack-file reads (host only): the FP8 pack loader's byte ranges.

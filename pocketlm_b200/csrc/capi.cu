@@ -75,9 +75,6 @@ bool g_decode_prologue = true;
 // With the decode prologue and bf16 hidden states: the router logits launch stages x (f16 + row scale) in an
 // extra cluster that runs beside the logits clusters, instead of the prologue's one warp per token.
 bool g_router_stages_x = true;
-// With the router staging x: its staging cluster also requests the shared expert's gate/up weights into L2,
-// and the prologue puts the shared expert's chunks first (A/B knob).
-bool g_prefetch_shared = false;
 // Staggered k-block walks in the cp.async warp-MMA stages (MmaArgs::kb_rotate).
 int g_kb_rotate = 0;
 // cp.async decode stages: the activation staging folded into the gate/up GEMV and the combine into the
@@ -1420,19 +1417,10 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
                                                     static_cast<int>(H), hidden_dtype, hidden, static_cast<int>(S_main));
     // the router launch stages x with a cluster of its own, off the prologue's path
     bool router_staged = prologue && g_router_stages_x && hidden_dtype == kDtypeBF16;
-    // with it, the shared expert's gate/up weights (tiled) go to L2 while the router runs, and its chunks
-    // lead the GEMV's work list
-    const bool prefetch_shared = router_staged && g_prefetch_shared && has_shared && weight_layout == 1 && !side;
-    RouterPrefetch pf{};
-    if (prefetch_shared) {
-      pf.ranges[0] = tables + 0 * S + (S - 1);
-      pf.ranges[1] = tables + 2 * S + (S - 1);
-      pf.bytes = fp8_tiled_bytes(I, H);
-    }
     cudaError_t lerr = launch_router_logits_cluster(hidden, hidden_dtype, router_weight, router_dtype, l.logits,
                                                     static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s,
                                                     router_staged ? l.x16 : nullptr,
-                                                    router_staged ? l.xscale : nullptr, pf);
+                                                    router_staged ? l.xscale : nullptr);
     if (lerr == cudaErrorNotSupported) {
       router_staged = false;
       lerr = launch_router_logits_split(hidden, hidden_dtype, router_weight, router_dtype, l.logits,
@@ -1470,7 +1458,6 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
       dp.x16 = l.x16;
       dp.xscale = l.xscale;
       dp.stage_x = router_staged ? 0 : 1;
-      dp.shared_first = prefetch_shared ? 1 : 0;
       dp.zero = l.counters;
       dp.zero_n = l.n_counters;
       MOE_CUDA(launch_decode_prologue(dp, hidden_dtype, s), "decode prologue");
@@ -1924,12 +1911,6 @@ int moe_b200_kb_rotate(int enable) {
 int moe_b200_fold_epilogues(int enable) {
   if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
   g_fold_epilogues = enable != 0;
-  return kOk;
-}
-
-int moe_b200_prefetch_shared(int enable) {
-  if (enable != 0 && enable != 1) return fail(kBadDims, "enable must be 0 or 1");
-  g_prefetch_shared = enable != 0;
   return kOk;
 }
 

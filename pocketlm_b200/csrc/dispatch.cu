@@ -223,16 +223,12 @@ __global__ void __launch_bounds__(kPrologueThreads) decode_prologue_kernel(Decod
     if (b.pair_entry) b.pair_entry[kept + r] = -1;
   }
 
-  // 3. chunks of <= chunk pairs: segment tid (a routed expert), then the appended shared segment --
-  // or the shared segment first (its weights were prefetched into L2 while the router ran; the GEMV hands
-  // out work in chunk order, so they are read before the routed experts' stream evicts them)
+  // 3. chunks of <= chunk pairs: segment tid (a routed expert), then the appended shared segment
   const ChunkArgs& c = rd.chunks;
   const int cn = c.chunk;
-  const bool has_shared_seg = c.n_segments > b.n_buckets;
-  const int lead = (a.shared_first && has_shared_seg) ? (b.tail + cn - 1) / cn : 0;
   const int nch = tid < b.n_buckets ? (mine + cn - 1) / cn : 0;
   int routed_chunks = 0;
-  int ch = lead + cta_exclusive_scan256(nch, &routed_chunks);
+  int ch = cta_exclusive_scan256(nch, &routed_chunks);
   if (tid < b.n_buckets) {
     for (int q = 0; q < mine; q += cn, ++ch) {
       c.chunk_seg[ch] = tid;
@@ -241,15 +237,15 @@ __global__ void __launch_bounds__(kPrologueThreads) decode_prologue_kernel(Decod
     }
   }
   if (tid == 0) {
-    int n = lead > 0 ? 0 : routed_chunks;
-    if (has_shared_seg) {  // the shared expert's segment
+    int n = routed_chunks;
+    if (c.n_segments > b.n_buckets) {  // the shared expert's segment
       for (int q = 0; q < b.tail; q += cn, ++n) {
         c.chunk_seg[n] = b.n_buckets;
         c.chunk_start[n] = kept + q;
         c.chunk_len[n] = min(cn, b.tail - q);
       }
     }
-    *c.n_chunks = lead > 0 ? lead + routed_chunks : n;
+    *c.n_chunks = n;
   }
 }
 

@@ -75,7 +75,6 @@ struct DecodePrologueArgs {
   __half* x16;         // [tokens, hidden] x / xscale
   float* xscale;       // [tokens]
   int stage_x;         // 0: x16 / xscale were staged already (by the router launch)
-  int shared_first;    // 1: the shared expert's chunks lead the chunk list (its weights were prefetched)
   int32_t* zero;       // [zero_n] set to 0
   int64_t zero_n;
 };

@@ -372,25 +372,12 @@ template <typename T>
 __global__ void __cluster_dims__(kClusterParts, 1, 1) __launch_bounds__(kClusterWarps * kWarp)
     router_logits_cluster_kernel(const T* __restrict__ x, const T* __restrict__ w, float* __restrict__ logits,
                                  int tokens, int hidden, int experts, int kpart, __half* __restrict__ x16,
-                                 float* __restrict__ xscale, RouterPrefetch pf) {
+                                 float* __restrict__ xscale) {
   __shared__ float red[kClusterWarps][16][kClusterTokens];
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
   if (x16 != nullptr && blockIdx.y == gridDim.y - 1) {
-    // weights that need no routing (the shared expert's), requested into L2 while the logits are computed
-    if (pf.bytes > 0) {
-      constexpr int64_t kPiece = 64 * 1024;
-      const int64_t per = (pf.bytes + kPiece - 1) / kPiece;
-      const int64_t lin = static_cast<int64_t>(rank) * blockDim.x + threadIdx.x;
-      for (int64_t i = lin; i < kRouterPrefetchRanges * per; i += static_cast<int64_t>(kClusterParts) * blockDim.x) {
-        const uint8_t* base = reinterpret_cast<const uint8_t*>(pf.ranges[i / per] ? *pf.ranges[i / per] : 0ull);
-        if (!base) continue;
-        const int64_t off = (i % per) * kPiece;
-        const uint32_t bytes = static_cast<uint32_t>(min(kPiece, pf.bytes - off));
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"(bytes) : "memory");
-      }
-    }
     cluster_stage_x<T>(cluster, rank, x, tokens, hidden, kpart, x16, xscale, &red[0][0][0]);
     return;
   }
@@ -574,14 +561,13 @@ static cudaError_t launch_split_w(const void* x, int w_dtype, const void* w, flo
 
 cudaError_t launch_router_logits_cluster(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
                                          int tokens, int hidden, int experts, cudaStream_t stream, __half* x16,
-                                         float* xscale, RouterPrefetch prefetch) {
+                                         float* xscale) {
   if (tokens <= 0) return cudaSuccess;
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(w) % 16 == 0);
   if (x_dtype != w_dtype || (x_dtype != kDtypeBF16 && x_dtype != kDtypeF16) || !aligned || hidden % kSpan != 0)
     return cudaErrorNotSupported;
   if (x16 && (!xscale || tokens > kStageMaxTokens || (reinterpret_cast<uintptr_t>(x16) % 16) != 0))
     return cudaErrorNotSupported;
-  if (!x16 || prefetch.bytes < 0 || prefetch.bytes % 16 != 0) prefetch = RouterPrefetch{};
   const int kpart = static_cast<int>(ceil_div(ceil_div(hidden, kClusterParts), kSpan * kClusterWarps)) *
                     kSpan * kClusterWarps;
   // one more cluster row stages x when asked
@@ -589,11 +575,11 @@ cudaError_t launch_router_logits_cluster(const void* x, int x_dtype, const void*
   if (x_dtype == kDtypeBF16)
     router_logits_cluster_kernel<__nv_bfloat16><<<grid, kClusterWarps * kWarp, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), logits, tokens, hidden, experts,
-        kpart, x16, xscale, prefetch);
+        kpart, x16, xscale);
   else
     router_logits_cluster_kernel<__half><<<grid, kClusterWarps * kWarp, 0, stream>>>(
         static_cast<const __half*>(x), static_cast<const __half*>(w), logits, tokens, hidden, experts, kpart, x16,
-        xscale, prefetch);
+        xscale);
   return cudaGetLastError();
 }
 

@@ -40,18 +40,9 @@ cudaError_t launch_router_logits_split(const void* x, int x_dtype, const void* w
 // xscale; tokens <= 256, 16-byte aligned), one more cluster stages x meanwhile:
 // x16 = x / xscale in f16, xscale a power of two per row, exactly the
 // rows_to_f16 staging.
-// Device memory the staging cluster requests into L2 (cp.async.bulk.prefetch.L2) as it starts: up to
-// kRouterPrefetchRanges ranges of `bytes` (a multiple of 16) whose 16-byte aligned base addresses are read
-// from the device words ranges[i] (null entries and null words are skipped).
-constexpr int kRouterPrefetchRanges = 2;
-struct RouterPrefetch {
-  const uint64_t* ranges[kRouterPrefetchRanges];
-  int64_t bytes;
-};
 cudaError_t launch_router_logits_cluster(const void* x, int x_dtype, const void* w, int w_dtype, float* logits,
                                          int tokens, int hidden, int experts, cudaStream_t stream,
-                                         __half* x16 = nullptr, float* xscale = nullptr,
-                                         RouterPrefetch prefetch = RouterPrefetch{});
+                                         __half* x16 = nullptr, float* xscale = nullptr);
 
 // logits: nparts partial [T, E] matrices part_stride floats apart, summed in part order.
 cudaError_t launch_router_select(const float* logits, const float* bias, const RouterSelectParams& p,

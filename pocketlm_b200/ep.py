@@ -197,14 +197,18 @@ class PeerExchange:
             native._ptr(payload) if has else None, L.world if has else 0, native._ptr(self.peers[4]) if has else None,
             self.BARRIER_LIMIT_US, native._stream()), "moe_ep_barrier_p2p")
 
+    FUSED_SEND_MAX_ROWS = 128  # routed rows per rank the one-CTA send moves (more: the multi-CTA scatter)
+
     def _fused_send(self, L: "ExpertParallelLayer", x: torch.Tensor) -> bool:
         """Whether this step's send side runs as moe_ep_route_dispatch_p2p (the
-        router logits, then one CTA for selection, dispatch and both barriers)."""
+        router logits, then one CTA for selection, dispatch and both barriers).
+        Small decode batches only: one CTA stores every routed row over NVLink,
+        which for 128 rows of 14 KB (16 tokens of DS-V3) is about 1.8 MB."""
         cfg = L.cfg
         return (self.sync == "p2p" and isinstance(L.ops, CudaEPOps) and x.dtype == torch.bfloat16
                 and cfg.scoring_func == "sigmoid" and L.bias is not None
                 and L.router_weight.dtype in (torch.bfloat16, torch.float16)
-                and self.max_tokens <= 128 and self.max_tokens * cfg.top_k <= 1024 and cfg.n_routed <= 256
+                and self.max_tokens * cfg.top_k <= self.FUSED_SEND_MAX_ROWS and cfg.n_routed <= 256
                 and L.world <= 32 and cfg.hidden % 8 == 0)
 
     def forward(self, L: "ExpertParallelLayer", x: torch.Tensor):

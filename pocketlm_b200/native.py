@@ -147,7 +147,6 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_b200_kb_rotate": ([_INT], _INT),
     "moe_b200_fold_epilogues": ([_INT], _INT),
     "moe_b200_router_stages_x": ([_INT], _INT),
-    "moe_b200_prefetch_shared": ([_INT], _INT),
     "moe_b200_shared_side": ([_INT], _INT),
     "moe_b200_stage_timing": ([_INT], _INT),
     "moe_b200_stage_times": ([_P, _INT], _INT),

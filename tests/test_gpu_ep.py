@@ -48,6 +48,10 @@ def _rank_main(rank, world, port, outdir):
         peer_nccl = ExpertParallelLayer(cfg, rank, world, layer=full, device=dev, exchange="p2p", max_tokens=16,
                                         peer_sync="nccl")
         out_sync_nccl, _, _ = peer_nccl.forward(x2)
+        # buffers for 64 tokens per rank: past the fused send's row limit, the multi-launch scatter
+        peer_wide = ExpertParallelLayer(cfg, rank, world, layer=full, device=dev, exchange="p2p", max_tokens=64)
+        assert not peer_wide.peer._fused_send(peer_wide, x2) and peer.peer._fused_send(peer, x2)
+        out_wide, _, _ = peer_wide.forward(x2)
         # the same step replayed from a CUDA graph
         graphed = peer.capture(int(x2.shape[0]))
         out_graph = graphed(x2).clone()
@@ -68,7 +72,8 @@ def _rank_main(rank, world, port, outdir):
         from pocketlm_b200 import native
 
         err = int(native.load_library().moe_b200_device_error(None))
-        torch.save({"out": out.cpu(), "device_error": err, "out_sync_nccl": out_sync_nccl.cpu(), "ids": ids.cpu(), "ref": ref.cpu(), "ref_ids": ref_ids.cpu(), "x": x.cpu(),
+        torch.save({"out": out.cpu(), "device_error": err, "out_sync_nccl": out_sync_nccl.cpu(),
+                    "out_wide": out_wide.cpu(), "ids": ids.cpu(), "ref": ref.cpu(), "ref_ids": ref_ids.cpu(), "x": x.cpu(),
                     "out_p2p": out_p2p.cpu(), "ids_p2p": ids_p2p.cpu(), "out_p2p2": out_p2p2.cpu(),
                     "out_nccl2": out_nccl2.cpu(), "out_graph": out_graph.cpu(), "out_graph2": out_graph2.cpu(),
                     "xp": xp.cpu(), "out_pre": out_pre.cpu(), "ids_pre": ids_pre.cpu(),
@@ -102,6 +107,7 @@ def test_ep_two_gpus_matches_single_gpu_layer_and_oracle():
             assert torch.equal(r["out_p2p"], r["out"])
             assert torch.equal(r["out_p2p2"], r["out_nccl2"])
             assert torch.equal(r["out_sync_nccl"], r["out_nccl2"])  # barrier kind changes no bits
+            assert torch.equal(r["out_wide"], r["out_nccl2"])  # fused or multi-launch send: the same bits
             assert r["device_error"] == 0  # no range check fired, no barrier wait ran out
             assert torch.equal(r["out_graph"], r["out_nccl2"]) and torch.equal(r["out_graph2"], r["out_nccl2"])
             # prefill: the received rows run on the grouped GEMM, as the fused layer's pairs do
