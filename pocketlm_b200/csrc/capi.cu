@@ -13,7 +13,6 @@
 #include "common.cuh"
 #include "dequant.cuh"
 #include "dispatch.cuh"
-#include "dispatch_device.cuh"
 #include "fp8_gemv.cuh"
 #include "plan.cuh"
 #include "prefill_gemm.cuh"
@@ -682,34 +681,6 @@ __global__ void ep_pair_home_kernel(const int32_t* pair_entry, const int32_t* n_
     }
     pair_dst[p] = peer_yback[r] + static_cast<uint64_t>(e * H) * sizeof(float);
   }
-}
-
-// The receive side's set-up of a decode step in one CTA, in place of three
-// launches: the received rows bucketed by local expert (bucket_body_small:
-// row order kept inside an expert, as launch_bucket orders them), every
-// pair's home row (the mapping and range checks of ep_pair_home_kernel) and
-// the warp-MMA GEMV's chunk list (chunk_body).  Up to kBucketThreads rows.
-__global__ void __launch_bounds__(kBucketThreads) ep_receive_setup_kernel(BucketArgs b, ChunkArgs c,
-                                                                          const int32_t* row_src, int64_t src_stride,
-                                                                          int world, int64_t home_rows,
-                                                                          const uint64_t* peer_yback, int64_t H,
-                                                                          uint64_t* pair_dst, int64_t cap,
-                                                                          float* sink) {
-  extern __shared__ uint32_t bucket_sm[];
-  bucket_body_small(b, bucket_sm);  // ends with the CTA synchronised: offsets and pair entries are visible
-  const int64_t n = min(static_cast<int64_t>(b.bucket_offset[b.n_buckets]), cap);
-  for (int64_t p = threadIdx.x; p < n; p += kBucketThreads) {
-    const int32_t j = b.pair_entry[p];
-    const int32_t s = (j >= 0 && j < cap) ? row_src[j] : -1;
-    const int64_t r = s / src_stride, e = s % src_stride;
-    if (s < 0 || r >= world || e >= home_rows) {
-      atomicOr(&g_ep_error, kEpRangeError);
-      pair_dst[p] = reinterpret_cast<uint64_t>(sink);
-      continue;
-    }
-    pair_dst[p] = peer_yback[r] + static_cast<uint64_t>(e * H) * sizeof(float);
-  }
-  chunk_body(c);
 }
 
 // Pair p's fp32 output row y[p] to its home row pair_dst[p] (another GPU's
@@ -1830,34 +1801,18 @@ static int ep_experts(const uint16_t* rows_bf16, const int32_t* row_expert, int6
   ba.key_lo = 0; ba.n_buckets = static_cast<int>(S); ba.bucket_offset = l.m.seg_offset; ba.pair_row = l.m.pair_row;
   ba.pair_weight = l.m.pair_weight; ba.pair_entry = l.m.pair_entry; ba.entry_pair = l.m.entry_pair; ba.tail = 0;
   ba.block_counts = l.bucket_scratch;
+  MOE_CUDA(launch_bucket(ba, s), "expert buckets");
   const int32_t* n_pairs = l.m.seg_offset + S;  // rows routed to a local expert
-  bool chunks_ready = false;
-  if (home && !gemm && R <= kBucketThreads) {
-    // decode sizes: buckets, home rows and the chunk list in one CTA
-    const ChunkArgs ca{l.m.seg_offset, static_cast<int>(S), 8, l.m.chunk_seg, l.m.chunk_start, l.m.chunk_len,
-                       l.m.n_chunks};
-    const size_t smem = (static_cast<size_t>(kBucketThreads) + static_cast<size_t>(S)) * sizeof(int32_t);
-    MOE_CUDA(cudaFuncSetAttribute(ep_receive_setup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(smem)),
-             "receive set-up attributes");
-    ep_receive_setup_kernel<<<1, kBucketThreads, smem, s>>>(ba, ca, home->row_src, home->src_stride, home->world,
-                                                            home->home_rows, home->peer_yback, H, pair_dst, R, sink);
-    MOE_CUDA(cudaGetLastError(), "receive set-up");
-    chunks_ready = true;
-  } else {
-    MOE_CUDA(launch_bucket(ba, s), "expert buckets");
-    if (home) {
-      ep_pair_home_kernel<<<grid_for(R), 256, 0, s>>>(l.m.pair_entry, n_pairs, home->row_src, home->src_stride,
-                                                      home->world, home->home_rows, home->peer_yback, H, pair_dst, R,
-                                                      sink);
-      MOE_CUDA(cudaGetLastError(), "home rows");
-    }
+  if (home) {
+    ep_pair_home_kernel<<<grid_for(R), 256, 0, s>>>(l.m.pair_entry, n_pairs, home->row_src, home->src_stride,
+                                                    home->world, home->home_rows, home->peer_yback, H, pair_dst, R,
+                                                    sink);
+    MOE_CUDA(cudaGetLastError(), "home rows");
   }
   Tables t{tables, tables + S, tables + 2 * S, tables + 3 * S, tables + 4 * S, tables + 5 * S};
   // the GEMM's down epilogue stores each row at its home
   int code = gemm ? run_expert_stages_prefill(t, rows_bf16, true, 1, false, l, R, R, S, I, H, nan_free, s, pair_dst)
-                  : run_expert_stages_mma(t, rows_bf16, true, l, R, R, S, I, H, chunks_ready, nan_free, s,
-                                          weight_layout);
+                  : run_expert_stages_mma(t, rows_bf16, true, l, R, R, S, I, H, false, nan_free, s, weight_layout);
   if (code != kOk) return code;
   if (home) {
     if (!gemm) {
