@@ -57,3 +57,46 @@ def test_peer_entry_points_check_world_and_return_rows():
         assert code == -2, (world, home_rows)
     code = lib.moe_ep_experts_fp8(None, None, 16, H, I, None, 9, None, 1, None, None, 0, None)
     assert code == -1 and b"null" in lib.moe_b200_last_error()
+
+
+def test_barrier_checks_its_arguments_before_launching():
+    """moe_ep_barrier_p2p: tables, world, rank, limit and the payload pair are
+    checked on the host; nothing is launched when they are wrong."""
+    import ctypes
+
+    lib = native.load_library()
+    fake = ctypes.c_void_p(16)  # never dereferenced: the calls return before any launch
+    assert lib.moe_ep_barrier_p2p(None, 2, 0, fake, None, 0, None, 1000, None) == -1
+    assert lib.moe_ep_barrier_p2p(fake, 2, 0, None, None, 0, None, 1000, None) == -1
+    for world, rank, limit in ((0, 0, 1000), (2, 2, 1000), (2, -1, 1000), (2048, 0, 1000), (2, 0, 0)):
+        assert lib.moe_ep_barrier_p2p(fake, world, rank, fake, None, 0, None, limit, None) == -2, (world, rank)
+    # a payload needs its peer buffers and a length, and the other way round
+    assert lib.moe_ep_barrier_p2p(fake, 2, 0, fake, fake, 2, None, 1000, None) == -2
+    assert lib.moe_ep_barrier_p2p(fake, 2, 0, fake, None, 0, fake, 1000, None) == -2
+    assert lib.moe_ep_barrier_p2p(fake, 2, 0, fake, fake, 0, fake, 1000, None) == -2
+
+
+def test_fused_send_checks_its_arguments_before_launching():
+    """moe_ep_route_dispatch_p2p: pointers, dimensions (experts split evenly,
+    room for every source entry) and its one-CTA limits (128 tokens, 1024
+    entries, 256 experts, 32 ranks, aligned rows) are checked on the host."""
+    import ctypes
+
+    lib = native.load_library()
+    fake = ctypes.c_void_p(256)
+    odd = ctypes.c_void_p(258)
+
+    def call(x=fake, rw=fake, T=4, E=256, ng=8, tg=4, k=8, world=8, rank=0, cap=8 * 64, stride=None, sig=fake):
+        stride = T * (k + 1) if stride is None else stride
+        return lib.moe_ep_route_dispatch_p2p(x, rw, 1, fake, T, H, E, ng, tg, k, 2.5, world, rank, cap, stride,
+                                             fake, fake, fake, fake, sig, fake, 1000, fake, fake, fake, 1 << 20, None)
+
+    assert call(rw=None) == -1 and call(sig=None) == -1 and call(x=None) == -1
+    assert call(E=250) == -2                 # 250 experts do not split over 8 ranks
+    assert call(stride=4 * 8) == -2          # no room for the ranks' own shared-expert rows
+    assert call(rank=8) == -2 and call(world=0) == -2
+    assert call(T=129, cap=129 * 64, stride=129 * 9) == -5   # more tokens than one CTA selects
+    assert call(E=512, ng=8, world=8) == -5  # selection scratch holds 256 experts
+    assert call(world=64, E=256, cap=64 * 64) == -5
+    assert call(x=odd) == -5                 # rows must be 16-byte aligned
+    assert lib.moe_ep_route_dispatch_p2p_workspace_bytes(4, 256) >= 4 * 256 * 4
