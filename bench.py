@@ -1063,6 +1063,11 @@ def run_profile_case(args) -> dict:
     dev = torch.device("cuda", 0)
     native.load_library()
     cfg = synth.C2_DSV3
+    if args.profile_experts:
+        # the config-2 expert shapes with fewer routed experts: a few GB on the device, for multi-metric captures
+        cfg = synth.DsMoEConfig(f"c2-{args.profile_experts}e", hidden=cfg.hidden, inter=cfg.inter,
+                                n_routed=args.profile_experts, top_k=cfg.top_k, n_group=cfg.n_group,
+                                topk_group=cfg.topk_group, route_scale=cfg.route_scale)
     xd = synth.make_hidden(args.tokens, cfg.hidden, seed=args.seed).to(dev)
     # route on the GPU with the layer's own (device-generated) router, then
     # materialise exactly the experts that routing selects
@@ -1075,8 +1080,10 @@ def run_profile_case(args) -> dict:
     for _ in range(args.warmup + args.steps):
         layer.forward(xd)
     torch.cuda.synchronize()
-    return {"profile_case": f"c2-dsv3-decode-T{args.tokens}", "experts_materialised": len(experts),
-            "launches": args.warmup + args.steps}
+    gs = cfg.gate_scale_shape
+    gateup_bytes = len(experts) * (2 * cfg.inter * cfg.hidden + 2 * 4 * gs[0] * gs[1])
+    return {"profile_case": f"{cfg.name}-decode-T{args.tokens}", "experts_materialised": len(experts),
+            "gateup_algorithmic_bytes": gateup_bytes, "launches": args.warmup + args.steps}
 
 
 def run_profile_prefill(args) -> dict:
@@ -1194,6 +1201,8 @@ def main() -> None:
                         help="routed experts of the --profile-prefill layer (32 small case, 256 full config 3)")
     parser.add_argument("--profile-q4", action="store_true",
                         help="run the config-4 Q4 layer for --tokens tokens (an ncu case)")
+    parser.add_argument("--profile-experts", type=int, default=0,
+                        help="with --profile: routed experts of the profiled layer (0: config 2's 256)")
     parser.add_argument("--profile-no-experts", action="store_true",
                         help="with --profile: materialise no expert (for captures of the routing kernels)")
     args = parser.parse_args()

@@ -1155,10 +1155,12 @@ static LayerPlan plan_layer(Plan& p, int64_t T, int64_t H, int64_t I, int64_t E,
 
 // The expert stages on the tcgen05 grouped GEMM (tiled weights): gather the
 // pairs' fp16 rows, gate/up + SwiGLU, stage the activations, down.
+// y16: the down GEMM stores bf16 rows into m.y's memory (the whole layer's path, whose combine reads
+// them); otherwise fp32 rows, or rows through out_row.
 static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16, int64_t k, bool shared,
                                      const LayerPlan& l, int64_t T,
                                      int64_t pairs, int64_t n_segments, int64_t I, int64_t H, const uint8_t* nan_free,
-                                     cudaStream_t s, const uint64_t* out_row = nullptr) {
+                                     cudaStream_t s, const uint64_t* out_row = nullptr, bool y16 = false) {
   const MlpScratch& m = l.m;
   // each token's row staged once and written to its pairs' rows (the shared pairs follow the routed ones)
   cudaError_t serr = launch_scatter_rows(x, x_bf16 ? kDtypeBF16 : kDtypeF32, T, H, m.entry_pair, static_cast<int>(k),
@@ -1192,6 +1194,10 @@ static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16
   g2.w0 = t.dw; g2.s0 = t.ds; g2.w1 = nullptr; g2.s1 = nullptr;
   g2.a16 = l.act16; g2.ascale = l.ascale;
   g2.out = m.y; g2.out_row = out_row; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
+  if (y16 && !out_row) {
+    g2.out16 = reinterpret_cast<__nv_bfloat16*>(m.y);
+    g2.out = nullptr;
+  }
   g2.scale_cols = static_cast<int>(ceil_div(I, kBlock));
   MOE_CUDA(launch_prefill_gemm(g2, false, mtiles_bound * (H / 256), s), "down GEMM");
   stage_mark(s);
@@ -1481,9 +1487,11 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   const bool prefill = weight_layout == 1 && T >= kPrefillMinTokens && l.a16 != nullptr &&
                        prefill_supported(H, I, true) && prefill_supported(I, H, false);
   if (prefill) {
+    // each expert's output rounded to bf16 by the down GEMM (the reference rounds it there too,
+    // fp8_source.py:1839-1847): half the bytes written and read back by the combine
     code = run_expert_stages_prefill(t, hidden, hidden_dtype == kDtypeBF16, k, has_shared != 0, l, T,
                                      T * k + (has_shared ? T : 0), S, I,
-                                     H, nan_free, s);
+                                     H, nan_free, s, nullptr, true);
   } else if (use_mma) {
     const LayerCombine lc{reinterpret_cast<__nv_bfloat16*>(out_bf16), T, k, has_shared != 0};
     // with the side stream, the main stream stages only the routed pairs' activations
@@ -1499,6 +1507,10 @@ int moe_ds_moe_layer_fp8(const void* hidden, int hidden_dtype, int64_t T, int64_
   // 4. combine: routed slots in top-k order, then the shared expert; one bf16 rounding
   CombineArgs c{};
   c.y = l.m.y; c.row_ptr = nullptr; c.stride = static_cast<int>(k); c.row_pairs = l.m.entry_pair;
+  if (prefill) {
+    c.y = nullptr;
+    c.y16 = reinterpret_cast<const __nv_bfloat16*>(l.m.y);
+  }
   c.pair_weight = l.m.pair_weight; c.extra_base = has_shared ? static_cast<int>(T * k) : -1;
   c.T = static_cast<int>(T); c.H = static_cast<int>(H);
   c.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);

@@ -214,6 +214,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) grouped_gemv_kernel(GemvArgs 
 // in list order (the reference's summation order: fp8_linear.cpp:557-585 for
 // table order, :964-975 for pair order).
 // ---------------------------------------------------------------------------
+// row p's values h .. h + 3 (vec) or h of the fp32 or bf16 outputs
+MOE_D void load_y(const CombineArgs& a, int64_t p, int h, bool vec, float (&v)[4]) {
+  if (a.y16) {
+    const __nv_bfloat16* yp = a.y16 + p * a.H + h;
+    if (vec) {
+      const uint2 u = *reinterpret_cast<const uint2*>(yp);
+      v[0] = __uint_as_float(u.x << 16); v[1] = __uint_as_float(u.x & 0xFFFF0000u);
+      v[2] = __uint_as_float(u.y << 16); v[3] = __uint_as_float(u.y & 0xFFFF0000u);
+    } else {
+      v[0] = __bfloat162float(yp[0]);
+    }
+    return;
+  }
+  const float* yp = a.y + p * a.H + h;
+  if (vec) {
+    const float4 f = *reinterpret_cast<const float4*>(yp);
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  } else {
+    v[0] = yp[0];
+  }
+}
+
 __global__ void combine_kernel(CombineArgs a) {
   const bool vec = (a.H % 4) == 0;
   const int h = (blockIdx.x * blockDim.x + threadIdx.x) * (vec ? 4 : 1);
@@ -228,20 +250,14 @@ __global__ void combine_kernel(CombineArgs a) {
       const int p = a.row_pairs ? a.row_pairs[j] : j;
       if (p < 0) continue;
       const float w = a.pair_weight ? a.pair_weight[p] : 1.0f;
-      const float* yp = a.y + static_cast<int64_t>(p) * a.H + h;
-      if (vec) {
-        const float4 v = *reinterpret_cast<const float4*>(yp);
-        acc[0] = fmaf(w, v.x, acc[0]);
-        acc[1] = fmaf(w, v.y, acc[1]);
-        acc[2] = fmaf(w, v.z, acc[2]);
-        acc[3] = fmaf(w, v.w, acc[3]);
-      } else {
-        acc[0] = fmaf(w, yp[0], acc[0]);
-      }
+      float v[4];
+      load_y(a, p, h, vec, v);
+      for (int i = 0; i < width; ++i) acc[i] = fmaf(w, v[i], acc[i]);
     }
     if (a.extra_base >= 0) {
-      const float* yp = a.y + static_cast<int64_t>(a.extra_base + t) * a.H + h;
-      for (int i = 0; i < width; ++i) acc[i] += yp[i];
+      float v[4];
+      load_y(a, a.extra_base + t, h, vec, v);
+      for (int i = 0; i < width; ++i) acc[i] += v[i];
     }
     const int64_t o = static_cast<int64_t>(t) * a.H + h;
     for (int i = 0; i < width; ++i) {

@@ -30,7 +30,8 @@ struct GemvArgs {
 };
 
 struct CombineArgs {
-  const float* y;            // [P, H]
+  const float* y;            // [P, H] fp32, or null when y16 is given
+  const __nv_bfloat16* y16;  // [P, H] bf16 (the prefill GEMM's rounded expert outputs), or null
   const int32_t* row_ptr;    // [T + 1] or null: row t owns [t*stride, (t+1)*stride)
   int stride;
   const int32_t* row_pairs;  // pair index per list entry (-1 = skip), or null: entry = pair

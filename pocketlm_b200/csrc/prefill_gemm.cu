@@ -608,9 +608,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         // absent expert: its pairs' output rows are zero
         if (row_in_tile < tr.rows) {
           const int64_t pz = tr.row0 + row_in_tile;
-          float* row = !GATEUP && a.out_row ? reinterpret_cast<float*>(a.out_row[pz]) : a.out + pz * N;
-          float4* out = reinterpret_cast<float4*>(row + tr.nt * (GATEUP ? kBN / 2 : kBN));
-          for (int j = 0; j < (GATEUP ? kBN / 2 : kBN) / 4; ++j) out[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (!GATEUP && a.out16) {
+            uint4* out = reinterpret_cast<uint4*>(a.out16 + pz * N + tr.nt * kBN);
+            for (int j = 0; j < kBN / 8; ++j) out[j] = make_uint4(0u, 0u, 0u, 0u);
+          } else {
+            float* row = !GATEUP && a.out_row ? reinterpret_cast<float*>(a.out_row[pz]) : a.out + pz * N;
+            float4* out = reinterpret_cast<float4*>(row + tr.nt * (GATEUP ? kBN / 2 : kBN));
+            for (int j = 0; j < (GATEUP ? kBN / 2 : kBN) / 4; ++j) out[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
         }
         continue;
       }
@@ -634,31 +639,37 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       // four lanes per row (64 contiguous bytes) on the way out; 16-byte
       // slots XOR-swizzled by row so both phases are free of bank conflicts
       const int row_base = half * kSubM + quad * kWarp;  // the warp's first row in the tile
-      // the output rows this lane stores in emit16: rows lane / 4 + 8 i of the warp's 32
-      float* out_row[4] = {nullptr, nullptr, nullptr, nullptr};
+      // the output rows this lane stores in emit64: rows lane / 4 + 8 i of the warp's 32 (byte addresses of
+      // the tile's first column: fp32 rows, or bf16 rows with out16)
+      const bool y16 = !GATEUP && a.out16 != nullptr;
+      unsigned char* out_row[4] = {nullptr, nullptr, nullptr, nullptr};
       if (!GATEUP) {
-        float* mine = nullptr;
-        if (valid) mine = (a.out_row ? reinterpret_cast<float*>(a.out_row[p]) : a.out + p * N) + tr.nt * kBN;
+        unsigned char* mine = nullptr;
+        if (valid)
+          mine = y16 ? reinterpret_cast<unsigned char*>(a.out16 + p * N + tr.nt * kBN)
+                     : reinterpret_cast<unsigned char*>(
+                           (a.out_row ? reinterpret_cast<float*>(a.out_row[p]) : a.out + p * N) + tr.nt * kBN);
         const uint64_t m64 = reinterpret_cast<uint64_t>(mine);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int src = lane / 4 + 8 * i;
           const uint32_t lo = __shfl_sync(0xFFFFFFFFu, static_cast<uint32_t>(m64), src);
           const uint32_t hi = __shfl_sync(0xFFFFFFFFu, static_cast<uint32_t>(m64 >> 32), src);
-          out_row[i] = reinterpret_cast<float*>((static_cast<uint64_t>(hi) << 32) | lo);
+          out_row[i] = reinterpret_cast<unsigned char*>((static_cast<uint64_t>(hi) << 32) | lo);
         }
       }
-      auto emit16 = [&](const float (&v)[16], int c0) {
+      // 64 bytes of each of the warp's rows (16 fp32 or 32 bf16 columns) starting at byte b0 of the tile
+      auto emit64 = [&](const uint32_t (&v)[16], int b0) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          st_shared_v4(stage + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16), __float_as_uint(v[4 * j]),
-                       __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+          st_shared_v4(stage + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                       v[4 * j + 3]);
         __syncwarp();
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int rr = lane / 4 + 8 * i, j = lane % 4;
           const uint4 w = ld_shared_v4(stage + rr * 64 + ((j ^ ((rr >> 1) & 3)) * 16));
-          if (row_base + rr < tr.rows) *reinterpret_cast<uint4*>(out_row[i] + c0 + 4 * j) = w;
+          if (row_base + rr < tr.rows) *reinterpret_cast<uint4*>(out_row[i] + b0 + 16 * j) = w;
         }
         __syncwarp();
       };
@@ -697,15 +708,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
           tmem_ld16(taddr + c0, d0);
           tmem_ld16(taddr + c0 + 16, d1);
           tmem_ld_wait();
-          float o[16];
+          float o0[16], o1[16];
 #pragma unroll
-          for (int q = 0; q < 16; ++q)
-            o[q] = __uint_as_float(d0[q]) * xs * (WF == kPrefillQ4Row ? __half2float(csc0[c0 + q]) : 1.0f);
-          emit16(o, c0);
+          for (int q = 0; q < 16; ++q) {
+            o0[q] = __uint_as_float(d0[q]) * xs * (WF == kPrefillQ4Row ? __half2float(csc0[c0 + q]) : 1.0f);
+            o1[q] = __uint_as_float(d1[q]) * xs * (WF == kPrefillQ4Row ? __half2float(csc0[c0 + 16 + q]) : 1.0f);
+          }
+          uint32_t w[16];
+          if (y16) {
+            // 32 columns rounded to bf16, two per word
 #pragma unroll
-          for (int q = 0; q < 16; ++q)
-            o[q] = __uint_as_float(d1[q]) * xs * (WF == kPrefillQ4Row ? __half2float(csc0[c0 + 16 + q]) : 1.0f);
-          emit16(o, c0 + 16);
+            for (int q = 0; q < 8; ++q) {
+              const __nv_bfloat162 lo = __floats2bfloat162_rn(o0[2 * q], o0[2 * q + 1]);
+              const __nv_bfloat162 hi = __floats2bfloat162_rn(o1[2 * q], o1[2 * q + 1]);
+              w[q] = *reinterpret_cast<const uint32_t*>(&lo);
+              w[8 + q] = *reinterpret_cast<const uint32_t*>(&hi);
+            }
+            emit64(w, c0 * 2);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) w[q] = __float_as_uint(o0[q]);
+            emit64(w, c0 * 4);
+#pragma unroll
+            for (int q = 0; q < 16; ++q) w[q] = __float_as_uint(o1[q]);
+            emit64(w, (c0 + 16) * 4);
+          }
         }
       }
       tc_fence_before();
@@ -892,7 +919,9 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, bool gateup, int64_t max_t
   if (!prefill_supported(a.K, a.N, gateup) || a.rows_a <= 0) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(a.a16) & 15u) != 0) return cudaErrorInvalidValue;
   // outputs: rows of out, or (down GEMM only) the row table
-  if (gateup ? (!a.out || a.out_row) : (!a.out && !a.out_row)) return cudaErrorInvalidValue;
+  if (gateup ? (!a.out || a.out_row || a.out16) : (!a.out && !a.out_row && !a.out16)) return cudaErrorInvalidValue;
+  if (a.out16 && (a.out_row || (reinterpret_cast<uintptr_t>(a.out16) & 15u) != 0 || a.N % 8 != 0))
+    return cudaErrorInvalidValue;
   auto encode = encode_fn();
   if (!encode) return cudaErrorNotSupported;
   // A boxes of 128, 64 and 32 rows (the smaller ones for small tiles)

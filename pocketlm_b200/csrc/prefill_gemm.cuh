@@ -1,5 +1,6 @@
 // Prefill grouped GEMM on tcgen05 (prefill_gemm.cu).
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -23,6 +24,9 @@ struct PrefillArgs {
   // down GEMM only, or null: pair p's output row goes to out_row[p] (N fp32,
   // 16-byte aligned; may be another GPU's memory) instead of out + p * N
   const uint64_t* out_row;
+  // down GEMM only, or null: the outputs as bf16 rows [rows_a, N] instead of fp32 (each expert's
+  // output rounded once, as the reference rounds it before its weighted add)
+  __nv_bfloat16* out16;
   int N;                   // output columns (gate/up: intermediate size)
   int K;
   int scale_cols;          // ceil(K / 128)

@@ -113,7 +113,9 @@ def test_ep_two_gpus_matches_single_gpu_layer_and_oracle():
             # prefill: the received rows run on the grouped GEMM, as the fused layer's pairs do
             same = (torch.sort(r["ids_pre"], 1).values == torch.sort(r["ref_pre_ids"], 1).values).all(dim=1)
             assert same.float().mean() > 0.99
-            assert rel_l2(r["out_pre"][same], r["ref_pre"][same]) <= 1e-3
+            # the single-GPU layer's prefill rounds each expert output to bf16 before its combine; the
+            # exchange returns fp32 rows
+            assert rel_l2(r["out_pre"][same], r["ref_pre"][same]) <= 4e-3
             assert torch.equal(r["out_pre_p2p"], r["out_pre"])
             expected, route = oracle.ds_moe_layer(r["xp"], layer)
             bad, excused = id_mismatches(r["ids_pre"], route)

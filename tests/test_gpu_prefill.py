@@ -3,8 +3,12 @@
 decode GEMV path on the same layer.
 
 The prefill GEMM folds each 128 x 128 block scale into the weights as it
-converts them to fp16 (w * s rounded to fp16), so it agrees with the exact
-GEMV path to a few parts in 1e4 rather than bit for bit."""
+converts them to fp16 (w * s rounded to fp16) and, in the whole layer,
+rounds each expert's output row to bf16 before the combine (where the
+reference rounds it too), so it agrees with the exact GEMV path, which keeps
+fp32 rows, to about 1e-3 rather than bit for bit (checked at 4e-3)."""
+
+GEMV_TOL = 4e-3
 
 import pytest
 import torch
@@ -45,7 +49,7 @@ def _run(cfg, tokens, seed, bias="uniform"):
 @pytest.mark.parametrize("cfg,tokens", [(synth.C1_TINY, 512), (synth.C1_TINY, 2048), (C_MID, 1024)])
 def test_prefill_matches_oracle_and_gemv(cuda_device, cfg, tokens):
     layer, x, out, ids, gemv = _run(cfg, tokens, seed=40 + tokens)
-    assert rel_l2(out, gemv) <= 2e-3 and cos_dist(out, gemv) <= 1e-5
+    assert rel_l2(out, gemv) <= GEMV_TOL and cos_dist(out, gemv) <= 1e-5
     expected, route = oracle.ds_moe_layer(x.cpu(), layer)
     bad, excused = id_mismatches(ids, route)
     assert bad == excused
@@ -58,13 +62,13 @@ def test_prefill_zipf_routing_uneven_experts(cuda_device):
     layer, x, out, ids, gemv = _run(C_MID, 1536, seed=77, bias="zipf")
     counts = torch.bincount(ids.reshape(-1).cpu(), minlength=C_MID.n_routed)
     assert counts.max() > 4 * counts.float().mean()
-    assert rel_l2(out, gemv) <= 2e-3
+    assert rel_l2(out, gemv) <= GEMV_TOL
 
 
 def test_prefill_dsv3_shape(cuda_device):
     cfg = synth.C2_DSV3
     layer, x, out, ids, gemv = _run(cfg, 512, seed=91)
-    assert rel_l2(out, gemv) <= 2e-3 and cos_dist(out, gemv) <= 1e-5
+    assert rel_l2(out, gemv) <= GEMV_TOL and cos_dist(out, gemv) <= 1e-5
     n = 48  # the oracle on a slice of the batch: every token is computed independently
     expected, route = oracle.ds_moe_layer(x[:n].cpu(), layer)
     bad, excused = id_mismatches(ids[:n], route)
@@ -84,4 +88,4 @@ def test_prefill_skips_absent_experts_like_the_gemv(cuda_device):
     gemv = DsMoELayerGPU(layer, allow_partial=True, tiled=False).forward(x).clone()
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all()
-    assert rel_l2(out, gemv) <= 2e-3 and cos_dist(out, gemv) <= 1e-5
+    assert rel_l2(out, gemv) <= GEMV_TOL and cos_dist(out, gemv) <= 1e-5
