@@ -573,10 +573,12 @@ def run_ours(args, rank: int, world: int) -> dict | None:
 def run_prefill(args, dev, flush, peaks, token_list) -> dict:
     """Config 3 on one GPU: the DS-V3 layer with the Zipf-skewed router bias,
     prefill batches on the tcgen05 grouped GEMM (prefill_gemm.cu).  Each step
-    is one eager layer forward (7 + 4 launches; launch cost is negligible at
-    these sizes), CUDA-event timed after warm-up with an L2 flush between
-    steps.  FLOPs are the layer's algorithmic ones: T * (k + 1) * 3 * 2 * H * I
-    for the experts + T * 2 * H * E for the router."""
+    is one replay of the layer captured as a CUDA graph, as the decode steps
+    are (the eager forward's time is reported beside it: its host launches
+    leave gaps of 0.2-0.9 ms depending on the host), CUDA-event timed after
+    warm-up with an L2 flush between steps.  FLOPs are the layer's
+    algorithmic ones: T * (k + 1) * 3 * 2 * H * I for the experts + T * 2 * H
+    * E for the router."""
     from pocketlm_b200 import synth
     from pocketlm_b200.runtime import DsMoELayerGPU
 
@@ -593,10 +595,13 @@ def run_prefill(args, dev, flush, peaks, token_list) -> dict:
         torch.cuda.synchronize()
         steps = max(3, min(args.steps, 10))
         y = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=dev)
-        ms = statistics.mean(time_steps(lambda: gpu_layer.forward(x, out=y), steps, args.warmup, flush))
+        eager_ms = statistics.mean(time_steps(lambda: gpu_layer.forward(x, out=y), steps, args.warmup, flush))
+        graphed = gpu_layer.capture(T)
+        graphed.input.copy_(x)
+        ms = statistics.mean(time_steps(graphed.replay, steps, args.warmup, flush))
         torch.cuda.synchronize()
-        checked[T] = (x.cpu(), y.cpu(), ids.cpu())  # the last timed forward's output
-        del y
+        checked[T] = (x.cpu(), graphed.output.cpu(), graphed.ids.cpu())  # the last timed replay's output
+        del y, graphed
         stages = stage_times(gpu_layer, x, 3, flush)
         flops = T * (cfg.top_k + 1) * 3 * 2 * cfg.hidden * cfg.inter + T * 2 * cfg.hidden * cfg.n_routed
         pairs = T * (cfg.top_k + 1)
@@ -604,7 +609,7 @@ def run_prefill(args, dev, flush, peaks, token_list) -> dict:
         gu_ms = stages[1] if len(stages) > 1 else None
         counts = torch.bincount(ids.reshape(-1), minlength=cfg.n_routed)
         out[str(T)] = {
-            "tokens": T, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
+            "tokens": T, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3), "eager_ms_per_step": eager_ms,
             "tflops": flops / (ms / 1e3) / 1e12,
             "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / bf16_peak,
             "frac_of_fp8_nominal": flops / (ms / 1e3) / 1e12 / 4500.0,

@@ -214,11 +214,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) grouped_gemv_kernel(GemvArgs 
 // in list order (the reference's summation order: fp8_linear.cpp:557-585 for
 // table order, :964-975 for pair order).
 // ---------------------------------------------------------------------------
-// row p's values h .. h + 3 (vec) or h of the fp32 or bf16 outputs
-MOE_D void load_y(const CombineArgs& a, int64_t p, int h, bool vec, float (&v)[4]) {
+// W values of row p from column h (W = 8: bf16 rows, 16-byte loads; 4: fp32 or bf16; 1: any)
+template <int W>
+MOE_D void load_y(const CombineArgs& a, int64_t p, int h, float (&v)[W]) {
   if (a.y16) {
     const __nv_bfloat16* yp = a.y16 + p * a.H + h;
-    if (vec) {
+    if constexpr (W == 8) {
+      const uint4 u = *reinterpret_cast<const uint4*>(yp);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+      }
+    } else if constexpr (W == 4) {
       const uint2 u = *reinterpret_cast<const uint2*>(yp);
       v[0] = __uint_as_float(u.x << 16); v[1] = __uint_as_float(u.x & 0xFFFF0000u);
       v[2] = __uint_as_float(u.y << 16); v[3] = __uint_as_float(u.y & 0xFFFF0000u);
@@ -228,39 +237,44 @@ MOE_D void load_y(const CombineArgs& a, int64_t p, int h, bool vec, float (&v)[4
     return;
   }
   const float* yp = a.y + p * a.H + h;
-  if (vec) {
+  if constexpr (W == 4) {
     const float4 f = *reinterpret_cast<const float4*>(yp);
     v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
   } else {
-    v[0] = yp[0];
+#pragma unroll
+    for (int i = 0; i < W; ++i) v[i] = yp[i];
   }
 }
 
+template <int W>
 __global__ void combine_kernel(CombineArgs a) {
-  const bool vec = (a.H % 4) == 0;
-  const int h = (blockIdx.x * blockDim.x + threadIdx.x) * (vec ? 4 : 1);
+  const int h = (blockIdx.x * blockDim.x + threadIdx.x) * W;
   if (h >= a.H) return;
-  const int width = vec ? 4 : 1;
   for (int t = blockIdx.y; t < a.T; t += gridDim.y) {  // rows past grid.y's limit of 65535 loop
     const int lo = a.row_ptr ? a.row_ptr[t] : t * a.stride;
     const int hi = a.row_ptr ? a.row_ptr[t + 1] : lo + a.stride;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float acc[W];
+#pragma unroll
+    for (int i = 0; i < W; ++i) acc[i] = 0.0f;
 #pragma unroll 8
     for (int j = lo; j < hi; ++j) {
       const int p = a.row_pairs ? a.row_pairs[j] : j;
       if (p < 0) continue;
       const float w = a.pair_weight ? a.pair_weight[p] : 1.0f;
-      float v[4];
-      load_y(a, p, h, vec, v);
-      for (int i = 0; i < width; ++i) acc[i] = fmaf(w, v[i], acc[i]);
+      float v[W];
+      load_y<W>(a, p, h, v);
+#pragma unroll
+      for (int i = 0; i < W; ++i) acc[i] = fmaf(w, v[i], acc[i]);
     }
     if (a.extra_base >= 0) {
-      float v[4];
-      load_y(a, a.extra_base + t, h, vec, v);
-      for (int i = 0; i < width; ++i) acc[i] += v[i];
+      float v[W];
+      load_y<W>(a, a.extra_base + t, h, v);
+#pragma unroll
+      for (int i = 0; i < W; ++i) acc[i] += v[i];
     }
     const int64_t o = static_cast<int64_t>(t) * a.H + h;
-    for (int i = 0; i < width; ++i) {
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
       if (a.out_f32) a.out_f32[o + i] = acc[i];
       if (a.out_f16) a.out_f16[o + i] = __float2half_rn(acc[i]);
       if (a.out_bf16)
@@ -329,11 +343,15 @@ cudaError_t launch_grouped_gemv(const GemvArgs& a, int x_dtype, int ns, int epi,
 
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t stream) {
   if (a.T <= 0) return cudaSuccess;
-  const int per_thread = (a.H % 4) == 0 ? 4 : 1;
+  // bf16 rows: 8 columns per thread (one 16-byte load per pair); fp32: 4
+  const bool y16_aligned = a.y16 && (reinterpret_cast<uintptr_t>(a.y16) & 15u) == 0;
+  const int per_thread = (y16_aligned && a.H % 8 == 0) ? 8 : (a.H % 4) == 0 ? 4 : 1;
   const int threads = 64;
   dim3 grid(static_cast<unsigned>(ceil_div(ceil_div(a.H, per_thread), threads)),
             static_cast<unsigned>(std::min(a.T, 65535)));
-  combine_kernel<<<grid, threads, 0, stream>>>(a);
+  if (per_thread == 8) combine_kernel<8><<<grid, threads, 0, stream>>>(a);
+  else if (per_thread == 4) combine_kernel<4><<<grid, threads, 0, stream>>>(a);
+  else combine_kernel<1><<<grid, threads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

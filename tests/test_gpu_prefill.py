@@ -89,3 +89,15 @@ def test_prefill_skips_absent_experts_like_the_gemv(cuda_device):
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all()
     assert rel_l2(out, gemv) <= GEMV_TOL and cos_dist(out, gemv) <= 1e-5
+
+
+def test_prefill_graph_replay_matches_eager(cuda_device):
+    """A prefill-sized layer (the tcgen05 path) captured as a CUDA graph: every
+    replay gives the eager forward's bits (the bench times prefill this way)."""
+    layer = synth.make_fp8_layer(C_MID, seed=93, device="cuda", bias_kind="zipf")
+    gpu = DsMoELayerGPU(layer)
+    x = synth.make_hidden(1024, C_MID.hidden, seed=94, device="cuda")
+    eager = gpu.forward(x).clone()
+    graphed = gpu.capture(1024)
+    for _ in range(2):
+        assert torch.equal(graphed(x), eager)
