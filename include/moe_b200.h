@@ -333,11 +333,13 @@ int64_t moe_moe_forward_fp16_workspace_bytes(int64_t seq_len, int64_t hidden_siz
  *   moe_route_topk -> moe_ep_dispatch_pack -> all-to-all of send_offsets'
  *   counts, rows and expert ids (the caller's collective) ->
  *   moe_ep_experts_fp8 over the received rows (+ the rank's own rows for
- *   the shared expert) -> reverse all-to-all of the fp32 outputs ->
- *   moe_ep_combine.
- * The arithmetic per (token, expert) pair and the combine order (top-k slot
- * order, then the shared expert, fp32, one bf16 rounding) are those of
- * moe_ds_moe_layer_fp8.
+ *   the shared expert) -> the outputs rounded to bf16 (round to nearest
+ *   even) -> reverse all-to-all of them -> moe_ep_combine.
+ * The arithmetic per (token, expert) pair is that of moe_ds_moe_layer_fp8;
+ * every expert output is rounded to bf16 before the combine, as the
+ * reference rounds it (fp8_source.py:1839-1847) and as the whole layer's
+ * prefill does; the combine order is top-k slot order, then the shared
+ * expert, in fp32, with one final bf16 rounding.
  * ------------------------------------------------------------------------- */
 
 /* Group the (token, slot) entries of ids / weights ([tokens, top_k]) by
@@ -362,9 +364,10 @@ int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int
 int64_t moe_ep_experts_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t intermediate, int64_t num_local);
 
 /* out_bf16[t] = bf16(sum_slot pos_weight[p] * y[p] (+ y[tokens*top_k + t]
- * when has_shared)), p = entry_pos[t * top_k + slot], slots in order. */
-int moe_ep_combine(const float* y, const int32_t* entry_pos, const float* pos_weight, int64_t tokens, int64_t top_k,
-                   int64_t hidden_dim, int has_shared, uint16_t* out_bf16, void* stream);
+ * when has_shared)), p = entry_pos[t * top_k + slot], slots in order; y is
+ * the bf16 output rows, summed in fp32. */
+int moe_ep_combine(const uint16_t* y_bf16, const int32_t* entry_pos, const float* pos_weight, int64_t tokens,
+                   int64_t top_k, int64_t hidden_dim, int has_shared, uint16_t* out_bf16, void* stream);
 
 /* No reference counterpart (the reference runs on one host; its ranks do not
  * exist).  A barrier of the expert-parallel ranks over peer memory, in place
@@ -387,7 +390,7 @@ int moe_ep_barrier_p2p(const uint64_t* peer_sig, int64_t world, int64_t rank, ui
  * receive buffers in peer-accessible memory (e.g. torch symmetric memory) --
  * rows [capacity (+ own rows), hidden] bf16, expert int32 [capacity] (-1 =
  * empty, reset before each step), src int32 [capacity], and a return buffer
- * [src_stride + tokens, hidden] fp32 -- whose addresses on every rank the
+ * [src_stride + tokens, hidden] bf16 -- whose addresses on every rank the
  * caller passes as device arrays uint64 [world].  A step:
  *   moe_ep_count_ranks -> all-gather of the [world] counts into
  *   count_matrix [world][world] (row = source rank) -> moe_ep_dispatch_p2p
@@ -440,16 +443,17 @@ int moe_ep_dispatch_p2p(const int64_t* ids, const uint16_t* hidden_bf16, int64_t
                         int64_t capacity, int64_t src_stride, const uint64_t* peer_rows, const uint64_t* peer_expert,
                         const uint64_t* peer_src, void* workspace, int64_t workspace_bytes, void* stream);
 int64_t moe_ep_dispatch_p2p_workspace_bytes(int64_t tokens, int64_t top_k, int64_t world);
-/* Received row j with recv_expert[j] >= 0 goes to row recv_src[j] % src_stride
- * of rank recv_src[j] / src_stride's return buffer.  Every src code is checked
+/* Received row j's fp32 output y[j] (recv_expert[j] >= 0), rounded to bf16,
+ * goes to row recv_src[j] % src_stride of rank recv_src[j] / src_stride's
+ * return buffer (bf16 rows).  Every src code is checked
  * before the store: a rank outside [0, world) or a row at or past home_rows
  * (the rows of each rank's return buffer, <= src_stride) is skipped and sets
  * code 64 in moe_b200_device_error. */
 int moe_ep_return_p2p(const float* y, int64_t rows, const int32_t* recv_expert, const int32_t* recv_src,
                       int64_t hidden_dim, int64_t src_stride, int64_t world, int64_t home_rows,
                       const uint64_t* peer_yback, void* stream);
-/* moe_ep_experts_fp8 and moe_ep_return_p2p in one call: received row j's fp32
- * output goes straight to row (row_src[j] % src_stride) of the return buffer
+/* moe_ep_experts_fp8 and moe_ep_return_p2p in one call: received row j's
+ * output, rounded to bf16, goes straight to row (row_src[j] % src_stride) of the return buffer
  * of rank row_src[j] / src_stride (peer_yback [world], as above), stored over
  * NVLink by the down GEMM's epilogue or by a copy kernel after the warp-MMA
  * experts.  Rows whose expert id is out of range are neither computed nor

@@ -629,9 +629,15 @@ __global__ void ep_p2p_scatter_kernel(const uint16_t* hidden, const int64_t* ids
   __threadfence_system();
 }
 
+// fp32 -> bf16 of four values (round to nearest even), as 8 bytes
+MOE_D uint2 bf16x4(const float4& f) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(f.x, f.y), hi = __floats2bfloat162_rn(f.z, f.w);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
 // Expert outputs home: received row j (valid: expert >= 0) came from entry
-// e of rank r (src = r * src_stride + e); its fp32 output row goes to row e
-// of rank r's return buffer.  One warp per row.
+// e of rank r (src = r * src_stride + e); its output row goes, rounded to
+// bf16, to row e of rank r's return buffer.  One warp per row.
 __global__ void ep_p2p_return_kernel(const float* y, int64_t rows, const int32_t* recv_expert, const int32_t* recv_src,
                                      int64_t H, int64_t src_stride, int world, int64_t home_rows,
                                      const uint64_t* peer_yback, int vec) {
@@ -647,12 +653,12 @@ __global__ void ep_p2p_return_kernel(const float* y, int64_t rows, const int32_t
       continue;
     }
     const float* src = y + j * H;
-    float* dst = reinterpret_cast<float*>(peer_yback[r]) + e * H;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peer_yback[r]) + e * H;
     if (vec) {
       for (int64_t i = lane; i < H / 4; i += 32)
-        reinterpret_cast<float4*>(dst)[i] = __ldcs(reinterpret_cast<const float4*>(src) + i);
+        reinterpret_cast<uint2*>(dst)[i] = bf16x4(__ldcs(reinterpret_cast<const float4*>(src) + i));
     } else {
-      for (int64_t i = lane; i < H; i += 32) dst[i] = src[i];
+      for (int64_t i = lane; i < H; i += 32) dst[i] = __float2bfloat16_rn(src[i]);
     }
   }
   __threadfence_system();
@@ -679,12 +685,12 @@ __global__ void ep_pair_home_kernel(const int32_t* pair_entry, const int32_t* n_
       pair_dst[p] = reinterpret_cast<uint64_t>(sink);
       continue;
     }
-    pair_dst[p] = peer_yback[r] + static_cast<uint64_t>(e * H) * sizeof(float);
+    pair_dst[p] = peer_yback[r] + static_cast<uint64_t>(e * H) * sizeof(__nv_bfloat16);
   }
 }
 
-// Pair p's fp32 output row y[p] to its home row pair_dst[p] (another GPU's
-// memory or this one's).  One warp per pair.
+// Pair p's fp32 output row y[p], rounded to bf16, to its home row
+// pair_dst[p] (another GPU's memory or this one's).  One warp per pair.
 __global__ void ep_pairs_home_kernel(const float* y, const int32_t* n_pairs, const uint64_t* pair_dst, int64_t H,
                                      int64_t cap, int vec) {
   const int lane = threadIdx.x % 32;
@@ -692,12 +698,12 @@ __global__ void ep_pairs_home_kernel(const float* y, const int32_t* n_pairs, con
   for (int64_t p = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) / 32; p < n;
        p += static_cast<int64_t>(gridDim.x) * blockDim.x / 32) {
     const float* src = y + p * H;
-    float* dst = reinterpret_cast<float*>(pair_dst[p]);
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(pair_dst[p]);
     if (vec) {
       for (int64_t i = lane; i < H / 4; i += 32)
-        reinterpret_cast<float4*>(dst)[i] = __ldcs(reinterpret_cast<const float4*>(src) + i);
+        reinterpret_cast<uint2*>(dst)[i] = bf16x4(__ldcs(reinterpret_cast<const float4*>(src) + i));
     } else {
-      for (int64_t i = lane; i < H; i += 32) dst[i] = src[i];
+      for (int64_t i = lane; i < H; i += 32) dst[i] = __float2bfloat16_rn(src[i]);
     }
   }
   __threadfence_system();
@@ -1194,6 +1200,7 @@ static int run_expert_stages_prefill(const Tables& t, const void* x, bool x_bf16
   g2.w0 = t.dw; g2.s0 = t.ds; g2.w1 = nullptr; g2.s1 = nullptr;
   g2.a16 = l.act16; g2.ascale = l.ascale;
   g2.out = m.y; g2.out_row = out_row; g2.N = static_cast<int>(H); g2.K = static_cast<int>(I);
+  g2.out_row_bf16 = out_row ? 1 : 0;  // rows stored home through the table are the return buffer's bf16 rows
   if (y16 && !out_row) {
     g2.out16 = reinterpret_cast<__nv_bfloat16*>(m.y);
     g2.out = nullptr;
@@ -1874,12 +1881,12 @@ int moe_ep_experts_return_p2p(const uint16_t* rows_bf16, const int32_t* row_expe
                     weight_layout, nullptr, &home, workspace, workspace_bytes, stream);
 }
 
-int moe_ep_combine(const float* y, const int32_t* entry_pos, const float* pos_weight, int64_t tokens, int64_t top_k,
-                   int64_t hidden_dim, int has_shared, uint16_t* out_bf16, void* stream) {
-  if (!y || !entry_pos || !pos_weight || !out_bf16) return fail(kNullPointer, "null pointer");
+int moe_ep_combine(const uint16_t* y_bf16, const int32_t* entry_pos, const float* pos_weight, int64_t tokens,
+                   int64_t top_k, int64_t hidden_dim, int has_shared, uint16_t* out_bf16, void* stream) {
+  if (!y_bf16 || !entry_pos || !pos_weight || !out_bf16) return fail(kNullPointer, "null pointer");
   if (tokens <= 0 || top_k <= 0 || hidden_dim <= 0) return fail(kBadDims, "bad dimensions");
   CombineArgs c{};
-  c.y = y; c.row_ptr = nullptr; c.stride = static_cast<int>(top_k); c.row_pairs = entry_pos;
+  c.y = nullptr; c.y16 = reinterpret_cast<const __nv_bfloat16*>(y_bf16); c.row_ptr = nullptr; c.stride = static_cast<int>(top_k); c.row_pairs = entry_pos;
   c.pair_weight = pos_weight; c.extra_base = has_shared ? static_cast<int>(tokens * top_k) : -1;
   c.T = static_cast<int>(tokens); c.H = static_cast<int>(hidden_dim);
   c.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);

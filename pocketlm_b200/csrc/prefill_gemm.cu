@@ -608,8 +608,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
         // absent expert: its pairs' output rows are zero
         if (row_in_tile < tr.rows) {
           const int64_t pz = tr.row0 + row_in_tile;
-          if (!GATEUP && a.out16) {
-            uint4* out = reinterpret_cast<uint4*>(a.out16 + pz * N + tr.nt * kBN);
+          if (!GATEUP && (a.out16 || (a.out_row && a.out_row_bf16))) {
+            __nv_bfloat16* row16 =
+                a.out16 ? a.out16 + pz * N : reinterpret_cast<__nv_bfloat16*>(a.out_row[pz]);
+            uint4* out = reinterpret_cast<uint4*>(row16 + tr.nt * kBN);
             for (int j = 0; j < kBN / 8; ++j) out[j] = make_uint4(0u, 0u, 0u, 0u);
           } else {
             float* row = !GATEUP && a.out_row ? reinterpret_cast<float*>(a.out_row[pz]) : a.out + pz * N;
@@ -641,12 +643,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_gemm_kernel(const __grid_
       const int row_base = half * kSubM + quad * kWarp;  // the warp's first row in the tile
       // the output rows this lane stores in emit64: rows lane / 4 + 8 i of the warp's 32 (byte addresses of
       // the tile's first column: fp32 rows, or bf16 rows with out16)
-      const bool y16 = !GATEUP && a.out16 != nullptr;
+      const bool y16 = !GATEUP && (a.out16 != nullptr || (a.out_row && a.out_row_bf16));
       unsigned char* out_row[4] = {nullptr, nullptr, nullptr, nullptr};
       if (!GATEUP) {
         unsigned char* mine = nullptr;
         if (valid)
-          mine = y16 ? reinterpret_cast<unsigned char*>(a.out16 + p * N + tr.nt * kBN)
+          mine = y16 ? reinterpret_cast<unsigned char*>(
+                           (a.out16 ? a.out16 + p * N : reinterpret_cast<__nv_bfloat16*>(a.out_row[p])) + tr.nt * kBN)
                      : reinterpret_cast<unsigned char*>(
                            (a.out_row ? reinterpret_cast<float*>(a.out_row[p]) : a.out + p * N) + tr.nt * kBN);
         const uint64_t m64 = reinterpret_cast<uint64_t>(mine);

@@ -27,6 +27,7 @@ struct PrefillArgs {
   // down GEMM only, or null: the outputs as bf16 rows [rows_a, N] instead of fp32 (each expert's
   // output rounded once, as the reference rounds it before its weighted add)
   __nv_bfloat16* out16;
+  int out_row_bf16;        // with out_row: the table's rows are bf16 (N values), not fp32
   int N;                   // output columns (gate/up: intermediate size)
   int K;
   int scale_cols;          // ceil(K / 128)

@@ -123,8 +123,11 @@ class CudaEPOps:
         native._check(code, "moe_ep_experts_return_p2p")
 
     def combine(self, y: torch.Tensor, p: Packed, T: int) -> torch.Tensor:
+        """y: the expert output rows in bf16 (rounded once, as the reference rounds them)."""
         L = self.layer
         k = L.cfg.top_k
+        if y.dtype != torch.bfloat16:
+            y = y.to(torch.bfloat16)
         out = torch.empty((T, L.cfg.hidden), dtype=torch.bfloat16, device=y.device)
         code = self.lib.moe_ep_combine(native._ptr(y), native._ptr(p.entry_pos), native._ptr(p.pos_weight), T, k,
                                        L.cfg.hidden, 1, native._ptr(out), native._stream())
@@ -163,7 +166,8 @@ class PeerExchange:
         self.rows = symm.empty((self.capacity + self.max_tokens, H), dtype=torch.bfloat16, device=dev)
         self.expert = symm.empty((self.capacity + self.max_tokens,), dtype=torch.int32, device=dev)
         self.src = symm.empty((self.capacity + self.max_tokens,), dtype=torch.int32, device=dev)
-        self.yback = symm.empty((self.stride + self.max_tokens, H), dtype=torch.float32, device=dev)
+        # return rows in bf16: each expert output is rounded there, as the reference rounds it
+        self.yback = symm.empty((self.stride + self.max_tokens, H), dtype=torch.bfloat16, device=dev)
         # the [world][world] counts (row = source rank) and the barrier's signal slots, peer-written too
         self.matrix = symm.empty((L.world * L.world,), dtype=torch.int32, device=dev)
         self.sig = symm.empty((L.world,), dtype=torch.int32, device=dev)
@@ -436,9 +440,11 @@ class ExpertParallelLayer:
         row_expert[R:].fill_(self.n_local)  # the shared expert, last in the local tables
         y = ops.experts(rows, row_expert) if R + T > 0 else torch.empty((0, H), dtype=torch.float32,
                                                                         device=x.device)
-        y_back = torch.empty((T * k + T, H), dtype=torch.float32, device=x.device)
-        dist.all_to_all_single(y_back[:T * k], y[:R], sc, rc, group=self.group)
-        y_back[T * k:].copy_(y[R:])
+        # the outputs rounded to bf16 (round to nearest even, as the peer exchange's kernels round them)
+        y16 = y.to(torch.bfloat16)
+        y_back = torch.empty((T * k + T, H), dtype=torch.bfloat16, device=x.device)
+        dist.all_to_all_single(y_back[:T * k], y16[:R], sc, rc, group=self.group)
+        y_back[T * k:].copy_(y16[R:])
         if T == 0:
             return torch.empty((0, H), dtype=torch.bfloat16, device=x.device), ids, w
         return ops.combine(y_back, p, T), ids, w

@@ -99,8 +99,9 @@ def test_ep_two_gpus_matches_single_gpu_layer_and_oracle():
             bad, excused = id_mismatches(r["ids"], route)
             assert bad == excused
             same = (torch.sort(r["ids"], 1).values == torch.sort(r["ref_ids"], 1).values).all(dim=1)
-            # same routing -> same per-pair arithmetic and combine order as the fused layer
-            assert rel_l2(r["out"][same], r["ref"][same]) <= 1e-3
+            # same routing -> same per-pair arithmetic and combine order as the fused layer, except that the
+            # exchange rounds each expert output to bf16 (as the reference does) where the decode layer keeps fp32
+            assert rel_l2(r["out"][same], r["ref"][same]) <= 4e-3
             assert rel_l2(r["out"], expected) <= REL_L2_GATE and cos_dist(r["out"], expected) <= COS_GATE
             # the peer-memory exchange: the same rows reach the same experts in the same order
             assert torch.equal(r["ids_p2p"], r["ids"])
@@ -113,9 +114,8 @@ def test_ep_two_gpus_matches_single_gpu_layer_and_oracle():
             # prefill: the received rows run on the grouped GEMM, as the fused layer's pairs do
             same = (torch.sort(r["ids_pre"], 1).values == torch.sort(r["ref_pre_ids"], 1).values).all(dim=1)
             assert same.float().mean() > 0.99
-            # the single-GPU layer's prefill rounds each expert output to bf16 before its combine; the
-            # exchange returns fp32 rows
-            assert rel_l2(r["out_pre"][same], r["ref_pre"][same]) <= 4e-3
+            # both round each expert output to bf16 before the combine (the reference's rounding point)
+            assert rel_l2(r["out_pre"][same], r["ref_pre"][same]) <= 1e-3
             assert torch.equal(r["out_pre_p2p"], r["out_pre"])
             expected, route = oracle.ds_moe_layer(r["xp"], layer)
             bad, excused = id_mismatches(r["ids_pre"], route)

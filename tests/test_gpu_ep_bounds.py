@@ -37,7 +37,7 @@ def _table(*tensors) -> torch.Tensor:
 def test_return_p2p_skips_out_of_range_src(cuda_device):
     assert _device_error() == 0
     H, src_stride, home_rows = 64, 8, 6
-    big = torch.full((32, H), SENTINEL, dtype=torch.float32, device=cuda_device)
+    big = torch.full((32, H), SENTINEL, dtype=torch.bfloat16, device=cuda_device)  # bf16 return rows
     base = big[16:]  # 16 owned rows on either side of the declared return buffer
     peers = _table(base, base)  # declared world 1; entry 1 exists only so a missed rank check stays local
     y = torch.randn((6, H), device=cuda_device)
@@ -48,7 +48,7 @@ def test_return_p2p_skips_out_of_range_src(cuda_device):
                                     home_rows, native._ptr(peers), native._stream())
     native._check(code, "moe_ep_return_p2p")
     assert _device_error() == EP_RANGE_ERROR
-    assert torch.equal(base[0], y[0]) and torch.equal(base[5], y[1])
+    assert torch.equal(base[0], y[0].to(torch.bfloat16)) and torch.equal(base[5], y[1].to(torch.bfloat16))
     untouched = torch.ones(32, dtype=torch.bool)
     untouched[16 + 0] = untouched[16 + 5] = False
     assert (big[untouched] == SENTINEL).all()
@@ -110,7 +110,7 @@ def test_experts_return_p2p_keeps_bad_homes_local(cuda_device, n_rows):
     src_stride = n_rows + 8
     home_rows = n_rows  # declared; the real buffer has 16 more rows on each side
     margin = 16
-    big = torch.full((src_stride + 2 * margin, H), SENTINEL, dtype=torch.float32, device=cuda_device)
+    big = torch.full((src_stride + 2 * margin, H), SENTINEL, dtype=torch.bfloat16, device=cuda_device)
     base = big[margin:]
     peers = _table(base, base)
     src = torch.randperm(n_rows, generator=gen).to(torch.int32)
@@ -129,7 +129,7 @@ def test_experts_return_p2p_keeps_bad_homes_local(cuda_device, n_rows):
     good = [j for j in range(n_rows) if j not in bad]
     src_cpu = src.cpu()
     homes = torch.tensor([int(src_cpu[j]) for j in good])
-    assert torch.equal(base[homes.to(cuda_device)], want[good])
+    assert torch.equal(base[homes.to(cuda_device)], want[good].to(torch.bfloat16))  # rounded once, to nearest
     untouched = torch.ones(big.shape[0], dtype=torch.bool)
     untouched[homes + margin] = False
     assert (big[untouched.to(cuda_device)] == SENTINEL).all()
