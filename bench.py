@@ -904,8 +904,9 @@ def run_stack(args, rank: int, world: int) -> dict | None:
             graphed = stack.capture(T) if stack.peer is not None else None
             step = (lambda: graphed(x)) if graphed is not None else (lambda: stack.forward(x))
             # the first replays of a fresh whole-stack graph run slower (measured: the first batch's graph-only
-            # time above its own end-to-end time); ten replays before timing
-            warm = max(args.warmup, 10)
+            # time 10 % above its own end-to-end time after 10 warm-up replays, about 90 ms of them); fifty
+            # replays before timing -- a fixed count, since every rank replays in lockstep
+            warm = max(args.warmup, 50)
             ms = timed_max_over_ranks(step, steps, warm, flush, dev)
             x_host = x.cpu().pin_memory()
             out_host = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
