@@ -364,9 +364,10 @@ int moe_ep_experts_fp8(const uint16_t* rows_bf16, const int32_t* row_expert, int
 int64_t moe_ep_experts_workspace_bytes(int64_t rows, int64_t hidden_dim, int64_t intermediate, int64_t num_local);
 
 /* out_bf16[t] = bf16(sum_slot pos_weight[p] * y[p] (+ y[tokens*top_k + t]
- * when has_shared)), p = entry_pos[t * top_k + slot], slots in order; y is
- * the bf16 output rows, summed in fp32. */
-int moe_ep_combine(const uint16_t* y_bf16, const int32_t* entry_pos, const float* pos_weight, int64_t tokens,
+ * when has_shared)), p = entry_pos[t * top_k + slot], slots in order, summed
+ * in fp32; y holds the output rows as bf16 (y_dtype 1: the exchanges' rounded
+ * rows) or fp32 (0). */
+int moe_ep_combine(const void* y, int y_dtype, const int32_t* entry_pos, const float* pos_weight, int64_t tokens,
                    int64_t top_k, int64_t hidden_dim, int has_shared, uint16_t* out_bf16, void* stream);
 
 /* No reference counterpart (the reference runs on one host; its ranks do not

@@ -1881,12 +1881,15 @@ int moe_ep_experts_return_p2p(const uint16_t* rows_bf16, const int32_t* row_expe
                     weight_layout, nullptr, &home, workspace, workspace_bytes, stream);
 }
 
-int moe_ep_combine(const uint16_t* y_bf16, const int32_t* entry_pos, const float* pos_weight, int64_t tokens,
+int moe_ep_combine(const void* y, int y_dtype, const int32_t* entry_pos, const float* pos_weight, int64_t tokens,
                    int64_t top_k, int64_t hidden_dim, int has_shared, uint16_t* out_bf16, void* stream) {
-  if (!y_bf16 || !entry_pos || !pos_weight || !out_bf16) return fail(kNullPointer, "null pointer");
+  if (!y || !entry_pos || !pos_weight || !out_bf16) return fail(kNullPointer, "null pointer");
   if (tokens <= 0 || top_k <= 0 || hidden_dim <= 0) return fail(kBadDims, "bad dimensions");
+  if (y_dtype != kDtypeBF16 && y_dtype != kDtypeF32) return fail(kUnsupported, "y_dtype must be bf16 or fp32");
   CombineArgs c{};
-  c.y = nullptr; c.y16 = reinterpret_cast<const __nv_bfloat16*>(y_bf16); c.row_ptr = nullptr; c.stride = static_cast<int>(top_k); c.row_pairs = entry_pos;
+  if (y_dtype == kDtypeBF16) c.y16 = static_cast<const __nv_bfloat16*>(y);
+  else c.y = static_cast<const float*>(y);
+  c.row_ptr = nullptr; c.stride = static_cast<int>(top_k); c.row_pairs = entry_pos;
   c.pair_weight = pos_weight; c.extra_base = has_shared ? static_cast<int>(tokens * top_k) : -1;
   c.T = static_cast<int>(tokens); c.H = static_cast<int>(hidden_dim);
   c.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);

@@ -129,7 +129,8 @@ class CudaEPOps:
         if y.dtype != torch.bfloat16:
             y = y.to(torch.bfloat16)
         out = torch.empty((T, L.cfg.hidden), dtype=torch.bfloat16, device=y.device)
-        code = self.lib.moe_ep_combine(native._ptr(y), native._ptr(p.entry_pos), native._ptr(p.pos_weight), T, k,
+        code = self.lib.moe_ep_combine(native._ptr(y), native.DTYPE_BF16, native._ptr(p.entry_pos),
+                                       native._ptr(p.pos_weight), T, k,
                                        L.cfg.hidden, 1, native._ptr(out), native._stream())
         native._check(code, "moe_ep_combine")
         return out
@@ -258,8 +259,9 @@ class PeerExchange:
         if T == 0:
             return out, ids, w
         w_flat = w.reshape(-1).contiguous()  # referenced until the launch (a temporary could be freed first)
-        native._check(lib.moe_ep_combine(native._ptr(self.yback), native._ptr(self.identity), native._ptr(w_flat),
-                                         T, k, H, 1, native._ptr(out), native._stream()), "moe_ep_combine")
+        native._check(lib.moe_ep_combine(native._ptr(self.yback), native.DTYPE_BF16, native._ptr(self.identity),
+                                         native._ptr(w_flat), T, k, H, 1, native._ptr(out), native._stream()),
+                      "moe_ep_combine")
         return out, ids, w
 
 
@@ -291,8 +293,9 @@ class PeerExchange:
         if T == 0:
             return out, ids, w
         w_flat = w.reshape(-1)  # referenced until the launch
-        native._check(lib.moe_ep_combine(native._ptr(self.yback), native._ptr(self.identity), native._ptr(w_flat),
-                                         T, k, H, 1, native._ptr(out), native._stream()), "moe_ep_combine")
+        native._check(lib.moe_ep_combine(native._ptr(self.yback), native.DTYPE_BF16, native._ptr(self.identity),
+                                         native._ptr(w_flat), T, k, H, 1, native._ptr(out), native._stream()),
+                      "moe_ep_combine")
         return out, ids, w
 
 

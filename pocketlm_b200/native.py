@@ -127,7 +127,7 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_ep_dispatch_workspace_bytes": ([_I64, _I64], _I64),
     "moe_ep_experts_fp8": ([_P, _P, _I64, _I64, _I64, _P, _I64, _P, _INT, _P, _P, _I64, _P], _INT),
     "moe_ep_experts_workspace_bytes": ([_I64] * 4, _I64),
-    "moe_ep_combine": ([_P, _P, _P, _I64, _I64, _I64, _INT, _P, _P], _INT),
+    "moe_ep_combine": ([_P, _INT, _P, _P, _I64, _I64, _I64, _INT, _P, _P], _INT),
     "moe_ep_count_ranks": ([_P, _I64, _I64, _I64, _I64, _P, _P], _INT),
     "moe_ep_barrier_p2p": ([_P, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _INT),
     "moe_ep_route_dispatch_p2p_workspace_bytes": ([_I64, _I64], _I64),

@@ -234,8 +234,10 @@ class DsMoELayerGPU:
             native._ptr(rows), native._ptr(row_expert), R, H, cfg.inter, native._ptr(tables), S,
             native._ptr(self.nan_free), layout, native._ptr(y), native._ptr(ws), ws.numel(), native._stream()),
             "moe_ep_experts_fp8")
-        native._check(lib.moe_ep_combine(native._ptr(y), native._ptr(entry_pos), native._ptr(pos_weight), T, k, H, 1,
-                                         native._ptr(out), native._stream()), "moe_ep_combine")
+        # fp32 rows: the fused layer's arithmetic for the same routing
+        native._check(lib.moe_ep_combine(native._ptr(y), native.DTYPE_F32, native._ptr(entry_pos),
+                                         native._ptr(pos_weight), T, k, H, 1, native._ptr(out), native._stream()),
+                      "moe_ep_combine")
         return out
 
     def capture(self, tokens: int, *, input_dtype: torch.dtype = torch.bfloat16) -> "GraphedDsMoELayer":

@@ -100,3 +100,15 @@ def test_fused_send_checks_its_arguments_before_launching():
     assert call(world=64, E=256, cap=64 * 64) == -5
     assert call(x=odd) == -5                 # rows must be 16-byte aligned
     assert lib.moe_ep_route_dispatch_p2p_workspace_bytes(4, 256) >= 4 * 256 * 4
+
+
+def test_combine_checks_row_dtype_and_pointers():
+    """moe_ep_combine takes the output rows as bf16 (y_dtype 1, the exchanges' rows) or fp32 (0); anything
+    else, or a missing pointer, is refused before any launch."""
+    import ctypes
+
+    lib = native.load_library()
+    fake = ctypes.c_void_p(256)
+    assert lib.moe_ep_combine(None, 1, fake, fake, 2, 8, H, 1, fake, None) == -1
+    assert lib.moe_ep_combine(fake, 2, fake, fake, 2, 8, H, 1, fake, None) == -5   # f16 rows: not a layout it reads
+    assert lib.moe_ep_combine(fake, 1, fake, fake, 0, 8, H, 1, fake, None) == -2
