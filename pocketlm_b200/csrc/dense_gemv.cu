@@ -71,15 +71,28 @@ MOE_D void mma_m16n8k16<1>(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint
 
 MOE_D uint32_t word_at(const uint4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
 
-// int4 word -> the four f16 pairs (n0,n4) (n1,n5) (n2,n6) (n3,n7) as exact signed codes
+// int4 word -> the four f16 pairs (n0,n4) (n1,n5) (n2,n6) (n3,n7) as exact
+// signed codes, one shift per word: the low nibbles of each byte pair are
+// masked in place and biased to 1024 + (n ^ 8) (minus 1032: the code), the high
+// nibbles masked in place and biased to 1024 + 16 (n ^ 8), brought down by one
+// multiply-add (x / 16 - 72: the code).  Every step is exact in f16.
 MOE_D void q4_word_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
-  const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t biased = ((w >> (4 * i)) & 0x000F000Fu) ^ 0x64086408u;
-    const __half2 v = __hsub2(*reinterpret_cast<const __half2*>(&biased), bias);
-    h[i] = *reinterpret_cast<const uint32_t*>(&v);
-  }
+  const __half2 bias_lo = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032
+  const __half2 sixteenth = __halves2half2(__float2half(0.0625f), __float2half(0.0625f));
+  const __half2 bias_hi = __halves2half2(__float2half(-72.0f), __float2half(-72.0f));
+  const uint32_t w8 = w >> 8;
+  const uint32_t v0 = (w & 0x000F000Fu) ^ 0x64086408u;   // n0, n4
+  const uint32_t v1 = (w & 0x00F000F0u) ^ 0x64806480u;   // n1, n5 (x 16)
+  const uint32_t v2 = (w8 & 0x000F000Fu) ^ 0x64086408u;  // n2, n6
+  const uint32_t v3 = (w8 & 0x00F000F0u) ^ 0x64806480u;  // n3, n7 (x 16)
+  const __half2 r0 = __hsub2(*reinterpret_cast<const __half2*>(&v0), bias_lo);
+  const __half2 r1 = __hfma2(*reinterpret_cast<const __half2*>(&v1), sixteenth, bias_hi);
+  const __half2 r2 = __hsub2(*reinterpret_cast<const __half2*>(&v2), bias_lo);
+  const __half2 r3 = __hfma2(*reinterpret_cast<const __half2*>(&v3), sixteenth, bias_hi);
+  h[0] = *reinterpret_cast<const uint32_t*>(&r0);
+  h[1] = *reinterpret_cast<const uint32_t*>(&r1);
+  h[2] = *reinterpret_cast<const uint32_t*>(&r2);
+  h[3] = *reinterpret_cast<const uint32_t*>(&r3);
 }
 
 MOE_D uint4 ld_weights(const uint8_t* p) { return __ldcs(reinterpret_cast<const uint4*>(p)); }
