@@ -21,11 +21,13 @@
 //    multiply bf16 activations, split as hi = bf16(x) and lo = bf16(x - hi)
 //    (two MMAs) so fp32 activations keep 16 bits of mantissa.
 //  * int4: a lane's 16 bytes are 32 weights; each 32-bit word holds 8 codes
-//    n0..n7 (n0 in the low nibble).  (w >> s) & 0x000F000F pairs nibbles
-//    (n_s/4, n_s/4+4); xor-ing 0x64086408 makes each half 1024 + (n ^ 8),
-//    i.e. 1032 + code exactly, and subtracting 1032 leaves the signed code
-//    as an exact f16 (the magic-number int4 -> f16 conversion of
-//    Kim et al., "Who Says Elephants Can't Run", 2022).  The resulting
+//    n0..n7 (n0 in the low nibble).  w & 0x000F000F pairs nibbles (n0, n4);
+//    xor-ing 0x64086408 makes each half 1024 + (n ^ 8), i.e. 1032 + code
+//    exactly, and subtracting 1032 leaves the signed code as an exact f16
+//    (the magic-number int4 -> f16 conversion of Kim et al., "Who Says
+//    Elephants Can't Run", 2022).  The high nibbles (n1, n5) are masked in
+//    place (w & 0x00F000F0, 16x the value) and brought down by one
+//    multiply-add; w >> 8 gives (n2, n6) and (n3, n7) the same way.  The resulting
 //    pairs (n0,n4) (n1,n5) | (n2,n6) (n3,n7) feed two MMAs; the activations
 //    are staged with every group of 8 stored as k0 k4 k1 k5 k2 k6 k3 k7
 //    so one 16-byte load gives the matching B pairs.  Codes times f16
