@@ -508,8 +508,8 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                 cpu = {"value": None, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)),
                        "kind": "reference", "sample": f"unavailable: {type(exc).__name__}: {exc}"}
         del host_layer
-        prefill, q4 = {}, {}
-        if args.prefill_tokens != "none" or args.q4_tokens != "none":
+        prefill, q4, mla = {}, {}, {}
+        if args.prefill_tokens != "none" or args.q4_tokens != "none" or args.mla_cache != "none":
             del gpu_layer, layer, graphed
             torch.cuda.empty_cache()
         if args.prefill_tokens != "none":
@@ -517,6 +517,8 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                                   [int(v) for v in args.prefill_tokens.split(",") if v])
         if args.q4_tokens != "none":
             q4 = run_q4(args, dev, flush, peaks, [int(v) for v in args.q4_tokens.split(",") if v])
+        if args.mla_cache != "none" and rank == 0:  # no collectives inside: the other ranks go on
+            mla = run_mla(args, dev, flush, peaks, int(args.mla_cache))
     clock_info = clocks.summary()
     if rank != 0:
         return None
@@ -524,7 +526,7 @@ def run_ours(args, rank: int, world: int) -> dict | None:
     peak = peaks["hbm_gbs"]
     achieved = head["fused_experts_gbs"] if fused else head["gateup_gbs"]
     roofline_bytes = head["gateup_bytes"] + head["down_bytes"] if fused else head["gateup_bytes"]
-    for block in (prefill, q4):
+    for block in (prefill, q4, mla):
         for key, rep in (block.pop("parity", None) or {}).items():
             parity[key] = rep
     parity_summary = {"gate": {"rel_l2": 2e-2, "cos_dist": 1e-3, "ids": "bit-exact, ties within 1e-6 excused"},
@@ -567,6 +569,7 @@ def run_ours(args, rank: int, world: int) -> dict | None:
                   for T, r in sorted(results.items())},
         "prefill": prefill,
         "q4": q4,
+        "mla": mla,
     }
 
 
@@ -707,6 +710,94 @@ def run_q4(args, dev, flush, peaks, token_list) -> dict:
     torch.cuda.empty_cache()
     return {"workload": "c4-mixtral-q4", "kernel": "dense_mma_gemv_kernel<Q4> (dense_gemv.cu) / "
             "prefill_gemm_kernel<*, Q4> (prefill_gemm.cu)", "sweep": out, "cpu_baseline": cpu, "parity": parity}
+
+
+def run_mla(args, dev, flush, peaks, cache_len: int) -> dict:
+    """The DeepSeek-V3 MLA attention block for one decode token (ds_forward.cpp:647-782:
+    hidden 7168, q_lora_rank 1536, kv_lora_rank 512, 128 heads, nope 128, rope 64, v 128),
+    fp32 like the reference, over a cache of cache_len positions, through
+    native.ds_attention_block_forward with weights and caches resident (the previous
+    cache copied into the new one each call, as the reference's API returns it).  Bytes:
+    the five fp32 projections, the cache read by the attention and the cache copy."""
+    from pocketlm_b200 import native
+
+    H, qr, R, heads, nope, rope, v = 7168, 1536, 512, 128, 128, 64, 128
+    prev = cache_len - 1
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+
+    def rnd(*shape, scale=1.0):
+        return torch.randn(shape, generator=g, device=dev) * scale
+
+    w = dict(q_a=rnd(qr, H, scale=H ** -0.5), q_b=rnd(heads * (nope + rope), qr, scale=qr ** -0.5),
+             kv_a=rnd(R + rope, H, scale=H ** -0.5), kv_b=rnd(heads * (nope + v), R, scale=R ** -0.5),
+             o_w=rnd(H, heads * v, scale=(heads * v) ** -0.5), q_norm=1 + 0.1 * rnd(qr), kv_norm=1 + 0.1 * rnd(R))
+    prev_kv, prev_pe = rnd(prev, R), rnd(prev, rope)
+    angles = torch.arange(rope // 2, device=dev, dtype=torch.float32) * cache_len * 1e-3
+    cos, sin = angles.cos(), angles.sin()
+    hidden = rnd(H)
+    dims = dict(q_lora_rank=qr, kv_lora_rank=R, num_heads=heads, qk_nope_dim=nope, qk_rope_dim=rope, v_head_dim=v,
+                rms_eps=1e-6, softmax_scale=(nope + rope) ** -0.5)
+    order = ("q_a", "q_b", "kv_a", "kv_b", "o_w", "q_norm", "kv_norm")
+    session = native.DeepSeekNativeSession(num_layers=1, hidden_dim=H, num_experts=0, top_k=0)
+
+    def call(x):
+        return native.ds_attention_block_forward(session, x, *(w[k] for k in order), previous_kv_cache=prev_kv,
+                                                 previous_pe_cache=prev_pe, rope_cos=cos, rope_sin=sin, **dims)
+
+    out, _ = call(hidden)
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 20))
+    ms = statistics.mean(time_steps(lambda: call(hidden), steps, args.warmup, flush))
+    host_x = hidden.cpu().pin_memory()
+    e2e_ms = statistics.mean(time_steps(lambda: call(host_x)[0].cpu(), steps, args.warmup, flush))
+    weight_elems = sum(w[k].numel() for k in order)
+    cache_row = R + rope
+    nbytes = 4 * (weight_elems + cache_len * cache_row + 2 * prev * cache_row)
+    res = {"workload": f"dsv3-mla-attention-block-cache{cache_len}",
+           "kernels": "mla_gemv_kernel x3, mla_norm_rope_kernel, mla_qabs_kernel, mla_attention_kernel, "
+                      "mla_merge_kernel (mla.cu)",
+           "ms_per_token": ms, "tokens_per_s": 1e3 / ms, "algorithmic_bytes": nbytes,
+           "hbm_frac": nbytes / (ms / 1e3) / (peaks["hbm_gbs"] * 1e9), "peak_source": f"{peaks['source']} hbm_gbs",
+           "e2e_ms_per_token": e2e_ms, "gpu_launches_per_token": 7,
+           "invocations_counted": session.fused_attention_invocation_count()}
+    parity = {}
+    host = {k: t.cpu() for k, t in w.items()}
+    if not args.no_parity:
+        import oracle.mla as omla
+
+        want, (wkv, wpe) = omla.attention_block(hidden.cpu(), *(host[k] for k in order), prev_kv.cpu(), prev_pe.cpu(),
+                                                cos.cpu(), sin.cpu(), **dims)
+        got, (kv, pe) = call(hidden)
+        rel = float((got.cpu() - want).norm() / want.norm())
+        rel_kv = float((kv[-1].cpu() - wkv[-1]).norm() / wkv[-1].norm())
+        parity[f"mla-block-cache{cache_len}"] = {"rel_l2": rel, "new_cache_row_rel_l2": rel_kv, "gate": 1e-5,
+                                                 "pass": rel <= 1e-5 and rel_kv <= 1e-5}
+    cpu = None
+    if not args.no_cpu_baseline:
+        try:
+            import oracle.ref as oref
+
+            if not oref.available():
+                raise FileNotFoundError("oracle/_ref not built")
+            hx, pk, pp = hidden.cpu(), prev_kv.cpu(), prev_pe.cpu()
+            args_ref = (hx, *(host[k] for k in order), pk, pp, cos.cpu(), sin.cpu())
+            oref.attention_block(*args_ref, **dims)  # warm
+            t0 = time.perf_counter()
+            reps = 3
+            for _ in range(reps):
+                oref.attention_block(*args_ref, **dims)
+            per = (time.perf_counter() - t0) / reps
+            cpu = {"value": 1.0 / per, "unit": "tokens/s", "cores": int(os.environ.get("OMP_NUM_THREADS", "1")),
+                   "kind": "reference", "sample": f"{reps} calls of the reference's ds_attention_block_forward_f32 "
+                   f"(oracle/_ref, OpenMP) on the same weights and cache; {per * 1e3:.1f} ms per call"}
+        except Exception as exc:  # the baseline is reported, not required
+            cpu = {"unavailable": f"{type(exc).__name__}: {exc}"}
+    res["cpu_baseline"] = cpu
+    res["parity"] = parity
+    session.close()
+    del w, host, prev_kv, prev_pe
+    torch.cuda.empty_cache()
+    return res
 
 
 def timed_max_over_ranks(fn, steps: int, warmup: int, flush: torch.Tensor, dev: torch.device) -> float:
@@ -1130,6 +1221,32 @@ def run_profile_q4(args) -> dict:
     return {"profile_case": f"c4-mixtral-q4-T{args.tokens}", "launches": args.warmup + args.steps}
 
 
+def run_profile_mla(args) -> dict:
+    """An MLA case for ncu: the DS-V3 attention block over a cache of
+    --mla-cache positions (777 MB of fp32 weights and cache), eager calls."""
+    from pocketlm_b200 import native
+
+    dev = torch.device("cuda", 0)
+    native.load_library()
+    H, qr, R, heads, nope, rope, v = 7168, 1536, 512, 128, 128, 64, 128
+    L = int(args.mla_cache)
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    w = [torch.randn(s, generator=g, device=dev) * 0.01 for s in
+         ((qr, H), (heads * (nope + rope), qr), (R + rope, H), (heads * (nope + v), R), (H, heads * v))]
+    norms = [torch.ones(qr, device=dev), torch.ones(R, device=dev)]
+    prev_kv, prev_pe = torch.randn((L - 1, R), device=dev), torch.randn((L - 1, rope), device=dev)
+    cos, sin = torch.ones(rope // 2, device=dev), torch.zeros(rope // 2, device=dev)
+    x = torch.randn(H, device=dev)
+    with native.DeepSeekNativeSession(num_layers=1, hidden_dim=H, num_experts=0, top_k=0) as session:
+        for _ in range(args.warmup + args.steps):
+            native.ds_attention_block_forward(session, x, *w, *norms, previous_kv_cache=prev_kv,
+                                              previous_pe_cache=prev_pe, rope_cos=cos, rope_sin=sin, q_lora_rank=qr,
+                                              kv_lora_rank=R, num_heads=heads, qk_nope_dim=nope, qk_rope_dim=rope,
+                                              v_head_dim=v, rms_eps=1e-6, softmax_scale=(nope + rope) ** -0.5)
+    torch.cuda.synchronize()
+    return {"profile_case": f"dsv3-mla-block-cache{L}", "launches": args.warmup + args.steps}
+
+
 def run_reference(args, rank: int, world: int) -> dict | None:
     if rank != 0:
         return None
@@ -1186,6 +1303,8 @@ def main() -> None:
                         help="expert GEMV kernel (moe_b200_select_gemv); auto is the product default")
     parser.add_argument("--prefill-tokens", default="2048,8192,16384",
                         help="config-3 prefill batch sizes measured after the decode sweep, or 'none'")
+    parser.add_argument("--mla-cache", default="4096",
+                        help="cache positions of the MLA attention block leg ('none' to skip)")
     parser.add_argument("--q4-tokens", default="1,32,512,4096",
                         help="config-4 (Mixtral Q4) batch sizes measured after the prefill sweep, or 'none'")
     parser.add_argument("--ep-prefill-tokens", default="8192",
@@ -1205,6 +1324,8 @@ def main() -> None:
                         help="run the small prefill ncu case (DS-V3 expert shapes, 32 experts) instead")
     parser.add_argument("--profile-prefill-experts", type=int, default=32,
                         help="routed experts of the --profile-prefill layer (32 small case, 256 full config 3)")
+    parser.add_argument("--profile-mla", action="store_true",
+                        help="eager MLA attention blocks (DS-V3 shape, --mla-cache positions) for ncu; no JSON bench line")
     parser.add_argument("--profile-q4", action="store_true",
                         help="run the config-4 Q4 layer for --tokens tokens (an ncu case)")
     parser.add_argument("--profile-experts", type=int, default=0,
@@ -1236,6 +1357,8 @@ def main() -> None:
             result = run_profile_prefill(args)
         elif args.profile_q4:
             result = run_profile_q4(args)
+        elif args.profile_mla:
+            result = run_profile_mla(args)
         elif args.profile:
             result = run_profile_case(args)
         else:

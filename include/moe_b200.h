@@ -506,6 +506,62 @@ int moe_ds_moe_layer_forward_fp8_f32(void* handle, const uint64_t* gate_weight_p
                                      void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * MLA attention for one decode token (mla.cu), fp32 like the reference.
+ * All pointers are device pointers; workspace may be null (a stream-ordered
+ * allocation) or at least the *_workspace_bytes size.
+ * ------------------------------------------------------------------------- */
+
+/* replaces ds_attention_invocation_count / ds_fused_attention_invocation_count,
+ * ds_forward.cpp:289-304 (-1 for a null handle) */
+int64_t moe_ds_attention_invocation_count(void* handle);
+int64_t moe_ds_fused_attention_invocation_count(void* handle);
+
+/* Workspace of moe_mla_attention_flash_forward; -1 for dimensions it rejects. */
+int64_t moe_mla_attention_workspace_bytes(int64_t num_heads, int64_t cache_len, int64_t qk_nope_dim,
+                                          int64_t qk_rope_dim, int64_t kv_lora_rank, int64_t v_head_dim);
+
+/* replaces ds_mla_attention_flash_forward, ds_forward.cpp:517-597 (same
+ * arguments, then workspace and stream): q_nope [heads, nope], q_pe
+ * [heads, rope] (already rotated), kv_cache [cache_len, kv_lora_rank],
+ * pe_cache [cache_len, rope], wkv_b [heads, nope + v, kv_lora_rank] ->
+ * output_heads [heads, v].  Returns 0; 1 for a null pointer and 2 for bad
+ * dimensions as the reference does; MOE_B200 status codes (negative) for
+ * kv_lora_rank > 1024, qk_rope_dim > 256, qk_nope_dim > 8192, a small
+ * workspace or a CUDA error. */
+int moe_mla_attention_flash_forward(const float* q_nope, const float* q_pe, const float* kv_cache,
+                                    const float* pe_cache, const float* wkv_b, float* output_heads, int64_t num_heads,
+                                    int64_t cache_len, int64_t qk_nope_dim, int64_t qk_rope_dim, int64_t kv_lora_rank,
+                                    int64_t v_head_dim, float softmax_scale, void* workspace, int64_t workspace_bytes,
+                                    void* stream);
+
+/* Workspace of moe_ds_attention_block_forward_f32; -1 for dimensions it rejects. */
+int64_t moe_ds_attention_block_workspace_bytes(int64_t hidden_dim, int64_t q_lora_rank, int64_t kv_lora_rank,
+                                               int64_t num_heads, int64_t qk_nope_dim, int64_t qk_rope_dim,
+                                               int64_t v_head_dim, int64_t previous_len);
+
+/* replaces ds_attention_block_forward_f32, ds_forward.cpp:647-782 (same
+ * arguments, then workspace and stream): q_low = RMSNorm(q_a . hidden), q =
+ * q_b . q_low per head with RoPE on its rope part, the new cache row (kv_a .
+ * hidden: RMSNorm on the latent part, RoPE on the pe part) appended after the
+ * previous_len rows copied from previous_*_cache, the attention core over
+ * previous_len + 1 positions, hidden_out = o_weight . heads.  next_*_cache
+ * may equal previous_*_cache (append in place: no copy; the buffers then
+ * hold previous_len + 1 rows).  Returns 0; 1 (null pointer), 2 (bad
+ * dimensions), 3 (previous_len > 0 without previous caches) as the reference
+ * does; MOE_B200 status codes (negative) otherwise.  Counts one monolithic
+ * call and one (fused) attention invocation on the session. */
+int moe_ds_attention_block_forward_f32(void* handle, const float* hidden_in, const float* q_a_weight,
+                                       const float* q_b_weight, const float* kv_a_weight, const float* kv_b_weight,
+                                       const float* o_weight, const float* q_norm_weight, const float* kv_norm_weight,
+                                       const float* previous_kv_cache, const float* previous_pe_cache,
+                                       const float* rope_cos, const float* rope_sin, float* next_kv_cache,
+                                       float* next_pe_cache, float* hidden_out, int64_t hidden_dim,
+                                       int64_t q_lora_rank, int64_t kv_lora_rank, int64_t num_heads,
+                                       int64_t qk_nope_dim, int64_t qk_rope_dim, int64_t v_head_dim,
+                                       int64_t previous_len, float rms_eps, float softmax_scale, void* workspace,
+                                       int64_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Profiling (no reference counterpart): when enabled, moe_ds_moe_layer_fp8
  * records CUDA events on its stream at the boundaries of its stages:
  * start | route, dispatch, chunk list (+ f16 staging of x on the MMA path) |

@@ -234,3 +234,55 @@ def router_softmax_topk_u16(hidden, router_weights, k: int):
     _check(f(_ptr(x), _ptr(w), _I64(w.shape[1]), _I64(w.shape[0]), _I64(k),
              _I64(1 if x.dtype == torch.bfloat16 else 0), _ptr(ids), _ptr(weights)), "ref router")
     return ids, weights
+
+
+def mla_attention_flash(q_nope, q_pe, kv_cache, pe_cache, wkv_b, softmax_scale: float):
+    """ds_mla_attention_flash_forward (ds_forward.cpp:517) on the host cores."""
+    qn, qp = q_nope.detach().cpu().contiguous().float(), q_pe.detach().cpu().contiguous().float()
+    kv, pe = kv_cache.detach().cpu().contiguous().float(), pe_cache.detach().cpu().contiguous().float()
+    w = wkv_b.detach().cpu().contiguous().float()
+    heads, nope, rope = qn.shape[0], qn.shape[1], qp.shape[1]
+    v_dim = w.shape[1] - nope
+    out = torch.empty((heads, v_dim), dtype=torch.float32)
+    f = lib("ds_forward").ds_mla_attention_flash_forward
+    f.restype = _INT
+    _check(f(_ptr(qn), _ptr(qp), _ptr(kv), _ptr(pe), _ptr(w), _ptr(out), _I64(heads), _I64(kv.shape[0]),
+             _I64(nope), _I64(rope), _I64(kv.shape[1]), _I64(v_dim), ctypes.c_float(softmax_scale)),
+           "ref mla attention")
+    return out
+
+
+def attention_block(hidden, q_a, q_b, kv_a, kv_b, o_w, q_norm, kv_norm, previous_kv, previous_pe, cos, sin, *,
+                    q_lora_rank: int, kv_lora_rank: int, num_heads: int, qk_nope_dim: int, qk_rope_dim: int,
+                    v_head_dim: int, rms_eps: float, softmax_scale: float):
+    """ds_attention_block_forward_f32 (ds_forward.cpp:647) on the host cores,
+    through a session of its own -> (hidden_out, (next_kv, next_pe))."""
+    def f32(t):
+        return t.detach().cpu().contiguous().reshape(-1).float()
+
+    x = f32(hidden)
+    H = x.numel()
+    prev_len = 0 if previous_kv is None else previous_kv.numel() // kv_lora_rank
+    next_kv = torch.empty((prev_len + 1, kv_lora_rank), dtype=torch.float32)
+    next_pe = torch.empty((prev_len + 1, qk_rope_dim), dtype=torch.float32)
+    out = torch.empty((H,), dtype=torch.float32)
+    args = [f32(t) for t in (q_a, q_b, kv_a, kv_b, o_w, q_norm, kv_norm)]
+    pk = f32(previous_kv) if prev_len else None
+    pp = f32(previous_pe) if prev_len else None
+    c, s = f32(cos), f32(sin)
+    L = lib("ds_forward")
+    L.ds_session_create.restype = _P
+    L.ds_session_create.argtypes = [_I64, _I64, _I64, _I64, _P, _P]
+    L.ds_session_destroy.argtypes = [_P]
+    handle = L.ds_session_create(1, H, 0, 0, None, None)
+    try:
+        f = L.ds_attention_block_forward_f32
+        f.restype = _INT
+        _check(f(_P(handle), _ptr(x), *(_ptr(a) for a in args), _ptr(pk) if pk is not None else _P(0),
+                 _ptr(pp) if pp is not None else _P(0), _ptr(c), _ptr(s),
+                 _ptr(next_kv), _ptr(next_pe), _ptr(out), _I64(H), _I64(q_lora_rank), _I64(kv_lora_rank),
+                 _I64(num_heads), _I64(qk_nope_dim), _I64(qk_rope_dim), _I64(v_head_dim), _I64(prev_len),
+                 ctypes.c_float(rms_eps), ctypes.c_float(softmax_scale)), "ref attention block")
+    finally:
+        L.ds_session_destroy(_P(handle))
+    return out, (next_kv, next_pe)

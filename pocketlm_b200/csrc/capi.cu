@@ -14,6 +14,7 @@
 #include "dequant.cuh"
 #include "dispatch.cuh"
 #include "fp8_gemv.cuh"
+#include "mla.cuh"
 #include "plan.cuh"
 #include "prefill_gemm.cuh"
 #include "route_host.cuh"
@@ -2012,6 +2013,8 @@ struct DsSession {
   int64_t monolithic_calls = 0;
   int64_t expert_invocations = 0;
   int64_t layers_executed = 0;
+  int64_t attention_invocations = 0;
+  int64_t fused_attention_invocations = 0;
 };
 
 void* moe_ds_session_create(int64_t num_layers, int64_t hidden_dim, int64_t num_experts, int64_t top_k) {
@@ -2030,6 +2033,94 @@ void moe_ds_session_destroy(void* handle) { delete static_cast<DsSession*>(handl
 int64_t moe_ds_monolithic_call_counter(void* h) { return h ? static_cast<DsSession*>(h)->monolithic_calls : -1; }
 int64_t moe_ds_expert_invocation_count(void* h) { return h ? static_cast<DsSession*>(h)->expert_invocations : -1; }
 int64_t moe_ds_layers_executed_count(void* h) { return h ? static_cast<DsSession*>(h)->layers_executed : -1; }
+int64_t moe_ds_attention_invocation_count(void* h) {
+  return h ? static_cast<DsSession*>(h)->attention_invocations : -1;
+}
+int64_t moe_ds_fused_attention_invocation_count(void* h) {
+  return h ? static_cast<DsSession*>(h)->fused_attention_invocations : -1;
+}
+
+// ---------------------------------------------------------------------------
+// MLA attention (mla.cu)
+// ---------------------------------------------------------------------------
+
+int64_t moe_mla_attention_workspace_bytes(int64_t num_heads, int64_t cache_len, int64_t qk_nope_dim,
+                                          int64_t qk_rope_dim, int64_t kv_lora_rank, int64_t v_head_dim) {
+  const MlaDims d{num_heads, cache_len, qk_nope_dim, qk_rope_dim, kv_lora_rank, v_head_dim};
+  if (num_heads <= 0 || cache_len <= 0 || qk_nope_dim < 0 || qk_rope_dim < 0 || kv_lora_rank <= 0 ||
+      v_head_dim <= 0 || mla_supported(d) != kOk)
+    return -1;
+  return mla_core_workspace_bytes(d);
+}
+
+int moe_mla_attention_flash_forward(const float* q_nope, const float* q_pe, const float* kv_cache,
+                                    const float* pe_cache, const float* wkv_b, float* output_heads, int64_t num_heads,
+                                    int64_t cache_len, int64_t qk_nope_dim, int64_t qk_rope_dim, int64_t kv_lora_rank,
+                                    int64_t v_head_dim, float softmax_scale, void* workspace, int64_t workspace_bytes,
+                                    void* stream) {
+  if (!q_nope || !q_pe || !kv_cache || !pe_cache || !wkv_b || !output_heads) return 1;  // ds_forward.cpp:531-536
+  if (num_heads <= 0 || cache_len <= 0 || qk_nope_dim < 0 || qk_rope_dim < 0 || kv_lora_rank <= 0 ||
+      v_head_dim <= 0)
+    return 2;  // :537-543
+  const MlaDims d{num_heads, cache_len, qk_nope_dim, qk_rope_dim, kv_lora_rank, v_head_dim};
+  int code = mla_supported(d);
+  if (code != kOk) return code;
+  cudaStream_t s = as_stream(stream);
+  Scratch scratch(workspace, workspace_bytes, static_cast<size_t>(mla_core_workspace_bytes(d)), s);
+  if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
+  return mla_core_run(d, q_nope, qk_nope_dim, q_pe, qk_rope_dim, nullptr, nullptr, kv_cache, pe_cache, wkv_b,
+                      output_heads, softmax_scale, scratch.base(), s);
+}
+
+int64_t moe_ds_attention_block_workspace_bytes(int64_t hidden_dim, int64_t q_lora_rank, int64_t kv_lora_rank,
+                                               int64_t num_heads, int64_t qk_nope_dim, int64_t qk_rope_dim,
+                                               int64_t v_head_dim, int64_t previous_len) {
+  const MlaDims d{num_heads, previous_len + 1, qk_nope_dim, qk_rope_dim, kv_lora_rank, v_head_dim};
+  if (hidden_dim <= 0 || q_lora_rank <= 0 || kv_lora_rank <= 0 || num_heads <= 0 || qk_nope_dim < 0 ||
+      qk_rope_dim < 0 || v_head_dim <= 0 || previous_len < 0 || mla_supported(d) != kOk)
+    return -1;
+  return mla_block_workspace_bytes(d, q_lora_rank);
+}
+
+int moe_ds_attention_block_forward_f32(void* handle, const float* hidden_in, const float* q_a_weight,
+                                       const float* q_b_weight, const float* kv_a_weight, const float* kv_b_weight,
+                                       const float* o_weight, const float* q_norm_weight, const float* kv_norm_weight,
+                                       const float* previous_kv_cache, const float* previous_pe_cache,
+                                       const float* rope_cos, const float* rope_sin, float* next_kv_cache,
+                                       float* next_pe_cache, float* hidden_out, int64_t hidden_dim,
+                                       int64_t q_lora_rank, int64_t kv_lora_rank, int64_t num_heads,
+                                       int64_t qk_nope_dim, int64_t qk_rope_dim, int64_t v_head_dim,
+                                       int64_t previous_len, float rms_eps, float softmax_scale, void* workspace,
+                                       int64_t workspace_bytes, void* stream) {
+  DsSession* session = static_cast<DsSession*>(handle);
+  if (!session || !hidden_in || !q_a_weight || !q_b_weight || !kv_a_weight || !kv_b_weight || !o_weight ||
+      !q_norm_weight || !kv_norm_weight || !rope_cos || !rope_sin || !next_kv_cache || !next_pe_cache ||
+      !hidden_out)
+    return 1;  // ds_forward.cpp:673-680
+  if (hidden_dim <= 0 || q_lora_rank <= 0 || kv_lora_rank <= 0 || num_heads <= 0 || qk_nope_dim < 0 ||
+      qk_rope_dim < 0 || v_head_dim <= 0 || previous_len < 0)
+    return 2;  // :681-686
+  if (previous_len > 0 && (!previous_kv_cache || !previous_pe_cache)) return 3;  // :687-689
+  const MlaDims d{num_heads, previous_len + 1, qk_nope_dim, qk_rope_dim, kv_lora_rank, v_head_dim};
+  int code = mla_supported(d);
+  if (code != kOk) return code;
+  cudaStream_t s = as_stream(stream);
+  Scratch scratch(workspace, workspace_bytes, static_cast<size_t>(mla_block_workspace_bytes(d, q_lora_rank)), s);
+  if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");
+  MlaBlockArgs a{};
+  a.hidden = hidden_in; a.q_a = q_a_weight; a.q_b = q_b_weight; a.kv_a = kv_a_weight; a.kv_b = kv_b_weight;
+  a.o_w = o_weight; a.q_norm = q_norm_weight; a.kv_norm = kv_norm_weight;
+  a.prev_kv = previous_kv_cache; a.prev_pe = previous_pe_cache; a.rope_cos = rope_cos; a.rope_sin = rope_sin;
+  a.next_kv = next_kv_cache; a.next_pe = next_pe_cache; a.out = hidden_out;
+  a.H = hidden_dim; a.q_rank = q_lora_rank; a.prev_len = previous_len;
+  a.eps = rms_eps; a.softmax_scale = softmax_scale;
+  code = mla_block_run(d, a, scratch.base(), s);
+  if (code != kOk) return code;
+  session->monolithic_calls += 1;  // :778-780
+  session->attention_invocations += 1;
+  session->fused_attention_invocations += 1;
+  return 0;
+}
 
 __global__ void combine_dense_kernel(const float* outputs, const float* route, int64_t E, int64_t width, float* out) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < width;

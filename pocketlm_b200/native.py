@@ -59,6 +59,14 @@ def _native_ds_moe_disabled() -> bool:
     return _flag("PCKETLM_DISABLE_NATIVE_DS_MOE")
 
 
+def _native_flash_mla_disabled() -> bool:
+    return _flag("PCKETLM_DISABLE_NATIVE_FLASH_MLA")
+
+
+def _native_fused_ds_attention_disabled() -> bool:
+    return _flag("PCKETLM_DISABLE_FUSED_DS_ATTENTION")
+
+
 def _ds_monolithic_disabled() -> bool:
     return _flag("PCKETLM_DISABLE_DS_MONOLITHIC")
 
@@ -106,6 +114,12 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "moe_ds_monolithic_call_counter": ([_P], _I64),
     "moe_ds_expert_invocation_count": ([_P], _I64),
     "moe_ds_layers_executed_count": ([_P], _I64),
+    "moe_ds_attention_invocation_count": ([_P], _I64),
+    "moe_ds_fused_attention_invocation_count": ([_P], _I64),
+    "moe_mla_attention_workspace_bytes": ([_I64] * 6, _I64),
+    "moe_mla_attention_flash_forward": ([_P] * 6 + [_I64] * 6 + [_F32, _P, _I64, _P], _INT),
+    "moe_ds_attention_block_workspace_bytes": ([_I64] * 8, _I64),
+    "moe_ds_attention_block_forward_f32": ([_P] * 16 + [_I64] * 8 + [_F32, _F32, _P, _I64, _P], _INT),
     "moe_ds_moe_layer_forward_f32": ([_P, _P, _P, _I64, _I64, _I64, _P, _P], _INT),
     "moe_ds_moe_layer_forward_fp8_f32": ([_P] * 9 + [_I64] * 6 + [_P, _P, _I64, _P], _INT),
     "moe_q4_dequant_to_fp16": ([_P, _P, _P, _I64, _I64, _P], _INT),
@@ -339,6 +353,14 @@ def native_ds_router_available() -> bool:
 
 def native_ds_moe_available() -> bool:
     return native_ds_forward_available() and not _native_ds_moe_disabled()
+
+
+def native_flash_mla_available() -> bool:
+    return native_ds_forward_available() and not _native_flash_mla_disabled()
+
+
+def native_fused_ds_attention_available() -> bool:
+    return native_ds_forward_available() and not _native_fused_ds_attention_disabled()
 
 
 def _require(available: bool, what: str, disabled: bool) -> None:
@@ -706,8 +728,8 @@ def route_topk(hidden: torch.Tensor, router_weight: torch.Tensor, bias: torch.Te
 class DeepSeekNativeSession:
     """Opaque session with the reference's observable counters
     (ds_forward.cpp:192-335).  The fp8 pack / KV callbacks of the reference
-    belong to its attention and pack streaming, which this path does not
-    have; the arguments are accepted and ignored."""
+    belong to its callback-driven layer loop and pack streaming, which this
+    path does not have; the arguments are accepted and ignored."""
 
     def __init__(self, *, num_layers: int, hidden_dim: int, num_experts: int, top_k: int,
                  fp8_pack_callback: object | None = None, kv_session_handle: int | None = None):
@@ -750,6 +772,12 @@ class DeepSeekNativeSession:
 
     def layers_executed_count(self) -> int:
         return int(self._lib.moe_ds_layers_executed_count(self._handle))
+
+    def attention_invocation_count(self) -> int:
+        return int(self._lib.moe_ds_attention_invocation_count(self._handle))
+
+    def fused_attention_invocation_count(self) -> int:
+        return int(self._lib.moe_ds_fused_attention_invocation_count(self._handle))
 
 
 def _python_ds_moe_layer_forward(expert_outputs: torch.Tensor, route_weights: torch.Tensor) -> torch.Tensor:
@@ -802,6 +830,112 @@ def ds_moe_layer_forward_fp8(session: DeepSeekNativeSession, items, hidden: torc
     if code != 0:
         raise RuntimeError(f"ds_moe_layer_forward_fp8_f32 failed with code {code}")
     return out.to(_out_device(hidden))
+
+
+# ---------------------------------------------------------------------------
+# MLA attention (native/__init__.py:878-1075; ds_forward.cpp:517-782)
+# ---------------------------------------------------------------------------
+
+def ds_mla_attention_flash_forward(q_nope: torch.Tensor, q_pe: torch.Tensor, kv_cache: torch.Tensor,
+                                   pe_cache: torch.Tensor, wkv_b: torch.Tensor, *,
+                                   softmax_scale: float) -> torch.Tensor:
+    """Compressed-KV MLA attention core for one query token on the GPU
+    (ds_forward.cpp:517-597): q_nope [heads, nope], q_pe [heads, rope],
+    kv_cache [cache_len, kv_lora_rank], pe_cache [cache_len, rope], wkv_b
+    [heads, nope + v, kv_lora_rank] -> [heads, v] fp32 on q_nope's device.
+    The shape checks and messages are the reference's (native/__init__.py:895-916)."""
+    if q_nope.ndim != 2 or q_pe.ndim != 2:
+        raise ValueError("q_nope and q_pe must be [heads, dim]")
+    if kv_cache.ndim != 2 or pe_cache.ndim != 2:
+        raise ValueError("kv_cache and pe_cache must be [cache_len, dim]")
+    if wkv_b.ndim != 3:
+        raise ValueError("wkv_b must be [heads, qk_nope + v_head_dim, kv_lora_rank]")
+    heads, nope, rope = int(q_nope.shape[0]), int(q_nope.shape[1]), int(q_pe.shape[1])
+    cache_len, rank = int(kv_cache.shape[0]), int(kv_cache.shape[1])
+    if int(q_pe.shape[0]) != heads or int(wkv_b.shape[0]) != heads:
+        raise ValueError("head count mismatch")
+    if int(pe_cache.shape[0]) != cache_len or int(pe_cache.shape[1]) != rope:
+        raise ValueError("pe_cache shape mismatch")
+    if int(wkv_b.shape[2]) != rank or int(wkv_b.shape[1]) <= nope:
+        raise ValueError("wkv_b shape mismatch")
+    v_dim = int(wkv_b.shape[1]) - nope
+    _require(native_flash_mla_available(), "flash MLA", _native_flash_mla_disabled())
+    qn, qp = _gpu(q_nope, torch.float32), _gpu(q_pe, torch.float32)
+    kv, pe, wkv = _gpu(kv_cache, torch.float32), _gpu(pe_cache, torch.float32), _gpu(wkv_b, torch.float32)
+    lib = load_library()
+    out = torch.empty((heads, v_dim), dtype=torch.float32, device=qn.device)
+    ws = _workspace(lib.moe_mla_attention_workspace_bytes(heads, cache_len, nope, rope, rank, v_dim))
+    code = lib.moe_mla_attention_flash_forward(_ptr(qn), _ptr(qp), _ptr(kv), _ptr(pe), _ptr(wkv), _ptr(out), heads,
+                                               cache_len, nope, rope, rank, v_dim, float(softmax_scale), _ptr(ws),
+                                               ws.numel(), _stream())
+    _check(code, "ds_mla_attention_flash_forward")
+    return out.to(_out_device(q_nope))
+
+
+def ds_attention_block_forward(session: DeepSeekNativeSession, hidden: torch.Tensor, q_a_weight: torch.Tensor,
+                               q_b_weight: torch.Tensor, kv_a_weight: torch.Tensor, kv_b_weight: torch.Tensor,
+                               o_weight: torch.Tensor, q_norm_weight: torch.Tensor, kv_norm_weight: torch.Tensor, *,
+                               previous_kv_cache: torch.Tensor | None, previous_pe_cache: torch.Tensor | None,
+                               rope_cos: torch.Tensor, rope_sin: torch.Tensor, q_lora_rank: int, kv_lora_rank: int,
+                               num_heads: int, qk_nope_dim: int, qk_rope_dim: int, v_head_dim: int, rms_eps: float,
+                               softmax_scale: float) -> tuple[torch.Tensor, tuple[torch.Tensor, torch.Tensor]]:
+    """A one-token DeepSeek attention block as one call (ds_forward.cpp:647-782)
+    on the GPU: returns hidden_out [hidden_dim] and the new caches
+    ([previous_len + 1, kv_lora_rank], [previous_len + 1, qk_rope_dim]), fp32 on
+    hidden's device.  The shape checks and messages are the reference's
+    (native/__init__.py:969-1005); weights stay where they are when they are
+    already fp32 on the GPU (one upload per call otherwise)."""
+    H = int(hidden.numel())
+    if H <= 0:
+        raise ValueError("hidden must not be empty")
+    q_rank, rank, heads = int(q_lora_rank), int(kv_lora_rank), int(num_heads)
+    nope, rope, v_dim = int(qk_nope_dim), int(qk_rope_dim), int(v_head_dim)
+    if tuple(q_a_weight.shape) != (q_rank, H):
+        raise ValueError("q_a_weight must be [q_lora_rank, hidden_dim]")
+    if tuple(q_b_weight.shape) != (heads * (nope + rope), q_rank):
+        raise ValueError("q_b_weight shape does not match DeepSeek attention config")
+    if tuple(kv_a_weight.shape) != (rank + rope, H):
+        raise ValueError("kv_a_weight shape does not match DeepSeek attention config")
+    if tuple(kv_b_weight.shape) != (heads * (nope + v_dim), rank):
+        raise ValueError("kv_b_weight shape does not match DeepSeek attention config")
+    if tuple(o_weight.shape) != (H, heads * v_dim):
+        raise ValueError("o_weight shape does not match DeepSeek attention config")
+    if int(q_norm_weight.numel()) != q_rank or int(kv_norm_weight.numel()) != rank:
+        raise ValueError("norm weight sizes do not match ranks")
+    if int(rope_cos.numel()) != max(0, rope // 2) or int(rope_sin.numel()) != max(0, rope // 2):
+        raise ValueError("rope cos/sin sizes must be qk_rope_dim / 2")
+    prev_len = 0 if previous_kv_cache is None else int(previous_kv_cache.numel()) // max(rank, 1)
+    prev_pe_len = 0 if previous_pe_cache is None else int(previous_pe_cache.numel()) // max(rope, 1)
+    if previous_pe_cache is not None and rope == 0:
+        prev_pe_len = prev_len if int(previous_pe_cache.numel()) == 0 else -1
+    if prev_pe_len != prev_len:
+        raise ValueError("previous KV and PE cache lengths must match")
+    _require(native_fused_ds_attention_available(), "fused DeepSeek attention", _native_fused_ds_attention_disabled())
+    x = _gpu(hidden, torch.float32).reshape(-1)
+    q_a, q_b = _gpu(q_a_weight, torch.float32), _gpu(q_b_weight, torch.float32)
+    kv_a, kv_b, o_w = _gpu(kv_a_weight, torch.float32), _gpu(kv_b_weight, torch.float32), _gpu(o_weight, torch.float32)
+    q_norm = _gpu(q_norm_weight, torch.float32).reshape(-1)
+    kv_norm = _gpu(kv_norm_weight, torch.float32).reshape(-1)
+    cos, sin = _gpu(rope_cos, torch.float32).reshape(-1), _gpu(rope_sin, torch.float32).reshape(-1)
+    prev_kv = None if not prev_len else _gpu(previous_kv_cache, torch.float32).reshape(-1, rank)
+    prev_pe = None if not prev_len else _gpu(previous_pe_cache, torch.float32).reshape(-1, rope)
+    lib = load_library()
+    next_kv = torch.empty((prev_len + 1, rank), dtype=torch.float32, device=x.device)
+    next_pe = torch.empty((prev_len + 1, rope), dtype=torch.float32, device=x.device)
+    out = torch.empty((H,), dtype=torch.float32, device=x.device)
+    # a zero-size cos/sin still needs an address (the reference requires non-null pointers)
+    if cos.numel() == 0:
+        cos = torch.zeros((1,), dtype=torch.float32, device=x.device)
+        sin = torch.zeros((1,), dtype=torch.float32, device=x.device)
+    ws = _workspace(lib.moe_ds_attention_block_workspace_bytes(H, q_rank, rank, heads, nope, rope, v_dim, prev_len))
+    code = lib.moe_ds_attention_block_forward_f32(
+        session._handle, _ptr(x), _ptr(q_a), _ptr(q_b), _ptr(kv_a), _ptr(kv_b), _ptr(o_w), _ptr(q_norm),
+        _ptr(kv_norm), _ptr(prev_kv), _ptr(prev_pe), _ptr(cos),
+        _ptr(sin), _ptr(next_kv), _ptr(next_pe), _ptr(out), H, q_rank, rank, heads, nope, rope, v_dim, prev_len,
+        float(rms_eps), float(softmax_scale), _ptr(ws), ws.numel(), _stream())
+    _check(code, "ds_attention_block_forward_f32")
+    dev = _out_device(hidden)
+    return out.to(dev), (next_kv.to(dev), next_pe.to(dev))
 
 
 # ---------------------------------------------------------------------------
