@@ -17,6 +17,9 @@ router.py
     softmax top-k router, restated with the reference's torch CPU ops.
 layer.py
     Layer-level flows: run_fp8_moe's default path and the Q4 token loop.
+mla.py
+    The one-token MLA attention (ds_forward.cpp:517-782) with the reference's
+    per-position online softmax.
 ref.py
     The reference's own kernels compiled from source into oracle/_ref/
     (Makefile target `ref`), used to pin the restatement and as the CPU
@@ -29,6 +32,6 @@ restatements against golden vectors produced by the reference's own Python
 runtime (tests/golden/make_golden.py).
 """
 
-from . import kernels, layer, ref, router  # noqa: F401
+from . import kernels, layer, mla, ref, router  # noqa: F401
 from .layer import ds_moe_layer, mixtral_q4_layer  # noqa: F401
 from .router import RouteResult, boundary_gap, route_deepseek, route_softmax_topk  # noqa: F401

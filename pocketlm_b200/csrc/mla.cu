@@ -255,8 +255,10 @@ MOE_D void cp_async_wait() {
 template <bool VEC, int COLS>
 __global__ void __launch_bounds__(kAttnThreads) mla_attention_kernel(AttnArgs a) {
   extern __shared__ __align__(16) float sm[];
-  const int64_t R = a.R, rope = a.rope, RS = attn_rs(R), PS = attn_ps(rope);
-  const int64_t R4 = round4(R), P4 = round4(rope);
+  // shared-memory indices in 32 bits (R <= 1024, rope <= 256); global ones in 64
+  const int R = static_cast<int>(a.R), rope = static_cast<int>(a.rope);
+  const int RS = static_cast<int>(attn_rs(R)), PS = static_cast<int>(attn_ps(rope));
+  const int R4 = static_cast<int>(round4(R)), P4 = static_cast<int>(round4(rope));
   const int nbuf = VEC ? a.nbuf : 1;
   float* qa_s = sm;                              // [16][RS]
   float* qp_s = qa_s + kAttnHeads * RS;          // [16][PS]
@@ -283,45 +285,45 @@ __global__ void __launch_bounds__(kAttnThreads) mla_attention_kernel(AttnArgs a)
     float* kv_s = kv_b + (k % nbuf) * kAttnPos * RS;
     float* pe_s = pe_b + (k % nbuf) * kAttnPos * PS;
     if (VEC) {
-      const int64_t r4 = R / 4, e4 = rope / 4;
-      for (int64_t i = t; i < np * r4; i += kAttnThreads) {
-        const int64_t q = i / r4, c = 4 * (i - q * r4);
-        cp_async16(kv_s + q * RS + c, a.kv + (p0 + q) * R + c);
+      const int r4 = R / 4, e4 = rope / 4;
+      for (int i = t; i < np * r4; i += kAttnThreads) {
+        const int q = i / r4, c = 4 * (i - q * r4);
+        cp_async16(kv_s + q * RS + c, a.kv + (p0 + q) * a.R + c);
       }
-      for (int64_t i = t; i < np * e4; i += kAttnThreads) {
-        const int64_t q = i / e4, c = 4 * (i - q * e4);
-        cp_async16(pe_s + q * PS + c, a.pe + (p0 + q) * rope + c);
+      for (int i = t; i < np * e4; i += kAttnThreads) {
+        const int q = i / e4, c = 4 * (i - q * e4);
+        cp_async16(pe_s + q * PS + c, a.pe + (p0 + q) * a.rope + c);
       }
     } else {
       for (int q = 0; q < kAttnPos; ++q) {
         const bool live = q < np;
-        for (int64_t c = t; c < R4; c += kAttnThreads)
-          kv_s[q * RS + c] = (live && c < R) ? a.kv[(p0 + q) * R + c] : 0.0f;
-        for (int64_t c = t; c < P4; c += kAttnThreads)
-          pe_s[q * PS + c] = (live && c < rope) ? a.pe[(p0 + q) * rope + c] : 0.0f;
+        for (int c = t; c < R4; c += kAttnThreads)
+          kv_s[q * RS + c] = (live && c < R) ? a.kv[(p0 + q) * a.R + c] : 0.0f;
+        for (int c = t; c < P4; c += kAttnThreads)
+          pe_s[q * PS + c] = (live && c < rope) ? a.pe[(p0 + q) * a.rope + c] : 0.0f;
       }
     }
   };
 
   // the CTA's queries (rows of heads past nh are never read)
   if (VEC) {
-    const int64_t r4 = R / 4, e4 = rope / 4;
-    for (int64_t i = t; i < nh * r4; i += kAttnThreads) {
-      const int64_t hl = i / r4, c = 4 * (i - hl * r4);
-      cp_async16(qa_s + hl * RS + c, a.q_abs + (h0 + hl) * R + c);
+    const int r4 = R / 4, e4 = rope / 4;
+    for (int i = t; i < nh * r4; i += kAttnThreads) {
+      const int hl = i / r4, c = 4 * (i - hl * r4);
+      cp_async16(qa_s + hl * RS + c, a.q_abs + (h0 + hl) * a.R + c);
     }
-    for (int64_t i = t; i < nh * e4; i += kAttnThreads) {
-      const int64_t hl = i / e4, c = 4 * (i - hl * e4);
-      cp_async16(qp_s + hl * PS + c, a.q_pe + (h0 + hl) * rope + c);
+    for (int i = t; i < nh * e4; i += kAttnThreads) {
+      const int hl = i / e4, c = 4 * (i - hl * e4);
+      cp_async16(qp_s + hl * PS + c, a.q_pe + (h0 + hl) * a.rope + c);
     }
     if (nbuf == 2) fetch(0);
     cp_async_commit();
   } else {
     for (int hl = 0; hl < kAttnHeads; ++hl) {
-      for (int64_t c = t; c < R4; c += kAttnThreads)
-        qa_s[hl * RS + c] = (hl < nh && c < R) ? a.q_abs[(h0 + hl) * R + c] : 0.0f;
-      for (int64_t c = t; c < P4; c += kAttnThreads)
-        qp_s[hl * PS + c] = (hl < nh && c < rope) ? a.q_pe[(h0 + hl) * rope + c] : 0.0f;
+      for (int c = t; c < R4; c += kAttnThreads)
+        qa_s[hl * RS + c] = (hl < nh && c < R) ? a.q_abs[(h0 + hl) * a.R + c] : 0.0f;
+      for (int c = t; c < P4; c += kAttnThreads)
+        qp_s[hl * PS + c] = (hl < nh && c < rope) ? a.q_pe[(h0 + hl) * a.rope + c] : 0.0f;
     }
   }
   if (t < kAttnHeads) {
@@ -373,8 +375,8 @@ __global__ void __launch_bounds__(kAttnThreads) mla_attention_kernel(AttnArgs a)
       for (int x = 0; x < 4; ++x)
 #pragma unroll
         for (int y = 0; y < 4; ++y) sc[x][y] = 0.0f;
-      auto block_dot = [&](const float* qs, const float* ks, int64_t stride, int64_t n4) {
-        for (int64_t i = kk; i < n4; i += 16) {
+      auto block_dot = [&](const float* qs, const float* ks, int stride, int n4) {
+        for (int i = kk; i < n4; i += 16) {
           float4 qv[4], kv4[4];
 #pragma unroll
           for (int x = 0; x < 4; ++x) qv[x] = reinterpret_cast<const float4*>(qs + (hb + x) * stride)[i];
@@ -429,23 +431,35 @@ __global__ void __launch_bounds__(kAttnThreads) mla_attention_kernel(AttnArgs a)
     }
     __syncthreads();
 
-    // latent sums: column c = t + 256 j of every head
+    // latent sums: columns c = t + 256 j of every head (columns past R stay 0 and are not stored)
+    {
+      const float4* al4 = reinterpret_cast<const float4*>(alpha_s);
 #pragma unroll
-    for (int j = 0; j < COLS; ++j) {
-      const int64_t c = t + static_cast<int64_t>(kAttnThreads) * j;
-      if (c < R) {
+      for (int g = 0; g < kAttnHeads / 4; ++g) {
+        const float4 al = al4[g];
 #pragma unroll
-        for (int h = 0; h < kAttnHeads; ++h) acc[j][h] *= alpha_s[h];
-        for (int q = 0; q < np; ++q) {
-          const float kvv = kv_s[q * RS + c];
-          const float4* p4 = reinterpret_cast<const float4*>(pt_s + q * kAttnHeads);
+        for (int j = 0; j < COLS; ++j) {
+          acc[j][4 * g] *= al.x;
+          acc[j][4 * g + 1] *= al.y;
+          acc[j][4 * g + 2] *= al.z;
+          acc[j][4 * g + 3] *= al.w;
+        }
+      }
+      for (int q = 0; q < np; ++q) {
+        const float4* p4 = reinterpret_cast<const float4*>(pt_s + q * kAttnHeads);
+        float4 pv[kAttnHeads / 4];
+#pragma unroll
+        for (int g = 0; g < kAttnHeads / 4; ++g) pv[g] = p4[g];
+#pragma unroll
+        for (int j = 0; j < COLS; ++j) {
+          const int c = t + kAttnThreads * j;
+          const float kvv = c < R ? kv_s[q * RS + c] : 0.0f;
 #pragma unroll
           for (int g = 0; g < kAttnHeads / 4; ++g) {
-            const float4 pv = p4[g];
-            acc[j][4 * g] = fmaf(pv.x, kvv, acc[j][4 * g]);
-            acc[j][4 * g + 1] = fmaf(pv.y, kvv, acc[j][4 * g + 1]);
-            acc[j][4 * g + 2] = fmaf(pv.z, kvv, acc[j][4 * g + 2]);
-            acc[j][4 * g + 3] = fmaf(pv.w, kvv, acc[j][4 * g + 3]);
+            acc[j][4 * g] = fmaf(pv[g].x, kvv, acc[j][4 * g]);
+            acc[j][4 * g + 1] = fmaf(pv[g].y, kvv, acc[j][4 * g + 1]);
+            acc[j][4 * g + 2] = fmaf(pv[g].z, kvv, acc[j][4 * g + 2]);
+            acc[j][4 * g + 3] = fmaf(pv[g].w, kvv, acc[j][4 * g + 3]);
           }
         }
       }
@@ -455,11 +469,11 @@ __global__ void __launch_bounds__(kAttnThreads) mla_attention_kernel(AttnArgs a)
 
 #pragma unroll
   for (int j = 0; j < COLS; ++j) {
-    const int64_t c = t + static_cast<int64_t>(kAttnThreads) * j;
+    const int c = t + kAttnThreads * j;
     if (c < R) {
 #pragma unroll
       for (int h = 0; h < kAttnHeads; ++h)
-        if (h < nh) a.part_acc[(split * a.heads + h0 + h) * R + c] = acc[j][h];
+        if (h < nh) a.part_acc[(split * a.heads + h0 + h) * a.R + c] = acc[j][h];
     }
   }
   if (t < nh) {
