@@ -135,3 +135,26 @@ def test_wrapper_shape_errors():
     bad = dict(kw, previous_kv_cache=torch.zeros(3, R), previous_pe_cache=torch.zeros(2, rope))
     with pytest.raises(ValueError, match="previous KV and PE cache lengths must match"):
         native.ds_attention_block_forward(None, torch.zeros(H), *ws, **bad)
+
+
+@pytest.mark.skipif(not oref.available(), reason="reference build (oracle/_ref) missing")
+@pytest.mark.parametrize("H,qr,R,heads,nope,rope,v,prev", [(64, 16, 16, 4, 8, 8, 8, 32), (256, 96, 64, 6, 16, 8, 16, 0),
+                                                           (128, 32, 24, 5, 8, 6, 8, 10), (96, 24, 20, 3, 4, 5, 6, 7)])
+def test_oracle_block_matches_compiled_reference(H, qr, R, heads, nope, rope, v, prev):
+    """The block restatement against ds_attention_block_forward_f32 compiled from the reference's source,
+    an odd rope width (no rotation, as the reference) included."""
+    g = torch.Generator().manual_seed(H + prev)
+
+    def rnd(*shape, scale=1.0):
+        return torch.randn(shape, generator=g) * scale
+
+    args = (rnd(H), rnd(qr, H, scale=0.05), rnd(heads * (nope + rope), qr, scale=0.05), rnd(R + rope, H, scale=0.05),
+            rnd(heads * (nope + v), R, scale=0.05), rnd(H, heads * v, scale=0.05), 1 + 0.1 * rnd(qr), 1 + 0.1 * rnd(R),
+            rnd(prev, R, scale=0.5) if prev else None, rnd(prev, rope, scale=0.5) if prev else None)
+    angles = torch.arange(rope // 2, dtype=torch.float32) * 0.37
+    kw = dict(q_lora_rank=qr, kv_lora_rank=R, num_heads=heads, qk_nope_dim=nope, qk_rope_dim=rope, v_head_dim=v,
+              rms_eps=1e-6, softmax_scale=0.2)
+    out, (kv, pe) = omla.attention_block(*args, angles.cos(), angles.sin(), **kw)
+    want, (wkv, wpe) = oref.attention_block(*args, angles.cos(), angles.sin(), **kw)
+    assert _rel(out, want) <= BLOCK_TOL
+    assert torch.allclose(kv, wkv, atol=1e-6, rtol=1e-6) and torch.allclose(pe, wpe, atol=1e-6, rtol=1e-6)
