@@ -7,7 +7,8 @@
 // latency-bound (the DeepSeek-V3 shapes stream 750 MB of fp32 weights), so
 // the work is laid out for bandwidth:
 //  * projections (q_a and kv_a in one launch, q_b, o_proj): one warp per
-//    output row, eight 16-byte streaming loads in flight per lane;
+//    output row (2 or 4 per row when rows are few), eight 16-byte streaming
+//    loads in flight per lane;
 //  * RMSNorm of q_low and of the new latent row, RoPE of the new pe row: one
 //    CTA each (the mean square needs the whole vector);
 //  * absorbed queries q_abs[h] = W_UK[h]^T q_nope[h] (and q_pe's RoPE): one
@@ -67,68 +68,93 @@ struct GemvRows {
   int vec;
 };
 
+// SPLIT warps share a row (its columns in SPLIT contiguous pieces) when there
+// are too few rows to keep every SM streaming; their sums are added in piece
+// order through shared memory.  Every warp of a CTA runs the same number of
+// row blocks, so the barriers are reached by all of them.
+template <int SPLIT>
 __global__ void __launch_bounds__(kGemvThreads) mla_gemv_kernel(GemvRows a) {
-  constexpr int kWarps = kGemvThreads / kWarp;
-  const int lane = threadIdx.x % kWarp;
+  constexpr int kWarps = kGemvThreads / kWarp, kRowsPerCta = kWarps / SPLIT;
+  __shared__ float part[kWarps];
+  const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+  const int slot = warp / SPLIT, piece = warp % SPLIT;
   const int64_t rows = a.rows0 + a.rows1, cols = a.cols;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + threadIdx.x / kWarp; r < rows; r += stride) {
-    const float* w;
-    const float* x = a.x;
-    if (r < a.rows0) {
-      const int64_t grp = r / a.group;
-      w = a.w0 + grp * a.group_stride + (r - grp * a.group) * cols;
-      x += grp * a.x_stride;
-    } else {
-      w = a.w1 + (r - a.rows0) * cols;
-    }
-    float acc0 = 0.0f, acc1 = 0.0f;
-    if (a.vec) {
-      const float4* w4 = reinterpret_cast<const float4*>(w);
-      const float4* x4 = reinterpret_cast<const float4*>(x);
-      const int64_t n4 = cols / 4;
-      int64_t i = lane;
-      for (; i + (kGemvUnroll - 1) * kWarp < n4; i += kGemvUnroll * kWarp) {
-        float4 wv[kGemvUnroll];
+  const int64_t blocks = (rows + kRowsPerCta - 1) / kRowsPerCta;
+  for (int64_t rb = blockIdx.x; rb < blocks; rb += gridDim.x) {
+    const int64_t r = rb * kRowsPerCta + slot;
+    float sum = 0.0f;
+    if (r < rows) {
+      const float* w;
+      const float* x = a.x;
+      if (r < a.rows0) {
+        const int64_t grp = r / a.group;
+        w = a.w0 + grp * a.group_stride + (r - grp * a.group) * cols;
+        x += grp * a.x_stride;
+      } else {
+        w = a.w1 + (r - a.rows0) * cols;
+      }
+      float acc0 = 0.0f, acc1 = 0.0f;
+      if (a.vec) {
+        const float4* w4 = reinterpret_cast<const float4*>(w);
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        const int64_t n4 = cols / 4, i1 = (piece + 1) * n4 / SPLIT;
+        int64_t i = piece * n4 / SPLIT + lane;
+        for (; i + (kGemvUnroll - 1) * kWarp < i1; i += kGemvUnroll * kWarp) {
+          float4 wv[kGemvUnroll];
 #pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u) wv[u] = __ldcs(w4 + i + u * kWarp);
+          for (int u = 0; u < kGemvUnroll; ++u) wv[u] = __ldcs(w4 + i + u * kWarp);
 #pragma unroll
-        for (int u = 0; u < kGemvUnroll; u += 2) {
-          const float4 xa = __ldg(x4 + i + u * kWarp), xb = __ldg(x4 + i + (u + 1) * kWarp);
-          acc0 = fmaf(wv[u].x, xa.x, acc0);
-          acc1 = fmaf(wv[u + 1].x, xb.x, acc1);
-          acc0 = fmaf(wv[u].y, xa.y, acc0);
-          acc1 = fmaf(wv[u + 1].y, xb.y, acc1);
-          acc0 = fmaf(wv[u].z, xa.z, acc0);
-          acc1 = fmaf(wv[u + 1].z, xb.z, acc1);
-          acc0 = fmaf(wv[u].w, xa.w, acc0);
-          acc1 = fmaf(wv[u + 1].w, xb.w, acc1);
+          for (int u = 0; u < kGemvUnroll; u += 2) {
+            const float4 xa = __ldg(x4 + i + u * kWarp), xb = __ldg(x4 + i + (u + 1) * kWarp);
+            acc0 = fmaf(wv[u].x, xa.x, acc0);
+            acc1 = fmaf(wv[u + 1].x, xb.x, acc1);
+            acc0 = fmaf(wv[u].y, xa.y, acc0);
+            acc1 = fmaf(wv[u + 1].y, xb.y, acc1);
+            acc0 = fmaf(wv[u].z, xa.z, acc0);
+            acc1 = fmaf(wv[u + 1].z, xb.z, acc1);
+            acc0 = fmaf(wv[u].w, xa.w, acc0);
+            acc1 = fmaf(wv[u + 1].w, xb.w, acc1);
+          }
         }
-      }
-      // the rest (fewer than 8 float4 per lane): all loads issued before the multiply-adds
-      float4 wv[kGemvUnroll - 1], xv[kGemvUnroll - 1];
+        // the rest (fewer than 8 float4 per lane): all loads issued before the multiply-adds
+        float4 wv[kGemvUnroll - 1], xv[kGemvUnroll - 1];
 #pragma unroll
-      for (int u = 0; u < kGemvUnroll - 1; ++u) {
-        const bool in = i + u * kWarp < n4;
-        wv[u] = in ? __ldcs(w4 + i + u * kWarp) : make_float4(0.f, 0.f, 0.f, 0.f);
-        xv[u] = in ? __ldg(x4 + i + u * kWarp) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+        for (int u = 0; u < kGemvUnroll - 1; ++u) {
+          const bool in = i + u * kWarp < i1;
+          wv[u] = in ? __ldcs(w4 + i + u * kWarp) : make_float4(0.f, 0.f, 0.f, 0.f);
+          xv[u] = in ? __ldg(x4 + i + u * kWarp) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
 #pragma unroll
-      for (int u = 0; u < kGemvUnroll - 1; ++u) {
-        float& acc = (u % 2) ? acc1 : acc0;
-        acc = fmaf(wv[u].x, xv[u].x, acc);
-        acc = fmaf(wv[u].y, xv[u].y, acc);
-        acc = fmaf(wv[u].z, xv[u].z, acc);
-        acc = fmaf(wv[u].w, xv[u].w, acc);
+        for (int u = 0; u < kGemvUnroll - 1; ++u) {
+          float& acc = (u % 2) ? acc1 : acc0;
+          acc = fmaf(wv[u].x, xv[u].x, acc);
+          acc = fmaf(wv[u].y, xv[u].y, acc);
+          acc = fmaf(wv[u].z, xv[u].z, acc);
+          acc = fmaf(wv[u].w, xv[u].w, acc);
+        }
+      } else {
+        const int64_t c1 = (piece + 1) * cols / SPLIT;
+        for (int64_t c = piece * cols / SPLIT + lane; c < c1; c += kWarp) acc0 = fmaf(__ldcs(w + c), __ldg(x + c), acc0);
       }
-    } else {
-      for (int64_t i = lane; i < cols; i += kWarp) acc0 = fmaf(__ldcs(w + i), __ldg(x + i), acc0);
+      sum = warp_sum(acc0 + acc1);
     }
-    const float s = warp_sum(acc0 + acc1);
-    if (lane == 0) {
-      if (r < a.rows0) a.y0[r] = s;
-      else a.y1[r - a.rows0] = s;
+    if (SPLIT == 1) {
+      if (r < rows && lane == 0) {
+        if (r < a.rows0) a.y0[r] = sum;
+        else a.y1[r - a.rows0] = sum;
+      }
+      continue;
     }
+    if (lane == 0) part[warp] = sum;
+    __syncthreads();
+    if (piece == 0 && lane == 0 && r < rows) {
+      float total = part[warp];
+#pragma unroll
+      for (int k = 1; k < SPLIT; ++k) total += part[warp + k];
+      if (r < a.rows0) a.y0[r] = total;
+      else a.y1[r - a.rows0] = total;
+    }
+    __syncthreads();
   }
 }
 
@@ -569,10 +595,13 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 cudaError_t launch_gemv(GemvRows g, cudaStream_t s) {
   g.vec = g.cols % 4 == 0 && g.group_stride % 4 == 0 && g.x_stride % 4 == 0 && aligned16(g.w0) &&
           (g.rows1 == 0 || aligned16(g.w1)) && aligned16(g.x);
-  const int64_t rows = g.rows0 + g.rows1;
-  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, kGemvThreads / kWarp),
-                                                              static_cast<int64_t>(gemv_grid_ctas()) * 8));
-  mla_gemv_kernel<<<static_cast<unsigned>(ctas), kGemvThreads, 0, s>>>(g);
+  const int64_t rows = g.rows0 + g.rows1, sms = gemv_grid_ctas();
+  // warps per row: enough rows for 24 streaming warps per SM take one each, fewer share
+  const int split = rows >= sms * 24 ? 1 : rows >= sms * 6 ? 2 : 4;
+  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows * split, kGemvThreads / kWarp), sms * 8));
+  if (split == 1) mla_gemv_kernel<1><<<static_cast<unsigned>(ctas), kGemvThreads, 0, s>>>(g);
+  else if (split == 2) mla_gemv_kernel<2><<<static_cast<unsigned>(ctas), kGemvThreads, 0, s>>>(g);
+  else mla_gemv_kernel<4><<<static_cast<unsigned>(ctas), kGemvThreads, 0, s>>>(g);
   return cudaGetLastError();
 }
 
