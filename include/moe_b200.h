@@ -546,7 +546,8 @@ int64_t moe_ds_attention_block_workspace_bytes(int64_t hidden_dim, int64_t q_lor
  * previous_len rows copied from previous_*_cache, the attention core over
  * previous_len + 1 positions, hidden_out = o_weight . heads.  next_*_cache
  * may equal previous_*_cache (append in place: no copy; the buffers then
- * hold previous_len + 1 rows).  Returns 0; 1 (null pointer), 2 (bad
+ * hold previous_len + 1 rows) and must not otherwise overlap them
+ * (MOE_B200 -2).  Returns 0; 1 (null pointer), 2 (bad
  * dimensions), 3 (previous_len > 0 without previous caches) as the reference
  * does; MOE_B200 status codes (negative) otherwise.  Counts one monolithic
  * call and one (fused) attention invocation on the session. */

@@ -2104,6 +2104,13 @@ int moe_ds_attention_block_forward_f32(void* handle, const float* hidden_in, con
   const MlaDims d{num_heads, previous_len + 1, qk_nope_dim, qk_rope_dim, kv_lora_rank, v_head_dim};
   int code = mla_supported(d);
   if (code != kOk) return code;
+  // the new cache either is the previous one (append in place) or does not overlap it (copied)
+  auto overlaps = [](const float* a, const float* b, int64_t n) {
+    return a != b && a < b + n && b < a + n;
+  };
+  if (previous_len > 0 && (overlaps(next_kv_cache, previous_kv_cache, previous_len * kv_lora_rank) ||
+                           overlaps(next_pe_cache, previous_pe_cache, previous_len * qk_rope_dim)))
+    return fail(kBadDims, "next caches partly overlap the previous ones (equal pointers append in place)");
   cudaStream_t s = as_stream(stream);
   Scratch scratch(workspace, workspace_bytes, static_cast<size_t>(mla_block_workspace_bytes(d, q_lora_rank)), s);
   if (!scratch.ok()) return fail(kNoMemory, "workspace too small or allocation failed");

@@ -620,8 +620,8 @@ int mla_supported(const MlaDims& d) {
   if (d.R > kMlaMaxLatent) return fail(kUnsupported, "kv_lora_rank above 1024");
   if (d.rope > kMlaMaxRope) return fail(kUnsupported, "qk_rope_dim above 256");
   if (d.nope > kMlaMaxNope) return fail(kUnsupported, "qk_nope_dim above 8192");
-  if (d.heads > (int64_t(1) << 24) || d.v > (int64_t(1) << 24) || d.L > (int64_t(1) << 40))
-    return fail(kUnsupported, "dimension too large");
+  if (d.heads > (int64_t(1) << 24) || d.v > (int64_t(1) << 24) || d.L > INT32_MAX)
+    return fail(kUnsupported, "dimension too large");  // grid sizes and the kernels' 32-bit step counts
   return kOk;
 }
 

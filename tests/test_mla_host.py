@@ -103,6 +103,14 @@ def test_block_entry_argument_codes():
         prev = list(dims)
         prev[7] = 3  # previous_len without previous caches
         assert f(ctypes.c_void_p(session), *ptrs[1:], *prev, *tail) == 3
+        # next caches partly overlapping the previous ones (not equal): rejected before any device work
+        over = list(ptrs)
+        over[9], over[10] = FAKE, FAKE  # previous caches
+        over[13], over[14] = ctypes.c_void_p(0x1000 + 4), ctypes.c_void_p(0x1000 + 4)  # next = previous + 1 float
+        assert f(ctypes.c_void_p(session), *over[1:], *prev, *tail) == -2
+        huge = list(dims)
+        huge[7] = 2 ** 31  # cache length beyond the kernels' 32-bit step counts
+        assert f(ctypes.c_void_p(session), *over[1:9], FAKE, FAKE, *over[11:], *huge, *tail) == -5
         assert lib.moe_ds_attention_invocation_count(ctypes.c_void_p(session)) == 0
         assert lib.moe_ds_fused_attention_invocation_count(ctypes.c_void_p(session)) == 0
         assert lib.moe_ds_attention_invocation_count(None) == -1
