@@ -529,17 +529,16 @@ __global__ void __launch_bounds__(kMergeThreads) mla_merge_kernel(const float* _
   const float inv = total > 0.0f ? 1.0f / total : 0.0f;
   const int64_t c = static_cast<int64_t>(blockIdx.y) * kMergeThreads + threadIdx.x;
   if (c >= R) return;
-  constexpr int kU = 16;  // loads in flight per thread
+  constexpr int kU = 16;  // loads in flight per thread: every batch whole, the splits past the end predicated off
   float acc = 0.0f;
-  int64_t s = 0;
-  for (; s + kU <= splits; s += kU) {
+  for (int64_t s0 = 0; s0 < splits; s0 += kU) {
     float v[kU];
 #pragma unroll
-    for (int u = 0; u < kU; ++u) v[u] = __ldcg(part_acc + ((s + u) * heads + h) * R + c);
+    for (int u = 0; u < kU; ++u) v[u] = s0 + u < splits ? __ldcg(part_acc + ((s0 + u) * heads + h) * R + c) : 0.0f;
 #pragma unroll
-    for (int u = 0; u < kU; ++u) acc = fmaf(wsp[s + u], v[u], acc);
+    for (int u = 0; u < kU; ++u)
+      if (s0 + u < splits) acc = fmaf(wsp[s0 + u], v[u], acc);
   }
-  for (; s < splits; ++s) acc = fmaf(wsp[s], __ldcg(part_acc + (s * heads + h) * R + c), acc);
   latent[h * R + c] = acc * inv;
 }
 
